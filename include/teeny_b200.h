@@ -1,0 +1,154 @@
+/*
+ * teeny_b200.h -- C ABI of the B200 (sm_100a) kernels behind teenygrad's
+ * operator surface.
+ *
+ * Every entry point takes device pointers and plain sizes, enqueues work on the
+ * context's stream (no implicit synchronisation) and returns a tb_status.  The
+ * reference executes one RuntimeOp per graph node: it packs kernel arguments
+ * (RuntimeOp::pack_args, core/teeny-core/src/model/mod.rs:145), computes a grid
+ * (RuntimeOp::grid, model/mod.rs:156) and launches teenyc-compiled PTX through
+ * CudaDevice::launch (drivers/teeny-cuda/src/device/mod.rs:315-385), then
+ * synchronises.  A RuntimeOp implementation in drivers/teeny-cuda calls the
+ * matching tb_* function instead of pack_args + cuLaunchKernel; each function
+ * below names the reference kernel whose RuntimeOp it replaces.
+ *
+ * Layouts are the reference's: row-major, contiguous, PyTorch weight layout
+ * ([out, in]) for linear layers, NCHW for convolutions.
+ */
+#ifndef TEENY_B200_H
+#define TEENY_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TB_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define TB_API __attribute__((visibility("default")))
+#else
+#define TB_API
+#endif
+
+typedef struct tb_ctx tb_ctx;
+
+typedef enum tb_status {
+    TB_OK = 0,
+    TB_ERR_ARG = 1,         /* null pointer / bad enum */
+    TB_ERR_SHAPE = 2,       /* unsupported or inconsistent sizes */
+    TB_ERR_ALIGN = 3,       /* pointer or row stride not 16-byte aligned */
+    TB_ERR_CUDA = 4,        /* CUDA runtime error (tb_last_error has the text) */
+    TB_ERR_UNSUPPORTED = 5, /* dtype / option combination not implemented */
+    TB_ERR_DEVICE = 6,      /* a kernel reported a bounded-wait timeout */
+    TB_ERR_NCCL = 7,        /* NCCL failure or timeout */
+    TB_ERR_OOM = 8          /* device allocation failed */
+} tb_status;
+
+typedef enum tb_dtype { TB_F32 = 0, TB_BF16 = 1, TB_I8 = 2, TB_I32 = 3 } tb_dtype;
+
+typedef enum tb_act {
+    TB_ACT_NONE = -1,
+    TB_ACT_SILU = 0,      /* silu_forward, nn/activation/sigmoid.rs:120-156 */
+    TB_ACT_GELU_TANH = 1, /* gelu_forward, nn/activation/gelu.rs:32-75 */
+    TB_ACT_RELU = 2,      /* relu_forward, nn/activation/relu.rs:28 */
+    TB_ACT_SIGMOID = 3    /* sigmoid_forward, nn/activation/sigmoid.rs */
+} tb_act;
+
+/* Epilogue flags for the linear layers. */
+#define TB_EPI_BIAS 1     /* + bias[N] (f32) */
+#define TB_EPI_RESIDUAL 2 /* + residual[M,N] (same dtype as y) */
+#define TB_EPI_SWIGLU 4   /* y[:, j] = silu(acc[:, gate j]) * acc[:, up j]; W rows interleaved
+                             in blocks of 128 (gate block, up block), y has N/2 columns */
+#define TB_EPI_OUT_F32 8  /* write y as f32 instead of the input dtype */
+
+/* ------------------------------------------------------------ context --- */
+TB_API int tb_init(tb_ctx** out, int device);
+TB_API int tb_destroy(tb_ctx* ctx);
+/* stream is a cudaStream_t (NULL = legacy default stream). */
+TB_API int tb_set_stream(tb_ctx* ctx, void* stream);
+TB_API const char* tb_strerror(int status);
+TB_API const char* tb_last_error(tb_ctx* ctx);
+/* Synchronises the stream and reads the device error word that bounded waits
+ * set (0 = none); clears it when `clear` is non-zero. */
+TB_API int tb_device_error(tb_ctx* ctx, int* code, int clear);
+TB_API int tb_abi_version(void);
+
+/* -------------------------------------------------------------- norms --- */
+/* rms_norm_forward (kernels/teeny-kernels/src/nn/norm/rmsnorm.rs:40-122):
+ * y = x * rsqrt(mean(x^2) + eps) * w, rrms[M] optional (may be NULL).
+ * dtype TB_F32 or TB_BF16 for x, w, y; math in f32. */
+TB_API int tb_rmsnorm_fwd(tb_ctx* ctx, int dtype, const void* x, const void* w, void* y, float* rrms,
+                   int64_t M, int64_t N, float eps);
+
+/* layer_norm_forward_inference (nn/norm/layernorm.rs:43-157). */
+TB_API int tb_layernorm_fwd(tb_ctx* ctx, int dtype, const void* x, const void* w, const void* b, void* y,
+                     int64_t M, int64_t N, float eps);
+
+/* -------------------------------------------------------- elementwise --- */
+/* silu / gelu(tanh) / relu / sigmoid forward over n elements. */
+TB_API int tb_act_fwd(tb_ctx* ctx, int act, int dtype, const void* x, void* y, int64_t n);
+/* SwiGLU: y = silu(gate) * up (silu_forward + elemwise_mul_forward,
+ * nn/tensor/elemwise_binary.rs:189, fused). */
+TB_API int tb_swiglu_fwd(tb_ctx* ctx, int dtype, const void* gate, const void* up, void* y, int64_t n);
+/* elemwise_add_forward (nn/tensor/elemwise_add.rs:29). */
+TB_API int tb_add_fwd(tb_ctx* ctx, int dtype, const void* a, const void* b, void* y, int64_t n);
+
+/* ------------------------------------------------------------- linear --- */
+/* linear_forward (nn/mlp/linear.rs:22-117; LinearForward RuntimeOp :251-388):
+ * y[M, N] = x[M, K] * w[N, K]^T (+ bias) (+ residual), epilogue per `flags`.
+ * TB_BF16: tcgen05 tensor cores, f32 accumulate (K % 8 == 0, N % 8 == 0).
+ * TB_F32: f32 CUDA-core path (exact f32 accumulate). */
+TB_API int tb_linear_fwd(tb_ctx* ctx, int dtype, const void* x, const void* w, const float* bias,
+                  const void* residual, void* y, int64_t M, int64_t N, int64_t K, int flags);
+
+/* matmul_forward (math/gemm.rs:44-105; MatMulRuntimeOp gemm.rs:232):
+ * c[M, N] = a[M, K] * b[K, N]. */
+TB_API int tb_matmul_fwd(tb_ctx* ctx, int dtype, const void* a, const void* b, void* c, int64_t M,
+                  int64_t N, int64_t K);
+
+/* --------------------------------------------------------------- int8 --- */
+/* quantize_affine, symmetric per output channel, 8 bits
+ * (utilities/teeny-quant/src/quant/affine.rs:55-148): bit-exact.
+ * w f32 [N, K] -> q int8 [N, K], scale f32 [N]. */
+TB_API int tb_quantize_int8(tb_ctx* ctx, const float* w, int8_t* q, float* scale, int64_t N, int64_t K);
+/* Same, reading bf16 weights (upcast exactly, as teeny-quant's read_f32). */
+TB_API int tb_quantize_int8_bf16(tb_ctx* ctx, const void* w_bf16, int8_t* q, float* scale, int64_t N,
+                          int64_t K);
+/* dequantize_affine (affine.rs:151-159): w = q * scale[n]. */
+TB_API int tb_dequantize_int8(tb_ctx* ctx, const int8_t* q, const float* scale, float* w, int64_t N,
+                       int64_t K);
+/* int8 weight-only linear (the op graph/mod.rs:2595-2600 leaves as TODO):
+ * y[M, N] = scale[n] * x[M, K](bf16) * q[N, K]^T (+ residual), bf16 out unless
+ * TB_EPI_OUT_F32.  Tensor cores (int8 dequantised to bf16 in shared memory). */
+TB_API int tb_int8_linear_fwd(tb_ctx* ctx, const void* x, const int8_t* q, const float* scale,
+                       const void* residual, void* y, int64_t M, int64_t N, int64_t K, int flags);
+
+/* ---------------------------------------------------------- attention --- */
+/* flash_attention2_forward (nn/attention/flash_attn2.rs:53-158) extended with
+ * causal masking and GQA.  q [B, Hq, Sq, D], k/v [B, Hkv, Sk, D],
+ * o [B, Hq, Sq, D], lse [B, Hq, Sq] f32 (natural log of the scaled scores'
+ * sum of exps; may be NULL).  Causal: query i sees key j iff
+ * j <= i + (Sk - Sq).  TB_BF16 runs on tcgen05 (D = 64 or 128);
+ * TB_F32 on CUDA cores (D <= 128). */
+TB_API int tb_attn_fwd(tb_ctx* ctx, int dtype, const void* q, const void* k, const void* v, void* o,
+                float* lse, int B, int Hq, int Hkv, int Sq, int Sk, int D, float scale, int causal);
+
+/* ------------------------------------------------------------ decoder --- */
+/* RoPE, rotate-half pairing (d, d + D/2), inv_freq = theta^(-2i/D).
+ * x, y [T, H, D] (may alias), pos [T] int32. */
+TB_API int tb_rope_fwd(tb_ctx* ctx, int dtype, const void* x, const int32_t* pos, void* y, int64_t T,
+                int H, int D, float theta);
+/* Embedding gather: y[t, :] = table[ids[t], :]. */
+TB_API int tb_embedding_fwd(tb_ctx* ctx, int dtype, const void* table, const int32_t* ids, void* y,
+                     int64_t T, int64_t D, int64_t vocab);
+/* Row argmax; the lowest index wins ties, NaN never wins. x [M, N]. */
+TB_API int tb_argmax_fwd(tb_ctx* ctx, int dtype, const void* x, int32_t* out, int64_t M, int64_t N);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TEENY_B200_H */

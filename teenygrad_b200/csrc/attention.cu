@@ -1,0 +1,572 @@
+// Attention forward on B200.
+//
+//  * attn_tc_kernel<D>: flash-style forward for bf16 Q/K/V, D in {64, 128}.
+//    One CTA per (128-query tile, head, batch).  Warp 0 streams K and V tiles
+//    of 128 keys with TMA (two-stage ring), warp 1 issues tcgen05.mma:
+//    S = Q K^T into one of two TMEM score buffers, then O += P V into a TMEM
+//    accumulator.  Warps 2-5 own one query row per thread: they read the row
+//    of S from TMEM, run the online softmax in the exp2 domain, rescale O in
+//    TMEM when the running max grows, and write P (bf16) into a 128-B
+//    swizzled shared-memory tile that the next MMA reads as its A operand.
+//    The same online-softmax recurrence as flash_attention2_forward
+//    (nn/attention/flash_attn2.rs:98-140), over 128-key tiles instead of one
+//    key at a time, plus the causal mask and GQA head mapping.
+//  * attn_decode_kernel: decode against a KV cache (few queries, long
+//    context).  Split over the context; the last CTA of a (batch, kv-head)
+//    group merges the partial (max, sum, output) triples.
+//  * attn_f32_kernel: exact f32 path (fixtures, fp32 configurations).
+#include <math.h>
+
+#include "common.cuh"
+#include "attention.h"
+
+namespace tb {
+
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm volatile("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+template <int D>
+struct AttnCfg {
+    static constexpr int BM = 128, BN = 128;
+    static constexpr int TILE = 128 * D * 2;           // Q, K or V tile bytes
+    static constexpr int P_BYTES = 128 * 128 * 2;
+    static constexpr int SMEM = TILE /*Q*/ + 2 * TILE /*K*/ + 2 * TILE /*V*/ + P_BYTES + 1024 + 256;
+    static constexpr int O_COL = 256;                  // TMEM columns: S0 [0,128), S1 [128,256), O
+};
+
+template <int D>
+__global__ void __launch_bounds__(192, 1)
+attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+               const __grid_constant__ CUtensorMap tmV, AttnOut out, int Hq, int Hkv, int Sq, int Sk,
+               float scale_log2, int causal, int* err) {
+    using C = AttnCfg<D>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sQ = smem;
+    uint8_t* sK = sQ + C::TILE;
+    uint8_t* sV = sK + 2 * C::TILE;
+    uint8_t* sP = sV + 2 * C::TILE;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sP + C::P_BYTES);
+    const uint32_t q_full = smem_u32(bars + 0);
+    const uint32_t k_full0 = smem_u32(bars + 1);     // [2]
+    const uint32_t v_full0 = smem_u32(bars + 3);     // [2]
+    const uint32_t kv_empty0 = smem_u32(bars + 5);   // [2]
+    const uint32_t s_full0 = smem_u32(bars + 7);     // [2]
+    const uint32_t p_full = smem_u32(bars + 9);
+    const uint32_t o_done = smem_u32(bars + 10);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+
+    const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+    const int q_tile = gridDim.x - 1 - blockIdx.x;   // heaviest causal tiles first
+    const int h = blockIdx.y, b = blockIdx.z;
+    const int hk = h / (Hq / Hkv);
+    const int q0 = q_tile * C::BM;
+    const int diag = Sk - Sq;                         // causal: key j visible to query i iff j <= i + diag
+    int n_tiles = (Sk + C::BN - 1) / C::BN;
+    if (causal) {
+        int last_key = q0 + C::BM - 1 + diag;
+        int nt_c = last_key < 0 ? 0 : last_key / C::BN + 1;
+        n_tiles = min(n_tiles, nt_c);
+    }
+    constexpr int DB = D / 64;                        // 64-wide d blocks per tile
+
+    if (threadIdx.x == 0) {
+        mbar_init(q_full, 1);
+        for (int s = 0; s < 2; s++) {
+            mbar_init(k_full0 + 8 * s, 1);
+            mbar_init(v_full0 + 8 * s, 1);
+            mbar_init(kv_empty0 + 8 * s, 1);
+            mbar_init(s_full0 + 8 * s, 1);
+        }
+        mbar_init(p_full, 128);
+        mbar_init(o_done, 1);
+        fence_barrier_init();
+    }
+    if (warp == 1) tmem_alloc(smem_u32(tmem_slot), 512);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0 && n_tiles > 0) {
+            tma_prefetch_desc(&tmQ);
+            tma_prefetch_desc(&tmK);
+            tma_prefetch_desc(&tmV);
+            mbar_expect_tx(q_full, C::TILE);
+            for (int d = 0; d < DB; d++) tma_load_4d(smem_u32(sQ + d * 16384), &tmQ, q_full, 64 * d, h, q0, b);
+            int issued = 0;
+            for (int j = 0; j < n_tiles; j++) {
+                int st = j & 1;
+                if (j >= 2 && !mbar_wait(kv_empty0 + 8 * st, ((j >> 1) - 1) & 1, err, DEV_ERR_TIMEOUT_EMPTY)) break;
+                mbar_expect_tx(k_full0 + 8 * st, C::TILE);
+                for (int d = 0; d < DB; d++)
+                    tma_load_4d(smem_u32(sK + st * C::TILE + d * 16384), &tmK, k_full0 + 8 * st, 64 * d, hk, j * C::BN, b);
+                mbar_expect_tx(v_full0 + 8 * st, C::TILE);
+                for (int d = 0; d < DB; d++)
+                    tma_load_4d(smem_u32(sV + st * C::TILE + d * 16384), &tmV, v_full0 + 8 * st, 64 * d, hk, j * C::BN, b);
+                issued = j + 1;
+            }
+            mbar_wait(q_full, 0, err, DEV_ERR_TIMEOUT_FULL);
+            for (int j = (issued > 2 ? issued - 2 : 0); j < issued; j++) {
+                mbar_wait(k_full0 + 8 * (j & 1), (j >> 1) & 1, err, DEV_ERR_TIMEOUT_FULL);
+                mbar_wait(v_full0 + 8 * (j & 1), (j >> 1) & 1, err, DEV_ERR_TIMEOUT_FULL);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && n_tiles > 0) {
+            constexpr uint32_t idesc_s = idesc_bf16_f32(128, C::BN, false, false);
+            constexpr uint32_t idesc_o = idesc_bf16_f32(128, D, false, true);
+            const uint32_t q_base = smem_u32(sQ), p_base = smem_u32(sP);
+            bool ok = mbar_wait(q_full, 0, err, DEV_ERR_TIMEOUT_FULL);
+            for (int j = 0; ok && j <= n_tiles; j++) {
+                if (j < n_tiles) {
+                    int st = j & 1;
+                    if (!mbar_wait(k_full0 + 8 * st, (j >> 1) & 1, err, DEV_ERR_TIMEOUT_FULL)) break;
+                    tc_fence_after();
+                    const uint32_t k_base = smem_u32(sK + st * C::TILE);
+#pragma unroll
+                    for (int kk = 0; kk < D / 16; kk++) {
+                        uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+                        umma_f16_ss(tmem + st * 128, sdesc_sw128(q_base + off, 16, 1024),
+                                    sdesc_sw128(k_base + off, 16, 1024), idesc_s, kk != 0);
+                    }
+                    umma_commit(s_full0 + 8 * st);
+                }
+                if (j > 0) {
+                    const int jp = j - 1, st = jp & 1;
+                    if (!mbar_wait(p_full, jp & 1, err, DEV_ERR_TIMEOUT_MISC)) break;
+                    if (!mbar_wait(v_full0 + 8 * st, (jp >> 1) & 1, err, DEV_ERR_TIMEOUT_FULL)) break;
+                    tc_fence_after();
+                    const uint32_t v_base = smem_u32(sV + st * C::TILE);
+#pragma unroll
+                    for (int kk = 0; kk < C::BN / 16; kk++) {
+                        uint64_t ad = sdesc_sw128(p_base + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
+                        uint64_t bd = sdesc_sw128(v_base + kk * 16 * 128, 16384, 1024);
+                        umma_f16_ss(tmem + C::O_COL, ad, bd, idesc_o, (jp | kk) != 0);
+                    }
+                    umma_commit(kv_empty0 + 8 * st);
+                    umma_commit(o_done);
+                }
+            }
+        }
+    } else {
+        // ---------------- softmax warps 2..5: thread <-> query row
+        const int quarter = warp & 3;
+        const int r = quarter * 32 + lane;
+        const int qi = q0 + r;
+        const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
+        float m_run = -INFINITY, l_run = 0.f;
+        bool ok = true;
+        for (int j = 0; j < n_tiles; j++) {
+            const int sb = j & 1;
+            ok = mbar_wait(s_full0 + 8 * sb, (j >> 1) & 1, err, DEV_ERR_TIMEOUT_MISC);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) break;
+            tc_fence_after();
+            float s[128];
+#pragma unroll
+            for (int c = 0; c < 4; c++) tmem_ld32(t_lane + sb * 128 + c * 32, s + c * 32);
+            tmem_wait_ld();
+            const int k0 = j * C::BN;
+            const int lim = causal ? min(Sk - 1, qi + diag) : Sk - 1;   // last visible key
+            float mx = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < 128; c++) {
+                float v = (k0 + c <= lim) ? s[c] * scale_log2 : -INFINITY;
+                s[c] = v;
+                mx = fmaxf(mx, v);
+            }
+            const float m_new = fmaxf(m_run, mx);
+            const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+            const float alpha = ex2(m_run - m_use);   // m_run = -inf -> 0
+            float rs = 0.f;
+#pragma unroll
+            for (int c = 0; c < 128; c++) {
+                float p = ex2(s[c] - m_use);
+                s[c] = p;
+                rs += p;
+            }
+            l_run = l_run * alpha + rs;
+            m_run = m_new;
+            if (j > 0) {
+                ok = __all_sync(0xffffffffu, mbar_wait(o_done, (j - 1) & 1, err, DEV_ERR_TIMEOUT_MISC));
+                if (!ok) break;
+                tc_fence_after();
+                if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+#pragma unroll 1
+                    for (int c = 0; c < D; c += 16) {
+                        float o[16];
+                        tmem_ld16(t_lane + C::O_COL + c, o);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 16; i++) o[i] *= alpha;
+                        tmem_st16(t_lane + C::O_COL + c, o);
+                    }
+                    tmem_wait_st();
+                }
+            }
+            // P row -> shared memory, 128-B swizzled K-major (keys) tile
+            uint8_t* prow = sP + r * 128;
+#pragma unroll
+            for (int ch = 0; ch < 16; ch++) {
+                const int kc = ch >> 3, c8 = ch & 7;
+                uint4 v;
+                v.x = pack_bf16x2(s[ch * 8 + 0], s[ch * 8 + 1]);
+                v.y = pack_bf16x2(s[ch * 8 + 2], s[ch * 8 + 3]);
+                v.z = pack_bf16x2(s[ch * 8 + 4], s[ch * 8 + 5]);
+                v.w = pack_bf16x2(s[ch * 8 + 6], s[ch * 8 + 7]);
+                *reinterpret_cast<uint4*>(prow + kc * 16384 + ((c8 ^ (r & 7)) << 4)) = v;
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            tc_fence_before();
+            mbar_arrive(p_full);
+        }
+        if (ok && n_tiles > 0) {
+            ok = __all_sync(0xffffffffu, mbar_wait(o_done, (n_tiles - 1) & 1, err, DEV_ERR_TIMEOUT_ACC));
+        }
+        if (ok) {
+            tc_fence_after();
+            const float inv_l = (l_run > 0.f) ? 1.0f / l_run : 0.f;
+            const bool valid = qi < Sq;
+            const int64_t obase = (int64_t)b * out.o_sb + (int64_t)h * out.o_sh + (int64_t)qi * out.o_ss;
+#pragma unroll 1
+            for (int c = 0; c < D; c += 32) {
+                float o[32];
+                if (n_tiles > 0) {
+                    tmem_ld32(t_lane + C::O_COL + c, o);
+                    tmem_wait_ld();
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 32; i++) o[i] = 0.f;
+                }
+                if (valid) {
+                    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(out.o) + obase + c;
+#pragma unroll
+                    for (int i = 0; i < 32; i += 8) {
+                        uint4 v;
+                        v.x = pack_bf16x2(o[i] * inv_l, o[i + 1] * inv_l);
+                        v.y = pack_bf16x2(o[i + 2] * inv_l, o[i + 3] * inv_l);
+                        v.z = pack_bf16x2(o[i + 4] * inv_l, o[i + 5] * inv_l);
+                        v.w = pack_bf16x2(o[i + 6] * inv_l, o[i + 7] * inv_l);
+                        *reinterpret_cast<uint4*>(dst + i) = v;
+                    }
+                }
+            }
+            if (valid && out.lse) {
+                float lse = (l_run > 0.f) ? (m_run + log2f(l_run)) * kLn2 : -INFINITY;
+                out.lse[((int64_t)b * Hq + h) * Sq + qi] = lse;
+            }
+        }
+    }
+    __syncwarp();
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
+// -------------------------------------------------------------- decode -----
+// Grid (B * Hkv, splits).  Each CTA (128 threads) handles keys
+// [split * chunk, ...) for the G = Hq / Hkv query heads that share one kv
+// head, 64 keys at a time staged in shared memory.  Partials (running max m,
+// sum l, unnormalised o) go to ws; the last CTA of the group merges them.
+// Supports D = 64 or 128, G <= 8, Sq = 1 per sequence.
+template <int D>
+__global__ void __launch_bounds__(128)
+attn_decode_kernel(DecodeArgs a, int* err) {
+    constexpr int KC = 64;             // keys per staged sub-chunk
+    constexpr int RS = D + 8;          // padded smem row (bf16) against bank conflicts
+    __shared__ __align__(16) __nv_bfloat16 sk[KC * RS];
+    __shared__ __align__(16) __nv_bfloat16 sv[KC * RS];
+    __shared__ float sq[8][D];
+    __shared__ float sp[8][KC];
+    __shared__ float s_m[8], s_l[8], s_alpha[8];
+    __shared__ int s_last;
+
+    const int G = a.Hq / a.Hkv;
+    const int bg = blockIdx.x, split = blockIdx.y;
+    const int b = bg / a.Hkv, g = bg % a.Hkv;
+    const int L = a.len_ptr ? *a.len_ptr : a.len;
+    const int kbeg = split * a.chunk;
+    const int kend = min(L, kbeg + a.chunk);
+    const int tid = threadIdx.x;
+
+    // queries of this group -> smem (f32, pre-scaled into the exp2 domain)
+    for (int i = tid; i < G * D; i += 128) {
+        int gg = i / D, d = i % D;
+        const __nv_bfloat16* qp = a.q + (int64_t)b * a.q_sb + (int64_t)(g * G + gg) * a.q_sh + d;
+        sq[gg][d] = __bfloat162float(*qp) * a.scale_log2;
+    }
+    if (tid < 8) {
+        s_m[tid] = -INFINITY;
+        s_l[tid] = 0.f;
+    }
+    // each thread owns output elements (gg, d) for idx = tid + 128 * i
+    constexpr int OPT = (8 * D) / 128;
+    float acc[OPT];
+#pragma unroll
+    for (int i = 0; i < OPT; i++) acc[i] = 0.f;
+    __syncthreads();
+
+    const __nv_bfloat16* kbase = a.k + (int64_t)b * a.kv_sb + (int64_t)g * a.kv_sh;
+    const __nv_bfloat16* vbase = a.v + (int64_t)b * a.kv_sb + (int64_t)g * a.kv_sh;
+    for (int k0 = kbeg; k0 < kend; k0 += KC) {
+        const int nk = min(KC, kend - k0);
+        // stage K and V rows (16 B per thread per step)
+        constexpr int CPR = D / 8;   // 16-B chunks per row
+        for (int i = tid; i < KC * CPR; i += 128) {
+            int r = i / CPR, c = i % CPR;
+            uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
+            if (r < nk) {
+                kv = *reinterpret_cast<const uint4*>(kbase + (int64_t)(k0 + r) * a.kv_ss + c * 8);
+                vv = *reinterpret_cast<const uint4*>(vbase + (int64_t)(k0 + r) * a.kv_ss + c * 8);
+            }
+            *reinterpret_cast<uint4*>(&sk[r * RS + c * 8]) = kv;
+            *reinterpret_cast<uint4*>(&sv[r * RS + c * 8]) = vv;
+        }
+        __syncthreads();
+        // scores: G x KC dot products
+        for (int i = tid; i < G * KC; i += 128) {
+            int gg = i / KC, r = i % KC;
+            float sacc = -INFINITY;
+            if (r < nk) {
+                sacc = 0.f;
+                const __nv_bfloat16* kr = &sk[r * RS];
+#pragma unroll 8
+                for (int d = 0; d < D; d += 2) {
+                    __nv_bfloat162 kk = *reinterpret_cast<const __nv_bfloat162*>(kr + d);
+                    sacc = fmaf(sq[gg][d], __low2float(kk), sacc);
+                    sacc = fmaf(sq[gg][d + 1], __high2float(kk), sacc);
+                }
+            }
+            sp[gg][r] = sacc;
+        }
+        __syncthreads();
+        // per-head max / exp / sum: warp w handles heads w, w+4
+        {
+            const int w = tid / 32, ln = tid & 31;
+            for (int gg = w; gg < G; gg += 4) {
+                float v0 = sp[gg][ln], v1 = sp[gg][ln + 32];
+                float mx = fmaxf(v0, v1);
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+                float m_old = s_m[gg];
+                float m_new = fmaxf(m_old, mx);
+                float p0 = ex2(v0 - m_new), p1 = ex2(v1 - m_new);
+                sp[gg][ln] = p0;
+                sp[gg][ln + 32] = p1;
+                float sum = p0 + p1;
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+                if (ln == 0) {
+                    float al = ex2(m_old - m_new);
+                    s_alpha[gg] = al;
+                    s_l[gg] = s_l[gg] * al + sum;
+                    s_m[gg] = m_new;
+                }
+            }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int i = 0; i < OPT; i++) {
+            int idx = tid + 128 * i;
+            int gg = idx / D, d = idx % D;
+            if (gg < G) {
+                float o = acc[i] * s_alpha[gg];
+                for (int r = 0; r < nk; r++) o = fmaf(sp[gg][r], __bfloat162float(sv[r * RS + d]), o);
+                acc[i] = o;
+            }
+        }
+        __syncthreads();
+    }
+
+    // partials -> ws[(bg * splits + split)][G][D + 2]
+    const int stride = D + 2;
+    float* wp = a.ws + ((int64_t)bg * gridDim.y + split) * 8 * stride;
+#pragma unroll
+    for (int i = 0; i < OPT; i++) {
+        int idx = tid + 128 * i;
+        int gg = idx / D, d = idx % D;
+        if (gg < G) wp[gg * stride + d] = acc[i];
+    }
+    if (tid < G) {
+        wp[tid * stride + D] = s_m[tid];
+        wp[tid * stride + D + 1] = s_l[tid];
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_last = (atomicAdd(&a.counters[bg], 1u) == gridDim.y - 1);
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    // merge
+    const int nsp = gridDim.y;
+    for (int idx = tid; idx < G * D; idx += 128) {
+        int gg = idx / D, d = idx % D;
+        float M = -INFINITY;
+        for (int sp_i = 0; sp_i < nsp; sp_i++) {
+            const float* p = a.ws + ((int64_t)bg * nsp + sp_i) * 8 * stride + gg * stride;
+            M = fmaxf(M, __ldcg(p + D));
+        }
+        float l = 0.f, o = 0.f;
+        for (int sp_i = 0; sp_i < nsp; sp_i++) {
+            const float* p = a.ws + ((int64_t)bg * nsp + sp_i) * 8 * stride + gg * stride;
+            float mi = __ldcg(p + D);
+            float w = (mi == -INFINITY) ? 0.f : ex2(mi - M);
+            l += __ldcg(p + D + 1) * w;
+            o += __ldcg(p + d) * w;
+        }
+        float r = l > 0.f ? o / l : 0.f;
+        a.o[(int64_t)b * a.o_sb + (int64_t)(g * G + gg) * a.o_sh + d] = __float2bfloat16_rn(r);
+        if (d == 0 && a.lse) a.lse[(int64_t)b * a.Hq + g * G + gg] = l > 0.f ? (M + log2f(l)) * kLn2 : -INFINITY;
+    }
+    if (tid == 0) a.counters[bg] = 0u;
+}
+
+// ---------------------------------------------------------------- f32 ------
+// One warp per query row, exact f32 two-pass softmax over visible keys.
+__global__ void attn_f32_kernel(const float* __restrict__ q, const float* __restrict__ k,
+                                const float* __restrict__ v, float* __restrict__ o, float* __restrict__ lse,
+                                int B, int Hq, int Hkv, int Sq, int Sk, int D, float scale, int causal) {
+    int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    int lane = threadIdx.x & 31;
+    if (row >= (int64_t)B * Hq * Sq) return;
+    int i = (int)(row % Sq);
+    int64_t bh = row / Sq;
+    int h = (int)(bh % Hq), b = (int)(bh / Hq);
+    int hk = h / (Hq / Hkv);
+    const float* qr = q + row * D;
+    const float* kb = k + ((int64_t)b * Hkv + hk) * Sk * D;
+    const float* vb = v + ((int64_t)b * Hkv + hk) * Sk * D;
+    int jmax = causal ? min(Sk - 1, i + (Sk - Sq)) : Sk - 1;
+    float qv[4];
+    for (int t = 0; t < 4; t++) qv[t] = (lane + 32 * t < D) ? qr[lane + 32 * t] : 0.f;
+    float m = -INFINITY;
+    for (int j = 0; j <= jmax; j++) {
+        float s = 0.f;
+        for (int t = 0; t < 4; t++)
+            if (lane + 32 * t < D) s = fmaf(qv[t], kb[(int64_t)j * D + lane + 32 * t], s);
+#pragma unroll
+        for (int of = 16; of > 0; of >>= 1) s += __shfl_xor_sync(0xffffffffu, s, of);
+        m = fmaxf(m, s * scale);
+    }
+    float l = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int j = 0; j <= jmax; j++) {
+        float s = 0.f;
+        for (int t = 0; t < 4; t++)
+            if (lane + 32 * t < D) s = fmaf(qv[t], kb[(int64_t)j * D + lane + 32 * t], s);
+#pragma unroll
+        for (int of = 16; of > 0; of >>= 1) s += __shfl_xor_sync(0xffffffffu, s, of);
+        float p = expf(s * scale - m);
+        l += p;
+        for (int t = 0; t < 4; t++)
+            if (lane + 32 * t < D) acc[t] = fmaf(p, vb[(int64_t)j * D + lane + 32 * t], acc[t]);
+    }
+    float* orow = o + row * D;
+    for (int t = 0; t < 4; t++)
+        if (lane + 32 * t < D) orow[lane + 32 * t] = (jmax >= 0) ? acc[t] / l : 0.f;
+    if (lse && lane == 0) lse[row] = (jmax >= 0) ? m + logf(l) : -INFINITY;
+}
+
+// ------------------------------------------------------------ host side ----
+static int tmap_heads(tb_ctx* ctx, CUtensorMap* m, const void* base, int D, int H, int S, int B,
+                      int64_t sh, int64_t ss, int64_t sb) {
+    // dims (d, h, s, b), box (64, 1, 128, 1); strides in elements -> bytes
+    uint64_t dims[4] = {(uint64_t)D, (uint64_t)H, (uint64_t)S, (uint64_t)B};
+    uint64_t strides[3] = {(uint64_t)sh * 2, (uint64_t)ss * 2, (uint64_t)sb * 2};
+    uint32_t box[4] = {64, 1, 128, 1};
+    return make_tmap(ctx, m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, base, dims, strides, box,
+                     CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+int attn_tc_launch(tb_ctx* ctx, const AttnTensors& t, int B, int Hq, int Hkv, int Sq, int Sk, int D,
+                   float scale, int causal) {
+    CUtensorMap mq, mk, mv;
+    int rc = tmap_heads(ctx, &mq, t.q, D, Hq, Sq, B, t.q_sh, t.q_ss, t.q_sb);
+    if (!rc) rc = tmap_heads(ctx, &mk, t.k, D, Hkv, t.kv_len_alloc, B, t.kv_sh, t.kv_ss, t.kv_sb);
+    if (!rc) rc = tmap_heads(ctx, &mv, t.v, D, Hkv, t.kv_len_alloc, B, t.kv_sh, t.kv_ss, t.kv_sb);
+    if (rc) return rc;
+    AttnOut out{t.o, t.o_sh, t.o_ss, t.o_sb, t.lse};
+    dim3 grid((Sq + 127) / 128, Hq, B);
+    const float sl2 = scale * kLog2e;
+    if (D == 64) {
+        // 512 TMEM columns per CTA: keep one CTA per SM (the padding does that).
+        constexpr int smem = AttnCfg<64>::SMEM > 120 * 1024 ? AttnCfg<64>::SMEM : 120 * 1024;
+        TB_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        attn_tc_kernel<64><<<grid, 192, smem, ctx->stream>>>(mq, mk, mv, out, Hq, Hkv, Sq, Sk, sl2, causal, ctx->d_err);
+    } else {
+        constexpr int smem = AttnCfg<128>::SMEM;
+        TB_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        attn_tc_kernel<128><<<grid, 192, smem, ctx->stream>>>(mq, mk, mv, out, Hq, Hkv, Sq, Sk, sl2, causal, ctx->d_err);
+    }
+    return check_launch(ctx, "attn_tc");
+}
+
+int attn_decode_launch(tb_ctx* ctx, DecodeArgs a, int B, int D, int max_len, float* ws, unsigned* counters) {
+    const int groups = B * a.Hkv;
+    int chunk = 256;
+    int splits = (max_len + chunk - 1) / chunk;
+    if (splits < 1) splits = 1;
+    a.chunk = chunk;
+    a.ws = ws;
+    a.counters = counters;
+    dim3 grid(groups, splits);
+    if (D == 64) attn_decode_kernel<64><<<grid, 128, 0, ctx->stream>>>(a, ctx->d_err);
+    else attn_decode_kernel<128><<<grid, 128, 0, ctx->stream>>>(a, ctx->d_err);
+    return check_launch(ctx, "attn_decode");
+}
+
+size_t attn_decode_ws_bytes(int B, int Hkv, int D, int max_len) {
+    int splits = (max_len + 255) / 256;
+    if (splits < 1) splits = 1;
+    return (size_t)B * Hkv * splits * 8 * (D + 2) * sizeof(float);
+}
+
+}  // namespace tb
+
+using namespace tb;
+
+extern "C" int tb_attn_fwd(tb_ctx* ctx, int dtype, const void* q, const void* k, const void* v, void* o,
+                           float* lse, int B, int Hq, int Hkv, int Sq, int Sk, int D, float scale, int causal) {
+    if (!ctx || !q || !k || !v || !o) return TB_ERR_ARG;
+    TB_REQUIRE(ctx, B >= 0 && Hq > 0 && Hkv > 0 && Hq % Hkv == 0 && Sq >= 0 && Sk >= 0 && D > 0,
+               TB_ERR_SHAPE, "attn: bad shape");
+    if (B == 0 || Sq == 0) return TB_OK;
+    if (dtype == TB_F32) {
+        TB_REQUIRE(ctx, D <= 128, TB_ERR_SHAPE, "attn f32: D <= 128");
+        int64_t rows = (int64_t)B * Hq * Sq;
+        attn_f32_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, ctx->stream>>>(
+            (const float*)q, (const float*)k, (const float*)v, (float*)o, lse, B, Hq, Hkv, Sq, Sk, D, scale, causal);
+        return check_launch(ctx, "attn_f32");
+    }
+    if (dtype != TB_BF16) return set_error(ctx, TB_ERR_UNSUPPORTED, "attn: dtype %d", dtype);
+    TB_REQUIRE(ctx, D == 64 || D == 128, TB_ERR_SHAPE, "attn bf16: D must be 64 or 128");
+    TB_REQUIRE(ctx, aligned16(q) && aligned16(k) && aligned16(v) && aligned16(o), TB_ERR_ALIGN, "attn: alignment");
+    if (Sk == 0) return set_error(ctx, TB_ERR_SHAPE, "attn bf16: Sk must be > 0");
+    AttnTensors t{};
+    t.q = q; t.q_sh = (int64_t)Sq * D; t.q_ss = D; t.q_sb = (int64_t)Hq * Sq * D;
+    t.k = k; t.v = v; t.kv_sh = (int64_t)Sk * D; t.kv_ss = D; t.kv_sb = (int64_t)Hkv * Sk * D;
+    t.kv_len_alloc = Sk;
+    t.o = o; t.o_sh = (int64_t)Sq * D; t.o_ss = D; t.o_sb = (int64_t)Hq * Sq * D;
+    t.lse = lse;
+    if (Sq <= 16 && Hq / Hkv <= 8 && Sq == 1) {
+        // single-query decode: split-KV CUDA-core kernel
+        DecodeArgs a{};
+        a.q = (const __nv_bfloat16*)q; a.q_sb = t.q_sb; a.q_sh = t.q_sh;
+        a.k = (const __nv_bfloat16*)k; a.v = (const __nv_bfloat16*)v;
+        a.kv_sb = t.kv_sb; a.kv_sh = t.kv_sh; a.kv_ss = t.kv_ss;
+        a.o = (__nv_bfloat16*)o; a.o_sb = t.o_sb; a.o_sh = t.o_sh;
+        a.lse = lse; a.Hq = Hq; a.Hkv = Hkv; a.len = Sk; a.len_ptr = nullptr;
+        a.scale_log2 = scale * kLog2e;
+        int rc = ensure_workspace(ctx, attn_decode_ws_bytes(B, Hkv, D, Sk), (size_t)B * Hkv);
+        if (rc) return rc;
+        return attn_decode_launch(ctx, a, B, D, Sk, (float*)ctx->ws, ctx->counters);
+    }
+    return attn_tc_launch(ctx, t, B, Hq, Hkv, Sq, Sk, D, scale, causal);
+}

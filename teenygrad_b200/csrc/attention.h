@@ -1,0 +1,54 @@
+// Internal attention launch interface shared with the decoder executor.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "tb_internal.h"
+
+namespace tb {
+
+// Output addressing: element (b, h, s, d) of O lives at b*o_sb + h*o_sh + s*o_ss + d.
+struct AttnOut {
+    void* o;
+    int64_t o_sh, o_ss, o_sb;
+    float* lse;   // [B, Hq, Sq] or null
+};
+
+// Strides in elements; d is always contiguous.
+struct AttnTensors {
+    const void* q;
+    int64_t q_sh, q_ss, q_sb;
+    const void* k;
+    const void* v;
+    int64_t kv_sh, kv_ss, kv_sb;
+    int kv_len_alloc;   // rows addressable along s (the cache capacity)
+    void* o;
+    int64_t o_sh, o_ss, o_sb;
+    float* lse;
+};
+
+struct DecodeArgs {
+    const __nv_bfloat16* q;
+    int64_t q_sb, q_sh;
+    const __nv_bfloat16* k;
+    const __nv_bfloat16* v;
+    int64_t kv_sb, kv_sh, kv_ss;
+    __nv_bfloat16* o;
+    int64_t o_sb, o_sh;
+    float* lse;
+    int Hq, Hkv;
+    int len;               // context length if len_ptr is null
+    const int* len_ptr;    // device-resident context length (CUDA-graph replay)
+    float scale_log2;
+    int chunk;
+    float* ws;
+    unsigned* counters;
+};
+
+int attn_tc_launch(tb_ctx* ctx, const AttnTensors& t, int B, int Hq, int Hkv, int Sq, int Sk, int D,
+                   float scale, int causal);
+int attn_decode_launch(tb_ctx* ctx, DecodeArgs a, int B, int D, int max_len, float* ws, unsigned* counters);
+size_t attn_decode_ws_bytes(int B, int Hkv, int D, int max_len);
+
+}  // namespace tb

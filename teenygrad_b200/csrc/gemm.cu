@@ -1,0 +1,676 @@
+// Linear layers on B200.
+//
+//  * gemm_tc_kernel: y[M,N] = x[M,K] w[N,K]^T for prefill-sized M.  One CTA
+//    per 128 x BN output tile; warp 0 streams K-blocks of 64 with TMA (128-B
+//    swizzle) into a STAGES-deep ring, warp 1 issues tcgen05.mma (M=128, N=BN,
+//    K=16, f32 accumulator in TMEM), all 8 warps run the fused epilogue
+//    (bias, residual, SwiGLU, bf16/f32 store) straight out of TMEM.
+//  * gemv_tc_kernel: decode-sized M (<= 64 tokens).  Swap-AB: the weight rows
+//    are the MMA's M dimension (two 128-row halves per CTA), the tokens its N.
+//    K is split across CTAs; the last CTA of a tile reduces the partials and
+//    runs the epilogue.  Weights are bf16, or int8 converted to bf16 in shared
+//    memory by six converter warps (exact: |q| <= 127).
+//  * linear_f32_kernel / matmul_f32_kernel: exact-f32 CUDA-core tiles for the
+//    fp32 configurations (the reference's TF32 dot, linear.rs:86, misses the
+//    1e-4 fp32 tolerance at K >= 256).
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace tb {
+
+struct Epi {
+    void* out;             // y
+    int64_t ldo;           // row stride of y (elements)
+    const float* bias;     // [N] or null
+    const void* resid;     // [M, N] same dtype as y, or null
+    int64_t ldr;
+    const float* scale;    // int8 per-output-channel scale, or null
+    int out_f32;           // y is f32
+    int swiglu;            // gate/up interleaved in 128-row blocks
+};
+
+// ------------------------------------------------------------ store helpers --
+__device__ __forceinline__ void store_row8(void* out, bool f32, int64_t off, const float* v) {
+    if (f32) {
+        float4* p = reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + off);
+        p[0] = make_float4(v[0], v[1], v[2], v[3]);
+        p[1] = make_float4(v[4], v[5], v[6], v[7]);
+    } else {
+        uint4 a;
+        a.x = pack_bf16x2(v[0], v[1]);
+        a.y = pack_bf16x2(v[2], v[3]);
+        a.z = pack_bf16x2(v[4], v[5]);
+        a.w = pack_bf16x2(v[6], v[7]);
+        *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(out) + off) = a;
+    }
+}
+
+__device__ __forceinline__ void load_row8(const void* p, bool f32, int64_t off, float* v) {
+    if (f32) {
+        const float4* q = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p) + off);
+        float4 a = q[0], b = q[1];
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+        v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    } else {
+        uint4 a = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(p) + off);
+        uint32_t w[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            v[2 * i] = bf16_lo(w[i]);
+            v[2 * i + 1] = bf16_hi(w[i]);
+        }
+    }
+}
+
+// =====================================================================
+// Prefill GEMM
+// =====================================================================
+constexpr int GEMM_BM = 128;
+constexpr int GEMM_BK = 64;
+
+template <int BN, int STAGES>
+constexpr int gemm_smem_bytes() {
+    return STAGES * (GEMM_BM * 128 + BN * 128) + 1024 /*align*/ + 256 /*barriers*/;
+}
+
+// B_MN: b operand stored [K, N] (N contiguous), as matmul_forward's B.
+template <int BN, int STAGES, bool B_MN>
+__global__ void __launch_bounds__(256, 1)
+gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+               Epi ep, int M, int N, int K, int* err) {
+    constexpr int A_BYTES = GEMM_BM * 128;
+    constexpr int B_BYTES = BN * 128;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + STAGES * A_BYTES;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+    uint32_t full0 = smem_u32(bars);
+    uint32_t empty0 = smem_u32(bars + STAGES);
+    uint32_t accb = smem_u32(bars + 2 * STAGES);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 1);
+
+    const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.y * GEMM_BM, n0 = blockIdx.x * BN;
+    const int nk = (K + GEMM_BK - 1) / GEMM_BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; s++) {
+            mbar_init(full0 + 8 * s, 1);
+            mbar_init(empty0 + 8 * s, 1);
+        }
+        mbar_init(accb, 1);
+        fence_barrier_init();
+    }
+    if (warp == 1) tmem_alloc(smem_u32(tmem_slot), BN);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0 && lane == 0) {
+        // ---------------- TMA producer
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+        int issued = 0;
+        for (int kb = 0; kb < nk; kb++) {
+            int s = kb % STAGES;
+            if (kb >= STAGES && !mbar_wait(empty0 + 8 * s, ((kb / STAGES) - 1) & 1, err, DEV_ERR_TIMEOUT_EMPTY)) break;
+            mbar_expect_tx(full0 + 8 * s, A_BYTES + B_BYTES);
+            tma_load_2d(smem_u32(sA + s * A_BYTES), &tmA, full0 + 8 * s, kb * GEMM_BK, m0);
+            if (!B_MN) {
+                tma_load_2d(smem_u32(sB + s * B_BYTES), &tmB, full0 + 8 * s, kb * GEMM_BK, n0);
+            } else {
+#pragma unroll
+                for (int j = 0; j < BN / 64; j++)
+                    tma_load_2d(smem_u32(sB + s * B_BYTES + j * 64 * 128), &tmB, full0 + 8 * s, n0 + 64 * j, kb * GEMM_BK);
+            }
+            issued = kb + 1;
+        }
+        // Drain: every issued stage must have landed before the CTA can exit.
+        for (int kb = (issued > STAGES ? issued - STAGES : 0); kb < issued; kb++)
+            mbar_wait(full0 + 8 * (kb % STAGES), (kb / STAGES) & 1, err, DEV_ERR_TIMEOUT_FULL);
+    } else if (warp == 1 && lane == 0) {
+        // ---------------- MMA issuer
+        constexpr uint32_t idesc = idesc_bf16_f32(GEMM_BM, BN, false, B_MN);
+        for (int kb = 0; kb < nk; kb++) {
+            int s = kb % STAGES;
+            if (!mbar_wait(full0 + 8 * s, (kb / STAGES) & 1, err, DEV_ERR_TIMEOUT_FULL)) break;
+            tc_fence_after();
+            uint32_t a_base = smem_u32(sA + s * A_BYTES);
+            uint32_t b_base = smem_u32(sB + s * B_BYTES);
+#pragma unroll
+            for (int kk = 0; kk < GEMM_BK / 16; kk++) {
+                uint64_t ad = sdesc_sw128(a_base + kk * 32, 16, 1024);
+                uint64_t bd = B_MN ? sdesc_sw128(b_base + kk * 16 * 128, 64 * 128, 1024)
+                                   : sdesc_sw128(b_base + kk * 32, 16, 1024);
+                umma_f16_ss(tmem, ad, bd, idesc, (kb | kk) != 0);
+            }
+            umma_commit(empty0 + 8 * s);
+        }
+        umma_commit(accb);
+    }
+    __syncwarp();
+
+    // ---------------- epilogue: warp w reads TMEM lanes 32*(w%4).., column half w/4
+    bool ok = mbar_wait(accb, 0, err, DEV_ERR_TIMEOUT_ACC);
+    __syncwarp();
+    tc_fence_after();
+    const int q = warp & 3, half = warp >> 2;
+    const int row = m0 + q * 32 + lane;
+    const uint32_t t_row = tmem + ((uint32_t)(q * 32) << 16);
+    const bool f32o = ep.out_f32 != 0;
+    if (ok) {
+        if (!ep.swiglu) {
+#pragma unroll 1
+            for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 32) {
+                float v[32];
+                tmem_ld32(t_row + c, v);
+                tmem_wait_ld();
+                const int col0 = n0 + c;
+                if (row < M) {
+#pragma unroll
+                    for (int j = 0; j < 32; j += 8) {
+                        int col = col0 + j;
+                        if (col < N) {
+                            if (ep.bias) {
+#pragma unroll
+                                for (int i = 0; i < 8; i++) v[j + i] += ep.bias[col + i];
+                            }
+                            if (ep.resid) {
+                                float r[8];
+                                load_row8(ep.resid, f32o, (int64_t)row * ep.ldr + col, r);
+#pragma unroll
+                                for (int i = 0; i < 8; i++) v[j + i] += r[i];
+                            }
+                            store_row8(ep.out, f32o, (int64_t)row * ep.ldo + col, v + j);
+                        }
+                    }
+                }
+            }
+        } else {
+            // tile columns [0,128) = gate rows, [128,256) = up rows of the same outputs
+#pragma unroll 1
+            for (int c = half * 64; c < half * 64 + 64; c += 32) {
+                float g[32], u[32];
+                tmem_ld32(t_row + c, g);
+                tmem_ld32(t_row + 128 + c, u);
+                tmem_wait_ld();
+                const int ocol0 = n0 / 2 + c;
+                if (row < M) {
+#pragma unroll
+                    for (int j = 0; j < 32; j += 8) {
+                        float o[8];
+#pragma unroll
+                        for (int i = 0; i < 8; i++) o[i] = silu_f(g[j + i]) * u[j + i];
+                        if (ocol0 + j < N / 2) store_row8(ep.out, f32o, (int64_t)row * ep.ldo + ocol0 + j, o);
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) tmem_dealloc(tmem, BN);
+}
+
+// =====================================================================
+// Decode GEMV (swap-AB, split-K)
+// =====================================================================
+template <int NT, int STAGES, bool INT8>
+struct GemvCfg {
+    static constexpr int W_BYTES = INT8 ? 256 * 64 : 256 * 128;  // int8: 64 K per row, no swizzle
+    static constexpr int X_BYTES = NT * 128;
+    static constexpr int C_STAGES = INT8 ? 2 : 0;                 // converted bf16 ring
+    static constexpr int C_BYTES = 256 * 128;
+    static constexpr int SMEM = STAGES * (W_BYTES + X_BYTES) + C_STAGES * C_BYTES + 1024 + 512;
+    static constexpr int TMEM_COLS = (2 * NT) < 32 ? 32 : (2 * NT);
+};
+
+template <int NT, int STAGES, bool INT8>
+__global__ void __launch_bounds__(256, 1)
+gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
+               Epi ep, int Nw, int K, int Mtok, int kb_per_split, int splits, float* ws,
+               unsigned* counters, int* err) {
+    using C = GemvCfg<NT, STAGES, INT8>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sC = smem;                                   // converted bf16 ring (int8 only)
+    uint8_t* sW = sC + C::C_STAGES * C::C_BYTES;
+    uint8_t* sX = sW + STAGES * C::W_BYTES;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sX + STAGES * C::X_BYTES);
+    const uint32_t full0 = smem_u32(bars);
+    const uint32_t empty0 = smem_u32(bars + STAGES);
+    const uint32_t cfull0 = smem_u32(bars + 2 * STAGES);
+    const uint32_t cempty0 = smem_u32(bars + 2 * STAGES + 2);
+    const uint32_t accb = smem_u32(bars + 2 * STAGES + 4);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+    int* s_last = reinterpret_cast<int*>(bars + 2 * STAGES + 6);
+
+    const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+    const int tile = blockIdx.x, split = blockIdx.y;
+    const int nk_total = (K + 63) / 64;
+    const int kb0 = split * kb_per_split;
+    const int kb1 = min(nk_total, kb0 + kb_per_split);
+    const int nk = kb1 - kb0;
+    constexpr int N_CONV_WARPS = 6;   // warps 2..7
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; s++) {
+            mbar_init(full0 + 8 * s, 1);
+            mbar_init(empty0 + 8 * s, INT8 ? 1 + N_CONV_WARPS : 1);
+        }
+        for (int s = 0; s < 2; s++) {
+            mbar_init(cfull0 + 8 * s, N_CONV_WARPS);
+            mbar_init(cempty0 + 8 * s, 1);
+        }
+        mbar_init(accb, 1);
+        fence_barrier_init();
+    }
+    if (warp == 1) tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tmW);
+        tma_prefetch_desc(&tmX);
+        int issued = 0;
+        for (int i = 0; i < nk; i++) {
+            int s = i % STAGES;
+            if (i >= STAGES && !mbar_wait(empty0 + 8 * s, ((i / STAGES) - 1) & 1, err, DEV_ERR_TIMEOUT_EMPTY)) break;
+            mbar_expect_tx(full0 + 8 * s, C::W_BYTES + C::X_BYTES);
+            int kcoord = (kb0 + i) * 64;
+            tma_load_2d(smem_u32(sW + s * C::W_BYTES), &tmW, full0 + 8 * s, kcoord, tile * 256);
+            tma_load_2d(smem_u32(sX + s * C::X_BYTES), &tmX, full0 + 8 * s, kcoord, 0);
+            issued = i + 1;
+        }
+        for (int i = (issued > STAGES ? issued - STAGES : 0); i < issued; i++)
+            mbar_wait(full0 + 8 * (i % STAGES), (i / STAGES) & 1, err, DEV_ERR_TIMEOUT_FULL);
+    } else if (warp == 1 && lane == 0) {
+        constexpr uint32_t idesc = idesc_bf16_f32(128, NT, false, false);
+        for (int i = 0; i < nk; i++) {
+            int s = i % STAGES;
+            uint32_t w_base;
+            if (INT8) {
+                int c = i & 1;
+                if (!mbar_wait(cfull0 + 8 * c, (i >> 1) & 1, err, DEV_ERR_TIMEOUT_MISC)) break;
+                if (!mbar_wait(full0 + 8 * s, (i / STAGES) & 1, err, DEV_ERR_TIMEOUT_FULL)) break;
+                w_base = smem_u32(sC + c * C::C_BYTES);
+            } else {
+                if (!mbar_wait(full0 + 8 * s, (i / STAGES) & 1, err, DEV_ERR_TIMEOUT_FULL)) break;
+                w_base = smem_u32(sW + s * C::W_BYTES);
+            }
+            tc_fence_after();
+            uint32_t x_base = smem_u32(sX + s * C::X_BYTES);
+#pragma unroll
+            for (int kk = 0; kk < 4; kk++) {
+                uint64_t bd = sdesc_sw128(x_base + kk * 32, 16, 1024);
+#pragma unroll
+                for (int h = 0; h < 2; h++) {
+                    uint64_t ad = sdesc_sw128(w_base + h * 128 * 128 + kk * 32, 16, 1024);
+                    umma_f16_ss(tmem + h * NT, ad, bd, idesc, (i | kk) != 0);
+                }
+            }
+            if (INT8) umma_commit(cempty0 + 8 * (i & 1));
+            umma_commit(empty0 + 8 * s);
+        }
+        umma_commit(accb);
+    } else if (INT8 && warp >= 2) {
+        // ---------------- int8 -> bf16 converters (warps 2..7)
+        const int ct = threadIdx.x - 64;   // 0..191
+        for (int i = 0; i < nk; i++) {
+            int s = i % STAGES, c = i & 1;
+            bool ok1 = mbar_wait(full0 + 8 * s, (i / STAGES) & 1, err, DEV_ERR_TIMEOUT_FULL);
+            bool ok2 = i < 2 || mbar_wait(cempty0 + 8 * c, ((i >> 1) - 1) & 1, err, DEV_ERR_TIMEOUT_MISC);
+            if (!ok1 || !ok2) break;
+            const uint8_t* src = sW + s * C::W_BYTES;   // [256 rows][64 B], unswizzled
+            uint8_t* dst = sC + c * C::C_BYTES;          // [256 rows][128 B], 128-B swizzle
+            for (int it = ct; it < 256 * 4; it += 192) {
+                int r = it >> 2, ch = it & 3;
+                uint4 raw = *reinterpret_cast<const uint4*>(src + r * 64 + ch * 16);
+                uint32_t w4[4] = {raw.x, raw.y, raw.z, raw.w};
+                uint32_t o[8];
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    int b0 = (int)(int8_t)(w4[j] & 0xff), b1 = (int)(int8_t)((w4[j] >> 8) & 0xff);
+                    int b2 = (int)(int8_t)((w4[j] >> 16) & 0xff), b3 = (int)(int8_t)(w4[j] >> 24);
+                    o[2 * j] = pack_bf16x2((float)b0, (float)b1);
+                    o[2 * j + 1] = pack_bf16x2((float)b2, (float)b3);
+                }
+                int p0 = ((2 * ch) ^ (r & 7)) * 16, p1 = ((2 * ch + 1) ^ (r & 7)) * 16;
+                *reinterpret_cast<uint4*>(dst + r * 128 + p0) = make_uint4(o[0], o[1], o[2], o[3]);
+                *reinterpret_cast<uint4*>(dst + r * 128 + p1) = make_uint4(o[4], o[5], o[6], o[7]);
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(cfull0 + 8 * c);
+                mbar_arrive(empty0 + 8 * s);
+            }
+        }
+    }
+    __syncwarp();
+
+    // ---------------- epilogue
+    bool ok = mbar_wait(accb, 0, err, DEV_ERR_TIMEOUT_ACC);
+    __syncwarp();
+    tc_fence_after();
+    const int q = warp & 3, part = warp >> 2;
+    constexpr int TP = NT / 2;   // tokens per thread
+    const int l = q * 32 + lane;
+    const uint32_t t_row = tmem + ((uint32_t)(q * 32) << 16);
+    float acc[2][TP];
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+        if (TP == 8) tmem_ld8(t_row + h * NT + part * TP, acc[h]);
+        else if (TP == 16) tmem_ld16(t_row + h * NT + part * TP, acc[h]);
+        else tmem_ld32(t_row + h * NT + part * TP, acc[h]);
+    }
+    tmem_wait_ld();
+    if (nk <= 0) {
+#pragma unroll
+        for (int h = 0; h < 2; h++)
+#pragma unroll
+            for (int t = 0; t < TP; t++) acc[h][t] = 0.f;
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) tmem_dealloc(tmem, C::TMEM_COLS);
+    if (!ok) return;
+
+    const int n_h0 = tile * 256 + l, n_h1 = tile * 256 + 128 + l;
+    const int m_begin = part * TP;
+    if (splits > 1) {
+        // partials: ws[split][m][Nw]
+#pragma unroll
+        for (int t = 0; t < TP; t++) {
+            int m = m_begin + t;
+            if (m < Mtok) {
+                float* dst = ws + ((int64_t)split * Mtok + m) * Nw;
+                if (n_h0 < Nw) dst[n_h0] = acc[0][t];
+                if (n_h1 < Nw) dst[n_h1] = acc[1][t];
+            }
+        }
+        __threadfence();
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            unsigned prev = atomicAdd(&counters[tile], 1u);
+            *s_last = (prev == (unsigned)(splits - 1));
+        }
+        __syncthreads();
+        if (!*s_last) return;
+        __threadfence();
+#pragma unroll
+        for (int t = 0; t < TP; t++) {
+            int m = m_begin + t;
+            float a0 = 0.f, a1 = 0.f;
+            if (m < Mtok) {
+                for (int sp = 0; sp < splits; sp++) {
+                    const float* src = ws + ((int64_t)sp * Mtok + m) * Nw;
+                    if (n_h0 < Nw) a0 += __ldcg(src + n_h0);
+                    if (n_h1 < Nw) a1 += __ldcg(src + n_h1);
+                }
+            }
+            acc[0][t] = a0;
+            acc[1][t] = a1;
+        }
+        if (threadIdx.x == 0) counters[tile] = 0u;
+    }
+
+    // final epilogue: y[m][n]
+    const bool f32o = ep.out_f32 != 0;
+    if (ep.swiglu) {
+        const int on = tile * 128 + l;   // output column
+        if (n_h1 < Nw) {
+            float sg = ep.scale ? ep.scale[n_h0] : 1.f, su = ep.scale ? ep.scale[n_h1] : 1.f;
+#pragma unroll
+            for (int t = 0; t < TP; t++) {
+                int m = m_begin + t;
+                if (m < Mtok) {
+                    float o = silu_f(acc[0][t] * sg) * (acc[1][t] * su);
+                    int64_t off = (int64_t)m * ep.ldo + on;
+                    if (f32o) reinterpret_cast<float*>(ep.out)[off] = o;
+                    else reinterpret_cast<__nv_bfloat16*>(ep.out)[off] = __float2bfloat16_rn(o);
+                }
+            }
+        }
+    } else {
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            int n = h ? n_h1 : n_h0;
+            if (n >= Nw) continue;
+            float sc = ep.scale ? ep.scale[n] : 1.f;
+            float bi = ep.bias ? ep.bias[n] : 0.f;
+#pragma unroll
+            for (int t = 0; t < TP; t++) {
+                int m = m_begin + t;
+                if (m < Mtok) {
+                    float o = acc[h][t] * sc + bi;
+                    if (ep.resid) {
+                        int64_t roff = (int64_t)m * ep.ldr + n;
+                        o += f32o ? reinterpret_cast<const float*>(ep.resid)[roff]
+                                  : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(ep.resid)[roff]);
+                    }
+                    int64_t off = (int64_t)m * ep.ldo + n;
+                    if (f32o) reinterpret_cast<float*>(ep.out)[off] = o;
+                    else reinterpret_cast<__nv_bfloat16*>(ep.out)[off] = __float2bfloat16_rn(o);
+                }
+            }
+        }
+    }
+}
+
+// =====================================================================
+// f32 CUDA-core paths (exact f32 FMA accumulate)
+// =====================================================================
+// 64x64 output tile, 256 threads, 4x4 outputs per thread, K-slices of 16.
+// B_KN: b is [K, N] (matmul_forward); else b is [N, K] (linear_forward).
+template <bool B_KN>
+__global__ void __launch_bounds__(256)
+gemm_f32_kernel(const float* __restrict__ a, const float* __restrict__ b, const float* __restrict__ bias,
+                const float* __restrict__ resid, float* __restrict__ y, int M, int N, int K) {
+    __shared__ float sa[16][64 + 4];
+    __shared__ float sb[16][64 + 4];
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
+    float acc[4][4] = {};
+    for (int k0 = 0; k0 < K; k0 += 16) {
+        for (int i = threadIdx.x; i < 64 * 16; i += 256) {
+            int r = i / 16, kk = i % 16;
+            int gm = m0 + r, gk = k0 + kk;
+            sa[kk][r] = (gm < M && gk < K) ? a[(int64_t)gm * K + gk] : 0.f;
+            if (B_KN) {
+                int c = i % 64, kr = i / 64;
+                int gn = n0 + c, gk2 = k0 + kr;
+                sb[kr][c] = (gn < N && gk2 < K) ? b[(int64_t)gk2 * N + gn] : 0.f;
+            } else {
+                int gn = n0 + r;
+                sb[kk][r] = (gn < N && gk < K) ? b[(int64_t)gn * K + gk] : 0.f;
+            }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int kk = 0; kk < 16; kk++) {
+            float av[4], bv[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                av[i] = sa[kk][ty + 16 * i];
+                bv[i] = sb[kk][tx + 16 * i];
+            }
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        int m = m0 + ty + 16 * i;
+        if (m >= M) continue;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            int n = n0 + tx + 16 * j;
+            if (n >= N) continue;
+            float v = acc[i][j];
+            if (bias) v += bias[n];
+            if (resid) v += resid[(int64_t)m * N + n];
+            y[(int64_t)m * N + n] = v;
+        }
+    }
+}
+
+// ------------------------------------------------------------ host side --
+template <int BN, int STAGES, bool B_MN>
+static int launch_gemm_tc(tb_ctx* ctx, const void* a, const void* b, const Epi& ep, int M, int N, int K) {
+    CUtensorMap ta, tbm;
+    int rc = make_tmap_2d(ctx, &ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a, M, K, K, 64, GEMM_BM);
+    if (rc) return rc;
+    if (!B_MN) rc = make_tmap_2d(ctx, &tbm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, b, N, K, K, 64, BN);
+    else rc = make_tmap_2d(ctx, &tbm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, b, K, N, N, 64, 64);
+    if (rc) return rc;
+    constexpr int smem = gemm_smem_bytes<BN, STAGES>();
+    auto kern = gemm_tc_kernel<BN, STAGES, B_MN>;
+    TB_CUDA_TRY(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    dim3 grid((N + BN - 1) / BN, (M + GEMM_BM - 1) / GEMM_BM);
+    kern<<<grid, 256, smem, ctx->stream>>>(ta, tbm, ep, M, N, K, ctx->d_err);
+    return check_launch(ctx, "gemm_tc");
+}
+
+template <int NT, int STAGES, bool INT8>
+static int launch_gemv_tc(tb_ctx* ctx, const void* x, const void* w, const Epi& ep, int Mtok, int Nw, int K) {
+    using C = GemvCfg<NT, STAGES, INT8>;
+    CUtensorMap tw, tx;
+    int rc;
+    if (INT8) {
+        uint64_t dims[2] = {(uint64_t)K, (uint64_t)Nw};
+        uint64_t strides[1] = {(uint64_t)K};
+        uint32_t box[2] = {64, 256};
+        rc = make_tmap(ctx, &tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+    } else {
+        rc = make_tmap_2d(ctx, &tw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w, Nw, K, K, 64, 256);
+    }
+    if (rc) return rc;
+    rc = make_tmap_2d(ctx, &tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, Mtok, K, K, 64, NT);
+    if (rc) return rc;
+    const int tiles = (Nw + 255) / 256;
+    const int nk = (K + 63) / 64;
+    // Aim for about two CTAs per SM in one wave; each split gets >= 2 K-blocks.
+    int splits = std::max(1, std::min(nk / 2, (2 * ctx->num_sms + tiles - 1) / tiles));
+    int kb_per = (nk + splits - 1) / splits;
+    splits = (nk + kb_per - 1) / kb_per;
+    float* ws = nullptr;
+    if (splits > 1) {
+        rc = ensure_workspace(ctx, (size_t)splits * Mtok * Nw * sizeof(float), tiles);
+        if (rc) return rc;
+        ws = reinterpret_cast<float*>(ctx->ws);
+    } else {
+        rc = ensure_workspace(ctx, 0, tiles);
+        if (rc) return rc;
+    }
+    auto kern = gemv_tc_kernel<NT, STAGES, INT8>;
+    TB_CUDA_TRY(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    dim3 grid(tiles, splits);
+    kern<<<grid, 256, C::SMEM, ctx->stream>>>(tw, tx, ep, Nw, K, Mtok, kb_per, splits, ws, ctx->counters, ctx->d_err);
+    return check_launch(ctx, "gemv_tc");
+}
+
+template <bool INT8>
+static int dispatch_gemv(tb_ctx* ctx, const void* x, const void* w, const Epi& ep, int M, int N, int K) {
+    // bf16, <= 32 tokens: 3 stages (~105 KB) so two CTAs share an SM.
+    if (M <= 16) return launch_gemv_tc<16, INT8 ? 6 : 3, INT8>(ctx, x, w, ep, M, N, K);
+    if (M <= 32) return launch_gemv_tc<32, INT8 ? 6 : 3, INT8>(ctx, x, w, ep, M, N, K);
+    return launch_gemv_tc<64, INT8 ? 4 : 4, INT8>(ctx, x, w, ep, M, N, K);
+}
+
+}  // namespace tb
+
+using namespace tb;
+
+extern "C" {
+
+int tb_linear_fwd(tb_ctx* ctx, int dtype, const void* x, const void* w, const float* bias,
+                  const void* residual, void* y, int64_t M, int64_t N, int64_t K, int flags) {
+    if (!ctx || !x || !w || !y) return TB_ERR_ARG;
+    TB_REQUIRE(ctx, M >= 0 && N > 0 && K > 0 && M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31),
+               TB_ERR_SHAPE, "linear: bad shape M=%lld N=%lld K=%lld", (long long)M, (long long)N, (long long)K);
+    if (M == 0) return TB_OK;
+    if ((flags & TB_EPI_BIAS) && !bias) return set_error(ctx, TB_ERR_ARG, "linear: TB_EPI_BIAS without bias");
+    if ((flags & TB_EPI_RESIDUAL) && !residual) return set_error(ctx, TB_ERR_ARG, "linear: TB_EPI_RESIDUAL without residual");
+    const bool swiglu = (flags & TB_EPI_SWIGLU) != 0;
+    if (dtype == TB_F32) {
+        if (swiglu) return set_error(ctx, TB_ERR_UNSUPPORTED, "linear f32: SwiGLU epilogue is bf16-only");
+        dim3 grid((unsigned)((N + 63) / 64), (unsigned)((M + 63) / 64));
+        gemm_f32_kernel<false><<<grid, 256, 0, ctx->stream>>>(
+            (const float*)x, (const float*)w, (flags & TB_EPI_BIAS) ? bias : nullptr,
+            (flags & TB_EPI_RESIDUAL) ? (const float*)residual : nullptr, (float*)y, (int)M, (int)N, (int)K);
+        return check_launch(ctx, "linear_f32");
+    }
+    if (dtype != TB_BF16) return set_error(ctx, TB_ERR_UNSUPPORTED, "linear: dtype %d", dtype);
+    TB_REQUIRE(ctx, K % 8 == 0 && N % 8 == 0, TB_ERR_SHAPE, "linear bf16: K and N must be multiples of 8");
+    TB_REQUIRE(ctx, aligned16(x) && aligned16(w) && aligned16(y) && (!residual || aligned16(residual)),
+               TB_ERR_ALIGN, "linear bf16: pointers must be 16-byte aligned");
+    if (swiglu) {
+        TB_REQUIRE(ctx, N % 256 == 0, TB_ERR_SHAPE, "linear SwiGLU: N must be a multiple of 256");
+        TB_REQUIRE(ctx, !(flags & (TB_EPI_BIAS | TB_EPI_RESIDUAL)), TB_ERR_UNSUPPORTED,
+                   "linear SwiGLU: no bias/residual");
+    }
+    Epi ep{};
+    ep.out = y;
+    ep.out_f32 = (flags & TB_EPI_OUT_F32) ? 1 : 0;
+    ep.ldo = swiglu ? N / 2 : N;
+    ep.bias = (flags & TB_EPI_BIAS) ? bias : nullptr;
+    ep.resid = (flags & TB_EPI_RESIDUAL) ? residual : nullptr;
+    ep.ldr = N;
+    ep.swiglu = swiglu ? 1 : 0;
+    if (M <= 64) return dispatch_gemv<false>(ctx, x, w, ep, (int)M, (int)N, (int)K);
+    if (N <= 128 && !swiglu) return launch_gemm_tc<128, 6, false>(ctx, x, w, ep, (int)M, (int)N, (int)K);
+    return launch_gemm_tc<256, 4, false>(ctx, x, w, ep, (int)M, (int)N, (int)K);
+}
+
+int tb_matmul_fwd(tb_ctx* ctx, int dtype, const void* a, const void* b, void* c, int64_t M, int64_t N, int64_t K) {
+    if (!ctx || !a || !b || !c) return TB_ERR_ARG;
+    TB_REQUIRE(ctx, M >= 0 && N > 0 && K > 0 && M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31),
+               TB_ERR_SHAPE, "matmul: bad shape");
+    if (M == 0) return TB_OK;
+    if (dtype == TB_F32) {
+        dim3 grid((unsigned)((N + 63) / 64), (unsigned)((M + 63) / 64));
+        gemm_f32_kernel<true><<<grid, 256, 0, ctx->stream>>>((const float*)a, (const float*)b, nullptr, nullptr,
+                                                             (float*)c, (int)M, (int)N, (int)K);
+        return check_launch(ctx, "matmul_f32");
+    }
+    if (dtype != TB_BF16) return set_error(ctx, TB_ERR_UNSUPPORTED, "matmul: dtype %d", dtype);
+    TB_REQUIRE(ctx, K % 8 == 0 && N % 8 == 0, TB_ERR_SHAPE, "matmul bf16: K and N must be multiples of 8");
+    TB_REQUIRE(ctx, aligned16(a) && aligned16(b) && aligned16(c), TB_ERR_ALIGN, "matmul bf16: alignment");
+    Epi ep{};
+    ep.out = c;
+    ep.ldo = N;
+    return launch_gemm_tc<256, 4, true>(ctx, a, b, ep, (int)M, (int)N, (int)K);
+}
+
+int tb_int8_linear_fwd(tb_ctx* ctx, const void* x, const int8_t* q, const float* scale,
+                       const void* residual, void* y, int64_t M, int64_t N, int64_t K, int flags) {
+    if (!ctx || !x || !q || !scale || !y) return TB_ERR_ARG;
+    TB_REQUIRE(ctx, M >= 0 && M <= 64 && N > 0 && K > 0 && N < (1ll << 31) && K < (1ll << 31), TB_ERR_SHAPE,
+               "int8 linear: 0 <= M <= 64 tokens (decode GEMV path)");
+    if (M == 0) return TB_OK;
+    TB_REQUIRE(ctx, K % 16 == 0 && N % 8 == 0, TB_ERR_SHAPE, "int8 linear: K %% 16 and N %% 8 must be 0");
+    TB_REQUIRE(ctx, aligned16(x) && aligned16(q), TB_ERR_ALIGN, "int8 linear: alignment");
+    if ((flags & TB_EPI_RESIDUAL) && !residual) return set_error(ctx, TB_ERR_ARG, "int8 linear: residual missing");
+    const bool swiglu = (flags & TB_EPI_SWIGLU) != 0;
+    if (swiglu) TB_REQUIRE(ctx, N % 256 == 0, TB_ERR_SHAPE, "int8 SwiGLU: N %% 256");
+    Epi ep{};
+    ep.out = y;
+    ep.out_f32 = (flags & TB_EPI_OUT_F32) ? 1 : 0;
+    ep.ldo = swiglu ? N / 2 : N;
+    ep.resid = (flags & TB_EPI_RESIDUAL) ? residual : nullptr;
+    ep.ldr = N;
+    ep.scale = scale;
+    ep.swiglu = swiglu ? 1 : 0;
+    return dispatch_gemv<true>(ctx, x, q, ep, (int)M, (int)N, (int)K);
+}
+
+}  // extern "C"

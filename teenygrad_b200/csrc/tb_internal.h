@@ -1,0 +1,63 @@
+// Host-side internals shared by the library's translation units.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <mutex>
+#include <string>
+
+#include "../../include/teeny_b200.h"
+
+struct tb_ctx {
+    int device = 0;
+    int num_sms = 148;
+    cudaStream_t stream = nullptr;
+    int* d_err = nullptr;           // device error word (bounded-wait timeouts)
+    void* ws = nullptr;             // split-K partials etc.; grows on demand
+    size_t ws_bytes = 0;
+    unsigned* counters = nullptr;   // split-K arrival counters, kept at zero between launches
+    size_t n_counters = 0;
+    std::string last_error;
+    void* comm = nullptr;           // NCCL communicator state (comm.cu)
+};
+
+namespace tb {
+
+int set_error(tb_ctx* ctx, int status, const char* fmt, ...);
+
+// Records cudaGetLastError() (launch-configuration errors) into ctx.
+int check_launch(tb_ctx* ctx, const char* what);
+
+// Ensures ctx->ws has at least `bytes` and ctx->counters at least `n` zeroed
+// entries.  Grows with cudaMalloc (synchronous): not for use during capture.
+int ensure_workspace(tb_ctx* ctx, size_t bytes, size_t n_counters);
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
+// dims/strides in elements / bytes as the driver API defines them
+// (strides[0] is the stride of dim 1).  Returns 0 on success.
+int make_tmap(tb_ctx* ctx, CUtensorMap* out, CUtensorMapDataType dt, int rank, const void* base,
+              const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+              CUtensorMapSwizzle swz);
+
+// 2-D K-major bf16/int8 operand: rows x cols (cols contiguous), box = box_cols x box_rows.
+int make_tmap_2d(tb_ctx* ctx, CUtensorMap* out, CUtensorMapDataType dt, int elem_bytes,
+                 const void* base, uint64_t rows, uint64_t cols, uint64_t row_stride_elems,
+                 uint32_t box_cols, uint32_t box_rows);
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace tb
+
+#define TB_CUDA_TRY(ctx, call)                                                              \
+    do {                                                                                    \
+        cudaError_t e_ = (call);                                                            \
+        if (e_ != cudaSuccess)                                                              \
+            return tb::set_error((ctx), TB_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(e_)); \
+    } while (0)
+
+#define TB_REQUIRE(ctx, cond, status, ...)                \
+    do {                                                  \
+        if (!(cond)) return tb::set_error((ctx), (status), __VA_ARGS__); \
+    } while (0)

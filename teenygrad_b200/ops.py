@@ -1,0 +1,303 @@
+"""Host-side operator surface over the C ABI, on torch CUDA tensors.
+
+The reference dispatches each graph node to a kernel struct implementing
+``RuntimeOp`` (core/teeny-core/src/model/mod.rs:78-330): ``pack_args`` +
+``grid`` + a launch.  Here each op is a function (and a class with the
+reference kernel's name, for code written against that surface) that checks
+shapes, allocates the output and calls the matching ``tb_*`` entry point on
+the current torch stream.  Errors surface as :class:`TeenyError` (the
+reference returns ``anyhow::Result``).
+
+torch is used only for device memory and streams.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+
+from ._lib import (TB_ACT, TB_BF16, TB_EPI_BIAS, TB_EPI_OUT_F32, TB_EPI_RESIDUAL, TB_EPI_SWIGLU,
+                   TB_F32, TeenyError, check, lib)
+
+_DT = {torch.float32: TB_F32, torch.bfloat16: TB_BF16}
+_ctxs: dict[int, ctypes.c_void_p] = {}
+
+
+def context(device: int | None = None) -> ctypes.c_void_p:
+    """Per-device tb_ctx, bound to torch's current stream at each call."""
+    if device is None:
+        device = torch.cuda.current_device()
+    ctx = _ctxs.get(device)
+    if ctx is None:
+        ctx = ctypes.c_void_p()
+        st = lib().tb_init(ctypes.byref(ctx), ctypes.c_int(device))
+        if st != 0:
+            raise TeenyError(st, f"tb_init(device={device}) failed: needs an sm_100 GPU")
+        _ctxs[device] = ctx
+    lib().tb_set_stream(ctx, ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream))
+    return ctx
+
+
+def device_error(clear: bool = True) -> int:
+    ctx = context()
+    code = ctypes.c_int(0)
+    check(ctx, lib().tb_device_error(ctx, ctypes.byref(code), ctypes.c_int(int(clear))))
+    return code.value
+
+
+def _p(t):
+    return ctypes.c_void_p(0 if t is None else t.data_ptr())
+
+
+def _dt(t):
+    if t.dtype not in _DT:
+        raise TeenyError(5, f"unsupported dtype {t.dtype}")
+    return _DT[t.dtype]
+
+
+def _cuda(*ts):
+    for t in ts:
+        if t is not None:
+            if not t.is_cuda:
+                raise TeenyError(1, "tensors must be on a CUDA device (no CPU fallback)")
+            if not t.is_contiguous():
+                raise TeenyError(2, "tensors must be contiguous")
+
+
+_i64 = ctypes.c_int64
+_f = ctypes.c_float
+
+
+# --------------------------------------------------------------- norms ----
+def rms_norm(x, w, eps=1e-8, return_rrms=False):
+    """rms_norm_forward (nn/norm/rmsnorm.rs:40-122); x [..., N]."""
+    _cuda(x, w)
+    N = x.shape[-1]
+    M = x.numel() // N
+    y = torch.empty_like(x)
+    rrms = torch.empty(M, device=x.device, dtype=torch.float32) if return_rrms else None
+    ctx = context()
+    check(ctx, lib().tb_rmsnorm_fwd(ctx, _dt(x), _p(x), _p(w), _p(y), _p(rrms), _i64(M), _i64(N), _f(eps)))
+    return (y, rrms) if return_rrms else y
+
+
+def layer_norm(x, w, b, eps=1e-5):
+    """layer_norm_forward_inference (nn/norm/layernorm.rs:43-157)."""
+    _cuda(x, w, b)
+    N = x.shape[-1]
+    y = torch.empty_like(x)
+    ctx = context()
+    check(ctx, lib().tb_layernorm_fwd(ctx, _dt(x), _p(x), _p(w), _p(b), _p(y), _i64(x.numel() // N), _i64(N), _f(eps)))
+    return y
+
+
+# --------------------------------------------------------- elementwise ----
+def activation(kind, x):
+    _cuda(x)
+    y = torch.empty_like(x)
+    ctx = context()
+    check(ctx, lib().tb_act_fwd(ctx, ctypes.c_int(TB_ACT[kind]), _dt(x), _p(x), _p(y), _i64(x.numel())))
+    return y
+
+
+def silu(x):
+    return activation("silu", x)
+
+
+def gelu_tanh(x):
+    return activation("gelu_tanh", x)
+
+
+def relu(x):
+    return activation("relu", x)
+
+
+def sigmoid(x):
+    return activation("sigmoid", x)
+
+
+def swiglu(gate, up):
+    _cuda(gate, up)
+    y = torch.empty_like(gate)
+    ctx = context()
+    check(ctx, lib().tb_swiglu_fwd(ctx, _dt(gate), _p(gate), _p(up), _p(y), _i64(gate.numel())))
+    return y
+
+
+def add(a, b):
+    _cuda(a, b)
+    y = torch.empty_like(a)
+    ctx = context()
+    check(ctx, lib().tb_add_fwd(ctx, _dt(a), _p(a), _p(b), _p(y), _i64(a.numel())))
+    return y
+
+
+# --------------------------------------------------------------- linear ---
+def linear(x, w, bias=None, residual=None, swiglu=False, out_f32=False):
+    """linear_forward (nn/mlp/linear.rs:22-117): y = x w^T (+ bias) (+ residual).
+
+    swiglu=True expects w rows interleaved in blocks of 128 (gate, up) and
+    returns silu(gate) * up with N/2 columns (see interleave_gate_up)."""
+    _cuda(x, w, bias, residual)
+    K = x.shape[-1]
+    M = x.numel() // K
+    N = w.shape[0]
+    flags = (TB_EPI_BIAS if bias is not None else 0) | (TB_EPI_RESIDUAL if residual is not None else 0)
+    flags |= (TB_EPI_SWIGLU if swiglu else 0) | (TB_EPI_OUT_F32 if out_f32 else 0)
+    ncol = N // 2 if swiglu else N
+    y = torch.empty(*x.shape[:-1], ncol, device=x.device, dtype=torch.float32 if out_f32 else x.dtype)
+    if bias is not None and bias.dtype != torch.float32:
+        bias = bias.float().contiguous()
+    ctx = context()
+    check(ctx, lib().tb_linear_fwd(ctx, _dt(x), _p(x), _p(w), _p(bias), _p(residual), _p(y),
+                                   _i64(M), _i64(N), _i64(K), ctypes.c_int(flags)))
+    return y
+
+
+def interleave_gate_up(w_gate, w_up, block=128):
+    """[F, K] gate and up weights -> [2F, K] in the (gate block, up block) order
+    the fused SwiGLU epilogue expects."""
+    F, K = w_gate.shape
+    g = w_gate.reshape(F // block, block, K)
+    u = w_up.reshape(F // block, block, K)
+    return torch.stack([g, u], dim=1).reshape(2 * F, K).contiguous()
+
+
+def matmul(a, b):
+    """matmul_forward (math/gemm.rs:44-105): c = a @ b, b [K, N]."""
+    _cuda(a, b)
+    M, K = a.shape
+    N = b.shape[1]
+    c = torch.empty(M, N, device=a.device, dtype=a.dtype)
+    ctx = context()
+    check(ctx, lib().tb_matmul_fwd(ctx, _dt(a), _p(a), _p(b), _p(c), _i64(M), _i64(N), _i64(K)))
+    return c
+
+
+# ----------------------------------------------------------------- int8 ---
+def quantize_int8(w):
+    """quantize_affine, symmetric per output channel (teeny-quant affine.rs:55-148)."""
+    _cuda(w)
+    N, K = w.shape
+    q = torch.empty(N, K, device=w.device, dtype=torch.int8)
+    s = torch.empty(N, device=w.device, dtype=torch.float32)
+    ctx = context()
+    fn = lib().tb_quantize_int8 if w.dtype == torch.float32 else lib().tb_quantize_int8_bf16
+    check(ctx, fn(ctx, _p(w), _p(q), _p(s), _i64(N), _i64(K)))
+    return q, s
+
+
+def dequantize_int8(q, s):
+    _cuda(q, s)
+    N, K = q.shape
+    w = torch.empty(N, K, device=q.device, dtype=torch.float32)
+    ctx = context()
+    check(ctx, lib().tb_dequantize_int8(ctx, _p(q), _p(s), _p(w), _i64(N), _i64(K)))
+    return w
+
+
+def int8_linear(x, q, s, residual=None, swiglu=False, out_f32=False):
+    _cuda(x, q, s, residual)
+    K = x.shape[-1]
+    M = x.numel() // K
+    N = q.shape[0]
+    flags = (TB_EPI_RESIDUAL if residual is not None else 0) | (TB_EPI_SWIGLU if swiglu else 0)
+    flags |= TB_EPI_OUT_F32 if out_f32 else 0
+    ncol = N // 2 if swiglu else N
+    y = torch.empty(*x.shape[:-1], ncol, device=x.device, dtype=torch.float32 if out_f32 else x.dtype)
+    ctx = context()
+    check(ctx, lib().tb_int8_linear_fwd(ctx, _p(x), _p(q), _p(s), _p(residual), _p(y), _i64(M), _i64(N),
+                                        _i64(K), ctypes.c_int(flags)))
+    return y
+
+
+# ------------------------------------------------------------ attention ---
+def attention(q, k, v, scale=None, causal=False, return_lse=False):
+    """flash_attention2_forward (nn/attention/flash_attn2.rs:53-158) + causal + GQA.
+    q [B, Hq, Sq, D], k/v [B, Hkv, Sk, D]."""
+    _cuda(q, k, v)
+    B, Hq, Sq, D = q.shape
+    Hkv, Sk = k.shape[1], k.shape[2]
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    o = torch.empty_like(q)
+    lse = torch.empty(B, Hq, Sq, device=q.device, dtype=torch.float32) if return_lse else None
+    ctx = context()
+    check(ctx, lib().tb_attn_fwd(ctx, _dt(q), _p(q), _p(k), _p(v), _p(o), _p(lse), ctypes.c_int(B),
+                                 ctypes.c_int(Hq), ctypes.c_int(Hkv), ctypes.c_int(Sq), ctypes.c_int(Sk),
+                                 ctypes.c_int(D), _f(scale), ctypes.c_int(int(causal))))
+    return (o, lse) if return_lse else o
+
+
+# --------------------------------------------------------- decoder ops ----
+def rope(x, pos, theta=10000.0):
+    """x [T, H, D], pos [T] int32."""
+    _cuda(x, pos)
+    T, H, D = x.shape
+    y = torch.empty_like(x)
+    ctx = context()
+    check(ctx, lib().tb_rope_fwd(ctx, _dt(x), _p(x), _p(pos), _p(y), _i64(T), ctypes.c_int(H), ctypes.c_int(D), _f(theta)))
+    return y
+
+
+def embedding(table, ids):
+    _cuda(table, ids)
+    T = ids.numel()
+    D = table.shape[1]
+    y = torch.empty(T, D, device=table.device, dtype=table.dtype)
+    ctx = context()
+    check(ctx, lib().tb_embedding_fwd(ctx, _dt(table), _p(table), _p(ids), _p(y), _i64(T), _i64(D), _i64(table.shape[0])))
+    return y
+
+
+def argmax(x):
+    _cuda(x)
+    M, N = x.shape
+    out = torch.empty(M, device=x.device, dtype=torch.int32)
+    ctx = context()
+    check(ctx, lib().tb_argmax_fwd(ctx, _dt(x), _p(x), _p(out), _i64(M), _i64(N)))
+    return out
+
+
+# ------------------------------------------- reference kernel-struct names --
+class _Op:
+    fn = None
+
+    def __init__(self, **consts):
+        self.consts = consts
+
+    def __call__(self, *args, **kw):
+        return type(self).fn(*args, **{**self.consts, **kw})
+
+
+class RmsNormForward(_Op):
+    fn = staticmethod(rms_norm)
+
+
+class LayerNormForwardInference(_Op):
+    fn = staticmethod(layer_norm)
+
+
+class SiluForward(_Op):
+    fn = staticmethod(silu)
+
+
+class GeluForward(_Op):
+    fn = staticmethod(gelu_tanh)
+
+
+class ReluForward(_Op):
+    fn = staticmethod(relu)
+
+
+class LinearForward(_Op):
+    fn = staticmethod(linear)
+
+
+class MatMulForward(_Op):
+    fn = staticmethod(matmul)
+
+
+class FlashAttention2Forward(_Op):
+    fn = staticmethod(attention)

@@ -1,0 +1,283 @@
+"""GPU parity: every hot-path op through the C ABI against the CPU oracle.
+
+Tolerances (the north star's): fp32 paths <= 1e-4, bf16 tensor-core paths with
+f32 accumulate <= 2e-2 (max abs error normalised by max(1, max |ref|));
+int8 quantise / dequantise, argmax, embedding: bit-exact.
+"""
+import math
+
+import numpy as np
+import pytest
+
+from gpu_util import (BF16_TOL, F32_TOL, assert_close, bf16_round, dev, no_device_error, np_of, rng,
+                      to_gpu, torch)
+from golden_io import load
+
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _gpu():
+    dev()
+    yield
+    no_device_error()
+
+
+def ops():
+    from teenygrad_b200 import ops as o
+    return o
+
+
+# ------------------------------------------------------------------ norms --
+def test_rmsnorm_golden_f32():
+    x = load("rmsnorm", "x.bin", (16, 128))
+    w = load("rmsnorm", "weight.bin")
+    y, rrms = ops().rms_norm(to_gpu(x), to_gpu(w), eps=1e-8, return_rrms=True)
+    assert_close(np_of(y), load("rmsnorm", "expected_forward.bin", (16, 128)), F32_TOL)
+    assert_close(np_of(rrms), load("rmsnorm", "expected_rrms.bin"), F32_TOL)
+
+
+@pytest.mark.parametrize("M,N", [(16, 2048), (257, 2048), (3, 129), (128, 256)])
+def test_rmsnorm_bf16(M, N):
+    r = rng(M + N)
+    x = bf16_round(r.standard_normal((M, N)))
+    w = bf16_round(r.uniform(0.5, 1.5, N))
+    ref, rr = oracle.rmsnorm(x, w, 1e-5)
+    y, rrms = ops().rms_norm(to_gpu(x, torch.bfloat16), to_gpu(w, torch.bfloat16), eps=1e-5, return_rrms=True)
+    assert_close(np_of(y), ref, BF16_TOL)
+    assert_close(np_of(rrms), rr, 1e-5)
+
+
+def test_layernorm_golden_and_bf16():
+    x = load("layernorm", "x.bin", (16, 128))
+    y = ops().layer_norm(to_gpu(x), to_gpu(load("layernorm", "weight.bin")), to_gpu(load("layernorm", "bias.bin")), 1e-5)
+    assert_close(np_of(y), load("layernorm", "expected_forward.bin", (16, 128)), F32_TOL)
+    r = rng(5)
+    x = bf16_round(r.standard_normal((300, 2048)) * 3 + 1)
+    w, b = bf16_round(r.uniform(0.5, 1.5, 2048)), bf16_round(r.normal(0, 0.1, 2048))
+    ref = oracle.layernorm(x, w, b, 1e-5)
+    y = ops().layer_norm(*(to_gpu(a, torch.bfloat16) for a in (x, w, b)), 1e-5)
+    assert_close(np_of(y), ref, BF16_TOL)
+
+
+# ------------------------------------------------------------ elementwise --
+@pytest.mark.parametrize("name,kind,tol", [("silu", "silu", 1e-5), ("gelu", "gelu_tanh", 2e-5),
+                                           ("relu", "relu", 0.0), ("sigmoid", "sigmoid", 1e-5)])
+def test_activation_golden(name, kind, tol):
+    x = load(name, "x.bin")
+    y = ops().activation(kind, to_gpu(x))
+    np.testing.assert_allclose(np_of(y), load(name, "expected_forward.bin"), atol=tol, rtol=0)
+
+
+@pytest.mark.parametrize("n", [1, 7, 1000003])
+def test_elementwise_bf16_and_tails(n):
+    r = rng(n)
+    a = bf16_round(r.standard_normal(n) * 3)
+    b = bf16_round(r.standard_normal(n))
+    for kind in ("silu", "gelu_tanh", "relu", "sigmoid"):
+        y = ops().activation(kind, to_gpu(a, torch.bfloat16))
+        assert_close(np_of(y), oracle.act(kind, a), BF16_TOL, kind)
+    assert_close(np_of(ops().swiglu(to_gpu(a, torch.bfloat16), to_gpu(b, torch.bfloat16))), oracle.swiglu(a, b), BF16_TOL)
+    assert_close(np_of(ops().add(to_gpu(a, torch.bfloat16), to_gpu(b, torch.bfloat16))), oracle.add(a, b), BF16_TOL)
+    af = a.astype(np.float32)
+    assert_close(np_of(ops().swiglu(to_gpu(af), to_gpu(b))), oracle.swiglu(af, b), F32_TOL)
+    np.testing.assert_array_equal(np_of(ops().add(to_gpu(af), to_gpu(b))), oracle.add(af, b))
+
+
+# ----------------------------------------------------------------- linear --
+def test_linear_golden_f32():
+    x = load("linear", "input.bin", (64, 64))
+    w = load("linear", "weight.bin", (48, 64))
+    b = load("linear", "bias.bin")
+    y0 = ops().linear(to_gpu(x), to_gpu(w))
+    y1 = ops().linear(to_gpu(x), to_gpu(w), bias=to_gpu(b))
+    exp0 = load("linear", "expected_no_bias.bin", (64, 48))
+    exp1 = load("linear", "expected_with_bias.bin", (64, 48))
+    # values reach |y| ~ 300: relative 1e-4
+    assert_close(np_of(y0) / 300, exp0 / 300, F32_TOL)
+    assert_close(np_of(y1) / 300, exp1 / 300, F32_TOL)
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 768, 256), (128, 256, 1024), (37, 50, 3)])
+def test_linear_f32(M, N, K):
+    r = rng(M * N + K)
+    x = r.standard_normal((M, K)).astype(np.float32)
+    w = (r.standard_normal((N, K)) * 0.02).astype(np.float32)
+    res = r.standard_normal((M, N)).astype(np.float32)
+    y = ops().linear(to_gpu(x), to_gpu(w), residual=to_gpu(res))
+    assert_close(np_of(y), oracle.linear(x, w, resid=res), F32_TOL)
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 384, 512), (200, 264, 520), (1000, 1024, 2048), (129, 128, 64)])
+def test_linear_bf16_tc(M, N, K):
+    r = rng(M + N + K)
+    x = bf16_round(r.standard_normal((M, K)))
+    w = bf16_round(r.standard_normal((N, K)) * 0.02)
+    bias = r.standard_normal(N).astype(np.float32) * 0.1
+    res = bf16_round(r.standard_normal((M, N)))
+    xg, wg = to_gpu(x, torch.bfloat16), to_gpu(w, torch.bfloat16)
+    assert_close(np_of(ops().linear(xg, wg)), oracle.linear(x, w), BF16_TOL, "plain")
+    y = ops().linear(xg, wg, bias=to_gpu(bias), residual=to_gpu(res, torch.bfloat16))
+    assert_close(np_of(y), oracle.linear(x, w, bias, res), BF16_TOL, "bias+res")
+    y32 = ops().linear(xg, wg, out_f32=True)
+    assert y32.dtype == torch.float32
+    assert_close(np_of(y32), oracle.linear(x, w), 2e-3, "f32 out")
+
+
+@pytest.mark.parametrize("M", [256, 1, 16, 64])
+def test_linear_bf16_swiglu(M):
+    r = rng(M)
+    K, F = 512, 512
+    x = bf16_round(r.standard_normal((M, K)))
+    wg = bf16_round(r.standard_normal((F, K)) * 0.05)
+    wu = bf16_round(r.standard_normal((F, K)) * 0.05)
+    W = ops().interleave_gate_up(to_gpu(wg, torch.bfloat16), to_gpu(wu, torch.bfloat16))
+    y = ops().linear(to_gpu(x, torch.bfloat16), W, swiglu=True)
+    ref = oracle.swiglu(oracle.linear(x, wg), oracle.linear(x, wu))
+    assert y.shape == (M, F)
+    assert_close(np_of(y), ref, BF16_TOL)
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 3072, 2048), (16, 2048, 2048), (33, 1000, 512), (64, 32000, 2048), (16, 2048, 8192)])
+def test_linear_bf16_decode_gemv(M, N, K):
+    r = rng(M * 7 + N)
+    x = bf16_round(r.standard_normal((M, K)))
+    w = bf16_round(r.standard_normal((N, K)) * 0.02)
+    res = bf16_round(r.standard_normal((M, N)))
+    y = ops().linear(to_gpu(x, torch.bfloat16), to_gpu(w, torch.bfloat16), residual=to_gpu(res, torch.bfloat16))
+    assert_close(np_of(y), oracle.linear(x, w, resid=res), BF16_TOL)
+    # twice in a row: split-K counters must be back at zero
+    y2 = ops().linear(to_gpu(x, torch.bfloat16), to_gpu(w, torch.bfloat16), residual=to_gpu(res, torch.bfloat16))
+    assert torch.equal(y, y2)
+
+
+def test_matmul():
+    r = rng(11)
+    a = r.standard_normal((70, 96)).astype(np.float32)
+    b = r.standard_normal((96, 40)).astype(np.float32)
+    assert_close(np_of(ops().matmul(to_gpu(a), to_gpu(b))), oracle.matmul(a, b), F32_TOL)
+    a = bf16_round(r.standard_normal((300, 512)))
+    b = bf16_round(r.standard_normal((512, 264)) * 0.05)
+    got = ops().matmul(to_gpu(a, torch.bfloat16), to_gpu(b, torch.bfloat16))
+    assert_close(np_of(got), oracle.matmul(a, b), BF16_TOL)
+
+
+# ------------------------------------------------------------------- int8 --
+def test_quantize_int8_bit_exact():
+    r = rng(3)
+    w = (r.standard_normal((513, 700)) * 0.02).astype(np.float32)
+    w[0] = 0.0
+    w[1, :5] = [0.5, -0.5, 1.5, -2.5, 127.0]
+    w[2, 0] = -0.0
+    q, s = ops().quantize_int8(to_gpu(w))
+    qo, so = oracle.quantize_int8(w)
+    np.testing.assert_array_equal(q.cpu().numpy(), qo)
+    np.testing.assert_array_equal(s.cpu().numpy(), so)
+    deq = ops().dequantize_int8(q, s)
+    np.testing.assert_array_equal(deq.cpu().numpy(), oracle.dequantize_int8(qo, so))
+    # bf16 weights (upcast exactly)
+    wb = bf16_round(w)
+    qb, sb = ops().quantize_int8(to_gpu(wb, torch.bfloat16))
+    qo, so = oracle.quantize_int8(wb)
+    np.testing.assert_array_equal(qb.cpu().numpy(), qo)
+    np.testing.assert_array_equal(sb.cpu().numpy(), so)
+
+
+@pytest.mark.parametrize("M,N,K", [(64, 2048, 2048), (16, 3072, 2048), (1, 2048, 8192), (64, 1000, 512)])
+def test_int8_linear(M, N, K):
+    r = rng(M + N + K)
+    w = (r.standard_normal((N, K)) * 0.02).astype(np.float32)
+    q, s = oracle.quantize_int8(w)
+    x = bf16_round(r.standard_normal((M, K)))
+    res = bf16_round(r.standard_normal((M, N)))
+    y = ops().int8_linear(to_gpu(x, torch.bfloat16), to_gpu(q, torch.int8), to_gpu(s), residual=to_gpu(res, torch.bfloat16))
+    assert_close(np_of(y), oracle.int8_linear(x, q, s, resid=res), BF16_TOL)
+
+
+def test_int8_linear_swiglu():
+    r = rng(9)
+    M, K, F = 64, 1024, 512
+    wg = (r.standard_normal((F, K)) * 0.05).astype(np.float32)
+    wu = (r.standard_normal((F, K)) * 0.05).astype(np.float32)
+    W = ops().interleave_gate_up(torch.from_numpy(wg), torch.from_numpy(wu)).numpy()
+    q, s = oracle.quantize_int8(W)
+    x = bf16_round(r.standard_normal((M, K)))
+    y = ops().int8_linear(to_gpu(x, torch.bfloat16), to_gpu(q, torch.int8), to_gpu(s), swiglu=True)
+    full = oracle.int8_linear(x, q, s).reshape(M, F // 128, 2, 128)
+    ref = oracle.swiglu(full[:, :, 0, :].reshape(M, F), full[:, :, 1, :].reshape(M, F))
+    assert_close(np_of(y), ref, BF16_TOL)
+
+
+# -------------------------------------------------------------- attention --
+def test_attention_golden_f32():
+    q = load("flash_attn2", "q.bin", (1, 4, 8, 64))
+    k = load("flash_attn2", "k.bin", (1, 4, 8, 64))
+    v = load("flash_attn2", "v.bin", (1, 4, 8, 64))
+    o, lse = ops().attention(to_gpu(q), to_gpu(k), to_gpu(v), scale=0.125, return_lse=True)
+    assert_close(np_of(o), load("flash_attn2", "expected_forward_o.bin", (1, 4, 8, 64)), F32_TOL)
+    assert_close(np_of(lse), load("flash_attn2", "expected_forward_l.bin", (1, 4, 8)), F32_TOL)
+
+
+def test_attention_f32_causal_gqa():
+    r = rng(4)
+    q = r.standard_normal((1, 4, 128, 64)).astype(np.float32)
+    k = r.standard_normal((1, 2, 128, 64)).astype(np.float32)
+    v = r.standard_normal((1, 2, 128, 64)).astype(np.float32)
+    o, lse = ops().attention(to_gpu(q), to_gpu(k), to_gpu(v), scale=0.125, causal=True, return_lse=True)
+    ro, rl = oracle.attention(q, k, v, 0.125, True)
+    assert_close(np_of(o), ro, F32_TOL)
+    assert_close(np_of(lse), rl, F32_TOL)
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,Sq,Sk,D,causal", [
+    (1, 2, 2, 128, 128, 64, False),
+    (1, 4, 2, 300, 300, 64, True),
+    (2, 4, 1, 256, 256, 128, True),
+    (1, 2, 2, 200, 456, 128, True),
+    (1, 2, 2, 130, 77, 64, False),
+])
+def test_attention_bf16_tc(B, Hq, Hkv, Sq, Sk, D, causal):
+    r = rng(B * 1000 + Sq + Sk + D)
+    q = bf16_round(r.standard_normal((B, Hq, Sq, D)))
+    k = bf16_round(r.standard_normal((B, Hkv, Sk, D)))
+    v = bf16_round(r.standard_normal((B, Hkv, Sk, D)))
+    sc = 1.0 / math.sqrt(D)
+    o, lse = ops().attention(*(to_gpu(a, torch.bfloat16) for a in (q, k, v)), scale=sc, causal=causal, return_lse=True)
+    ro, rl = oracle.attention(q, k, v, sc, causal)
+    assert_close(np_of(o), ro, BF16_TOL, "O")
+    assert_close(np_of(lse), rl, 1e-3, "LSE")
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,Sk,D", [(4, 32, 8, 1000, 64), (2, 8, 8, 2048, 128), (3, 4, 1, 5, 64)])
+def test_attention_decode(B, Hq, Hkv, Sk, D):
+    r = rng(Sk + D)
+    q = bf16_round(r.standard_normal((B, Hq, 1, D)))
+    k = bf16_round(r.standard_normal((B, Hkv, Sk, D)))
+    v = bf16_round(r.standard_normal((B, Hkv, Sk, D)))
+    sc = 1.0 / math.sqrt(D)
+    o, lse = ops().attention(*(to_gpu(a, torch.bfloat16) for a in (q, k, v)), scale=sc, causal=True, return_lse=True)
+    ro, rl = oracle.attention(q, k, v, sc, True)
+    assert_close(np_of(o), ro, BF16_TOL, "O")
+    assert_close(np_of(lse), rl, 1e-3, "LSE")
+
+
+# ---------------------------------------------------------- decoder pieces --
+def test_rope_embedding_argmax():
+    r = rng(8)
+    x = bf16_round(r.standard_normal((40, 8, 64)))
+    pos = r.integers(0, 2048, 40).astype(np.int32)
+    y = ops().rope(to_gpu(x, torch.bfloat16), to_gpu(pos, torch.int32))
+    assert_close(np_of(y), oracle.rope(x, pos, 10000.0), BF16_TOL)
+    table = bf16_round(r.standard_normal((1000, 256)))
+    ids = r.integers(0, 1000, 77).astype(np.int32)
+    e = ops().embedding(to_gpu(table, torch.bfloat16), to_gpu(ids, torch.int32))
+    np.testing.assert_array_equal(np_of(e), oracle.embedding(table, ids))
+    logits = r.standard_normal((16, 32000)).astype(np.float32)
+    logits[3, 100] = logits[3, 200] = 50.0            # tie -> lower index
+    logits[5, :] = -np.inf
+    logits[7, 10] = np.nan
+    got = ops().argmax(to_gpu(logits)).cpu().numpy()
+    np.testing.assert_array_equal(got, oracle.argmax(logits))
+    assert got[3] == 100
