@@ -147,6 +147,74 @@ TB_API int tb_embedding_fwd(tb_ctx* ctx, int dtype, const void* table, const int
 /* Row argmax; the lowest index wins ties, NaN never wins. x [M, N]. */
 TB_API int tb_argmax_fwd(tb_ctx* ctx, int dtype, const void* x, int32_t* out, int64_t M, int64_t N);
 
+/* ------------------------------------------------------ decoder model --- */
+/* A Llama-style decoder assembled from the ops above (the reference's
+ * teeny-llm is a placeholder, apps/teeny-llm/src/server/main.rs:6-8, and its
+ * graph lowering lacks attention/RoPE/gather, kernels/teeny-kernels/src/graph/
+ * mod.rs:2472-2530).  It plays the role of LoadedModel (drivers/teeny-cuda/
+ * src/model/mod.rs:231-700): it owns the parameters, a KV cache and every
+ * activation buffer (allocated once at create, not per forward), runs prefill
+ * stream-ordered without per-op synchronisation, and replays each decode step
+ * as one captured CUDA graph (capture_graph, model/mod.rs:1245).
+ * Pre-norm blocks: x += Wo attn(rope(Wqkv rmsnorm(x))); x += Wdown swiglu(
+ * Wgate/up rmsnorm(x)); logits = lm_head rmsnorm(x_last); greedy argmax. */
+typedef struct tb_decoder tb_decoder;
+
+typedef struct tb_decoder_config {
+    int n_layers, d_model, n_heads, n_kv_heads, head_dim, ffn_hidden, vocab;
+    float rope_theta, norm_eps;
+    int max_batch;          /* sequences per call */
+    int max_seq;            /* KV-cache capacity per sequence (prompt + generated) */
+    int max_prefill_tokens; /* activation rows for prefill (0: max_batch * max_seq) */
+    int weights_int8;       /* 1: linear layers use int8 weight-only GEMV (tokens per call <= 64) */
+} tb_decoder_config;
+
+enum tb_param_kind {
+    TB_P_EMBED = 0,      /* [vocab, d] */
+    TB_P_ATTN_NORM = 1,  /* [d] per layer */
+    TB_P_WQ = 2,         /* [Hq*hd, d] */
+    TB_P_WK = 3,         /* [Hkv*hd, d] */
+    TB_P_WV = 4,         /* [Hkv*hd, d] */
+    TB_P_WO = 5,         /* [d, Hq*hd] */
+    TB_P_MLP_NORM = 6,   /* [d] */
+    TB_P_W_GATE = 7,     /* [F, d] */
+    TB_P_W_UP = 8,       /* [F, d] */
+    TB_P_W_DOWN = 9,     /* [d, F] */
+    TB_P_FINAL_NORM = 10,/* [d] */
+    TB_P_LM_HEAD = 11    /* [vocab, d] */
+};
+
+TB_API int tb_decoder_create(tb_ctx* ctx, const tb_decoder_config* cfg, tb_decoder** out);
+TB_API int tb_decoder_destroy(tb_decoder* dec);
+/* Copies one parameter (f32 or bf16, host or device memory, row-major in the
+ * PyTorch layout listed above) into the decoder's own layout. */
+TB_API int tb_decoder_set_param(tb_decoder* dec, int layer, int kind, const void* src, int src_dtype,
+                                int src_on_host);
+/* Fills every parameter from a counter-based N(0, std) generator (norm
+ * weights = 1).  Deterministic in seed. */
+TB_API int tb_decoder_init_random(tb_decoder* dec, uint64_t seed, float std);
+/* Call after the parameters are set: quantises the linear layers when
+ * weights_int8 is set (tb_quantize_int8 semantics, bit-exact). */
+TB_API int tb_decoder_prepare(tb_decoder* dec);
+/* Prefill B prompts of S tokens (ids: device int32 [B, S]).  Resets the KV
+ * cache, writes the first greedy token.  logits (device f32 [B, vocab]) and
+ * next_ids (device int32 [B]) may be NULL. */
+TB_API int tb_decoder_prefill(tb_decoder* dec, const int32_t* ids, int B, int S, float* logits,
+                              int32_t* next_ids);
+/* One decode step for the B sequences of the last prefill: consumes ids
+ * (device int32 [B], NULL = the previous step's greedy tokens), appends to the
+ * KV cache, writes logits / next_ids (either may be NULL). */
+TB_API int tb_decoder_decode_step(tb_decoder* dec, const int32_t* ids, float* logits, int32_t* next_ids);
+/* Prefill + (n_new - 1) graph-replayed greedy decode steps; out_ids is device
+ * int32 [B, n_new]. */
+TB_API int tb_decoder_generate(tb_decoder* dec, const int32_t* prompt_ids, int B, int S, int n_new,
+                               int32_t* out_ids);
+/* Decode-only workloads: fill the KV cache of B sequences with len positions
+ * of N(0, 1) keys/values and set the current tokens (device int32 [B]). */
+TB_API int tb_decoder_fill_kv_random(tb_decoder* dec, int B, int len, uint64_t seed, const int32_t* ids);
+/* Tokens currently in the KV cache per sequence. */
+TB_API int tb_decoder_seq_len(tb_decoder* dec, int* len);
+
 #ifdef __cplusplus
 }
 #endif

@@ -292,7 +292,7 @@ attn_decode_kernel(DecodeArgs a, int* err) {
     const int G = a.Hq / a.Hkv;
     const int bg = blockIdx.x, split = blockIdx.y;
     const int b = bg / a.Hkv, g = bg % a.Hkv;
-    const int L = a.len_ptr ? *a.len_ptr : a.len;
+    const int L = a.len_ptr ? (*a.len_ptr + a.len) : a.len;   // device length + offset (graph replay)
     const int kbeg = split * a.chunk;
     const int kend = min(L, kbeg + a.chunk);
     const int tid = threadIdx.x;

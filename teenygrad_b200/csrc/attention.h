@@ -38,7 +38,7 @@ struct DecodeArgs {
     int64_t o_sb, o_sh;
     float* lse;
     int Hq, Hkv;
-    int len;               // context length if len_ptr is null
+    int len;               // context length if len_ptr is null, else added to *len_ptr
     const int* len_ptr;    // device-resident context length (CUDA-graph replay)
     float scale_log2;
     int chunk;

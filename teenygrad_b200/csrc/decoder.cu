@@ -1,0 +1,691 @@
+// Decoder executor: parameters, KV cache, activation buffers, prefill and
+// CUDA-graph decode steps, built from the library's kernels.
+#include <math.h>
+
+#include <vector>
+
+#include "attention.h"
+#include "common.cuh"
+#include "gemm.h"
+
+namespace tb {
+
+// ------------------------------------------------------------------ kernels --
+// src row i -> dst row (row_off + (i / block) * block_stride + i % block).
+__global__ void convert_rows_kernel(const void* __restrict__ src, int src_f32, __nv_bfloat16* __restrict__ dst,
+                                    int64_t rows, int64_t cols, int64_t row_off, int64_t block,
+                                    int64_t block_stride) {
+    int64_t total = rows * cols;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        int64_t r = i / cols, c = i % cols;
+        int64_t dr = row_off + (r / block) * block_stride + (r % block);
+        float v = src_f32 ? reinterpret_cast<const float*>(src)[i]
+                          : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(src)[i]);
+        dst[dr * cols + c] = __float2bfloat16_rn(v);
+    }
+}
+
+__device__ __forceinline__ uint64_t splitmix64(uint64_t x) {
+    x += 0x9E3779B97F4A7C15ull;
+    x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+    x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+    return x ^ (x >> 31);
+}
+
+// Counter-based N(0, std): Box-Muller on two splitmix64 draws of (seed, i).
+__global__ void init_normal_kernel(__nv_bfloat16* __restrict__ dst, int64_t n, uint64_t seed, float std) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        uint64_t h1 = splitmix64(seed ^ ((uint64_t)i * 0xD1B54A32D192ED03ull));
+        uint64_t h2 = splitmix64(h1 ^ 0x8CB92BA72F3D8DD7ull);
+        float u1 = ((float)(h1 >> 40) + 0.5f) * (1.0f / 16777216.0f);
+        float u2 = (float)(h2 >> 40) * (1.0f / 16777216.0f);
+        dst[i] = __float2bfloat16_rn(std * sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2));
+    }
+}
+
+__global__ void fill_bf16_kernel(__nv_bfloat16* dst, int64_t n, float v) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        dst[i] = __float2bfloat16_rn(v);
+}
+
+// Same cos/sin as tb_rope_fwd: inv_freq_i = theta^(-2i/hd), angle = pos * inv_freq_i.
+__global__ void rope_table_kernel(float2* tab, int max_seq, int hd, float theta) {
+    int half = hd / 2;
+    int64_t total = (int64_t)max_seq * half;
+    for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += (int64_t)gridDim.x * blockDim.x) {
+        int i = (int)(idx % half);
+        int pos = (int)(idx / half);
+        float inv = powf(theta, -2.0f * (float)i / (float)hd);
+        float s, c;
+        sincosf((float)pos * inv, &s, &c);
+        tab[idx] = make_float2(c, s);
+    }
+}
+
+// One warp per (token, head slot).  Head slots: [0, Hq) query heads (RoPE in
+// place in the qkv row), [Hq, Hq+Hkv) key heads (RoPE, written to the K
+// cache), [Hq+Hkv, Hq+2Hkv) value heads (copied to the V cache).  Position of
+// token s of a sequence = base + s, base from device memory when pos_dev != 0.
+__global__ void rope_kv_kernel(__nv_bfloat16* __restrict__ qkv, int qkv_n, int B, int S_new, int Hq, int Hkv,
+                               int hd, const float2* __restrict__ tab, const int* __restrict__ pos_dev,
+                               int pos_host, __nv_bfloat16* __restrict__ kc, __nv_bfloat16* __restrict__ vc,
+                               int max_seq, int* err) {
+    const int nh = Hq + 2 * Hkv;
+    int64_t gw = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    int lane = threadIdx.x & 31;
+    int64_t t = gw / nh;
+    int hh = (int)(gw % nh);
+    if (t >= (int64_t)B * S_new) return;
+    int b = (int)(t / S_new), s = (int)(t % S_new);
+    int pos = (pos_dev ? *pos_dev : pos_host) + s;
+    if (pos < 0 || pos >= max_seq) {
+        if (lane == 0) atomicOr(err, 1 << 5);
+        return;
+    }
+    __nv_bfloat16* row = qkv + t * qkv_n;
+    const int half = hd / 2;
+    if (hh < Hq + Hkv) {
+        __nv_bfloat16* src = row + (int64_t)hh * hd;
+        __nv_bfloat16* dst = src;
+        if (hh >= Hq) dst = kc + (((int64_t)b * Hkv + (hh - Hq)) * max_seq + pos) * hd;
+        const float2* tb = tab + (int64_t)pos * half;
+        for (int i = lane; i < half; i += 32) {
+            float2 cs = tb[i];
+            float a = __bfloat162float(src[i]), c = __bfloat162float(src[i + half]);
+            float o1 = a * cs.x - c * cs.y, o2 = c * cs.x + a * cs.y;
+            dst[i] = __float2bfloat16_rn(o1);
+            dst[i + half] = __float2bfloat16_rn(o2);
+        }
+    } else {
+        int hk = hh - Hq - Hkv;
+        const __nv_bfloat16* src = row + (int64_t)(Hq + Hkv + hk) * hd;
+        __nv_bfloat16* dst = vc + (((int64_t)b * Hkv + hk) * max_seq + pos) * hd;
+        for (int i = lane; i < hd / 8; i += 32)
+            reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(src)[i];
+    }
+}
+
+// RMSNorm with an input row stride (last-token gather for the LM head).
+__global__ void rmsnorm_ld_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, const __nv_bfloat16* __restrict__ w,
+                                  __nv_bfloat16* __restrict__ y, int M, int N, float eps) {
+    int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    int lane = threadIdx.x & 31;
+    if (row >= M) return;
+    const __nv_bfloat16* xr = x + (int64_t)row * ldx;
+    float ss = 0.f;
+    for (int c = lane * 8; c < N; c += 256) {
+        uint4 v = *reinterpret_cast<const uint4*>(xr + c);
+        uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            float a = bf16_lo(u[i]), b = bf16_hi(u[i]);
+            ss += a * a + b * b;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    float r = rsqrtf(ss * (1.0f / (float)N) + eps);
+    for (int c = lane * 8; c < N; c += 256) {
+        uint4 v = *reinterpret_cast<const uint4*>(xr + c);
+        uint4 g = *reinterpret_cast<const uint4*>(w + c);
+        uint32_t u[4] = {v.x, v.y, v.z, v.w}, gw[4] = {g.x, g.y, g.z, g.w}, o[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+            o[i] = pack_bf16x2(bf16_lo(u[i]) * r * bf16_lo(gw[i]), bf16_hi(u[i]) * r * bf16_hi(gw[i]));
+        *reinterpret_cast<uint4*>(y + (int64_t)row * N + c) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+}
+
+__device__ __forceinline__ void amax_merge2(float& v, int& i, float v2, int i2) {
+    if (i2 < 0) return;
+    if (i < 0 || v2 > v || (v2 == v && i2 < i)) {
+        v = v2;
+        i = i2;
+    }
+}
+
+// Greedy token per row (lowest index on ties, NaN skipped) -> cur_ids[b] and
+// out_ids[b * max_gen + state[1]].
+__global__ void argmax_step_kernel(const float* __restrict__ logits, int V, int32_t* __restrict__ cur_ids,
+                                   int32_t* __restrict__ out_ids, int max_gen, const int* __restrict__ state) {
+    const float* xr = logits + (int64_t)blockIdx.x * V;
+    float bv = -INFINITY;
+    int bi = -1;
+    for (int c = threadIdx.x; c < V; c += blockDim.x) {
+        float v = xr[c];
+        if (v != v) continue;
+        amax_merge2(bv, bi, v, c);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        float v2 = __shfl_xor_sync(0xffffffffu, bv, o);
+        int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+        amax_merge2(bv, bi, v2, i2);
+    }
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+    if (lane == 0) {
+        sv[warp] = bv;
+        si[warp] = bi;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < (int)(blockDim.x / 32); w++) amax_merge2(bv, bi, sv[w], si[w]);
+        int id = bi < 0 ? 0 : bi;
+        cur_ids[blockIdx.x] = id;
+        int step = state[1];
+        if (step < max_gen) out_ids[(int64_t)blockIdx.x * max_gen + step] = id;
+    }
+}
+
+__global__ void advance_kernel(int* state, int dpos, int dstep) {
+    state[0] += dpos;
+    state[1] += dstep;
+}
+
+__global__ void set_state_kernel(int* state, int pos, int step) {
+    state[0] = pos;
+    state[1] = step;
+}
+
+static int grid_for(tb_ctx* ctx, int64_t n) {
+    int64_t b = (n + 255) / 256;
+    int64_t cap = (int64_t)ctx->num_sms * 8;
+    return (int)(b < 1 ? 1 : (b > cap ? cap : b));
+}
+
+}  // namespace tb
+
+using namespace tb;
+using bf16 = __nv_bfloat16;
+
+struct tb_decoder {
+    tb_ctx* ctx = nullptr;
+    tb_decoder_config cfg{};
+    int q_dim = 0, kv_dim = 0, qkv_n = 0;
+    int64_t max_tokens = 0;
+    struct Layer {
+        bf16 *attn_norm, *mlp_norm, *wqkv, *wo, *wgu, *wdown;
+        int8_t *qqkv = nullptr, *qo = nullptr, *qgu = nullptr, *qdown = nullptr;
+        float *sqkv = nullptr, *so = nullptr, *sgu = nullptr, *sdown = nullptr;
+    };
+    std::vector<Layer> layers;
+    bf16 *embed = nullptr, *lm_head = nullptr, *final_norm = nullptr;
+    int8_t* qlm = nullptr;
+    float* slm = nullptr;
+    bf16 *kcache = nullptr, *vcache = nullptr;
+    int64_t cache_layer_elems = 0;
+    float2* rope_tab = nullptr;
+    bf16 *x = nullptr, *h = nullptr, *qkv = nullptr, *attn = nullptr, *act = nullptr;
+    float* logits = nullptr;
+    int32_t *ids_in = nullptr, *cur_ids = nullptr, *out_ids = nullptr;
+    int* state = nullptr;   // [0] tokens in cache, [1] tokens generated
+    float* ws = nullptr;
+    size_t ws_bytes = 0;
+    unsigned* counters = nullptr;
+    size_t n_counters = 0;
+    cudaStream_t cap_stream = nullptr;
+    cudaGraphExec_t graph = nullptr;
+    int graph_B = 0;
+    int B = 0;       // batch of the current sequences
+    int S0 = 0;      // prompt length
+    int host_len = 0, host_step = 0;
+    bool quantized = false;
+    std::vector<void*> allocs;
+
+    template <typename T>
+    int alloc(T** p, size_t n) {
+        void* v = nullptr;
+        if (cudaMalloc(&v, n * sizeof(T) + 16) != cudaSuccess) {
+            cudaGetLastError();
+            return set_error(ctx, TB_ERR_OOM, "decoder: cudaMalloc of %zu bytes failed", n * sizeof(T));
+        }
+        allocs.push_back(v);
+        *p = reinterpret_cast<T*>(v);
+        return TB_OK;
+    }
+};
+
+namespace {
+
+#define TB_TRY(x)          \
+    do {                   \
+        int rc_ = (x);     \
+        if (rc_) return rc_; \
+    } while (0)
+
+int lin(tb_decoder* d, const void* x, const void* w, const int8_t* wq, const float* wscale, void* y, int M, int N,
+        int K, const void* resid, bool swiglu, bool out_f32) {
+    Epi ep{};
+    ep.out = y;
+    ep.ldo = swiglu ? N / 2 : N;
+    ep.resid = resid;
+    ep.ldr = N;
+    ep.out_f32 = out_f32 ? 1 : 0;
+    ep.swiglu = swiglu ? 1 : 0;
+    const bool int8 = d->cfg.weights_int8 && wq;
+    if (int8) ep.scale = wscale;
+    return linear_launch(d->ctx, int8 ? 1 : 0, x, int8 ? (const void*)wq : w, ep, M, N, K, d->ws, d->ws_bytes,
+                         d->counters, d->n_counters);
+}
+
+int rms(tb_decoder* d, const bf16* x, int64_t ldx, const bf16* w, bf16* y, int M) {
+    const int N = d->cfg.d_model;
+    rmsnorm_ld_kernel<<<(M + 7) / 8, 256, 0, d->ctx->stream>>>(x, ldx, w, y, M, N, d->cfg.norm_eps);
+    return check_launch(d->ctx, "rmsnorm");
+}
+
+// One transformer layer over T = B * S_new tokens.  decode: S_new == 1 and
+// positions come from d->state[0].
+int layer_forward(tb_decoder* d, int l, int B, int S_new, bool decode) {
+    const tb_decoder_config& c = d->cfg;
+    tb_ctx* ctx = d->ctx;
+    tb_decoder::Layer& L = d->layers[l];
+    const int T = B * S_new;
+    const int dm = c.d_model, hd = c.head_dim;
+    bf16* kc = d->kcache + (int64_t)l * d->cache_layer_elems;
+    bf16* vc = d->vcache + (int64_t)l * d->cache_layer_elems;
+
+    TB_TRY(rms(d, d->x, dm, L.attn_norm, d->h, T));
+    TB_TRY(lin(d, d->h, L.wqkv, L.qqkv, L.sqkv, d->qkv, T, d->qkv_n, dm, nullptr, false, false));
+    {
+        int64_t warps = (int64_t)T * (c.n_heads + 2 * c.n_kv_heads);
+        rope_kv_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, ctx->stream>>>(
+            d->qkv, d->qkv_n, B, S_new, c.n_heads, c.n_kv_heads, hd, d->rope_tab, decode ? d->state : nullptr, 0,
+            kc, vc, c.max_seq, ctx->d_err);
+        TB_TRY(check_launch(ctx, "rope_kv"));
+    }
+    const float scale = 1.0f / sqrtf((float)hd);
+    if (!decode) {
+        AttnTensors t{};
+        t.q = d->qkv;
+        t.q_sh = hd;
+        t.q_ss = d->qkv_n;
+        t.q_sb = (int64_t)S_new * d->qkv_n;
+        t.k = kc;
+        t.v = vc;
+        t.kv_sh = (int64_t)c.max_seq * hd;
+        t.kv_ss = hd;
+        t.kv_sb = (int64_t)c.n_kv_heads * c.max_seq * hd;
+        t.kv_len_alloc = c.max_seq;
+        t.o = d->attn;
+        t.o_sh = hd;
+        t.o_ss = d->q_dim;
+        t.o_sb = (int64_t)S_new * d->q_dim;
+        t.lse = nullptr;
+        TB_TRY(attn_tc_launch(ctx, t, B, c.n_heads, c.n_kv_heads, S_new, S_new, hd, scale, 1));
+    } else {
+        DecodeArgs a{};
+        a.q = d->qkv;
+        a.q_sb = d->qkv_n;
+        a.q_sh = hd;
+        a.k = kc;
+        a.v = vc;
+        a.kv_sb = (int64_t)c.n_kv_heads * c.max_seq * hd;
+        a.kv_sh = (int64_t)c.max_seq * hd;
+        a.kv_ss = hd;
+        a.o = d->attn;
+        a.o_sb = d->q_dim;
+        a.o_sh = hd;
+        a.lse = nullptr;
+        a.Hq = c.n_heads;
+        a.Hkv = c.n_kv_heads;
+        a.len = 1;                 // keys = tokens already cached + this one
+        a.len_ptr = d->state;
+        a.scale_log2 = scale * 1.4426950408889634f;
+        TB_TRY(attn_decode_launch(ctx, a, B, hd, c.max_seq, d->ws, d->counters));
+    }
+    TB_TRY(lin(d, d->attn, L.wo, L.qo, L.so, d->x, T, dm, d->q_dim, d->x, false, false));
+    TB_TRY(rms(d, d->x, dm, L.mlp_norm, d->h, T));
+    TB_TRY(lin(d, d->h, L.wgu, L.qgu, L.sgu, d->act, T, 2 * c.ffn_hidden, dm, nullptr, true, false));
+    TB_TRY(lin(d, d->act, L.wdown, L.qdown, L.sdown, d->x, T, dm, c.ffn_hidden, d->x, false, false));
+    return TB_OK;
+}
+
+// Final norm on each sequence's last token, LM head, greedy argmax.
+int head_forward(tb_decoder* d, int B, int64_t last_row_stride, int64_t last_row_off) {
+    const tb_decoder_config& c = d->cfg;
+    TB_TRY(rms(d, d->x + last_row_off, last_row_stride, d->final_norm, d->h, B));
+    TB_TRY(lin(d, d->h, d->lm_head, d->qlm, d->slm, d->logits, B, c.vocab, c.d_model, nullptr, false, true));
+    argmax_step_kernel<<<B, 512, 0, d->ctx->stream>>>(d->logits, c.vocab, d->cur_ids, d->out_ids, c.max_seq, d->state);
+    return check_launch(d->ctx, "argmax_step");
+}
+
+int decode_step_body(tb_decoder* d) {
+    const int B = d->B;
+    TB_TRY(tb_embedding_fwd(d->ctx, TB_BF16, d->embed, d->cur_ids, d->x, B, d->cfg.d_model, d->cfg.vocab));
+    for (int l = 0; l < d->cfg.n_layers; l++) TB_TRY(layer_forward(d, l, B, 1, true));
+    TB_TRY(head_forward(d, B, d->cfg.d_model, 0));
+    advance_kernel<<<1, 1, 0, d->ctx->stream>>>(d->state, 1, 1);
+    return check_launch(d->ctx, "advance");
+}
+
+int ensure_graph(tb_decoder* d) {
+    if (d->graph && d->graph_B == d->B) return TB_OK;
+    if (d->graph) {
+        cudaGraphExecDestroy(d->graph);
+        d->graph = nullptr;
+    }
+    tb_ctx* ctx = d->ctx;
+    cudaStream_t saved = ctx->stream;
+    // order capture after everything already queued on the caller's stream
+    TB_CUDA_TRY(ctx, cudaStreamSynchronize(saved));
+    ctx->stream = d->cap_stream;
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamBeginCapture(d->cap_stream, cudaStreamCaptureModeThreadLocal);
+    if (e != cudaSuccess) {
+        ctx->stream = saved;
+        return set_error(ctx, TB_ERR_CUDA, "decode graph: begin capture: %s", cudaGetErrorString(e));
+    }
+    int rc = decode_step_body(d);
+    e = cudaStreamEndCapture(d->cap_stream, &g);
+    ctx->stream = saved;
+    if (rc) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
+    if (e != cudaSuccess) return set_error(ctx, TB_ERR_CUDA, "decode graph: end capture: %s", cudaGetErrorString(e));
+    e = cudaGraphInstantiate(&d->graph, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return set_error(ctx, TB_ERR_CUDA, "decode graph: instantiate: %s", cudaGetErrorString(e));
+    d->graph_B = d->B;
+    return TB_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int tb_decoder_create(tb_ctx* ctx, const tb_decoder_config* cfg, tb_decoder** out) {
+    if (!ctx || !cfg || !out) return TB_ERR_ARG;
+    *out = nullptr;
+    const tb_decoder_config c = *cfg;
+    TB_REQUIRE(ctx, c.n_layers > 0 && c.d_model > 0 && c.n_heads > 0 && c.n_kv_heads > 0 && c.vocab > 0,
+               TB_ERR_SHAPE, "decoder: bad config");
+    TB_REQUIRE(ctx, c.head_dim == 64 || c.head_dim == 128, TB_ERR_SHAPE, "decoder: head_dim must be 64 or 128");
+    TB_REQUIRE(ctx, c.n_heads % c.n_kv_heads == 0 && c.n_heads / c.n_kv_heads <= 8, TB_ERR_SHAPE,
+               "decoder: n_heads must be a multiple of n_kv_heads, group <= 8");
+    TB_REQUIRE(ctx, c.d_model % 64 == 0 && c.ffn_hidden % 128 == 0 && c.vocab % 8 == 0, TB_ERR_SHAPE,
+               "decoder: d_model %% 64, ffn_hidden %% 128, vocab %% 8 must be 0");
+    TB_REQUIRE(ctx, c.max_batch > 0 && c.max_seq > 0, TB_ERR_SHAPE, "decoder: max_batch / max_seq");
+    TB_REQUIRE(ctx, !c.weights_int8 || c.max_batch <= 64, TB_ERR_SHAPE, "decoder int8: max_batch <= 64");
+    tb_decoder* d = new tb_decoder();
+    d->ctx = ctx;
+    d->cfg = c;
+    d->q_dim = c.n_heads * c.head_dim;
+    d->kv_dim = c.n_kv_heads * c.head_dim;
+    d->qkv_n = d->q_dim + 2 * d->kv_dim;
+    d->max_tokens = c.max_prefill_tokens > 0 ? c.max_prefill_tokens : (int64_t)c.max_batch * c.max_seq;
+    if (d->max_tokens < c.max_batch) d->max_tokens = c.max_batch;
+    const int64_t dm = c.d_model, F = c.ffn_hidden, V = c.vocab;
+    int rc = TB_OK;
+    auto A = [&](auto** p, size_t n) {
+        if (!rc) rc = d->alloc(p, n);
+    };
+    d->layers.resize(c.n_layers);
+    for (auto& L : d->layers) {
+        A(&L.attn_norm, dm);
+        A(&L.mlp_norm, dm);
+        A(&L.wqkv, (size_t)d->qkv_n * dm);
+        A(&L.wo, (size_t)dm * d->q_dim);
+        A(&L.wgu, (size_t)2 * F * dm);
+        A(&L.wdown, (size_t)dm * F);
+        if (c.weights_int8) {
+            A(&L.qqkv, (size_t)d->qkv_n * dm);
+            A(&L.qo, (size_t)dm * d->q_dim);
+            A(&L.qgu, (size_t)2 * F * dm);
+            A(&L.qdown, (size_t)dm * F);
+            A(&L.sqkv, d->qkv_n);
+            A(&L.so, dm);
+            A(&L.sgu, 2 * F);
+            A(&L.sdown, dm);
+        }
+    }
+    A(&d->embed, (size_t)V * dm);
+    A(&d->lm_head, (size_t)V * dm);
+    A(&d->final_norm, dm);
+    if (c.weights_int8) {
+        A(&d->qlm, (size_t)V * dm);
+        A(&d->slm, V);
+    }
+    d->cache_layer_elems = (int64_t)c.max_batch * c.n_kv_heads * c.max_seq * c.head_dim;
+    A(&d->kcache, (size_t)d->cache_layer_elems * c.n_layers);
+    A(&d->vcache, (size_t)d->cache_layer_elems * c.n_layers);
+    A(&d->rope_tab, (size_t)c.max_seq * (c.head_dim / 2));
+    const int64_t T = d->max_tokens;
+    A(&d->x, (size_t)T * dm);
+    A(&d->h, (size_t)T * dm);
+    A(&d->qkv, (size_t)T * d->qkv_n);
+    A(&d->attn, (size_t)T * d->q_dim);
+    A(&d->act, (size_t)T * F);
+    A(&d->logits, (size_t)c.max_batch * V);
+    A(&d->ids_in, (size_t)T);
+    A(&d->cur_ids, (size_t)c.max_batch);
+    A(&d->out_ids, (size_t)c.max_batch * c.max_seq);
+    A(&d->state, 4);
+    // split-K / decode-attention scratch, sized for the largest decode-step user
+    size_t need = attn_decode_ws_bytes(c.max_batch, c.n_kv_heads, c.head_dim, c.max_seq), ncnt = (size_t)c.max_batch * c.n_kv_heads;
+    const int Mg = c.max_batch <= 64 ? c.max_batch : 64;
+    const int shapes[5][2] = {{d->qkv_n, (int)dm}, {(int)dm, d->q_dim}, {(int)(2 * F), (int)dm}, {(int)dm, (int)F}, {(int)V, (int)dm}};
+    for (auto& s : shapes) {
+        size_t b = 0, n = 0;
+        gemv_ws_need(ctx, Mg, s[0], s[1], &b, &n);
+        need = need > b ? need : b;
+        ncnt = ncnt > n ? ncnt : n;
+    }
+    d->ws_bytes = need < 1024 ? 1024 : need;
+    d->n_counters = ncnt;
+    A(&d->ws, d->ws_bytes / sizeof(float) + 1);
+    A(&d->counters, ncnt);
+    if (rc) {
+        tb_decoder_destroy(d);
+        return rc;
+    }
+    cudaMemset(d->counters, 0, ncnt * sizeof(unsigned));
+    cudaMemset(d->state, 0, 4 * sizeof(int));
+    cudaMemset(d->kcache, 0, (size_t)d->cache_layer_elems * c.n_layers * sizeof(bf16));
+    cudaMemset(d->vcache, 0, (size_t)d->cache_layer_elems * c.n_layers * sizeof(bf16));
+    rope_table_kernel<<<grid_for(ctx, (int64_t)c.max_seq * c.head_dim / 2), 256, 0, ctx->stream>>>(
+        d->rope_tab, c.max_seq, c.head_dim, c.rope_theta);
+    if (cudaStreamCreateWithFlags(&d->cap_stream, cudaStreamNonBlocking) != cudaSuccess) {
+        tb_decoder_destroy(d);
+        return set_error(ctx, TB_ERR_CUDA, "decoder: stream create failed");
+    }
+    rc = check_launch(ctx, "decoder init");
+    if (rc) {
+        tb_decoder_destroy(d);
+        return rc;
+    }
+    TB_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+    *out = d;
+    return TB_OK;
+}
+
+int tb_decoder_destroy(tb_decoder* d) {
+    if (!d) return TB_OK;
+    cudaSetDevice(d->ctx->device);
+    if (d->graph) cudaGraphExecDestroy(d->graph);
+    if (d->cap_stream) cudaStreamDestroy(d->cap_stream);
+    for (void* p : d->allocs) cudaFree(p);
+    delete d;
+    return TB_OK;
+}
+
+int tb_decoder_set_param(tb_decoder* d, int layer, int kind, const void* src, int src_dtype, int src_on_host) {
+    if (!d || !src) return TB_ERR_ARG;
+    tb_ctx* ctx = d->ctx;
+    const tb_decoder_config& c = d->cfg;
+    TB_REQUIRE(ctx, src_dtype == TB_F32 || src_dtype == TB_BF16, TB_ERR_UNSUPPORTED, "set_param: dtype");
+    const bool per_layer = kind >= TB_P_ATTN_NORM && kind <= TB_P_W_DOWN;
+    TB_REQUIRE(ctx, !per_layer || (layer >= 0 && layer < c.n_layers), TB_ERR_ARG, "set_param: layer %d", layer);
+    const int64_t dm = c.d_model, F = c.ffn_hidden;
+    bf16* dst = nullptr;
+    int64_t rows = 0, cols = dm, row_off = 0, block = 1ll << 40, bstride = 0;
+    tb_decoder::Layer* L = per_layer ? &d->layers[layer] : nullptr;
+    switch (kind) {
+        case TB_P_EMBED: dst = d->embed; rows = c.vocab; break;
+        case TB_P_LM_HEAD: dst = d->lm_head; rows = c.vocab; break;
+        case TB_P_FINAL_NORM: dst = d->final_norm; rows = 1; break;
+        case TB_P_ATTN_NORM: dst = L->attn_norm; rows = 1; break;
+        case TB_P_MLP_NORM: dst = L->mlp_norm; rows = 1; break;
+        case TB_P_WQ: dst = L->wqkv; rows = d->q_dim; break;
+        case TB_P_WK: dst = L->wqkv; rows = d->kv_dim; row_off = d->q_dim; break;
+        case TB_P_WV: dst = L->wqkv; rows = d->kv_dim; row_off = d->q_dim + d->kv_dim; break;
+        case TB_P_WO: dst = L->wo; rows = dm; cols = d->q_dim; break;
+        case TB_P_W_GATE: dst = L->wgu; rows = F; block = 128; bstride = 256; break;
+        case TB_P_W_UP: dst = L->wgu; rows = F; row_off = 128; block = 128; bstride = 256; break;
+        case TB_P_W_DOWN: dst = L->wdown; rows = dm; cols = F; break;
+        default: return set_error(ctx, TB_ERR_ARG, "set_param: kind %d", kind);
+    }
+    const size_t bytes = (size_t)rows * cols * (src_dtype == TB_F32 ? 4 : 2);
+    const void* dsrc = src;
+    void* staging = nullptr;
+    if (src_on_host) {
+        TB_CUDA_TRY(ctx, cudaMalloc(&staging, bytes));
+        TB_CUDA_TRY(ctx, cudaMemcpyAsync(staging, src, bytes, cudaMemcpyHostToDevice, ctx->stream));
+        dsrc = staging;
+    }
+    convert_rows_kernel<<<grid_for(ctx, rows * cols), 256, 0, ctx->stream>>>(dsrc, src_dtype == TB_F32, dst, rows, cols,
+                                                                            row_off, block, bstride);
+    int rc = check_launch(ctx, "set_param");
+    if (staging) {
+        cudaStreamSynchronize(ctx->stream);
+        cudaFree(staging);
+    }
+    d->quantized = false;
+    return rc;
+}
+
+int tb_decoder_init_random(tb_decoder* d, uint64_t seed, float std) {
+    if (!d) return TB_ERR_ARG;
+    tb_ctx* ctx = d->ctx;
+    const tb_decoder_config& c = d->cfg;
+    const int64_t dm = c.d_model, F = c.ffn_hidden;
+    uint64_t stream_id = 0;
+    auto normal = [&](bf16* p, int64_t n) {
+        init_normal_kernel<<<grid_for(ctx, n), 256, 0, ctx->stream>>>(p, n, seed * 0x100000001B3ull + (++stream_id), std);
+    };
+    auto ones = [&](bf16* p, int64_t n) { fill_bf16_kernel<<<grid_for(ctx, n), 256, 0, ctx->stream>>>(p, n, 1.0f); };
+    for (auto& L : d->layers) {
+        ones(L.attn_norm, dm);
+        ones(L.mlp_norm, dm);
+        normal(L.wqkv, (int64_t)d->qkv_n * dm);
+        normal(L.wo, dm * d->q_dim);
+        normal(L.wgu, 2 * F * dm);
+        normal(L.wdown, dm * F);
+    }
+    normal(d->embed, (int64_t)c.vocab * dm);
+    normal(d->lm_head, (int64_t)c.vocab * dm);
+    ones(d->final_norm, dm);
+    d->quantized = false;
+    return check_launch(ctx, "init_random");
+}
+
+int tb_decoder_prepare(tb_decoder* d) {
+    if (!d) return TB_ERR_ARG;
+    if (!d->cfg.weights_int8 || d->quantized) return TB_OK;
+    tb_ctx* ctx = d->ctx;
+    const tb_decoder_config& c = d->cfg;
+    const int64_t dm = c.d_model, F = c.ffn_hidden;
+    for (auto& L : d->layers) {
+        TB_TRY(tb_quantize_int8_bf16(ctx, L.wqkv, L.qqkv, L.sqkv, d->qkv_n, dm));
+        TB_TRY(tb_quantize_int8_bf16(ctx, L.wo, L.qo, L.so, dm, d->q_dim));
+        TB_TRY(tb_quantize_int8_bf16(ctx, L.wgu, L.qgu, L.sgu, 2 * F, dm));
+        TB_TRY(tb_quantize_int8_bf16(ctx, L.wdown, L.qdown, L.sdown, dm, F));
+    }
+    TB_TRY(tb_quantize_int8_bf16(ctx, d->lm_head, d->qlm, d->slm, c.vocab, dm));
+    d->quantized = true;
+    return TB_OK;
+}
+
+int tb_decoder_prefill(tb_decoder* d, const int32_t* ids, int B, int S, float* logits, int32_t* next_ids) {
+    if (!d || !ids) return TB_ERR_ARG;
+    tb_ctx* ctx = d->ctx;
+    const tb_decoder_config& c = d->cfg;
+    TB_REQUIRE(ctx, B > 0 && B <= c.max_batch && S > 0 && S < c.max_seq && (int64_t)B * S <= d->max_tokens,
+               TB_ERR_SHAPE, "prefill: B=%d S=%d exceeds the decoder's capacity", B, S);
+    TB_REQUIRE(ctx, !c.weights_int8 || (int64_t)B * S <= 64, TB_ERR_UNSUPPORTED,
+               "prefill with int8 weights: at most 64 tokens per call");
+    TB_REQUIRE(ctx, !c.weights_int8 || d->quantized, TB_ERR_ARG, "int8 decoder: call tb_decoder_prepare first");
+    d->B = B;
+    d->S0 = S;
+    set_state_kernel<<<1, 1, 0, ctx->stream>>>(d->state, 0, 0);
+    TB_TRY(tb_embedding_fwd(ctx, TB_BF16, d->embed, ids, d->x, (int64_t)B * S, c.d_model, c.vocab));
+    for (int l = 0; l < c.n_layers; l++) TB_TRY(layer_forward(d, l, B, S, false));
+    TB_TRY(head_forward(d, B, (int64_t)S * c.d_model, (int64_t)(S - 1) * c.d_model));
+    advance_kernel<<<1, 1, 0, ctx->stream>>>(d->state, S, 1);
+    TB_TRY(check_launch(ctx, "prefill"));
+    d->host_len = S;
+    d->host_step = 1;
+    if (logits)
+        TB_CUDA_TRY(ctx, cudaMemcpyAsync(logits, d->logits, (size_t)B * c.vocab * sizeof(float), cudaMemcpyDeviceToDevice, ctx->stream));
+    if (next_ids)
+        TB_CUDA_TRY(ctx, cudaMemcpyAsync(next_ids, d->cur_ids, (size_t)B * sizeof(int32_t), cudaMemcpyDeviceToDevice, ctx->stream));
+    return TB_OK;
+}
+
+int tb_decoder_decode_step(tb_decoder* d, const int32_t* ids, float* logits, int32_t* next_ids) {
+    if (!d) return TB_ERR_ARG;
+    tb_ctx* ctx = d->ctx;
+    const tb_decoder_config& c = d->cfg;
+    TB_REQUIRE(ctx, d->B > 0, TB_ERR_ARG, "decode_step: no sequences (call prefill or fill_kv_random)");
+    TB_REQUIRE(ctx, d->host_len < c.max_seq, TB_ERR_SHAPE, "decode_step: KV cache full (%d)", c.max_seq);
+    TB_REQUIRE(ctx, !c.weights_int8 || d->quantized, TB_ERR_ARG, "int8 decoder: call tb_decoder_prepare first");
+    if (ids)
+        TB_CUDA_TRY(ctx, cudaMemcpyAsync(d->cur_ids, ids, (size_t)d->B * sizeof(int32_t), cudaMemcpyDeviceToDevice, ctx->stream));
+    TB_TRY(ensure_graph(d));
+    TB_CUDA_TRY(ctx, cudaGraphLaunch(d->graph, ctx->stream));
+    d->host_len++;
+    d->host_step++;
+    if (logits)
+        TB_CUDA_TRY(ctx, cudaMemcpyAsync(logits, d->logits, (size_t)d->B * c.vocab * sizeof(float), cudaMemcpyDeviceToDevice, ctx->stream));
+    if (next_ids)
+        TB_CUDA_TRY(ctx, cudaMemcpyAsync(next_ids, d->cur_ids, (size_t)d->B * sizeof(int32_t), cudaMemcpyDeviceToDevice, ctx->stream));
+    return TB_OK;
+}
+
+int tb_decoder_generate(tb_decoder* d, const int32_t* prompt_ids, int B, int S, int n_new, int32_t* out_ids) {
+    if (!d || !prompt_ids || !out_ids) return TB_ERR_ARG;
+    TB_REQUIRE(d->ctx, n_new >= 1 && S + n_new <= d->cfg.max_seq, TB_ERR_SHAPE, "generate: S + n_new > max_seq");
+    TB_TRY(tb_decoder_prefill(d, prompt_ids, B, S, nullptr, nullptr));
+    for (int i = 1; i < n_new; i++) TB_TRY(tb_decoder_decode_step(d, nullptr, nullptr, nullptr));
+    TB_CUDA_TRY(d->ctx, cudaMemcpy2DAsync(out_ids, (size_t)n_new * sizeof(int32_t), d->out_ids,
+                                          (size_t)d->cfg.max_seq * sizeof(int32_t), (size_t)n_new * sizeof(int32_t), B,
+                                          cudaMemcpyDeviceToDevice, d->ctx->stream));
+    return TB_OK;
+}
+
+int tb_decoder_fill_kv_random(tb_decoder* d, int B, int len, uint64_t seed, const int32_t* ids) {
+    if (!d || !ids) return TB_ERR_ARG;
+    tb_ctx* ctx = d->ctx;
+    const tb_decoder_config& c = d->cfg;
+    TB_REQUIRE(ctx, B > 0 && B <= c.max_batch && len >= 0 && len < c.max_seq, TB_ERR_SHAPE, "fill_kv_random: B / len");
+    // every (layer, b, kv head) row block of the cache: positions [0, len) get N(0,1)
+    for (int l = 0; l < c.n_layers; l++) {
+        for (int which = 0; which < 2; which++) {
+            bf16* base = (which ? d->vcache : d->kcache) + (int64_t)l * d->cache_layer_elems;
+            for (int bh = 0; bh < B * c.n_kv_heads; bh++) {
+                int64_t n = (int64_t)len * c.head_dim;
+                init_normal_kernel<<<grid_for(ctx, n), 256, 0, ctx->stream>>>(
+                    base + (int64_t)bh * c.max_seq * c.head_dim, n,
+                    seed * 0x100000001B3ull + ((uint64_t)l << 32) + ((uint64_t)which << 31) + bh, 1.0f);
+            }
+        }
+    }
+    TB_CUDA_TRY(ctx, cudaMemcpyAsync(d->cur_ids, ids, (size_t)B * sizeof(int32_t), cudaMemcpyDeviceToDevice, ctx->stream));
+    set_state_kernel<<<1, 1, 0, ctx->stream>>>(d->state, len, 0);
+    d->B = B;
+    d->S0 = len;
+    d->host_len = len;
+    d->host_step = 0;
+    return check_launch(ctx, "fill_kv_random");
+}
+
+int tb_decoder_seq_len(tb_decoder* d, int* len) {
+    if (!d || !len) return TB_ERR_ARG;
+    *len = d->host_len;
+    return TB_OK;
+}
+
+}  // extern "C"

@@ -16,19 +16,10 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "gemm.h"
 
 namespace tb {
 
-struct Epi {
-    void* out;             // y
-    int64_t ldo;           // row stride of y (elements)
-    const float* bias;     // [N] or null
-    const void* resid;     // [M, N] same dtype as y, or null
-    int64_t ldr;
-    const float* scale;    // int8 per-output-channel scale, or null
-    int out_f32;           // y is f32
-    int swiglu;            // gate/up interleaved in 128-row blocks
-};
 
 // ------------------------------------------------------------ store helpers --
 __device__ __forceinline__ void store_row8(void* out, bool f32, int64_t off, const float* v) {
@@ -540,8 +531,27 @@ static int launch_gemm_tc(tb_ctx* ctx, const void* a, const void* b, const Epi& 
     return check_launch(ctx, "gemm_tc");
 }
 
+static void gemv_split(int num_sms, int Nw, int K, int* splits_out, int* kb_per_out) {
+    const int tiles = (Nw + 255) / 256;
+    const int nk = (K + 63) / 64;
+    // Aim for about two CTAs per SM in one wave; each split gets >= 2 K-blocks.
+    int splits = std::max(1, std::min(nk / 2, (2 * num_sms + tiles - 1) / tiles));
+    int kb_per = (nk + splits - 1) / splits;
+    splits = (nk + kb_per - 1) / kb_per;
+    *splits_out = splits;
+    *kb_per_out = kb_per;
+}
+
+void gemv_ws_need(tb_ctx* ctx, int M, int N, int K, size_t* bytes, size_t* counters) {
+    int splits, kb_per;
+    gemv_split(ctx->num_sms, N, K, &splits, &kb_per);
+    *bytes = splits > 1 ? (size_t)splits * M * N * sizeof(float) : 0;
+    *counters = (size_t)(N + 255) / 256;
+}
+
 template <int NT, int STAGES, bool INT8>
-static int launch_gemv_tc(tb_ctx* ctx, const void* x, const void* w, const Epi& ep, int Mtok, int Nw, int K) {
+static int launch_gemv_tc(tb_ctx* ctx, const void* x, const void* w, const Epi& ep, int Mtok, int Nw, int K,
+                          float* ws, size_t ws_bytes, unsigned* counters, size_t n_counters) {
     using C = GemvCfg<NT, STAGES, INT8>;
     CUtensorMap tw, tx;
     int rc;
@@ -556,34 +566,46 @@ static int launch_gemv_tc(tb_ctx* ctx, const void* x, const void* w, const Epi& 
     if (rc) return rc;
     rc = make_tmap_2d(ctx, &tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, Mtok, K, K, 64, NT);
     if (rc) return rc;
+    int splits, kb_per;
+    gemv_split(ctx->num_sms, Nw, K, &splits, &kb_per);
     const int tiles = (Nw + 255) / 256;
-    const int nk = (K + 63) / 64;
-    // Aim for about two CTAs per SM in one wave; each split gets >= 2 K-blocks.
-    int splits = std::max(1, std::min(nk / 2, (2 * ctx->num_sms + tiles - 1) / tiles));
-    int kb_per = (nk + splits - 1) / splits;
-    splits = (nk + kb_per - 1) / kb_per;
-    float* ws = nullptr;
-    if (splits > 1) {
-        rc = ensure_workspace(ctx, (size_t)splits * Mtok * Nw * sizeof(float), tiles);
-        if (rc) return rc;
-        ws = reinterpret_cast<float*>(ctx->ws);
-    } else {
-        rc = ensure_workspace(ctx, 0, tiles);
-        if (rc) return rc;
-    }
+    if ((size_t)tiles > n_counters || !counters)
+        return set_error(ctx, TB_ERR_ARG, "gemv: %d tile counters needed, %zu given", tiles, n_counters);
+    if (splits > 1 && (!ws || (size_t)splits * Mtok * Nw * sizeof(float) > ws_bytes))
+        return set_error(ctx, TB_ERR_ARG, "gemv: split-K workspace too small");
     auto kern = gemv_tc_kernel<NT, STAGES, INT8>;
     TB_CUDA_TRY(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     dim3 grid(tiles, splits);
-    kern<<<grid, 256, C::SMEM, ctx->stream>>>(tw, tx, ep, Nw, K, Mtok, kb_per, splits, ws, ctx->counters, ctx->d_err);
+    kern<<<grid, 256, C::SMEM, ctx->stream>>>(tw, tx, ep, Nw, K, Mtok, kb_per, splits, ws, counters, ctx->d_err);
     return check_launch(ctx, "gemv_tc");
 }
 
 template <bool INT8>
-static int dispatch_gemv(tb_ctx* ctx, const void* x, const void* w, const Epi& ep, int M, int N, int K) {
+static int dispatch_gemv(tb_ctx* ctx, const void* x, const void* w, const Epi& ep, int M, int N, int K,
+                         float* ws, size_t wsb, unsigned* cnt, size_t ncnt) {
     // bf16, <= 32 tokens: 3 stages (~105 KB) so two CTAs share an SM.
-    if (M <= 16) return launch_gemv_tc<16, INT8 ? 6 : 3, INT8>(ctx, x, w, ep, M, N, K);
-    if (M <= 32) return launch_gemv_tc<32, INT8 ? 6 : 3, INT8>(ctx, x, w, ep, M, N, K);
-    return launch_gemv_tc<64, INT8 ? 4 : 4, INT8>(ctx, x, w, ep, M, N, K);
+    if (M <= 16) return launch_gemv_tc<16, INT8 ? 6 : 3, INT8>(ctx, x, w, ep, M, N, K, ws, wsb, cnt, ncnt);
+    if (M <= 32) return launch_gemv_tc<32, INT8 ? 6 : 3, INT8>(ctx, x, w, ep, M, N, K, ws, wsb, cnt, ncnt);
+    return launch_gemv_tc<64, 4, INT8>(ctx, x, w, ep, M, N, K, ws, wsb, cnt, ncnt);
+}
+
+int linear_launch(tb_ctx* ctx, int int8, const void* x, const void* w, const Epi& ep, int M, int N, int K,
+                  float* ws, size_t ws_bytes, unsigned* counters, size_t n_counters) {
+    if (int8) {
+        if (M > 64) return set_error(ctx, TB_ERR_UNSUPPORTED, "int8 linear: at most 64 tokens");
+        return dispatch_gemv<true>(ctx, x, w, ep, M, N, K, ws, ws_bytes, counters, n_counters);
+    }
+    if (M <= 64) return dispatch_gemv<false>(ctx, x, w, ep, M, N, K, ws, ws_bytes, counters, n_counters);
+    if (N <= 128 && !ep.swiglu) return launch_gemm_tc<128, 6, false>(ctx, x, w, ep, M, N, K);
+    return launch_gemm_tc<256, 4, false>(ctx, x, w, ep, M, N, K);
+}
+
+static int ctx_linear(tb_ctx* ctx, int int8, const void* x, const void* w, const Epi& ep, int M, int N, int K) {
+    size_t bytes = 0, cnt = 0;
+    if (M <= 64) gemv_ws_need(ctx, M, N, K, &bytes, &cnt);
+    int rc = ensure_workspace(ctx, bytes, cnt);
+    if (rc) return rc;
+    return linear_launch(ctx, int8, x, w, ep, M, N, K, (float*)ctx->ws, ctx->ws_bytes, ctx->counters, ctx->n_counters);
 }
 
 }  // namespace tb
@@ -626,9 +648,7 @@ int tb_linear_fwd(tb_ctx* ctx, int dtype, const void* x, const void* w, const fl
     ep.resid = (flags & TB_EPI_RESIDUAL) ? residual : nullptr;
     ep.ldr = N;
     ep.swiglu = swiglu ? 1 : 0;
-    if (M <= 64) return dispatch_gemv<false>(ctx, x, w, ep, (int)M, (int)N, (int)K);
-    if (N <= 128 && !swiglu) return launch_gemm_tc<128, 6, false>(ctx, x, w, ep, (int)M, (int)N, (int)K);
-    return launch_gemm_tc<256, 4, false>(ctx, x, w, ep, (int)M, (int)N, (int)K);
+    return ctx_linear(ctx, 0, x, w, ep, (int)M, (int)N, (int)K);
 }
 
 int tb_matmul_fwd(tb_ctx* ctx, int dtype, const void* a, const void* b, void* c, int64_t M, int64_t N, int64_t K) {
@@ -670,7 +690,7 @@ int tb_int8_linear_fwd(tb_ctx* ctx, const void* x, const int8_t* q, const float*
     ep.ldr = N;
     ep.scale = scale;
     ep.swiglu = swiglu ? 1 : 0;
-    return dispatch_gemv<true>(ctx, x, q, ep, (int)M, (int)N, (int)K);
+    return ctx_linear(ctx, 1, x, q, ep, (int)M, (int)N, (int)K);
 }
 
 }  // extern "C"

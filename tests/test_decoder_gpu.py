@@ -1,0 +1,114 @@
+"""GPU parity of the decoder executor against the oracle decoder composition.
+
+Logits: bf16 tolerance 2e-2 (normalised max abs error).  Tokens: the greedy
+token must match wherever the oracle's top-2 margin exceeds the tolerance.
+"""
+import numpy as np
+import pytest
+
+from decoder_util import SmallCfg, upload
+from gpu_util import BF16_TOL, assert_close, dev, no_device_error, np_of, torch
+from oracle.decoder import OracleDecoder, random_params
+
+pytestmark = pytest.mark.gpu
+
+
+def make(cfg, int8=False, max_batch=4, max_seq=160):
+    from teenygrad_b200.decoder import Decoder, DecoderConfig
+    dc = DecoderConfig(n_layers=cfg.n_layers, d_model=cfg.d_model, n_heads=cfg.n_heads, n_kv_heads=cfg.n_kv_heads,
+                       head_dim=cfg.head_dim, ffn_hidden=cfg.ffn_hidden, vocab=cfg.vocab, rope_theta=cfg.rope_theta,
+                       norm_eps=cfg.norm_eps, max_batch=max_batch, max_seq=max_seq, weights_int8=int8)
+    return Decoder(dc)
+
+
+def check_tokens(got, logits_ref):
+    ref = np.argmax(logits_ref, axis=1)
+    srt = np.sort(logits_ref, axis=1)
+    margin = srt[:, -1] - srt[:, -2]
+    scale = max(1.0, np.abs(logits_ref).max())
+    sure = margin > 2 * BF16_TOL * scale
+    assert np.array_equal(np.asarray(got)[sure], ref[sure])
+
+
+@pytest.mark.parametrize("S", [70, 129])
+def test_decoder_prefill_and_decode_bf16(S):
+    dev()
+    cfg = SmallCfg()
+    p = random_params(cfg, seed=3)
+    dec = make(cfg)
+    upload(dec, p)
+    ora = OracleDecoder(cfg, p)
+    ids = np.random.default_rng(S).integers(0, cfg.vocab, (2, S)).astype(np.int32)
+    nxt, logits = dec.prefill(torch.from_numpy(ids).cuda(), return_logits=True)
+    ref = ora.forward(ids)
+    assert_close(np_of(logits), ref, BF16_TOL, "prefill logits")
+    check_tokens(nxt.cpu().numpy(), ref)
+    for step in range(4):   # teacher-forced on the oracle's greedy tokens
+        tok = np.argmax(ref, axis=1).astype(np.int32)
+        nxt, logits = dec.decode_step(torch.from_numpy(tok).cuda(), return_logits=True)
+        ref = ora.forward(tok[:, None])
+        assert_close(np_of(logits), ref, BF16_TOL, f"decode step {step}")
+        check_tokens(nxt.cpu().numpy(), ref)
+    assert dec.seq_len() == S + 4
+    no_device_error()
+
+
+def test_decoder_generate_matches_stepwise():
+    dev()
+    cfg = SmallCfg()
+    p = random_params(cfg, seed=4)
+    dec = make(cfg)
+    upload(dec, p)
+    ids = torch.from_numpy(np.random.default_rng(9).integers(0, cfg.vocab, (3, 40)).astype(np.int32)).cuda()
+    out = dec.generate(ids, n_new=6)
+    toks = [dec.prefill(ids)]
+    for _ in range(5):
+        toks.append(dec.decode_step())
+    step = torch.stack(toks, dim=1)
+    assert torch.equal(out, step)
+    no_device_error()
+
+
+def test_decoder_int8():
+    dev()
+    cfg = SmallCfg()
+    p = random_params(cfg, seed=5)
+    dec = make(cfg, int8=True)
+    upload(dec, p)
+    ora = OracleDecoder(cfg, p, int8=True)
+    ids = np.random.default_rng(2).integers(0, cfg.vocab, (2, 20)).astype(np.int32)
+    nxt, logits = dec.prefill(torch.from_numpy(ids).cuda(), return_logits=True)
+    ref = ora.forward(ids)
+    assert_close(np_of(logits), ref, BF16_TOL, "int8 prefill")
+    for _ in range(3):
+        tok = np.argmax(ref, axis=1).astype(np.int32)
+        nxt, logits = dec.decode_step(torch.from_numpy(tok).cuda(), return_logits=True)
+        ref = ora.forward(tok[:, None])
+        assert_close(np_of(logits), ref, BF16_TOL, "int8 decode")
+    no_device_error()
+
+
+def test_decoder_fill_kv_random_decode_only():
+    dev()
+    cfg = SmallCfg()
+    dec = make(cfg, int8=True, max_batch=8, max_seq=300)
+    dec.init_random(seed=1)
+    ids = torch.arange(8, dtype=torch.int32, device="cuda")
+    dec.fill_kv_random(ids, 256, seed=3)
+    a = dec.decode_step()
+    b = dec.decode_step()
+    assert a.shape == (8,) and int(a.max()) < cfg.vocab and int(b.min()) >= 0
+    assert dec.seq_len() == 258
+    no_device_error()
+
+
+def test_decoder_rejects_bad_shapes():
+    dev()
+    from teenygrad_b200 import TeenyError
+    cfg = SmallCfg()
+    dec = make(cfg, max_seq=64)
+    dec.init_random(0)
+    with pytest.raises(TeenyError):
+        dec.prefill(torch.zeros(5, 10, dtype=torch.int32, device="cuda"))   # B > max_batch
+    with pytest.raises(TeenyError):
+        dec.prefill(torch.zeros(1, 64, dtype=torch.int32, device="cuda"))   # S >= max_seq
