@@ -466,7 +466,9 @@ int tb_decoder_create(tb_ctx* ctx, const tb_decoder_config* cfg, tb_decoder** ou
     A(&d->state, 4);
     // split-K / decode-attention scratch, sized for the largest decode-step user
     size_t need = attn_decode_ws_bytes(c.max_batch, c.n_kv_heads, c.head_dim, c.max_seq), ncnt = (size_t)c.max_batch * c.n_kv_heads;
-    const int Mg = c.max_batch <= 64 ? c.max_batch : 64;
+    // the GEMV path serves every call of <= 64 tokens (decode, small prefills)
+    const int64_t mt = d->max_tokens > c.max_batch ? d->max_tokens : c.max_batch;
+    const int Mg = mt <= 64 ? (int)mt : 64;
     const int shapes[5][2] = {{d->qkv_n, (int)dm}, {(int)dm, d->q_dim}, {(int)(2 * F), (int)dm}, {(int)dm, (int)F}, {(int)V, (int)dm}};
     for (auto& s : shapes) {
         size_t b = 0, n = 0;

@@ -207,40 +207,60 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 }
 
 // =====================================================================
-// Decode GEMV (swap-AB, split-K)
+// Decode GEMV (swap-AB, split-K reduced inside a thread-block cluster)
 // =====================================================================
+// Grid (tiles, CS) with cluster dims (1, CS, 1): the CS CTAs of a cluster
+// split the K range of one 256-row weight tile.  Each CTA parks its f32
+// partial tile [NT tokens][256 rows] in its own shared memory; after a
+// cluster barrier CTA rank r sums the CS partials of rows pairs
+// [r*128/CS, (r+1)*128/CS) over DSMEM (fixed order: deterministic) and runs
+// the epilogue for them.
 template <int NT, int STAGES, bool INT8>
 struct GemvCfg {
     static constexpr int W_BYTES = INT8 ? 256 * 64 : 256 * 128;  // int8: 64 K per row, no swizzle
     static constexpr int X_BYTES = NT * 128;
     static constexpr int C_STAGES = INT8 ? 2 : 0;                 // converted bf16 ring
     static constexpr int C_BYTES = 256 * 128;
-    static constexpr int SMEM = STAGES * (W_BYTES + X_BYTES) + C_STAGES * C_BYTES + 1024 + 512;
+    static constexpr int RED_BYTES = NT * 256 * 4;                // partial tile (reuses the rings)
+    static constexpr int RING = STAGES * (W_BYTES + X_BYTES) + C_STAGES * C_BYTES;
+    static constexpr int SMEM = (RING > RED_BYTES ? RING : RED_BYTES) + 1024 + 512;
     static constexpr int TMEM_COLS = (2 * NT) < 32 ? 32 : (2 * NT);
 };
+
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ float ld_dsmem_f32(uint32_t local_addr, uint32_t rank) {
+    uint32_t remote;
+    float v;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_addr), "r"(rank));
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote));
+    return v;
+}
 
 template <int NT, int STAGES, bool INT8>
 __global__ void __launch_bounds__(256, 1)
 gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
-               Epi ep, int Nw, int K, int Mtok, int kb_per_split, int splits, float* ws,
-               unsigned* counters, int* err) {
+               Epi ep, int Nw, int K, int Mtok, int kb_per_split, int* err) {
     using C = GemvCfg<NT, STAGES, INT8>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sC = smem;                                   // converted bf16 ring (int8 only)
     uint8_t* sW = sC + C::C_STAGES * C::C_BYTES;
     uint8_t* sX = sW + STAGES * C::W_BYTES;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sX + STAGES * C::X_BYTES);
+    float* red = reinterpret_cast<float*>(smem);          // [NT][256] partials, after the MMAs
+    constexpr int BAR_OFF = (C::RING > C::RED_BYTES ? C::RING : C::RED_BYTES);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + BAR_OFF);
     const uint32_t full0 = smem_u32(bars);
     const uint32_t empty0 = smem_u32(bars + STAGES);
     const uint32_t cfull0 = smem_u32(bars + 2 * STAGES);
     const uint32_t cempty0 = smem_u32(bars + 2 * STAGES + 2);
     const uint32_t accb = smem_u32(bars + 2 * STAGES + 4);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
-    int* s_last = reinterpret_cast<int*>(bars + 2 * STAGES + 6);
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
-    const int tile = blockIdx.x, split = blockIdx.y;
+    const int tile = blockIdx.x, split = blockIdx.y, CS = gridDim.y;
     const int nk_total = (K + 63) / 64;
     const int kb0 = split * kb_per_split;
     const int kb1 = min(nk_total, kb0 + kb_per_split);
@@ -345,8 +365,9 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
     }
     __syncwarp();
 
-    // ---------------- epilogue
+    // ---------------- accumulator -> registers
     bool ok = mbar_wait(accb, 0, err, DEV_ERR_TIMEOUT_ACC);
+    ok = __all_sync(0xffffffffu, ok);
     __syncwarp();
     tc_fence_after();
     const int q = warp & 3, part = warp >> 2;
@@ -361,97 +382,90 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
         else tmem_ld32(t_row + h * NT + part * TP, acc[h]);
     }
     tmem_wait_ld();
-    if (nk <= 0) {
+    if (nk <= 0 || !ok) {
 #pragma unroll
         for (int h = 0; h < 2; h++)
 #pragma unroll
             for (int t = 0; t < TP; t++) acc[h][t] = 0.f;
     }
     tc_fence_before();
-    __syncthreads();
+    __syncthreads();   // every MMA has read its smem operands; the rings are free
     if (warp == 1) tmem_dealloc(tmem, C::TMEM_COLS);
-    if (!ok) return;
 
-    const int n_h0 = tile * 256 + l, n_h1 = tile * 256 + 128 + l;
-    const int m_begin = part * TP;
-    if (splits > 1) {
-        // partials: ws[split][m][Nw]
-#pragma unroll
-        for (int t = 0; t < TP; t++) {
-            int m = m_begin + t;
-            if (m < Mtok) {
-                float* dst = ws + ((int64_t)split * Mtok + m) * Nw;
-                if (n_h0 < Nw) dst[n_h0] = acc[0][t];
-                if (n_h1 < Nw) dst[n_h1] = acc[1][t];
-            }
-        }
-        __threadfence();
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            unsigned prev = atomicAdd(&counters[tile], 1u);
-            *s_last = (prev == (unsigned)(splits - 1));
-        }
-        __syncthreads();
-        if (!*s_last) return;
-        __threadfence();
-#pragma unroll
-        for (int t = 0; t < TP; t++) {
-            int m = m_begin + t;
-            float a0 = 0.f, a1 = 0.f;
-            if (m < Mtok) {
-                for (int sp = 0; sp < splits; sp++) {
-                    const float* src = ws + ((int64_t)sp * Mtok + m) * Nw;
-                    if (n_h0 < Nw) a0 += __ldcg(src + n_h0);
-                    if (n_h1 < Nw) a1 += __ldcg(src + n_h1);
-                }
-            }
-            acc[0][t] = a0;
-            acc[1][t] = a1;
-        }
-        if (threadIdx.x == 0) counters[tile] = 0u;
-    }
-
-    // final epilogue: y[m][n]
     const bool f32o = ep.out_f32 != 0;
-    if (ep.swiglu) {
-        const int on = tile * 128 + l;   // output column
-        if (n_h1 < Nw) {
-            float sg = ep.scale ? ep.scale[n_h0] : 1.f, su = ep.scale ? ep.scale[n_h1] : 1.f;
-#pragma unroll
-            for (int t = 0; t < TP; t++) {
-                int m = m_begin + t;
-                if (m < Mtok) {
-                    float o = silu_f(acc[0][t] * sg) * (acc[1][t] * su);
-                    int64_t off = (int64_t)m * ep.ldo + on;
-                    if (f32o) reinterpret_cast<float*>(ep.out)[off] = o;
-                    else reinterpret_cast<__nv_bfloat16*>(ep.out)[off] = __float2bfloat16_rn(o);
-                }
+    auto store = [&](int m, int n, float o) {
+        int64_t off = (int64_t)m * ep.ldo + n;
+        if (f32o) reinterpret_cast<float*>(ep.out)[off] = o;
+        else reinterpret_cast<__nv_bfloat16*>(ep.out)[off] = __float2bfloat16_rn(o);
+    };
+    // epilogue for (token m, row pair p): gate/first row p, second row p + 128
+    auto finish = [&](int m, int p, float a0, float a1) {
+        const int n0 = tile * 256 + p, n1 = n0 + 128;
+        if (ep.swiglu) {
+            if (n1 < Nw) {
+                float sg = ep.scale ? ep.scale[n0] : 1.f, su = ep.scale ? ep.scale[n1] : 1.f;
+                store(m, tile * 128 + p, silu_f(a0 * sg) * (a1 * su));
             }
+            return;
         }
-    } else {
 #pragma unroll
         for (int h = 0; h < 2; h++) {
-            int n = h ? n_h1 : n_h0;
+            const int n = h ? n1 : n0;
             if (n >= Nw) continue;
-            float sc = ep.scale ? ep.scale[n] : 1.f;
-            float bi = ep.bias ? ep.bias[n] : 0.f;
+            float o = (h ? a1 : a0) * (ep.scale ? ep.scale[n] : 1.f) + (ep.bias ? ep.bias[n] : 0.f);
+            if (ep.resid) {
+                int64_t roff = (int64_t)m * ep.ldr + n;
+                o += f32o ? reinterpret_cast<const float*>(ep.resid)[roff]
+                          : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(ep.resid)[roff]);
+            }
+            store(m, n, o);
+        }
+    };
+
+    if (CS == 1) {
+        if (ok) {
 #pragma unroll
             for (int t = 0; t < TP; t++) {
-                int m = m_begin + t;
-                if (m < Mtok) {
-                    float o = acc[h][t] * sc + bi;
-                    if (ep.resid) {
-                        int64_t roff = (int64_t)m * ep.ldr + n;
-                        o += f32o ? reinterpret_cast<const float*>(ep.resid)[roff]
-                                  : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(ep.resid)[roff]);
-                    }
-                    int64_t off = (int64_t)m * ep.ldo + n;
-                    if (f32o) reinterpret_cast<float*>(ep.out)[off] = o;
-                    else reinterpret_cast<__nv_bfloat16*>(ep.out)[off] = __float2bfloat16_rn(o);
-                }
+                const int m = part * TP + t;
+                if (m < Mtok) finish(m, l, acc[0][t], acc[1][t]);
             }
         }
+        return;
     }
+    // partial tile -> own shared memory, [m][row]
+#pragma unroll
+    for (int t = 0; t < TP; t++) {
+        red[(part * TP + t) * 256 + l] = acc[0][t];
+        red[(part * TP + t) * 256 + l + 128] = acc[1][t];
+    }
+    cluster_sync_all();
+    {
+        const int pairs = 128 / CS;           // row pairs reduced by this CTA
+        const int items = pairs * NT;
+        const uint32_t red_base = smem_u32(red);
+        for (int it = threadIdx.x; it < items; it += 256) {
+            const int m = it / pairs, p = split * pairs + (it % pairs);
+            // issue all 2 * CS remote loads before summing (fixed order)
+            float v0[8], v1[8];
+#pragma unroll
+            for (int r = 0; r < 8; r++) {
+                if (r < CS) {
+                    v0[r] = ld_dsmem_f32(red_base + (uint32_t)(m * 256 + p) * 4u, (uint32_t)r);
+                    v1[r] = ld_dsmem_f32(red_base + (uint32_t)(m * 256 + p + 128) * 4u, (uint32_t)r);
+                }
+            }
+            float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+            for (int r = 0; r < 8; r++) {
+                if (r < CS) {
+                    a0 += v0[r];
+                    a1 += v1[r];
+                }
+            }
+            if (ok && m < Mtok) finish(m, p, a0, a1);
+        }
+    }
+    cluster_sync_all();   // peers may still be reading this CTA's partials
 }
 
 // =====================================================================
@@ -531,27 +545,26 @@ static int launch_gemm_tc(tb_ctx* ctx, const void* a, const void* b, const Epi& 
     return check_launch(ctx, "gemm_tc");
 }
 
+// Cluster size (K splits per weight tile): the largest of 8, 4, 2, 1 that
+// keeps the grid within about one CTA per SM and every split >= 2 K-blocks.
 static void gemv_split(int num_sms, int Nw, int K, int* splits_out, int* kb_per_out) {
     const int tiles = (Nw + 255) / 256;
     const int nk = (K + 63) / 64;
-    // Aim for about two CTAs per SM in one wave; each split gets >= 2 K-blocks.
-    int splits = std::max(1, std::min(nk / 2, (2 * num_sms + tiles - 1) / tiles));
-    int kb_per = (nk + splits - 1) / splits;
-    splits = (nk + kb_per - 1) / kb_per;
-    *splits_out = splits;
+    int cs = 8;
+    while (cs > 1 && (tiles * cs > num_sms + num_sms / 4 || nk < 2 * cs)) cs >>= 1;
+    int kb_per = (nk + cs - 1) / cs;
+    *splits_out = cs;
     *kb_per_out = kb_per;
 }
 
 void gemv_ws_need(tb_ctx* ctx, int M, int N, int K, size_t* bytes, size_t* counters) {
-    int splits, kb_per;
-    gemv_split(ctx->num_sms, N, K, &splits, &kb_per);
-    *bytes = splits > 1 ? (size_t)splits * M * N * sizeof(float) : 0;
-    *counters = (size_t)(N + 255) / 256;
+    (void)ctx; (void)M; (void)N; (void)K;
+    *bytes = 0;       // partials stay in shared memory (cluster reduction)
+    *counters = 0;
 }
 
 template <int NT, int STAGES, bool INT8>
-static int launch_gemv_tc(tb_ctx* ctx, const void* x, const void* w, const Epi& ep, int Mtok, int Nw, int K,
-                          float* ws, size_t ws_bytes, unsigned* counters, size_t n_counters) {
+static int launch_gemv_tc(tb_ctx* ctx, const void* x, const void* w, const Epi& ep, int Mtok, int Nw, int K) {
     using C = GemvCfg<NT, STAGES, INT8>;
     CUtensorMap tw, tx;
     int rc;
@@ -566,36 +579,42 @@ static int launch_gemv_tc(tb_ctx* ctx, const void* x, const void* w, const Epi& 
     if (rc) return rc;
     rc = make_tmap_2d(ctx, &tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, Mtok, K, K, 64, NT);
     if (rc) return rc;
-    int splits, kb_per;
-    gemv_split(ctx->num_sms, Nw, K, &splits, &kb_per);
+    int cs, kb_per;
+    gemv_split(ctx->num_sms, Nw, K, &cs, &kb_per);
     const int tiles = (Nw + 255) / 256;
-    if ((size_t)tiles > n_counters || !counters)
-        return set_error(ctx, TB_ERR_ARG, "gemv: %d tile counters needed, %zu given", tiles, n_counters);
-    if (splits > 1 && (!ws || (size_t)splits * Mtok * Nw * sizeof(float) > ws_bytes))
-        return set_error(ctx, TB_ERR_ARG, "gemv: split-K workspace too small");
     auto kern = gemv_tc_kernel<NT, STAGES, INT8>;
     TB_CUDA_TRY(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
-    dim3 grid(tiles, splits);
-    kern<<<grid, 256, C::SMEM, ctx->stream>>>(tw, tx, ep, Nw, K, Mtok, kb_per, splits, ws, counters, ctx->d_err);
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3(tiles, cs, 1);
+    lc.blockDim = dim3(256, 1, 1);
+    lc.dynamicSmemBytes = C::SMEM;
+    lc.stream = ctx->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = cs;
+    attr[0].val.clusterDim.z = 1;
+    lc.attrs = attr;
+    lc.numAttrs = 1;
+    TB_CUDA_TRY(ctx, cudaLaunchKernelEx(&lc, kern, tw, tx, ep, Nw, K, Mtok, kb_per, ctx->d_err));
     return check_launch(ctx, "gemv_tc");
 }
 
 template <bool INT8>
-static int dispatch_gemv(tb_ctx* ctx, const void* x, const void* w, const Epi& ep, int M, int N, int K,
-                         float* ws, size_t wsb, unsigned* cnt, size_t ncnt) {
-    // bf16, <= 32 tokens: 3 stages (~105 KB) so two CTAs share an SM.
-    if (M <= 16) return launch_gemv_tc<16, INT8 ? 6 : 3, INT8>(ctx, x, w, ep, M, N, K, ws, wsb, cnt, ncnt);
-    if (M <= 32) return launch_gemv_tc<32, INT8 ? 6 : 3, INT8>(ctx, x, w, ep, M, N, K, ws, wsb, cnt, ncnt);
-    return launch_gemv_tc<64, 4, INT8>(ctx, x, w, ep, M, N, K, ws, wsb, cnt, ncnt);
+static int dispatch_gemv(tb_ctx* ctx, const void* x, const void* w, const Epi& ep, int M, int N, int K) {
+    // One CTA per SM, rings of ~200 KB keep enough weight bytes in flight.
+    if (M <= 16) return launch_gemv_tc<16, 6, INT8>(ctx, x, w, ep, M, N, K);
+    if (M <= 32) return launch_gemv_tc<32, 6, INT8>(ctx, x, w, ep, M, N, K);
+    return launch_gemv_tc<64, INT8 ? 6 : 5, INT8>(ctx, x, w, ep, M, N, K);
 }
 
 int linear_launch(tb_ctx* ctx, int int8, const void* x, const void* w, const Epi& ep, int M, int N, int K,
                   float* ws, size_t ws_bytes, unsigned* counters, size_t n_counters) {
     if (int8) {
         if (M > 64) return set_error(ctx, TB_ERR_UNSUPPORTED, "int8 linear: at most 64 tokens");
-        return dispatch_gemv<true>(ctx, x, w, ep, M, N, K, ws, ws_bytes, counters, n_counters);
+        return dispatch_gemv<true>(ctx, x, w, ep, M, N, K);
     }
-    if (M <= 64) return dispatch_gemv<false>(ctx, x, w, ep, M, N, K, ws, ws_bytes, counters, n_counters);
+    if (M <= 64) return dispatch_gemv<false>(ctx, x, w, ep, M, N, K);
     if (N <= 128 && !ep.swiglu) return launch_gemm_tc<128, 6, false>(ctx, x, w, ep, M, N, K);
     return launch_gemm_tc<256, 4, false>(ctx, x, w, ep, M, N, K);
 }
