@@ -62,6 +62,8 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
     const uint32_t o_done = smem_u32(bars + 10);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
 
+    pdl_trigger();
+    pdl_wait();
     const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
     const int q_tile = gridDim.x - 1 - blockIdx.x;   // heaviest causal tiles first
     const int h = blockIdx.y, b = blockIdx.z;
@@ -272,43 +274,44 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
 }
 
 // -------------------------------------------------------------- decode -----
-// Grid (B * Hkv, splits).  Each CTA (128 threads) handles keys
-// [split * chunk, ...) for the G = Hq / Hkv query heads that share one kv
-// head, 64 keys at a time staged in shared memory.  Partials (running max m,
-// sum l, unnormalised o) go to ws; the last CTA of the group merges them.
-// Supports D = 64 or 128, G <= 8, Sq = 1 per sequence.
+// Grid (B * Hkv, splits), 128 threads.  A CTA owns keys [split * chunk, ...)
+// of one (batch, kv head) group and all G = Hq / Hkv query heads reading it,
+// walking them 128 keys at a time: thread t scores key t against the G
+// queries (K row in registers, queries broadcast from shared memory), the
+// block forms the chunk's max / exp / sum per head, then thread (head, dim
+// pair) accumulates P V with V staged in shared memory by cp.async.  Each CTA
+// leaves (max, sum, unnormalised o) per head in ws; the last CTA of the group
+// merges the splits in split order (deterministic).  D = 64 or 128, G <= 8.
 template <int D>
 __global__ void __launch_bounds__(128)
 attn_decode_kernel(DecodeArgs a, int* err) {
-    constexpr int KC = 64;             // keys per staged sub-chunk
-    constexpr int RS = D + 8;          // padded smem row (bf16) against bank conflicts
-    __shared__ __align__(16) __nv_bfloat16 sk[KC * RS];
-    __shared__ __align__(16) __nv_bfloat16 sv[KC * RS];
+    constexpr int KC = 128;
+    __shared__ __align__(16) __nv_bfloat16 sv[KC * D];
     __shared__ float sq[8][D];
     __shared__ float sp[8][KC];
+    __shared__ float s_wred[8][4];
     __shared__ float s_m[8], s_l[8], s_alpha[8];
     __shared__ int s_last;
 
+    pdl_trigger();
+    pdl_wait();
     const int G = a.Hq / a.Hkv;
-    const int bg = blockIdx.x, split = blockIdx.y;
+    const int bg = blockIdx.x, split = blockIdx.y, nsp = gridDim.y;
     const int b = bg / a.Hkv, g = bg % a.Hkv;
-    const int L = a.len_ptr ? (*a.len_ptr + a.len) : a.len;   // device length + offset (graph replay)
+    const int L = a.len_ptr ? (*a.len_ptr + a.len) : a.len;
     const int kbeg = split * a.chunk;
     const int kend = min(L, kbeg + a.chunk);
-    const int tid = threadIdx.x;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
-    // queries of this group -> smem (f32, pre-scaled into the exp2 domain)
     for (int i = tid; i < G * D; i += 128) {
         int gg = i / D, d = i % D;
-        const __nv_bfloat16* qp = a.q + (int64_t)b * a.q_sb + (int64_t)(g * G + gg) * a.q_sh + d;
-        sq[gg][d] = __bfloat162float(*qp) * a.scale_log2;
+        sq[gg][d] = __bfloat162float(a.q[(int64_t)b * a.q_sb + (int64_t)(g * G + gg) * a.q_sh + d]) * a.scale_log2;
     }
     if (tid < 8) {
         s_m[tid] = -INFINITY;
         s_l[tid] = 0.f;
     }
-    // each thread owns output elements (gg, d) for idx = tid + 128 * i
-    constexpr int OPT = (8 * D) / 128;
+    constexpr int OPT = (8 * D) / 128;   // output elements per thread (covers G <= 8)
     float acc[OPT];
 #pragma unroll
     for (int i = 0; i < OPT; i++) acc[i] = 0.f;
@@ -318,81 +321,96 @@ attn_decode_kernel(DecodeArgs a, int* err) {
     const __nv_bfloat16* vbase = a.v + (int64_t)b * a.kv_sb + (int64_t)g * a.kv_sh;
     for (int k0 = kbeg; k0 < kend; k0 += KC) {
         const int nk = min(KC, kend - k0);
-        // stage K and V rows (16 B per thread per step)
-        constexpr int CPR = D / 8;   // 16-B chunks per row
+        // V chunk -> smem (async), rows >= nk zero
+        constexpr int CPR = D / 8;
         for (int i = tid; i < KC * CPR; i += 128) {
             int r = i / CPR, c = i % CPR;
-            uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
+            uint32_t dst = smem_u32(&sv[r * D + c * 8]);
             if (r < nk) {
-                kv = *reinterpret_cast<const uint4*>(kbase + (int64_t)(k0 + r) * a.kv_ss + c * 8);
-                vv = *reinterpret_cast<const uint4*>(vbase + (int64_t)(k0 + r) * a.kv_ss + c * 8);
+                const void* src = vbase + (int64_t)(k0 + r) * a.kv_ss + c * 8;
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+            } else {
+                *reinterpret_cast<uint4*>(&sv[r * D + c * 8]) = make_uint4(0, 0, 0, 0);
             }
-            *reinterpret_cast<uint4*>(&sk[r * RS + c * 8]) = kv;
-            *reinterpret_cast<uint4*>(&sv[r * RS + c * 8]) = vv;
         }
-        __syncthreads();
-        // scores: G x KC dot products
-        for (int i = tid; i < G * KC; i += 128) {
-            int gg = i / KC, r = i % KC;
-            float sacc = -INFINITY;
-            if (r < nk) {
-                sacc = 0.f;
-                const __nv_bfloat16* kr = &sk[r * RS];
-#pragma unroll 8
-                for (int d = 0; d < D; d += 2) {
-                    __nv_bfloat162 kk = *reinterpret_cast<const __nv_bfloat162*>(kr + d);
-                    sacc = fmaf(sq[gg][d], __low2float(kk), sacc);
-                    sacc = fmaf(sq[gg][d + 1], __high2float(kk), sacc);
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        // scores: thread tid <-> key k0 + tid
+        float s[8];
+#pragma unroll
+        for (int gg = 0; gg < 8; gg++) s[gg] = -INFINITY;
+        if (tid < nk) {
+            const uint4* kr = reinterpret_cast<const uint4*>(kbase + (int64_t)(k0 + tid) * a.kv_ss);
+#pragma unroll
+            for (int gg = 0; gg < 8; gg++)
+                if (gg < G) s[gg] = 0.f;
+#pragma unroll
+            for (int c = 0; c < D / 8; c++) {
+                uint4 kv = __ldg(kr + c);
+                uint32_t w[4] = {kv.x, kv.y, kv.z, kv.w};
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    float k0f = bf16_lo(w[j]), k1f = bf16_hi(w[j]);
+#pragma unroll
+                    for (int gg = 0; gg < 8; gg++) {
+                        if (gg < G) {
+                            s[gg] = fmaf(sq[gg][c * 8 + 2 * j], k0f, s[gg]);
+                            s[gg] = fmaf(sq[gg][c * 8 + 2 * j + 1], k1f, s[gg]);
+                        }
+                    }
                 }
             }
-            sp[gg][r] = sacc;
+        }
+        // chunk max per head
+#pragma unroll
+        for (int gg = 0; gg < 8; gg++) {
+            if (gg < G) {
+                float m = s[gg];
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+                if (lane == 0) s_wred[gg][warp] = m;
+            }
         }
         __syncthreads();
-        // per-head max / exp / sum: warp w handles heads w, w+4
-        {
-            const int w = tid / 32, ln = tid & 31;
-            for (int gg = w; gg < G; gg += 4) {
-                float v0 = sp[gg][ln], v1 = sp[gg][ln + 32];
-                float mx = fmaxf(v0, v1);
+        if (tid < G) {
+            float m = fmaxf(fmaxf(s_wred[tid][0], s_wred[tid][1]), fmaxf(s_wred[tid][2], s_wred[tid][3]));
+            float m_old = s_m[tid], m_new = fmaxf(m_old, m);
+            s_alpha[tid] = ex2(m_old - m_new);
+            s_m[tid] = m_new;
+        }
+        __syncthreads();
 #pragma unroll
-                for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-                float m_old = s_m[gg];
-                float m_new = fmaxf(m_old, mx);
-                float p0 = ex2(v0 - m_new), p1 = ex2(v1 - m_new);
-                sp[gg][ln] = p0;
-                sp[gg][ln + 32] = p1;
-                float sum = p0 + p1;
+        for (int gg = 0; gg < 8; gg++) {
+            if (gg < G) {
+                float p = (tid < nk) ? ex2(s[gg] - s_m[gg]) : 0.f;
+                sp[gg][tid] = p;
+                float sum = p;
 #pragma unroll
                 for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-                if (ln == 0) {
-                    float al = ex2(m_old - m_new);
-                    s_alpha[gg] = al;
-                    s_l[gg] = s_l[gg] * al + sum;
-                    s_m[gg] = m_new;
-                }
+                if (lane == 0) s_wred[gg][warp] = sum;
             }
         }
+        asm volatile("cp.async.wait_all;" ::: "memory");
         __syncthreads();
+        if (tid < G) s_l[tid] = s_l[tid] * s_alpha[tid] + (s_wred[tid][0] + s_wred[tid][1] + s_wred[tid][2] + s_wred[tid][3]);
+        // P V: idx = tid + 128 * i -> (head gg, dim d)
 #pragma unroll
         for (int i = 0; i < OPT; i++) {
-            int idx = tid + 128 * i;
-            int gg = idx / D, d = idx % D;
+            const int idx = tid + 128 * i, gg = idx / D, d = idx % D;
             if (gg < G) {
                 float o = acc[i] * s_alpha[gg];
-                for (int r = 0; r < nk; r++) o = fmaf(sp[gg][r], __bfloat162float(sv[r * RS + d]), o);
+                for (int r = 0; r < nk; r++) o = fmaf(sp[gg][r], __bfloat162float(sv[r * D + d]), o);
                 acc[i] = o;
             }
         }
         __syncthreads();
     }
 
-    // partials -> ws[(bg * splits + split)][G][D + 2]
+    // partial -> ws[(bg * nsp + split)][8][D + 2]
     const int stride = D + 2;
-    float* wp = a.ws + ((int64_t)bg * gridDim.y + split) * 8 * stride;
+    float* wp = a.ws + ((int64_t)bg * nsp + split) * 8 * stride;
 #pragma unroll
     for (int i = 0; i < OPT; i++) {
-        int idx = tid + 128 * i;
-        int gg = idx / D, d = idx % D;
+        const int idx = tid + 128 * i, gg = idx / D, d = idx % D;
         if (gg < G) wp[gg * stride + d] = acc[i];
     }
     if (tid < G) {
@@ -401,29 +419,37 @@ attn_decode_kernel(DecodeArgs a, int* err) {
     }
     __threadfence();
     __syncthreads();
-    if (tid == 0) s_last = (atomicAdd(&a.counters[bg], 1u) == gridDim.y - 1);
+    if (tid == 0) s_last = (atomicAdd(&a.counters[bg], 1u) == (unsigned)(nsp - 1));
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    // merge
-    const int nsp = gridDim.y;
+    constexpr int MAXSP = 16;
     for (int idx = tid; idx < G * D; idx += 128) {
-        int gg = idx / D, d = idx % D;
+        const int gg = idx / D, d = idx % D;
+        float mv[MAXSP], lv[MAXSP], ov[MAXSP];
+#pragma unroll
+        for (int sp_i = 0; sp_i < MAXSP; sp_i++) {
+            if (sp_i < nsp) {
+                const float* p = a.ws + ((int64_t)bg * nsp + sp_i) * 8 * stride + gg * stride;
+                mv[sp_i] = __ldcg(p + D);
+                lv[sp_i] = __ldcg(p + D + 1);
+                ov[sp_i] = __ldcg(p + d);
+            }
+        }
         float M = -INFINITY;
-        for (int sp_i = 0; sp_i < nsp; sp_i++) {
-            const float* p = a.ws + ((int64_t)bg * nsp + sp_i) * 8 * stride + gg * stride;
-            M = fmaxf(M, __ldcg(p + D));
-        }
+#pragma unroll
+        for (int sp_i = 0; sp_i < MAXSP; sp_i++)
+            if (sp_i < nsp) M = fmaxf(M, mv[sp_i]);
         float l = 0.f, o = 0.f;
-        for (int sp_i = 0; sp_i < nsp; sp_i++) {
-            const float* p = a.ws + ((int64_t)bg * nsp + sp_i) * 8 * stride + gg * stride;
-            float mi = __ldcg(p + D);
-            float w = (mi == -INFINITY) ? 0.f : ex2(mi - M);
-            l += __ldcg(p + D + 1) * w;
-            o += __ldcg(p + d) * w;
+#pragma unroll
+        for (int sp_i = 0; sp_i < MAXSP; sp_i++) {
+            if (sp_i < nsp) {
+                float w = (mv[sp_i] == -INFINITY) ? 0.f : ex2(mv[sp_i] - M);
+                l += lv[sp_i] * w;
+                o += ov[sp_i] * w;
+            }
         }
-        float r = l > 0.f ? o / l : 0.f;
-        a.o[(int64_t)b * a.o_sb + (int64_t)(g * G + gg) * a.o_sh + d] = __float2bfloat16_rn(r);
+        a.o[(int64_t)b * a.o_sb + (int64_t)(g * G + gg) * a.o_sh + d] = __float2bfloat16_rn(l > 0.f ? o / l : 0.f);
         if (d == 0 && a.lse) a.lse[(int64_t)b * a.Hq + g * G + gg] = l > 0.f ? (M + log2f(l)) * kLn2 : -INFINITY;
     }
     if (tid == 0) a.counters[bg] = 0u;
@@ -499,31 +525,37 @@ int attn_tc_launch(tb_ctx* ctx, const AttnTensors& t, int B, int Hq, int Hkv, in
         // 512 TMEM columns per CTA: keep one CTA per SM (the padding does that).
         constexpr int smem = AttnCfg<64>::SMEM > 120 * 1024 ? AttnCfg<64>::SMEM : 120 * 1024;
         TB_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-        attn_tc_kernel<64><<<grid, 192, smem, ctx->stream>>>(mq, mk, mv, out, Hq, Hkv, Sq, Sk, sl2, causal, ctx->d_err);
+        return launch(ctx, "attn_tc", attn_tc_kernel<64>, grid, dim3(192), smem, mq, mk, mv, out, Hq, Hkv, Sq, Sk, sl2, causal, ctx->d_err);
     } else {
         constexpr int smem = AttnCfg<128>::SMEM;
         TB_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-        attn_tc_kernel<128><<<grid, 192, smem, ctx->stream>>>(mq, mk, mv, out, Hq, Hkv, Sq, Sk, sl2, causal, ctx->d_err);
+        return launch(ctx, "attn_tc", attn_tc_kernel<128>, grid, dim3(192), smem, mq, mk, mv, out, Hq, Hkv, Sq, Sk, sl2, causal, ctx->d_err);
     }
     return check_launch(ctx, "attn_tc");
 }
 
+// Context chunk per CTA: a multiple of 128 keys, at most 16 splits.
+static int decode_chunk(int max_len) {
+    int sub = (max_len + 127) / 128;          // 128-key sub-chunks
+    int per = (sub + 15) / 16;                // sub-chunks per split
+    return 128 * (per < 1 ? 1 : per);
+}
+
 int attn_decode_launch(tb_ctx* ctx, DecodeArgs a, int B, int D, int max_len, float* ws, unsigned* counters) {
     const int groups = B * a.Hkv;
-    int chunk = 256;
-    int splits = (max_len + chunk - 1) / chunk;
+    a.chunk = decode_chunk(max_len);
+    int splits = (max_len + a.chunk - 1) / a.chunk;
     if (splits < 1) splits = 1;
-    a.chunk = chunk;
     a.ws = ws;
     a.counters = counters;
     dim3 grid(groups, splits);
-    if (D == 64) attn_decode_kernel<64><<<grid, 128, 0, ctx->stream>>>(a, ctx->d_err);
-    else attn_decode_kernel<128><<<grid, 128, 0, ctx->stream>>>(a, ctx->d_err);
-    return check_launch(ctx, "attn_decode");
+    if (D == 64) return launch(ctx, "attn_decode", attn_decode_kernel<64>, grid, dim3(128), 0, a, ctx->d_err);
+    return launch(ctx, "attn_decode", attn_decode_kernel<128>, grid, dim3(128), 0, a, ctx->d_err);
 }
 
 size_t attn_decode_ws_bytes(int B, int Hkv, int D, int max_len) {
-    int splits = (max_len + 255) / 256;
+    const int chunk = decode_chunk(max_len);
+    int splits = (max_len + chunk - 1) / chunk;
     if (splits < 1) splits = 1;
     return (size_t)B * Hkv * splits * 8 * (D + 2) * sizeof(float);
 }

@@ -225,6 +225,17 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float* v) {
         : "memory");
 }
 
+// ------------------------------------------ programmatic dependent launch --
+// Kernels launched with the programmatic-serialization attribute may start
+// while their predecessor is still running.  pdl_wait() blocks until every
+// prerequisite grid has completed and its writes are visible; each kernel
+// calls it before its first read of data produced upstream and before its
+// first global write.  pdl_trigger() lets the successor launch early (it takes
+// effect once every CTA of this grid has executed it or exited).  Both are
+// no-ops for a normal launch.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ------------------------------------------------------------ descriptors --
 // Shared-memory matrix descriptor (tcgen05), 128-byte swizzle.
 //   bits  0-13 start address >> 4

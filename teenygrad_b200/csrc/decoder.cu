@@ -62,52 +62,70 @@ __global__ void rope_table_kernel(float2* tab, int max_seq, int hd, float theta)
     }
 }
 
-// One warp per (token, head slot).  Head slots: [0, Hq) query heads (RoPE in
-// place in the qkv row), [Hq, Hq+Hkv) key heads (RoPE, written to the K
-// cache), [Hq+Hkv, Hq+2Hkv) value heads (copied to the V cache).  Position of
-// token s of a sequence = base + s, base from device memory when pos_dev != 0.
+// One thread per (token, head slot, 8-element chunk c of the first half):
+// it rotates the 16-byte chunks c of both halves (rotate-half pairing).
+// Head slots: [0, Hq) query heads (in place in the qkv row), [Hq, Hq+Hkv) key
+// heads (written to the K cache), [Hq+Hkv, Hq+2Hkv) value heads (copied to the
+// V cache).  Position of token s = base + s, base from device memory when
+// pos_dev != 0.
 __global__ void rope_kv_kernel(__nv_bfloat16* __restrict__ qkv, int qkv_n, int B, int S_new, int Hq, int Hkv,
                                int hd, const float2* __restrict__ tab, const int* __restrict__ pos_dev,
                                int pos_host, __nv_bfloat16* __restrict__ kc, __nv_bfloat16* __restrict__ vc,
                                int max_seq, int* err) {
+    pdl_trigger();
+    pdl_wait();
     const int nh = Hq + 2 * Hkv;
-    int64_t gw = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
-    int lane = threadIdx.x & 31;
-    int64_t t = gw / nh;
-    int hh = (int)(gw % nh);
-    if (t >= (int64_t)B * S_new) return;
-    int b = (int)(t / S_new), s = (int)(t % S_new);
-    int pos = (pos_dev ? *pos_dev : pos_host) + s;
-    if (pos < 0 || pos >= max_seq) {
-        if (lane == 0) atomicOr(err, 1 << 5);
-        return;
-    }
-    __nv_bfloat16* row = qkv + t * qkv_n;
-    const int half = hd / 2;
-    if (hh < Hq + Hkv) {
-        __nv_bfloat16* src = row + (int64_t)hh * hd;
-        __nv_bfloat16* dst = src;
-        if (hh >= Hq) dst = kc + (((int64_t)b * Hkv + (hh - Hq)) * max_seq + pos) * hd;
-        const float2* tb = tab + (int64_t)pos * half;
-        for (int i = lane; i < half; i += 32) {
-            float2 cs = tb[i];
-            float a = __bfloat162float(src[i]), c = __bfloat162float(src[i + half]);
-            float o1 = a * cs.x - c * cs.y, o2 = c * cs.x + a * cs.y;
-            dst[i] = __float2bfloat16_rn(o1);
-            dst[i + half] = __float2bfloat16_rn(o2);
+    const int half = hd / 2, cph = half / 8;        // chunks per half
+    const int64_t total = (int64_t)B * S_new * nh * cph;
+    const int base = pos_dev ? *pos_dev : pos_host;
+    for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+         idx += (int64_t)gridDim.x * blockDim.x) {
+        const int c = (int)(idx % cph);
+        const int64_t th = idx / cph;
+        const int hh = (int)(th % nh);
+        const int64_t t = th / nh;
+        const int b = (int)(t / S_new), s = (int)(t % S_new);
+        const int pos = base + s;
+        if (pos < 0 || pos >= max_seq) {
+            atomicOr(err, 1 << 5);
+            continue;
         }
-    } else {
-        int hk = hh - Hq - Hkv;
-        const __nv_bfloat16* src = row + (int64_t)(Hq + Hkv + hk) * hd;
-        __nv_bfloat16* dst = vc + (((int64_t)b * Hkv + hk) * max_seq + pos) * hd;
-        for (int i = lane; i < hd / 8; i += 32)
-            reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(src)[i];
+        __nv_bfloat16* src = qkv + t * qkv_n + (int64_t)hh * hd;
+        uint4* lo = reinterpret_cast<uint4*>(src + 8 * c);
+        uint4* hi = reinterpret_cast<uint4*>(src + half + 8 * c);
+        if (hh >= Hq + Hkv) {
+            __nv_bfloat16* dst = vc + (((int64_t)b * Hkv + (hh - Hq - Hkv)) * max_seq + pos) * hd;
+            reinterpret_cast<uint4*>(dst + 8 * c)[0] = *lo;
+            reinterpret_cast<uint4*>(dst + half + 8 * c)[0] = *hi;
+            continue;
+        }
+        uint4 va = *lo, vb = *hi;
+        uint32_t xa[4] = {va.x, va.y, va.z, va.w}, xb[4] = {vb.x, vb.y, vb.z, vb.w}, oa[4], ob[4];
+        const float4* tp = reinterpret_cast<const float4*>(tab + (int64_t)pos * half + 8 * c);
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            float4 cs = tp[j];   // (cos, sin) of elements 2j, 2j+1
+            float a0 = bf16_lo(xa[j]), a1 = bf16_hi(xa[j]), b0 = bf16_lo(xb[j]), b1 = bf16_hi(xb[j]);
+            oa[j] = pack_bf16x2(a0 * cs.x - b0 * cs.y, a1 * cs.z - b1 * cs.w);
+            ob[j] = pack_bf16x2(b0 * cs.x + a0 * cs.y, b1 * cs.z + a1 * cs.w);
+        }
+        uint4* dlo = lo;
+        uint4* dhi = hi;
+        if (hh >= Hq) {
+            __nv_bfloat16* dst = kc + (((int64_t)b * Hkv + (hh - Hq)) * max_seq + pos) * hd;
+            dlo = reinterpret_cast<uint4*>(dst + 8 * c);
+            dhi = reinterpret_cast<uint4*>(dst + half + 8 * c);
+        }
+        *dlo = make_uint4(oa[0], oa[1], oa[2], oa[3]);
+        *dhi = make_uint4(ob[0], ob[1], ob[2], ob[3]);
     }
 }
 
 // RMSNorm with an input row stride (last-token gather for the LM head).
 __global__ void rmsnorm_ld_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, const __nv_bfloat16* __restrict__ w,
                                   __nv_bfloat16* __restrict__ y, int M, int N, float eps) {
+    pdl_trigger();
+    pdl_wait();
     int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
     int lane = threadIdx.x & 31;
     if (row >= M) return;
@@ -144,14 +162,23 @@ __device__ __forceinline__ void amax_merge2(float& v, int& i, float v2, int i2) 
     }
 }
 
-// Greedy token per row (lowest index on ties, NaN skipped) -> cur_ids[b] and
-// out_ids[b * max_gen + state[1]].
-__global__ void argmax_step_kernel(const float* __restrict__ logits, int V, int32_t* __restrict__ cur_ids,
-                                   int32_t* __restrict__ out_ids, int max_gen, const int* __restrict__ state) {
-    const float* xr = logits + (int64_t)blockIdx.x * V;
+// Greedy token per row, lowest index on ties, NaN skipped.  Grid (B, chunks):
+// each CTA reduces its chunk of the row to (value, index), folds it into a
+// per-row 64-bit key with atomicMax (key = order-preserving bits of the value
+// << 32 | ~index, so equal values prefer the lower index), and the last CTA
+// of the row writes cur_ids[b] and out_ids[b * max_gen + state[1]] and resets
+// the key and counter.
+__global__ void argmax_step_kernel(const float* __restrict__ logits, int V, int chunk, int32_t* __restrict__ cur_ids,
+                                   int32_t* __restrict__ out_ids, int max_gen, const int* __restrict__ state,
+                                   unsigned long long* __restrict__ keys, unsigned* __restrict__ cnt) {
+    pdl_trigger();
+    pdl_wait();
+    const int row = blockIdx.x;
+    const float* xr = logits + (int64_t)row * V;
+    const int c0 = blockIdx.y * chunk, c1 = min(V, c0 + chunk);
     float bv = -INFINITY;
     int bi = -1;
-    for (int c = threadIdx.x; c < V; c += blockDim.x) {
+    for (int c = c0 + threadIdx.x; c < c1; c += blockDim.x) {
         float v = xr[c];
         if (v != v) continue;
         amax_merge2(bv, bi, v, c);
@@ -164,6 +191,7 @@ __global__ void argmax_step_kernel(const float* __restrict__ logits, int V, int3
     }
     __shared__ float sv[32];
     __shared__ int si[32];
+    __shared__ int s_last;
     int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
     if (lane == 0) {
         sv[warp] = bv;
@@ -172,19 +200,36 @@ __global__ void argmax_step_kernel(const float* __restrict__ logits, int V, int3
     __syncthreads();
     if (threadIdx.x == 0) {
         for (int w = 1; w < (int)(blockDim.x / 32); w++) amax_merge2(bv, bi, sv[w], si[w]);
-        int id = bi < 0 ? 0 : bi;
-        cur_ids[blockIdx.x] = id;
+        if (bi >= 0) {
+            uint32_t u = __float_as_uint(bv);
+            uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+            atomicMax(&keys[row], ((unsigned long long)ord << 32) | (unsigned long long)(~(uint32_t)bi));
+        }
+        __threadfence();
+        s_last = atomicAdd(&cnt[row], 1u) == gridDim.y - 1;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && s_last) {
+        __threadfence();
+        unsigned long long k = atomicExch(&keys[row], 0ull);
+        int id = k ? (int)(~(uint32_t)(k & 0xffffffffull)) : 0;
+        cur_ids[row] = id;
         int step = state[1];
-        if (step < max_gen) out_ids[(int64_t)blockIdx.x * max_gen + step] = id;
+        if (step < max_gen) out_ids[(int64_t)row * max_gen + step] = id;
+        cnt[row] = 0u;
     }
 }
 
 __global__ void advance_kernel(int* state, int dpos, int dstep) {
+    pdl_trigger();
+    pdl_wait();
     state[0] += dpos;
     state[1] += dstep;
 }
 
 __global__ void set_state_kernel(int* state, int pos, int step) {
+    pdl_trigger();
+    pdl_wait();
     state[0] = pos;
     state[1] = step;
 }
@@ -225,6 +270,8 @@ struct tb_decoder {
     size_t ws_bytes = 0;
     unsigned* counters = nullptr;
     size_t n_counters = 0;
+    unsigned long long* amax_keys = nullptr;   // [max_batch], zero between launches
+    unsigned* amax_cnt = nullptr;              // [max_batch], zero between launches
     cudaStream_t cap_stream = nullptr;
     cudaGraphExec_t graph = nullptr;
     int graph_B = 0;
@@ -249,6 +296,14 @@ struct tb_decoder {
 
 namespace {
 
+// Enables programmatic dependent launch for the decoder's kernel chain.
+struct PdlScope {
+    tb_ctx* ctx;
+    bool saved;
+    explicit PdlScope(tb_ctx* c) : ctx(c), saved(c->pdl) { c->pdl = true; }
+    ~PdlScope() { ctx->pdl = saved; }
+};
+
 #define TB_TRY(x)          \
     do {                   \
         int rc_ = (x);     \
@@ -272,8 +327,8 @@ int lin(tb_decoder* d, const void* x, const void* w, const int8_t* wq, const flo
 
 int rms(tb_decoder* d, const bf16* x, int64_t ldx, const bf16* w, bf16* y, int M) {
     const int N = d->cfg.d_model;
-    rmsnorm_ld_kernel<<<(M + 7) / 8, 256, 0, d->ctx->stream>>>(x, ldx, w, y, M, N, d->cfg.norm_eps);
-    return check_launch(d->ctx, "rmsnorm");
+    return launch(d->ctx, "rmsnorm", rmsnorm_ld_kernel, dim3((M + 7) / 8), dim3(256), 0, x, ldx, w, y, M, N,
+                  d->cfg.norm_eps);
 }
 
 // One transformer layer over T = B * S_new tokens.  decode: S_new == 1 and
@@ -290,11 +345,10 @@ int layer_forward(tb_decoder* d, int l, int B, int S_new, bool decode) {
     TB_TRY(rms(d, d->x, dm, L.attn_norm, d->h, T));
     TB_TRY(lin(d, d->h, L.wqkv, L.qqkv, L.sqkv, d->qkv, T, d->qkv_n, dm, nullptr, false, false));
     {
-        int64_t warps = (int64_t)T * (c.n_heads + 2 * c.n_kv_heads);
-        rope_kv_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, ctx->stream>>>(
-            d->qkv, d->qkv_n, B, S_new, c.n_heads, c.n_kv_heads, hd, d->rope_tab, decode ? d->state : nullptr, 0,
-            kc, vc, c.max_seq, ctx->d_err);
-        TB_TRY(check_launch(ctx, "rope_kv"));
+        const int64_t work = (int64_t)T * (c.n_heads + 2 * c.n_kv_heads) * (hd / 16);
+        TB_TRY(launch(ctx, "rope_kv", rope_kv_kernel, dim3(grid_for(ctx, work)), dim3(256), 0, d->qkv, d->qkv_n, B,
+                      S_new, c.n_heads, c.n_kv_heads, hd, (const float2*)d->rope_tab,
+                      decode ? (const int*)d->state : (const int*)nullptr, 0, kc, vc, c.max_seq, ctx->d_err));
     }
     const float scale = 1.0f / sqrtf((float)hd);
     if (!decode) {
@@ -348,8 +402,10 @@ int head_forward(tb_decoder* d, int B, int64_t last_row_stride, int64_t last_row
     const tb_decoder_config& c = d->cfg;
     TB_TRY(rms(d, d->x + last_row_off, last_row_stride, d->final_norm, d->h, B));
     TB_TRY(lin(d, d->h, d->lm_head, d->qlm, d->slm, d->logits, B, c.vocab, c.d_model, nullptr, false, true));
-    argmax_step_kernel<<<B, 512, 0, d->ctx->stream>>>(d->logits, c.vocab, d->cur_ids, d->out_ids, c.max_seq, d->state);
-    return check_launch(d->ctx, "argmax_step");
+    const int chunk = 2048, nch = (c.vocab + chunk - 1) / chunk;
+    return launch(d->ctx, "argmax_step", argmax_step_kernel, dim3(B, nch), dim3(256), 0, (const float*)d->logits,
+                  c.vocab, chunk, d->cur_ids, d->out_ids, c.max_seq, (const int*)d->state, d->amax_keys,
+                  d->amax_cnt);
 }
 
 int decode_step_body(tb_decoder* d) {
@@ -357,8 +413,7 @@ int decode_step_body(tb_decoder* d) {
     TB_TRY(tb_embedding_fwd(d->ctx, TB_BF16, d->embed, d->cur_ids, d->x, B, d->cfg.d_model, d->cfg.vocab));
     for (int l = 0; l < d->cfg.n_layers; l++) TB_TRY(layer_forward(d, l, B, 1, true));
     TB_TRY(head_forward(d, B, d->cfg.d_model, 0));
-    advance_kernel<<<1, 1, 0, d->ctx->stream>>>(d->state, 1, 1);
-    return check_launch(d->ctx, "advance");
+    return launch(d->ctx, "advance", advance_kernel, dim3(1), dim3(1), 0, d->state, 1, 1);
 }
 
 int ensure_graph(tb_decoder* d) {
@@ -372,6 +427,7 @@ int ensure_graph(tb_decoder* d) {
     // order capture after everything already queued on the caller's stream
     TB_CUDA_TRY(ctx, cudaStreamSynchronize(saved));
     ctx->stream = d->cap_stream;
+    PdlScope pdl(ctx);
     cudaGraph_t g = nullptr;
     cudaError_t e = cudaStreamBeginCapture(d->cap_stream, cudaStreamCaptureModeThreadLocal);
     if (e != cudaSuccess) {
@@ -480,11 +536,15 @@ int tb_decoder_create(tb_ctx* ctx, const tb_decoder_config* cfg, tb_decoder** ou
     d->n_counters = ncnt;
     A(&d->ws, d->ws_bytes / sizeof(float) + 1);
     A(&d->counters, ncnt);
+    A(&d->amax_keys, (size_t)c.max_batch);
+    A(&d->amax_cnt, (size_t)c.max_batch);
     if (rc) {
         tb_decoder_destroy(d);
         return rc;
     }
     cudaMemset(d->counters, 0, ncnt * sizeof(unsigned));
+    cudaMemset(d->amax_keys, 0, (size_t)c.max_batch * sizeof(unsigned long long));
+    cudaMemset(d->amax_cnt, 0, (size_t)c.max_batch * sizeof(unsigned));
     cudaMemset(d->state, 0, 4 * sizeof(int));
     cudaMemset(d->kcache, 0, (size_t)d->cache_layer_elems * c.n_layers * sizeof(bf16));
     cudaMemset(d->vcache, 0, (size_t)d->cache_layer_elems * c.n_layers * sizeof(bf16));
@@ -612,12 +672,12 @@ int tb_decoder_prefill(tb_decoder* d, const int32_t* ids, int B, int S, float* l
     TB_REQUIRE(ctx, !c.weights_int8 || d->quantized, TB_ERR_ARG, "int8 decoder: call tb_decoder_prepare first");
     d->B = B;
     d->S0 = S;
-    set_state_kernel<<<1, 1, 0, ctx->stream>>>(d->state, 0, 0);
+    PdlScope pdl(ctx);
+    TB_TRY(launch(ctx, "set_state", set_state_kernel, dim3(1), dim3(1), 0, d->state, 0, 0));
     TB_TRY(tb_embedding_fwd(ctx, TB_BF16, d->embed, ids, d->x, (int64_t)B * S, c.d_model, c.vocab));
     for (int l = 0; l < c.n_layers; l++) TB_TRY(layer_forward(d, l, B, S, false));
     TB_TRY(head_forward(d, B, (int64_t)S * c.d_model, (int64_t)(S - 1) * c.d_model));
-    advance_kernel<<<1, 1, 0, ctx->stream>>>(d->state, S, 1);
-    TB_TRY(check_launch(ctx, "prefill"));
+    TB_TRY(launch(ctx, "advance", advance_kernel, dim3(1), dim3(1), 0, d->state, S, 1));
     d->host_len = S;
     d->host_step = 1;
     if (logits)

@@ -269,6 +269,8 @@ __global__ void dequantize_int8_kernel(const int8_t* __restrict__ q, const float
 template <typename T>
 __global__ void embedding_kernel(const T* __restrict__ table, const int32_t* __restrict__ ids,
                                  T* __restrict__ y, int64_t T_, int64_t D, int64_t vocab, int* err) {
+    pdl_trigger();
+    pdl_wait();
     int64_t t = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
     int lane = threadIdx.x & 31;
     if (t >= T_) return;
@@ -473,10 +475,10 @@ int tb_embedding_fwd(tb_ctx* ctx, int dtype, const void* table, const int32_t* i
     if (T == 0) return TB_OK;
     int blocks = (int)((T + 7) / 8);
     if (dtype == TB_F32)
-        embedding_kernel<float><<<blocks, 256, 0, ctx->stream>>>((const float*)table, ids, (float*)y, T, D, vocab, ctx->d_err);
-    else
-        embedding_kernel<__nv_bfloat16><<<blocks, 256, 0, ctx->stream>>>((const __nv_bfloat16*)table, ids, (__nv_bfloat16*)y, T, D, vocab, ctx->d_err);
-    return check_launch(ctx, "embedding");
+        return launch(ctx, "embedding", embedding_kernel<float>, dim3(blocks), dim3(256), 0, (const float*)table, ids,
+                      (float*)y, T, D, vocab, ctx->d_err);
+    return launch(ctx, "embedding", embedding_kernel<__nv_bfloat16>, dim3(blocks), dim3(256), 0,
+                  (const __nv_bfloat16*)table, ids, (__nv_bfloat16*)y, T, D, vocab, ctx->d_err);
 }
 
 int tb_argmax_fwd(tb_ctx* ctx, int dtype, const void* x, int32_t* out, int64_t M, int64_t N) {

@@ -82,6 +82,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     uint32_t accb = smem_u32(bars + 2 * STAGES);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 1);
 
+    pdl_trigger();
+    pdl_wait();
     const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
     const int m0 = blockIdx.y * GEMM_BM, n0 = blockIdx.x * BN;
     const int nk = (K + GEMM_BK - 1) / GEMM_BK;
@@ -259,6 +261,7 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
     const uint32_t accb = smem_u32(bars + 2 * STAGES + 4);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
 
+    pdl_trigger();
     const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
     const int tile = blockIdx.x, split = blockIdx.y, CS = gridDim.y;
     const int nk_total = (K + 63) / 64;
@@ -288,10 +291,20 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
     if (warp == 0 && lane == 0) {
         tma_prefetch_desc(&tmW);
         tma_prefetch_desc(&tmX);
-        int issued = 0;
-        for (int i = 0; i < nk; i++) {
+        // Weights do not depend on the previous kernel: start streaming the
+        // first STAGES K-blocks before waiting for it, then fetch activations.
+        const int pre = nk < STAGES ? nk : STAGES;
+        for (int i = 0; i < pre; i++) {
+            mbar_expect_tx(full0 + 8 * i, C::W_BYTES + C::X_BYTES);
+            tma_load_2d(smem_u32(sW + i * C::W_BYTES), &tmW, full0 + 8 * i, (kb0 + i) * 64, tile * 256);
+        }
+        pdl_wait();
+        for (int i = 0; i < pre; i++)
+            tma_load_2d(smem_u32(sX + i * C::X_BYTES), &tmX, full0 + 8 * i, (kb0 + i) * 64, 0);
+        int issued = pre;
+        for (int i = pre; i < nk; i++) {
             int s = i % STAGES;
-            if (i >= STAGES && !mbar_wait(empty0 + 8 * s, ((i / STAGES) - 1) & 1, err, DEV_ERR_TIMEOUT_EMPTY)) break;
+            if (!mbar_wait(empty0 + 8 * s, ((i / STAGES) - 1) & 1, err, DEV_ERR_TIMEOUT_EMPTY)) break;
             mbar_expect_tx(full0 + 8 * s, C::W_BYTES + C::X_BYTES);
             int kcoord = (kb0 + i) * 64;
             tma_load_2d(smem_u32(sW + s * C::W_BYTES), &tmW, full0 + 8 * s, kcoord, tile * 256);
@@ -366,6 +379,7 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
     __syncwarp();
 
     // ---------------- accumulator -> registers
+    pdl_wait();   // (already satisfied: the activations arrived) before any global write
     bool ok = mbar_wait(accb, 0, err, DEV_ERR_TIMEOUT_ACC);
     ok = __all_sync(0xffffffffu, ok);
     __syncwarp();
@@ -541,8 +555,7 @@ static int launch_gemm_tc(tb_ctx* ctx, const void* a, const void* b, const Epi& 
     auto kern = gemm_tc_kernel<BN, STAGES, B_MN>;
     TB_CUDA_TRY(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     dim3 grid((N + BN - 1) / BN, (M + GEMM_BM - 1) / GEMM_BM);
-    kern<<<grid, 256, smem, ctx->stream>>>(ta, tbm, ep, M, N, K, ctx->d_err);
-    return check_launch(ctx, "gemm_tc");
+    return launch(ctx, "gemm_tc", kern, grid, dim3(256), smem, ta, tbm, ep, M, N, K, ctx->d_err);
 }
 
 // Cluster size (K splits per weight tile): the largest of 8, 4, 2, 1 that
@@ -589,13 +602,18 @@ static int launch_gemv_tc(tb_ctx* ctx, const void* x, const void* w, const Epi& 
     lc.blockDim = dim3(256, 1, 1);
     lc.dynamicSmemBytes = C::SMEM;
     lc.stream = ctx->stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 1;
     attr[0].val.clusterDim.y = cs;
     attr[0].val.clusterDim.z = 1;
     lc.attrs = attr;
     lc.numAttrs = 1;
+    if (ctx->pdl) {
+        attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[1].val.programmaticStreamSerializationAllowed = 1;
+        lc.numAttrs = 2;
+    }
     TB_CUDA_TRY(ctx, cudaLaunchKernelEx(&lc, kern, tw, tx, ep, Nw, K, Mtok, kb_per, ctx->d_err));
     return check_launch(ctx, "gemv_tc");
 }

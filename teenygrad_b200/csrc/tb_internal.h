@@ -7,6 +7,7 @@
 
 #include <mutex>
 #include <string>
+#include <utility>
 
 #include "../../include/teeny_b200.h"
 
@@ -21,6 +22,7 @@ struct tb_ctx {
     size_t n_counters = 0;
     std::string last_error;
     void* comm = nullptr;           // NCCL communicator state (comm.cu)
+    bool pdl = false;               // launch with programmatic stream serialization
 };
 
 namespace tb {
@@ -47,6 +49,29 @@ int make_tmap_2d(tb_ctx* ctx, CUtensorMap* out, CUtensorMapDataType dt, int elem
                  uint32_t box_cols, uint32_t box_rows);
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// cudaLaunchKernelEx on ctx->stream; adds the programmatic-serialization
+// attribute when ctx->pdl is set (the kernel must call pdl_wait()).
+template <typename... KArgs, typename... Args>
+int launch(tb_ctx* ctx, const char* what, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+           Args&&... args) {
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = grid;
+    lc.blockDim = block;
+    lc.dynamicSmemBytes = smem;
+    lc.stream = ctx->stream;
+    cudaLaunchAttribute attr[1];
+    lc.attrs = attr;
+    lc.numAttrs = 0;
+    if (ctx->pdl) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        lc.numAttrs = 1;
+    }
+    cudaError_t e = cudaLaunchKernelEx(&lc, kern, std::forward<Args>(args)...);
+    if (e != cudaSuccess) return set_error(ctx, TB_ERR_CUDA, "%s launch: %s", what, cudaGetErrorString(e));
+    return TB_OK;
+}
 
 }  // namespace tb
 
