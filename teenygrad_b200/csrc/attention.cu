@@ -274,16 +274,32 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
 }
 
 // -------------------------------------------------------------- decode -----
-// Grid (B * Hkv, splits), 128 threads.  A CTA owns keys [split * chunk, ...)
-// of one (batch, kv head) group and all G = Hq / Hkv query heads reading it,
-// walking them 128 keys at a time: thread t scores key t against the G
-// queries (K row in registers, queries broadcast from shared memory), the
-// block forms the chunk's max / exp / sum per head, then thread (head, dim
-// pair) accumulates P V with V staged in shared memory by cp.async.  Each CTA
-// leaves (max, sum, unnormalised o) per head in ws; the last CTA of the group
-// merges the splits in split order (deterministic).  D = 64 or 128, G <= 8.
+// Grid (B * Hkv, 8) launched as clusters of (1, 8, 1): the 8 CTAs of a
+// cluster split the context of one (batch, kv head) group; each covers
+// `chunk` keys (a multiple of 32) in rounds of 128, for all G = Hq / Hkv query
+// heads that read the group.  Per round: thread t scores key t (its K row in
+// registers, the queries broadcast from shared memory), the block forms the
+// round's max / exp / sum per head, then thread (head, dim) accumulates P V
+// with V staged in shared memory by cp.async.  Each CTA leaves its
+// (max, sum, unnormalised o) per head in its own shared memory; after a
+// cluster barrier CTA rank r merges output dims [r*D/8, (r+1)*D/8) of every
+// head over DSMEM, in rank order (deterministic).  D = 64 or 128, G <= 8.
+constexpr int DEC_SPLITS = 8;
+
+__device__ __forceinline__ void dec_cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ float dec_ld_dsmem(uint32_t local_addr, uint32_t rank) {
+    uint32_t remote;
+    float v;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_addr), "r"(rank));
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote));
+    return v;
+}
+
 template <int D>
-__global__ void __launch_bounds__(128)
+__global__ void __launch_bounds__(128, D == 64 ? 8 : 4)
 attn_decode_kernel(DecodeArgs a, int* err) {
     constexpr int KC = 128;
     __shared__ __align__(16) __nv_bfloat16 sv[KC * D];
@@ -291,21 +307,32 @@ attn_decode_kernel(DecodeArgs a, int* err) {
     __shared__ float sp[8][KC];
     __shared__ float s_wred[8][4];
     __shared__ float s_m[8], s_l[8], s_alpha[8];
-    __shared__ int s_last;
+    __shared__ float s_o[8][D];          // this CTA's unnormalised output, read by peers
 
     pdl_trigger();
     pdl_wait();
     const int G = a.Hq / a.Hkv;
-    const int bg = blockIdx.x, split = blockIdx.y, nsp = gridDim.y;
+    const int bg = blockIdx.x, split = blockIdx.y;
     const int b = bg / a.Hkv, g = bg % a.Hkv;
     const int L = a.len_ptr ? (*a.len_ptr + a.len) : a.len;
     const int kbeg = split * a.chunk;
     const int kend = min(L, kbeg + a.chunk);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const __nv_bfloat16* kbase = a.k + (int64_t)b * a.kv_sb + (int64_t)g * a.kv_sh;
+    const __nv_bfloat16* vbase = a.v + (int64_t)b * a.kv_sb + (int64_t)g * a.kv_sh;
 
-    for (int i = tid; i < G * D; i += 128) {
-        int gg = i / D, d = i % D;
-        sq[gg][d] = __bfloat162float(a.q[(int64_t)b * a.q_sb + (int64_t)(g * G + gg) * a.q_sh + d]) * a.scale_log2;
+    // queries: issue every load before the first use
+    constexpr int QPT = (8 * D + 127) / 128;
+    float qv[QPT];
+#pragma unroll
+    for (int j = 0; j < QPT; j++) {
+        const int i = tid + 128 * j, gg = i / D, d = i % D;
+        qv[j] = (gg < G) ? __bfloat162float(a.q[(int64_t)b * a.q_sb + (int64_t)(g * G + gg) * a.q_sh + d]) : 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < QPT; j++) {
+        const int i = tid + 128 * j, gg = i / D, d = i % D;
+        if (gg < 8) sq[gg][d] = qv[j] * a.scale_log2;
     }
     if (tid < 8) {
         s_m[tid] = -INFINITY;
@@ -315,41 +342,37 @@ attn_decode_kernel(DecodeArgs a, int* err) {
     float acc[OPT];
 #pragma unroll
     for (int i = 0; i < OPT; i++) acc[i] = 0.f;
-    __syncthreads();
 
-    const __nv_bfloat16* kbase = a.k + (int64_t)b * a.kv_sb + (int64_t)g * a.kv_sh;
-    const __nv_bfloat16* vbase = a.v + (int64_t)b * a.kv_sb + (int64_t)g * a.kv_sh;
     for (int k0 = kbeg; k0 < kend; k0 += KC) {
         const int nk = min(KC, kend - k0);
-        // V chunk -> smem (async), rows >= nk zero
+        // V round -> smem (async); K row of this thread -> registers
         constexpr int CPR = D / 8;
         for (int i = tid; i < KC * CPR; i += 128) {
-            int r = i / CPR, c = i % CPR;
-            uint32_t dst = smem_u32(&sv[r * D + c * 8]);
+            const int r = i / CPR, c = i % CPR;
             if (r < nk) {
+                const uint32_t dst = smem_u32(&sv[r * D + c * 8]);
                 const void* src = vbase + (int64_t)(k0 + r) * a.kv_ss + c * 8;
                 asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
-            } else {
-                *reinterpret_cast<uint4*>(&sv[r * D + c * 8]) = make_uint4(0, 0, 0, 0);
             }
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
-        // scores: thread tid <-> key k0 + tid
-        float s[8];
-#pragma unroll
-        for (int gg = 0; gg < 8; gg++) s[gg] = -INFINITY;
+        uint4 kreg[D / 8];
         if (tid < nk) {
             const uint4* kr = reinterpret_cast<const uint4*>(kbase + (int64_t)(k0 + tid) * a.kv_ss);
 #pragma unroll
-            for (int gg = 0; gg < 8; gg++)
-                if (gg < G) s[gg] = 0.f;
+            for (int c = 0; c < D / 8; c++) kreg[c] = __ldg(kr + c);
+        }
+        __syncthreads();   // sq ready (first round); previous round's sv / sp reads done
+        float s[8];
+#pragma unroll
+        for (int gg = 0; gg < 8; gg++) s[gg] = (gg < G && tid < nk) ? 0.f : -INFINITY;
+        if (tid < nk) {
 #pragma unroll
             for (int c = 0; c < D / 8; c++) {
-                uint4 kv = __ldg(kr + c);
-                uint32_t w[4] = {kv.x, kv.y, kv.z, kv.w};
+                const uint32_t w[4] = {kreg[c].x, kreg[c].y, kreg[c].z, kreg[c].w};
 #pragma unroll
                 for (int j = 0; j < 4; j++) {
-                    float k0f = bf16_lo(w[j]), k1f = bf16_hi(w[j]);
+                    const float k0f = bf16_lo(w[j]), k1f = bf16_hi(w[j]);
 #pragma unroll
                     for (int gg = 0; gg < 8; gg++) {
                         if (gg < G) {
@@ -360,7 +383,6 @@ attn_decode_kernel(DecodeArgs a, int* err) {
                 }
             }
         }
-        // chunk max per head
 #pragma unroll
         for (int gg = 0; gg < 8; gg++) {
             if (gg < G) {
@@ -372,8 +394,8 @@ attn_decode_kernel(DecodeArgs a, int* err) {
         }
         __syncthreads();
         if (tid < G) {
-            float m = fmaxf(fmaxf(s_wred[tid][0], s_wred[tid][1]), fmaxf(s_wred[tid][2], s_wred[tid][3]));
-            float m_old = s_m[tid], m_new = fmaxf(m_old, m);
+            const float m = fmaxf(fmaxf(s_wred[tid][0], s_wred[tid][1]), fmaxf(s_wred[tid][2], s_wred[tid][3]));
+            const float m_old = s_m[tid], m_new = fmaxf(m_old, m);
             s_alpha[tid] = ex2(m_old - m_new);
             s_m[tid] = m_new;
         }
@@ -381,7 +403,7 @@ attn_decode_kernel(DecodeArgs a, int* err) {
 #pragma unroll
         for (int gg = 0; gg < 8; gg++) {
             if (gg < G) {
-                float p = (tid < nk) ? ex2(s[gg] - s_m[gg]) : 0.f;
+                const float p = (tid < nk) ? ex2(s[gg] - s_m[gg]) : 0.f;
                 sp[gg][tid] = p;
                 float sum = p;
 #pragma unroll
@@ -392,67 +414,57 @@ attn_decode_kernel(DecodeArgs a, int* err) {
         asm volatile("cp.async.wait_all;" ::: "memory");
         __syncthreads();
         if (tid < G) s_l[tid] = s_l[tid] * s_alpha[tid] + (s_wred[tid][0] + s_wred[tid][1] + s_wred[tid][2] + s_wred[tid][3]);
-        // P V: idx = tid + 128 * i -> (head gg, dim d)
 #pragma unroll
         for (int i = 0; i < OPT; i++) {
             const int idx = tid + 128 * i, gg = idx / D, d = idx % D;
             if (gg < G) {
-                float o = acc[i] * s_alpha[gg];
-                for (int r = 0; r < nk; r++) o = fmaf(sp[gg][r], __bfloat162float(sv[r * D + d]), o);
-                acc[i] = o;
+                float o0 = acc[i] * s_alpha[gg], o1 = 0.f;
+                int r = 0;
+                for (; r + 1 < nk; r += 2) {
+                    o0 = fmaf(sp[gg][r], __bfloat162float(sv[r * D + d]), o0);
+                    o1 = fmaf(sp[gg][r + 1], __bfloat162float(sv[(r + 1) * D + d]), o1);
+                }
+                if (r < nk) o0 = fmaf(sp[gg][r], __bfloat162float(sv[r * D + d]), o0);
+                acc[i] = o0 + o1;
             }
         }
-        __syncthreads();
     }
 
-    // partial -> ws[(bg * nsp + split)][8][D + 2]
-    const int stride = D + 2;
-    float* wp = a.ws + ((int64_t)bg * nsp + split) * 8 * stride;
+    // partial stays in shared memory; merge across the cluster over DSMEM
 #pragma unroll
     for (int i = 0; i < OPT; i++) {
         const int idx = tid + 128 * i, gg = idx / D, d = idx % D;
-        if (gg < G) wp[gg * stride + d] = acc[i];
+        if (gg < 8) s_o[gg][d] = acc[i];
     }
-    if (tid < G) {
-        wp[tid * stride + D] = s_m[tid];
-        wp[tid * stride + D + 1] = s_l[tid];
-    }
-    __threadfence();
     __syncthreads();
-    if (tid == 0) s_last = (atomicAdd(&a.counters[bg], 1u) == (unsigned)(nsp - 1));
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-    constexpr int MAXSP = 16;
-    for (int idx = tid; idx < G * D; idx += 128) {
-        const int gg = idx / D, d = idx % D;
-        float mv[MAXSP], lv[MAXSP], ov[MAXSP];
+    dec_cluster_sync();
+    {
+        constexpr int DS = D / DEC_SPLITS;            // dims merged by this CTA per head
+        const int gg = tid / DS, d = split * DS + tid % DS;
+        if (tid < G * DS) {
+            const uint32_t am = smem_u32(&s_m[gg]), al = smem_u32(&s_l[gg]), ao = smem_u32(&s_o[gg][d]);
+            float mv[DEC_SPLITS], lv[DEC_SPLITS], ov[DEC_SPLITS];
 #pragma unroll
-        for (int sp_i = 0; sp_i < MAXSP; sp_i++) {
-            if (sp_i < nsp) {
-                const float* p = a.ws + ((int64_t)bg * nsp + sp_i) * 8 * stride + gg * stride;
-                mv[sp_i] = __ldcg(p + D);
-                lv[sp_i] = __ldcg(p + D + 1);
-                ov[sp_i] = __ldcg(p + d);
+            for (int r = 0; r < DEC_SPLITS; r++) {
+                mv[r] = dec_ld_dsmem(am, r);
+                lv[r] = dec_ld_dsmem(al, r);
+                ov[r] = dec_ld_dsmem(ao, r);
             }
-        }
-        float M = -INFINITY;
+            float M = -INFINITY;
 #pragma unroll
-        for (int sp_i = 0; sp_i < MAXSP; sp_i++)
-            if (sp_i < nsp) M = fmaxf(M, mv[sp_i]);
-        float l = 0.f, o = 0.f;
+            for (int r = 0; r < DEC_SPLITS; r++) M = fmaxf(M, mv[r]);
+            float l = 0.f, o = 0.f;
 #pragma unroll
-        for (int sp_i = 0; sp_i < MAXSP; sp_i++) {
-            if (sp_i < nsp) {
-                float w = (mv[sp_i] == -INFINITY) ? 0.f : ex2(mv[sp_i] - M);
-                l += lv[sp_i] * w;
-                o += ov[sp_i] * w;
+            for (int r = 0; r < DEC_SPLITS; r++) {
+                const float w = (mv[r] == -INFINITY) ? 0.f : ex2(mv[r] - M);
+                l += lv[r] * w;
+                o += ov[r] * w;
             }
+            a.o[(int64_t)b * a.o_sb + (int64_t)(g * G + gg) * a.o_sh + d] = __float2bfloat16_rn(l > 0.f ? o / l : 0.f);
+            if (d == 0 && a.lse) a.lse[(int64_t)b * a.Hq + g * G + gg] = l > 0.f ? (M + log2f(l)) * kLn2 : -INFINITY;
         }
-        a.o[(int64_t)b * a.o_sb + (int64_t)(g * G + gg) * a.o_sh + d] = __float2bfloat16_rn(l > 0.f ? o / l : 0.f);
-        if (d == 0 && a.lse) a.lse[(int64_t)b * a.Hq + g * G + gg] = l > 0.f ? (M + log2f(l)) * kLn2 : -INFINITY;
     }
-    if (tid == 0) a.counters[bg] = 0u;
+    dec_cluster_sync();   // peers may still be reading this CTA's partial
 }
 
 // ---------------------------------------------------------------- f32 ------
@@ -534,30 +546,49 @@ int attn_tc_launch(tb_ctx* ctx, const AttnTensors& t, int B, int Hq, int Hkv, in
     return check_launch(ctx, "attn_tc");
 }
 
-// Context chunk per CTA: a multiple of 128 keys, at most 16 splits.
+// Keys per CTA: the context split 8 ways, rounded up to a multiple of 32.
 static int decode_chunk(int max_len) {
-    int sub = (max_len + 127) / 128;          // 128-key sub-chunks
-    int per = (sub + 15) / 16;                // sub-chunks per split
-    return 128 * (per < 1 ? 1 : per);
+    int c = (max_len + DEC_SPLITS - 1) / DEC_SPLITS;
+    c = (c + 31) / 32 * 32;
+    return c < 32 ? 32 : c;
 }
 
 int attn_decode_launch(tb_ctx* ctx, DecodeArgs a, int B, int D, int max_len, float* ws, unsigned* counters) {
-    const int groups = B * a.Hkv;
+    (void)ws;
+    (void)counters;
     a.chunk = decode_chunk(max_len);
-    int splits = (max_len + a.chunk - 1) / a.chunk;
-    if (splits < 1) splits = 1;
-    a.ws = ws;
-    a.counters = counters;
-    dim3 grid(groups, splits);
-    if (D == 64) return launch(ctx, "attn_decode", attn_decode_kernel<64>, grid, dim3(128), 0, a, ctx->d_err);
-    return launch(ctx, "attn_decode", attn_decode_kernel<128>, grid, dim3(128), 0, a, ctx->d_err);
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3(B * a.Hkv, DEC_SPLITS, 1);
+    lc.blockDim = dim3(128, 1, 1);
+    lc.dynamicSmemBytes = 0;
+    lc.stream = ctx->stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = DEC_SPLITS;
+    attr[0].val.clusterDim.z = 1;
+    lc.attrs = attr;
+    lc.numAttrs = 1;
+    if (ctx->pdl) {
+        attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[1].val.programmaticStreamSerializationAllowed = 1;
+        lc.numAttrs = 2;
+    }
+    cudaError_t e;
+    if (D == 64) {
+        cudaFuncSetAttribute(attn_decode_kernel<64>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+        e = cudaLaunchKernelEx(&lc, attn_decode_kernel<64>, a, ctx->d_err);
+    } else {
+        cudaFuncSetAttribute(attn_decode_kernel<128>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+        e = cudaLaunchKernelEx(&lc, attn_decode_kernel<128>, a, ctx->d_err);
+    }
+    if (e != cudaSuccess) return set_error(ctx, TB_ERR_CUDA, "attn_decode launch: %s", cudaGetErrorString(e));
+    return TB_OK;
 }
 
 size_t attn_decode_ws_bytes(int B, int Hkv, int D, int max_len) {
-    const int chunk = decode_chunk(max_len);
-    int splits = (max_len + chunk - 1) / chunk;
-    if (splits < 1) splits = 1;
-    return (size_t)B * Hkv * splits * 8 * (D + 2) * sizeof(float);
+    (void)B; (void)Hkv; (void)D; (void)max_len;
+    return 0;   // partials stay in shared memory (cluster merge)
 }
 
 }  // namespace tb

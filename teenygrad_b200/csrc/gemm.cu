@@ -559,12 +559,12 @@ static int launch_gemm_tc(tb_ctx* ctx, const void* a, const void* b, const Epi& 
 }
 
 // Cluster size (K splits per weight tile): the largest of 8, 4, 2, 1 that
-// keeps the grid within about one CTA per SM and every split >= 2 K-blocks.
+// keeps the grid within two CTAs per SM and every split >= 2 K-blocks.
 static void gemv_split(int num_sms, int Nw, int K, int* splits_out, int* kb_per_out) {
     const int tiles = (Nw + 255) / 256;
     const int nk = (K + 63) / 64;
     int cs = 8;
-    while (cs > 1 && (tiles * cs > num_sms + num_sms / 4 || nk < 2 * cs)) cs >>= 1;
+    while (cs > 1 && (tiles * cs > 2 * num_sms || nk < 2 * cs)) cs >>= 1;
     int kb_per = (nk + cs - 1) / cs;
     *splits_out = cs;
     *kb_per_out = kb_per;
@@ -620,9 +620,10 @@ static int launch_gemv_tc(tb_ctx* ctx, const void* x, const void* w, const Epi& 
 
 template <bool INT8>
 static int dispatch_gemv(tb_ctx* ctx, const void* x, const void* w, const Epi& ep, int M, int N, int K) {
-    // One CTA per SM, rings of ~200 KB keep enough weight bytes in flight.
-    if (M <= 16) return launch_gemv_tc<16, 6, INT8>(ctx, x, w, ep, M, N, K);
-    if (M <= 32) return launch_gemv_tc<32, 6, INT8>(ctx, x, w, ep, M, N, K);
+    // <= 32 tokens: 3-stage rings (~105 KB) let two CTAs share an SM, so the
+    // next layer's GEMV can start streaming weights (PDL) beside this one.
+    if (M <= 16) return launch_gemv_tc<16, INT8 ? 6 : 3, INT8>(ctx, x, w, ep, M, N, K);
+    if (M <= 32) return launch_gemv_tc<32, INT8 ? 6 : 3, INT8>(ctx, x, w, ep, M, N, K);
     return launch_gemv_tc<64, INT8 ? 6 : 5, INT8>(ctx, x, w, ep, M, N, K);
 }
 
