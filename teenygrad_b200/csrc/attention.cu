@@ -274,17 +274,21 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
 }
 
 // -------------------------------------------------------------- decode -----
-// Grid (B * Hkv, 8) launched as clusters of (1, 8, 1): the 8 CTAs of a
-// cluster split the context of one (batch, kv head) group; each covers
-// `chunk` keys (a multiple of 32) in rounds of 128, for all G = Hq / Hkv query
-// heads that read the group.  Per round: thread t scores key t (its K row in
-// registers, the queries broadcast from shared memory), the block forms the
-// round's max / exp / sum per head, then thread (head, dim) accumulates P V
-// with V staged in shared memory by cp.async.  Each CTA leaves its
-// (max, sum, unnormalised o) per head in its own shared memory; after a
-// cluster barrier CTA rank r merges output dims [r*D/8, (r+1)*D/8) of every
-// head over DSMEM, in rank order (deterministic).  D = 64 or 128, G <= 8.
-constexpr int DEC_SPLITS = 8;
+// Decode attention against the KV cache: a few queries, a long context.
+// Grid (B * Hkv, 4) in clusters of (1, 4, 1); each CTA has 4 warps, so the 16
+// warps of a cluster split the context of one (batch, kv head) group into
+// `chunk`-key ranges (chunk a multiple of 32).  A warp walks its range 32
+// keys at a time with its own online softmax: lane j holds key j's K row and
+// its two (D=64) or four (D=128) output dims of the 32 V rows in registers,
+// all loaded up front with coalesced loads; scores use the G = Hq / Hkv
+// queries broadcast from shared memory, the slab's probabilities go through
+// a per-warp shared buffer for the P V product.  Partials (max, sum, o) stay
+// in shared memory; after a cluster barrier CTA rank r merges output dims
+// [r*D/4, (r+1)*D/4) of every head over DSMEM in fixed order (deterministic).
+// D = 64 or 128, G <= 8.
+constexpr int DEC_CTAS = 4;                 // cluster size
+constexpr int DEC_WARPS = 4;                // warps per CTA
+constexpr int DEC_SPLITS = DEC_CTAS * DEC_WARPS;
 
 __device__ __forceinline__ void dec_cluster_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
@@ -298,173 +302,182 @@ __device__ __forceinline__ float dec_ld_dsmem(uint32_t local_addr, uint32_t rank
     return v;
 }
 
-template <int D>
-__global__ void __launch_bounds__(128, D == 64 ? 8 : 4)
+template <int D, int G>
+__global__ void __launch_bounds__(128, D == 64 ? 4 : 2)
 attn_decode_kernel(DecodeArgs a, int* err) {
-    constexpr int KC = 128;
-    __shared__ __align__(16) __nv_bfloat16 sv[KC * D];
-    __shared__ float sq[8][D];
-    __shared__ float sp[8][KC];
-    __shared__ float s_wred[8][4];
-    __shared__ float s_m[8], s_l[8], s_alpha[8];
-    __shared__ float s_o[8][D];          // this CTA's unnormalised output, read by peers
+    constexpr int DPL = D / 32;                       // output dims per lane
+    __shared__ __align__(16) float sq[8][D];          // queries (exp2-scaled)
+    __shared__ __align__(16) float sp[DEC_WARPS][32][8];   // slab probabilities [key][head]
+    __shared__ float s_m[DEC_WARPS][8], s_l[DEC_WARPS][8];
+    __shared__ float s_o[DEC_WARPS][8][D];
 
     pdl_trigger();
     pdl_wait();
-    const int G = a.Hq / a.Hkv;
-    const int bg = blockIdx.x, split = blockIdx.y;
+    const int bg = blockIdx.x, cr = blockIdx.y;
     const int b = bg / a.Hkv, g = bg % a.Hkv;
     const int L = a.len_ptr ? (*a.len_ptr + a.len) : a.len;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int split = cr * DEC_WARPS + warp;
     const int kbeg = split * a.chunk;
     const int kend = min(L, kbeg + a.chunk);
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const __nv_bfloat16* kbase = a.k + (int64_t)b * a.kv_sb + (int64_t)g * a.kv_sh;
     const __nv_bfloat16* vbase = a.v + (int64_t)b * a.kv_sb + (int64_t)g * a.kv_sh;
 
-    // queries: issue every load before the first use
-    constexpr int QPT = (8 * D + 127) / 128;
-    float qv[QPT];
-#pragma unroll
-    for (int j = 0; j < QPT; j++) {
-        const int i = tid + 128 * j, gg = i / D, d = i % D;
-        qv[j] = (gg < G) ? __bfloat162float(a.q[(int64_t)b * a.q_sb + (int64_t)(g * G + gg) * a.q_sh + d]) : 0.f;
+    for (int i = tid; i < 8 * D; i += 128) {
+        const int gg = i / D, d = i % D;
+        sq[gg][d] = (gg < G) ? __bfloat162float(a.q[(int64_t)b * a.q_sb + (int64_t)(g * G + gg) * a.q_sh + d]) * a.scale_log2
+                             : 0.f;
     }
-#pragma unroll
-    for (int j = 0; j < QPT; j++) {
-        const int i = tid + 128 * j, gg = i / D, d = i % D;
-        if (gg < 8) sq[gg][d] = qv[j] * a.scale_log2;
-    }
-    if (tid < 8) {
-        s_m[tid] = -INFINITY;
-        s_l[tid] = 0.f;
-    }
-    constexpr int OPT = (8 * D) / 128;   // output elements per thread (covers G <= 8)
-    float acc[OPT];
-#pragma unroll
-    for (int i = 0; i < OPT; i++) acc[i] = 0.f;
+    __syncthreads();
 
-    for (int k0 = kbeg; k0 < kend; k0 += KC) {
-        const int nk = min(KC, kend - k0);
-        // V round -> smem (async); K row of this thread -> registers
-        constexpr int CPR = D / 8;
-        for (int i = tid; i < KC * CPR; i += 128) {
-            const int r = i / CPR, c = i % CPR;
-            if (r < nk) {
-                const uint32_t dst = smem_u32(&sv[r * D + c * 8]);
-                const void* src = vbase + (int64_t)(k0 + r) * a.kv_ss + c * 8;
-                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+    float m_run[G], l_run[G], o[G][DPL];
+#pragma unroll
+    for (int gg = 0; gg < G; gg++) {
+        m_run[gg] = -INFINITY;
+        l_run[gg] = 0.f;
+#pragma unroll
+        for (int j = 0; j < DPL; j++) o[gg][j] = 0.f;
+    }
+    for (int k0 = kbeg; k0 < kend; k0 += 32) {
+        const int nk = min(32, kend - k0);
+        // ---- loads: this lane's K row, and dims [lane*DPL, +DPL) of the 32 V rows
+        uint4 kr[D / 8];
+        const bool mine = lane < nk;
+        if (mine) {
+            const uint4* kp = reinterpret_cast<const uint4*>(kbase + (int64_t)(k0 + lane) * a.kv_ss);
+#pragma unroll
+            for (int c = 0; c < D / 8; c++) kr[c] = __ldg(kp + c);
+        }
+        uint32_t vr[32][DPL / 2];
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+            if (j < nk) {
+                const __nv_bfloat16* vp = vbase + (int64_t)(k0 + j) * a.kv_ss + lane * DPL;
+                if (DPL == 2) vr[j][0] = __ldg(reinterpret_cast<const unsigned int*>(vp));
+                else {
+                    uint2 t = __ldg(reinterpret_cast<const uint2*>(vp));
+                    vr[j][0] = t.x;
+                    vr[j][DPL / 2 - 1] = t.y;
+                }
+            } else {
+#pragma unroll
+                for (int q = 0; q < DPL / 2; q++) vr[j][q] = 0u;
             }
         }
-        asm volatile("cp.async.commit_group;" ::: "memory");
-        uint4 kreg[D / 8];
-        if (tid < nk) {
-            const uint4* kr = reinterpret_cast<const uint4*>(kbase + (int64_t)(k0 + tid) * a.kv_ss);
+        // ---- scores of this lane's key
+        float s[G];
 #pragma unroll
-            for (int c = 0; c < D / 8; c++) kreg[c] = __ldg(kr + c);
-        }
-        __syncthreads();   // sq ready (first round); previous round's sv / sp reads done
-        float s[8];
-#pragma unroll
-        for (int gg = 0; gg < 8; gg++) s[gg] = (gg < G && tid < nk) ? 0.f : -INFINITY;
-        if (tid < nk) {
+        for (int gg = 0; gg < G; gg++) s[gg] = 0.f;
+        if (mine) {
 #pragma unroll
             for (int c = 0; c < D / 8; c++) {
-                const uint32_t w[4] = {kreg[c].x, kreg[c].y, kreg[c].z, kreg[c].w};
+                const uint32_t w[4] = {kr[c].x, kr[c].y, kr[c].z, kr[c].w};
+                float kf[8];
 #pragma unroll
                 for (int j = 0; j < 4; j++) {
-                    const float k0f = bf16_lo(w[j]), k1f = bf16_hi(w[j]);
+                    kf[2 * j] = bf16_lo(w[j]);
+                    kf[2 * j + 1] = bf16_hi(w[j]);
+                }
 #pragma unroll
-                    for (int gg = 0; gg < 8; gg++) {
-                        if (gg < G) {
-                            s[gg] = fmaf(sq[gg][c * 8 + 2 * j], k0f, s[gg]);
-                            s[gg] = fmaf(sq[gg][c * 8 + 2 * j + 1], k1f, s[gg]);
-                        }
+                for (int gg = 0; gg < G; gg++) {
+                    {
+                        const float4 q0 = *reinterpret_cast<const float4*>(&sq[gg][c * 8]);
+                        const float4 q1 = *reinterpret_cast<const float4*>(&sq[gg][c * 8 + 4]);
+                        s[gg] = fmaf(q0.x, kf[0], s[gg]);
+                        s[gg] = fmaf(q0.y, kf[1], s[gg]);
+                        s[gg] = fmaf(q0.z, kf[2], s[gg]);
+                        s[gg] = fmaf(q0.w, kf[3], s[gg]);
+                        s[gg] = fmaf(q1.x, kf[4], s[gg]);
+                        s[gg] = fmaf(q1.y, kf[5], s[gg]);
+                        s[gg] = fmaf(q1.z, kf[6], s[gg]);
+                        s[gg] = fmaf(q1.w, kf[7], s[gg]);
                     }
                 }
             }
         }
+        // ---- online softmax per head over the slab
 #pragma unroll
-        for (int gg = 0; gg < 8; gg++) {
-            if (gg < G) {
-                float m = s[gg];
+        for (int gg = 0; gg < G; gg++) {
+            {
+                const float sv = mine ? s[gg] : -INFINITY;
+                float mx = sv;
 #pragma unroll
-                for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-                if (lane == 0) s_wred[gg][warp] = m;
-            }
-        }
-        __syncthreads();
-        if (tid < G) {
-            const float m = fmaxf(fmaxf(s_wred[tid][0], s_wred[tid][1]), fmaxf(s_wred[tid][2], s_wred[tid][3]));
-            const float m_old = s_m[tid], m_new = fmaxf(m_old, m);
-            s_alpha[tid] = ex2(m_old - m_new);
-            s_m[tid] = m_new;
-        }
-        __syncthreads();
-#pragma unroll
-        for (int gg = 0; gg < 8; gg++) {
-            if (gg < G) {
-                const float p = (tid < nk) ? ex2(s[gg] - s_m[gg]) : 0.f;
-                sp[gg][tid] = p;
+                for (int of = 16; of > 0; of >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, of));
+                const float m_new = fmaxf(m_run[gg], mx);
+                const float alpha = ex2(m_run[gg] - m_new);
+                const float p = mine ? ex2(sv - m_new) : 0.f;
                 float sum = p;
 #pragma unroll
-                for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-                if (lane == 0) s_wred[gg][warp] = sum;
-            }
-        }
-        asm volatile("cp.async.wait_all;" ::: "memory");
-        __syncthreads();
-        if (tid < G) s_l[tid] = s_l[tid] * s_alpha[tid] + (s_wred[tid][0] + s_wred[tid][1] + s_wred[tid][2] + s_wred[tid][3]);
+                for (int of = 16; of > 0; of >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, of);
+                l_run[gg] = l_run[gg] * alpha + sum;
+                m_run[gg] = m_new;
 #pragma unroll
-        for (int i = 0; i < OPT; i++) {
-            const int idx = tid + 128 * i, gg = idx / D, d = idx % D;
-            if (gg < G) {
-                float o0 = acc[i] * s_alpha[gg], o1 = 0.f;
-                int r = 0;
-                for (; r + 1 < nk; r += 2) {
-                    o0 = fmaf(sp[gg][r], __bfloat162float(sv[r * D + d]), o0);
-                    o1 = fmaf(sp[gg][r + 1], __bfloat162float(sv[(r + 1) * D + d]), o1);
-                }
-                if (r < nk) o0 = fmaf(sp[gg][r], __bfloat162float(sv[r * D + d]), o0);
-                acc[i] = o0 + o1;
+                for (int j = 0; j < DPL; j++) o[gg][j] *= alpha;
+                sp[warp][lane][gg] = p;
             }
         }
+        __syncwarp();
+        // ---- P V for this lane's dims
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+            float vf[DPL];
+#pragma unroll
+            for (int q = 0; q < DPL / 2; q++) {
+                vf[2 * q] = bf16_lo(vr[j][q]);
+                vf[2 * q + 1] = bf16_hi(vr[j][q]);
+            }
+            const float4 p0 = *reinterpret_cast<const float4*>(&sp[warp][j][0]);
+            const float4 p1 = *reinterpret_cast<const float4*>(&sp[warp][j][4]);
+            const float pj[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+#pragma unroll
+            for (int gg = 0; gg < G; gg++)
+#pragma unroll
+                for (int q = 0; q < DPL; q++) o[gg][q] = fmaf(pj[gg], vf[q], o[gg][q]);
+        }
+        __syncwarp();
     }
 
-    // partial stays in shared memory; merge across the cluster over DSMEM
+    // ---- partial of this warp -> shared memory
 #pragma unroll
-    for (int i = 0; i < OPT; i++) {
-        const int idx = tid + 128 * i, gg = idx / D, d = idx % D;
-        if (gg < 8) s_o[gg][d] = acc[i];
+    for (int gg = 0; gg < G; gg++) {
+#pragma unroll
+        for (int q = 0; q < DPL; q++) s_o[warp][gg][lane * DPL + q] = o[gg][q];
+        if (lane == 0) {
+            s_m[warp][gg] = m_run[gg];
+            s_l[warp][gg] = l_run[gg];
+        }
     }
     __syncthreads();
     dec_cluster_sync();
     {
-        constexpr int DS = D / DEC_SPLITS;            // dims merged by this CTA per head
-        const int gg = tid / DS, d = split * DS + tid % DS;
-        if (tid < G * DS) {
-            const uint32_t am = smem_u32(&s_m[gg]), al = smem_u32(&s_l[gg]), ao = smem_u32(&s_o[gg][d]);
+        constexpr int DS = D / DEC_CTAS;              // dims merged by this CTA per head
+        const int gg = tid / DS, d = cr * DS + tid % DS;
+        if (gg < G) {
             float mv[DEC_SPLITS], lv[DEC_SPLITS], ov[DEC_SPLITS];
 #pragma unroll
-            for (int r = 0; r < DEC_SPLITS; r++) {
-                mv[r] = dec_ld_dsmem(am, r);
-                lv[r] = dec_ld_dsmem(al, r);
-                ov[r] = dec_ld_dsmem(ao, r);
+            for (int r = 0; r < DEC_CTAS; r++) {
+#pragma unroll
+                for (int w = 0; w < DEC_WARPS; w++) {
+                    mv[r * DEC_WARPS + w] = dec_ld_dsmem(smem_u32(&s_m[w][gg]), r);
+                    lv[r * DEC_WARPS + w] = dec_ld_dsmem(smem_u32(&s_l[w][gg]), r);
+                    ov[r * DEC_WARPS + w] = dec_ld_dsmem(smem_u32(&s_o[w][gg][d]), r);
+                }
             }
             float M = -INFINITY;
 #pragma unroll
-            for (int r = 0; r < DEC_SPLITS; r++) M = fmaxf(M, mv[r]);
-            float l = 0.f, o = 0.f;
+            for (int i = 0; i < DEC_SPLITS; i++) M = fmaxf(M, mv[i]);
+            float l = 0.f, acc = 0.f;
 #pragma unroll
-            for (int r = 0; r < DEC_SPLITS; r++) {
-                const float w = (mv[r] == -INFINITY) ? 0.f : ex2(mv[r] - M);
-                l += lv[r] * w;
-                o += ov[r] * w;
+            for (int i = 0; i < DEC_SPLITS; i++) {
+                const float w = (mv[i] == -INFINITY) ? 0.f : ex2(mv[i] - M);
+                l += lv[i] * w;
+                acc += ov[i] * w;
             }
-            a.o[(int64_t)b * a.o_sb + (int64_t)(g * G + gg) * a.o_sh + d] = __float2bfloat16_rn(l > 0.f ? o / l : 0.f);
+            a.o[(int64_t)b * a.o_sb + (int64_t)(g * G + gg) * a.o_sh + d] = __float2bfloat16_rn(l > 0.f ? acc / l : 0.f);
             if (d == 0 && a.lse) a.lse[(int64_t)b * a.Hq + g * G + gg] = l > 0.f ? (M + log2f(l)) * kLn2 : -INFINITY;
         }
     }
-    dec_cluster_sync();   // peers may still be reading this CTA's partial
+    dec_cluster_sync();   // peers may still be reading this CTA's partials
 }
 
 // ---------------------------------------------------------------- f32 ------
@@ -546,7 +559,7 @@ int attn_tc_launch(tb_ctx* ctx, const AttnTensors& t, int B, int Hq, int Hkv, in
     return check_launch(ctx, "attn_tc");
 }
 
-// Keys per CTA: the context split 8 ways, rounded up to a multiple of 32.
+// Keys per warp: the context split DEC_SPLITS ways, rounded up to a multiple of 32.
 static int decode_chunk(int max_len) {
     int c = (max_len + DEC_SPLITS - 1) / DEC_SPLITS;
     c = (c + 31) / 32 * 32;
@@ -558,14 +571,14 @@ int attn_decode_launch(tb_ctx* ctx, DecodeArgs a, int B, int D, int max_len, flo
     (void)counters;
     a.chunk = decode_chunk(max_len);
     cudaLaunchConfig_t lc = {};
-    lc.gridDim = dim3(B * a.Hkv, DEC_SPLITS, 1);
+    lc.gridDim = dim3(B * a.Hkv, DEC_CTAS, 1);
     lc.blockDim = dim3(128, 1, 1);
     lc.dynamicSmemBytes = 0;
     lc.stream = ctx->stream;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 1;
-    attr[0].val.clusterDim.y = DEC_SPLITS;
+    attr[0].val.clusterDim.y = DEC_CTAS;
     attr[0].val.clusterDim.z = 1;
     lc.attrs = attr;
     lc.numAttrs = 1;
@@ -574,14 +587,16 @@ int attn_decode_launch(tb_ctx* ctx, DecodeArgs a, int B, int D, int max_len, flo
         attr[1].val.programmaticStreamSerializationAllowed = 1;
         lc.numAttrs = 2;
     }
-    cudaError_t e;
-    if (D == 64) {
-        cudaFuncSetAttribute(attn_decode_kernel<64>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-        e = cudaLaunchKernelEx(&lc, attn_decode_kernel<64>, a, ctx->d_err);
-    } else {
-        cudaFuncSetAttribute(attn_decode_kernel<128>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-        e = cudaLaunchKernelEx(&lc, attn_decode_kernel<128>, a, ctx->d_err);
+    const int G = a.Hq / a.Hkv;
+    cudaError_t e = cudaErrorInvalidValue;
+#define TB_DEC_CASE(DD, GG)                                                                                   \
+    if (D == DD && G == GG) {                                                                                 \
+        cudaFuncSetAttribute(attn_decode_kernel<DD, GG>, cudaFuncAttributePreferredSharedMemoryCarveout, 100); \
+        e = cudaLaunchKernelEx(&lc, attn_decode_kernel<DD, GG>, a, ctx->d_err);                               \
     }
+    TB_DEC_CASE(64, 1) TB_DEC_CASE(64, 2) TB_DEC_CASE(64, 4) TB_DEC_CASE(64, 8)
+    TB_DEC_CASE(128, 1) TB_DEC_CASE(128, 2) TB_DEC_CASE(128, 4) TB_DEC_CASE(128, 8)
+#undef TB_DEC_CASE
     if (e != cudaSuccess) return set_error(ctx, TB_ERR_CUDA, "attn_decode launch: %s", cudaGetErrorString(e));
     return TB_OK;
 }
@@ -618,7 +633,8 @@ extern "C" int tb_attn_fwd(tb_ctx* ctx, int dtype, const void* q, const void* k,
     t.kv_len_alloc = Sk;
     t.o = o; t.o_sh = (int64_t)Sq * D; t.o_ss = D; t.o_sb = (int64_t)Hq * Sq * D;
     t.lse = lse;
-    if (Sq <= 16 && Hq / Hkv <= 8 && Sq == 1) {
+    const int grp = Hq / Hkv;
+    if (Sq == 1 && (grp == 1 || grp == 2 || grp == 4 || grp == 8)) {
         // single-query decode: split-KV CUDA-core kernel
         DecodeArgs a{};
         a.q = (const __nv_bfloat16*)q; a.q_sb = t.q_sb; a.q_sh = t.q_sh;
