@@ -275,18 +275,20 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
 
 // -------------------------------------------------------------- decode -----
 // Decode attention against the KV cache: a few queries, a long context.
-// Grid (B * Hkv, 4) in clusters of (1, 4, 1); each CTA has 4 warps, so the 16
-// warps of a cluster split the context of one (batch, kv head) group into
-// `chunk`-key ranges (chunk a multiple of 32).  A warp walks its range 32
-// keys at a time with its own online softmax: lane j holds key j's K row and
-// its two (D=64) or four (D=128) output dims of the 32 V rows in registers,
-// all loaded up front with coalesced loads; scores use the G = Hq / Hkv
-// queries broadcast from shared memory, the slab's probabilities go through
-// a per-warp shared buffer for the P V product.  Partials (max, sum, o) stay
-// in shared memory; after a cluster barrier CTA rank r merges output dims
-// [r*D/4, (r+1)*D/4) of every head over DSMEM in fixed order (deterministic).
-// D = 64 or 128, G <= 8.
-constexpr int DEC_CTAS = 4;                 // cluster size
+// Grid (B * Hkv, DEC_CTAS) in clusters of (1, DEC_CTAS, 1), 4 warps per CTA:
+// the 4 * DEC_CTAS warps of a cluster split the context of one (batch, kv
+// head) group into `chunk`-key ranges (a multiple of 32).  A warp streams its
+// range in 32-key slabs: one lane issues 1-D bulk async copies (TMA engine)
+// of the slab's contiguous K and V rows into the warp's double-buffered
+// shared memory, so the next slab is in flight while this one is processed.
+// Lane j scores key j against the G = Hq / Hkv queries (broadcast from shared
+// memory; the K row is read in a lane-rotated chunk order, conflict-free),
+// the slab's max / exp / sum run on warp shuffles (online softmax), and the
+// P V product gives each lane D/32 output dims of every head.  Partials
+// (max, sum, o) stay in shared memory; after a cluster barrier CTA rank r
+// merges output dims [r*D/DEC_CTAS, ...) of every head over DSMEM, in fixed
+// order (deterministic).  D = 64 or 128, G in {1, 2, 4, 8}.
+constexpr int DEC_CTAS = 2;                 // cluster size (8 warp-splits per group: one wave at 2 CTAs per SM)
 constexpr int DEC_WARPS = 4;                // warps per CTA
 constexpr int DEC_SPLITS = DEC_CTAS * DEC_WARPS;
 
@@ -302,27 +304,68 @@ __device__ __forceinline__ float dec_ld_dsmem(uint32_t local_addr, uint32_t rank
     return v;
 }
 
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+
+template <int D>
+struct DecSmem {
+    static constexpr int SLAB = 32 * D * 2;                        // bytes of K (or V) per slab
+    static constexpr int KV = DEC_WARPS * 2 * 2 * SLAB;            // [warp][buf][K|V]
+    static constexpr int BYTES = KV + 8 * D * 4 /*sq*/ + DEC_WARPS * 32 * 8 * 4 /*sp*/ +
+                                 DEC_WARPS * 8 * (D + 2) * 4 /*partials*/ + DEC_WARPS * 2 * 8 /*bars*/ + 128;
+};
+
 template <int D, int G>
-__global__ void __launch_bounds__(128, D == 64 ? 4 : 2)
+__global__ void __launch_bounds__(128)
 attn_decode_kernel(DecodeArgs a, int* err) {
     constexpr int DPL = D / 32;                       // output dims per lane
-    __shared__ __align__(16) float sq[8][D];          // queries (exp2-scaled)
-    __shared__ __align__(16) float sp[DEC_WARPS][32][8];   // slab probabilities [key][head]
-    __shared__ float s_m[DEC_WARPS][8], s_l[DEC_WARPS][8];
-    __shared__ float s_o[DEC_WARPS][8][D];
+    using SM = DecSmem<D>;
+    extern __shared__ __align__(128) uint8_t dsm[];
+    uint8_t* kv = dsm;                                              // [warp][buf][K|V][32][D] bf16
+    float (*sq)[D] = reinterpret_cast<float (*)[D]>(dsm + SM::KV);
+    float (*sp)[32][8] = reinterpret_cast<float (*)[32][8]>(dsm + SM::KV + 8 * D * 4);
+    float* sparts = reinterpret_cast<float*>(dsm + SM::KV + 8 * D * 4 + DEC_WARPS * 32 * 8 * 4);   // [warp][8][D+2]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(dsm + SM::KV + 8 * D * 4 + DEC_WARPS * 32 * 8 * 4 +
+                                                 DEC_WARPS * 8 * (D + 2) * 4);
 
     pdl_trigger();
-    pdl_wait();
     const int bg = blockIdx.x, cr = blockIdx.y;
     const int b = bg / a.Hkv, g = bg % a.Hkv;
-    const int L = a.len_ptr ? (*a.len_ptr + a.len) : a.len;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t bar0 = smem_u32(&bars[warp * 2]), bar1 = smem_u32(&bars[warp * 2 + 1]);
+    if (lane == 0) {
+        mbar_init(bar0, 1);
+        mbar_init(bar1, 1);
+        fence_barrier_init();
+    }
+    __syncwarp();
+    pdl_wait();
+    const int L = a.len_ptr ? (*a.len_ptr + a.len) : a.len;
     const int split = cr * DEC_WARPS + warp;
     const int kbeg = split * a.chunk;
     const int kend = min(L, kbeg + a.chunk);
+    const int nslab = kend > kbeg ? (kend - kbeg + 31) / 32 : 0;
     const __nv_bfloat16* kbase = a.k + (int64_t)b * a.kv_sb + (int64_t)g * a.kv_sh;
     const __nv_bfloat16* vbase = a.v + (int64_t)b * a.kv_sb + (int64_t)g * a.kv_sh;
+    uint8_t* wkv = kv + warp * 2 * 2 * SM::SLAB;
 
+    auto issue = [&](int i) {   // lane 0 only
+        const int k0 = kbeg + 32 * i;
+        const int nk = min(32, kend - k0);
+        const uint32_t bytes = (uint32_t)(nk * D * 2);
+        const uint32_t bar = (i & 1) ? bar1 : bar0;
+        uint8_t* buf = wkv + (i & 1) * 2 * SM::SLAB;
+        mbar_expect_tx(bar, 2 * bytes);
+        bulk_g2s(smem_u32(buf), kbase + (int64_t)k0 * a.kv_ss, bytes, bar);
+        bulk_g2s(smem_u32(buf + SM::SLAB), vbase + (int64_t)k0 * a.kv_ss, bytes, bar);
+    };
+    if (lane == 0) {
+        if (nslab > 0) issue(0);
+        if (nslab > 1) issue(1);
+    }
     for (int i = tid; i < 8 * D; i += 128) {
         const int gg = i / D, d = i % D;
         sq[gg][d] = (gg < G) ? __bfloat162float(a.q[(int64_t)b * a.q_sb + (int64_t)(g * G + gg) * a.q_sh + d]) * a.scale_log2
@@ -338,40 +381,26 @@ attn_decode_kernel(DecodeArgs a, int* err) {
 #pragma unroll
         for (int j = 0; j < DPL; j++) o[gg][j] = 0.f;
     }
-    for (int k0 = kbeg; k0 < kend; k0 += 32) {
+    bool ok = true;
+    for (int i = 0; i < nslab; i++) {
+        const int k0 = kbeg + 32 * i;
         const int nk = min(32, kend - k0);
-        // ---- loads: this lane's K row, and dims [lane*DPL, +DPL) of the 32 V rows
-        uint4 kr[D / 8];
         const bool mine = lane < nk;
-        if (mine) {
-            const uint4* kp = reinterpret_cast<const uint4*>(kbase + (int64_t)(k0 + lane) * a.kv_ss);
-#pragma unroll
-            for (int c = 0; c < D / 8; c++) kr[c] = __ldg(kp + c);
-        }
-        uint32_t vr[32][DPL / 2];
-#pragma unroll
-        for (int j = 0; j < 32; j++) {
-            if (j < nk) {
-                const __nv_bfloat16* vp = vbase + (int64_t)(k0 + j) * a.kv_ss + lane * DPL;
-                if (DPL == 2) vr[j][0] = __ldg(reinterpret_cast<const unsigned int*>(vp));
-                else {
-                    uint2 t = __ldg(reinterpret_cast<const uint2*>(vp));
-                    vr[j][0] = t.x;
-                    vr[j][DPL / 2 - 1] = t.y;
-                }
-            } else {
-#pragma unroll
-                for (int q = 0; q < DPL / 2; q++) vr[j][q] = 0u;
-            }
-        }
-        // ---- scores of this lane's key
+        ok = __all_sync(0xffffffffu, mbar_wait((i & 1) ? bar1 : bar0, (i >> 1) & 1, err, DEV_ERR_TIMEOUT_FULL));
+        if (!ok) break;
+        const __nv_bfloat16* sk = reinterpret_cast<const __nv_bfloat16*>(wkv + (i & 1) * 2 * SM::SLAB);
+        const __nv_bfloat16* sv = sk + 32 * D;
+        // ---- scores of this lane's key (chunks visited in lane-rotated order)
         float s[G];
 #pragma unroll
         for (int gg = 0; gg < G; gg++) s[gg] = 0.f;
         if (mine) {
+            const uint4* kr = reinterpret_cast<const uint4*>(sk + lane * D);
 #pragma unroll
-            for (int c = 0; c < D / 8; c++) {
-                const uint32_t w[4] = {kr[c].x, kr[c].y, kr[c].z, kr[c].w};
+            for (int cc = 0; cc < D / 8; cc++) {
+                const int c = (cc + lane) & (D / 8 - 1);
+                const uint4 kw = kr[c];
+                const uint32_t w[4] = {kw.x, kw.y, kw.z, kw.w};
                 float kf[8];
 #pragma unroll
                 for (int j = 0; j < 4; j++) {
@@ -380,51 +409,53 @@ attn_decode_kernel(DecodeArgs a, int* err) {
                 }
 #pragma unroll
                 for (int gg = 0; gg < G; gg++) {
-                    {
-                        const float4 q0 = *reinterpret_cast<const float4*>(&sq[gg][c * 8]);
-                        const float4 q1 = *reinterpret_cast<const float4*>(&sq[gg][c * 8 + 4]);
-                        s[gg] = fmaf(q0.x, kf[0], s[gg]);
-                        s[gg] = fmaf(q0.y, kf[1], s[gg]);
-                        s[gg] = fmaf(q0.z, kf[2], s[gg]);
-                        s[gg] = fmaf(q0.w, kf[3], s[gg]);
-                        s[gg] = fmaf(q1.x, kf[4], s[gg]);
-                        s[gg] = fmaf(q1.y, kf[5], s[gg]);
-                        s[gg] = fmaf(q1.z, kf[6], s[gg]);
-                        s[gg] = fmaf(q1.w, kf[7], s[gg]);
-                    }
+                    const float4 q0 = *reinterpret_cast<const float4*>(&sq[gg][c * 8]);
+                    const float4 q1 = *reinterpret_cast<const float4*>(&sq[gg][c * 8 + 4]);
+                    s[gg] = fmaf(q0.x, kf[0], s[gg]);
+                    s[gg] = fmaf(q0.y, kf[1], s[gg]);
+                    s[gg] = fmaf(q0.z, kf[2], s[gg]);
+                    s[gg] = fmaf(q0.w, kf[3], s[gg]);
+                    s[gg] = fmaf(q1.x, kf[4], s[gg]);
+                    s[gg] = fmaf(q1.y, kf[5], s[gg]);
+                    s[gg] = fmaf(q1.z, kf[6], s[gg]);
+                    s[gg] = fmaf(q1.w, kf[7], s[gg]);
                 }
             }
         }
         // ---- online softmax per head over the slab
 #pragma unroll
         for (int gg = 0; gg < G; gg++) {
-            {
-                const float sv = mine ? s[gg] : -INFINITY;
-                float mx = sv;
+            const float sv_ = mine ? s[gg] : -INFINITY;
+            float mx = sv_;
 #pragma unroll
-                for (int of = 16; of > 0; of >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, of));
-                const float m_new = fmaxf(m_run[gg], mx);
-                const float alpha = ex2(m_run[gg] - m_new);
-                const float p = mine ? ex2(sv - m_new) : 0.f;
-                float sum = p;
+            for (int of = 16; of > 0; of >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, of));
+            const float m_new = fmaxf(m_run[gg], mx);
+            const float alpha = ex2(m_run[gg] - m_new);
+            const float p = mine ? ex2(sv_ - m_new) : 0.f;
+            float sum = p;
 #pragma unroll
-                for (int of = 16; of > 0; of >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, of);
-                l_run[gg] = l_run[gg] * alpha + sum;
-                m_run[gg] = m_new;
+            for (int of = 16; of > 0; of >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, of);
+            l_run[gg] = l_run[gg] * alpha + sum;
+            m_run[gg] = m_new;
 #pragma unroll
-                for (int j = 0; j < DPL; j++) o[gg][j] *= alpha;
-                sp[warp][lane][gg] = p;
-            }
+            for (int j = 0; j < DPL; j++) o[gg][j] *= alpha;
+            sp[warp][lane][gg] = p;
         }
         __syncwarp();
         // ---- P V for this lane's dims
-#pragma unroll
-        for (int j = 0; j < 32; j++) {
+        for (int j = 0; j < nk; j++) {
             float vf[DPL];
-#pragma unroll
-            for (int q = 0; q < DPL / 2; q++) {
-                vf[2 * q] = bf16_lo(vr[j][q]);
-                vf[2 * q + 1] = bf16_hi(vr[j][q]);
+            const __nv_bfloat16* vr = sv + j * D + lane * DPL;
+            if (DPL == 2) {
+                const uint32_t w = *reinterpret_cast<const uint32_t*>(vr);
+                vf[0] = bf16_lo(w);
+                vf[1] = bf16_hi(w);
+            } else {
+                const uint2 w = *reinterpret_cast<const uint2*>(vr);
+                vf[0] = bf16_lo(w.x);
+                vf[1] = bf16_hi(w.x);
+                vf[DPL - 2] = bf16_lo(w.y);
+                vf[DPL - 1] = bf16_hi(w.y);
             }
             const float4 p0 = *reinterpret_cast<const float4*>(&sp[warp][j][0]);
             const float4 p1 = *reinterpret_cast<const float4*>(&sp[warp][j][4]);
@@ -435,16 +466,18 @@ attn_decode_kernel(DecodeArgs a, int* err) {
                 for (int q = 0; q < DPL; q++) o[gg][q] = fmaf(pj[gg], vf[q], o[gg][q]);
         }
         __syncwarp();
+        if (lane == 0 && i + 2 < nslab) issue(i + 2);   // this buffer has been read by every lane
     }
 
-    // ---- partial of this warp -> shared memory
+    // ---- partial of this warp -> shared memory ([warp][head][D + 2])
+    float* wp = sparts + warp * 8 * (D + 2);
 #pragma unroll
     for (int gg = 0; gg < G; gg++) {
 #pragma unroll
-        for (int q = 0; q < DPL; q++) s_o[warp][gg][lane * DPL + q] = o[gg][q];
+        for (int q = 0; q < DPL; q++) wp[gg * (D + 2) + lane * DPL + q] = ok ? o[gg][q] : 0.f;
         if (lane == 0) {
-            s_m[warp][gg] = m_run[gg];
-            s_l[warp][gg] = l_run[gg];
+            wp[gg * (D + 2) + D] = ok ? m_run[gg] : -INFINITY;
+            wp[gg * (D + 2) + D + 1] = ok ? l_run[gg] : 0.f;
         }
     }
     __syncthreads();
@@ -458,9 +491,10 @@ attn_decode_kernel(DecodeArgs a, int* err) {
             for (int r = 0; r < DEC_CTAS; r++) {
 #pragma unroll
                 for (int w = 0; w < DEC_WARPS; w++) {
-                    mv[r * DEC_WARPS + w] = dec_ld_dsmem(smem_u32(&s_m[w][gg]), r);
-                    lv[r * DEC_WARPS + w] = dec_ld_dsmem(smem_u32(&s_l[w][gg]), r);
-                    ov[r * DEC_WARPS + w] = dec_ld_dsmem(smem_u32(&s_o[w][gg][d]), r);
+                    const float* pw = sparts + (w * 8 + gg) * (D + 2);
+                    mv[r * DEC_WARPS + w] = dec_ld_dsmem(smem_u32(pw + D), r);
+                    lv[r * DEC_WARPS + w] = dec_ld_dsmem(smem_u32(pw + D + 1), r);
+                    ov[r * DEC_WARPS + w] = dec_ld_dsmem(smem_u32(pw + d), r);
                 }
             }
             float M = -INFINITY;
@@ -589,10 +623,11 @@ int attn_decode_launch(tb_ctx* ctx, DecodeArgs a, int B, int D, int max_len, flo
     }
     const int G = a.Hq / a.Hkv;
     cudaError_t e = cudaErrorInvalidValue;
-#define TB_DEC_CASE(DD, GG)                                                                                   \
-    if (D == DD && G == GG) {                                                                                 \
-        cudaFuncSetAttribute(attn_decode_kernel<DD, GG>, cudaFuncAttributePreferredSharedMemoryCarveout, 100); \
-        e = cudaLaunchKernelEx(&lc, attn_decode_kernel<DD, GG>, a, ctx->d_err);                               \
+#define TB_DEC_CASE(DD, GG)                                                                                     \
+    if (D == DD && G == GG) {                                                                                   \
+        lc.dynamicSmemBytes = DecSmem<DD>::BYTES;                                                               \
+        cudaFuncSetAttribute(attn_decode_kernel<DD, GG>, cudaFuncAttributeMaxDynamicSharedMemorySize, DecSmem<DD>::BYTES); \
+        e = cudaLaunchKernelEx(&lc, attn_decode_kernel<DD, GG>, a, ctx->d_err);                                 \
     }
     TB_DEC_CASE(64, 1) TB_DEC_CASE(64, 2) TB_DEC_CASE(64, 4) TB_DEC_CASE(64, 8)
     TB_DEC_CASE(128, 1) TB_DEC_CASE(128, 2) TB_DEC_CASE(128, 4) TB_DEC_CASE(128, 8)

@@ -121,36 +121,57 @@ __global__ void rope_kv_kernel(__nv_bfloat16* __restrict__ qkv, int qkv_n, int B
     }
 }
 
-// RMSNorm with an input row stride (last-token gather for the LM head).
+// RMSNorm with an input row stride (last-token gather for the LM head).  One
+// warp per row; the row (N <= 4096 bf16) stays in registers: every load is
+// issued before the reduction, and the second pass reads no memory.
 __global__ void rmsnorm_ld_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, const __nv_bfloat16* __restrict__ w,
                                   __nv_bfloat16* __restrict__ y, int M, int N, float eps) {
     pdl_trigger();
+    constexpr int MAXC = 16;   // 16-byte chunks per lane
+    const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    uint4 g[MAXC];
+#pragma unroll
+    for (int i = 0; i < MAXC; i++) {
+        const int c = (lane + 32 * i) * 8;
+        if (c < N) g[i] = __ldg(reinterpret_cast<const uint4*>(w + c));   // weights: before the wait
+    }
     pdl_wait();
-    int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
-    int lane = threadIdx.x & 31;
     if (row >= M) return;
     const __nv_bfloat16* xr = x + (int64_t)row * ldx;
-    float ss = 0.f;
-    for (int c = lane * 8; c < N; c += 256) {
-        uint4 v = *reinterpret_cast<const uint4*>(xr + c);
-        uint32_t u[4] = {v.x, v.y, v.z, v.w};
+    uint4 v[MAXC];
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            float a = bf16_lo(u[i]), b = bf16_hi(u[i]);
-            ss += a * a + b * b;
+    for (int i = 0; i < MAXC; i++) {
+        const int c = (lane + 32 * i) * 8;
+        if (c < N) v[i] = *reinterpret_cast<const uint4*>(xr + c);
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXC; i++) {
+        const int c = (lane + 32 * i) * 8;
+        if (c < N) {
+            const uint32_t u[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const float a = bf16_lo(u[j]), b = bf16_hi(u[j]);
+                ss += a * a + b * b;
+            }
         }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    float r = rsqrtf(ss * (1.0f / (float)N) + eps);
-    for (int c = lane * 8; c < N; c += 256) {
-        uint4 v = *reinterpret_cast<const uint4*>(xr + c);
-        uint4 g = *reinterpret_cast<const uint4*>(w + c);
-        uint32_t u[4] = {v.x, v.y, v.z, v.w}, gw[4] = {g.x, g.y, g.z, g.w}, o[4];
+    const float r = rsqrtf(ss * (1.0f / (float)N) + eps);
 #pragma unroll
-        for (int i = 0; i < 4; i++)
-            o[i] = pack_bf16x2(bf16_lo(u[i]) * r * bf16_lo(gw[i]), bf16_hi(u[i]) * r * bf16_hi(gw[i]));
-        *reinterpret_cast<uint4*>(y + (int64_t)row * N + c) = make_uint4(o[0], o[1], o[2], o[3]);
+    for (int i = 0; i < MAXC; i++) {
+        const int c = (lane + 32 * i) * 8;
+        if (c < N) {
+            const uint32_t u[4] = {v[i].x, v[i].y, v[i].z, v[i].w}, gw[4] = {g[i].x, g[i].y, g[i].z, g[i].w};
+            uint32_t o[4];
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+                o[j] = pack_bf16x2(bf16_lo(u[j]) * r * bf16_lo(gw[j]), bf16_hi(u[j]) * r * bf16_hi(gw[j]));
+            *reinterpret_cast<uint4*>(y + (int64_t)row * N + c) = make_uint4(o[0], o[1], o[2], o[3]);
+        }
     }
 }
 
@@ -462,8 +483,8 @@ int tb_decoder_create(tb_ctx* ctx, const tb_decoder_config* cfg, tb_decoder** ou
     TB_REQUIRE(ctx, c.head_dim == 64 || c.head_dim == 128, TB_ERR_SHAPE, "decoder: head_dim must be 64 or 128");
     TB_REQUIRE(ctx, c.n_heads % c.n_kv_heads == 0 && c.n_heads / c.n_kv_heads <= 8, TB_ERR_SHAPE,
                "decoder: n_heads must be a multiple of n_kv_heads, group <= 8");
-    TB_REQUIRE(ctx, c.d_model % 64 == 0 && c.ffn_hidden % 128 == 0 && c.vocab % 8 == 0, TB_ERR_SHAPE,
-               "decoder: d_model %% 64, ffn_hidden %% 128, vocab %% 8 must be 0");
+    TB_REQUIRE(ctx, c.d_model % 64 == 0 && c.d_model <= 4096 && c.ffn_hidden % 128 == 0 && c.vocab % 8 == 0,
+               TB_ERR_SHAPE, "decoder: d_model %% 64 (<= 4096), ffn_hidden %% 128, vocab %% 8 must be 0");
     TB_REQUIRE(ctx, c.max_batch > 0 && c.max_seq > 0, TB_ERR_SHAPE, "decoder: max_batch / max_seq");
     TB_REQUIRE(ctx, !c.weights_int8 || c.max_batch <= 64, TB_ERR_SHAPE, "decoder int8: max_batch <= 64");
     tb_decoder* d = new tb_decoder();

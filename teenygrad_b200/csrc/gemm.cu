@@ -241,6 +241,12 @@ __device__ __forceinline__ float ld_dsmem_f32(uint32_t local_addr, uint32_t rank
     return v;
 }
 
+__device__ __forceinline__ void st_dsmem_f32(uint32_t local_addr, uint32_t rank, float v) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_addr), "r"(rank));
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(remote), "f"(v) : "memory");
+}
+
 template <int NT, int STAGES, bool INT8>
 __global__ void __launch_bounds__(256, 1)
 gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
@@ -384,6 +390,9 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
     ok = __all_sync(0xffffffffu, ok);
     __syncwarp();
     tc_fence_after();
+    // Every MMA of this CTA has completed and every TMA landed: its rings may
+    // now be overwritten by peers' partials (first half of a split barrier).
+    if (CS > 1) asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
     const int q = warp & 3, part = warp >> 2;
     constexpr int TP = NT / 2;   // tokens per thread
     const int l = q * 32 + lane;
@@ -446,40 +455,35 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
         }
         return;
     }
-    // partial tile -> own shared memory, [m][row]
-#pragma unroll
-    for (int t = 0; t < TP; t++) {
-        red[(part * TP + t) * 256 + l] = acc[0][t];
-        red[(part * TP + t) * 256 + l + 128] = acc[1][t];
-    }
-    cluster_sync_all();
+    // Push model: rank r owns row pairs [r*P, (r+1)*P), P = 128 / CS.  Every
+    // CTA stores its partials for those rows straight into rank r's buffer
+    // slot [my rank] (red[src][m][p][2]), then one cluster barrier; each rank
+    // then sums its CS slots locally in rank order (deterministic).
     {
-        const int pairs = 128 / CS;           // row pairs reduced by this CTA
-        const int items = pairs * NT;
-        const uint32_t red_base = smem_u32(red);
+        const int P = 128 / CS;
+        const int owner = l / P, pl = l % P;
+        const uint32_t base = smem_u32(red);
+        asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");   // all peers' rings are free
+#pragma unroll
+        for (int t = 0; t < TP; t++) {
+            const int m = part * TP + t;
+            const uint32_t off = (uint32_t)((((split * NT + m) * P + pl) * 2) * 4);
+            st_dsmem_f32(base + off, (uint32_t)owner, acc[0][t]);
+            st_dsmem_f32(base + off + 4, (uint32_t)owner, acc[1][t]);
+        }
+        cluster_sync_all();
+        const int items = P * NT;
         for (int it = threadIdx.x; it < items; it += 256) {
-            const int m = it / pairs, p = split * pairs + (it % pairs);
-            // issue all 2 * CS remote loads before summing (fixed order)
-            float v0[8], v1[8];
-#pragma unroll
-            for (int r = 0; r < 8; r++) {
-                if (r < CS) {
-                    v0[r] = ld_dsmem_f32(red_base + (uint32_t)(m * 256 + p) * 4u, (uint32_t)r);
-                    v1[r] = ld_dsmem_f32(red_base + (uint32_t)(m * 256 + p + 128) * 4u, (uint32_t)r);
-                }
-            }
+            const int m = it / P, pl2 = it % P;
             float a0 = 0.f, a1 = 0.f;
-#pragma unroll
-            for (int r = 0; r < 8; r++) {
-                if (r < CS) {
-                    a0 += v0[r];
-                    a1 += v1[r];
-                }
+            for (int r = 0; r < CS; r++) {
+                const float2 v = *reinterpret_cast<const float2*>(&red[((r * NT + m) * P + pl2) * 2]);
+                a0 += v.x;
+                a1 += v.y;
             }
-            if (ok && m < Mtok) finish(m, p, a0, a1);
+            if (ok && m < Mtok) finish(m, split * P + pl2, a0, a1);
         }
     }
-    cluster_sync_all();   // peers may still be reading this CTA's partials
 }
 
 // =====================================================================
