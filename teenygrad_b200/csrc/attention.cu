@@ -600,9 +600,7 @@ static int decode_chunk(int max_len) {
     return c < 32 ? 32 : c;
 }
 
-int attn_decode_launch(tb_ctx* ctx, DecodeArgs a, int B, int D, int max_len, float* ws, unsigned* counters) {
-    (void)ws;
-    (void)counters;
+int attn_decode_launch(tb_ctx* ctx, DecodeArgs a, int B, int D, int max_len) {
     a.chunk = decode_chunk(max_len);
     cudaLaunchConfig_t lc = {};
     lc.gridDim = dim3(B * a.Hkv, DEC_CTAS, 1);
@@ -634,11 +632,6 @@ int attn_decode_launch(tb_ctx* ctx, DecodeArgs a, int B, int D, int max_len, flo
 #undef TB_DEC_CASE
     if (e != cudaSuccess) return set_error(ctx, TB_ERR_CUDA, "attn_decode launch: %s", cudaGetErrorString(e));
     return TB_OK;
-}
-
-size_t attn_decode_ws_bytes(int B, int Hkv, int D, int max_len) {
-    (void)B; (void)Hkv; (void)D; (void)max_len;
-    return 0;   // partials stay in shared memory (cluster merge)
 }
 
 }  // namespace tb
@@ -678,9 +671,7 @@ extern "C" int tb_attn_fwd(tb_ctx* ctx, int dtype, const void* q, const void* k,
         a.o = (__nv_bfloat16*)o; a.o_sb = t.o_sb; a.o_sh = t.o_sh;
         a.lse = lse; a.Hq = Hq; a.Hkv = Hkv; a.len = Sk; a.len_ptr = nullptr;
         a.scale_log2 = scale * kLog2e;
-        int rc = ensure_workspace(ctx, attn_decode_ws_bytes(B, Hkv, D, Sk), (size_t)B * Hkv);
-        if (rc) return rc;
-        return attn_decode_launch(ctx, a, B, D, Sk, (float*)ctx->ws, ctx->counters);
+        return attn_decode_launch(ctx, a, B, D, Sk);
     }
     return attn_tc_launch(ctx, t, B, Hq, Hkv, Sq, Sk, D, scale, causal);
 }

@@ -41,14 +41,12 @@ struct DecodeArgs {
     int len;               // context length if len_ptr is null, else added to *len_ptr
     const int* len_ptr;    // device-resident context length (CUDA-graph replay)
     float scale_log2;
-    int chunk;
-    float* ws;
-    unsigned* counters;
+    int chunk;             // keys per warp (set by attn_decode_launch)
 };
 
 int attn_tc_launch(tb_ctx* ctx, const AttnTensors& t, int B, int Hq, int Hkv, int Sq, int Sk, int D,
                    float scale, int causal);
-int attn_decode_launch(tb_ctx* ctx, DecodeArgs a, int B, int D, int max_len, float* ws, unsigned* counters);
-size_t attn_decode_ws_bytes(int B, int Hkv, int D, int max_len);
+// Decode attention over a KV cache of capacity >= max_len; no global scratch.
+int attn_decode_launch(tb_ctx* ctx, DecodeArgs a, int B, int D, int max_len);
 
 }  // namespace tb

@@ -26,33 +26,6 @@ int check_launch(tb_ctx* ctx, const char* what) {
     return TB_OK;
 }
 
-int ensure_workspace(tb_ctx* ctx, size_t bytes, size_t n_counters) {
-    if (bytes > ctx->ws_bytes) {
-        if (ctx->ws) TB_CUDA_TRY(ctx, cudaFree(ctx->ws));
-        ctx->ws = nullptr;
-        ctx->ws_bytes = 0;
-        size_t want = bytes < (8u << 20) ? (8u << 20) : bytes;
-        if (cudaMalloc(&ctx->ws, want) != cudaSuccess) {
-            cudaGetLastError();
-            return set_error(ctx, TB_ERR_OOM, "workspace allocation of %zu bytes failed", want);
-        }
-        ctx->ws_bytes = want;
-    }
-    if (n_counters > ctx->n_counters) {
-        if (ctx->counters) TB_CUDA_TRY(ctx, cudaFree(ctx->counters));
-        ctx->counters = nullptr;
-        ctx->n_counters = 0;
-        size_t want = n_counters < 4096 ? 4096 : n_counters;
-        if (cudaMalloc(&ctx->counters, want * sizeof(unsigned)) != cudaSuccess) {
-            cudaGetLastError();
-            return set_error(ctx, TB_ERR_OOM, "counter allocation failed");
-        }
-        TB_CUDA_TRY(ctx, cudaMemset(ctx->counters, 0, want * sizeof(unsigned)));
-        ctx->n_counters = want;
-    }
-    return TB_OK;
-}
-
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
@@ -154,8 +127,6 @@ int tb_init(tb_ctx** out, int device) {
 int tb_destroy(tb_ctx* ctx) {
     if (!ctx) return TB_OK;
     cudaSetDevice(ctx->device);
-    if (ctx->ws) cudaFree(ctx->ws);
-    if (ctx->counters) cudaFree(ctx->counters);
     if (ctx->d_err) cudaFree(ctx->d_err);
     delete ctx;
     return TB_OK;

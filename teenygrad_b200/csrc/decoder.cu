@@ -287,10 +287,6 @@ struct tb_decoder {
     float* logits = nullptr;
     int32_t *ids_in = nullptr, *cur_ids = nullptr, *out_ids = nullptr;
     int* state = nullptr;   // [0] tokens in cache, [1] tokens generated
-    float* ws = nullptr;
-    size_t ws_bytes = 0;
-    unsigned* counters = nullptr;
-    size_t n_counters = 0;
     unsigned long long* amax_keys = nullptr;   // [max_batch], zero between launches
     unsigned* amax_cnt = nullptr;              // [max_batch], zero between launches
     cudaStream_t cap_stream = nullptr;
@@ -342,8 +338,7 @@ int lin(tb_decoder* d, const void* x, const void* w, const int8_t* wq, const flo
     ep.swiglu = swiglu ? 1 : 0;
     const bool int8 = d->cfg.weights_int8 && wq;
     if (int8) ep.scale = wscale;
-    return linear_launch(d->ctx, int8 ? 1 : 0, x, int8 ? (const void*)wq : w, ep, M, N, K, d->ws, d->ws_bytes,
-                         d->counters, d->n_counters);
+    return linear_launch(d->ctx, int8 ? 1 : 0, x, int8 ? (const void*)wq : w, ep, M, N, K);
 }
 
 int rms(tb_decoder* d, const bf16* x, int64_t ldx, const bf16* w, bf16* y, int M) {
@@ -409,7 +404,7 @@ int layer_forward(tb_decoder* d, int l, int B, int S_new, bool decode) {
         a.len = 1;                 // keys = tokens already cached + this one
         a.len_ptr = d->state;
         a.scale_log2 = scale * 1.4426950408889634f;
-        TB_TRY(attn_decode_launch(ctx, a, B, hd, c.max_seq, d->ws, d->counters));
+        TB_TRY(attn_decode_launch(ctx, a, B, hd, c.max_seq));
     }
     TB_TRY(lin(d, d->attn, L.wo, L.qo, L.so, d->x, T, dm, d->q_dim, d->x, false, false));
     TB_TRY(rms(d, d->x, dm, L.mlp_norm, d->h, T));
@@ -541,29 +536,12 @@ int tb_decoder_create(tb_ctx* ctx, const tb_decoder_config* cfg, tb_decoder** ou
     A(&d->cur_ids, (size_t)c.max_batch);
     A(&d->out_ids, (size_t)c.max_batch * c.max_seq);
     A(&d->state, 4);
-    // split-K / decode-attention scratch, sized for the largest decode-step user
-    size_t need = attn_decode_ws_bytes(c.max_batch, c.n_kv_heads, c.head_dim, c.max_seq), ncnt = (size_t)c.max_batch * c.n_kv_heads;
-    // the GEMV path serves every call of <= 64 tokens (decode, small prefills)
-    const int64_t mt = d->max_tokens > c.max_batch ? d->max_tokens : c.max_batch;
-    const int Mg = mt <= 64 ? (int)mt : 64;
-    const int shapes[5][2] = {{d->qkv_n, (int)dm}, {(int)dm, d->q_dim}, {(int)(2 * F), (int)dm}, {(int)dm, (int)F}, {(int)V, (int)dm}};
-    for (auto& s : shapes) {
-        size_t b = 0, n = 0;
-        gemv_ws_need(ctx, Mg, s[0], s[1], &b, &n);
-        need = need > b ? need : b;
-        ncnt = ncnt > n ? ncnt : n;
-    }
-    d->ws_bytes = need < 1024 ? 1024 : need;
-    d->n_counters = ncnt;
-    A(&d->ws, d->ws_bytes / sizeof(float) + 1);
-    A(&d->counters, ncnt);
     A(&d->amax_keys, (size_t)c.max_batch);
     A(&d->amax_cnt, (size_t)c.max_batch);
     if (rc) {
         tb_decoder_destroy(d);
         return rc;
     }
-    cudaMemset(d->counters, 0, ncnt * sizeof(unsigned));
     cudaMemset(d->amax_keys, 0, (size_t)c.max_batch * sizeof(unsigned long long));
     cudaMemset(d->amax_cnt, 0, (size_t)c.max_batch * sizeof(unsigned));
     cudaMemset(d->state, 0, 4 * sizeof(int));

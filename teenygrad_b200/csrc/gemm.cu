@@ -574,12 +574,6 @@ static void gemv_split(int num_sms, int Nw, int K, int* splits_out, int* kb_per_
     *kb_per_out = kb_per;
 }
 
-void gemv_ws_need(tb_ctx* ctx, int M, int N, int K, size_t* bytes, size_t* counters) {
-    (void)ctx; (void)M; (void)N; (void)K;
-    *bytes = 0;       // partials stay in shared memory (cluster reduction)
-    *counters = 0;
-}
-
 template <int NT, int STAGES, bool INT8>
 static int launch_gemv_tc(tb_ctx* ctx, const void* x, const void* w, const Epi& ep, int Mtok, int Nw, int K) {
     using C = GemvCfg<NT, STAGES, INT8>;
@@ -631,8 +625,7 @@ static int dispatch_gemv(tb_ctx* ctx, const void* x, const void* w, const Epi& e
     return launch_gemv_tc<64, INT8 ? 6 : 5, INT8>(ctx, x, w, ep, M, N, K);
 }
 
-int linear_launch(tb_ctx* ctx, int int8, const void* x, const void* w, const Epi& ep, int M, int N, int K,
-                  float* ws, size_t ws_bytes, unsigned* counters, size_t n_counters) {
+int linear_launch(tb_ctx* ctx, int int8, const void* x, const void* w, const Epi& ep, int M, int N, int K) {
     if (int8) {
         if (M > 64) return set_error(ctx, TB_ERR_UNSUPPORTED, "int8 linear: at most 64 tokens");
         return dispatch_gemv<true>(ctx, x, w, ep, M, N, K);
@@ -640,14 +633,6 @@ int linear_launch(tb_ctx* ctx, int int8, const void* x, const void* w, const Epi
     if (M <= 64) return dispatch_gemv<false>(ctx, x, w, ep, M, N, K);
     if (N <= 128 && !ep.swiglu) return launch_gemm_tc<128, 6, false>(ctx, x, w, ep, M, N, K);
     return launch_gemm_tc<256, 4, false>(ctx, x, w, ep, M, N, K);
-}
-
-static int ctx_linear(tb_ctx* ctx, int int8, const void* x, const void* w, const Epi& ep, int M, int N, int K) {
-    size_t bytes = 0, cnt = 0;
-    if (M <= 64) gemv_ws_need(ctx, M, N, K, &bytes, &cnt);
-    int rc = ensure_workspace(ctx, bytes, cnt);
-    if (rc) return rc;
-    return linear_launch(ctx, int8, x, w, ep, M, N, K, (float*)ctx->ws, ctx->ws_bytes, ctx->counters, ctx->n_counters);
 }
 
 }  // namespace tb
@@ -690,7 +675,7 @@ int tb_linear_fwd(tb_ctx* ctx, int dtype, const void* x, const void* w, const fl
     ep.resid = (flags & TB_EPI_RESIDUAL) ? residual : nullptr;
     ep.ldr = N;
     ep.swiglu = swiglu ? 1 : 0;
-    return ctx_linear(ctx, 0, x, w, ep, (int)M, (int)N, (int)K);
+    return linear_launch(ctx, 0, x, w, ep, (int)M, (int)N, (int)K);
 }
 
 int tb_matmul_fwd(tb_ctx* ctx, int dtype, const void* a, const void* b, void* c, int64_t M, int64_t N, int64_t K) {
@@ -732,7 +717,7 @@ int tb_int8_linear_fwd(tb_ctx* ctx, const void* x, const int8_t* q, const float*
     ep.ldr = N;
     ep.scale = scale;
     ep.swiglu = swiglu ? 1 : 0;
-    return ctx_linear(ctx, 1, x, q, ep, (int)M, (int)N, (int)K);
+    return linear_launch(ctx, 1, x, q, ep, (int)M, (int)N, (int)K);
 }
 
 }  // extern "C"

@@ -19,13 +19,9 @@ struct Epi {
     int swiglu;            // gate/up interleaved in 128-row blocks
 };
 
-// Split-K workspace the decode GEMV needs for (M tokens, N rows, K): bytes of
-// f32 partials and the number of tile counters (zero-initialised, left at zero).
-void gemv_ws_need(tb_ctx* ctx, int M, int N, int K, size_t* bytes, size_t* counters);
-
 // y = epilogue(x[M,K] w[N,K]^T).  int8 = 1: w is int8 with ep.scale (M <= 64).
-// ws / counters: caller-owned split-K scratch (see gemv_ws_need).
-int linear_launch(tb_ctx* ctx, int int8, const void* x, const void* w, const Epi& ep, int M, int N, int K,
-                  float* ws, size_t ws_bytes, unsigned* counters, size_t n_counters);
+// Needs no global scratch: the decode GEMV reduces its K splits in shared
+// memory across a thread-block cluster.
+int linear_launch(tb_ctx* ctx, int int8, const void* x, const void* w, const Epi& ep, int M, int N, int K);
 
 }  // namespace tb

@@ -16,10 +16,6 @@ struct tb_ctx {
     int num_sms = 148;
     cudaStream_t stream = nullptr;
     int* d_err = nullptr;           // device error word (bounded-wait timeouts)
-    void* ws = nullptr;             // split-K partials etc.; grows on demand
-    size_t ws_bytes = 0;
-    unsigned* counters = nullptr;   // split-K arrival counters, kept at zero between launches
-    size_t n_counters = 0;
     std::string last_error;
     void* comm = nullptr;           // NCCL communicator state (comm.cu)
     bool pdl = false;               // launch with programmatic stream serialization
@@ -31,10 +27,6 @@ int set_error(tb_ctx* ctx, int status, const char* fmt, ...);
 
 // Records cudaGetLastError() (launch-configuration errors) into ctx.
 int check_launch(tb_ctx* ctx, const char* what);
-
-// Ensures ctx->ws has at least `bytes` and ctx->counters at least `n` zeroed
-// entries.  Grows with cudaMalloc (synchronous): not for use during capture.
-int ensure_workspace(tb_ctx* ctx, size_t bytes, size_t n_counters);
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
 // dims/strides in elements / bytes as the driver API defines them
