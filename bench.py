@@ -33,6 +33,8 @@ C4 = dict(n_layers=16, d_model=2048, n_heads=32, n_kv_heads=8, head_dim=64, ffn_
 C5 = dict(n_layers=16, d_model=2048, n_heads=32, n_kv_heads=8, head_dim=64, ffn_hidden=8192, vocab=32000,
           batch=64, ctx=2048)
 C3 = dict(B=8, H=32, S=4096, D=128)
+C2 = dict(B=32, C=64, H=56, W=56, layers=4)
+C1 = dict(B=1, S=128, d=256, heads=4, ffn=1024)
 
 
 def peaks():
@@ -442,13 +444,76 @@ def run_c3(args, rank, world, local):
             "clocks": clocks}
 
 
+def run_c2(args, rank, world, local):
+    """4 x (3x3 conv 64->64, pad 1 + bias + folded BN + ReLU), NCHW, batch 32, 56x56."""
+    import torch
+    from teenygrad_b200 import ops
+    c = C2
+    B, C, H, W = c["B"], c["C"], c["H"], c["W"]
+    g = torch.Generator(device="cpu").manual_seed(0)
+    res = {}
+    pk = peaks()
+    flops_conv = 2 * B * C * H * W * C * 9
+    for dt in (torch.bfloat16, torch.float32):
+        x = torch.randn(B, C, H, W, generator=g).to("cuda", dt)
+        layers = []
+        for _ in range(c["layers"]):
+            w = (torch.randn(C, C, 3, 3, generator=g) * math.sqrt(2.0 / (C * 9))).to("cuda", dt)
+            bias = (torch.randn(C, generator=g) * 0.1).cuda()
+            gam, bet = (torch.rand(C, generator=g) + 0.5).cuda(), (torch.randn(C, generator=g) * 0.1).cuda()
+            mu, var = (torch.randn(C, generator=g) * 0.1).cuda(), (torch.rand(C, generator=g) + 0.5).cuda()
+            sc, sh = ops.bn_fold(gam, bet, mu, var, 1e-5, bias)
+            layers.append((w, sc, sh))
+
+        def stage():
+            y = x
+            for w, sc, sh in layers:
+                y = ops.conv2d(y, w, scale=sc, shift=sh, pad=1, act="relu")
+            return y
+
+        for _ in range(args.warmup):
+            stage()
+        ms = time_loop(stage, max(args.steps, 3))
+        ms_conv = time_loop(lambda: ops.conv2d(x, layers[0][0], scale=layers[0][1], shift=layers[0][2], pad=1, act="relu"), 5)
+        res[str(dt).split(".")[1]] = (ms, ms_conv)
+    ms_bf16, conv_bf16 = res["bfloat16"]
+    ms_f32, conv_f32 = res["float32"]
+    tf = flops_conv / (conv_bf16 / 1e3) / 1e12
+    return {"metric": "images/s (ResNet-style conv stage, 4 x conv3x3 + bias + BN + ReLU)", "value": round(world * B / (ms_bf16 / 1e3), 1),
+            "unit": "images/s", "n_gpus": world, "steps": max(args.steps, 3), "warmup": args.warmup, "ms_per_step": round(ms_bf16, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "C2: 4 x 3x3 conv 64->64 + bias + folded BN + ReLU, B32 56x56 NCHW",
+                       "fp32_ms_per_step": round(ms_f32, 3), "fp32_images_per_s": round(B / (ms_f32 / 1e3), 1),
+                       "bf16_conv_ms": round(conv_bf16, 4), "fp32_conv_ms": round(conv_f32, 4),
+                       "fp32_conv_tflops": round(flops_conv / (conv_f32 / 1e3) / 1e12, 1)},
+            "roofline": {"kernel": "conv_tc_kernel (+ NHWC transpose), one conv", "bound": "tensor", "achieved": round(tf, 1),
+                         "peak": pk["tc"], "unit": "TFLOP/s", "frac": round(tf / pk["tc"], 3), "traffic": None,
+                         "peak_source": pk["src"]}}
+
+
+def run_c1(args, rank, world, local):
+    import torch
+    from teenygrad_b200.block import block_forward, random_block_params
+    c = C1
+    p = random_block_params(d=c["d"], F=c["ffn"], seed=0)
+    x = torch.randn(c["B"], c["S"], c["d"], device="cuda")
+    for _ in range(args.warmup):
+        block_forward(x, p, c["heads"])
+    us = graph_time(lambda: block_forward(x, p, c["heads"]), iters=50) * 1e3
+    return {"metric": "us per block (fp32 pre-norm transformer block)", "value": round(us, 2), "unit": "us",
+            "n_gpus": world, "steps": 50, "warmup": args.warmup, "ms_per_step": round(us / 1e3, 5),
+            "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "C1: B1 S128 d256 4x64 heads, causal SDPA, RMSNorm 1e-6, SwiGLU 1024, fp32",
+                       "timing": "CUDA graph of one block forward (latency-bound; 10 launches)"}}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="c4", choices=["c4", "c5", "c3"])
+    ap.add_argument("--workload", default="c4", choices=["c4", "c5", "c3", "c2", "c1"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
@@ -468,9 +533,9 @@ def main():
         return 0
 
     rank, world, local = dist_setup(max(args.gpus, world_env))
-    run = {"c4": run_c4, "c5": run_c5, "c3": run_c3}[args.workload]
+    run = {"c4": run_c4, "c5": run_c5, "c3": run_c3, "c2": run_c2, "c1": run_c1}[args.workload]
     res = run(args, rank, world, local)
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload in ("c4", "c5"):
         res["cpu_baseline"] = cpu_baseline_c5() if args.workload == "c5" else cpu_baseline_c4()
     if rank == 0:
         print(json.dumps(res), flush=True)

@@ -136,6 +136,34 @@ TB_API int tb_int8_linear_fwd(tb_ctx* ctx, const void* x, const int8_t* q, const
 TB_API int tb_attn_fwd(tb_ctx* ctx, int dtype, const void* q, const void* k, const void* v, void* o,
                 float* lse, int B, int Hq, int Hkv, int Sq, int Sk, int D, float scale, int causal);
 
+/* --------------------------------------------------------------- conv --- */
+/* conv2d_bias_forward (nn/conv/conv2d.rs:643-764; Conv2dBiasForward RuntimeOp
+ * :766-820; the inference fusion of graph/mod.rs:845-918) with the folded-BN
+ * epilogue of nn/fused/conv2d_bn_silu.rs:141-170:
+ *   y = act(scale[co] * (conv(x, w) [+ bias[co] if shift is NULL]) + shift[co])
+ * NCHW x [B, Cin, H, W], w [Cout, Cin, KH, KW], y [B, Cout, OH, OW], groups = 1,
+ * zero padding.  bias / bn_scale / bn_shift are f32 [Cout] and may be NULL
+ * (scale 1, shift 0).  act: TB_ACT_NONE, TB_ACT_RELU or TB_ACT_SILU.
+ * TB_BF16 with stride 1 and OW % 8 == 0 runs as a tcgen05 implicit GEMM and
+ * needs a workspace of tb_conv2d_workspace_size() bytes (NHWC copy of x,
+ * reordered weights); other bf16 shapes and TB_F32 run on CUDA cores with f32
+ * accumulation and need none. */
+TB_API int tb_conv2d_workspace_size(int dtype, int B, int Cin, int Cout, int H, int W, int KH, int KW, int stride,
+                                    int pad, size_t* bytes);
+TB_API int tb_conv2d_fwd(tb_ctx* ctx, int dtype, const void* x, const void* w, const float* bias,
+                         const float* bn_scale, const float* bn_shift, void* y, int B, int Cin, int Cout, int H,
+                         int W, int KH, int KW, int stride, int pad, int act, void* workspace,
+                         size_t workspace_bytes);
+/* BN folding (nn/fused/conv2d_bn_silu.rs:33-35): scale = gamma / sqrt(var + eps),
+ * shift = beta - scale * mean (+ scale * bias when bias is given).  f32 [C]. */
+TB_API int tb_bn_fold(tb_ctx* ctx, const float* gamma, const float* beta, const float* mean, const float* var,
+                      const float* bias, float eps, float* scale, float* shift, int C);
+/* batch_norm_2d_nchw_forward_inference (nn/norm/batchnorm.rs:574-686):
+ * y = (x - mean[c]) * rsqrt(var[c] + eps) * gamma[c] + beta[c], x [B, C, HW]. */
+TB_API int tb_batchnorm_fwd(tb_ctx* ctx, int dtype, const void* x, const float* gamma, const float* beta,
+                            const float* mean, const float* var, void* y, int64_t B, int64_t C, int64_t HW,
+                            float eps);
+
 /* ------------------------------------------------------------ decoder --- */
 /* RoPE, rotate-half pairing (d, d + D/2), inv_freq = theta^(-2i/D).
  * x, y [T, H, D] (may alias), pos [T] int32. */

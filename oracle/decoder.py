@@ -116,3 +116,22 @@ def random_params(cfg, seed=0, std=0.02):
                            w_gate=w(F, d), w_up=w(F, d), w_down=w(d, F)))
     return dict(embed=round_bf16(r.standard_normal((V, d)).astype(np.float32)), lm_head=w(V, d),
                 final_norm=g(d), layers=layers)
+
+
+def block_forward(x, p, n_heads, eps=1e-6):
+    """CPU oracle of the fp32 pre-norm block (teenygrad_b200.block), numpy f32."""
+    B, S, d = x.shape
+    hd = d // n_heads
+    X = x.reshape(B * S, d)
+    h = rmsnorm(X, p["attn_norm"], eps)[0]
+    q, k, v = (linear(h, p[n]) for n in ("wq", "wk", "wv"))
+
+    def heads(t):
+        return t.reshape(B, S, n_heads, hd).transpose(0, 2, 1, 3)
+
+    o, _ = attention(heads(q), heads(k), heads(v), 1.0 / np.sqrt(hd), True)
+    o = o.transpose(0, 2, 1, 3).reshape(B * S, d)
+    X = linear(o, p["wo"], None, X)
+    h = rmsnorm(X, p["mlp_norm"], eps)[0]
+    a = swiglu(linear(h, p["w_gate"]), linear(h, p["w_up"]))
+    return linear(a, p["w_down"], None, X).reshape(B, S, d)

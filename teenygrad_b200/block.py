@@ -1,0 +1,46 @@
+"""Pre-norm transformer block from the library's ops.
+
+x -> x + Wo attn(rmsnorm(x))  -> x + Wd (silu(Wg h) * (Wu h)), h = rmsnorm(x)
+
+fp32 end to end (f32 CUDA-core linear and attention paths), causal SDPA with
+scale 1/sqrt(head_dim), no RoPE (the config names none).  The reference has
+no block-level op; this is the composition its graph would lower to from
+RmsNorm / Linear / attention / SiLU / Mul / Add nodes
+(kernels/teeny-kernels/src/graph/mod.rs:1117, :1228, :1734).
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import ops
+
+
+def block_forward(x, p, n_heads, eps=1e-6):
+    """x [B, S, d] f32; p: dict of f32 cuda tensors attn_norm [d], wq/wk/wv/wo
+    [d, d], mlp_norm [d], w_gate/w_up [F, d], w_down [d, F]."""
+    B, S, d = x.shape
+    hd = d // n_heads
+    h = ops.rms_norm(x, p["attn_norm"], eps)
+    q, k, v = (ops.linear(h, p[n]) for n in ("wq", "wk", "wv"))
+
+    def heads(t):
+        return t.view(B, S, n_heads, hd).transpose(1, 2).contiguous()
+
+    o = ops.attention(heads(q), heads(k), heads(v), scale=1.0 / math.sqrt(hd), causal=True)
+    o = o.transpose(1, 2).contiguous().view(B, S, d)
+    x = ops.linear(o, p["wo"], residual=x)
+    h = ops.rms_norm(x, p["mlp_norm"], eps)
+    a = ops.swiglu(ops.linear(h, p["w_gate"]), ops.linear(h, p["w_up"]))
+    return ops.linear(a, p["w_down"], residual=x)
+
+
+def random_block_params(d=256, F=1024, seed=0, device="cuda"):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+
+    def w(*s):
+        return (torch.randn(*s, generator=g) * 0.02).to(device)
+
+    return dict(attn_norm=torch.ones(d, device=device), wq=w(d, d), wk=w(d, d), wv=w(d, d), wo=w(d, d),
+                mlp_norm=torch.ones(d, device=device), w_gate=w(F, d), w_up=w(F, d), w_down=w(d, F))

@@ -48,6 +48,13 @@ static EncodeTiledFn get_encode_fn() {
 int make_tmap(tb_ctx* ctx, CUtensorMap* out, CUtensorMapDataType dt, int rank, const void* base,
               const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
               CUtensorMapSwizzle swz) {
+    const cuuint32_t ones[5] = {1, 1, 1, 1, 1};
+    return make_tmap_strided(ctx, out, dt, rank, base, dims, strides_bytes, box, ones, swz);
+}
+
+int make_tmap_strided(tb_ctx* ctx, CUtensorMap* out, CUtensorMapDataType dt, int rank, const void* base,
+                      const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+                      const cuuint32_t* elem_strides, CUtensorMapSwizzle swz) {
     EncodeTiledFn fn = get_encode_fn();
     if (!fn) return set_error(ctx, TB_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
     cuuint64_t d[5];
@@ -56,7 +63,7 @@ int make_tmap(tb_ctx* ctx, CUtensorMap* out, CUtensorMapDataType dt, int rank, c
     for (int i = 0; i < rank; i++) {
         d[i] = dims[i];
         b[i] = box[i];
-        e[i] = 1;
+        e[i] = elem_strides[i];
         if (i + 1 < rank) s[i] = strides_bytes[i];
     }
     CUresult r = fn(out, dt, (cuuint32_t)rank, const_cast<void*>(base), d, s, b, e,

@@ -35,6 +35,11 @@ int make_tmap(tb_ctx* ctx, CUtensorMap* out, CUtensorMapDataType dt, int rank, c
               const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
               CUtensorMapSwizzle swz);
 
+// As make_tmap, with per-dimension element (traversal) strides.
+int make_tmap_strided(tb_ctx* ctx, CUtensorMap* out, CUtensorMapDataType dt, int rank, const void* base,
+                      const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+                      const cuuint32_t* elem_strides, CUtensorMapSwizzle swz);
+
 // 2-D K-major bf16/int8 operand: rows x cols (cols contiguous), box = box_cols x box_rows.
 int make_tmap_2d(tb_ctx* ctx, CUtensorMap* out, CUtensorMapDataType dt, int elem_bytes,
                  const void* base, uint64_t rows, uint64_t cols, uint64_t row_stride_elems,

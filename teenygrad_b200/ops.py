@@ -301,3 +301,57 @@ class MatMulForward(_Op):
 
 class FlashAttention2Forward(_Op):
     fn = staticmethod(attention)
+
+
+# ----------------------------------------------------------------- conv ---
+def bn_fold(gamma, beta, mean, var, eps=1e-5, bias=None):
+    """BN folding of nn/fused/conv2d_bn_silu.rs:33-35 (f32 [C])."""
+    _cuda(gamma, beta, mean, var, bias)
+    C = gamma.numel()
+    scale = torch.empty(C, device=gamma.device, dtype=torch.float32)
+    shift = torch.empty_like(scale)
+    ctx = context()
+    check(ctx, lib().tb_bn_fold(ctx, _p(gamma), _p(beta), _p(mean), _p(var), _p(bias), _f(eps), _p(scale), _p(shift),
+                                ctypes.c_int(C)))
+    return scale, shift
+
+
+def batch_norm_inference(x, gamma, beta, mean, var, eps=1e-5):
+    """batch_norm_2d_nchw_forward_inference (nn/norm/batchnorm.rs:574-686); x [B, C, ...]."""
+    _cuda(x, gamma, beta, mean, var)
+    B, C = x.shape[0], x.shape[1]
+    HW = x.numel() // max(1, B * C)
+    y = torch.empty_like(x)
+    ctx = context()
+    check(ctx, lib().tb_batchnorm_fwd(ctx, _dt(x), _p(x), _p(gamma), _p(beta), _p(mean), _p(var), _p(y), _i64(B),
+                                      _i64(C), _i64(HW), _f(eps)))
+    return y
+
+
+_CONV_ACT = {None: -1, "relu": 2, "silu": 0}
+
+
+def conv2d(x, w, bias=None, scale=None, shift=None, stride=1, pad=0, act=None):
+    """conv2d_bias_forward (nn/conv/conv2d.rs:643-764) + folded-BN epilogue
+    (nn/fused/conv2d_bn_silu.rs:141-170); NCHW, groups = 1."""
+    _cuda(x, w, bias, scale, shift)
+    B, C, H, W = x.shape
+    Co, _, KH, KW = w.shape
+    OH = (H + 2 * pad - KH) // stride + 1
+    OW = (W + 2 * pad - KW) // stride + 1
+    y = torch.empty(B, Co, OH, OW, device=x.device, dtype=x.dtype)
+    nbytes = ctypes.c_size_t(0)
+    st = lib().tb_conv2d_workspace_size(ctypes.c_int(_dt(x)), *(ctypes.c_int(v) for v in (B, C, Co, H, W, KH, KW, stride, pad)),
+                                        ctypes.byref(nbytes))
+    check(None, st)
+    ws = torch.empty(max(1, nbytes.value), device=x.device, dtype=torch.uint8) if nbytes.value else None
+    ctx = context()
+    f = [t if t is None or t.dtype == torch.float32 else t.float().contiguous() for t in (bias, scale, shift)]
+    check(ctx, lib().tb_conv2d_fwd(ctx, ctypes.c_int(_dt(x)), _p(x), _p(w), _p(f[0]), _p(f[1]), _p(f[2]), _p(y),
+                                   *(ctypes.c_int(v) for v in (B, C, Co, H, W, KH, KW, stride, pad, _CONV_ACT[act])),
+                                   _p(ws), ctypes.c_size_t(nbytes.value)))
+    return y
+
+
+class Conv2dBiasForward(_Op):
+    fn = staticmethod(conv2d)

@@ -1,0 +1,86 @@
+"""GPU parity of conv2d (+ bias, folded BN, activation), BN folding and
+batch-norm inference against the reference fixtures and the CPU oracle."""
+import numpy as np
+import pytest
+
+from gpu_util import BF16_TOL, F32_TOL, assert_close, bf16_round, dev, no_device_error, np_of, rng, to_gpu, torch
+from golden_io import load
+
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _gpu():
+    dev()
+    yield
+    no_device_error()
+
+
+def ops():
+    from teenygrad_b200 import ops as o
+    return o
+
+
+@pytest.mark.parametrize("name,pad,oh", [("conv2d", 0, 6), ("conv2d_padded", 1, 8)])
+def test_conv2d_golden_f32(name, pad, oh):
+    x = load(name, "x.bin", (1, 2, 8, 8))
+    w = load(name, "w.bin", (4, 2, 3, 3))
+    y = ops().conv2d(to_gpu(x), to_gpu(w), pad=pad)
+    assert_close(np_of(y), load(name, "expected_forward.bin", (1, 4, oh, oh)), F32_TOL)
+
+
+def test_batchnorm_golden_and_fold():
+    x = load("batchnorm", "x.bin", (64, 32))
+    args = [to_gpu(load("batchnorm", f)) for f in ("weight.bin", "bias.bin", "running_mean.bin", "running_var.bin")]
+    y = ops().batch_norm_inference(to_gpu(x), *args, eps=1e-5)
+    assert_close(np_of(y), load("batchnorm", "expected_forward_inference.bin", (64, 32)), F32_TOL)
+    r = rng(1)
+    g, be, mu, var, b = (r.uniform(0.5, 1.5, 64), r.normal(0, .1, 64), r.normal(0, .1, 64), r.uniform(.5, 1.5, 64),
+                         r.normal(0, .1, 64))
+    sc, sh = ops().bn_fold(*(to_gpu(a) for a in (g, be, mu, var)), eps=1e-5, bias=to_gpu(b))
+    rsc, rsh = oracle.bn_fold(g, be, mu, var, 1e-5, b)
+    assert_close(np_of(sc), rsc, 1e-6)
+    assert_close(np_of(sh), rsh, 1e-6)
+
+
+def _conv_case(B, C, Co, H, W, k, stride, pad, act, dtype, seed, with_bn=True):
+    r = rng(seed)
+    x = r.standard_normal((B, C, H, W)).astype(np.float32)
+    w = (r.standard_normal((Co, C, k, k)) * np.sqrt(2.0 / (C * k * k))).astype(np.float32)
+    bias = r.normal(0, 0.1, Co).astype(np.float32)
+    if dtype == torch.bfloat16:
+        x, w = bf16_round(x), bf16_round(w)
+    sc = sh = None
+    if with_bn:
+        sc, sh = oracle.bn_fold(r.uniform(0.5, 1.5, Co), r.normal(0, .1, Co), r.normal(0, .1, Co),
+                                r.uniform(0.5, 1.5, Co), 1e-5, bias)
+    ref = oracle.conv2d(x, w, bias=bias, scale=sc, shift=sh, stride=stride, pad=pad, act=act)
+    y = ops().conv2d(to_gpu(x, dtype), to_gpu(w, dtype), bias=to_gpu(bias),
+                     scale=None if sc is None else to_gpu(sc), shift=None if sh is None else to_gpu(sh),
+                     stride=stride, pad=pad, act=act)
+    return np_of(y), ref
+
+
+@pytest.mark.parametrize("B,C,Co,H,W,act", [(2, 64, 64, 24, 24, "relu"), (1, 3, 40, 20, 16, "silu"),
+                                            (2, 128, 96, 16, 32, None), (32, 64, 64, 56, 56, "relu")])
+def test_conv2d_bf16_tensor_cores(B, C, Co, H, W, act):
+    got, ref = _conv_case(B, C, Co, H, W, 3, 1, 1, act, torch.bfloat16, seed=B + C + Co)
+    assert_close(got, ref, BF16_TOL)
+
+
+def test_conv2d_bf16_cuda_core_shapes():
+    got, ref = _conv_case(2, 16, 24, 17, 19, 3, 2, 1, "relu", torch.bfloat16, seed=5)   # stride 2, OW % 8 != 0
+    assert_close(got, ref, BF16_TOL)
+
+
+@pytest.mark.parametrize("B,C,Co,H,W,k,s,p", [(1, 64, 64, 56, 56, 3, 1, 1), (2, 5, 7, 9, 11, 3, 2, 0), (1, 8, 16, 10, 10, 1, 1, 0)])
+def test_conv2d_f32(B, C, Co, H, W, k, s, p):
+    got, ref = _conv_case(B, C, Co, H, W, k, s, p, "relu", torch.float32, seed=k + s + C)
+    assert_close(got, ref, F32_TOL)
+
+
+def test_conv2d_plain_bias_no_bn():
+    got, ref = _conv_case(1, 64, 64, 16, 16, 3, 1, 1, None, torch.bfloat16, seed=11, with_bn=False)
+    assert_close(got, ref, BF16_TOL)
