@@ -43,6 +43,21 @@ __global__ void init_normal_kernel(__nv_bfloat16* __restrict__ dst, int64_t n, u
     }
 }
 
+// N(0, 1) keys / values for positions [0, len) of `blocks` cache rows blocks
+// of max_seq * hd elements each (decode-only workloads).
+__global__ void fill_cache_normal_kernel(__nv_bfloat16* __restrict__ base, int blocks, int len, int hd, int max_seq,
+                                         uint64_t seed) {
+    const int64_t per = (int64_t)len * hd, total = per * blocks;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t blk = i / per, off = i % per;
+        uint64_t h1 = splitmix64(seed ^ ((uint64_t)i * 0xD1B54A32D192ED03ull));
+        uint64_t h2 = splitmix64(h1 ^ 0x8CB92BA72F3D8DD7ull);
+        float u1 = ((float)(h1 >> 40) + 0.5f) * (1.0f / 16777216.0f);
+        float u2 = (float)(h2 >> 40) * (1.0f / 16777216.0f);
+        base[blk * (int64_t)max_seq * hd + off] = __float2bfloat16_rn(sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2));
+    }
+}
+
 __global__ void fill_bf16_kernel(__nv_bfloat16* dst, int64_t n, float v) {
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
         dst[i] = __float2bfloat16_rn(v);
@@ -726,12 +741,9 @@ int tb_decoder_fill_kv_random(tb_decoder* d, int B, int len, uint64_t seed, cons
     for (int l = 0; l < c.n_layers; l++) {
         for (int which = 0; which < 2; which++) {
             bf16* base = (which ? d->vcache : d->kcache) + (int64_t)l * d->cache_layer_elems;
-            for (int bh = 0; bh < B * c.n_kv_heads; bh++) {
-                int64_t n = (int64_t)len * c.head_dim;
-                init_normal_kernel<<<grid_for(ctx, n), 256, 0, ctx->stream>>>(
-                    base + (int64_t)bh * c.max_seq * c.head_dim, n,
-                    seed * 0x100000001B3ull + ((uint64_t)l << 32) + ((uint64_t)which << 31) + bh, 1.0f);
-            }
+            const int blocks = B * c.n_kv_heads;
+            fill_cache_normal_kernel<<<grid_for(ctx, (int64_t)blocks * len * c.head_dim), 256, 0, ctx->stream>>>(
+                base, blocks, len, c.head_dim, c.max_seq, seed * 0x100000001B3ull + ((uint64_t)l << 8) + which);
         }
     }
     TB_CUDA_TRY(ctx, cudaMemcpyAsync(d->cur_ids, ids, (size_t)B * sizeof(int32_t), cudaMemcpyDeviceToDevice, ctx->stream));
