@@ -259,6 +259,21 @@ TB_API int tb_decoder_fill_kv_random(tb_decoder* dec, int B, int len, uint64_t s
 /* Tokens currently in the KV cache per sequence. */
 TB_API int tb_decoder_seq_len(tb_decoder* dec, int* len);
 
+/* ---------------------------------------------------------- multi-GPU --- */
+/* Batch-sharded runs: one process per GPU, each on its own shard; the only
+ * exchange is an all-gather of the final outputs (the reference has no
+ * distributed code at all).  NCCL is loaded at run time (libnccl.so.2).  The
+ * communicator is non-blocking and every host-side wait on it is bounded by
+ * timeout_ms, after which it is aborted and TB_ERR_NCCL returned. */
+TB_API int tb_comm_unique_id_bytes(void);
+/* Rank 0 creates the id and shares its bytes with the other ranks. */
+TB_API int tb_comm_get_unique_id(void* out);
+TB_API int tb_comm_init(tb_ctx* ctx, const void* unique_id, int nranks, int rank, int timeout_ms);
+/* recv[r * bytes_per_rank ...] = rank r's send buffer, on ctx's stream. */
+TB_API int tb_comm_allgather(tb_ctx* ctx, const void* send, void* recv, size_t bytes_per_rank);
+TB_API int tb_comm_abort(tb_ctx* ctx);
+TB_API int tb_comm_destroy(tb_ctx* ctx);
+
 #ifdef __cplusplus
 }
 #endif
