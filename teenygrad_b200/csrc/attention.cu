@@ -11,9 +11,8 @@
 //    The same online-softmax recurrence as flash_attention2_forward
 //    (nn/attention/flash_attn2.rs:98-140), over 128-key tiles instead of one
 //    key at a time, plus the causal mask and GQA head mapping.
-//  * attn_decode_kernel: decode against a KV cache (few queries, long
-//    context).  Split over the context; the last CTA of a (batch, kv-head)
-//    group merges the partial (max, sum, output) triples.
+//  * attn_decode_tc_kernel: decode against a KV cache (few queries, long
+//    context) on tcgen05, split over the context, splits merged over DSMEM.
 //  * attn_f32_kernel: exact f32 path (fixtures, fp32 configurations).
 #include <math.h>
 
@@ -274,23 +273,28 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
 }
 
 // -------------------------------------------------------------- decode -----
-// Decode attention against the KV cache: a few queries, a long context.
-// Grid (B * Hkv, DEC_CTAS) in clusters of (1, DEC_CTAS, 1), 4 warps per CTA:
-// the 4 * DEC_CTAS warps of a cluster split the context of one (batch, kv
-// head) group into `chunk`-key ranges (a multiple of 32).  A warp streams its
-// range in 32-key slabs: one lane issues 1-D bulk async copies (TMA engine)
-// of the slab's contiguous K and V rows into the warp's double-buffered
-// shared memory, so the next slab is in flight while this one is processed.
-// Lane j scores key j against the G = Hq / Hkv queries (broadcast from shared
-// memory; the K row is read in a lane-rotated chunk order, conflict-free),
-// the slab's max / exp / sum run on warp shuffles (online softmax), and the
-// P V product gives each lane D/32 output dims of every head.  Partials
-// (max, sum, o) stay in shared memory; after a cluster barrier CTA rank r
-// merges output dims [r*D/DEC_CTAS, ...) of every head over DSMEM, in fixed
-// order (deterministic).  D = 64 or 128, G in {1, 2, 4, 8}.
-constexpr int DEC_CTAS = 2;                 // cluster size (8 warp-splits per group: one wave at 2 CTAs per SM)
-constexpr int DEC_WARPS = 4;                // warps per CTA
-constexpr int DEC_SPLITS = DEC_CTAS * DEC_WARPS;
+// Decode attention against the KV cache on tcgen05 (few queries, long
+// context).  One CTA per (batch, kv head, split); the G = Hq / Hkv query heads
+// that share the kv head are padded to 16 rows.  Per 128-key tile:
+//   S^T = K_tile Q^T      (M = 128 keys, N = 16 query rows, K = D)  -> TMEM
+//   softmax               (thread t of warps 2-5 <-> key t: one TMEM lane)
+//   O  += P V_tile        (M = 128 rows, of which the first G are the queries,
+//                          N = D, K = 128 keys; P in a zero-padded smem tile,
+//                          V as the MN-major operand)               -> TMEM
+// Warp 0 streams K/V tiles with TMA (2-stage ring), warp 1 issues the MMAs.
+// The online softmax keeps per-query (max, sum) in registers of every
+// softmax thread (tile reductions over shuffles + shared memory).  Splits of
+// one group form a cluster and merge (max, sum, o) over DSMEM in fixed order.
+template <int D>
+struct DecTcCfg {
+    static constexpr int TILE = 128 * D * 2;            // K or V tile bytes
+    static constexpr int P_BYTES = 128 * 128 * 2;       // [128 rows][128 keys] bf16, rows >= G zero
+    static constexpr int Q_BYTES = 16 * D * 2;          // [16 rows][D] bf16, rows >= G zero
+    static constexpr int PART = 8 * (D + 2) * 4;        // merge partial (max, sum, o) per query
+    static constexpr int SMEM = 4 * TILE + P_BYTES + (Q_BYTES < 1024 ? 1024 : Q_BYTES) + PART + 1024 + 512;
+    static constexpr int O_COL = 32;                    // TMEM: S^T buffers at 0 and 16, O at 32
+    static constexpr int TMEM_COLS = (32 + D) <= 128 ? 128 : 256;
+};
 
 __device__ __forceinline__ void dec_cluster_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
@@ -304,214 +308,304 @@ __device__ __forceinline__ float dec_ld_dsmem(uint32_t local_addr, uint32_t rank
     return v;
 }
 
-__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-                 "l"(src), "r"(bytes), "r"(bar)
-                 : "memory");
+__device__ __forceinline__ void softmax_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// Barrier over the 128 softmax threads that also ANDs `v` across them: every
+// softmax warp takes the same branch after a bounded wait, so none is left
+// waiting at a named barrier that the others skipped.
+__device__ __forceinline__ bool softmax_bar_and(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred q, 1, 128, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)v)
+        : "memory");
+    return r != 0;
 }
 
 template <int D>
-struct DecSmem {
-    static constexpr int SLAB = 32 * D * 2;                        // bytes of K (or V) per slab
-    static constexpr int KV = DEC_WARPS * 2 * 2 * SLAB;            // [warp][buf][K|V]
-    static constexpr int BYTES = KV + 8 * D * 4 /*sq*/ + DEC_WARPS * 32 * 8 * 4 /*sp*/ +
-                                 DEC_WARPS * 8 * (D + 2) * 4 /*partials*/ + DEC_WARPS * 2 * 8 /*bars*/ + 128;
-};
-
-template <int D, int G>
-__global__ void __launch_bounds__(128)
-attn_decode_kernel(DecodeArgs a, int* err) {
-    constexpr int DPL = D / 32;                       // output dims per lane
-    using SM = DecSmem<D>;
-    extern __shared__ __align__(128) uint8_t dsm[];
-    uint8_t* kv = dsm;                                              // [warp][buf][K|V][32][D] bf16
-    float (*sq)[D] = reinterpret_cast<float (*)[D]>(dsm + SM::KV);
-    float (*sp)[32][8] = reinterpret_cast<float (*)[32][8]>(dsm + SM::KV + 8 * D * 4);
-    float* sparts = reinterpret_cast<float*>(dsm + SM::KV + 8 * D * 4 + DEC_WARPS * 32 * 8 * 4);   // [warp][8][D+2]
-    uint64_t* bars = reinterpret_cast<uint64_t*>(dsm + SM::KV + 8 * D * 4 + DEC_WARPS * 32 * 8 * 4 +
-                                                 DEC_WARPS * 8 * (D + 2) * 4);
+__global__ void __launch_bounds__(192, 1)
+attn_decode_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                      DecodeArgs a, int* err) {
+    using C = DecTcCfg<D>;
+    constexpr int DB = D / 64;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sK = smem;                        // [2 stages]
+    uint8_t* sV = sK + 2 * C::TILE;            // [2 stages]
+    uint8_t* sP = sV + 2 * C::TILE;
+    uint8_t* sQ = sP + C::P_BYTES;
+    float* spart = reinterpret_cast<float*>(sQ + (C::Q_BYTES < 1024 ? 1024 : C::Q_BYTES));   // [8][D+2]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(spart) + C::PART);
+    const uint32_t k_full0 = smem_u32(bars + 0), v_full0 = smem_u32(bars + 2), kv_empty0 = smem_u32(bars + 4);
+    const uint32_t s_full0 = smem_u32(bars + 6), p_full = smem_u32(bars + 8), o_done = smem_u32(bars + 9);
+    const uint32_t q_full = smem_u32(bars + 10);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+    float* sred = reinterpret_cast<float*>(bars + 12);      // [2][4 warps][8 queries]
 
     pdl_trigger();
-    const int bg = blockIdx.x, cr = blockIdx.y;
+    const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+    const int G = a.Hq / a.Hkv;
+    const int bg = blockIdx.x, split = blockIdx.y, nsp = gridDim.y;
     const int b = bg / a.Hkv, g = bg % a.Hkv;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const uint32_t bar0 = smem_u32(&bars[warp * 2]), bar1 = smem_u32(&bars[warp * 2 + 1]);
-    if (lane == 0) {
-        mbar_init(bar0, 1);
-        mbar_init(bar1, 1);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < 2; s++) {
+            mbar_init(k_full0 + 8 * s, 1);
+            mbar_init(v_full0 + 8 * s, 1);
+            mbar_init(kv_empty0 + 8 * s, 1);
+            mbar_init(s_full0 + 8 * s, 1);
+        }
+        mbar_init(p_full, 128);
+        mbar_init(o_done, 1);
+        mbar_init(q_full, 128);
         fence_barrier_init();
     }
-    __syncwarp();
+    if (warp == 1) tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
     pdl_wait();
     const int L = a.len_ptr ? (*a.len_ptr + a.len) : a.len;
-    const int split = cr * DEC_WARPS + warp;
     const int kbeg = split * a.chunk;
     const int kend = min(L, kbeg + a.chunk);
-    const int nslab = kend > kbeg ? (kend - kbeg + 31) / 32 : 0;
-    const __nv_bfloat16* kbase = a.k + (int64_t)b * a.kv_sb + (int64_t)g * a.kv_sh;
-    const __nv_bfloat16* vbase = a.v + (int64_t)b * a.kv_sb + (int64_t)g * a.kv_sh;
-    uint8_t* wkv = kv + warp * 2 * 2 * SM::SLAB;
+    const int n_tiles = kend > kbeg ? (kend - kbeg + 127) / 128 : 0;
+    const int64_t row0 = ((int64_t)b * a.Hkv + g) * a.kv_rows;   // first cache row of this group
 
-    auto issue = [&](int i) {   // lane 0 only
-        const int k0 = kbeg + 32 * i;
-        const int nk = min(32, kend - k0);
-        const uint32_t bytes = (uint32_t)(nk * D * 2);
-        const uint32_t bar = (i & 1) ? bar1 : bar0;
-        uint8_t* buf = wkv + (i & 1) * 2 * SM::SLAB;
-        mbar_expect_tx(bar, 2 * bytes);
-        bulk_g2s(smem_u32(buf), kbase + (int64_t)k0 * a.kv_ss, bytes, bar);
-        bulk_g2s(smem_u32(buf + SM::SLAB), vbase + (int64_t)k0 * a.kv_ss, bytes, bar);
-    };
-    if (lane == 0) {
-        if (nslab > 0) issue(0);
-        if (nslab > 1) issue(1);
+    if (warp == 0) {
+        if (lane == 0 && n_tiles > 0) {
+            tma_prefetch_desc(&tmK);
+            tma_prefetch_desc(&tmV);
+            int issued = 0;
+            for (int j = 0; j < n_tiles; j++) {
+                const int st = j & 1;
+                if (j >= 2 && !mbar_wait(kv_empty0 + 8 * st, ((j >> 1) - 1) & 1, err, DEV_ERR_TIMEOUT_EMPTY)) break;
+                const int r = (int)(row0 + kbeg + 128 * j);
+                mbar_expect_tx(k_full0 + 8 * st, C::TILE);
+                for (int d = 0; d < DB; d++) tma_load_2d(smem_u32(sK + st * C::TILE + d * 16384), &tmK, k_full0 + 8 * st, 64 * d, r);
+                mbar_expect_tx(v_full0 + 8 * st, C::TILE);
+                for (int d = 0; d < DB; d++) tma_load_2d(smem_u32(sV + st * C::TILE + d * 16384), &tmV, v_full0 + 8 * st, 64 * d, r);
+                issued = j + 1;
+            }
+            for (int j = (issued > 2 ? issued - 2 : 0); j < issued; j++) {
+                mbar_wait(k_full0 + 8 * (j & 1), (j >> 1) & 1, err, DEV_ERR_TIMEOUT_FULL);
+                mbar_wait(v_full0 + 8 * (j & 1), (j >> 1) & 1, err, DEV_ERR_TIMEOUT_FULL);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && n_tiles > 0) {
+            constexpr uint32_t idesc_s = idesc_bf16_f32(128, 16, false, false);
+            constexpr uint32_t idesc_o = idesc_bf16_f32(128, D, false, true);
+            const uint32_t q_base = smem_u32(sQ), p_base = smem_u32(sP);
+            bool ok = mbar_wait(q_full, 0, err, DEV_ERR_TIMEOUT_MISC);
+            for (int j = 0; ok && j <= n_tiles; j++) {
+                if (j < n_tiles) {
+                    const int st = j & 1;
+                    if (!mbar_wait(k_full0 + 8 * st, (j >> 1) & 1, err, DEV_ERR_TIMEOUT_FULL)) break;
+                    tc_fence_after();
+                    const uint32_t k_base = smem_u32(sK + st * C::TILE);
+#pragma unroll
+                    for (int kk = 0; kk < D / 16; kk++) {
+                        const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+                        const uint32_t qoff = (kk >> 2) * 2048 + (kk & 3) * 32;
+                        umma_f16_ss(tmem + st * 16, sdesc_sw128(k_base + off, 16, 1024), sdesc_sw128(q_base + qoff, 16, 1024),
+                                    idesc_s, kk != 0);
+                    }
+                    umma_commit(s_full0 + 8 * st);
+                }
+                if (j > 0) {
+                    const int jp = j - 1, st = jp & 1;
+                    if (!mbar_wait(p_full, jp & 1, err, DEV_ERR_TIMEOUT_MISC)) break;
+                    if (!mbar_wait(v_full0 + 8 * st, (jp >> 1) & 1, err, DEV_ERR_TIMEOUT_FULL)) break;
+                    tc_fence_after();
+                    const uint32_t v_base = smem_u32(sV + st * C::TILE);
+#pragma unroll
+                    for (int kk = 0; kk < 8; kk++) {
+                        const uint64_t ad = sdesc_sw128(p_base + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
+                        const uint64_t bd = sdesc_sw128(v_base + kk * 16 * 128, 16384, 1024);
+                        umma_f16_ss(tmem + C::O_COL, ad, bd, idesc_o, (jp | kk) != 0);
+                    }
+                    umma_commit(kv_empty0 + 8 * st);
+                    umma_commit(o_done);
+                }
+            }
+        }
+    } else {
+        // ---------------- softmax warps 2..5: thread <-> key row of the tile
+        const int sw = warp - 2;                          // 0..3
+        const int quarter = warp & 3;                     // TMEM lane quarter of this warp
+        const int kr = quarter * 32 + lane;               // key row within the tile
+        const int tid = threadIdx.x - 64;                 // 0..127
+        const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
+        // Q -> smem [16 rows][D], 128-B swizzle, rows >= G zero; P tile -> zero
+        for (int i = tid; i < 16 * (D / 8); i += 128) {
+            const int r = i / (D / 8), c = i % (D / 8);   // row, 16-byte chunk
+            uint4 v = make_uint4(0, 0, 0, 0);
+            if (r < G) v = *reinterpret_cast<const uint4*>(a.q + (int64_t)b * a.q_sb + (int64_t)(g * G + r) * a.q_sh + c * 8);
+            const int cc = c & 7, atom = c >> 3;
+            *reinterpret_cast<uint4*>(sQ + atom * 2048 + r * 128 + ((cc ^ (r & 7)) << 4)) = v;
+        }
+        for (int i = tid; i < C::P_BYTES / 16; i += 128) reinterpret_cast<uint4*>(sP)[i] = make_uint4(0, 0, 0, 0);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_arrive(q_full);
+
+        float m_run[8], l_run[8];
+#pragma unroll
+        for (int q = 0; q < 8; q++) {
+            m_run[q] = -INFINITY;
+            l_run[q] = 0.f;
+        }
+        bool ok = true;
+        for (int j = 0; j < n_tiles; j++) {
+            const int sb = j & 1;
+            ok = softmax_bar_and(mbar_wait(s_full0 + 8 * sb, (j >> 1) & 1, err, DEV_ERR_TIMEOUT_MISC));
+            if (!ok) break;
+            tc_fence_after();
+            float s[16];
+            tmem_ld16(t_lane + sb * 16, s);
+            tmem_wait_ld();
+            const bool valid = kbeg + 128 * j + kr < kend;
+            // tile max per query
+#pragma unroll
+            for (int q = 0; q < 8; q++) {
+                s[q] = (valid && q < G) ? s[q] * a.scale_log2 : -INFINITY;
+                float m = s[q];
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+                if (lane == 0) sred[sw * 8 + q] = m;
+            }
+            softmax_bar();
+            float alpha[8], p[8];
+#pragma unroll
+            for (int q = 0; q < 8; q++) {
+                const float tm = fmaxf(fmaxf(sred[q], sred[8 + q]), fmaxf(sred[16 + q], sred[24 + q]));
+                const float m_new = fmaxf(m_run[q], tm);
+                const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+                alpha[q] = ex2(m_run[q] - m_use);
+                p[q] = ex2(s[q] - m_use);
+                m_run[q] = m_new;
+                float sum = p[q];
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+                if (lane == 0) sred[32 + sw * 8 + q] = sum;
+            }
+            softmax_bar();
+#pragma unroll
+            for (int q = 0; q < 8; q++)
+                l_run[q] = l_run[q] * alpha[q] + (sred[32 + q] + sred[40 + q] + sred[48 + q] + sred[56 + q]);
+            if (j > 0) {
+                ok = softmax_bar_and(mbar_wait(o_done, (j - 1) & 1, err, DEV_ERR_TIMEOUT_MISC));
+                if (!ok) break;
+                tc_fence_after();
+                // rescale the O rows (queries 0..G-1 = TMEM lanes 0..G-1, lane quarter 0: warp 4)
+                if (quarter == 0) {
+                    float my_alpha = 1.f;
+#pragma unroll
+                    for (int q = 0; q < 8; q++)
+                        if (lane == q && q < G) my_alpha = alpha[q];
+                    if (__any_sync(0xffffffffu, my_alpha != 1.0f)) {
+#pragma unroll 1
+                        for (int c = 0; c < D; c += 16) {
+                            float o[16];
+                            tmem_ld16(t_lane + C::O_COL + c, o);
+                            tmem_wait_ld();
+#pragma unroll
+                            for (int i = 0; i < 16; i++) o[i] *= my_alpha;
+                            tmem_st16(t_lane + C::O_COL + c, o);
+                        }
+                        tmem_wait_st();
+                    }
+                }
+            }
+            // P[q][key] (bf16) into the swizzled K-major tile: row q, key column kr
+            {
+                const int atom = kr >> 6, kc = kr & 63;
+#pragma unroll
+                for (int q = 0; q < 8; q++) {
+                    if (q < G) {
+                        uint8_t* rowp = sP + atom * 16384 + q * 128;
+                        const int chunk = (kc >> 3) ^ (q & 7);
+                        *reinterpret_cast<__nv_bfloat16*>(rowp + chunk * 16 + (kc & 7) * 2) = __float2bfloat16_rn(p[q]);
+                    }
+                }
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            tc_fence_before();
+            mbar_arrive(p_full);
+        }
+        if (ok && n_tiles > 0) ok = __all_sync(0xffffffffu, mbar_wait(o_done, (n_tiles - 1) & 1, err, DEV_ERR_TIMEOUT_ACC));
+        // partial (max, sum, unnormalised o) of this split: warp 4 (TMEM quarter 0), lanes < G
+        if (quarter == 0) {
+            tc_fence_after();
+            float my_m = -INFINITY, my_l = 0.f;
+#pragma unroll
+            for (int q = 0; q < 8; q++)
+                if (lane == q) {
+                    my_m = m_run[q];
+                    my_l = l_run[q];
+                }
+#pragma unroll 1
+            for (int c = 0; c < D; c += 16) {
+                float o[16];
+                if (n_tiles > 0 && ok) {
+                    tmem_ld16(t_lane + C::O_COL + c, o);
+                    tmem_wait_ld();
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 16; i++) o[i] = 0.f;
+                }
+                if (lane < G)
+#pragma unroll
+                    for (int i = 0; i < 16; i++) spart[lane * (D + 2) + c + i] = o[i];
+            }
+            if (lane < G) {
+                spart[lane * (D + 2) + D] = (n_tiles > 0 && ok) ? my_m : -INFINITY;
+                spart[lane * (D + 2) + D + 1] = (n_tiles > 0 && ok) ? my_l : 0.f;
+            }
+        }
     }
-    for (int i = tid; i < 8 * D; i += 128) {
-        const int gg = i / D, d = i % D;
-        sq[gg][d] = (gg < G) ? __bfloat162float(a.q[(int64_t)b * a.q_sb + (int64_t)(g * G + gg) * a.q_sh + d]) * a.scale_log2
-                             : 0.f;
-    }
+    __syncwarp();
+    tc_fence_before();
     __syncthreads();
-
-    float m_run[G], l_run[G], o[G][DPL];
+    if (warp == 1) tmem_dealloc(tmem, C::TMEM_COLS);
+    // ---- merge the splits (cluster over blockIdx.y) and write O / LSE
+    if (nsp > 1) dec_cluster_sync();
+    const int DS = D / nsp;                               // dims merged by this CTA per query
+    for (int i = threadIdx.x; i < G * DS; i += 192) {
+        const int q = i / DS, d = split * DS + i % DS;
+        float M = -INFINITY, l = 0.f, o = 0.f;
+        if (nsp == 1) {
+            M = spart[q * (D + 2) + D];
+            l = spart[q * (D + 2) + D + 1];
+            o = spart[q * (D + 2) + d];
+        } else {
+            float mv[8], lv[8], ov[8];
+            const uint32_t base = smem_u32(spart + q * (D + 2));
 #pragma unroll
-    for (int gg = 0; gg < G; gg++) {
-        m_run[gg] = -INFINITY;
-        l_run[gg] = 0.f;
-#pragma unroll
-        for (int j = 0; j < DPL; j++) o[gg][j] = 0.f;
-    }
-    bool ok = true;
-    for (int i = 0; i < nslab; i++) {
-        const int k0 = kbeg + 32 * i;
-        const int nk = min(32, kend - k0);
-        const bool mine = lane < nk;
-        ok = __all_sync(0xffffffffu, mbar_wait((i & 1) ? bar1 : bar0, (i >> 1) & 1, err, DEV_ERR_TIMEOUT_FULL));
-        if (!ok) break;
-        const __nv_bfloat16* sk = reinterpret_cast<const __nv_bfloat16*>(wkv + (i & 1) * 2 * SM::SLAB);
-        const __nv_bfloat16* sv = sk + 32 * D;
-        // ---- scores of this lane's key (chunks visited in lane-rotated order)
-        float s[G];
-#pragma unroll
-        for (int gg = 0; gg < G; gg++) s[gg] = 0.f;
-        if (mine) {
-            const uint4* kr = reinterpret_cast<const uint4*>(sk + lane * D);
-#pragma unroll
-            for (int cc = 0; cc < D / 8; cc++) {
-                const int c = (cc + lane) & (D / 8 - 1);
-                const uint4 kw = kr[c];
-                const uint32_t w[4] = {kw.x, kw.y, kw.z, kw.w};
-                float kf[8];
-#pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    kf[2 * j] = bf16_lo(w[j]);
-                    kf[2 * j + 1] = bf16_hi(w[j]);
+            for (int r = 0; r < 8; r++) {
+                if (r < nsp) {
+                    mv[r] = dec_ld_dsmem(base + D * 4, r);
+                    lv[r] = dec_ld_dsmem(base + (D + 1) * 4, r);
+                    ov[r] = dec_ld_dsmem(base + d * 4, r);
                 }
+            }
 #pragma unroll
-                for (int gg = 0; gg < G; gg++) {
-                    const float4 q0 = *reinterpret_cast<const float4*>(&sq[gg][c * 8]);
-                    const float4 q1 = *reinterpret_cast<const float4*>(&sq[gg][c * 8 + 4]);
-                    s[gg] = fmaf(q0.x, kf[0], s[gg]);
-                    s[gg] = fmaf(q0.y, kf[1], s[gg]);
-                    s[gg] = fmaf(q0.z, kf[2], s[gg]);
-                    s[gg] = fmaf(q0.w, kf[3], s[gg]);
-                    s[gg] = fmaf(q1.x, kf[4], s[gg]);
-                    s[gg] = fmaf(q1.y, kf[5], s[gg]);
-                    s[gg] = fmaf(q1.z, kf[6], s[gg]);
-                    s[gg] = fmaf(q1.w, kf[7], s[gg]);
+            for (int r = 0; r < 8; r++)
+                if (r < nsp) M = fmaxf(M, mv[r]);
+#pragma unroll
+            for (int r = 0; r < 8; r++) {
+                if (r < nsp) {
+                    const float w = (mv[r] == -INFINITY) ? 0.f : ex2(mv[r] - M);
+                    l += lv[r] * w;
+                    o += ov[r] * w;
                 }
             }
         }
-        // ---- online softmax per head over the slab
-#pragma unroll
-        for (int gg = 0; gg < G; gg++) {
-            const float sv_ = mine ? s[gg] : -INFINITY;
-            float mx = sv_;
-#pragma unroll
-            for (int of = 16; of > 0; of >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, of));
-            const float m_new = fmaxf(m_run[gg], mx);
-            const float alpha = ex2(m_run[gg] - m_new);
-            const float p = mine ? ex2(sv_ - m_new) : 0.f;
-            float sum = p;
-#pragma unroll
-            for (int of = 16; of > 0; of >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, of);
-            l_run[gg] = l_run[gg] * alpha + sum;
-            m_run[gg] = m_new;
-#pragma unroll
-            for (int j = 0; j < DPL; j++) o[gg][j] *= alpha;
-            sp[warp][lane][gg] = p;
-        }
-        __syncwarp();
-        // ---- P V for this lane's dims
-        for (int j = 0; j < nk; j++) {
-            float vf[DPL];
-            const __nv_bfloat16* vr = sv + j * D + lane * DPL;
-            if (DPL == 2) {
-                const uint32_t w = *reinterpret_cast<const uint32_t*>(vr);
-                vf[0] = bf16_lo(w);
-                vf[1] = bf16_hi(w);
-            } else {
-                const uint2 w = *reinterpret_cast<const uint2*>(vr);
-                vf[0] = bf16_lo(w.x);
-                vf[1] = bf16_hi(w.x);
-                vf[DPL - 2] = bf16_lo(w.y);
-                vf[DPL - 1] = bf16_hi(w.y);
-            }
-            const float4 p0 = *reinterpret_cast<const float4*>(&sp[warp][j][0]);
-            const float4 p1 = *reinterpret_cast<const float4*>(&sp[warp][j][4]);
-            const float pj[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
-#pragma unroll
-            for (int gg = 0; gg < G; gg++)
-#pragma unroll
-                for (int q = 0; q < DPL; q++) o[gg][q] = fmaf(pj[gg], vf[q], o[gg][q]);
-        }
-        __syncwarp();
-        if (lane == 0 && i + 2 < nslab) issue(i + 2);   // this buffer has been read by every lane
+        a.o[(int64_t)b * a.o_sb + (int64_t)(g * G + q) * a.o_sh + d] = __float2bfloat16_rn(l > 0.f ? o / l : 0.f);
+        if (d == 0 && a.lse) a.lse[(int64_t)b * a.Hq + g * G + q] = l > 0.f ? (M + log2f(l)) * kLn2 : -INFINITY;
     }
-
-    // ---- partial of this warp -> shared memory ([warp][head][D + 2])
-    float* wp = sparts + warp * 8 * (D + 2);
-#pragma unroll
-    for (int gg = 0; gg < G; gg++) {
-#pragma unroll
-        for (int q = 0; q < DPL; q++) wp[gg * (D + 2) + lane * DPL + q] = ok ? o[gg][q] : 0.f;
-        if (lane == 0) {
-            wp[gg * (D + 2) + D] = ok ? m_run[gg] : -INFINITY;
-            wp[gg * (D + 2) + D + 1] = ok ? l_run[gg] : 0.f;
-        }
-    }
-    __syncthreads();
-    dec_cluster_sync();
-    {
-        constexpr int DS = D / DEC_CTAS;              // dims merged by this CTA per head
-        const int gg = tid / DS, d = cr * DS + tid % DS;
-        if (gg < G) {
-            float mv[DEC_SPLITS], lv[DEC_SPLITS], ov[DEC_SPLITS];
-#pragma unroll
-            for (int r = 0; r < DEC_CTAS; r++) {
-#pragma unroll
-                for (int w = 0; w < DEC_WARPS; w++) {
-                    const float* pw = sparts + (w * 8 + gg) * (D + 2);
-                    mv[r * DEC_WARPS + w] = dec_ld_dsmem(smem_u32(pw + D), r);
-                    lv[r * DEC_WARPS + w] = dec_ld_dsmem(smem_u32(pw + D + 1), r);
-                    ov[r * DEC_WARPS + w] = dec_ld_dsmem(smem_u32(pw + d), r);
-                }
-            }
-            float M = -INFINITY;
-#pragma unroll
-            for (int i = 0; i < DEC_SPLITS; i++) M = fmaxf(M, mv[i]);
-            float l = 0.f, acc = 0.f;
-#pragma unroll
-            for (int i = 0; i < DEC_SPLITS; i++) {
-                const float w = (mv[i] == -INFINITY) ? 0.f : ex2(mv[i] - M);
-                l += lv[i] * w;
-                acc += ov[i] * w;
-            }
-            a.o[(int64_t)b * a.o_sb + (int64_t)(g * G + gg) * a.o_sh + d] = __float2bfloat16_rn(l > 0.f ? acc / l : 0.f);
-            if (d == 0 && a.lse) a.lse[(int64_t)b * a.Hq + g * G + gg] = l > 0.f ? (M + log2f(l)) * kLn2 : -INFINITY;
-        }
-    }
-    dec_cluster_sync();   // peers may still be reading this CTA's partials
+    if (nsp > 1) dec_cluster_sync();   // peers may still be reading this CTA's partial
 }
 
 // ---------------------------------------------------------------- f32 ------
@@ -593,24 +687,32 @@ int attn_tc_launch(tb_ctx* ctx, const AttnTensors& t, int B, int Hq, int Hkv, in
     return check_launch(ctx, "attn_tc");
 }
 
-// Keys per warp: the context split DEC_SPLITS ways, rounded up to a multiple of 32.
-static int decode_chunk(int max_len) {
-    int c = (max_len + DEC_SPLITS - 1) / DEC_SPLITS;
-    c = (c + 31) / 32 * 32;
-    return c < 32 ? 32 : c;
-}
-
+// Splits per (batch, kv head) group: the largest of 8, 4, 2, 1 that keeps the
+// grid within the resident CTA slots and leaves every split >= 1 key tile.
 int attn_decode_launch(tb_ctx* ctx, DecodeArgs a, int B, int D, int max_len) {
-    a.chunk = decode_chunk(max_len);
+    const int G = a.Hq / a.Hkv;
+    if (a.Hq % a.Hkv != 0 || G < 1 || G > 8) return set_error(ctx, TB_ERR_SHAPE, "attn_decode: group size %d", G);
+    if (a.kv_ss != D || a.kv_sh != (int64_t)a.kv_rows * D || a.kv_sb != (int64_t)a.Hkv * a.kv_rows * D)
+        return set_error(ctx, TB_ERR_SHAPE, "attn_decode: K/V must be contiguous [B][Hkv][rows][D]");
+    const int groups = B * a.Hkv;
+    const int tiles = (max_len + 127) / 128;
+    const int slots = (D == 64 ? 2 : 1) * ctx->num_sms;
+    int nsp = 8;
+    while (nsp > 1 && (groups * nsp > slots || nsp > tiles)) nsp >>= 1;
+    a.chunk = ((tiles + nsp - 1) / nsp) * 128;
+    CUtensorMap mk, mv;
+    const uint64_t rows = (uint64_t)B * a.Hkv * a.kv_rows;
+    int rc = make_tmap_2d(ctx, &mk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.k, rows, D, D, 64, 128);
+    if (!rc) rc = make_tmap_2d(ctx, &mv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.v, rows, D, D, 64, 128);
+    if (rc) return rc;
     cudaLaunchConfig_t lc = {};
-    lc.gridDim = dim3(B * a.Hkv, DEC_CTAS, 1);
-    lc.blockDim = dim3(128, 1, 1);
-    lc.dynamicSmemBytes = 0;
+    lc.gridDim = dim3(groups, nsp, 1);
+    lc.blockDim = dim3(192, 1, 1);
     lc.stream = ctx->stream;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 1;
-    attr[0].val.clusterDim.y = DEC_CTAS;
+    attr[0].val.clusterDim.y = nsp;
     attr[0].val.clusterDim.z = 1;
     lc.attrs = attr;
     lc.numAttrs = 1;
@@ -619,17 +721,16 @@ int attn_decode_launch(tb_ctx* ctx, DecodeArgs a, int B, int D, int max_len) {
         attr[1].val.programmaticStreamSerializationAllowed = 1;
         lc.numAttrs = 2;
     }
-    const int G = a.Hq / a.Hkv;
-    cudaError_t e = cudaErrorInvalidValue;
-#define TB_DEC_CASE(DD, GG)                                                                                     \
-    if (D == DD && G == GG) {                                                                                   \
-        lc.dynamicSmemBytes = DecSmem<DD>::BYTES;                                                               \
-        cudaFuncSetAttribute(attn_decode_kernel<DD, GG>, cudaFuncAttributeMaxDynamicSharedMemorySize, DecSmem<DD>::BYTES); \
-        e = cudaLaunchKernelEx(&lc, attn_decode_kernel<DD, GG>, a, ctx->d_err);                                 \
+    cudaError_t e;
+    if (D == 64) {
+        lc.dynamicSmemBytes = DecTcCfg<64>::SMEM;
+        TB_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_decode_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, DecTcCfg<64>::SMEM));
+        e = cudaLaunchKernelEx(&lc, attn_decode_tc_kernel<64>, mk, mv, a, ctx->d_err);
+    } else {
+        lc.dynamicSmemBytes = DecTcCfg<128>::SMEM;
+        TB_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_decode_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, DecTcCfg<128>::SMEM));
+        e = cudaLaunchKernelEx(&lc, attn_decode_tc_kernel<128>, mk, mv, a, ctx->d_err);
     }
-    TB_DEC_CASE(64, 1) TB_DEC_CASE(64, 2) TB_DEC_CASE(64, 4) TB_DEC_CASE(64, 8)
-    TB_DEC_CASE(128, 1) TB_DEC_CASE(128, 2) TB_DEC_CASE(128, 4) TB_DEC_CASE(128, 8)
-#undef TB_DEC_CASE
     if (e != cudaSuccess) return set_error(ctx, TB_ERR_CUDA, "attn_decode launch: %s", cudaGetErrorString(e));
     return TB_OK;
 }
@@ -662,14 +763,14 @@ extern "C" int tb_attn_fwd(tb_ctx* ctx, int dtype, const void* q, const void* k,
     t.o = o; t.o_sh = (int64_t)Sq * D; t.o_ss = D; t.o_sb = (int64_t)Hq * Sq * D;
     t.lse = lse;
     const int grp = Hq / Hkv;
-    if (Sq == 1 && (grp == 1 || grp == 2 || grp == 4 || grp == 8)) {
+    if (Sq == 1 && grp <= 8) {
         // single-query decode: split-KV CUDA-core kernel
         DecodeArgs a{};
         a.q = (const __nv_bfloat16*)q; a.q_sb = t.q_sb; a.q_sh = t.q_sh;
         a.k = (const __nv_bfloat16*)k; a.v = (const __nv_bfloat16*)v;
         a.kv_sb = t.kv_sb; a.kv_sh = t.kv_sh; a.kv_ss = t.kv_ss;
         a.o = (__nv_bfloat16*)o; a.o_sb = t.o_sb; a.o_sh = t.o_sh;
-        a.lse = lse; a.Hq = Hq; a.Hkv = Hkv; a.len = Sk; a.len_ptr = nullptr;
+        a.lse = lse; a.Hq = Hq; a.Hkv = Hkv; a.len = Sk; a.len_ptr = nullptr; a.kv_rows = Sk;
         a.scale_log2 = scale * kLog2e;
         return attn_decode_launch(ctx, a, B, D, Sk);
     }

@@ -34,6 +34,7 @@ struct DecodeArgs {
     const __nv_bfloat16* k;
     const __nv_bfloat16* v;
     int64_t kv_sb, kv_sh, kv_ss;
+    int kv_rows;           // positions allocated per (batch, kv head): [B][Hkv][kv_rows][D]
     __nv_bfloat16* o;
     int64_t o_sb, o_sh;
     float* lse;
@@ -41,7 +42,7 @@ struct DecodeArgs {
     int len;               // context length if len_ptr is null, else added to *len_ptr
     const int* len_ptr;    // device-resident context length (CUDA-graph replay)
     float scale_log2;
-    int chunk;             // keys per warp (set by attn_decode_launch)
+    int chunk;             // keys per split (set by attn_decode_launch)
 };
 
 int attn_tc_launch(tb_ctx* ctx, const AttnTensors& t, int B, int Hq, int Hkv, int Sq, int Sk, int D,

@@ -410,6 +410,7 @@ int layer_forward(tb_decoder* d, int l, int B, int S_new, bool decode) {
         a.kv_sb = (int64_t)c.n_kv_heads * c.max_seq * hd;
         a.kv_sh = (int64_t)c.max_seq * hd;
         a.kv_ss = hd;
+        a.kv_rows = c.max_seq;
         a.o = d->attn;
         a.o_sb = d->q_dim;
         a.o_sh = hd;
