@@ -223,29 +223,11 @@ struct GemvCfg {
     static constexpr int X_BYTES = NT * 128;
     static constexpr int C_STAGES = INT8 ? 2 : 0;                 // converted bf16 ring
     static constexpr int C_BYTES = 256 * 128;
-    static constexpr int RED_BYTES = NT * 256 * 4;                // partial tile (reuses the rings)
+    static constexpr int RED_BYTES = 2 * NT * 256 * 4;            // send + receive partials (reuse the rings)
     static constexpr int RING = STAGES * (W_BYTES + X_BYTES) + C_STAGES * C_BYTES;
     static constexpr int SMEM = (RING > RED_BYTES ? RING : RED_BYTES) + 1024 + 512;
     static constexpr int TMEM_COLS = (2 * NT) < 32 ? 32 : (2 * NT);
 };
-
-__device__ __forceinline__ void cluster_sync_all() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
-__device__ __forceinline__ float ld_dsmem_f32(uint32_t local_addr, uint32_t rank) {
-    uint32_t remote;
-    float v;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_addr), "r"(rank));
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote));
-    return v;
-}
-
-__device__ __forceinline__ void st_dsmem_f32(uint32_t local_addr, uint32_t rank, float v) {
-    uint32_t remote;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_addr), "r"(rank));
-    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(remote), "f"(v) : "memory");
-}
 
 template <int NT, int STAGES, bool INT8>
 __global__ void __launch_bounds__(256, 1)
@@ -266,6 +248,7 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
     const uint32_t cempty0 = smem_u32(bars + 2 * STAGES + 2);
     const uint32_t accb = smem_u32(bars + 2 * STAGES + 4);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+    const uint32_t recvb = smem_u32(bars + 2 * STAGES + 6);   // partials from the peers have landed
 
     pdl_trigger();
     const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
@@ -286,6 +269,7 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
             mbar_init(cempty0 + 8 * s, 1);
         }
         mbar_init(accb, 1);
+        mbar_init(recvb, 1);
         fence_barrier_init();
     }
     if (warp == 1) tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
@@ -455,34 +439,58 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
         }
         return;
     }
-    // Push model: rank r owns row pairs [r*P, (r+1)*P), P = 128 / CS.  Every
-    // CTA stores its partials for those rows straight into rank r's buffer
-    // slot [my rank] (red[src][m][p][2]), then one cluster barrier; each rank
-    // then sums its CS slots locally in rank order (deterministic).
+    // Rank r of the cluster owns row pairs [r*P, (r+1)*P), P = 128 / CS.  Each
+    // CTA lays its partial out per owner (send[owner][m][pair][2]), then one
+    // thread sends every other owner its slice with a DSMEM bulk copy into
+    // the owner's receive slot [my rank], completing on the owner's mbarrier.
+    // Owners sum the CS slots in rank order (deterministic).  The split
+    // cluster barrier guarantees a peer's rings are idle before it is written.
     {
         const int P = 128 / CS;
+        const int SLICE = NT * P * 2 * 4;                  // bytes per owner
+        float* sendb = red;
+        float* recvf = red + NT * 256;
         const int owner = l / P, pl = l % P;
-        const uint32_t base = smem_u32(red);
-        asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");   // all peers' rings are free
 #pragma unroll
         for (int t = 0; t < TP; t++) {
             const int m = part * TP + t;
-            const uint32_t off = (uint32_t)((((split * NT + m) * P + pl) * 2) * 4);
-            st_dsmem_f32(base + off, (uint32_t)owner, acc[0][t]);
-            st_dsmem_f32(base + off + 4, (uint32_t)owner, acc[1][t]);
+            float* dst = sendb + ((owner * NT + m) * P + pl) * 2;
+            dst[0] = acc[0][t];
+            dst[1] = acc[1][t];
         }
-        cluster_sync_all();
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncthreads();
+        asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");   // all peers' rings are free
+        if (threadIdx.x == 0) {
+            mbar_expect_tx(recvb, (uint32_t)((CS - 1) * SLICE));
+            const uint32_t send0 = smem_u32(sendb), recv0 = smem_u32(recvf);
+            for (int r = 0; r < CS; r++) {
+                if (r == split) continue;
+                uint32_t rdst, rbar;
+                asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rdst) : "r"(recv0 + split * SLICE), "r"(r));
+                asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rbar) : "r"(recvb), "r"(r));
+                asm volatile(
+                    "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(rdst),
+                    "r"(send0 + r * SLICE), "r"(SLICE), "r"(rbar)
+                    : "memory");
+            }
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        }
+        const bool got = __all_sync(0xffffffffu, mbar_wait(recvb, 0, err, DEV_ERR_TIMEOUT_MISC));
         const int items = P * NT;
         for (int it = threadIdx.x; it < items; it += 256) {
             const int m = it / P, pl2 = it % P;
             float a0 = 0.f, a1 = 0.f;
             for (int r = 0; r < CS; r++) {
-                const float2 v = *reinterpret_cast<const float2*>(&red[((r * NT + m) * P + pl2) * 2]);
+                const float* src = (r == split) ? sendb + ((split * NT + m) * P + pl2) * 2
+                                                : recvf + (r * SLICE) / 4 + (m * P + pl2) * 2;
+                const float2 v = *reinterpret_cast<const float2*>(src);
                 a0 += v.x;
                 a1 += v.y;
             }
-            if (ok && m < Mtok) finish(m, split * P + pl2, a0, a1);
+            if (ok && got && m < Mtok) finish(m, split * P + pl2, a0, a1);
         }
+        if (threadIdx.x == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");   // own sends have read smem
     }
 }
 
