@@ -278,24 +278,22 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
 // that share the kv head are padded to 16 rows.  Per 128-key tile:
 //   S^T = K_tile Q^T      (M = 128 keys, N = 16 query rows, K = D)  -> TMEM
 //   softmax               (thread t of warps 2-5 <-> key t: one TMEM lane)
-//   O_j = P V_tile        (M = 128 rows: the first G are the queries, N = D,
-//                          K = 128 keys, V as the MN-major operand) -> TMEM
-// P lives in a double-buffered 8-row smem tile whose row-group stride is 0,
-// so the MMA's 128 rows read the 8 real rows repeatedly (rows >= G are zero;
-// output rows >= 8 are ignored).  Each tile's P V goes to its own TMEM buffer
-// and warp 4 folds it into register accumulators with the running-max factor
-// (o = o * alpha + O_j), so the softmax never waits for a P V product.
+//   O  += P V_tile        (M = 128 rows, of which the first G are the queries,
+//                          N = D, K = 128 keys; P in a zero-padded smem tile,
+//                          V as the MN-major operand)               -> TMEM
 // Warp 0 streams K/V tiles with TMA (2-stage ring), warp 1 issues the MMAs.
-// Splits of one group form a cluster and merge (max, sum, o) over DSMEM.
+// The online softmax keeps per-query (max, sum) in registers of every
+// softmax thread (tile reductions over shuffles + shared memory).  Splits of
+// one group form a cluster and merge (max, sum, o) over DSMEM in fixed order.
 template <int D>
 struct DecTcCfg {
     static constexpr int TILE = 128 * D * 2;            // K or V tile bytes
-    static constexpr int P_BYTES = 2 * 2 * 1024;        // [2 buffers][2 key halves][8 rows][64 keys] bf16
+    static constexpr int P_BYTES = 128 * 128 * 2;       // [128 rows][128 keys] bf16, rows >= G zero
     static constexpr int Q_BYTES = 16 * D * 2;          // [16 rows][D] bf16, rows >= G zero
     static constexpr int PART = 8 * (D + 2) * 4;        // merge partial (max, sum, o) per query
     static constexpr int SMEM = 4 * TILE + P_BYTES + (Q_BYTES < 1024 ? 1024 : Q_BYTES) + PART + 1024 + 512;
-    static constexpr int O_COL = 32;                    // TMEM: S^T buffers at 0 and 16, O_j buffers at 32, 32 + D
-    static constexpr int TMEM_COLS = (32 + 2 * D) <= 128 ? 128 : (32 + 2 * D) <= 256 ? 256 : 512;
+    static constexpr int O_COL = 32;                    // TMEM: S^T buffers at 0 and 16, O at 32
+    static constexpr int TMEM_COLS = (32 + D) <= 128 ? 128 : 256;
 };
 
 __device__ __forceinline__ void dec_cluster_sync() {
@@ -326,7 +324,7 @@ __device__ __forceinline__ bool softmax_bar_and(bool v) {
 }
 
 template <int D>
-__global__ void __launch_bounds__(192, D == 64 ? 3 : 1)
+__global__ void __launch_bounds__(192, 1)
 attn_decode_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                       DecodeArgs a, int* err) {
     using C = DecTcCfg<D>;
@@ -340,10 +338,10 @@ attn_decode_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_cons
     float* spart = reinterpret_cast<float*>(sQ + (C::Q_BYTES < 1024 ? 1024 : C::Q_BYTES));   // [8][D+2]
     uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(spart) + C::PART);
     const uint32_t k_full0 = smem_u32(bars + 0), v_full0 = smem_u32(bars + 2), kv_empty0 = smem_u32(bars + 4);
-    const uint32_t s_full0 = smem_u32(bars + 6), p_full0 = smem_u32(bars + 8), o_done0 = smem_u32(bars + 10);
-    const uint32_t q_full = smem_u32(bars + 12);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
-    float* sred = reinterpret_cast<float*>(bars + 14);      // [2][4 warps][8 queries]
+    const uint32_t s_full0 = smem_u32(bars + 6), p_full = smem_u32(bars + 8), o_done = smem_u32(bars + 9);
+    const uint32_t q_full = smem_u32(bars + 10);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+    float* sred = reinterpret_cast<float*>(bars + 12);      // [2][4 warps][8 queries]
 
     pdl_trigger();
     const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
@@ -357,9 +355,9 @@ attn_decode_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_cons
             mbar_init(v_full0 + 8 * s, 1);
             mbar_init(kv_empty0 + 8 * s, 1);
             mbar_init(s_full0 + 8 * s, 1);
-            mbar_init(p_full0 + 8 * s, 128);
-            mbar_init(o_done0 + 8 * s, 1);
         }
+        mbar_init(p_full, 128);
+        mbar_init(o_done, 1);
         mbar_init(q_full, 128);
         fence_barrier_init();
     }
@@ -417,21 +415,19 @@ attn_decode_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_cons
                     umma_commit(s_full0 + 8 * st);
                 }
                 if (j > 0) {
-                    const int jp = j - 1, st = jp & 1, pb = jp & 1;
-                    if (!mbar_wait(p_full0 + 8 * pb, (jp >> 1) & 1, err, DEV_ERR_TIMEOUT_MISC)) break;
+                    const int jp = j - 1, st = jp & 1;
+                    if (!mbar_wait(p_full, jp & 1, err, DEV_ERR_TIMEOUT_MISC)) break;
                     if (!mbar_wait(v_full0 + 8 * st, (jp >> 1) & 1, err, DEV_ERR_TIMEOUT_FULL)) break;
                     tc_fence_after();
                     const uint32_t v_base = smem_u32(sV + st * C::TILE);
-                    const uint32_t pbase = p_base + pb * 2048;
 #pragma unroll
                     for (int kk = 0; kk < 8; kk++) {
-                        // 8-row P atoms, row-group stride 0: the 128 MMA rows repeat rows 0-7
-                        const uint64_t ad = sdesc_sw128(pbase + (kk >> 2) * 1024 + (kk & 3) * 32, 16, 0);
+                        const uint64_t ad = sdesc_sw128(p_base + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
                         const uint64_t bd = sdesc_sw128(v_base + kk * 16 * 128, 16384, 1024);
-                        umma_f16_ss(tmem + C::O_COL + pb * D, ad, bd, idesc_o, kk != 0);
+                        umma_f16_ss(tmem + C::O_COL, ad, bd, idesc_o, (jp | kk) != 0);
                     }
                     umma_commit(kv_empty0 + 8 * st);
-                    umma_commit(o_done0 + 8 * pb);
+                    umma_commit(o_done);
                 }
             }
         }
@@ -451,11 +447,6 @@ attn_decode_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_cons
             *reinterpret_cast<uint4*>(sQ + atom * 2048 + r * 128 + ((cc ^ (r & 7)) << 4)) = v;
         }
         for (int i = tid; i < C::P_BYTES / 16; i += 128) reinterpret_cast<uint4*>(sP)[i] = make_uint4(0, 0, 0, 0);
-        // warp 4, lane q < G: running output row of query q, accumulated in spart[q][0, D)
-        float* o_acc = spart + lane * (D + 2);
-        if (quarter == 0 && lane < G)
-            for (int i = 0; i < D; i++) o_acc[i] = 0.f;
-        float alpha_prev = 1.f;   // warp 4: this lane's query factor for the previous tile
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         mbar_arrive(q_full);
 
@@ -503,18 +494,37 @@ attn_decode_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_cons
 #pragma unroll
             for (int q = 0; q < 8; q++)
                 l_run[q] = l_run[q] * alpha[q] + (sred[32 + q] + sred[40 + q] + sred[48 + q] + sred[56 + q]);
-            const int pb = j & 1;
-            if (j >= 2) {   // P buffer pb was read by the P V product of tile j - 2
-                ok = softmax_bar_and(mbar_wait(o_done0 + 8 * pb, ((j - 2) >> 1) & 1, err, DEV_ERR_TIMEOUT_MISC));
+            if (j > 0) {
+                ok = softmax_bar_and(mbar_wait(o_done, (j - 1) & 1, err, DEV_ERR_TIMEOUT_MISC));
                 if (!ok) break;
+                tc_fence_after();
+                // rescale the O rows (queries 0..G-1 = TMEM lanes 0..G-1, lane quarter 0: warp 4)
+                if (quarter == 0) {
+                    float my_alpha = 1.f;
+#pragma unroll
+                    for (int q = 0; q < 8; q++)
+                        if (lane == q && q < G) my_alpha = alpha[q];
+                    if (__any_sync(0xffffffffu, my_alpha != 1.0f)) {
+#pragma unroll 1
+                        for (int c = 0; c < D; c += 16) {
+                            float o[16];
+                            tmem_ld16(t_lane + C::O_COL + c, o);
+                            tmem_wait_ld();
+#pragma unroll
+                            for (int i = 0; i < 16; i++) o[i] *= my_alpha;
+                            tmem_st16(t_lane + C::O_COL + c, o);
+                        }
+                        tmem_wait_st();
+                    }
+                }
             }
-            // P[q][key] (bf16) into buffer pb: 8-row atoms per 64-key half, 128-B swizzle
+            // P[q][key] (bf16) into the swizzled K-major tile: row q, key column kr
             {
-                const int half = kr >> 6, kc = kr & 63;
+                const int atom = kr >> 6, kc = kr & 63;
 #pragma unroll
                 for (int q = 0; q < 8; q++) {
                     if (q < G) {
-                        uint8_t* rowp = sP + pb * 2048 + half * 1024 + q * 128;
+                        uint8_t* rowp = sP + atom * 16384 + q * 128;
                         const int chunk = (kc >> 3) ^ (q & 7);
                         *reinterpret_cast<__nv_bfloat16*>(rowp + chunk * 16 + (kc & 7) * 2) = __float2bfloat16_rn(p[q]);
                     }
@@ -522,49 +532,12 @@ attn_decode_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_cons
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             tc_fence_before();
-            mbar_arrive(p_full0 + 8 * pb);
-            // warp 4 folds the previous tile's P V: o = o * alpha_{j-1} + O_{j-1}
-            if (quarter == 0 && j > 0) {
-                const int jp = j - 1, ob = jp & 1;
-                const bool okw = __all_sync(0xffffffffu, mbar_wait(o_done0 + 8 * ob, (jp >> 1) & 1, err, DEV_ERR_TIMEOUT_MISC));
-                tc_fence_after();
-                if (okw) {
-#pragma unroll 1
-                    for (int c = 0; c < D; c += 16) {
-                        float o[16];
-                        tmem_ld16(t_lane + C::O_COL + ob * D + c, o);
-                        tmem_wait_ld();
-                        if (lane < G)
-#pragma unroll
-                            for (int i = 0; i < 16; i++) o_acc[c + i] = o_acc[c + i] * alpha_prev + o[i];
-                    }
-                }
-            }
-            if (quarter == 0) {
-#pragma unroll
-                for (int q = 0; q < 8; q++)
-                    if (lane == q && q < G) alpha_prev = alpha[q];
-            }
+            mbar_arrive(p_full);
         }
-        // the last tile's P V
-        if (ok && n_tiles > 0 && quarter == 0) {
-            const int jp = n_tiles - 1, ob = jp & 1;
-            ok = __all_sync(0xffffffffu, mbar_wait(o_done0 + 8 * ob, (jp >> 1) & 1, err, DEV_ERR_TIMEOUT_ACC));
-            tc_fence_after();
-            if (ok) {
-#pragma unroll 1
-                for (int c = 0; c < D; c += 16) {
-                    float o[16];
-                    tmem_ld16(t_lane + C::O_COL + ob * D + c, o);
-                    tmem_wait_ld();
-                    if (lane < G)
-#pragma unroll
-                        for (int i = 0; i < 16; i++) o_acc[c + i] = o_acc[c + i] * alpha_prev + o[i];
-                }
-            }
-        }
-        // partial (max, sum, unnormalised o) of this split: warp 4, lanes < G
+        if (ok && n_tiles > 0) ok = __all_sync(0xffffffffu, mbar_wait(o_done, (n_tiles - 1) & 1, err, DEV_ERR_TIMEOUT_ACC));
+        // partial (max, sum, unnormalised o) of this split: warp 4 (TMEM quarter 0), lanes < G
         if (quarter == 0) {
+            tc_fence_after();
             float my_m = -INFINITY, my_l = 0.f;
 #pragma unroll
             for (int q = 0; q < 8; q++)
@@ -572,12 +545,23 @@ attn_decode_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_cons
                     my_m = m_run[q];
                     my_l = l_run[q];
                 }
-            const bool have = n_tiles > 0 && ok;
+#pragma unroll 1
+            for (int c = 0; c < D; c += 16) {
+                float o[16];
+                if (n_tiles > 0 && ok) {
+                    tmem_ld16(t_lane + C::O_COL + c, o);
+                    tmem_wait_ld();
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 16; i++) o[i] = 0.f;
+                }
+                if (lane < G)
+#pragma unroll
+                    for (int i = 0; i < 16; i++) spart[lane * (D + 2) + c + i] = o[i];
+            }
             if (lane < G) {
-                if (!have)
-                    for (int i = 0; i < D; i++) o_acc[i] = 0.f;
-                spart[lane * (D + 2) + D] = have ? my_m : -INFINITY;
-                spart[lane * (D + 2) + D + 1] = have ? my_l : 0.f;
+                spart[lane * (D + 2) + D] = (n_tiles > 0 && ok) ? my_m : -INFINITY;
+                spart[lane * (D + 2) + D + 1] = (n_tiles > 0 && ok) ? my_l : 0.f;
             }
         }
     }
@@ -712,7 +696,7 @@ int attn_decode_launch(tb_ctx* ctx, DecodeArgs a, int B, int D, int max_len) {
         return set_error(ctx, TB_ERR_SHAPE, "attn_decode: K/V must be contiguous [B][Hkv][rows][D]");
     const int groups = B * a.Hkv;
     const int tiles = (max_len + 127) / 128;
-    const int slots = (D == 64 ? 3 : 1) * ctx->num_sms;   // resident CTAs (shared memory / registers)
+    const int slots = (D == 64 ? 2 : 1) * ctx->num_sms;
     int nsp = 8;
     while (nsp > 1 && (groups * nsp > slots || nsp > tiles)) nsp >>= 1;
     a.chunk = ((tiles + nsp - 1) / nsp) * 128;
