@@ -362,6 +362,31 @@ int rms(tb_decoder* d, const bf16* x, int64_t ldx, const bf16* w, bf16* y, int M
                   d->cfg.norm_eps);
 }
 
+// y = rmsnorm(x) W^T.  Up to 64 tokens the norm runs inside the GEMV (its
+// otherwise idle warps rescale each activation tile in shared memory), so the
+// normalised rows never reach HBM; larger token counts normalise into d->h and
+// run the tensor-core GEMM.
+int norm_lin(tb_decoder* d, const bf16* x, int64_t ldx, const bf16* norm_w, const void* w, const int8_t* wq,
+             const float* wscale, void* y, int M, int N, bool swiglu, bool out_f32) {
+    const int K = d->cfg.d_model;
+    if (M > 64) {
+        TB_TRY(rms(d, x, ldx, norm_w, d->h, M));
+        return lin(d, d->h, w, wq, wscale, y, M, N, K, nullptr, swiglu, out_f32);
+    }
+    Epi ep{};
+    ep.out = y;
+    ep.ldo = swiglu ? N / 2 : N;
+    ep.ldr = N;
+    ep.out_f32 = out_f32 ? 1 : 0;
+    ep.swiglu = swiglu ? 1 : 0;
+    ep.x_ld = ldx;
+    ep.norm_w = norm_w;
+    ep.norm_eps = d->cfg.norm_eps;
+    const bool int8 = d->cfg.weights_int8 && wq;
+    if (int8) ep.scale = wscale;
+    return linear_launch(d->ctx, int8 ? 1 : 0, x, int8 ? (const void*)wq : w, ep, M, N, K);
+}
+
 // One transformer layer over T = B * S_new tokens.  decode: S_new == 1 and
 // positions come from d->state[0].
 int layer_forward(tb_decoder* d, int l, int B, int S_new, bool decode) {
@@ -373,8 +398,7 @@ int layer_forward(tb_decoder* d, int l, int B, int S_new, bool decode) {
     bf16* kc = d->kcache + (int64_t)l * d->cache_layer_elems;
     bf16* vc = d->vcache + (int64_t)l * d->cache_layer_elems;
 
-    TB_TRY(rms(d, d->x, dm, L.attn_norm, d->h, T));
-    TB_TRY(lin(d, d->h, L.wqkv, L.qqkv, L.sqkv, d->qkv, T, d->qkv_n, dm, nullptr, false, false));
+    TB_TRY(norm_lin(d, d->x, dm, L.attn_norm, L.wqkv, L.qqkv, L.sqkv, d->qkv, T, d->qkv_n, false, false));
     {
         const int64_t work = (int64_t)T * (c.n_heads + 2 * c.n_kv_heads) * (hd / 16);
         TB_TRY(launch(ctx, "rope_kv", rope_kv_kernel, dim3(grid_for(ctx, work)), dim3(256), 0, d->qkv, d->qkv_n, B,
@@ -423,8 +447,7 @@ int layer_forward(tb_decoder* d, int l, int B, int S_new, bool decode) {
         TB_TRY(attn_decode_launch(ctx, a, B, hd, c.max_seq));
     }
     TB_TRY(lin(d, d->attn, L.wo, L.qo, L.so, d->x, T, dm, d->q_dim, d->x, false, false));
-    TB_TRY(rms(d, d->x, dm, L.mlp_norm, d->h, T));
-    TB_TRY(lin(d, d->h, L.wgu, L.qgu, L.sgu, d->act, T, 2 * c.ffn_hidden, dm, nullptr, true, false));
+    TB_TRY(norm_lin(d, d->x, dm, L.mlp_norm, L.wgu, L.qgu, L.sgu, d->act, T, 2 * c.ffn_hidden, true, false));
     TB_TRY(lin(d, d->act, L.wdown, L.qdown, L.sdown, d->x, T, dm, c.ffn_hidden, d->x, false, false));
     return TB_OK;
 }
@@ -432,8 +455,8 @@ int layer_forward(tb_decoder* d, int l, int B, int S_new, bool decode) {
 // Final norm on each sequence's last token, LM head, greedy argmax.
 int head_forward(tb_decoder* d, int B, int64_t last_row_stride, int64_t last_row_off) {
     const tb_decoder_config& c = d->cfg;
-    TB_TRY(rms(d, d->x + last_row_off, last_row_stride, d->final_norm, d->h, B));
-    TB_TRY(lin(d, d->h, d->lm_head, d->qlm, d->slm, d->logits, B, c.vocab, c.d_model, nullptr, false, true));
+    TB_TRY(norm_lin(d, d->x + last_row_off, last_row_stride, d->final_norm, d->lm_head, d->qlm, d->slm, d->logits, B,
+                    c.vocab, false, true));
     const int chunk = 2048, nch = (c.vocab + chunk - 1) / chunk;
     return launch(d->ctx, "argmax_step", argmax_step_kernel, dim3(B, nch), dim3(256), 0, (const float*)d->logits,
                   c.vocab, chunk, d->cur_ids, d->out_ids, c.max_seq, (const int*)d->state, d->amax_keys,

@@ -212,18 +212,23 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 // Decode GEMV (swap-AB, split-K reduced inside a thread-block cluster)
 // =====================================================================
 // Grid (tiles, CS) with cluster dims (1, CS, 1): the CS CTAs of a cluster
-// split the K range of one 256-row weight tile.  Each CTA parks its f32
-// partial tile [NT tokens][256 rows] in its own shared memory; after a
-// cluster barrier CTA rank r sums the CS partials of rows pairs
-// [r*128/CS, (r+1)*128/CS) over DSMEM (fixed order: deterministic) and runs
-// the epilogue for them.
+// split the K range of one 256-row weight tile.  Each CTA lays out its f32
+// partial tile [NT tokens][256 rows] per owner; CTA rank r receives the
+// partials of row pairs [r*128/CS, (r+1)*128/CS) from its peers by DSMEM bulk
+// copies, sums them in rank order (deterministic) and runs the epilogue.
+//
+// Fused RMSNorm (Epi::norm_w set): warps 2..7 build each activation tile from
+// the raw rows, bf16(x * w), and accumulate each token's sum of squares over
+// the CTA's K range.  1/rms is a per-token factor of every output, so it is
+// applied in the epilogue once the cluster's partial sums are added.
 template <int NT, int STAGES, bool INT8>
 struct GemvCfg {
     static constexpr int W_BYTES = INT8 ? 256 * 64 : 256 * 128;  // int8: 64 K per row, no swizzle
     static constexpr int X_BYTES = NT * 128;
     static constexpr int C_STAGES = INT8 ? 2 : 0;                 // converted bf16 ring
     static constexpr int C_BYTES = 256 * 128;
-    static constexpr int RED_BYTES = 2 * NT * 256 * 4;            // send + receive partials (reuse the rings)
+    // send + receive partials (reuse the rings); each owner slice carries NT sums of squares
+    static constexpr int RED_BYTES = 2 * (NT * 256 + 8 * NT) * 4;
     static constexpr int RING = STAGES * (W_BYTES + X_BYTES) + C_STAGES * C_BYTES;
     static constexpr int SMEM = (RING > RED_BYTES ? RING : RED_BYTES) + 1024 + 512;
     static constexpr int TMEM_COLS = (2 * NT) < 32 ? 32 : (2 * NT);
@@ -249,6 +254,9 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
     const uint32_t accb = smem_u32(bars + 2 * STAGES + 4);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
     const uint32_t recvb = smem_u32(bars + 2 * STAGES + 6);   // partials from the peers have landed
+    const uint32_t xrdy0 = smem_u32(bars + 2 * STAGES + 7);   // [STAGES] activation tile normalised
+    float* s_ss = reinterpret_cast<float*>(bars + 3 * STAGES + 7);   // [NT] sum of squares, then 1/rms
+    const bool NORM = ep.norm_w != nullptr;
 
     pdl_trigger();
     const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
@@ -270,6 +278,7 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
         }
         mbar_init(accb, 1);
         mbar_init(recvb, 1);
+        for (int s = 0; s < STAGES; s++) mbar_init(xrdy0 + 8 * s, N_CONV_WARPS);
         fence_barrier_init();
     }
     if (warp == 1) tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
@@ -283,22 +292,25 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
         tma_prefetch_desc(&tmX);
         // Weights do not depend on the previous kernel: start streaming the
         // first STAGES K-blocks before waiting for it, then fetch activations.
+        // With the norm fused the converter warps write the activation tiles.
+        const uint32_t tx_bytes = C::W_BYTES + (NORM ? 0 : C::X_BYTES);
         const int pre = nk < STAGES ? nk : STAGES;
         for (int i = 0; i < pre; i++) {
-            mbar_expect_tx(full0 + 8 * i, C::W_BYTES + C::X_BYTES);
+            mbar_expect_tx(full0 + 8 * i, tx_bytes);
             tma_load_2d(smem_u32(sW + i * C::W_BYTES), &tmW, full0 + 8 * i, (kb0 + i) * 64, tile * 256);
         }
         pdl_wait();
-        for (int i = 0; i < pre; i++)
-            tma_load_2d(smem_u32(sX + i * C::X_BYTES), &tmX, full0 + 8 * i, (kb0 + i) * 64, 0);
+        if (!NORM)
+            for (int i = 0; i < pre; i++)
+                tma_load_2d(smem_u32(sX + i * C::X_BYTES), &tmX, full0 + 8 * i, (kb0 + i) * 64, 0);
         int issued = pre;
         for (int i = pre; i < nk; i++) {
             int s = i % STAGES;
             if (!mbar_wait(empty0 + 8 * s, ((i / STAGES) - 1) & 1, err, DEV_ERR_TIMEOUT_EMPTY)) break;
-            mbar_expect_tx(full0 + 8 * s, C::W_BYTES + C::X_BYTES);
+            mbar_expect_tx(full0 + 8 * s, tx_bytes);
             int kcoord = (kb0 + i) * 64;
             tma_load_2d(smem_u32(sW + s * C::W_BYTES), &tmW, full0 + 8 * s, kcoord, tile * 256);
-            tma_load_2d(smem_u32(sX + s * C::X_BYTES), &tmX, full0 + 8 * s, kcoord, 0);
+            if (!NORM) tma_load_2d(smem_u32(sX + s * C::X_BYTES), &tmX, full0 + 8 * s, kcoord, 0);
             issued = i + 1;
         }
         for (int i = (issued > STAGES ? issued - STAGES : 0); i < issued; i++)
@@ -315,6 +327,7 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
                 w_base = smem_u32(sC + c * C::C_BYTES);
             } else {
                 if (!mbar_wait(full0 + 8 * s, (i / STAGES) & 1, err, DEV_ERR_TIMEOUT_FULL)) break;
+                if (NORM && !mbar_wait(xrdy0 + 8 * s, (i / STAGES) & 1, err, DEV_ERR_TIMEOUT_MISC)) break;
                 w_base = smem_u32(sW + s * C::W_BYTES);
             }
             tc_fence_after();
@@ -332,37 +345,110 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
             umma_commit(empty0 + 8 * s);
         }
         umma_commit(accb);
-    } else if (INT8 && warp >= 2) {
-        // ---------------- int8 -> bf16 converters (warps 2..7)
+    } else if ((INT8 || NORM) && warp >= 2) {
+        // ---------------- converter warps 2..7: the normalised activation tile
+        // (when the RMSNorm is fused) and int8 -> bf16 weights (int8 path)
         const int ct = threadIdx.x - 64;   // 0..191
+        constexpr int XI = (NT * 8 + 191) / 192;   // 16-B activation chunks per thread per stage
+        uint4 xv[XI], gv[XI];
+        const __nv_bfloat16* xg = reinterpret_cast<const __nv_bfloat16*>(ep.norm_x);
+        const __nv_bfloat16* gg = reinterpret_cast<const __nv_bfloat16*>(ep.norm_w);
+        // stage i's raw activation chunks and norm gains -> registers (one stage ahead)
+        auto load_x = [&](int i) {
+            const int kbase = (kb0 + i) * 64;
+#pragma unroll
+            for (int u = 0; u < XI; u++) {
+                const int it = ct + u * 192;
+                const int m = it >> 3, k0 = kbase + 8 * ((it & 7) ^ (m & 7));
+                const bool kin = it < NT * 8 && k0 < K;
+                xv[u] = (kin && m < Mtok) ? *reinterpret_cast<const uint4*>(xg + (int64_t)m * ep.x_ld + k0)
+                                          : make_uint4(0, 0, 0, 0);
+                gv[u] = kin ? *reinterpret_cast<const uint4*>(gg + k0) : make_uint4(0, 0, 0, 0);
+            }
+        };
+        float ssv[XI];   // sum of squares of this thread's raw activation chunks (one row each)
+#pragma unroll
+        for (int u = 0; u < XI; u++) ssv[u] = 0.f;
+        if (NORM) {
+            pdl_wait();
+            if (nk > 0) load_x(0);
+        }
         for (int i = 0; i < nk; i++) {
             int s = i % STAGES, c = i & 1;
-            bool ok1 = mbar_wait(full0 + 8 * s, (i / STAGES) & 1, err, DEV_ERR_TIMEOUT_FULL);
-            bool ok2 = i < 2 || mbar_wait(cempty0 + 8 * c, ((i >> 1) - 1) & 1, err, DEV_ERR_TIMEOUT_MISC);
-            if (!ok1 || !ok2) break;
-            const uint8_t* src = sW + s * C::W_BYTES;   // [256 rows][64 B], unswizzled
-            uint8_t* dst = sC + c * C::C_BYTES;          // [256 rows][128 B], 128-B swizzle
-            for (int it = ct; it < 256 * 4; it += 192) {
-                int r = it >> 2, ch = it & 3;
-                uint4 raw = *reinterpret_cast<const uint4*>(src + r * 64 + ch * 16);
-                uint32_t w4[4] = {raw.x, raw.y, raw.z, raw.w};
-                uint32_t o[8];
-#pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    int b0 = (int)(int8_t)(w4[j] & 0xff), b1 = (int)(int8_t)((w4[j] >> 8) & 0xff);
-                    int b2 = (int)(int8_t)((w4[j] >> 16) & 0xff), b3 = (int)(int8_t)(w4[j] >> 24);
-                    o[2 * j] = pack_bf16x2((float)b0, (float)b1);
-                    o[2 * j + 1] = pack_bf16x2((float)b2, (float)b3);
-                }
-                int p0 = ((2 * ch) ^ (r & 7)) * 16, p1 = ((2 * ch + 1) ^ (r & 7)) * 16;
-                *reinterpret_cast<uint4*>(dst + r * 128 + p0) = make_uint4(o[0], o[1], o[2], o[3]);
-                *reinterpret_cast<uint4*>(dst + r * 128 + p1) = make_uint4(o[4], o[5], o[6], o[7]);
+            if (INT8) {
+                // W landing in slot s also means the MMAs of stage i - STAGES are done (x slot free)
+                if (!mbar_wait(full0 + 8 * s, (i / STAGES) & 1, err, DEV_ERR_TIMEOUT_FULL)) break;
+            } else if (i >= STAGES) {
+                // x slot s is free once the MMAs of stage i - STAGES completed
+                if (!mbar_wait(empty0 + 8 * s, ((i / STAGES) - 1) & 1, err, DEV_ERR_TIMEOUT_EMPTY)) break;
             }
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(cfull0 + 8 * c);
-                mbar_arrive(empty0 + 8 * s);
+            if (NORM) {
+                // x tile [NT rows][64 k] bf16, 128-B swizzle: bf16(x[m,k] * w[k]); the
+                // per-token 1/rms is a common factor of each output and is applied in the epilogue
+                uint8_t* xt = sX + s * C::X_BYTES;
+#pragma unroll
+                for (int u = 0; u < XI; u++) {
+                    const int it = ct + u * 192;
+                    if (it < NT * 8) {
+                        const uint32_t xa[4] = {xv[u].x, xv[u].y, xv[u].z, xv[u].w};
+                        const uint32_t ga[4] = {gv[u].x, gv[u].y, gv[u].z, gv[u].w};
+                        uint32_t o[4];
+#pragma unroll
+                        for (int j = 0; j < 4; j++) {
+                            const float a0 = bf16_lo(xa[j]), a1 = bf16_hi(xa[j]);
+                            ssv[u] += a0 * a0 + a1 * a1;
+                            o[j] = pack_bf16x2(a0 * bf16_lo(ga[j]), a1 * bf16_hi(ga[j]));
+                        }
+                        *reinterpret_cast<uint4*>(xt + (it >> 3) * 128 + (it & 7) * 16) = make_uint4(o[0], o[1], o[2], o[3]);
+                    }
+                }
+                if (!INT8) {
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(xrdy0 + 8 * s);
+                }
+                if (i + 1 < nk) load_x(i + 1);
+            }
+            if (INT8) {
+                // the converted ring slot is free once the MMAs of stage i - 2 are done
+                if (i >= 2 && !mbar_wait(cempty0 + 8 * c, ((i >> 1) - 1) & 1, err, DEV_ERR_TIMEOUT_MISC)) break;
+                const uint8_t* src = sW + s * C::W_BYTES;   // [256 rows][64 B], unswizzled
+                uint8_t* dst = sC + c * C::C_BYTES;          // [256 rows][128 B], 128-B swizzle
+                for (int it = ct; it < 256 * 4; it += 192) {
+                    int r = it >> 2, ch = it & 3;
+                    uint4 raw = *reinterpret_cast<const uint4*>(src + r * 64 + ch * 16);
+                    uint32_t w4[4] = {raw.x, raw.y, raw.z, raw.w};
+                    uint32_t o[8];
+#pragma unroll
+                    for (int j = 0; j < 4; j++) {
+                        int b0 = (int)(int8_t)(w4[j] & 0xff), b1 = (int)(int8_t)((w4[j] >> 8) & 0xff);
+                        int b2 = (int)(int8_t)((w4[j] >> 16) & 0xff), b3 = (int)(int8_t)(w4[j] >> 24);
+                        o[2 * j] = pack_bf16x2((float)b0, (float)b1);
+                        o[2 * j + 1] = pack_bf16x2((float)b2, (float)b3);
+                    }
+                    int p0 = ((2 * ch) ^ (r & 7)) * 16, p1 = ((2 * ch + 1) ^ (r & 7)) * 16;
+                    *reinterpret_cast<uint4*>(dst + r * 128 + p0) = make_uint4(o[0], o[1], o[2], o[3]);
+                    *reinterpret_cast<uint4*>(dst + r * 128 + p1) = make_uint4(o[4], o[5], o[6], o[7]);
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(cfull0 + 8 * c);
+                    mbar_arrive(empty0 + 8 * s);
+                }
+            }
+        }
+        if (NORM) {
+            // the 8 chunks of a row sit in 8 consecutive lanes: partial sum of squares of
+            // each token row over this CTA's K range
+#pragma unroll
+            for (int u = 0; u < XI; u++) {
+                float v = ssv[u];
+                v += __shfl_xor_sync(0xffffffffu, v, 1);
+                v += __shfl_xor_sync(0xffffffffu, v, 2);
+                v += __shfl_xor_sync(0xffffffffu, v, 4);
+                const int it = ct + u * 192;
+                if ((lane & 7) == 0 && it < NT * 8) s_ss[it >> 3] = v;
             }
         }
     }
@@ -408,6 +494,10 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
     // epilogue for (token m, row pair p): gate/first row p, second row p + 128
     auto finish = [&](int m, int p, float a0, float a1) {
         const int n0 = tile * 256 + p, n1 = n0 + 128;
+        if (NORM) {
+            a0 *= s_ss[m];   // 1 / rms of token m
+            a1 *= s_ss[m];
+        }
         if (ep.swiglu) {
             if (n1 < Nw) {
                 float sg = ep.scale ? ep.scale[n0] : 1.f, su = ep.scale ? ep.scale[n1] : 1.f;
@@ -429,7 +519,12 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
         }
     };
 
+    const float inv_k = 1.0f / (float)K;
     if (CS == 1) {
+        if (NORM) {
+            if (threadIdx.x < NT) s_ss[threadIdx.x] = rsqrtf(s_ss[threadIdx.x] * inv_k + ep.norm_eps);
+            __syncthreads();
+        }
         if (ok) {
 #pragma unroll
             for (int t = 0; t < TP; t++) {
@@ -445,19 +540,25 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
     // the owner's receive slot [my rank], completing on the owner's mbarrier.
     // Owners sum the CS slots in rank order (deterministic).  The split
     // cluster barrier guarantees a peer's rings are idle before it is written.
+    // With the norm fused, every slice also carries the sender's NT partial sums of
+    // squares; each owner adds them in rank order to form 1 / rms.
     {
         const int P = 128 / CS;
-        const int SLICE = NT * P * 2 * 4;                  // bytes per owner
+        const int PF = NT * P * 2;                         // partial floats per owner
+        const int SF = PF + NT;                            // slice floats (+ sums of squares)
+        const int SLICE = SF * 4;                          // bytes per owner
         float* sendb = red;
-        float* recvf = red + NT * 256;
+        float* recvf = red + CS * SF;
         const int owner = l / P, pl = l % P;
 #pragma unroll
         for (int t = 0; t < TP; t++) {
             const int m = part * TP + t;
-            float* dst = sendb + ((owner * NT + m) * P + pl) * 2;
+            float* dst = sendb + owner * SF + (m * P + pl) * 2;
             dst[0] = acc[0][t];
             dst[1] = acc[1][t];
         }
+        if (NORM)
+            for (int it = threadIdx.x; it < CS * NT; it += 256) sendb[(it / NT) * SF + PF + it % NT] = s_ss[it % NT];
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncthreads();
         asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");   // all peers' rings are free
@@ -477,13 +578,20 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
             asm volatile("cp.async.bulk.commit_group;" ::: "memory");
         }
         const bool got = __all_sync(0xffffffffu, mbar_wait(recvb, 0, err, DEV_ERR_TIMEOUT_MISC));
+        if (NORM) {
+            if (threadIdx.x < NT) {
+                float t = 0.f;
+                for (int r = 0; r < CS; r++) t += (r == split ? sendb + split * SF : recvf + r * SF)[PF + threadIdx.x];
+                s_ss[threadIdx.x] = rsqrtf(t * inv_k + ep.norm_eps);
+            }
+            __syncthreads();
+        }
         const int items = P * NT;
         for (int it = threadIdx.x; it < items; it += 256) {
             const int m = it / P, pl2 = it % P;
             float a0 = 0.f, a1 = 0.f;
             for (int r = 0; r < CS; r++) {
-                const float* src = (r == split) ? sendb + ((split * NT + m) * P + pl2) * 2
-                                                : recvf + (r * SLICE) / 4 + (m * P + pl2) * 2;
+                const float* src = (r == split ? sendb + split * SF : recvf + r * SF) + (m * P + pl2) * 2;
                 const float2 v = *reinterpret_cast<const float2*>(src);
                 a0 += v.x;
                 a1 += v.y;
@@ -596,8 +704,11 @@ static int launch_gemv_tc(tb_ctx* ctx, const void* x, const void* w, const Epi& 
         rc = make_tmap_2d(ctx, &tw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w, Nw, K, K, 64, 256);
     }
     if (rc) return rc;
-    rc = make_tmap_2d(ctx, &tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, Mtok, K, K, 64, NT);
+    rc = make_tmap_2d(ctx, &tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, Mtok, K, ep.x_ld ? ep.x_ld : K, 64, NT);
     if (rc) return rc;
+    Epi e2 = ep;
+    e2.x_ld = ep.x_ld ? ep.x_ld : K;
+    e2.norm_x = x;
     int cs, kb_per;
     gemv_split(ctx->num_sms, Nw, K, &cs, &kb_per);
     const int tiles = (Nw + 255) / 256;
@@ -620,7 +731,7 @@ static int launch_gemv_tc(tb_ctx* ctx, const void* x, const void* w, const Epi& 
         attr[1].val.programmaticStreamSerializationAllowed = 1;
         lc.numAttrs = 2;
     }
-    TB_CUDA_TRY(ctx, cudaLaunchKernelEx(&lc, kern, tw, tx, ep, Nw, K, Mtok, kb_per, ctx->d_err));
+    TB_CUDA_TRY(ctx, cudaLaunchKernelEx(&lc, kern, tw, tx, e2, Nw, K, Mtok, kb_per, ctx->d_err));
     return check_launch(ctx, "gemv_tc");
 }
 
@@ -634,6 +745,12 @@ static int dispatch_gemv(tb_ctx* ctx, const void* x, const void* w, const Epi& e
 }
 
 int linear_launch(tb_ctx* ctx, int int8, const void* x, const void* w, const Epi& ep, int M, int N, int K) {
+    if (ep.norm_w || (ep.x_ld && ep.x_ld != K)) {
+        if (M > 64 || K % 8 || ep.x_ld % 8 || (reinterpret_cast<uintptr_t>(x) & 15) ||
+            (reinterpret_cast<uintptr_t>(ep.norm_w) & 15))
+            return set_error(ctx, TB_ERR_UNSUPPORTED,
+                             "linear: fused norm / strided rows need <= 64 tokens, K and row stride %% 8, 16-B alignment");
+    }
     if (int8) {
         if (M > 64) return set_error(ctx, TB_ERR_UNSUPPORTED, "int8 linear: at most 64 tokens");
         return dispatch_gemv<true>(ctx, x, w, ep, M, N, K);

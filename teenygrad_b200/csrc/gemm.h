@@ -17,6 +17,12 @@ struct Epi {
     const float* scale;    // int8 per-output-channel scale, or null
     int out_f32;           // y is f32
     int swiglu;            // gate/up interleaved in 128-row blocks
+    int64_t x_ld;          // row stride of x in elements (0: dense, = K)
+    // Optional RMSNorm of x fused into the decode GEMV (tokens <= 64): the
+    // GEMV consumes bf16(x * rsqrt(mean(x^2) + eps) * norm_w) instead of x.
+    const void* norm_w;    // bf16 [K] or null
+    float norm_eps;
+    const void* norm_x;    // (set by the launcher) the raw rows x
 };
 
 // y = epilogue(x[M,K] w[N,K]^T).  int8 = 1: w is int8 with ep.scale (M <= 64).
