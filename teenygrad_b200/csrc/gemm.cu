@@ -7,13 +7,16 @@
 //    (bias, residual, SwiGLU, bf16/f32 store) straight out of TMEM.
 //  * gemv_tc_kernel: decode-sized M (<= 64 tokens).  Swap-AB: the weight rows
 //    are the MMA's M dimension (two 128-row halves per CTA), the tokens its N.
-//    K is split across CTAs; the last CTA of a tile reduces the partials and
-//    runs the epilogue.  Weights are bf16, or int8 converted to bf16 in shared
-//    memory by six converter warps (exact: |q| <= 127).
+//    K is split across the CTAs of a thread-block cluster (up to 16), which
+//    exchange their partials over DSMEM; each CTA finishes a slice of the
+//    rows.  Weights are bf16, or int8 converted to bf16 in shared memory by
+//    six converter warps (exact: |q| <= 127).  An RMSNorm of the activations
+//    can be fused in front.
 //  * linear_f32_kernel / matmul_f32_kernel: exact-f32 CUDA-core tiles for the
 //    fp32 configurations (the reference's TF32 dot, linear.rs:86, misses the
 //    1e-4 fp32 tolerance at K >= 256).
 #include <algorithm>
+#include <atomic>
 
 #include "common.cuh"
 #include "gemm.h"
@@ -228,7 +231,7 @@ struct GemvCfg {
     static constexpr int C_STAGES = INT8 ? 2 : 0;                 // converted bf16 ring
     static constexpr int C_BYTES = 256 * 128;
     // send + receive partials (reuse the rings); each owner slice carries NT sums of squares
-    static constexpr int RED_BYTES = 2 * (NT * 256 + 8 * NT) * 4;
+    static constexpr int RED_BYTES = 2 * (NT * 256 + 16 * NT) * 4;
     static constexpr int RING = STAGES * (W_BYTES + X_BYTES) + C_STAGES * C_BYTES;
     static constexpr int SMEM = (RING > RED_BYTES ? RING : RED_BYTES) + 1024 + 512;
     static constexpr int TMEM_COLS = (2 * NT) < 32 ? 32 : (2 * NT);
@@ -680,10 +683,13 @@ static int launch_gemm_tc(tb_ctx* ctx, const void* a, const void* b, const Epi& 
 
 // Cluster size (K splits per weight tile): the largest of 8, 4, 2, 1 that
 // keeps the grid within two CTAs per SM and every split >= 2 K-blocks.
-static void gemv_split(int num_sms, int Nw, int K, int* splits_out, int* kb_per_out) {
+// Split-K factor: the largest power of two <= max_cs that keeps the grid
+// within two CTAs per SM (the second slot lets the next kernel's CTAs start
+// streaming their weights early) and gives every CTA at least two K-blocks.
+static void gemv_split(int num_sms, int max_cs, int Nw, int K, int* splits_out, int* kb_per_out) {
     const int tiles = (Nw + 255) / 256;
     const int nk = (K + 63) / 64;
-    int cs = 8;
+    int cs = max_cs;
     while (cs > 1 && (tiles * cs > 2 * num_sms || nk < 2 * cs)) cs >>= 1;
     int kb_per = (nk + cs - 1) / cs;
     *splits_out = cs;
@@ -709,10 +715,32 @@ static int launch_gemv_tc(tb_ctx* ctx, const void* x, const void* w, const Epi& 
     Epi e2 = ep;
     e2.x_ld = ep.x_ld ? ep.x_ld : K;
     e2.norm_x = x;
-    int cs, kb_per;
-    gemv_split(ctx->num_sms, Nw, K, &cs, &kb_per);
-    const int tiles = (Nw + 255) / 256;
     auto kern = gemv_tc_kernel<NT, STAGES, INT8>;
+    // bf16: clusters of 16 (non-portable) when the device can co-schedule them,
+    // else 8.  int8 (one CTA per SM, converter-bound) is fastest at 8.
+    static std::atomic<int> max_cs{INT8 ? 8 : 0};
+    if (max_cs.load() == 0) {
+        TB_CUDA_TRY(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+        int n = 0;
+        cudaLaunchConfig_t q = {};
+        q.gridDim = dim3(1, 16, 1);
+        q.blockDim = dim3(256, 1, 1);
+        q.dynamicSmemBytes = C::SMEM;
+        cudaLaunchAttribute qa[1];
+        qa[0].id = cudaLaunchAttributeClusterDimension;
+        qa[0].val.clusterDim.x = 1;
+        qa[0].val.clusterDim.y = 16;
+        qa[0].val.clusterDim.z = 1;
+        q.attrs = qa;
+        q.numAttrs = 1;
+        const bool ok16 = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess &&
+                          cudaOccupancyMaxActiveClusters(&n, kern, &q) == cudaSuccess && n >= 1;
+        cudaGetLastError();
+        max_cs.store(ok16 ? 16 : 8);
+    }
+    int cs, kb_per;
+    gemv_split(ctx->num_sms, max_cs.load(), Nw, K, &cs, &kb_per);
+    const int tiles = (Nw + 255) / 256;
     TB_CUDA_TRY(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     cudaLaunchConfig_t lc = {};
     lc.gridDim = dim3(tiles, cs, 1);
