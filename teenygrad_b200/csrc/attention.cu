@@ -275,25 +275,31 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
 // -------------------------------------------------------------- decode -----
 // Decode attention against the KV cache on tcgen05 (few queries, long
 // context).  One CTA per (batch, kv head, split); the G = Hq / Hkv query heads
-// that share the kv head are padded to 16 rows.  Per 128-key tile:
-//   S^T = K_tile Q^T      (M = 128 keys, N = 16 query rows, K = D)  -> TMEM
-//   softmax               (thread t of warps 2-5 <-> key t: one TMEM lane)
-//   O  += P V_tile        (M = 128 rows, of which the first G are the queries,
-//                          N = D, K = 128 keys; P in a zero-padded smem tile,
-//                          V as the MN-major operand)               -> TMEM
-// Warp 0 streams K/V tiles with TMA (2-stage ring), warp 1 issues the MMAs.
-// The online softmax keeps per-query (max, sum) in registers of every
-// softmax thread (tile reductions over shuffles + shared memory).  Splits of
-// one group form a cluster and merge (max, sum, o) over DSMEM in fixed order.
+// that share the kv head are the queries.  Per 128-key tile j:
+//   S^T = K_j Q^T   (M = 128 keys, N = 16 query rows, K = D)   -> TMEM S[j & 1]
+//   softmax         (thread t of warps 2-5 <-> key t: one TMEM lane)
+//   O  += P_j V_j   (M = 128, N = D, K = 128 keys)              -> TMEM O
+// P_j holds 8 query rows x 128 keys (2 KB, double-buffered); its descriptor
+// repeats those 8 rows over the MMA's 128 (row-group stride 0), and only O
+// rows 0..G-1 are read back.  Roles: warp 0 streams K tiles and warp 6 V
+// tiles (TMA, NS-stage rings), warp 1 issues the S MMAs and warp 7 the P V
+// MMAs, so S_{j+1} never queues behind P V_j.  The softmax keeps a reference
+// max per query that is raised (and O and the row sums rescaled) only when a
+// tile's max exceeds it by more than 8 in log2 units; otherwise
+// P = 2^(s - m) <= 256 is used as is and no wait on P V_{j-1} is needed.
+// Row sums stay per thread until the end.  Splits of one group form a
+// cluster and merge (max, sum, o) over DSMEM in a fixed order.
 template <int D>
 struct DecTcCfg {
+    static constexpr int NS = D == 64 ? 3 : 2;          // K / V ring stages
     static constexpr int TILE = 128 * D * 2;            // K or V tile bytes
-    static constexpr int P_BYTES = 128 * 128 * 2;       // [128 rows][128 keys] bf16, rows >= G zero
+    static constexpr int P_BYTES = 2048;                // [8 rows][128 keys] bf16: two 64-key atoms
     static constexpr int Q_BYTES = 16 * D * 2;          // [16 rows][D] bf16, rows >= G zero
     static constexpr int PART = 8 * (D + 2) * 4;        // merge partial (max, sum, o) per query
-    static constexpr int SMEM = 4 * TILE + P_BYTES + (Q_BYTES < 1024 ? 1024 : Q_BYTES) + PART + 1024 + 512;
+    static constexpr int SMEM = 2 * NS * TILE + 2 * P_BYTES + Q_BYTES + PART + 1024 + 1024;
     static constexpr int O_COL = 32;                    // TMEM: S^T buffers at 0 and 16, O at 32
     static constexpr int TMEM_COLS = (32 + D) <= 128 ? 128 : 256;
+    static constexpr float RESCALE_LOG2 = 8.f;          // raise the reference max past this margin
 };
 
 __device__ __forceinline__ void dec_cluster_sync() {
@@ -308,15 +314,16 @@ __device__ __forceinline__ float dec_ld_dsmem(uint32_t local_addr, uint32_t rank
     return v;
 }
 
+// Named barrier over the 128 softmax threads.  After a timed-out wait the
+// softmax loop still runs to its end (every later wait returns at once), so
+// all four warps always reach the same barriers.
 __device__ __forceinline__ void softmax_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
-// Barrier over the 128 softmax threads that also ANDs `v` across them: every
-// softmax warp takes the same branch after a bounded wait, so none is left
-// waiting at a named barrier that the others skipped.
-__device__ __forceinline__ bool softmax_bar_and(bool v) {
+// The same barrier, returning whether `v` holds for any of the 128 threads.
+__device__ __forceinline__ bool softmax_bar_or(bool v) {
     uint32_t r;
     asm volatile(
-        "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred q, 1, 128, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+        "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.or.pred q, 1, 128, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
         : "=r"(r)
         : "r"((uint32_t)v)
         : "memory");
@@ -324,24 +331,27 @@ __device__ __forceinline__ bool softmax_bar_and(bool v) {
 }
 
 template <int D>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(256, D == 64 ? 2 : 1)
 attn_decode_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                       DecodeArgs a, int* err) {
     using C = DecTcCfg<D>;
-    constexpr int DB = D / 64;
+    constexpr int NS = C::NS, DB = D / 64;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* sK = smem;                        // [2 stages]
-    uint8_t* sV = sK + 2 * C::TILE;            // [2 stages]
-    uint8_t* sP = sV + 2 * C::TILE;
-    uint8_t* sQ = sP + C::P_BYTES;
-    float* spart = reinterpret_cast<float*>(sQ + (C::Q_BYTES < 1024 ? 1024 : C::Q_BYTES));   // [8][D+2]
+    uint8_t* sK = smem;                        // [NS] K tiles
+    uint8_t* sV = sK + NS * C::TILE;           // [NS] V tiles
+    uint8_t* sP = sV + NS * C::TILE;           // [2] P tiles
+    uint8_t* sQ = sP + 2 * C::P_BYTES;
+    float* spart = reinterpret_cast<float*>(sQ + C::Q_BYTES);   // [8][D+2]
     uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(spart) + C::PART);
-    const uint32_t k_full0 = smem_u32(bars + 0), v_full0 = smem_u32(bars + 2), kv_empty0 = smem_u32(bars + 4);
-    const uint32_t s_full0 = smem_u32(bars + 6), p_full = smem_u32(bars + 8), o_done = smem_u32(bars + 9);
-    const uint32_t q_full = smem_u32(bars + 10);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
-    float* sred = reinterpret_cast<float*>(bars + 12);      // [2][4 warps][8 queries]
+    const uint32_t k_full0 = smem_u32(bars), v_full0 = smem_u32(bars + NS);
+    const uint32_t k_empty0 = smem_u32(bars + 2 * NS), v_empty0 = smem_u32(bars + 3 * NS);
+    const uint32_t s_full0 = smem_u32(bars + 4 * NS), s_free0 = smem_u32(bars + 4 * NS + 2);
+    const uint32_t p_full0 = smem_u32(bars + 4 * NS + 4), p_free0 = smem_u32(bars + 4 * NS + 6);
+    const uint32_t q_full = smem_u32(bars + 4 * NS + 8);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4 * NS + 9);
+    float* sred = reinterpret_cast<float*>(bars + 4 * NS + 10);   // [2 tiles][4 warps][8 queries]
+    float* ssum = sred + 64;                                       // [4 warps][8 queries]
 
     pdl_trigger();
     const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
@@ -350,15 +360,19 @@ attn_decode_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_cons
     const int b = bg / a.Hkv, g = bg % a.Hkv;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < 2; s++) {
+        for (int s = 0; s < NS; s++) {
             mbar_init(k_full0 + 8 * s, 1);
             mbar_init(v_full0 + 8 * s, 1);
-            mbar_init(kv_empty0 + 8 * s, 1);
-            mbar_init(s_full0 + 8 * s, 1);
+            mbar_init(k_empty0 + 8 * s, 1);
+            mbar_init(v_empty0 + 8 * s, 1);
         }
-        mbar_init(p_full, 128);
-        mbar_init(o_done, 1);
-        mbar_init(q_full, 128);
+        for (int s = 0; s < 2; s++) {
+            mbar_init(s_full0 + 8 * s, 1);
+            mbar_init(s_free0 + 8 * s, 4);
+            mbar_init(p_full0 + 8 * s, 4);
+            mbar_init(p_free0 + 8 * s, 1);
+        }
+        mbar_init(q_full, 4);
         fence_barrier_init();
     }
     if (warp == 1) tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
@@ -373,62 +387,70 @@ attn_decode_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_cons
     const int n_tiles = kend > kbeg ? (kend - kbeg + 127) / 128 : 0;
     const int64_t row0 = ((int64_t)b * a.Hkv + g) * a.kv_rows;   // first cache row of this group
 
-    if (warp == 0) {
+    if (warp == 0 || warp == 6) {
+        // ---------------- producers: warp 0 K tiles, warp 6 V tiles
         if (lane == 0 && n_tiles > 0) {
-            tma_prefetch_desc(&tmK);
-            tma_prefetch_desc(&tmV);
+            const bool isK = warp == 0;
+            const CUtensorMap* tm = isK ? &tmK : &tmV;
+            uint8_t* ring = isK ? sK : sV;
+            const uint32_t full0 = isK ? k_full0 : v_full0, empty0 = isK ? k_empty0 : v_empty0;
+            tma_prefetch_desc(tm);
             int issued = 0;
             for (int j = 0; j < n_tiles; j++) {
-                const int st = j & 1;
-                if (j >= 2 && !mbar_wait(kv_empty0 + 8 * st, ((j >> 1) - 1) & 1, err, DEV_ERR_TIMEOUT_EMPTY)) break;
+                const int st = j % NS;
+                if (j >= NS && !mbar_wait(empty0 + 8 * st, ((j / NS) - 1) & 1, err, DEV_ERR_TIMEOUT_EMPTY)) break;
                 const int r = (int)(row0 + kbeg + 128 * j);
-                mbar_expect_tx(k_full0 + 8 * st, C::TILE);
-                for (int d = 0; d < DB; d++) tma_load_2d(smem_u32(sK + st * C::TILE + d * 16384), &tmK, k_full0 + 8 * st, 64 * d, r);
-                mbar_expect_tx(v_full0 + 8 * st, C::TILE);
-                for (int d = 0; d < DB; d++) tma_load_2d(smem_u32(sV + st * C::TILE + d * 16384), &tmV, v_full0 + 8 * st, 64 * d, r);
+                mbar_expect_tx(full0 + 8 * st, C::TILE);
+                for (int d = 0; d < DB; d++) tma_load_2d(smem_u32(ring + st * C::TILE + d * 16384), tm, full0 + 8 * st, 64 * d, r);
                 issued = j + 1;
             }
-            for (int j = (issued > 2 ? issued - 2 : 0); j < issued; j++) {
-                mbar_wait(k_full0 + 8 * (j & 1), (j >> 1) & 1, err, DEV_ERR_TIMEOUT_FULL);
-                mbar_wait(v_full0 + 8 * (j & 1), (j >> 1) & 1, err, DEV_ERR_TIMEOUT_FULL);
-            }
+            // every load this CTA issued has landed before it can exit
+            for (int j = (issued > NS ? issued - NS : 0); j < issued; j++)
+                mbar_wait(full0 + 8 * (j % NS), (j / NS) & 1, err, DEV_ERR_TIMEOUT_FULL);
         }
     } else if (warp == 1) {
+        // ---------------- S^T = K Q^T issuer
         if (lane == 0 && n_tiles > 0) {
             constexpr uint32_t idesc_s = idesc_bf16_f32(128, 16, false, false);
-            constexpr uint32_t idesc_o = idesc_bf16_f32(128, D, false, true);
-            const uint32_t q_base = smem_u32(sQ), p_base = smem_u32(sP);
+            const uint32_t q_base = smem_u32(sQ);
             bool ok = mbar_wait(q_full, 0, err, DEV_ERR_TIMEOUT_MISC);
-            for (int j = 0; ok && j <= n_tiles; j++) {
-                if (j < n_tiles) {
-                    const int st = j & 1;
-                    if (!mbar_wait(k_full0 + 8 * st, (j >> 1) & 1, err, DEV_ERR_TIMEOUT_FULL)) break;
-                    tc_fence_after();
-                    const uint32_t k_base = smem_u32(sK + st * C::TILE);
+            for (int j = 0; ok && j < n_tiles; j++) {
+                const int st = j % NS, sb = j & 1;
+                if (!mbar_wait(k_full0 + 8 * st, (j / NS) & 1, err, DEV_ERR_TIMEOUT_FULL)) break;
+                if (j >= 2 && !mbar_wait(s_free0 + 8 * sb, ((j - 2) >> 1) & 1, err, DEV_ERR_TIMEOUT_MISC)) break;
+                tc_fence_after();
+                const uint32_t k_base = smem_u32(sK + st * C::TILE);
 #pragma unroll
-                    for (int kk = 0; kk < D / 16; kk++) {
-                        const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-                        const uint32_t qoff = (kk >> 2) * 2048 + (kk & 3) * 32;
-                        umma_f16_ss(tmem + st * 16, sdesc_sw128(k_base + off, 16, 1024), sdesc_sw128(q_base + qoff, 16, 1024),
-                                    idesc_s, kk != 0);
-                    }
-                    umma_commit(s_full0 + 8 * st);
+                for (int kk = 0; kk < D / 16; kk++) {
+                    const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+                    const uint32_t qoff = (kk >> 2) * 2048 + (kk & 3) * 32;
+                    umma_f16_ss(tmem + sb * 16, sdesc_sw128(k_base + off, 16, 1024), sdesc_sw128(q_base + qoff, 16, 1024),
+                                idesc_s, kk != 0);
                 }
-                if (j > 0) {
-                    const int jp = j - 1, st = jp & 1;
-                    if (!mbar_wait(p_full, jp & 1, err, DEV_ERR_TIMEOUT_MISC)) break;
-                    if (!mbar_wait(v_full0 + 8 * st, (jp >> 1) & 1, err, DEV_ERR_TIMEOUT_FULL)) break;
-                    tc_fence_after();
-                    const uint32_t v_base = smem_u32(sV + st * C::TILE);
+                umma_commit(k_empty0 + 8 * st);
+                umma_commit(s_full0 + 8 * sb);
+            }
+        }
+    } else if (warp == 7) {
+        // ---------------- O += P V issuer
+        if (lane == 0 && n_tiles > 0) {
+            constexpr uint32_t idesc_o = idesc_bf16_f32(128, D, false, true);
+            const uint32_t p_base = smem_u32(sP);
+            for (int j = 0; j < n_tiles; j++) {
+                const int st = j % NS, pb = j & 1;
+                if (!mbar_wait(p_full0 + 8 * pb, (j >> 1) & 1, err, DEV_ERR_TIMEOUT_MISC)) break;
+                if (!mbar_wait(v_full0 + 8 * st, (j / NS) & 1, err, DEV_ERR_TIMEOUT_FULL)) break;
+                tc_fence_after();
+                const uint32_t v_base = smem_u32(sV + st * C::TILE);
 #pragma unroll
-                    for (int kk = 0; kk < 8; kk++) {
-                        const uint64_t ad = sdesc_sw128(p_base + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
-                        const uint64_t bd = sdesc_sw128(v_base + kk * 16 * 128, 16384, 1024);
-                        umma_f16_ss(tmem + C::O_COL, ad, bd, idesc_o, (jp | kk) != 0);
-                    }
-                    umma_commit(kv_empty0 + 8 * st);
-                    umma_commit(o_done);
+                for (int kk = 0; kk < 8; kk++) {
+                    // 8 P rows repeated over the 128 MMA rows: row-group stride 0
+                    const uint64_t ad = sdesc_sw128(p_base + pb * C::P_BYTES + (kk >> 2) * 1024 + (kk & 3) * 32, 16, 0);
+                    const uint64_t bd = sdesc_sw128(v_base + kk * 16 * 128, 16384, 1024);
+                    umma_f16_ss(tmem + C::O_COL, ad, bd, idesc_o, (j | kk) != 0);
                 }
+                umma_commit(v_empty0 + 8 * st);
+                umma_commit(p_free0 + 8 * pb);
             }
         }
     } else {
@@ -438,7 +460,7 @@ attn_decode_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_cons
         const int kr = quarter * 32 + lane;               // key row within the tile
         const int tid = threadIdx.x - 64;                 // 0..127
         const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
-        // Q -> smem [16 rows][D], 128-B swizzle, rows >= G zero; P tile -> zero
+        // Q -> smem [16 rows][D], 128-B swizzle, rows >= G zero; both P tiles -> zero
         for (int i = tid; i < 16 * (D / 8); i += 128) {
             const int r = i / (D / 8), c = i % (D / 8);   // row, 16-byte chunk
             uint4 v = make_uint4(0, 0, 0, 0);
@@ -446,104 +468,133 @@ attn_decode_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_cons
             const int cc = c & 7, atom = c >> 3;
             *reinterpret_cast<uint4*>(sQ + atom * 2048 + r * 128 + ((cc ^ (r & 7)) << 4)) = v;
         }
-        for (int i = tid; i < C::P_BYTES / 16; i += 128) reinterpret_cast<uint4*>(sP)[i] = make_uint4(0, 0, 0, 0);
+        for (int i = tid; i < 2 * C::P_BYTES / 16; i += 128) reinterpret_cast<uint4*>(sP)[i] = make_uint4(0, 0, 0, 0);
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        mbar_arrive(q_full);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(q_full);
 
-        float m_run[8], l_run[8];
+        float m_ref[8], lsum[8];
 #pragma unroll
         for (int q = 0; q < 8; q++) {
-            m_run[q] = -INFINITY;
-            l_run[q] = 0.f;
+            m_ref[q] = -INFINITY;
+            lsum[q] = 0.f;
         }
         bool ok = true;
         for (int j = 0; j < n_tiles; j++) {
             const int sb = j & 1;
-            ok = softmax_bar_and(mbar_wait(s_full0 + 8 * sb, (j >> 1) & 1, err, DEV_ERR_TIMEOUT_MISC));
-            if (!ok) break;
+            ok = mbar_wait(s_full0 + 8 * sb, (j >> 1) & 1, err, DEV_ERR_TIMEOUT_MISC) && ok;
             tc_fence_after();
-            float s[16];
-            tmem_ld16(t_lane + sb * 16, s);
+            float s[8];
+            tmem_ld8(t_lane + sb * 16, s);
             tmem_wait_ld();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(s_free0 + 8 * sb);   // S buffer sb may be overwritten
             const bool valid = kbeg + 128 * j + kr < kend;
-            // tile max per query
+            bool over = false;   // a score of this thread passes its query's reference max by the margin
 #pragma unroll
             for (int q = 0; q < 8; q++) {
                 s[q] = (valid && q < G) ? s[q] * a.scale_log2 : -INFINITY;
-                float m = s[q];
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-                if (lane == 0) sred[sw * 8 + q] = m;
+                over |= s[q] > m_ref[q] + C::RESCALE_LOG2;
             }
-            softmax_bar();
-            float alpha[8], p[8];
+            // Common case: no score passes the margin, one barrier and no max
+            // reduction.  Otherwise (always on the first tile) reduce the tile max
+            // per query and raise the reference max where it passes the margin.
+            float alpha[8];
+            bool any = false;
 #pragma unroll
-            for (int q = 0; q < 8; q++) {
-                const float tm = fmaxf(fmaxf(sred[q], sred[8 + q]), fmaxf(sred[16 + q], sred[24 + q]));
-                const float m_new = fmaxf(m_run[q], tm);
-                const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-                alpha[q] = ex2(m_run[q] - m_use);
-                p[q] = ex2(s[q] - m_use);
-                m_run[q] = m_new;
-                float sum = p[q];
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-                if (lane == 0) sred[32 + sw * 8 + q] = sum;
-            }
-            softmax_bar();
-#pragma unroll
-            for (int q = 0; q < 8; q++)
-                l_run[q] = l_run[q] * alpha[q] + (sred[32 + q] + sred[40 + q] + sred[48 + q] + sred[56 + q]);
-            if (j > 0) {
-                ok = softmax_bar_and(mbar_wait(o_done, (j - 1) & 1, err, DEV_ERR_TIMEOUT_MISC));
-                if (!ok) break;
-                tc_fence_after();
-                // rescale the O rows (queries 0..G-1 = TMEM lanes 0..G-1, lane quarter 0: warp 4)
-                if (quarter == 0) {
-                    float my_alpha = 1.f;
-#pragma unroll
-                    for (int q = 0; q < 8; q++)
-                        if (lane == q && q < G) my_alpha = alpha[q];
-                    if (__any_sync(0xffffffffu, my_alpha != 1.0f)) {
-#pragma unroll 1
-                        for (int c = 0; c < D; c += 16) {
-                            float o[16];
-                            tmem_ld16(t_lane + C::O_COL + c, o);
-                            tmem_wait_ld();
-#pragma unroll
-                            for (int i = 0; i < 16; i++) o[i] *= my_alpha;
-                            tmem_st16(t_lane + C::O_COL + c, o);
-                        }
-                        tmem_wait_st();
-                    }
-                }
-            }
-            // P[q][key] (bf16) into the swizzled K-major tile: row q, key column kr
-            {
-                const int atom = kr >> 6, kc = kr & 63;
+            for (int q = 0; q < 8; q++) alpha[q] = 1.f;
+            if (softmax_bar_or(over)) {
+                float* red = sred + sb * 32;
 #pragma unroll
                 for (int q = 0; q < 8; q++) {
                     if (q < G) {
-                        uint8_t* rowp = sP + atom * 16384 + q * 128;
-                        const int chunk = (kc >> 3) ^ (q & 7);
-                        *reinterpret_cast<__nv_bfloat16*>(rowp + chunk * 16 + (kc & 7) * 2) = __float2bfloat16_rn(p[q]);
+                        float m = s[q];
+#pragma unroll
+                        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+                        if (lane == 0) red[sw * 8 + q] = m;
+                    }
+                }
+                softmax_bar();
+#pragma unroll
+                for (int q = 0; q < 8; q++) {
+                    if (q < G) {
+                        const float tm = fmaxf(fmaxf(red[q], red[8 + q]), fmaxf(red[16 + q], red[24 + q]));
+                        if (tm > m_ref[q] + C::RESCALE_LOG2) {
+                            alpha[q] = ex2(m_ref[q] - tm);   // m_ref = -inf -> 0
+                            m_ref[q] = tm;
+                            lsum[q] *= alpha[q];
+                            any = true;
+                        }
                     }
                 }
             }
+            if (any && j > 0 && quarter == 0) {
+                // O holds P V of tiles < j: rescale rows 0..G-1 once P V_{j-1} is done
+                ok = mbar_wait(p_free0 + 8 * ((j - 1) & 1), ((j - 1) >> 1) & 1, err, DEV_ERR_TIMEOUT_MISC) && ok;
+                tc_fence_after();
+                float my_alpha = 1.f;
+#pragma unroll
+                for (int q = 0; q < 8; q++)
+                    if (lane == q) my_alpha = alpha[q];
+#pragma unroll 1
+                for (int c = 0; c < D; c += 16) {
+                    float o[16];
+                    tmem_ld16(t_lane + C::O_COL + c, o);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 16; i++) o[i] *= my_alpha;
+                    tmem_st16(t_lane + C::O_COL + c, o);
+                }
+                tmem_wait_st();
+            }
+            float p[8];
+#pragma unroll
+            for (int q = 0; q < 8; q++) {
+                p[q] = q < G ? ex2(s[q] - m_ref[q]) : 0.f;   // s = -inf -> 0
+                lsum[q] += p[q];
+            }
+            // P_j (bf16) into the swizzled K-major tile: row q, key column kr; the
+            // buffer is free once P V_{j-2} is done
+            const int pb = j & 1;
+            if (j >= 2) ok = mbar_wait(p_free0 + 8 * pb, ((j - 2) >> 1) & 1, err, DEV_ERR_TIMEOUT_MISC) && ok;
+            {
+                uint8_t* pt = sP + pb * C::P_BYTES + (kr >> 6) * 1024;
+                const int kc = kr & 63;
+#pragma unroll
+                for (int q = 0; q < 8; q++)
+                    if (q < G)
+                        *reinterpret_cast<__nv_bfloat16*>(pt + q * 128 + (((kc >> 3) ^ q) << 4) + (kc & 7) * 2) =
+                            __float2bfloat16_rn(p[q]);
+            }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             tc_fence_before();
-            mbar_arrive(p_full);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(p_full0 + 8 * pb);
         }
-        if (ok && n_tiles > 0) ok = __all_sync(0xffffffffu, mbar_wait(o_done, (n_tiles - 1) & 1, err, DEV_ERR_TIMEOUT_ACC));
+        // row sums over the 128 key threads
+#pragma unroll
+        for (int q = 0; q < 8; q++) {
+            if (q < G) {
+                float v = lsum[q];
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                if (lane == 0) ssum[sw * 8 + q] = v;
+            }
+        }
+        softmax_bar();
         // partial (max, sum, unnormalised o) of this split: warp 4 (TMEM quarter 0), lanes < G
         if (quarter == 0) {
+            if (n_tiles > 0)
+                ok = mbar_wait(p_free0 + 8 * ((n_tiles - 1) & 1), ((n_tiles - 1) >> 1) & 1, err, DEV_ERR_TIMEOUT_ACC) && ok;
+            ok = __all_sync(0xffffffffu, ok);
             tc_fence_after();
             float my_m = -INFINITY, my_l = 0.f;
 #pragma unroll
             for (int q = 0; q < 8; q++)
-                if (lane == q) {
-                    my_m = m_run[q];
-                    my_l = l_run[q];
+                if (lane == q && q < G) {
+                    my_m = m_ref[q];
+                    my_l = ssum[q] + ssum[8 + q] + ssum[16 + q] + ssum[24 + q];
                 }
 #pragma unroll 1
             for (int c = 0; c < D; c += 16) {
@@ -572,7 +623,7 @@ attn_decode_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_cons
     // ---- merge the splits (cluster over blockIdx.y) and write O / LSE
     if (nsp > 1) dec_cluster_sync();
     const int DS = D / nsp;                               // dims merged by this CTA per query
-    for (int i = threadIdx.x; i < G * DS; i += 192) {
+    for (int i = threadIdx.x; i < G * DS; i += 256) {
         const int q = i / DS, d = split * DS + i % DS;
         float M = -INFINITY, l = 0.f, o = 0.f;
         if (nsp == 1) {
@@ -707,7 +758,7 @@ int attn_decode_launch(tb_ctx* ctx, DecodeArgs a, int B, int D, int max_len) {
     if (rc) return rc;
     cudaLaunchConfig_t lc = {};
     lc.gridDim = dim3(groups, nsp, 1);
-    lc.blockDim = dim3(192, 1, 1);
+    lc.blockDim = dim3(256, 1, 1);
     lc.stream = ctx->stream;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
