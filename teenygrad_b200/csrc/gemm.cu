@@ -230,8 +230,8 @@ struct GemvCfg {
     static constexpr int X_BYTES = NT * 128;
     static constexpr int C_STAGES = INT8 ? 2 : 0;                 // converted bf16 ring
     static constexpr int C_BYTES = 256 * 128;
-    // send + receive partials (reuse the rings); each owner slice carries NT sums of squares
-    static constexpr int RED_BYTES = 2 * (NT * 256 + 16 * NT) * 4;
+    // received partials (reuse the rings): CS slots of NT * 256 / CS values + NT sums of squares
+    static constexpr int RED_BYTES = (NT * 256 + 16 * NT) * 4;
     static constexpr int RING = STAGES * (W_BYTES + X_BYTES) + C_STAGES * C_BYTES;
     static constexpr int SMEM = (RING > RED_BYTES ? RING : RED_BYTES) + 1024 + 512;
     static constexpr int TMEM_COLS = (2 * NT) < 32 ? 32 : (2 * NT);
@@ -537,54 +537,63 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
         }
         return;
     }
-    // Rank r of the cluster owns row pairs [r*P, (r+1)*P), P = 128 / CS.  Each
-    // CTA lays its partial out per owner (send[owner][m][pair][2]), then one
-    // thread sends every other owner its slice with a DSMEM bulk copy into
-    // the owner's receive slot [my rank], completing on the owner's mbarrier.
+    // Rank r of the cluster owns row pairs [r*P, (r+1)*P), P = 128 / CS, and
+    // receives every peer's partial of them into receive slot [peer rank]
+    // (layout [token][pair][2]) of its own ring area.  Each thread pushes its
+    // TP tokens of one row pair straight from registers with st.async, which
+    // completes on the owner's mbarrier; its own slot is written locally.
     // Owners sum the CS slots in rank order (deterministic).  The split
     // cluster barrier guarantees a peer's rings are idle before it is written.
-    // With the norm fused, every slice also carries the sender's NT partial sums of
-    // squares; each owner adds them in rank order to form 1 / rms.
+    // With the norm fused, every slot also carries the sender's NT partial sums
+    // of squares; each owner adds them in rank order to form 1 / rms.
     {
         const int P = 128 / CS;
-        const int PF = NT * P * 2;                         // partial floats per owner
-        const int SF = PF + NT;                            // slice floats (+ sums of squares)
-        const int SLICE = SF * 4;                          // bytes per owner
-        float* sendb = red;
-        float* recvf = red + CS * SF;
+        const int PF = NT * P * 2;                         // partial floats per slot, [token][pair][2]
+        const int SF = PF + NT;                            // slot floats (+ sums of squares)
+        float* recvf = red;
         const int owner = l / P, pl = l % P;
-#pragma unroll
-        for (int t = 0; t < TP; t++) {
-            const int m = part * TP + t;
-            float* dst = sendb + owner * SF + (m * P + pl) * 2;
-            dst[0] = acc[0][t];
-            dst[1] = acc[1][t];
-        }
-        if (NORM)
-            for (int it = threadIdx.x; it < CS * NT; it += 256) sendb[(it / NT) * SF + PF + it % NT] = s_ss[it % NT];
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        __syncthreads();
+        if (threadIdx.x == 0) mbar_expect_tx(recvb, (uint32_t)((CS - 1) * (PF + (NORM ? NT : 0)) * 4));
         asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");   // all peers' rings are free
-        if (threadIdx.x == 0) {
-            mbar_expect_tx(recvb, (uint32_t)((CS - 1) * SLICE));
-            const uint32_t send0 = smem_u32(sendb), recv0 = smem_u32(recvf);
-            for (int r = 0; r < CS; r++) {
-                if (r == split) continue;
+        {
+            const int off = split * SF + (part * TP * P + pl) * 2;   // token part * TP, pair pl
+            if (owner == split) {
+#pragma unroll
+                for (int t = 0; t < TP; t++)
+                    *reinterpret_cast<float2*>(recvf + off + t * P * 2) = make_float2(acc[0][t], acc[1][t]);
+            } else {
                 uint32_t rdst, rbar;
-                asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rdst) : "r"(recv0 + split * SLICE), "r"(r));
-                asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rbar) : "r"(recvb), "r"(r));
-                asm volatile(
-                    "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(rdst),
-                    "r"(send0 + r * SLICE), "r"(SLICE), "r"(rbar)
-                    : "memory");
+                asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rdst) : "r"(smem_u32(recvf + off)), "r"(owner));
+                asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rbar) : "r"(recvb), "r"(owner));
+#pragma unroll
+                for (int t = 0; t < TP; t++)
+                    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(
+                                     rdst + t * P * 8),
+                                 "f"(acc[0][t]), "f"(acc[1][t]), "r"(rbar)
+                                 : "memory");
             }
-            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        }
+        if (NORM) {
+            for (int it = threadIdx.x; it < CS * NT; it += 256) {
+                const int r = it / NT, m = it % NT;
+                const uint32_t dst = smem_u32(recvf + split * SF + PF + m);
+                if (r == split) {
+                    recvf[split * SF + PF + m] = s_ss[m];
+                } else {
+                    uint32_t rdst, rbar;
+                    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rdst) : "r"(dst), "r"(r));
+                    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rbar) : "r"(recvb), "r"(r));
+                    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.f32 [%0], %1, [%2];" ::"r"(rdst),
+                                 "f"(s_ss[m]), "r"(rbar)
+                                 : "memory");
+                }
+            }
         }
         const bool got = __all_sync(0xffffffffu, mbar_wait(recvb, 0, err, DEV_ERR_TIMEOUT_MISC));
+        __syncthreads();   // the local slot, written by other threads
         if (NORM) {
             if (threadIdx.x < NT) {
                 float t = 0.f;
-                for (int r = 0; r < CS; r++) t += (r == split ? sendb + split * SF : recvf + r * SF)[PF + threadIdx.x];
+                for (int r = 0; r < CS; r++) t += recvf[r * SF + PF + threadIdx.x];
                 s_ss[threadIdx.x] = rsqrtf(t * inv_k + ep.norm_eps);
             }
             __syncthreads();
@@ -594,14 +603,12 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
             const int m = it / P, pl2 = it % P;
             float a0 = 0.f, a1 = 0.f;
             for (int r = 0; r < CS; r++) {
-                const float* src = (r == split ? sendb + split * SF : recvf + r * SF) + (m * P + pl2) * 2;
-                const float2 v = *reinterpret_cast<const float2*>(src);
+                const float2 v = *reinterpret_cast<const float2*>(recvf + r * SF + (m * P + pl2) * 2);
                 a0 += v.x;
                 a1 += v.y;
             }
             if (ok && got && m < Mtok) finish(m, split * P + pl2, a0, a1);
         }
-        if (threadIdx.x == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");   // own sends have read smem
     }
 }
 
