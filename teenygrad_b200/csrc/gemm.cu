@@ -592,8 +592,12 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
         __syncthreads();   // the local slot, written by other threads
         if (NORM) {
             if (threadIdx.x < NT) {
+                float v[16];   // all loads in flight, then a fixed-order sum
+#pragma unroll
+                for (int r = 0; r < 16; r++) v[r] = r < CS ? recvf[r * SF + PF + threadIdx.x] : 0.f;
                 float t = 0.f;
-                for (int r = 0; r < CS; r++) t += recvf[r * SF + PF + threadIdx.x];
+#pragma unroll
+                for (int r = 0; r < 16; r++) t += v[r];
                 s_ss[threadIdx.x] = rsqrtf(t * inv_k + ep.norm_eps);
             }
             __syncthreads();
@@ -601,11 +605,15 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
         const int items = P * NT;
         for (int it = threadIdx.x; it < items; it += 256) {
             const int m = it / P, pl2 = it % P;
+            float2 v[16];   // all loads in flight, then a fixed-order sum
+#pragma unroll
+            for (int r = 0; r < 16; r++)
+                v[r] = r < CS ? *reinterpret_cast<const float2*>(recvf + r * SF + (m * P + pl2) * 2) : make_float2(0.f, 0.f);
             float a0 = 0.f, a1 = 0.f;
-            for (int r = 0; r < CS; r++) {
-                const float2 v = *reinterpret_cast<const float2*>(recvf + r * SF + (m * P + pl2) * 2);
-                a0 += v.x;
-                a1 += v.y;
+#pragma unroll
+            for (int r = 0; r < 16; r++) {
+                a0 += v[r].x;
+                a1 += v[r].y;
             }
             if (ok && got && m < Mtok) finish(m, split * P + pl2, a0, a1);
         }
