@@ -357,8 +357,12 @@ def run_c4(args, rank, world, local):
                  "decode_gemv_ms_per_step": round(gemv_ms, 4)}
     if comm is not None:
         comm.close()
-    launches_prefill = 1 + 8 * c["n_layers"] + 3 + 2
-    launches_decode = 1 + 8 * c["n_layers"] + 3 + 1
+    # prefill: set_state, embedding, per layer (rmsnorm, QKV GEMM, rope_kv, attention,
+    # O GEMM, rmsnorm, gate/up GEMM, down GEMM), LM-head GEMV (norm fused), argmax, advance.
+    # decode: embedding, per layer (QKV GEMV with norm + RoPE + KV-cache write fused,
+    # attention, O GEMV, gate/up GEMV with norm fused, down GEMV), LM head, argmax, advance.
+    launches_prefill = 2 + 8 * c["n_layers"] + 3
+    launches_decode = 1 + 5 * c["n_layers"] + 3
     launches = launches_prefill + (G - 1) * launches_decode
     res = {
         "metric": "tokens/s (1B decoder)", "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,

@@ -11,14 +11,16 @@
 namespace tb {
 
 // ------------------------------------------------------------------ kernels --
-// src row i -> dst row (row_off + (i / block) * block_stride + i % block).
+// src row i -> dst row (row_off + (i / block) * block_stride + i % block),
+// then (perm_hd != 0) through the QKV row permutation of head_dim perm_hd.
 __global__ void convert_rows_kernel(const void* __restrict__ src, int src_f32, __nv_bfloat16* __restrict__ dst,
                                     int64_t rows, int64_t cols, int64_t row_off, int64_t block,
-                                    int64_t block_stride) {
+                                    int64_t block_stride, int perm_hd) {
     int64_t total = rows * cols;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
         int64_t r = i / cols, c = i % cols;
         int64_t dr = row_off + (r / block) * block_stride + (r % block);
+        if (perm_hd) dr = qkv_perm_row(dr, perm_hd);
         float v = src_f32 ? reinterpret_cast<const float*>(src)[i]
                           : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(src)[i]);
         dst[dr * cols + c] = __float2bfloat16_rn(v);
@@ -285,6 +287,9 @@ struct tb_decoder {
     tb_ctx* ctx = nullptr;
     tb_decoder_config cfg{};
     int q_dim = 0, kv_dim = 0, qkv_n = 0;
+    // qkv_n % 256 == 0: the QKV weight rows are stored permuted (qkv_perm_row)
+    // so that decode applies RoPE and fills the KV cache in the GEMV epilogue.
+    bool qkv_perm = false;
     int64_t max_tokens = 0;
     struct Layer {
         bf16 *attn_norm, *mlp_norm, *wqkv, *wo, *wgu, *wdown;
@@ -343,8 +348,9 @@ struct PdlScope {
     } while (0)
 
 int lin(tb_decoder* d, const void* x, const void* w, const int8_t* wq, const float* wscale, void* y, int M, int N,
-        int K, const void* resid, bool swiglu, bool out_f32) {
+        int K, const void* resid, bool swiglu, bool out_f32, int perm_hd = 0) {
     Epi ep{};
+    ep.perm_hd = perm_hd;
     ep.out = y;
     ep.ldo = swiglu ? N / 2 : N;
     ep.resid = resid;
@@ -367,13 +373,13 @@ int rms(tb_decoder* d, const bf16* x, int64_t ldx, const bf16* w, bf16* y, int M
 // normalised rows never reach HBM; larger token counts normalise into d->h and
 // run the tensor-core GEMM.
 int norm_lin(tb_decoder* d, const bf16* x, int64_t ldx, const bf16* norm_w, const void* w, const int8_t* wq,
-             const float* wscale, void* y, int M, int N, bool swiglu, bool out_f32) {
+             const float* wscale, void* y, int M, int N, bool swiglu, bool out_f32, const Epi* qkv = nullptr) {
     const int K = d->cfg.d_model;
     if (M > 64) {
         TB_TRY(rms(d, x, ldx, norm_w, d->h, M));
-        return lin(d, d->h, w, wq, wscale, y, M, N, K, nullptr, swiglu, out_f32);
+        return lin(d, d->h, w, wq, wscale, y, M, N, K, nullptr, swiglu, out_f32, qkv ? qkv->perm_hd : 0);
     }
-    Epi ep{};
+    Epi ep = qkv ? *qkv : Epi{};
     ep.out = y;
     ep.ldo = swiglu ? N / 2 : N;
     ep.ldr = N;
@@ -398,8 +404,25 @@ int layer_forward(tb_decoder* d, int l, int B, int S_new, bool decode) {
     bf16* kc = d->kcache + (int64_t)l * d->cache_layer_elems;
     bf16* vc = d->vcache + (int64_t)l * d->cache_layer_elems;
 
-    TB_TRY(norm_lin(d, d->x, dm, L.attn_norm, L.wqkv, L.qqkv, L.sqkv, d->qkv, T, d->qkv_n, false, false));
-    {
+    // QKV projection.  With permuted QKV weights and <= 64 tokens (the decode
+    // GEMV) RoPE and the KV-cache writes happen in the GEMV epilogue; otherwise
+    // the projection is written in natural order and rope_kv follows.
+    const bool fused_rope = d->qkv_perm && T <= 64;
+    Epi qe{};
+    if (d->qkv_perm) qe.perm_hd = hd;
+    if (fused_rope) {
+        qe.rope_tab = d->rope_tab;
+        qe.rope_hq = c.n_heads;
+        qe.rope_hkv = c.n_kv_heads;
+        qe.rope_s_new = S_new;
+        qe.pos_ptr = decode ? d->state : nullptr;
+        qe.pos_host = 0;
+        qe.kcache = kc;
+        qe.vcache = vc;
+        qe.max_seq = c.max_seq;
+    }
+    TB_TRY(norm_lin(d, d->x, dm, L.attn_norm, L.wqkv, L.qqkv, L.sqkv, d->qkv, T, d->qkv_n, false, false, &qe));
+    if (!fused_rope) {
         const int64_t work = (int64_t)T * (c.n_heads + 2 * c.n_kv_heads) * (hd / 16);
         TB_TRY(launch(ctx, "rope_kv", rope_kv_kernel, dim3(grid_for(ctx, work)), dim3(256), 0, d->qkv, d->qkv_n, B,
                       S_new, c.n_heads, c.n_kv_heads, hd, (const float2*)d->rope_tab,
@@ -527,6 +550,7 @@ int tb_decoder_create(tb_ctx* ctx, const tb_decoder_config* cfg, tb_decoder** ou
     d->q_dim = c.n_heads * c.head_dim;
     d->kv_dim = c.n_kv_heads * c.head_dim;
     d->qkv_n = d->q_dim + 2 * d->kv_dim;
+    d->qkv_perm = d->qkv_n % 256 == 0;
     d->max_tokens = c.max_prefill_tokens > 0 ? c.max_prefill_tokens : (int64_t)c.max_batch * c.max_seq;
     if (d->max_tokens < c.max_batch) d->max_tokens = c.max_batch;
     const int64_t dm = c.d_model, F = c.ffn_hidden, V = c.vocab;
@@ -646,8 +670,10 @@ int tb_decoder_set_param(tb_decoder* d, int layer, int kind, const void* src, in
         TB_CUDA_TRY(ctx, cudaMemcpyAsync(staging, src, bytes, cudaMemcpyHostToDevice, ctx->stream));
         dsrc = staging;
     }
+    const bool qkv = kind == TB_P_WQ || kind == TB_P_WK || kind == TB_P_WV;
     convert_rows_kernel<<<grid_for(ctx, rows * cols), 256, 0, ctx->stream>>>(dsrc, src_dtype == TB_F32, dst, rows, cols,
-                                                                            row_off, block, bstride);
+                                                                            row_off, block, bstride,
+                                                                            qkv && d->qkv_perm ? c.head_dim : 0);
     int rc = check_launch(ctx, "set_param");
     if (staging) {
         cudaStreamSynchronize(ctx->stream);

@@ -180,7 +180,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 #pragma unroll
                                 for (int i = 0; i < 8; i++) v[j + i] += r[i];
                             }
-                            store_row8(ep.out, f32o, (int64_t)row * ep.ldo + col, v + j);
+                            const int64_t ocol = ep.perm_hd ? qkv_unperm_row(col, ep.perm_hd) : col;
+                            store_row8(ep.out, f32o, (int64_t)row * ep.ldo + ocol, v + j);
                         }
                     }
                 }
@@ -501,6 +502,42 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
             a0 *= s_ss[m];   // 1 / rms of token m
             a1 *= s_ss[m];
         }
+        if (ep.rope_tab) {
+            // (a0, a1) = dims (i, i + hd/2) of head slot H; the projection is rounded
+            // to bf16 first, as the unfused path stores it, then rotated (rotate-half)
+            const int hd = ep.perm_hd, hh = hd / 2;
+            const int H = tile * (256 / hd) + p / hh, i = p % hh;
+            if (H >= ep.rope_hq + 2 * ep.rope_hkv) return;
+            const int b = m / ep.rope_s_new, s = m % ep.rope_s_new;
+            const int pos = (ep.pos_ptr ? *ep.pos_ptr : ep.pos_host) + s;
+            if (pos < 0 || pos >= ep.max_seq) {
+                atomicOr(err, 1 << 5);
+                return;
+            }
+            if (ep.scale) {
+                a0 *= ep.scale[n0];
+                a1 *= ep.scale[n1];
+            }
+            float x0 = __bfloat162float(__float2bfloat16_rn(a0)), x1 = __bfloat162float(__float2bfloat16_rn(a1));
+            __nv_bfloat16* dst;
+            if (H < ep.rope_hq + ep.rope_hkv) {
+                const float2 cs = ep.rope_tab[(int64_t)pos * hh + i];
+                const float y0 = x0 * cs.x - x1 * cs.y, y1 = x1 * cs.x + x0 * cs.y;
+                x0 = y0;
+                x1 = y1;
+            }
+            if (H < ep.rope_hq)
+                dst = reinterpret_cast<__nv_bfloat16*>(ep.out) + (int64_t)m * ep.ldo + (int64_t)H * hd;
+            else if (H < ep.rope_hq + ep.rope_hkv)
+                dst = reinterpret_cast<__nv_bfloat16*>(ep.kcache) +
+                      (((int64_t)b * ep.rope_hkv + (H - ep.rope_hq)) * ep.max_seq + pos) * hd;
+            else
+                dst = reinterpret_cast<__nv_bfloat16*>(ep.vcache) +
+                      (((int64_t)b * ep.rope_hkv + (H - ep.rope_hq - ep.rope_hkv)) * ep.max_seq + pos) * hd;
+            dst[i] = __float2bfloat16_rn(x0);
+            dst[i + hh] = __float2bfloat16_rn(x1);
+            return;
+        }
         if (ep.swiglu) {
             if (n1 < Nw) {
                 float sg = ep.scale ? ep.scale[n0] : 1.f, su = ep.scale ? ep.scale[n1] : 1.f;
@@ -788,6 +825,11 @@ static int dispatch_gemv(tb_ctx* ctx, const void* x, const void* w, const Epi& e
 }
 
 int linear_launch(tb_ctx* ctx, int int8, const void* x, const void* w, const Epi& ep, int M, int N, int K) {
+    if (ep.perm_hd) {
+        if ((ep.perm_hd != 64 && ep.perm_hd != 128) || N % 256 || ep.bias || ep.resid || ep.swiglu || ep.out_f32 ||
+            (ep.rope_tab && (M > 64 || ep.rope_s_new <= 0)) || (!ep.rope_tab && (M <= 64 || int8)))
+            return set_error(ctx, TB_ERR_UNSUPPORTED, "linear: permuted QKV epilogue configuration");
+    }
     if (ep.norm_w || (ep.x_ld && ep.x_ld != K)) {
         if (M > 64 || K % 8 || ep.x_ld % 8 || (reinterpret_cast<uintptr_t>(x) & 15) ||
             (reinterpret_cast<uintptr_t>(ep.norm_w) & 15))

@@ -30,10 +30,14 @@ def check_tokens(got, logits_ref):
     assert np.array_equal(np.asarray(got)[sure], ref[sure])
 
 
-@pytest.mark.parametrize("S", [70, 129])
-def test_decoder_prefill_and_decode_bf16(S):
+# S = 20: 40 prompt tokens take the decode GEMV (RoPE and KV-cache writes in its
+# epilogue); S = 70, 129: the tensor-core GEMM and the separate RoPE kernel.
+# n_heads = 5, n_kv_heads = 1: q+k+v rows (448) are not a multiple of 256, so the
+# QKV weights stay unpermuted and decode uses the separate RoPE kernel too.
+@pytest.mark.parametrize("S,heads", [(20, (4, 2)), (70, (4, 2)), (129, (4, 2)), (20, (5, 1)), (70, (5, 1))])
+def test_decoder_prefill_and_decode_bf16(S, heads):
     dev()
-    cfg = SmallCfg()
+    cfg = SmallCfg(n_heads=heads[0], n_kv_heads=heads[1])
     p = random_params(cfg, seed=3)
     dec = make(cfg)
     upload(dec, p)
