@@ -4,14 +4,9 @@
 //  * bf16: implicit GEMM on tcgen05.  The input is first transposed to NHWC
 //    with channels padded to a multiple of 8 (caller workspace), the weights
 //    reordered to [Cout][KH][KW][Cin_pad].  GEMM view: M = output pixels,
-//    N = Cout, K = KH * KW * Cin_pad.  One CTA computes a tile of 16 x 8
-//    output pixels (rows h, columns w) x 64 output channels; each K-block is
-//    one filter tap (kh, kw) x 64 input channels, fetched by a 4-D TMA box
-//    (64 channels, 8 columns, 16 rows, 1 image) whose column / row coordinates
-//    are shifted by the tap and may be negative: out-of-range positions read
-//    as zero, which is exactly the convolution's zero padding.  The epilogue
-//    stages the tile in shared memory as [channel][row][column] and writes it
-//    to NCHW with one TMA store.  Unit stride, OW % 8 == 0.
+//    N = Cout, K = KH * KW * Cin_pad.  A persistent kernel computes tiles of
+//    16 x 8 output pixels x 64 output channels (see conv_tc_kernel).  Unit
+//    stride, OW % 8 == 0, KH <= 7, KW <= 9.
 //  * CUDA cores: implicit GEMM with exact f32 FMA accumulation, for f32 I/O
 //    (the reference's fp32 kernels, conv2d.rs:44-148 / :643-764, and its 1e-4
 //    tolerance) and for the bf16 shapes the tensor-core path does not take.
@@ -37,27 +32,64 @@ __device__ __forceinline__ float conv_epi(const ConvEpi& e, int co, float v) {
 
 // ------------------------------------------------------------ layout prep --
 // x [B][C][H][W] (f32 or bf16) -> xn [B][H][W][Cp] bf16, channels >= C zero.
+// One CTA per (image row, 64 columns, 64 channels): 16-byte loads along w
+// into a shared [channel][column] tile (when rows are 16-byte aligned), then
+// 16-byte stores of 8 channels of one pixel.
 template <typename T>
-__global__ void nchw_to_nhwc_kernel(const T* __restrict__ x, __nv_bfloat16* __restrict__ xn, int B, int C, int H,
-                                    int W, int Cp) {
-    __shared__ float tile[32][33];
-    const int bh = blockIdx.z;          // b * H + h
+__global__ void __launch_bounds__(256)
+nchw_to_nhwc_kernel(const T* __restrict__ x, __nv_bfloat16* __restrict__ xn, int B, int C, int H, int W, int Cp) {
+    constexpr int V = 16 / sizeof(T);     // elements per 16-byte load
+    __shared__ __nv_bfloat16 tile[64][64 + 2];
+    pdl_trigger();
+    pdl_wait();
+    const int bh = blockIdx.z;            // b * H + h
     const int b = bh / H, h = bh % H;
-    const int c0 = blockIdx.y * 32, w0 = blockIdx.x * 32;
-    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
-        const int c = c0 + i, w = w0 + threadIdx.x;
-        float v = 0.f;
-        if (c < C && w < W) {
-            const T* p = x + (((int64_t)b * C + c) * H + h) * W + w;
-            if constexpr (sizeof(T) == 4) v = *p;
-            else v = __bfloat162float(*p);
+    const int w0 = blockIdx.x * 64, c0 = blockIdx.y * 64;
+    const bool vec = (W % V) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+    for (int i = threadIdx.x; i < 64 * (64 / V); i += 256) {
+        const int c = i / (64 / V), wv = (i % (64 / V)) * V;
+        const int gc = c0 + c, gw = w0 + wv;
+        const T* row = x + (((int64_t)b * C + gc) * H + h) * W;
+        float v[V];
+        if (gc < C && vec && gw + V <= W) {
+            if constexpr (sizeof(T) == 4) {
+                const float4 f = *reinterpret_cast<const float4*>(row + gw);
+                v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
+            } else {
+                const uint4 u = *reinterpret_cast<const uint4*>(row + gw);
+                const uint32_t a[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    v[2 * k] = bf16_lo(a[k]);
+                    v[2 * k + 1] = bf16_hi(a[k]);
+                }
+            }
+        } else {
+#pragma unroll
+            for (int k = 0; k < V; k++) {
+                float t = 0.f;
+                if (gc < C && gw + k < W) {
+                    if constexpr (sizeof(T) == 4) t = row[gw + k];
+                    else t = __bfloat162float(row[gw + k]);
+                }
+                v[k] = t;
+            }
         }
-        tile[i][threadIdx.x] = v;
+#pragma unroll
+        for (int k = 0; k < V; k++) tile[c][wv + k] = __float2bfloat16_rn(v[k]);
     }
     __syncthreads();
-    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
-        const int w = w0 + i, c = c0 + threadIdx.x;
-        if (w < W && c < Cp) xn[(((int64_t)b * H + h) * W + w) * Cp + c] = __float2bfloat16_rn(tile[threadIdx.x][i]);
+    for (int i = threadIdx.x; i < 64 * 8; i += 256) {
+        const int w = i / 8, cg = (i % 8) * 8;
+        const int gw = w0 + w, gc = c0 + cg;
+        if (gw >= W || gc >= Cp) continue;
+        uint32_t o[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const __nv_bfloat16 lo = tile[cg + 2 * k][w], hi = tile[cg + 2 * k + 1][w];
+            o[k] = (uint32_t)__bfloat16_as_ushort(lo) | ((uint32_t)__bfloat16_as_ushort(hi) << 16);
+        }
+        *reinterpret_cast<uint4*>(xn + (((int64_t)b * H + h) * W + gw) * Cp + gc) = make_uint4(o[0], o[1], o[2], o[3]);
     }
 }
 
@@ -84,116 +116,279 @@ __global__ void reorder_weights_kernel(const T* __restrict__ w, __nv_bfloat16* _
 }
 
 // ---------------------------------------------------------- tcgen05 conv --
-constexpr int CONV_BH = 16, CONV_BW = 8, CONV_BN = 64, CONV_STAGES = 6;
-constexpr int CONV_A_BYTES = 128 * 128;            // 128 pixels x 64 channels
-constexpr int CONV_B_BYTES = CONV_BN * 128;        // 64 couts x 64 channels
+// Persistent implicit GEMM: one CTA per SM loops over output tiles of
+// 16 x 8 pixels x 64 output channels.  Per tile and 64-channel input chunk,
+// ONE TMA load brings the haloed input patch [16 + KH - 1 rows][16 columns]
+// [64 channels] (NHWC, 128-B swizzle, zero fill outside the image = the
+// convolution's padding); every filter tap (kh, kw) is then the MMA's A
+// operand read in place: start row kh * 16 + kw of the patch, 8-pixel row
+// groups 2 KB apart (the patch row pitch).  The 128-B swizzle is a function
+// of the absolute shared-memory address, so a start shifted by whole 128-B
+// rows reads the rows TMA wrote there (descriptor base offset 0).  Weight slices
+// [64 couts][64 channels] per (tap, chunk) are loaded once and stay resident
+// when they fit (each CTA then keeps one 64-channel output block), else they
+// stream through a ring.  The four 16-channel K-steps of a tap accumulate
+// into four TMEM accumulators (back-to-back MMAs on one accumulator wait for
+// each other), which the epilogue adds.  The f32
+// accumulator is double-buffered in TMEM so the epilogue of one tile (warps
+// 4-7: bias -> BN -> activation, staged as [channel][row][column] and written
+// to NCHW by a TMA store) overlaps the MMAs of the next.
+constexpr int CONV_BH = 16, CONV_BW = 8, CONV_BN = 64;
+constexpr int CONV_PW = 16;                        // patch columns (>= 8 + KW - 1)
+constexpr int CONV_WS = 4;                         // weight slice stages
+constexpr int CONV_W_BYTES = CONV_BN * 128;        // 64 couts x 64 channels
 constexpr int CONV_OUT_BYTES = CONV_BN * 128 * 2;  // [64][16][8] bf16
-constexpr int CONV_SMEM = CONV_STAGES * (CONV_A_BYTES + CONV_B_BYTES) + CONV_OUT_BYTES + 1024 + 256;
+// Consecutive MMAs into one accumulator serialise on it; K-steps rotate over
+// CONV_NACC accumulators (summed in the epilogue) so they overlap.
+constexpr int CONV_NACC = 4;
+constexpr int CONV_TMEM = 2 * CONV_NACC * CONV_BN;  // double-buffered: 512 columns
 
-__device__ __forceinline__ void tma_store_4d(const CUtensorMap* m, uint32_t src, int c0, int c1, int c2, int c3) {
+__host__ __device__ constexpr int conv_patch_bytes(int KH) { return (CONV_BH + KH - 1) * CONV_PW * 128; }
+// wslots: weight slices held in shared memory (all of them when resident, else the ring)
+__host__ __device__ constexpr int conv_smem_bytes(int KH, int AS, int wslots) {
+    return AS * conv_patch_bytes(KH) + wslots * CONV_W_BYTES + 2 * CONV_OUT_BYTES + CONV_BN * 16 + 1024 + 256;
+}
+
+__device__ __forceinline__ void tma_store_4d_async(const CUtensorMap* m, uint32_t src, int c0, int c1, int c2, int c3) {
     asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
                      reinterpret_cast<uint64_t>(m)),
                  "r"(src), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
                  : "memory");
     asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
 
-// grid: (tiles_w * tiles_h * B, ceil(Cout / 64))
+// Shapes the tensor-core path takes: unit stride, output rows of 16-byte
+// multiples (the NCHW TMA store), filter taps inside the 16-column patch.
+struct ConvShape;
+bool conv_tc_ok(const ConvShape& s, int stride, int KH, int KW);
+
 __global__ void __launch_bounds__(256, 1)
 conv_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
-               const __grid_constant__ CUtensorMap tmY, ConvEpi ep, int OH, int OW, int Cout, int KH, int KW,
-               int Cp, int stride, int pad, int* err) {
+               const __grid_constant__ CUtensorMap tmY, ConvEpi ep, int B, int OH, int OW, int Cout, int KH, int KW,
+               int Cp, int pad, int AS, int wres, int* err) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int a_bytes = conv_patch_bytes(KH);
+    const int nc = (Cp + 63) / 64;            // 64-channel chunks
+    const int taps = KH * KW;
+    const int wslots = wres ? taps * nc : CONV_WS;
     uint8_t* sA = smem;
-    uint8_t* sB = sA + CONV_STAGES * CONV_A_BYTES;
-    __nv_bfloat16* sO = reinterpret_cast<__nv_bfloat16*>(sB + CONV_STAGES * CONV_B_BYTES);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(sO) + CONV_OUT_BYTES);
-    const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + CONV_STAGES), accb = smem_u32(bars + 2 * CONV_STAGES);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * CONV_STAGES + 1);
+    uint8_t* sW = sA + AS * a_bytes;
+    uint8_t* sO = sW + wslots * CONV_W_BYTES;                  // [2] output staging
+    float4* sEpi = reinterpret_cast<float4*>(sO + 2 * CONV_OUT_BYTES);   // [64] (bias, scale, shift, -)
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sO + 2 * CONV_OUT_BYTES + CONV_BN * 16);
+    // a_full[AS<=4], a_empty[4], w_full[WS], w_empty[WS], acc_full[2], acc_empty[2]
+    const uint32_t a_full0 = smem_u32(bars), a_empty0 = smem_u32(bars + 4);
+    const uint32_t w_full0 = smem_u32(bars + 8), w_empty0 = smem_u32(bars + 8 + CONV_WS);
+    const uint32_t acc_full0 = smem_u32(bars + 8 + 2 * CONV_WS), acc_empty0 = smem_u32(bars + 10 + 2 * CONV_WS);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12 + 2 * CONV_WS);
 
     pdl_trigger();
-    pdl_wait();
     const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
     const int tiles_w = (OW + CONV_BW - 1) / CONV_BW, tiles_h = (OH + CONV_BH - 1) / CONV_BH;
-    int t = blockIdx.x;
-    const int tw = t % tiles_w;
-    t /= tiles_w;
-    const int th = t % tiles_h;
-    const int b = t / tiles_h;
-    const int ow0 = tw * CONV_BW, oh0 = th * CONV_BH, n0 = blockIdx.y * CONV_BN;
-    const int nc = (Cp + 63) / 64;            // 64-channel chunks per tap
-    const int nk = KH * KW * nc;
+    const int nN = (Cout + CONV_BN - 1) / CONV_BN;
+    const int units = tiles_w * tiles_h * B * nN;
+    auto tile_of = [&](int t, int& b, int& oh0, int& ow0, int& n0) {
+        n0 = (t % nN) * CONV_BN;
+        int p = t / nN;
+        ow0 = (p % tiles_w) * CONV_BW;
+        p /= tiles_w;
+        oh0 = (p % tiles_h) * CONV_BH;
+        b = p / tiles_h;
+    };
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < CONV_STAGES; s++) {
-            mbar_init(full0 + 8 * s, 1);
-            mbar_init(empty0 + 8 * s, 1);
+        for (int s = 0; s < AS; s++) {
+            mbar_init(a_full0 + 8 * s, 1);
+            mbar_init(a_empty0 + 8 * s, 1);
         }
-        mbar_init(accb, 1);
+        for (int s = 0; s < CONV_WS; s++) {
+            mbar_init(w_full0 + 8 * s, 1);
+            mbar_init(w_empty0 + 8 * s, 1);
+        }
+        for (int s = 0; s < 2; s++) {
+            mbar_init(acc_full0 + 8 * s, 1);
+            mbar_init(acc_empty0 + 8 * s, 4);
+        }
         fence_barrier_init();
     }
-    if (warp == 1) tmem_alloc(smem_u32(tmem_slot), CONV_BN);
+    if (warp == 1) tmem_alloc(smem_u32(tmem_slot), CONV_TMEM);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    pdl_wait();
 
-    if (warp == 0 && lane == 0) {
-        tma_prefetch_desc(&tmX);
-        tma_prefetch_desc(&tmW);
-        int issued = 0;
-        for (int kb = 0; kb < nk; kb++) {
-            const int s = kb % CONV_STAGES;
-            if (kb >= CONV_STAGES && !mbar_wait(empty0 + 8 * s, ((kb / CONV_STAGES) - 1) & 1, err, DEV_ERR_TIMEOUT_EMPTY)) break;
-            const int tap = kb / nc, c0 = (kb % nc) * 64;
-            const int kh = tap / KW, kw = tap % KW;
-            mbar_expect_tx(full0 + 8 * s, CONV_A_BYTES + CONV_B_BYTES);
-            tma_load_4d(smem_u32(sA + s * CONV_A_BYTES), &tmX, full0 + 8 * s, c0, ow0 * stride + kw - pad,
-                        oh0 * stride + kh - pad, b);
-            tma_load_2d(smem_u32(sB + s * CONV_B_BYTES), &tmW, full0 + 8 * s, tap * Cp + c0, n0);
-            issued = kb + 1;
+    if (warp == 0) {
+        // ---------------- producer: haloed input patch per (tile, chunk), weight slice per tap
+        if (lane == 0) {
+            tma_prefetch_desc(&tmX);
+            tma_prefetch_desc(&tmW);
+            int ai = 0, wi = 0;
+            bool ok = true;
+            if (wres && blockIdx.x < units) {
+                // every weight slice of this CTA's output block (grid % nN == 0: fixed block)
+                const int n0 = (blockIdx.x % nN) * CONV_BN;
+                mbar_expect_tx(w_full0, (uint32_t)(wslots * CONV_W_BYTES));
+                for (int k = 0; k < wslots; k++)
+                    tma_load_2d(smem_u32(sW + k * CONV_W_BYTES), &tmW, w_full0, (k % taps) * Cp + (k / taps) * 64, n0);
+            }
+            for (int t = blockIdx.x; ok && t < units; t += gridDim.x) {
+                int b, oh0, ow0, n0;
+                tile_of(t, b, oh0, ow0, n0);
+                for (int c = 0; ok && c < nc; c++) {
+                    const int sa = ai % AS;
+                    if (ai >= AS && !mbar_wait(a_empty0 + 8 * sa, ((ai / AS) - 1) & 1, err, DEV_ERR_TIMEOUT_EMPTY)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_expect_tx(a_full0 + 8 * sa, (uint32_t)a_bytes);
+                    tma_load_4d(smem_u32(sA + sa * a_bytes), &tmX, a_full0 + 8 * sa, c * 64, ow0 - pad, oh0 - pad, b);
+                    ai++;
+                    for (int tap = 0; !wres && tap < taps; tap++) {
+                        const int sw = wi % CONV_WS;
+                        if (wi >= CONV_WS &&
+                            !mbar_wait(w_empty0 + 8 * sw, ((wi / CONV_WS) - 1) & 1, err, DEV_ERR_TIMEOUT_EMPTY)) {
+                            ok = false;
+                            break;
+                        }
+                        mbar_expect_tx(w_full0 + 8 * sw, CONV_W_BYTES);
+                        tma_load_2d(smem_u32(sW + sw * CONV_W_BYTES), &tmW, w_full0 + 8 * sw, tap * Cp + c * 64, n0);
+                        wi++;
+                    }
+                }
+            }
+            // every load issued has landed before the CTA can exit
+            for (int k = (ai > AS ? ai - AS : 0); k < ai; k++)
+                mbar_wait(a_full0 + 8 * (k % AS), (k / AS) & 1, err, DEV_ERR_TIMEOUT_FULL);
+            for (int k = (wi > CONV_WS ? wi - CONV_WS : 0); k < wi; k++)
+                mbar_wait(w_full0 + 8 * (k % CONV_WS), (k / CONV_WS) & 1, err, DEV_ERR_TIMEOUT_FULL);
+            if (wres && blockIdx.x < units) mbar_wait(w_full0, 0, err, DEV_ERR_TIMEOUT_FULL);
         }
-        for (int kb = (issued > CONV_STAGES ? issued - CONV_STAGES : 0); kb < issued; kb++)
-            mbar_wait(full0 + 8 * (kb % CONV_STAGES), (kb / CONV_STAGES) & 1, err, DEV_ERR_TIMEOUT_FULL);
-    } else if (warp == 1 && lane == 0) {
-        constexpr uint32_t idesc = idesc_bf16_f32(128, CONV_BN, false, false);
-        for (int kb = 0; kb < nk; kb++) {
-            const int s = kb % CONV_STAGES;
-            if (!mbar_wait(full0 + 8 * s, (kb / CONV_STAGES) & 1, err, DEV_ERR_TIMEOUT_FULL)) break;
-            tc_fence_after();
-            const uint32_t a_base = smem_u32(sA + s * CONV_A_BYTES), b_base = smem_u32(sB + s * CONV_B_BYTES);
+    } else if (warp == 1) {
+        // ---------------- MMA issuer: taps read the patch in place
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_bf16_f32(128, CONV_BN, false, false);
+            // descriptors built once; an operand at byte offset o adds o >> 4 (start-address field)
+            const uint64_t a_desc0 = sdesc_sw128(smem_u32(sA), 16, CONV_PW * 128);
+            const uint64_t b_desc0 = sdesc_sw128(smem_u32(sW), 16, 1024);
+            int ai = 0, wi = 0, tl = 0;
+            bool ok = !wres || blockIdx.x >= units || mbar_wait(w_full0, 0, err, DEV_ERR_TIMEOUT_FULL);
+            for (int t = blockIdx.x; ok && t < units; t += gridDim.x, tl++) {
+                const int ab = tl & 1;
+                if (tl >= 2 && !mbar_wait(acc_empty0 + 8 * ab, ((tl >> 1) - 1) & 1, err, DEV_ERR_TIMEOUT_MISC)) break;
+                tc_fence_after();
+                for (int c = 0; ok && c < nc; c++) {
+                    const int sa = ai % AS;
+                    if (!mbar_wait(a_full0 + 8 * sa, (ai / AS) & 1, err, DEV_ERR_TIMEOUT_FULL)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint64_t a_st = a_desc0 + (uint64_t)((sa * a_bytes) >> 4);
+                    const uint32_t d_tmem = tmem + ab * (CONV_NACC * CONV_BN);
+                    for (int tap = 0, kh = 0, kw = 0; tap < taps; tap++) {
+                        const int sw = wres ? c * taps + tap : wi % CONV_WS;
+                        if (!wres && !mbar_wait(w_full0 + 8 * sw, (wi / CONV_WS) & 1, err, DEV_ERR_TIMEOUT_FULL)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint64_t a_tap = a_st + (uint64_t)((kh * CONV_PW + kw) * 8);   // rows of 128 B
+                        const uint64_t b_tap = b_desc0 + (uint64_t)(sw * (CONV_W_BYTES >> 4));
+                        // K-step kk of every tap goes to accumulator kk (CONV_NACC == 4)
 #pragma unroll
-            for (int kk = 0; kk < 4; kk++)
-                umma_f16_ss(tmem, sdesc_sw128(a_base + kk * 32, 16, 1024), sdesc_sw128(b_base + kk * 32, 16, 1024),
-                            idesc, (kb | kk) != 0);
-            umma_commit(empty0 + 8 * s);
+                        for (int kk = 0; kk < 4; kk++)
+                            umma_f16_ss(d_tmem + kk * CONV_BN, a_tap + 2 * kk, b_tap + 2 * kk, idesc, (c | tap) != 0);
+                        if (++kw == KW) {
+                            kw = 0;
+                            kh++;
+                        }
+                        if (!wres) {
+                            umma_commit(w_empty0 + 8 * sw);
+                            wi++;
+                        }
+                    }
+                    umma_commit(a_empty0 + 8 * sa);
+                    ai++;
+                }
+                umma_commit(acc_full0 + 8 * ab);
+            }
         }
-        umma_commit(accb);
+    } else if (warp >= 4) {
+        // ---------------- epilogue: thread <-> pixel row r = 32 * (warp % 4) + lane (h = r / 8, w = r % 8)
+        const int q = warp & 3, r = q * 32 + lane;
+        bool ok = true;
+        int tl = 0, cur_n0 = -1;
+        for (int t = blockIdx.x; t < units; t += gridDim.x, tl++) {
+            int b, oh0, ow0, n0;
+            tile_of(t, b, oh0, ow0, n0);
+            const int ab = tl & 1;
+            if (n0 != cur_n0) {
+                // per-channel (bias, scale, shift) of this output block -> shared memory
+                asm volatile("bar.sync 2, 128;" ::: "memory");   // previous block's values no longer read
+                if (threadIdx.x - 128 < CONV_BN) {
+                    const int co = n0 + (threadIdx.x - 128);
+                    float4 e = make_float4(0.f, 1.f, 0.f, 0.f);
+                    if (co < Cout) {
+                        if (ep.bias && !ep.shift) e.x = ep.bias[co];
+                        if (ep.scale) e.y = ep.scale[co];
+                        if (ep.shift) e.z = ep.shift[co];
+                    }
+                    sEpi[threadIdx.x - 128] = e;
+                }
+                asm volatile("bar.sync 2, 128;" ::: "memory");
+                cur_n0 = n0;
+            }
+            ok = mbar_wait(acc_full0 + 8 * ab, (tl >> 1) & 1, err, DEV_ERR_TIMEOUT_ACC) && ok;
+            tc_fence_after();
+            float v[64];
+            {
+                const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + ab * (CONV_NACC * CONV_BN);
+                tmem_ld32(tb, v);
+                tmem_ld32(tb + 32, v + 32);
+                tmem_wait_ld();
+#pragma unroll
+                for (int k = 1; k < CONV_NACC; k++) {
+                    float u[64];
+                    tmem_ld32(tb + k * CONV_BN, u);
+                    tmem_ld32(tb + k * CONV_BN + 32, u + 32);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int j = 0; j < 64; j++) v[j] += u[j];
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acc_empty0 + 8 * ab);
+            // staging buffer ab was last read by the store issued two tiles ago
+            if (warp == 4 && lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+            asm volatile("bar.sync 2, 128;" ::: "memory");
+            __nv_bfloat16* so = reinterpret_cast<__nv_bfloat16*>(sO + ab * CONV_OUT_BYTES);
+            // v -> ((v + bias) * scale + shift) -> activation, as conv_epi; 16 channels
+            // per batch of shared-memory reads
+#pragma unroll
+            for (int j0 = 0; j0 < 64; j0 += 16) {
+                float4 e[16];
+#pragma unroll
+                for (int j = 0; j < 16; j++) e[j] = sEpi[j0 + j];
+#pragma unroll
+                for (int j = 0; j < 16; j++) {
+                    float o = (v[j0 + j] + e[j].x) * e[j].y + e[j].z;
+                    if (ep.act == TB_ACT_RELU) o = o > 0.f ? o : 0.f;
+                    else if (ep.act == TB_ACT_SILU) o = o / (1.0f + expf(-o));
+                    so[(j0 + j) * 128 + r] = __float2bfloat16_rn(n0 + j0 + j < Cout ? o : 0.f);
+                }
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            asm volatile("bar.sync 2, 128;" ::: "memory");
+            if (warp == 4 && lane == 0 && ok) tma_store_4d_async(&tmY, smem_u32(so), ow0, oh0, n0, b);
+        }
+        if (warp == 4 && lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
     }
     __syncwarp();
-
-    // epilogue: thread <-> pixel row r = 32 * (warp % 4) + lane (h = r / 8, w = r % 8),
-    // warps 0-3 channels [0, 32), warps 4-7 channels [32, 64)
-    bool ok = __all_sync(0xffffffffu, mbar_wait(accb, 0, err, DEV_ERR_TIMEOUT_ACC));
-    tc_fence_after();
-    const int q = warp & 3, half = warp >> 2;
-    const int r = q * 32 + lane;
-    float v[32];
-    tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + half * 32, v);
-    tmem_wait_ld();
-#pragma unroll
-    for (int j = 0; j < 32; j++) {
-        const int co = n0 + half * 32 + j;
-        const float o = co < Cout ? conv_epi(ep, co, v[j]) : 0.f;
-        sO[(half * 32 + j) * 128 + r] = __float2bfloat16_rn(o);
-    }
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     tc_fence_before();
     __syncthreads();
-    if (warp == 1) tmem_dealloc(tmem, CONV_BN);
-    if (threadIdx.x == 0 && ok) tma_store_4d(&tmY, smem_u32(sO), ow0, oh0, n0, b);
+    if (warp == 1) tmem_dealloc(tmem, CONV_TMEM);
 }
 
 // ------------------------------------------------------------- f32 conv ---
@@ -306,6 +501,10 @@ static size_t conv_ws_bytes(const ConvShape& s) {
     return ((xn + 255) / 256) * 256 + ((wr + 255) / 256) * 256;
 }
 
+bool conv_tc_ok(const ConvShape& s, int stride, int KH, int KW) {
+    return stride == 1 && s.OW % 8 == 0 && KH <= 7 && KW <= CONV_PW - CONV_BW + 1;
+}
+
 static bool conv_shape(int B, int C, int Co, int H, int W, int KH, int KW, int stride, int pad, ConvShape* s) {
     if (B <= 0 || C <= 0 || Co <= 0 || H <= 0 || W <= 0 || KH <= 0 || KW <= 0 || stride <= 0 || pad < 0) return false;
     s->B = B; s->C = C; s->Co = Co; s->H = H; s->W = W; s->KH = KH; s->KW = KW; s->stride = stride; s->pad = pad;
@@ -326,7 +525,7 @@ int tb_conv2d_workspace_size(int dtype, int B, int Cin, int Cout, int H, int W, 
     if (!bytes) return TB_ERR_ARG;
     ConvShape s;
     if (!conv_shape(B, Cin, Cout, H, W, KH, KW, stride, pad, &s)) return TB_ERR_SHAPE;
-    *bytes = (dtype == TB_BF16 && stride == 1 && s.OW % 8 == 0) ? conv_ws_bytes(s) : 0;
+    *bytes = (dtype == TB_BF16 && conv_tc_ok(s, stride, KH, KW)) ? conv_ws_bytes(s) : 0;
     return TB_OK;
 }
 
@@ -344,7 +543,7 @@ int tb_conv2d_fwd(tb_ctx* ctx, int dtype, const void* x, const void* w, const fl
         return launch(ctx, "conv2d_f32", conv_simt_kernel<float>, sgrid, dim3(256), 0, (const float*)x, (const float*)w,
                       ep, (float*)y, B, Cin, Cout, H, W, KH, KW, stride, pad, s.OH, s.OW);
     if (dtype != TB_BF16) return set_error(ctx, TB_ERR_UNSUPPORTED, "conv2d: dtype %d", dtype);
-    if (stride != 1 || s.OW % 8 != 0)   // tensor-core path: unit stride, output rows of 16-byte multiples
+    if (!conv_tc_ok(s, stride, KH, KW))   // tensor-core path: see conv_tc_ok
         return launch(ctx, "conv2d_simt_bf16", conv_simt_kernel<__nv_bfloat16>, sgrid, dim3(256), 0,
                       (const __nv_bfloat16*)x, (const __nv_bfloat16*)w, ep, (__nv_bfloat16*)y, B, Cin, Cout, H, W, KH,
                       KW, stride, pad, s.OH, s.OW);
@@ -356,8 +555,8 @@ int tb_conv2d_fwd(tb_ctx* ctx, int dtype, const void* x, const void* w, const fl
     __nv_bfloat16* wr = reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<uint8_t*>(workspace) +
                                                          (((size_t)B * H * W * s.Cp * 2 + 255) / 256) * 256);
     {
-        dim3 grid((W + 31) / 32, (s.Cp + 31) / 32, B * H);
-        int rc = launch(ctx, "nchw_to_nhwc", nchw_to_nhwc_kernel<__nv_bfloat16>, grid, dim3(32, 8), 0,
+        dim3 grid((W + 63) / 64, (s.Cp + 63) / 64, B * H);
+        int rc = launch(ctx, "nchw_to_nhwc", nchw_to_nhwc_kernel<__nv_bfloat16>, grid, dim3(256), 0,
                         (const __nv_bfloat16*)x, xn, B, Cin, H, W, s.Cp);
         if (rc) return rc;
         const int64_t tot = (int64_t)Cout * KH * KW * s.Cp;
@@ -370,7 +569,7 @@ int tb_conv2d_fwd(tb_ctx* ctx, int dtype, const void* x, const void* w, const fl
     {
         uint64_t dims[4] = {(uint64_t)s.Cp, (uint64_t)W, (uint64_t)H, (uint64_t)B};
         uint64_t strides[3] = {(uint64_t)s.Cp * 2, (uint64_t)W * s.Cp * 2, (uint64_t)H * W * s.Cp * 2};
-        uint32_t box[4] = {64, CONV_BW, CONV_BH, 1};
+        uint32_t box[4] = {64, CONV_PW, (uint32_t)(CONV_BH + KH - 1), 1};
         cuuint32_t es[4] = {1, 1, 1, 1};
         int rc = make_tmap_strided(ctx, &mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, xn, dims, strides, box, es,
                                    CU_TENSOR_MAP_SWIZZLE_128B);
@@ -384,11 +583,22 @@ int tb_conv2d_fwd(tb_ctx* ctx, int dtype, const void* x, const void* w, const fl
         rc = make_tmap(ctx, &my, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, y, ydims, ystr, ybox, CU_TENSOR_MAP_SWIZZLE_NONE);
         if (rc) return rc;
     }
-    TB_CUDA_TRY(ctx, cudaFuncSetAttribute(conv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, CONV_SMEM));
-    const int tiles = ((s.OW + CONV_BW - 1) / CONV_BW) * ((s.OH + CONV_BH - 1) / CONV_BH) * B;
-    dim3 grid((unsigned)tiles, (unsigned)((Cout + CONV_BN - 1) / CONV_BN));
-    return launch(ctx, "conv_tc", conv_tc_kernel, grid, dim3(256), CONV_SMEM, mx, mw, my, ep, s.OH, s.OW, Cout, KH,
-                  KW, s.Cp, stride, pad, ctx->d_err);
+    // Resident weights (all taps x chunks of one 64-channel output block) when
+    // they fit beside two patch stages; otherwise a 4-slice weight ring.
+    constexpr int kSmemMax = 220 * 1024;
+    const int nN = (Cout + CONV_BN - 1) / CONV_BN;
+    const int wall = KH * KW * ((s.Cp + 63) / 64);
+    const int wres = conv_smem_bytes(KH, 2, wall) <= kSmemMax && nN <= ctx->num_sms ? 1 : 0;
+    const int wslots = wres ? wall : CONV_WS;
+    const int AS = conv_smem_bytes(KH, 3, wslots) <= kSmemMax ? 3 : 2;
+    const int smem = conv_smem_bytes(KH, AS, wslots);
+    TB_CUDA_TRY(ctx, cudaFuncSetAttribute(conv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    const int64_t units = (int64_t)((s.OW + CONV_BW - 1) / CONV_BW) * ((s.OH + CONV_BH - 1) / CONV_BH) * B * nN;
+    // resident weights: a grid that is a multiple of nN keeps each CTA on one output block
+    int grid = wres ? (ctx->num_sms / nN) * nN : ctx->num_sms;
+    if (units < grid) grid = (int)units;
+    return launch(ctx, "conv_tc", conv_tc_kernel, dim3(grid), dim3(256), smem, mx, mw, my, ep, B, s.OH, s.OW, Cout,
+                  KH, KW, s.Cp, pad, AS, wres, ctx->d_err);
 }
 
 int tb_bn_fold(tb_ctx* ctx, const float* gamma, const float* beta, const float* mean, const float* var,
