@@ -5,8 +5,8 @@
 //    with channels padded to a multiple of 8 (caller workspace), the weights
 //    reordered to [Cout][KH][KW][Cin_pad].  GEMM view: M = output pixels,
 //    N = Cout, K = KH * KW * Cin_pad.  A persistent kernel computes tiles of
-//    16 x 8 output pixels x 64 output channels (see conv_tc_kernel).  Unit
-//    stride, OW % 8 == 0, KH <= 7, KW <= 9.
+//    32 x 8 output pixels x 64 output channels (see conv_tc_kernel).  Unit
+//    stride, OW % 8 == 0, filters up to 5 x 5 (see conv_tc_ok).
 //  * CUDA cores: implicit GEMM with exact f32 FMA accumulation, for f32 I/O
 //    (the reference's fp32 kernels, conv2d.rs:44-148 / :643-764, and its 1e-4
 //    tolerance) and for the bf16 shapes the tensor-core path does not take.
@@ -116,37 +116,36 @@ __global__ void reorder_weights_kernel(const T* __restrict__ w, __nv_bfloat16* _
 }
 
 // ---------------------------------------------------------- tcgen05 conv --
-// Persistent implicit GEMM: one CTA per SM loops over output tiles of
-// 16 x 8 pixels x 64 output channels.  Per tile and 64-channel input chunk,
-// ONE TMA load brings the haloed input patch [16 + KH - 1 rows][16 columns]
-// [64 channels] (NHWC, 128-B swizzle, zero fill outside the image = the
-// convolution's padding); every filter tap (kh, kw) is then the MMA's A
-// operand read in place: start row kh * 16 + kw of the patch, 8-pixel row
-// groups 2 KB apart (the patch row pitch).  The 128-B swizzle is a function
-// of the absolute shared-memory address, so a start shifted by whole 128-B
-// rows reads the rows TMA wrote there (descriptor base offset 0).  Weight slices
-// [64 couts][64 channels] per (tap, chunk) are loaded once and stay resident
-// when they fit (each CTA then keeps one 64-channel output block), else they
-// stream through a ring.  The four 16-channel K-steps of a tap accumulate
-// into four TMEM accumulators (back-to-back MMAs on one accumulator wait for
-// each other), which the epilogue adds.  The f32
-// accumulator is double-buffered in TMEM so the epilogue of one tile (warps
-// 4-7: bias -> BN -> activation, staged as [channel][row][column] and written
-// to NCHW by a TMA store) overlaps the MMAs of the next.
-constexpr int CONV_BH = 16, CONV_BW = 8, CONV_BN = 64;
-constexpr int CONV_PW = 16;                        // patch columns (>= 8 + KW - 1)
-constexpr int CONV_WS = 4;                         // weight slice stages
-constexpr int CONV_W_BYTES = CONV_BN * 128;        // 64 couts x 64 channels
-constexpr int CONV_OUT_BYTES = CONV_BN * 128 * 2;  // [64][16][8] bf16
-// Consecutive MMAs into one accumulator serialise on it; K-steps rotate over
-// CONV_NACC accumulators (summed in the epilogue) so they overlap.
-constexpr int CONV_NACC = 4;
-constexpr int CONV_TMEM = 2 * CONV_NACC * CONV_BN;  // double-buffered: 512 columns
+// Persistent implicit GEMM for Y^T: output channels are the MMA's rows (A =
+// weights [64 couts][64 channels] of one tap and channel chunk), output
+// pixels its columns (B = a tile of 32 x 8 pixels).  A tcgen05.mma holds the
+// tensor pipe for about the same time whatever its N, so every instruction
+// carries N = 256 pixels; the M = 128 instruction also reads the 64 weight
+// rows that follow (next slice), which land in TMEM lanes 64-127 and are
+// never read.  Per tile and 64-channel chunk ONE TMA load brings the haloed
+// NHWC patch [32 + KH - 1 rows][8 + KW - 1 columns][64 channels] (128-B
+// swizzle; zero fill outside the image = the padding).  Tap (kh, kw) is the
+// B operand read in place: start patch row kh * PW + kw, 8-pixel groups one
+// patch row (PW * 128 B) apart; the swizzle is a function of the absolute
+// shared-memory address, so shifted starts read what TMA wrote (descriptor
+// base offset 0).  Weights stay resident when they fit, else stream through
+// a ring.  TMEM holds two [128 x 256] f32 accumulators so the epilogue of one
+// tile overlaps the MMAs of the next.  Epilogue: warps 4, 5, 8, 9 (TMEM lanes
+// 0-63 = channels; 128 pixels each) apply bias -> BN -> activation and stage
+// [row][channel][column] (16-byte rows, conflict-free) for a TMA store to NCHW.
+constexpr int CONV_BH = 32, CONV_BW = 8, CONV_BN = 64;   // tile: 32 x 8 pixels x 64 output channels
+constexpr int CONV_NPIX = CONV_BH * CONV_BW;             // 256 = MMA N
+constexpr int CONV_WS = 4;                               // weight ring slices (streaming mode)
+constexpr int CONV_W_BYTES = CONV_BN * 128;              // [64 couts][64 channels] bf16
+constexpr int CONV_OUT_BYTES = CONV_NPIX * CONV_BN * 2;   // [32 rows][64 couts][8 columns] bf16
+constexpr int CONV_TMEM = 2 * CONV_NPIX;                  // two 256-column accumulators
+constexpr int CONV_THREADS = 320;                         // warps 0 TMA, 1 MMA, 4-5 + 8-9 epilogue
 
-__host__ __device__ constexpr int conv_patch_bytes(int KH) { return (CONV_BH + KH - 1) * CONV_PW * 128; }
+__host__ __device__ constexpr int conv_pw(int KW) { return CONV_BW + KW - 1; }
+__host__ __device__ constexpr int conv_patch_bytes(int KH, int KW) { return (CONV_BH + KH - 1) * conv_pw(KW) * 128; }
 // wslots: weight slices held in shared memory (all of them when resident, else the ring)
-__host__ __device__ constexpr int conv_smem_bytes(int KH, int AS, int wslots) {
-    return AS * conv_patch_bytes(KH) + wslots * CONV_W_BYTES + 2 * CONV_OUT_BYTES + CONV_BN * 16 + 1024 + 256;
+__host__ __device__ constexpr int conv_smem_bytes(int KH, int KW, int AS, int wslots) {
+    return AS * ((conv_patch_bytes(KH, KW) + 1023) / 1024 * 1024) + wslots * CONV_W_BYTES + 2 * CONV_OUT_BYTES + 1024 + 256;
 }
 
 __device__ __forceinline__ void tma_store_4d_async(const CUtensorMap* m, uint32_t src, int c0, int c1, int c2, int c3) {
@@ -158,27 +157,29 @@ __device__ __forceinline__ void tma_store_4d_async(const CUtensorMap* m, uint32_
 }
 
 // Shapes the tensor-core path takes: unit stride, output rows of 16-byte
-// multiples (the NCHW TMA store), filter taps inside the 16-column patch.
+// multiples (the NCHW TMA store), KH <= 7, KW <= 9, and the shared-memory
+// footprint within 227 KB (e.g. 5 x 5 fits, 7 x 7 does not).
 struct ConvShape;
 bool conv_tc_ok(const ConvShape& s, int stride, int KH, int KW);
 
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(CONV_THREADS, 1)
 conv_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
                const __grid_constant__ CUtensorMap tmY, ConvEpi ep, int B, int OH, int OW, int Cout, int KH, int KW,
                int Cp, int pad, int AS, int wres, int* err) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    const int a_bytes = conv_patch_bytes(KH);
+    const int PW = conv_pw(KW);
+    const int a_bytes = (conv_patch_bytes(KH, KW) + 1023) / 1024 * 1024;
     const int nc = (Cp + 63) / 64;            // 64-channel chunks
     const int taps = KH * KW;
     const int wslots = wres ? taps * nc : CONV_WS;
-    uint8_t* sA = smem;
-    uint8_t* sW = sA + AS * a_bytes;
-    uint8_t* sO = sW + wslots * CONV_W_BYTES;                  // [2] output staging
-    float4* sEpi = reinterpret_cast<float4*>(sO + 2 * CONV_OUT_BYTES);   // [64] (bias, scale, shift, -)
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sO + 2 * CONV_OUT_BYTES + CONV_BN * 16);
-    // a_full[AS<=4], a_empty[4], w_full[WS], w_empty[WS], acc_full[2], acc_empty[2]
-    const uint32_t a_full0 = smem_u32(bars), a_empty0 = smem_u32(bars + 4);
+    uint8_t* sP = smem;                                        // [AS] patches
+    uint8_t* sW = sP + AS * a_bytes;                           // weight slices
+    uint8_t* sO = sW + wslots * CONV_W_BYTES;                  // [2] output staging (also the
+                                                               // rows past the last weight slice)
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sO + 2 * CONV_OUT_BYTES);
+    // p_full[4], p_empty[4], w_full[WS], w_empty[WS], acc_full[2], acc_empty[2]
+    const uint32_t p_full0 = smem_u32(bars), p_empty0 = smem_u32(bars + 4);
     const uint32_t w_full0 = smem_u32(bars + 8), w_empty0 = smem_u32(bars + 8 + CONV_WS);
     const uint32_t acc_full0 = smem_u32(bars + 8 + 2 * CONV_WS), acc_empty0 = smem_u32(bars + 10 + 2 * CONV_WS);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12 + 2 * CONV_WS);
@@ -199,8 +200,8 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ 
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < AS; s++) {
-            mbar_init(a_full0 + 8 * s, 1);
-            mbar_init(a_empty0 + 8 * s, 1);
+            mbar_init(p_full0 + 8 * s, 1);
+            mbar_init(p_empty0 + 8 * s, 1);
         }
         for (int s = 0; s < CONV_WS; s++) {
             mbar_init(w_full0 + 8 * s, 1);
@@ -220,11 +221,11 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ 
     pdl_wait();
 
     if (warp == 0) {
-        // ---------------- producer: haloed input patch per (tile, chunk), weight slice per tap
+        // ---------------- producer: haloed input patch per (tile, chunk); weights
         if (lane == 0) {
             tma_prefetch_desc(&tmX);
             tma_prefetch_desc(&tmW);
-            int ai = 0, wi = 0;
+            int pi = 0, wi = 0;
             bool ok = true;
             if (wres && blockIdx.x < units) {
                 // every weight slice of this CTA's output block (grid % nN == 0: fixed block)
@@ -237,14 +238,14 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ 
                 int b, oh0, ow0, n0;
                 tile_of(t, b, oh0, ow0, n0);
                 for (int c = 0; ok && c < nc; c++) {
-                    const int sa = ai % AS;
-                    if (ai >= AS && !mbar_wait(a_empty0 + 8 * sa, ((ai / AS) - 1) & 1, err, DEV_ERR_TIMEOUT_EMPTY)) {
+                    const int sp = pi % AS;
+                    if (pi >= AS && !mbar_wait(p_empty0 + 8 * sp, ((pi / AS) - 1) & 1, err, DEV_ERR_TIMEOUT_EMPTY)) {
                         ok = false;
                         break;
                     }
-                    mbar_expect_tx(a_full0 + 8 * sa, (uint32_t)a_bytes);
-                    tma_load_4d(smem_u32(sA + sa * a_bytes), &tmX, a_full0 + 8 * sa, c * 64, ow0 - pad, oh0 - pad, b);
-                    ai++;
+                    mbar_expect_tx(p_full0 + 8 * sp, (uint32_t)conv_patch_bytes(KH, KW));
+                    tma_load_4d(smem_u32(sP + sp * a_bytes), &tmX, p_full0 + 8 * sp, c * 64, ow0 - pad, oh0 - pad, b);
+                    pi++;
                     for (int tap = 0; !wres && tap < taps; tap++) {
                         const int sw = wi % CONV_WS;
                         if (wi >= CONV_WS &&
@@ -259,33 +260,33 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ 
                 }
             }
             // every load issued has landed before the CTA can exit
-            for (int k = (ai > AS ? ai - AS : 0); k < ai; k++)
-                mbar_wait(a_full0 + 8 * (k % AS), (k / AS) & 1, err, DEV_ERR_TIMEOUT_FULL);
+            for (int k = (pi > AS ? pi - AS : 0); k < pi; k++)
+                mbar_wait(p_full0 + 8 * (k % AS), (k / AS) & 1, err, DEV_ERR_TIMEOUT_FULL);
             for (int k = (wi > CONV_WS ? wi - CONV_WS : 0); k < wi; k++)
                 mbar_wait(w_full0 + 8 * (k % CONV_WS), (k / CONV_WS) & 1, err, DEV_ERR_TIMEOUT_FULL);
             if (wres && blockIdx.x < units) mbar_wait(w_full0, 0, err, DEV_ERR_TIMEOUT_FULL);
         }
     } else if (warp == 1) {
-        // ---------------- MMA issuer: taps read the patch in place
+        // ---------------- MMA issuer: D^T[couts][pixels] += W_tap (A) x patch_tap (B)
         if (lane == 0) {
-            constexpr uint32_t idesc = idesc_bf16_f32(128, CONV_BN, false, false);
+            constexpr uint32_t idesc = idesc_bf16_f32(128, CONV_NPIX, false, false);
             // descriptors built once; an operand at byte offset o adds o >> 4 (start-address field)
-            const uint64_t a_desc0 = sdesc_sw128(smem_u32(sA), 16, CONV_PW * 128);
-            const uint64_t b_desc0 = sdesc_sw128(smem_u32(sW), 16, 1024);
-            int ai = 0, wi = 0, tl = 0;
+            const uint64_t b_desc0 = sdesc_sw128(smem_u32(sP), 16, (uint32_t)PW * 128);
+            const uint64_t a_desc0 = sdesc_sw128(smem_u32(sW), 16, 1024);
+            int pi = 0, wi = 0, tl = 0;
             bool ok = !wres || blockIdx.x >= units || mbar_wait(w_full0, 0, err, DEV_ERR_TIMEOUT_FULL);
             for (int t = blockIdx.x; ok && t < units; t += gridDim.x, tl++) {
                 const int ab = tl & 1;
                 if (tl >= 2 && !mbar_wait(acc_empty0 + 8 * ab, ((tl >> 1) - 1) & 1, err, DEV_ERR_TIMEOUT_MISC)) break;
                 tc_fence_after();
+                const uint32_t d_tmem = tmem + ab * CONV_NPIX;
                 for (int c = 0; ok && c < nc; c++) {
-                    const int sa = ai % AS;
-                    if (!mbar_wait(a_full0 + 8 * sa, (ai / AS) & 1, err, DEV_ERR_TIMEOUT_FULL)) {
+                    const int sp = pi % AS;
+                    if (!mbar_wait(p_full0 + 8 * sp, (pi / AS) & 1, err, DEV_ERR_TIMEOUT_FULL)) {
                         ok = false;
                         break;
                     }
-                    const uint64_t a_st = a_desc0 + (uint64_t)((sa * a_bytes) >> 4);
-                    const uint32_t d_tmem = tmem + ab * (CONV_NACC * CONV_BN);
+                    const uint64_t b_st = b_desc0 + (uint64_t)((sp * a_bytes) >> 4);
                     for (int tap = 0, kh = 0, kw = 0; tap < taps; tap++) {
                         const int sw = wres ? c * taps + tap : wi % CONV_WS;
                         if (!wres && !mbar_wait(w_full0 + 8 * sw, (wi / CONV_WS) & 1, err, DEV_ERR_TIMEOUT_FULL)) {
@@ -293,95 +294,86 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ 
                             break;
                         }
                         tc_fence_after();
-                        const uint64_t a_tap = a_st + (uint64_t)((kh * CONV_PW + kw) * 8);   // rows of 128 B
-                        const uint64_t b_tap = b_desc0 + (uint64_t)(sw * (CONV_W_BYTES >> 4));
-                        // K-step kk of every tap goes to accumulator kk (CONV_NACC == 4)
+                        const uint64_t b_tap = b_st + (uint64_t)((kh * PW + kw) * 8);   // rows of 128 B
+                        const uint64_t a_tap = a_desc0 + (uint64_t)(sw * (CONV_W_BYTES >> 4));
 #pragma unroll
                         for (int kk = 0; kk < 4; kk++)
-                            umma_f16_ss(d_tmem + kk * CONV_BN, a_tap + 2 * kk, b_tap + 2 * kk, idesc, (c | tap) != 0);
-                        if (++kw == KW) {
-                            kw = 0;
-                            kh++;
-                        }
+                            umma_f16_ss(d_tmem, a_tap + 2 * kk, b_tap + 2 * kk, idesc, (c | tap | kk) != 0);
                         if (!wres) {
                             umma_commit(w_empty0 + 8 * sw);
                             wi++;
                         }
+                        if (++kw == KW) {
+                            kw = 0;
+                            kh++;
+                        }
                     }
-                    umma_commit(a_empty0 + 8 * sa);
-                    ai++;
+                    umma_commit(p_empty0 + 8 * sp);
+                    pi++;
                 }
                 umma_commit(acc_full0 + 8 * ab);
             }
         }
-    } else if (warp >= 4) {
-        // ---------------- epilogue: thread <-> pixel row r = 32 * (warp % 4) + lane (h = r / 8, w = r % 8)
-        const int q = warp & 3, r = q * 32 + lane;
+    } else if (warp == 4 || warp == 5 || warp == 8 || warp == 9) {
+        // ---------------- epilogue: thread <-> output channel co = 32 * (warp % 4) + lane
+        // (TMEM lane), pixel columns [128 * half, 128 * half + 128) of the tile
+        const int q = warp & 3, half = warp >> 3;
+        const int col = q * 32 + lane;            // channel within the block
         bool ok = true;
         int tl = 0, cur_n0 = -1;
+        float eb = 0.f, es = 1.f, et = 0.f;
         for (int t = blockIdx.x; t < units; t += gridDim.x, tl++) {
             int b, oh0, ow0, n0;
             tile_of(t, b, oh0, ow0, n0);
             const int ab = tl & 1;
+            const int co = n0 + col;
             if (n0 != cur_n0) {
-                // per-channel (bias, scale, shift) of this output block -> shared memory
-                asm volatile("bar.sync 2, 128;" ::: "memory");   // previous block's values no longer read
-                if (threadIdx.x - 128 < CONV_BN) {
-                    const int co = n0 + (threadIdx.x - 128);
-                    float4 e = make_float4(0.f, 1.f, 0.f, 0.f);
-                    if (co < Cout) {
-                        if (ep.bias && !ep.shift) e.x = ep.bias[co];
-                        if (ep.scale) e.y = ep.scale[co];
-                        if (ep.shift) e.z = ep.shift[co];
-                    }
-                    sEpi[threadIdx.x - 128] = e;
+                eb = 0.f;
+                es = 1.f;
+                et = 0.f;
+                if (co < Cout) {
+                    if (ep.bias && !ep.shift) eb = ep.bias[co];
+                    if (ep.scale) es = ep.scale[co];
+                    if (ep.shift) et = ep.shift[co];
                 }
-                asm volatile("bar.sync 2, 128;" ::: "memory");
                 cur_n0 = n0;
             }
             ok = mbar_wait(acc_full0 + 8 * ab, (tl >> 1) & 1, err, DEV_ERR_TIMEOUT_ACC) && ok;
             tc_fence_after();
-            float v[64];
-            {
-                const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + ab * (CONV_NACC * CONV_BN);
-                tmem_ld32(tb, v);
-                tmem_ld32(tb + 32, v + 32);
+            // staging buffer ab was last read by the store issued two tiles ago
+            if (warp == 4 && lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+            asm volatile("bar.sync 2, 128;" ::: "memory");
+            uint8_t* so = sO + ab * CONV_OUT_BYTES;
+#pragma unroll 1
+            for (int p0 = half * 128; p0 < half * 128 + 128; p0 += 32) {
+                float v[32];
+                tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + ab * CONV_NPIX + p0, v);
                 tmem_wait_ld();
+                // v -> ((v + bias) * scale + shift) -> activation (as conv_epi)
 #pragma unroll
-                for (int k = 1; k < CONV_NACC; k++) {
-                    float u[64];
-                    tmem_ld32(tb + k * CONV_BN, u);
-                    tmem_ld32(tb + k * CONV_BN + 32, u + 32);
-                    tmem_wait_ld();
+                for (int j = 0; j < 32; j++) {
+                    float o = (v[j] + eb) * es + et;
+                    if (ep.act == TB_ACT_RELU) o = o > 0.f ? o : 0.f;
+                    else if (ep.act == TB_ACT_SILU) o = o / (1.0f + expf(-o));
+                    v[j] = co < Cout ? o : 0.f;
+                }
+                // pixels p0 .. p0 + 31 = rows p0 / 8 .. + 3, 8 columns each: [row][channel][column]
 #pragma unroll
-                    for (int j = 0; j < 64; j++) v[j] += u[j];
+                for (int r = 0; r < 4; r++) {
+                    uint4 u;
+                    u.x = pack_bf16x2(v[8 * r + 0], v[8 * r + 1]);
+                    u.y = pack_bf16x2(v[8 * r + 2], v[8 * r + 3]);
+                    u.z = pack_bf16x2(v[8 * r + 4], v[8 * r + 5]);
+                    u.w = pack_bf16x2(v[8 * r + 6], v[8 * r + 7]);
+                    *reinterpret_cast<uint4*>(so + ((p0 / 8 + r) * CONV_BN + col) * 16) = u;
                 }
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(acc_empty0 + 8 * ab);
-            // staging buffer ab was last read by the store issued two tiles ago
-            if (warp == 4 && lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
-            asm volatile("bar.sync 2, 128;" ::: "memory");
-            __nv_bfloat16* so = reinterpret_cast<__nv_bfloat16*>(sO + ab * CONV_OUT_BYTES);
-            // v -> ((v + bias) * scale + shift) -> activation, as conv_epi; 16 channels
-            // per batch of shared-memory reads
-#pragma unroll
-            for (int j0 = 0; j0 < 64; j0 += 16) {
-                float4 e[16];
-#pragma unroll
-                for (int j = 0; j < 16; j++) e[j] = sEpi[j0 + j];
-#pragma unroll
-                for (int j = 0; j < 16; j++) {
-                    float o = (v[j0 + j] + e[j].x) * e[j].y + e[j].z;
-                    if (ep.act == TB_ACT_RELU) o = o > 0.f ? o : 0.f;
-                    else if (ep.act == TB_ACT_SILU) o = o / (1.0f + expf(-o));
-                    so[(j0 + j) * 128 + r] = __float2bfloat16_rn(n0 + j0 + j < Cout ? o : 0.f);
-                }
-            }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             asm volatile("bar.sync 2, 128;" ::: "memory");
-            if (warp == 4 && lane == 0 && ok) tma_store_4d_async(&tmY, smem_u32(so), ow0, oh0, n0, b);
+            if (warp == 4 && lane == 0 && ok) tma_store_4d_async(&tmY, smem_u32(so), ow0, n0, oh0, b);
         }
         if (warp == 4 && lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
     }
@@ -502,7 +494,8 @@ static size_t conv_ws_bytes(const ConvShape& s) {
 }
 
 bool conv_tc_ok(const ConvShape& s, int stride, int KH, int KW) {
-    return stride == 1 && s.OW % 8 == 0 && KH <= 7 && KW <= CONV_PW - CONV_BW + 1;
+    // two patch stages + the weight ring + output staging within 227 KB of shared memory
+    return stride == 1 && s.OW % 8 == 0 && KH <= 7 && KW <= 9 && conv_smem_bytes(KH, KW, 2, CONV_WS) <= 227 * 1024;
 }
 
 static bool conv_shape(int B, int C, int Co, int H, int W, int KH, int KW, int stride, int pad, ConvShape* s) {
@@ -569,7 +562,7 @@ int tb_conv2d_fwd(tb_ctx* ctx, int dtype, const void* x, const void* w, const fl
     {
         uint64_t dims[4] = {(uint64_t)s.Cp, (uint64_t)W, (uint64_t)H, (uint64_t)B};
         uint64_t strides[3] = {(uint64_t)s.Cp * 2, (uint64_t)W * s.Cp * 2, (uint64_t)H * W * s.Cp * 2};
-        uint32_t box[4] = {64, CONV_PW, (uint32_t)(CONV_BH + KH - 1), 1};
+        uint32_t box[4] = {64, (uint32_t)conv_pw(KW), (uint32_t)(CONV_BH + KH - 1), 1};
         cuuint32_t es[4] = {1, 1, 1, 1};
         int rc = make_tmap_strided(ctx, &mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, xn, dims, strides, box, es,
                                    CU_TENSOR_MAP_SWIZZLE_128B);
@@ -577,27 +570,28 @@ int tb_conv2d_fwd(tb_ctx* ctx, int dtype, const void* x, const void* w, const fl
         rc = make_tmap_2d(ctx, &mw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, wr, Cout, (uint64_t)KH * KW * s.Cp,
                           (uint64_t)KH * KW * s.Cp, 64, CONV_BN);
         if (rc) return rc;
-        uint64_t ydims[4] = {(uint64_t)s.OW, (uint64_t)s.OH, (uint64_t)Cout, (uint64_t)B};
-        uint64_t ystr[3] = {(uint64_t)s.OW * 2, (uint64_t)s.OH * s.OW * 2, (uint64_t)Cout * s.OH * s.OW * 2};
-        uint32_t ybox[4] = {CONV_BW, CONV_BH, CONV_BN, 1};
+        // NCHW output viewed as (w, channel, h, image): the staged tile is [h][channel][w]
+        uint64_t ydims[4] = {(uint64_t)s.OW, (uint64_t)Cout, (uint64_t)s.OH, (uint64_t)B};
+        uint64_t ystr[3] = {(uint64_t)s.OH * s.OW * 2, (uint64_t)s.OW * 2, (uint64_t)Cout * s.OH * s.OW * 2};
+        uint32_t ybox[4] = {CONV_BW, CONV_BN, CONV_BH, 1};
         rc = make_tmap(ctx, &my, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, y, ydims, ystr, ybox, CU_TENSOR_MAP_SWIZZLE_NONE);
         if (rc) return rc;
     }
     // Resident weights (all taps x chunks of one 64-channel output block) when
     // they fit beside two patch stages; otherwise a 4-slice weight ring.
-    constexpr int kSmemMax = 220 * 1024;
+    constexpr int kSmemMax = 227 * 1024;
     const int nN = (Cout + CONV_BN - 1) / CONV_BN;
     const int wall = KH * KW * ((s.Cp + 63) / 64);
-    const int wres = conv_smem_bytes(KH, 2, wall) <= kSmemMax && nN <= ctx->num_sms ? 1 : 0;
+    const int wres = conv_smem_bytes(KH, KW, 2, wall) <= kSmemMax && nN <= ctx->num_sms ? 1 : 0;
     const int wslots = wres ? wall : CONV_WS;
-    const int AS = conv_smem_bytes(KH, 3, wslots) <= kSmemMax ? 3 : 2;
-    const int smem = conv_smem_bytes(KH, AS, wslots);
+    const int AS = conv_smem_bytes(KH, KW, 3, wslots) <= kSmemMax ? 3 : 2;
+    const int smem = conv_smem_bytes(KH, KW, AS, wslots);
     TB_CUDA_TRY(ctx, cudaFuncSetAttribute(conv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     const int64_t units = (int64_t)((s.OW + CONV_BW - 1) / CONV_BW) * ((s.OH + CONV_BH - 1) / CONV_BH) * B * nN;
     // resident weights: a grid that is a multiple of nN keeps each CTA on one output block
     int grid = wres ? (ctx->num_sms / nN) * nN : ctx->num_sms;
     if (units < grid) grid = (int)units;
-    return launch(ctx, "conv_tc", conv_tc_kernel, dim3(grid), dim3(256), smem, mx, mw, my, ep, B, s.OH, s.OW, Cout,
+    return launch(ctx, "conv_tc", conv_tc_kernel, dim3(grid), dim3(CONV_THREADS), smem, mx, mw, my, ep, B, s.OH, s.OW, Cout,
                   KH, KW, s.Cp, pad, AS, wres, ctx->d_err);
 }
 
