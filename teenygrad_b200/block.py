@@ -23,7 +23,12 @@ def block_forward(x, p, n_heads, eps=1e-6):
     B, S, d = x.shape
     hd = d // n_heads
     h = ops.rms_norm(x, p["attn_norm"], eps)
-    q, k, v = (ops.linear(h, p[n]) for n in ("wq", "wk", "wv"))
+    # one projection GEMM for q, k and v: rows of wq, wk, wv stacked (each output
+    # element is the same dot product as with the separate weights)
+    wqkv = p.get("wqkv")
+    if wqkv is None:
+        wqkv = torch.cat([p["wq"], p["wk"], p["wv"]], 0)
+    q, k, v = ops.linear(h, wqkv).split(d, dim=-1)
 
     def heads(t):
         return t.view(B, S, n_heads, hd).transpose(1, 2).contiguous()
@@ -42,5 +47,7 @@ def random_block_params(d=256, F=1024, seed=0, device="cuda"):
     def w(*s):
         return (torch.randn(*s, generator=g) * 0.02).to(device)
 
-    return dict(attn_norm=torch.ones(d, device=device), wq=w(d, d), wk=w(d, d), wv=w(d, d), wo=w(d, d),
-                mlp_norm=torch.ones(d, device=device), w_gate=w(F, d), w_up=w(F, d), w_down=w(d, F))
+    p = dict(attn_norm=torch.ones(d, device=device), wq=w(d, d), wk=w(d, d), wv=w(d, d), wo=w(d, d),
+             mlp_norm=torch.ones(d, device=device), w_gate=w(F, d), w_up=w(F, d), w_down=w(d, F))
+    p["wqkv"] = torch.cat([p["wq"], p["wk"], p["wv"]], 0)
+    return p

@@ -660,43 +660,82 @@ attn_decode_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_cons
 }
 
 // ---------------------------------------------------------------- f32 ------
-// One warp per query row, exact f32 two-pass softmax over visible keys.
-__global__ void attn_f32_kernel(const float* __restrict__ q, const float* __restrict__ k,
-                                const float* __restrict__ v, float* __restrict__ o, float* __restrict__ lse,
-                                int B, int Hq, int Hkv, int Sq, int Sk, int D, float scale, int causal) {
-    int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
-    int lane = threadIdx.x & 31;
-    if (row >= (int64_t)B * Hq * Sq) return;
-    int i = (int)(row % Sq);
-    int64_t bh = row / Sq;
-    int h = (int)(bh % Hq), b = (int)(bh / Hq);
-    int hk = h / (Hq / Hkv);
-    const float* qr = q + row * D;
+// One warp per query row, f32 throughout.  Keys go 32 at a time, lane j
+// computing the full dot product of key j (q staged in shared memory); an
+// online softmax (running max, rescaled sum and output) merges the chunks,
+// and the output dims are spread over the lanes for P V.
+__global__ void __launch_bounds__(256)
+attn_f32_kernel(const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
+                float* __restrict__ o, float* __restrict__ lse, int B, int Hq, int Hkv, int Sq, int Sk, int D,
+                float scale, int causal) {
+    __shared__ float sq[8][128];
+    const int w = threadIdx.x / 32, lane = threadIdx.x & 31;
+    const int64_t row = (int64_t)blockIdx.x * 8 + w;
+    const bool live = row < (int64_t)B * Hq * Sq;
+    int i = 0, h = 0, b = 0;
+    if (live) {
+        i = (int)(row % Sq);
+        const int64_t bh = row / Sq;
+        h = (int)(bh % Hq);
+        b = (int)(bh / Hq);
+        for (int d = lane; d < D; d += 32) sq[w][d] = q[row * D + d];
+    }
+    __syncwarp();
+    if (!live) return;
+    const int hk = h / (Hq / Hkv);
     const float* kb = k + ((int64_t)b * Hkv + hk) * Sk * D;
     const float* vb = v + ((int64_t)b * Hkv + hk) * Sk * D;
-    int jmax = causal ? min(Sk - 1, i + (Sk - Sq)) : Sk - 1;
-    float qv[4];
-    for (int t = 0; t < 4; t++) qv[t] = (lane + 32 * t < D) ? qr[lane + 32 * t] : 0.f;
-    float m = -INFINITY;
-    for (int j = 0; j <= jmax; j++) {
-        float s = 0.f;
-        for (int t = 0; t < 4; t++)
-            if (lane + 32 * t < D) s = fmaf(qv[t], kb[(int64_t)j * D + lane + 32 * t], s);
+    const int jmax = causal ? min(Sk - 1, i + (Sk - Sq)) : Sk - 1;
+    float m = -INFINITY, l = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int j0 = 0; j0 <= jmax; j0 += 32) {
+        const int j = j0 + lane;
+        float sc = -INFINITY;
+        if (j <= jmax) {
+            const float* kr = kb + (int64_t)j * D;
+            float dot = 0.f;
+            if ((D & 3) == 0 && (reinterpret_cast<uintptr_t>(k) & 15) == 0) {   // 16-byte rows
+#pragma unroll 8
+                for (int d = 0; d < D; d += 4) {
+                    const float4 kv = *reinterpret_cast<const float4*>(kr + d);
+                    dot = fmaf(sq[w][d], kv.x, dot);
+                    dot = fmaf(sq[w][d + 1], kv.y, dot);
+                    dot = fmaf(sq[w][d + 2], kv.z, dot);
+                    dot = fmaf(sq[w][d + 3], kv.w, dot);
+                }
+            } else {
+                for (int d = 0; d < D; d++) dot = fmaf(sq[w][d], kr[d], dot);
+            }
+            sc = dot * scale;
+        }
+        float cm = sc;
 #pragma unroll
-        for (int of = 16; of > 0; of >>= 1) s += __shfl_xor_sync(0xffffffffu, s, of);
-        m = fmaxf(m, s * scale);
-    }
-    float l = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int j = 0; j <= jmax; j++) {
-        float s = 0.f;
-        for (int t = 0; t < 4; t++)
-            if (lane + 32 * t < D) s = fmaf(qv[t], kb[(int64_t)j * D + lane + 32 * t], s);
+        for (int of = 16; of > 0; of >>= 1) cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, of));
+        const float m_new = fmaxf(m, cm);          // finite: key j0 <= jmax is visible
+        const float alpha = expf(m - m_new);       // m = -inf on the first chunk -> 0
+        const float p = (j <= jmax) ? expf(sc - m_new) : 0.f;
+        float ps = p;
 #pragma unroll
-        for (int of = 16; of > 0; of >>= 1) s += __shfl_xor_sync(0xffffffffu, s, of);
-        float p = expf(s * scale - m);
-        l += p;
-        for (int t = 0; t < 4; t++)
-            if (lane + 32 * t < D) acc[t] = fmaf(p, vb[(int64_t)j * D + lane + 32 * t], acc[t]);
+        for (int of = 16; of > 0; of >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, of);
+        l = l * alpha + ps;
+#pragma unroll
+        for (int t = 0; t < 4; t++) acc[t] *= alpha;
+        const int nj = min(32, jmax - j0 + 1);
+        for (int jb = 0; jb < nj; jb += 8) {
+            // 8 value rows in flight at once
+            float vv[8][4];
+#pragma unroll
+            for (int u = 0; u < 8; u++)
+#pragma unroll
+                for (int t = 0; t < 4; t++)
+                    vv[u][t] = (jb + u < nj && lane + 32 * t < D) ? vb[(int64_t)(j0 + jb + u) * D + lane + 32 * t] : 0.f;
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                const float pj = __shfl_sync(0xffffffffu, p, (jb + u) & 31);
+#pragma unroll
+                for (int t = 0; t < 4; t++) acc[t] = fmaf(pj, vv[u][t], acc[t]);
+            }
+        }
+        m = m_new;
     }
     float* orow = o + row * D;
     for (int t = 0; t < 4; t++)

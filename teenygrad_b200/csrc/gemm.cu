@@ -660,61 +660,136 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
 // =====================================================================
 // f32 CUDA-core paths (exact f32 FMA accumulate)
 // =====================================================================
-// 64x64 output tile, 256 threads, 4x4 outputs per thread, K-slices of 16.
+// 64x64 output tile, 256 threads, 4x4 outputs per thread, K-slices of 32
+// (the next slice is loaded into registers while the current one is
+// multiplied from shared memory).  Small grids split K over a thread-block
+// cluster (gridDim.z CTAs); the partial tiles are summed over DSMEM in rank
+// order (deterministic), each rank finishing 64 / splits rows.
 // B_KN: b is [K, N] (matmul_forward); else b is [N, K] (linear_forward).
 template <bool B_KN>
 __global__ void __launch_bounds__(256)
 gemm_f32_kernel(const float* __restrict__ a, const float* __restrict__ b, const float* __restrict__ bias,
-                const float* __restrict__ resid, float* __restrict__ y, int M, int N, int K) {
-    __shared__ float sa[16][64 + 4];
-    __shared__ float sb[16][64 + 4];
-    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+                const float* __restrict__ resid, float* __restrict__ y, int M, int N, int K, int k_per_split) {
+    __shared__ float sa[2][32][64 + 4];
+    __shared__ float sb[2][32][64 + 4];
+    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
     const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
+    const int split = blockIdx.z, S = gridDim.z;
+    const int kbeg = split * k_per_split, kend = min(K, kbeg + k_per_split);
+    const int nsl = kend > kbeg ? (kend - kbeg + 31) / 32 : 0;
     float acc[4][4] = {};
-    for (int k0 = 0; k0 < K; k0 += 16) {
-        for (int i = threadIdx.x; i < 64 * 16; i += 256) {
-            int r = i / 16, kk = i % 16;
-            int gm = m0 + r, gk = k0 + kk;
-            sa[kk][r] = (gm < M && gk < K) ? a[(int64_t)gm * K + gk] : 0.f;
+    float ra[8], rb[8];
+    auto load = [&](int sl) {
+        const int k0 = kbeg + sl * 32;
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            const int e = tid + 256 * u;
+            {
+                const int r = e / 32, kk = e % 32, gm = m0 + r, gk = k0 + kk;
+                ra[u] = (gm < M && gk < kend) ? a[(int64_t)gm * K + gk] : 0.f;
+            }
             if (B_KN) {
-                int c = i % 64, kr = i / 64;
-                int gn = n0 + c, gk2 = k0 + kr;
-                sb[kr][c] = (gn < N && gk2 < K) ? b[(int64_t)gk2 * N + gn] : 0.f;
+                const int kr = e / 64, c = e % 64, gn = n0 + c, gk = k0 + kr;
+                rb[u] = (gn < N && gk < kend) ? b[(int64_t)gk * N + gn] : 0.f;
             } else {
-                int gn = n0 + r;
-                sb[kk][r] = (gn < N && gk < K) ? b[(int64_t)gn * K + gk] : 0.f;
+                const int r = e / 32, kk = e % 32, gn = n0 + r, gk = k0 + kk;
+                rb[u] = (gn < N && gk < kend) ? b[(int64_t)gn * K + gk] : 0.f;
             }
         }
-        __syncthreads();
+    };
+    auto store = [&](int buf) {
 #pragma unroll
-        for (int kk = 0; kk < 16; kk++) {
+        for (int u = 0; u < 8; u++) {
+            const int e = tid + 256 * u;
+            sa[buf][e % 32][e / 32] = ra[u];
+            if (B_KN) sb[buf][e / 64][e % 64] = rb[u];
+            else sb[buf][e % 32][e / 32] = rb[u];
+        }
+    };
+    if (nsl > 0) {
+        load(0);
+        store(0);
+    }
+    __syncthreads();
+    for (int sl = 0; sl < nsl; sl++) {
+        const int buf = sl & 1;
+        if (sl + 1 < nsl) load(sl + 1);
+#pragma unroll
+        for (int kk = 0; kk < 32; kk++) {
             float av[4], bv[4];
 #pragma unroll
             for (int i = 0; i < 4; i++) {
-                av[i] = sa[kk][ty + 16 * i];
-                bv[i] = sb[kk][tx + 16 * i];
+                av[i] = sa[buf][kk][ty + 16 * i];
+                bv[i] = sb[buf][kk][tx + 16 * i];
             }
 #pragma unroll
             for (int i = 0; i < 4; i++)
 #pragma unroll
                 for (int j = 0; j < 4; j++) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
         }
+        if (sl + 1 < nsl) store(buf ^ 1);
         __syncthreads();
     }
+    auto finish = [&](int m, int n, float v) {
+        if (m >= M || n >= N) return;
+        if (bias) v += bias[n];
+        if (resid) v += resid[(int64_t)m * N + n];
+        y[(int64_t)m * N + n] = v;
+    };
+    if (S == 1) {
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
-        int m = m0 + ty + 16 * i;
-        if (m >= M) continue;
+        for (int i = 0; i < 4; i++)
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
-            int n = n0 + tx + 16 * j;
-            if (n >= N) continue;
-            float v = acc[i][j];
-            if (bias) v += bias[n];
-            if (resid) v += resid[(int64_t)m * N + n];
-            y[(int64_t)m * N + n] = v;
-        }
+            for (int j = 0; j < 4; j++) finish(m0 + ty + 16 * i, n0 + tx + 16 * j, acc[i][j]);
+        return;
     }
+    // partial tile [64][64] -> this CTA's shared memory (sa reused), then rank r
+    // sums rows [r * 64 / S, (r + 1) * 64 / S) of all S partials over DSMEM
+    float* part = &sa[0][0][0];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) part[(ty + 16 * i) * 64 + tx + 16 * j] = acc[i][j];
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+    const int rows = 64 / S;
+    const uint32_t base = smem_u32(part);
+    for (int e = tid; e < rows * 64; e += 256) {
+        const int r = split * rows + e / 64, c = e % 64;
+        float v = 0.f;
+        for (int q = 0; q < S; q++) {
+            uint32_t addr;
+            float t;
+            asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(addr) : "r"(base + (uint32_t)(r * 64 + c) * 4), "r"(q));
+            asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(t) : "r"(addr) : "memory");
+            v += t;
+        }
+        finish(m0 + r, n0 + c, v);
+    }
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Launches gemm_f32_kernel, splitting K over a cluster of up to 8 CTAs when
+// the output tiles alone would leave most SMs idle.
+template <bool B_KN>
+static int launch_gemm_f32(tb_ctx* ctx, const float* a, const float* b, const float* bias, const float* resid, float* y,
+                           int M, int N, int K) {
+    const int tiles = ((N + 63) / 64) * ((M + 63) / 64);
+    int S = 1;
+    while (S < 8 && tiles * S * 2 <= ctx->num_sms && K / (S * 2) >= 64) S *= 2;
+    const int kps = (K + S - 1) / S;
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3((unsigned)((N + 63) / 64), (unsigned)((M + 63) / 64), (unsigned)S);
+    lc.blockDim = dim3(256, 1, 1);
+    lc.stream = ctx->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = S;
+    lc.attrs = attr;
+    lc.numAttrs = 1;
+    TB_CUDA_TRY(ctx, cudaLaunchKernelEx(&lc, gemm_f32_kernel<B_KN>, a, b, bias, resid, y, M, N, K, kps));
+    return check_launch(ctx, "gemm_f32");
 }
 
 // ------------------------------------------------------------ host side --
@@ -862,11 +937,9 @@ int tb_linear_fwd(tb_ctx* ctx, int dtype, const void* x, const void* w, const fl
     const bool swiglu = (flags & TB_EPI_SWIGLU) != 0;
     if (dtype == TB_F32) {
         if (swiglu) return set_error(ctx, TB_ERR_UNSUPPORTED, "linear f32: SwiGLU epilogue is bf16-only");
-        dim3 grid((unsigned)((N + 63) / 64), (unsigned)((M + 63) / 64));
-        gemm_f32_kernel<false><<<grid, 256, 0, ctx->stream>>>(
-            (const float*)x, (const float*)w, (flags & TB_EPI_BIAS) ? bias : nullptr,
-            (flags & TB_EPI_RESIDUAL) ? (const float*)residual : nullptr, (float*)y, (int)M, (int)N, (int)K);
-        return check_launch(ctx, "linear_f32");
+        return launch_gemm_f32<false>(ctx, (const float*)x, (const float*)w, (flags & TB_EPI_BIAS) ? bias : nullptr,
+                                      (flags & TB_EPI_RESIDUAL) ? (const float*)residual : nullptr, (float*)y, (int)M,
+                                      (int)N, (int)K);
     }
     if (dtype != TB_BF16) return set_error(ctx, TB_ERR_UNSUPPORTED, "linear: dtype %d", dtype);
     TB_REQUIRE(ctx, K % 8 == 0 && N % 8 == 0, TB_ERR_SHAPE, "linear bf16: K and N must be multiples of 8");
@@ -894,10 +967,8 @@ int tb_matmul_fwd(tb_ctx* ctx, int dtype, const void* a, const void* b, void* c,
                TB_ERR_SHAPE, "matmul: bad shape");
     if (M == 0) return TB_OK;
     if (dtype == TB_F32) {
-        dim3 grid((unsigned)((N + 63) / 64), (unsigned)((M + 63) / 64));
-        gemm_f32_kernel<true><<<grid, 256, 0, ctx->stream>>>((const float*)a, (const float*)b, nullptr, nullptr,
-                                                             (float*)c, (int)M, (int)N, (int)K);
-        return check_launch(ctx, "matmul_f32");
+        return launch_gemm_f32<true>(ctx, (const float*)a, (const float*)b, nullptr, nullptr, (float*)c, (int)M, (int)N,
+                                     (int)K);
     }
     if (dtype != TB_BF16) return set_error(ctx, TB_ERR_UNSUPPORTED, "matmul: dtype %d", dtype);
     TB_REQUIRE(ctx, K % 8 == 0 && N % 8 == 0, TB_ERR_SHAPE, "matmul bf16: K and N must be multiples of 8");
