@@ -67,10 +67,16 @@ template <int BN, int STAGES>
 constexpr int gemm_smem_bytes() {
     return STAGES * (GEMM_BM * 128 + BN * 128) + 1024 /*align*/ + 256 /*barriers*/;
 }
+constexpr int GEMM_THREADS = 384;   // warp 0 TMA, warp 1 MMA, warps 4-11 epilogue
 
+// Persistent: one CTA per SM walks the output tiles (t += gridDim.x; m fastest,
+// so concurrently running CTAs share the weight tile).  The f32 accumulator
+// is double-buffered in TMEM (2 x BN columns): the epilogue of tile i (warps
+// 4-11: TMEM lane quarter warp % 4, column half (warp - 4) / 4) overlaps the
+// MMAs of tile i + 1.
 // B_MN: b operand stored [K, N] (N contiguous), as matmul_forward's B.
 template <int BN, int STAGES, bool B_MN>
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                Epi ep, int M, int N, int K, int* err) {
     constexpr int A_BYTES = GEMM_BM * 128;
@@ -80,15 +86,16 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     uint8_t* sA = smem;
     uint8_t* sB = smem + STAGES * A_BYTES;
     uint64_t* bars = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
-    uint32_t full0 = smem_u32(bars);
-    uint32_t empty0 = smem_u32(bars + STAGES);
-    uint32_t accb = smem_u32(bars + 2 * STAGES);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 1);
+    const uint32_t full0 = smem_u32(bars);
+    const uint32_t empty0 = smem_u32(bars + STAGES);
+    const uint32_t accf0 = smem_u32(bars + 2 * STAGES);       // [2] accumulator ready
+    const uint32_t acce0 = smem_u32(bars + 2 * STAGES + 2);   // [2] accumulator drained
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
 
     pdl_trigger();
-    pdl_wait();
     const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.y * GEMM_BM, n0 = blockIdx.x * BN;
+    const int mt = (M + GEMM_BM - 1) / GEMM_BM, ntl = (N + BN - 1) / BN;
+    const int tiles = mt * ntl;
     const int nk = (K + GEMM_BK - 1) / GEMM_BK;
 
     if (threadIdx.x == 0) {
@@ -96,120 +103,151 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             mbar_init(full0 + 8 * s, 1);
             mbar_init(empty0 + 8 * s, 1);
         }
-        mbar_init(accb, 1);
+        for (int s = 0; s < 2; s++) {
+            mbar_init(accf0 + 8 * s, 1);
+            mbar_init(acce0 + 8 * s, 8);
+        }
         fence_barrier_init();
     }
-    if (warp == 1) tmem_alloc(smem_u32(tmem_slot), BN);
+    if (warp == 1) tmem_alloc(smem_u32(tmem_slot), 2 * BN);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    pdl_wait();
 
-    if (warp == 0 && lane == 0) {
+    if (warp == 0) {
         // ---------------- TMA producer
-        tma_prefetch_desc(&tmA);
-        tma_prefetch_desc(&tmB);
-        int issued = 0;
-        for (int kb = 0; kb < nk; kb++) {
-            int s = kb % STAGES;
-            if (kb >= STAGES && !mbar_wait(empty0 + 8 * s, ((kb / STAGES) - 1) & 1, err, DEV_ERR_TIMEOUT_EMPTY)) break;
-            mbar_expect_tx(full0 + 8 * s, A_BYTES + B_BYTES);
-            tma_load_2d(smem_u32(sA + s * A_BYTES), &tmA, full0 + 8 * s, kb * GEMM_BK, m0);
-            if (!B_MN) {
-                tma_load_2d(smem_u32(sB + s * B_BYTES), &tmB, full0 + 8 * s, kb * GEMM_BK, n0);
-            } else {
+        if (lane == 0) {
+            tma_prefetch_desc(&tmA);
+            tma_prefetch_desc(&tmB);
+            int it = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x) {
+                const int m0 = (t % mt) * GEMM_BM, n0 = (t / mt) * BN;
+                for (int kb = 0; kb < nk; kb++, it++) {
+                    const int s = it % STAGES;
+                    if (it >= STAGES && !mbar_wait(empty0 + 8 * s, ((it / STAGES) - 1) & 1, err, DEV_ERR_TIMEOUT_EMPTY)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_expect_tx(full0 + 8 * s, A_BYTES + B_BYTES);
+                    tma_load_2d(smem_u32(sA + s * A_BYTES), &tmA, full0 + 8 * s, kb * GEMM_BK, m0);
+                    if (!B_MN) {
+                        tma_load_2d(smem_u32(sB + s * B_BYTES), &tmB, full0 + 8 * s, kb * GEMM_BK, n0);
+                    } else {
 #pragma unroll
-                for (int j = 0; j < BN / 64; j++)
-                    tma_load_2d(smem_u32(sB + s * B_BYTES + j * 64 * 128), &tmB, full0 + 8 * s, n0 + 64 * j, kb * GEMM_BK);
+                        for (int j = 0; j < BN / 64; j++)
+                            tma_load_2d(smem_u32(sB + s * B_BYTES + j * 64 * 128), &tmB, full0 + 8 * s, n0 + 64 * j,
+                                        kb * GEMM_BK);
+                    }
+                }
             }
-            issued = kb + 1;
+            // every issued stage has landed before the CTA can exit
+            for (int k = (it > STAGES ? it - STAGES : 0); k < it; k++)
+                mbar_wait(full0 + 8 * (k % STAGES), (k / STAGES) & 1, err, DEV_ERR_TIMEOUT_FULL);
         }
-        // Drain: every issued stage must have landed before the CTA can exit.
-        for (int kb = (issued > STAGES ? issued - STAGES : 0); kb < issued; kb++)
-            mbar_wait(full0 + 8 * (kb % STAGES), (kb / STAGES) & 1, err, DEV_ERR_TIMEOUT_FULL);
-    } else if (warp == 1 && lane == 0) {
+    } else if (warp == 1) {
         // ---------------- MMA issuer
-        constexpr uint32_t idesc = idesc_bf16_f32(GEMM_BM, BN, false, B_MN);
-        for (int kb = 0; kb < nk; kb++) {
-            int s = kb % STAGES;
-            if (!mbar_wait(full0 + 8 * s, (kb / STAGES) & 1, err, DEV_ERR_TIMEOUT_FULL)) break;
-            tc_fence_after();
-            uint32_t a_base = smem_u32(sA + s * A_BYTES);
-            uint32_t b_base = smem_u32(sB + s * B_BYTES);
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_bf16_f32(GEMM_BM, BN, false, B_MN);
+            const uint64_t a_desc0 = sdesc_sw128(smem_u32(sA), 16, 1024);
+            const uint64_t b_desc0 = B_MN ? sdesc_sw128(smem_u32(sB), 64 * 128, 1024) : sdesc_sw128(smem_u32(sB), 16, 1024);
+            int it = 0, tl = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x, tl++) {
+                const int ab = tl & 1;
+                if (tl >= 2 && !mbar_wait(acce0 + 8 * ab, ((tl >> 1) - 1) & 1, err, DEV_ERR_TIMEOUT_MISC)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem + ab * BN;
+                for (int kb = 0; kb < nk; kb++, it++) {
+                    const int s = it % STAGES;
+                    if (!mbar_wait(full0 + 8 * s, (it / STAGES) & 1, err, DEV_ERR_TIMEOUT_FULL)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint64_t ad = a_desc0 + (uint64_t)((s * A_BYTES) >> 4);
+                    const uint64_t bd = b_desc0 + (uint64_t)((s * B_BYTES) >> 4);
 #pragma unroll
-            for (int kk = 0; kk < GEMM_BK / 16; kk++) {
-                uint64_t ad = sdesc_sw128(a_base + kk * 32, 16, 1024);
-                uint64_t bd = B_MN ? sdesc_sw128(b_base + kk * 16 * 128, 64 * 128, 1024)
-                                   : sdesc_sw128(b_base + kk * 32, 16, 1024);
-                umma_f16_ss(tmem, ad, bd, idesc, (kb | kk) != 0);
+                    for (int kk = 0; kk < GEMM_BK / 16; kk++)
+                        umma_f16_ss(d_tmem, ad + 2 * kk, bd + (B_MN ? kk * 128 : 2 * kk), idesc, (kb | kk) != 0);
+                    umma_commit(empty0 + 8 * s);
+                }
+                umma_commit(accf0 + 8 * ab);
             }
-            umma_commit(empty0 + 8 * s);
         }
-        umma_commit(accb);
-    }
-    __syncwarp();
-
-    // ---------------- epilogue: warp w reads TMEM lanes 32*(w%4).., column half w/4
-    bool ok = mbar_wait(accb, 0, err, DEV_ERR_TIMEOUT_ACC);
-    __syncwarp();
-    tc_fence_after();
-    const int q = warp & 3, half = warp >> 2;
-    const int row = m0 + q * 32 + lane;
-    const uint32_t t_row = tmem + ((uint32_t)(q * 32) << 16);
-    const bool f32o = ep.out_f32 != 0;
-    if (ok) {
-        if (!ep.swiglu) {
+    } else if (warp >= 4) {
+        // ---------------- epilogue: TMEM lane quarter q = warp % 4, column half
+        const int q = warp & 3, half = (warp - 4) >> 2;
+        const uint32_t t_lane = tmem + ((uint32_t)(q * 32) << 16);
+        const bool f32o = ep.out_f32 != 0;
+        bool ok = true;
+        int tl = 0;
+        for (int t = blockIdx.x; t < tiles; t += gridDim.x, tl++) {
+            const int m0 = (t % mt) * GEMM_BM, n0 = (t / mt) * BN;
+            const int ab = tl & 1;
+            ok = mbar_wait(accf0 + 8 * ab, (tl >> 1) & 1, err, DEV_ERR_TIMEOUT_ACC) && ok;
+            tc_fence_after();
+            const uint32_t t_row = t_lane + ab * BN;
+            const int row = m0 + q * 32 + lane;
+            if (!ep.swiglu) {
 #pragma unroll 1
-            for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 32) {
-                float v[32];
-                tmem_ld32(t_row + c, v);
-                tmem_wait_ld();
-                const int col0 = n0 + c;
-                if (row < M) {
+                for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 32) {
+                    float v[32];
+                    tmem_ld32(t_row + c, v);
+                    tmem_wait_ld();
+                    const int col0 = n0 + c;
+                    if (ok && row < M) {
 #pragma unroll
-                    for (int j = 0; j < 32; j += 8) {
-                        int col = col0 + j;
-                        if (col < N) {
-                            if (ep.bias) {
+                        for (int j = 0; j < 32; j += 8) {
+                            const int col = col0 + j;
+                            if (col < N) {
+                                if (ep.bias) {
 #pragma unroll
-                                for (int i = 0; i < 8; i++) v[j + i] += ep.bias[col + i];
+                                    for (int i = 0; i < 8; i++) v[j + i] += ep.bias[col + i];
+                                }
+                                if (ep.resid) {
+                                    float r[8];
+                                    load_row8(ep.resid, f32o, (int64_t)row * ep.ldr + col, r);
+#pragma unroll
+                                    for (int i = 0; i < 8; i++) v[j + i] += r[i];
+                                }
+                                const int64_t ocol = ep.perm_hd ? qkv_unperm_row(col, ep.perm_hd) : col;
+                                store_row8(ep.out, f32o, (int64_t)row * ep.ldo + ocol, v + j);
                             }
-                            if (ep.resid) {
-                                float r[8];
-                                load_row8(ep.resid, f32o, (int64_t)row * ep.ldr + col, r);
+                        }
+                    }
+                }
+            } else {
+                // tile columns [0,128) = gate rows, [128,256) = up rows of the same outputs
+#pragma unroll 1
+                for (int c = half * 64; c < half * 64 + 64; c += 32) {
+                    float g[32], u[32];
+                    tmem_ld32(t_row + c, g);
+                    tmem_ld32(t_row + 128 + c, u);
+                    tmem_wait_ld();
+                    const int ocol0 = n0 / 2 + c;
+                    if (ok && row < M) {
 #pragma unroll
-                                for (int i = 0; i < 8; i++) v[j + i] += r[i];
-                            }
-                            const int64_t ocol = ep.perm_hd ? qkv_unperm_row(col, ep.perm_hd) : col;
-                            store_row8(ep.out, f32o, (int64_t)row * ep.ldo + ocol, v + j);
+                        for (int j = 0; j < 32; j += 8) {
+                            float o[8];
+#pragma unroll
+                            for (int i = 0; i < 8; i++) o[i] = silu_f(g[j + i]) * u[j + i];
+                            if (ocol0 + j < N / 2) store_row8(ep.out, f32o, (int64_t)row * ep.ldo + ocol0 + j, o);
                         }
                     }
                 }
             }
-        } else {
-            // tile columns [0,128) = gate rows, [128,256) = up rows of the same outputs
-#pragma unroll 1
-            for (int c = half * 64; c < half * 64 + 64; c += 32) {
-                float g[32], u[32];
-                tmem_ld32(t_row + c, g);
-                tmem_ld32(t_row + 128 + c, u);
-                tmem_wait_ld();
-                const int ocol0 = n0 / 2 + c;
-                if (row < M) {
-#pragma unroll
-                    for (int j = 0; j < 32; j += 8) {
-                        float o[8];
-#pragma unroll
-                        for (int i = 0; i < 8; i++) o[i] = silu_f(g[j + i]) * u[j + i];
-                        if (ocol0 + j < N / 2) store_row8(ep.out, f32o, (int64_t)row * ep.ldo + ocol0 + j, o);
-                    }
-                }
-            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acce0 + 8 * ab);
         }
     }
+    __syncwarp();
     tc_fence_before();
     __syncthreads();
-    if (warp == 1) tmem_dealloc(tmem, BN);
+    if (warp == 1) tmem_dealloc(tmem, 2 * BN);
 }
 
 // =====================================================================
@@ -804,8 +842,9 @@ static int launch_gemm_tc(tb_ctx* ctx, const void* a, const void* b, const Epi& 
     constexpr int smem = gemm_smem_bytes<BN, STAGES>();
     auto kern = gemm_tc_kernel<BN, STAGES, B_MN>;
     TB_CUDA_TRY(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    dim3 grid((N + BN - 1) / BN, (M + GEMM_BM - 1) / GEMM_BM);
-    return launch(ctx, "gemm_tc", kern, grid, dim3(256), smem, ta, tbm, ep, M, N, K, ctx->d_err);
+    const int64_t tiles = (int64_t)((N + BN - 1) / BN) * ((M + GEMM_BM - 1) / GEMM_BM);
+    const int grid = (int)(tiles < ctx->num_sms ? tiles : ctx->num_sms);
+    return launch(ctx, "gemm_tc", kern, dim3(grid), dim3(GEMM_THREADS), smem, ta, tbm, ep, M, N, K, ctx->d_err);
 }
 
 // Cluster size (K splits per weight tile): the largest of 8, 4, 2, 1 that
