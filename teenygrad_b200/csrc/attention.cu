@@ -30,17 +30,27 @@ __device__ __forceinline__ float ex2(float x) {
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 
+// Per (128-query tile, head, image) CTA.  Warp 0 streams K tiles and warp 3 V
+// tiles (TMA, 2-stage rings), warp 1 issues S = Q K^T (M = 128 queries,
+// N = 128 keys) into one of two TMEM buffers and warp 2 issues O += P V
+// (N = D), each on its own issuing thread (one thread issues an MMA per
+// ~80 ns).  Softmax warps 4-7 own one query row per thread (exp2 domain).  A
+// row's reference max is raised (and its O row and sum rescaled) only when a
+// tile's max passes it by 2^8; P = 2^(s - m) <= 256 is otherwise used as is,
+// so a tile normally needs no wait on the previous P V.  P is bf16 in one of
+// two swizzled shared-memory tiles (A operand), V the MN-major B operand.
 template <int D>
 struct AttnCfg {
     static constexpr int BM = 128, BN = 128;
     static constexpr int TILE = 128 * D * 2;           // Q, K or V tile bytes
     static constexpr int P_BYTES = 128 * 128 * 2;
-    static constexpr int SMEM = TILE /*Q*/ + 2 * TILE /*K*/ + 2 * TILE /*V*/ + P_BYTES + 1024 + 256;
+    static constexpr int SMEM = TILE /*Q*/ + 2 * TILE /*K*/ + 2 * TILE /*V*/ + 2 * P_BYTES + 1024 + 256;
     static constexpr int O_COL = 256;                  // TMEM columns: S0 [0,128), S1 [128,256), O
+    static constexpr float RESCALE_LOG2 = 8.f;
 };
 
 template <int D>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(256, 1)
 attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                const __grid_constant__ CUtensorMap tmV, AttnOut out, int Hq, int Hkv, int Sq, int Sk,
                float scale_log2, int causal, int* err) {
@@ -50,19 +60,16 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
     uint8_t* sQ = smem;
     uint8_t* sK = sQ + C::TILE;
     uint8_t* sV = sK + 2 * C::TILE;
-    uint8_t* sP = sV + 2 * C::TILE;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sP + C::P_BYTES);
+    uint8_t* sP = sV + 2 * C::TILE;                  // [2]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * C::P_BYTES);
     const uint32_t q_full = smem_u32(bars + 0);
-    const uint32_t k_full0 = smem_u32(bars + 1);     // [2]
-    const uint32_t v_full0 = smem_u32(bars + 3);     // [2]
-    const uint32_t kv_empty0 = smem_u32(bars + 5);   // [2]
-    const uint32_t s_full0 = smem_u32(bars + 7);     // [2]
-    const uint32_t p_full = smem_u32(bars + 9);
-    const uint32_t o_done = smem_u32(bars + 10);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+    const uint32_t k_full0 = smem_u32(bars + 1), v_full0 = smem_u32(bars + 3);      // [2]
+    const uint32_t k_empty0 = smem_u32(bars + 5), v_empty0 = smem_u32(bars + 7);    // [2]
+    const uint32_t s_full0 = smem_u32(bars + 9), s_free0 = smem_u32(bars + 11);     // [2]
+    const uint32_t p_full0 = smem_u32(bars + 13), p_free0 = smem_u32(bars + 15);    // [2]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
 
     pdl_trigger();
-    pdl_wait();
     const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
     const int q_tile = gridDim.x - 1 - blockIdx.x;   // heaviest causal tiles first
     const int h = blockIdx.y, b = blockIdx.z;
@@ -82,11 +89,13 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
         for (int s = 0; s < 2; s++) {
             mbar_init(k_full0 + 8 * s, 1);
             mbar_init(v_full0 + 8 * s, 1);
-            mbar_init(kv_empty0 + 8 * s, 1);
+            mbar_init(k_empty0 + 8 * s, 1);
+            mbar_init(v_empty0 + 8 * s, 1);
             mbar_init(s_full0 + 8 * s, 1);
+            mbar_init(s_free0 + 8 * s, 4);
+            mbar_init(p_full0 + 8 * s, 4);
+            mbar_init(p_free0 + 8 * s, 1);
         }
-        mbar_init(p_full, 128);
-        mbar_init(o_done, 1);
         fence_barrier_init();
     }
     if (warp == 1) tmem_alloc(smem_u32(tmem_slot), 512);
@@ -94,127 +103,138 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    pdl_wait();
 
-    if (warp == 0) {
+    if (warp == 0 || warp == 3) {
+        // ---------------- producers: warp 0 Q and K tiles, warp 3 V tiles
         if (lane == 0 && n_tiles > 0) {
-            tma_prefetch_desc(&tmQ);
-            tma_prefetch_desc(&tmK);
-            tma_prefetch_desc(&tmV);
-            mbar_expect_tx(q_full, C::TILE);
-            for (int d = 0; d < DB; d++) tma_load_4d(smem_u32(sQ + d * 16384), &tmQ, q_full, 64 * d, h, q0, b);
+            const bool isK = warp == 0;
+            const CUtensorMap* tm = isK ? &tmK : &tmV;
+            uint8_t* ring = isK ? sK : sV;
+            const uint32_t full0 = isK ? k_full0 : v_full0, empty0 = isK ? k_empty0 : v_empty0;
+            tma_prefetch_desc(tm);
+            if (isK) {
+                tma_prefetch_desc(&tmQ);
+                mbar_expect_tx(q_full, C::TILE);
+                for (int d = 0; d < DB; d++) tma_load_4d(smem_u32(sQ + d * 16384), &tmQ, q_full, 64 * d, h, q0, b);
+            }
             int issued = 0;
             for (int j = 0; j < n_tiles; j++) {
-                int st = j & 1;
-                if (j >= 2 && !mbar_wait(kv_empty0 + 8 * st, ((j >> 1) - 1) & 1, err, DEV_ERR_TIMEOUT_EMPTY)) break;
-                mbar_expect_tx(k_full0 + 8 * st, C::TILE);
+                const int st = j & 1;
+                if (j >= 2 && !mbar_wait(empty0 + 8 * st, ((j >> 1) - 1) & 1, err, DEV_ERR_TIMEOUT_EMPTY)) break;
+                mbar_expect_tx(full0 + 8 * st, C::TILE);
                 for (int d = 0; d < DB; d++)
-                    tma_load_4d(smem_u32(sK + st * C::TILE + d * 16384), &tmK, k_full0 + 8 * st, 64 * d, hk, j * C::BN, b);
-                mbar_expect_tx(v_full0 + 8 * st, C::TILE);
-                for (int d = 0; d < DB; d++)
-                    tma_load_4d(smem_u32(sV + st * C::TILE + d * 16384), &tmV, v_full0 + 8 * st, 64 * d, hk, j * C::BN, b);
+                    tma_load_4d(smem_u32(ring + st * C::TILE + d * 16384), tm, full0 + 8 * st, 64 * d, hk, j * C::BN, b);
                 issued = j + 1;
             }
-            mbar_wait(q_full, 0, err, DEV_ERR_TIMEOUT_FULL);
-            for (int j = (issued > 2 ? issued - 2 : 0); j < issued; j++) {
-                mbar_wait(k_full0 + 8 * (j & 1), (j >> 1) & 1, err, DEV_ERR_TIMEOUT_FULL);
-                mbar_wait(v_full0 + 8 * (j & 1), (j >> 1) & 1, err, DEV_ERR_TIMEOUT_FULL);
-            }
+            if (isK) mbar_wait(q_full, 0, err, DEV_ERR_TIMEOUT_FULL);
+            for (int j = (issued > 2 ? issued - 2 : 0); j < issued; j++)
+                mbar_wait(full0 + 8 * (j & 1), (j >> 1) & 1, err, DEV_ERR_TIMEOUT_FULL);
         }
     } else if (warp == 1) {
+        // ---------------- S = Q K^T issuer
         if (lane == 0 && n_tiles > 0) {
             constexpr uint32_t idesc_s = idesc_bf16_f32(128, C::BN, false, false);
-            constexpr uint32_t idesc_o = idesc_bf16_f32(128, D, false, true);
-            const uint32_t q_base = smem_u32(sQ), p_base = smem_u32(sP);
+            const uint64_t q_desc = sdesc_sw128(smem_u32(sQ), 16, 1024);
+            const uint64_t k_desc = sdesc_sw128(smem_u32(sK), 16, 1024);
             bool ok = mbar_wait(q_full, 0, err, DEV_ERR_TIMEOUT_FULL);
-            for (int j = 0; ok && j <= n_tiles; j++) {
-                if (j < n_tiles) {
-                    int st = j & 1;
-                    if (!mbar_wait(k_full0 + 8 * st, (j >> 1) & 1, err, DEV_ERR_TIMEOUT_FULL)) break;
-                    tc_fence_after();
-                    const uint32_t k_base = smem_u32(sK + st * C::TILE);
+            for (int j = 0; ok && j < n_tiles; j++) {
+                const int st = j & 1;
+                if (!mbar_wait(k_full0 + 8 * st, (j >> 1) & 1, err, DEV_ERR_TIMEOUT_FULL)) break;
+                if (j >= 2 && !mbar_wait(s_free0 + 8 * st, ((j >> 1) - 1) & 1, err, DEV_ERR_TIMEOUT_MISC)) break;
+                tc_fence_after();
+                const uint64_t kd = k_desc + (uint64_t)((st * C::TILE) >> 4);
 #pragma unroll
-                    for (int kk = 0; kk < D / 16; kk++) {
-                        uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-                        umma_f16_ss(tmem + st * 128, sdesc_sw128(q_base + off, 16, 1024),
-                                    sdesc_sw128(k_base + off, 16, 1024), idesc_s, kk != 0);
-                    }
-                    umma_commit(s_full0 + 8 * st);
+                for (int kk = 0; kk < D / 16; kk++) {
+                    const uint32_t off = ((kk >> 2) * 16384 + (kk & 3) * 32) >> 4;
+                    umma_f16_ss(tmem + st * 128, q_desc + off, kd + off, idesc_s, kk != 0);
                 }
-                if (j > 0) {
-                    const int jp = j - 1, st = jp & 1;
-                    if (!mbar_wait(p_full, jp & 1, err, DEV_ERR_TIMEOUT_MISC)) break;
-                    if (!mbar_wait(v_full0 + 8 * st, (jp >> 1) & 1, err, DEV_ERR_TIMEOUT_FULL)) break;
-                    tc_fence_after();
-                    const uint32_t v_base = smem_u32(sV + st * C::TILE);
-#pragma unroll
-                    for (int kk = 0; kk < C::BN / 16; kk++) {
-                        uint64_t ad = sdesc_sw128(p_base + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
-                        uint64_t bd = sdesc_sw128(v_base + kk * 16 * 128, 16384, 1024);
-                        umma_f16_ss(tmem + C::O_COL, ad, bd, idesc_o, (jp | kk) != 0);
-                    }
-                    umma_commit(kv_empty0 + 8 * st);
-                    umma_commit(o_done);
-                }
+                umma_commit(k_empty0 + 8 * st);
+                umma_commit(s_full0 + 8 * st);
             }
         }
-    } else {
-        // ---------------- softmax warps 2..5: thread <-> query row
+    } else if (warp == 2) {
+        // ---------------- O += P V issuer
+        if (lane == 0 && n_tiles > 0) {
+            constexpr uint32_t idesc_o = idesc_bf16_f32(128, D, false, true);
+            const uint64_t p_desc = sdesc_sw128(smem_u32(sP), 16, 1024);
+            const uint64_t v_desc = sdesc_sw128(smem_u32(sV), 16384, 1024);
+            for (int j = 0; j < n_tiles; j++) {
+                const int st = j & 1;
+                if (!mbar_wait(p_full0 + 8 * st, (j >> 1) & 1, err, DEV_ERR_TIMEOUT_MISC)) break;
+                if (!mbar_wait(v_full0 + 8 * st, (j >> 1) & 1, err, DEV_ERR_TIMEOUT_FULL)) break;
+                tc_fence_after();
+                const uint64_t pd = p_desc + (uint64_t)((st * C::P_BYTES) >> 4);
+                const uint64_t vd = v_desc + (uint64_t)((st * C::TILE) >> 4);
+#pragma unroll
+                for (int kk = 0; kk < C::BN / 16; kk++)
+                    umma_f16_ss(tmem + C::O_COL, pd + (((kk >> 2) * 16384 + (kk & 3) * 32) >> 4), vd + ((kk * 16 * 128) >> 4),
+                                idesc_o, (j | kk) != 0);
+                umma_commit(v_empty0 + 8 * st);
+                umma_commit(p_free0 + 8 * st);
+            }
+        }
+    } else if (warp >= 4) {
+        // ---------------- softmax warps 4..7: thread <-> query row
         const int quarter = warp & 3;
         const int r = quarter * 32 + lane;
         const int qi = q0 + r;
         const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
-        float m_run = -INFINITY, l_run = 0.f;
+        const int lim = causal ? min(Sk - 1, qi + diag) : Sk - 1;   // last visible key
+        float m_ref = -INFINITY, l_run = 0.f;
         bool ok = true;
         for (int j = 0; j < n_tiles; j++) {
             const int sb = j & 1;
-            ok = mbar_wait(s_full0 + 8 * sb, (j >> 1) & 1, err, DEV_ERR_TIMEOUT_MISC);
-            ok = __all_sync(0xffffffffu, ok);
-            if (!ok) break;
+            ok = mbar_wait(s_full0 + 8 * sb, (j >> 1) & 1, err, DEV_ERR_TIMEOUT_MISC) && ok;
             tc_fence_after();
             float s[128];
 #pragma unroll
             for (int c = 0; c < 4; c++) tmem_ld32(t_lane + sb * 128 + c * 32, s + c * 32);
             tmem_wait_ld();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(s_free0 + 8 * sb);   // S buffer sb may be overwritten
             const int k0 = j * C::BN;
-            const int lim = causal ? min(Sk - 1, qi + diag) : Sk - 1;   // last visible key
             float mx = -INFINITY;
 #pragma unroll
             for (int c = 0; c < 128; c++) {
-                float v = (k0 + c <= lim) ? s[c] * scale_log2 : -INFINITY;
+                const float v = (k0 + c <= lim) ? s[c] * scale_log2 : -INFINITY;
                 s[c] = v;
                 mx = fmaxf(mx, v);
             }
-            const float m_new = fmaxf(m_run, mx);
-            const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-            const float alpha = ex2(m_run - m_use);   // m_run = -inf -> 0
+            float alpha = 1.f;
+            if (mx > m_ref + C::RESCALE_LOG2) {   // raise the reference max (m_ref = -inf: first visible tile)
+                alpha = ex2(m_ref - mx);           // -inf -> 0
+                m_ref = mx;
+                l_run *= alpha;
+            }
+            if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+                // O holds P V of tiles < j: rescale this warp's rows once P V_{j-1} is done
+                ok = mbar_wait(p_free0 + 8 * ((j - 1) & 1), ((j - 1) >> 1) & 1, err, DEV_ERR_TIMEOUT_MISC) && ok;
+                tc_fence_after();
+#pragma unroll 1
+                for (int c = 0; c < D; c += 16) {
+                    float o[16];
+                    tmem_ld16(t_lane + C::O_COL + c, o);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 16; i++) o[i] *= alpha;
+                    tmem_st16(t_lane + C::O_COL + c, o);
+                }
+                tmem_wait_st();
+            }
+            const float m_use = (m_ref == -INFINITY) ? 0.f : m_ref;
             float rs = 0.f;
 #pragma unroll
             for (int c = 0; c < 128; c++) {
-                float p = ex2(s[c] - m_use);
+                const float p = ex2(s[c] - m_use);   // s = -inf -> 0
                 s[c] = p;
                 rs += p;
             }
-            l_run = l_run * alpha + rs;
-            m_run = m_new;
-            if (j > 0) {
-                ok = __all_sync(0xffffffffu, mbar_wait(o_done, (j - 1) & 1, err, DEV_ERR_TIMEOUT_MISC));
-                if (!ok) break;
-                tc_fence_after();
-                if (__any_sync(0xffffffffu, alpha != 1.0f)) {
-#pragma unroll 1
-                    for (int c = 0; c < D; c += 16) {
-                        float o[16];
-                        tmem_ld16(t_lane + C::O_COL + c, o);
-                        tmem_wait_ld();
-#pragma unroll
-                        for (int i = 0; i < 16; i++) o[i] *= alpha;
-                        tmem_st16(t_lane + C::O_COL + c, o);
-                    }
-                    tmem_wait_st();
-                }
-            }
-            // P row -> shared memory, 128-B swizzled K-major (keys) tile
-            uint8_t* prow = sP + r * 128;
+            l_run += rs;
+            // P row -> shared memory tile sb (free once P V_{j-2} is done), 128-B swizzled K-major
+            if (j >= 2) ok = mbar_wait(p_free0 + 8 * sb, ((j - 2) >> 1) & 1, err, DEV_ERR_TIMEOUT_MISC) && ok;
+            uint8_t* prow = sP + sb * C::P_BYTES + r * 128;
 #pragma unroll
             for (int ch = 0; ch < 16; ch++) {
                 const int kc = ch >> 3, c8 = ch & 7;
@@ -227,11 +247,12 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             tc_fence_before();
-            mbar_arrive(p_full);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(p_full0 + 8 * sb);
         }
-        if (ok && n_tiles > 0) {
-            ok = __all_sync(0xffffffffu, mbar_wait(o_done, (n_tiles - 1) & 1, err, DEV_ERR_TIMEOUT_ACC));
-        }
+        if (n_tiles > 0)
+            ok = mbar_wait(p_free0 + 8 * ((n_tiles - 1) & 1), ((n_tiles - 1) >> 1) & 1, err, DEV_ERR_TIMEOUT_ACC) && ok;
+        ok = __all_sync(0xffffffffu, ok);
         if (ok) {
             tc_fence_after();
             const float inv_l = (l_run > 0.f) ? 1.0f / l_run : 0.f;
@@ -261,7 +282,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
                 }
             }
             if (valid && out.lse) {
-                float lse = (l_run > 0.f) ? (m_run + log2f(l_run)) * kLn2 : -INFINITY;
+                const float lse = (l_run > 0.f) ? (m_ref + log2f(l_run)) * kLn2 : -INFINITY;
                 out.lse[((int64_t)b * Hq + h) * Sq + qi] = lse;
             }
         }
@@ -768,11 +789,11 @@ int attn_tc_launch(tb_ctx* ctx, const AttnTensors& t, int B, int Hq, int Hkv, in
         // 512 TMEM columns per CTA: keep one CTA per SM (the padding does that).
         constexpr int smem = AttnCfg<64>::SMEM > 120 * 1024 ? AttnCfg<64>::SMEM : 120 * 1024;
         TB_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-        return launch(ctx, "attn_tc", attn_tc_kernel<64>, grid, dim3(192), smem, mq, mk, mv, out, Hq, Hkv, Sq, Sk, sl2, causal, ctx->d_err);
+        return launch(ctx, "attn_tc", attn_tc_kernel<64>, grid, dim3(256), smem, mq, mk, mv, out, Hq, Hkv, Sq, Sk, sl2, causal, ctx->d_err);
     } else {
         constexpr int smem = AttnCfg<128>::SMEM;
         TB_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-        return launch(ctx, "attn_tc", attn_tc_kernel<128>, grid, dim3(192), smem, mq, mk, mv, out, Hq, Hkv, Sq, Sk, sl2, causal, ctx->d_err);
+        return launch(ctx, "attn_tc", attn_tc_kernel<128>, grid, dim3(256), smem, mq, mk, mv, out, Hq, Hkv, Sq, Sk, sl2, causal, ctx->d_err);
     }
     return check_launch(ctx, "attn_tc");
 }

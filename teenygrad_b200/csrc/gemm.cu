@@ -276,8 +276,10 @@ struct GemvCfg {
     static constexpr int TMEM_COLS = (2 * NT) < 32 ? 32 : (2 * NT);
 };
 
+constexpr int GEMV_THREADS = 288;   // warp 0 TMA, warps 1 and 8 MMA (one 128-row half each), 2-7 converters
+
 template <int NT, int STAGES, bool INT8>
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(GEMV_THREADS, 1)
 gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                Epi ep, int Nw, int K, int Mtok, int kb_per_split, int* err) {
     using C = GemvCfg<NT, STAGES, INT8>;
@@ -312,13 +314,13 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
             mbar_init(full0 + 8 * s, 1);
-            mbar_init(empty0 + 8 * s, INT8 ? 1 + N_CONV_WARPS : 1);
+            mbar_init(empty0 + 8 * s, INT8 ? 2 + N_CONV_WARPS : 2);
         }
         for (int s = 0; s < 2; s++) {
             mbar_init(cfull0 + 8 * s, N_CONV_WARPS);
-            mbar_init(cempty0 + 8 * s, 1);
+            mbar_init(cempty0 + 8 * s, 2);
         }
-        mbar_init(accb, 1);
+        mbar_init(accb, 2);
         mbar_init(recvb, 1);
         for (int s = 0; s < STAGES; s++) mbar_init(xrdy0 + 8 * s, N_CONV_WARPS);
         fence_barrier_init();
@@ -357,8 +359,11 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
         }
         for (int i = (issued > STAGES ? issued - STAGES : 0); i < issued; i++)
             mbar_wait(full0 + 8 * (i % STAGES), (i / STAGES) & 1, err, DEV_ERR_TIMEOUT_FULL);
-    } else if (warp == 1 && lane == 0) {
+    } else if ((warp == 1 || warp == 8) && lane == 0) {
+        // two issuing threads (one MMA per ~80 ns each): warp 1 the weight rows
+        // [0, 128) of the tile, warp 8 the rows [128, 256), into separate accumulators
         constexpr uint32_t idesc = idesc_bf16_f32(128, NT, false, false);
+        const int h = warp == 1 ? 0 : 1;
         for (int i = 0; i < nk; i++) {
             int s = i % STAGES;
             uint32_t w_base;
@@ -376,18 +381,15 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
             uint32_t x_base = smem_u32(sX + s * C::X_BYTES);
 #pragma unroll
             for (int kk = 0; kk < 4; kk++) {
-                uint64_t bd = sdesc_sw128(x_base + kk * 32, 16, 1024);
-#pragma unroll
-                for (int h = 0; h < 2; h++) {
-                    uint64_t ad = sdesc_sw128(w_base + h * 128 * 128 + kk * 32, 16, 1024);
-                    umma_f16_ss(tmem + h * NT, ad, bd, idesc, (i | kk) != 0);
-                }
+                const uint64_t bd = sdesc_sw128(x_base + kk * 32, 16, 1024);
+                const uint64_t ad = sdesc_sw128(w_base + h * 128 * 128 + kk * 32, 16, 1024);
+                umma_f16_ss(tmem + h * NT, ad, bd, idesc, (i | kk) != 0);
             }
             if (INT8) umma_commit(cempty0 + 8 * (i & 1));
             umma_commit(empty0 + 8 * s);
         }
         umma_commit(accb);
-    } else if ((INT8 || NORM) && warp >= 2) {
+    } else if ((INT8 || NORM) && warp >= 2 && warp < 8) {
         // ---------------- converter warps 2..7: the normalised activation tile
         // (when the RMSNorm is fused) and int8 -> bf16 weights (int8 path)
         const int ct = threadIdx.x - 64;   // 0..191
@@ -510,14 +512,17 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
     const int l = q * 32 + lane;
     const uint32_t t_row = tmem + ((uint32_t)(q * 32) << 16);
     float acc[2][TP];
+    const bool ewarp = warp < 8;   // warps 0-7 hold the accumulator; warp 8 only joins the barriers
+    if (ewarp) {
 #pragma unroll
-    for (int h = 0; h < 2; h++) {
-        if (TP == 8) tmem_ld8(t_row + h * NT + part * TP, acc[h]);
-        else if (TP == 16) tmem_ld16(t_row + h * NT + part * TP, acc[h]);
-        else tmem_ld32(t_row + h * NT + part * TP, acc[h]);
+        for (int h = 0; h < 2; h++) {
+            if (TP == 8) tmem_ld8(t_row + h * NT + part * TP, acc[h]);
+            else if (TP == 16) tmem_ld16(t_row + h * NT + part * TP, acc[h]);
+            else tmem_ld32(t_row + h * NT + part * TP, acc[h]);
+        }
+        tmem_wait_ld();
     }
-    tmem_wait_ld();
-    if (nk <= 0 || !ok) {
+    if (nk <= 0 || !ok || !ewarp) {
 #pragma unroll
         for (int h = 0; h < 2; h++)
 #pragma unroll
@@ -603,7 +608,7 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
             if (threadIdx.x < NT) s_ss[threadIdx.x] = rsqrtf(s_ss[threadIdx.x] * inv_k + ep.norm_eps);
             __syncthreads();
         }
-        if (ok) {
+        if (ok && ewarp) {
 #pragma unroll
             for (int t = 0; t < TP; t++) {
                 const int m = part * TP + t;
@@ -629,7 +634,7 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
         const int owner = l / P, pl = l % P;
         if (threadIdx.x == 0) mbar_expect_tx(recvb, (uint32_t)((CS - 1) * (PF + (NORM ? NT : 0)) * 4));
         asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");   // all peers' rings are free
-        {
+        if (ewarp) {
             const int off = split * SF + (part * TP * P + pl) * 2;   // token part * TP, pair pl
             if (owner == split) {
 #pragma unroll
@@ -647,7 +652,7 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
                                  : "memory");
             }
         }
-        if (NORM) {
+        if (NORM && ewarp) {
             for (int it = threadIdx.x; it < CS * NT; it += 256) {
                 const int r = it / NT, m = it % NT;
                 const uint32_t dst = smem_u32(recvf + split * SF + PF + m);
@@ -678,7 +683,7 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
             __syncthreads();
         }
         const int items = P * NT;
-        for (int it = threadIdx.x; it < items; it += 256) {
+        for (int it = threadIdx.x; ewarp && it < items; it += 256) {
             const int m = it / P, pl2 = it % P;
             float2 v[16];   // all loads in flight, then a fixed-order sum
 #pragma unroll
@@ -890,7 +895,7 @@ static int launch_gemv_tc(tb_ctx* ctx, const void* x, const void* w, const Epi& 
         int n = 0;
         cudaLaunchConfig_t q = {};
         q.gridDim = dim3(1, 16, 1);
-        q.blockDim = dim3(256, 1, 1);
+        q.blockDim = dim3(GEMV_THREADS, 1, 1);
         q.dynamicSmemBytes = C::SMEM;
         cudaLaunchAttribute qa[1];
         qa[0].id = cudaLaunchAttributeClusterDimension;
@@ -910,7 +915,7 @@ static int launch_gemv_tc(tb_ctx* ctx, const void* x, const void* w, const Epi& 
     TB_CUDA_TRY(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     cudaLaunchConfig_t lc = {};
     lc.gridDim = dim3(tiles, cs, 1);
-    lc.blockDim = dim3(256, 1, 1);
+    lc.blockDim = dim3(GEMV_THREADS, 1, 1);
     lc.dynamicSmemBytes = C::SMEM;
     lc.stream = ctx->stream;
     cudaLaunchAttribute attr[2];
