@@ -23,7 +23,7 @@ namespace tb {
 
 __device__ __forceinline__ float ex2(float x) {
     float y;
-    asm volatile("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));   // pure: free to schedule
     return y;
 }
 
@@ -34,7 +34,9 @@ constexpr float kLn2 = 0.6931471805599453f;
 // tiles (TMA, 2-stage rings), warp 1 issues S = Q K^T (M = 128 queries,
 // N = 128 keys) into one of two TMEM buffers and warp 2 issues O += P V
 // (N = D), each on its own issuing thread (one thread issues an MMA per
-// ~80 ns).  Softmax warps 4-7 own one query row per thread (exp2 domain).  A
+// ~80 ns).  Softmax warps 4-11: two per row quarter, one query row and half
+// of each tile's keys per thread (exp2 domain); each half has its own running
+// max, sum and O accumulator, merged at the end.  A
 // row's reference max is raised (and its O row and sum rescaled) only when a
 // tile's max passes it by 2^8; P = 2^(s - m) <= 256 is otherwise used as is,
 // so a tile normally needs no wait on the previous P V.  P is bf16 in one of
@@ -45,12 +47,14 @@ struct AttnCfg {
     static constexpr int TILE = 128 * D * 2;           // Q, K or V tile bytes
     static constexpr int P_BYTES = 128 * 128 * 2;
     static constexpr int SMEM = TILE /*Q*/ + 2 * TILE /*K*/ + 2 * TILE /*V*/ + 2 * P_BYTES + 1024 + 256;
-    static constexpr int O_COL = 256;                  // TMEM columns: S0 [0,128), S1 [128,256), O
+    static constexpr int O_COL = 256;                  // TMEM columns: S0 [0,128), S1 [128,256), O_0, O_1 (D each)
     static constexpr float RESCALE_LOG2 = 8.f;
 };
 
+constexpr int ATTN_THREADS = 384;   // warps 0/3 TMA, 1 S MMA, 2 P.V MMA, 4-11 softmax
+
 template <int D>
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(ATTN_THREADS, 1)
 attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                const __grid_constant__ CUtensorMap tmV, AttnOut out, int Hq, int Hkv, int Sq, int Sk,
                float scale_log2, int causal, int* err) {
@@ -92,8 +96,8 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
             mbar_init(k_empty0 + 8 * s, 1);
             mbar_init(v_empty0 + 8 * s, 1);
             mbar_init(s_full0 + 8 * s, 1);
-            mbar_init(s_free0 + 8 * s, 4);
-            mbar_init(p_full0 + 8 * s, 4);
+            mbar_init(s_free0 + 8 * s, 8);
+            mbar_init(p_full0 + 8 * s, 8);
             mbar_init(p_free0 + 8 * s, 1);
         }
         fence_barrier_init();
@@ -166,20 +170,25 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
                 tc_fence_after();
                 const uint64_t pd = p_desc + (uint64_t)((st * C::P_BYTES) >> 4);
                 const uint64_t vd = v_desc + (uint64_t)((st * C::TILE) >> 4);
+                // keys 0-63 accumulate into O_0 (columns O_COL..), keys 64-127 into O_1 (O_COL + D..)
 #pragma unroll
                 for (int kk = 0; kk < C::BN / 16; kk++)
-                    umma_f16_ss(tmem + C::O_COL, pd + (((kk >> 2) * 16384 + (kk & 3) * 32) >> 4), vd + ((kk * 16 * 128) >> 4),
-                                idesc_o, (j | kk) != 0);
+                    umma_f16_ss(tmem + C::O_COL + (kk >> 2) * D, pd + (((kk >> 2) * 16384 + (kk & 3) * 32) >> 4),
+                                vd + ((kk * 16 * 128) >> 4), idesc_o, (j | (kk & 3)) != 0);
                 umma_commit(v_empty0 + 8 * st);
                 umma_commit(p_free0 + 8 * st);
             }
         }
     } else if (warp >= 4) {
-        // ---------------- softmax warps 4..7: thread <-> query row
-        const int quarter = warp & 3;
+        // ---------------- softmax warps 4..11: thread <-> query row r (TMEM lane quarter
+        // warp % 4) and key columns [64 * hf, 64 * hf + 64) of every tile (hf = (warp - 4) / 4).
+        // Each half keeps its own reference max, row sum and O accumulator (O_hf); the
+        // two are merged once at the end, so no exchange is needed per tile.
+        const int quarter = warp & 3, hf = (warp - 4) >> 2;
         const int r = quarter * 32 + lane;
         const int qi = q0 + r;
         const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
+        const uint32_t o_col = C::O_COL + hf * D;
         const int lim = causal ? min(Sk - 1, qi + diag) : Sk - 1;   // last visible key
         float m_ref = -INFINITY, l_run = 0.f;
         bool ok = true;
@@ -187,21 +196,34 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
             const int sb = j & 1;
             ok = mbar_wait(s_full0 + 8 * sb, (j >> 1) & 1, err, DEV_ERR_TIMEOUT_MISC) && ok;
             tc_fence_after();
-            float s[128];
-#pragma unroll
-            for (int c = 0; c < 4; c++) tmem_ld32(t_lane + sb * 128 + c * 32, s + c * 32);
+            float s[64];
+            tmem_ld32(t_lane + sb * 128 + hf * 64, s);
+            tmem_ld32(t_lane + sb * 128 + hf * 64 + 32, s + 32);
             tmem_wait_ld();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(s_free0 + 8 * sb);   // S buffer sb may be overwritten
-            const int k0 = j * C::BN;
-            float mx = -INFINITY;
+            const int k0 = j * C::BN + hf * 64;
+            // 8 independent max chains (latency, not issue, bounds this loop otherwise)
+            float mx8[8];
 #pragma unroll
-            for (int c = 0; c < 128; c++) {
-                const float v = (k0 + c <= lim) ? s[c] * scale_log2 : -INFINITY;
-                s[c] = v;
-                mx = fmaxf(mx, v);
+            for (int u = 0; u < 8; u++) mx8[u] = -INFINITY;
+            if (k0 + 63 <= lim) {   // every key of this half visible: no mask
+#pragma unroll
+                for (int c = 0; c < 64; c++) {
+                    s[c] *= scale_log2;
+                    mx8[c & 7] = fmaxf(mx8[c & 7], s[c]);
+                }
+            } else {
+#pragma unroll
+                for (int c = 0; c < 64; c++) {
+                    const float v = (k0 + c <= lim) ? s[c] * scale_log2 : -INFINITY;
+                    s[c] = v;
+                    mx8[c & 7] = fmaxf(mx8[c & 7], v);
+                }
             }
+            const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                                   fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
             float alpha = 1.f;
             if (mx > m_ref + C::RESCALE_LOG2) {   // raise the reference max (m_ref = -inf: first visible tile)
                 alpha = ex2(m_ref - mx);           // -inf -> 0
@@ -209,41 +231,42 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
                 l_run *= alpha;
             }
             if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
-                // O holds P V of tiles < j: rescale this warp's rows once P V_{j-1} is done
+                // O_hf holds P V of tiles < j: rescale once P V_{j-1} is done
                 ok = mbar_wait(p_free0 + 8 * ((j - 1) & 1), ((j - 1) >> 1) & 1, err, DEV_ERR_TIMEOUT_MISC) && ok;
                 tc_fence_after();
 #pragma unroll 1
                 for (int c = 0; c < D; c += 16) {
                     float o[16];
-                    tmem_ld16(t_lane + C::O_COL + c, o);
+                    tmem_ld16(t_lane + o_col + c, o);
                     tmem_wait_ld();
 #pragma unroll
                     for (int i = 0; i < 16; i++) o[i] *= alpha;
-                    tmem_st16(t_lane + C::O_COL + c, o);
+                    tmem_st16(t_lane + o_col + c, o);
                 }
                 tmem_wait_st();
             }
             const float m_use = (m_ref == -INFINITY) ? 0.f : m_ref;
-            float rs = 0.f;
+            float rs8[8];
 #pragma unroll
-            for (int c = 0; c < 128; c++) {
+            for (int u = 0; u < 8; u++) rs8[u] = 0.f;
+#pragma unroll
+            for (int c = 0; c < 64; c++) {
                 const float p = ex2(s[c] - m_use);   // s = -inf -> 0
                 s[c] = p;
-                rs += p;
+                rs8[c & 7] += p;
             }
-            l_run += rs;
-            // P row -> shared memory tile sb (free once P V_{j-2} is done), 128-B swizzled K-major
+            l_run += ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
+            // P row half -> shared memory tile sb (free once P V_{j-2} is done): one 64-key atom
             if (j >= 2) ok = mbar_wait(p_free0 + 8 * sb, ((j - 2) >> 1) & 1, err, DEV_ERR_TIMEOUT_MISC) && ok;
-            uint8_t* prow = sP + sb * C::P_BYTES + r * 128;
+            uint8_t* prow = sP + sb * C::P_BYTES + hf * 16384 + r * 128;
 #pragma unroll
-            for (int ch = 0; ch < 16; ch++) {
-                const int kc = ch >> 3, c8 = ch & 7;
+            for (int c8 = 0; c8 < 8; c8++) {
                 uint4 v;
-                v.x = pack_bf16x2(s[ch * 8 + 0], s[ch * 8 + 1]);
-                v.y = pack_bf16x2(s[ch * 8 + 2], s[ch * 8 + 3]);
-                v.z = pack_bf16x2(s[ch * 8 + 4], s[ch * 8 + 5]);
-                v.w = pack_bf16x2(s[ch * 8 + 6], s[ch * 8 + 7]);
-                *reinterpret_cast<uint4*>(prow + kc * 16384 + ((c8 ^ (r & 7)) << 4)) = v;
+                v.x = pack_bf16x2(s[c8 * 8 + 0], s[c8 * 8 + 1]);
+                v.y = pack_bf16x2(s[c8 * 8 + 2], s[c8 * 8 + 3]);
+                v.z = pack_bf16x2(s[c8 * 8 + 4], s[c8 * 8 + 5]);
+                v.w = pack_bf16x2(s[c8 * 8 + 6], s[c8 * 8 + 7]);
+                *reinterpret_cast<uint4*>(prow + ((c8 ^ (r & 7)) << 4)) = v;
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             tc_fence_before();
@@ -252,37 +275,52 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
         }
         if (n_tiles > 0)
             ok = mbar_wait(p_free0 + 8 * ((n_tiles - 1) & 1), ((n_tiles - 1) >> 1) & 1, err, DEV_ERR_TIMEOUT_ACC) && ok;
+        // Every P V is done, so the P tiles are free: exchange (max, sum) of the two halves there.
+        float* xch = reinterpret_cast<float*>(sP);   // [2 halves][128 rows][2]
+        xch[(hf * 128 + r) * 2] = m_ref;
+        xch[(hf * 128 + r) * 2 + 1] = l_run;
+        asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
+        const float m_o = xch[((hf ^ 1) * 128 + r) * 2], l_o = xch[((hf ^ 1) * 128 + r) * 2 + 1];
+        const float M = fmaxf(m_ref, m_o);
+        const float w_a = (hf == 0 ? m_ref : m_o) == -INFINITY ? 0.f : ex2((hf == 0 ? m_ref : m_o) - M);
+        const float w_b = (hf == 0 ? m_o : m_ref) == -INFINITY ? 0.f : ex2((hf == 0 ? m_o : m_ref) - M);
+        const float l_tot = (hf == 0 ? l_run : l_o) * w_a + (hf == 0 ? l_o : l_run) * w_b;
         ok = __all_sync(0xffffffffu, ok);
         if (ok) {
             tc_fence_after();
-            const float inv_l = (l_run > 0.f) ? 1.0f / l_run : 0.f;
+            const float inv_l = (l_tot > 0.f) ? 1.0f / l_tot : 0.f;
+            const float ca = w_a * inv_l, cb = w_b * inv_l;
             const bool valid = qi < Sq;
             const int64_t obase = (int64_t)b * out.o_sb + (int64_t)h * out.o_sh + (int64_t)qi * out.o_ss;
 #pragma unroll 1
-            for (int c = 0; c < D; c += 32) {
-                float o[32];
+            for (int c = hf * (D / 2); c < (hf + 1) * (D / 2); c += 32) {
+                float oa[32], ob[32];
                 if (n_tiles > 0) {
-                    tmem_ld32(t_lane + C::O_COL + c, o);
+                    tmem_ld32(t_lane + C::O_COL + c, oa);
+                    tmem_ld32(t_lane + C::O_COL + D + c, ob);
                     tmem_wait_ld();
                 } else {
 #pragma unroll
-                    for (int i = 0; i < 32; i++) o[i] = 0.f;
+                    for (int i = 0; i < 32; i++) oa[i] = ob[i] = 0.f;
                 }
                 if (valid) {
                     __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(out.o) + obase + c;
 #pragma unroll
                     for (int i = 0; i < 32; i += 8) {
+                        float o[8];
+#pragma unroll
+                        for (int e = 0; e < 8; e++) o[e] = oa[i + e] * ca + ob[i + e] * cb;
                         uint4 v;
-                        v.x = pack_bf16x2(o[i] * inv_l, o[i + 1] * inv_l);
-                        v.y = pack_bf16x2(o[i + 2] * inv_l, o[i + 3] * inv_l);
-                        v.z = pack_bf16x2(o[i + 4] * inv_l, o[i + 5] * inv_l);
-                        v.w = pack_bf16x2(o[i + 6] * inv_l, o[i + 7] * inv_l);
+                        v.x = pack_bf16x2(o[0], o[1]);
+                        v.y = pack_bf16x2(o[2], o[3]);
+                        v.z = pack_bf16x2(o[4], o[5]);
+                        v.w = pack_bf16x2(o[6], o[7]);
                         *reinterpret_cast<uint4*>(dst + i) = v;
                     }
                 }
             }
-            if (valid && out.lse) {
-                const float lse = (l_run > 0.f) ? (m_ref + log2f(l_run)) * kLn2 : -INFINITY;
+            if (valid && out.lse && hf == 0) {
+                const float lse = (l_tot > 0.f) ? (M + log2f(l_tot)) * kLn2 : -INFINITY;
                 out.lse[((int64_t)b * Hq + h) * Sq + qi] = lse;
             }
         }
@@ -789,11 +827,11 @@ int attn_tc_launch(tb_ctx* ctx, const AttnTensors& t, int B, int Hq, int Hkv, in
         // 512 TMEM columns per CTA: keep one CTA per SM (the padding does that).
         constexpr int smem = AttnCfg<64>::SMEM > 120 * 1024 ? AttnCfg<64>::SMEM : 120 * 1024;
         TB_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-        return launch(ctx, "attn_tc", attn_tc_kernel<64>, grid, dim3(256), smem, mq, mk, mv, out, Hq, Hkv, Sq, Sk, sl2, causal, ctx->d_err);
+        return launch(ctx, "attn_tc", attn_tc_kernel<64>, grid, dim3(ATTN_THREADS), smem, mq, mk, mv, out, Hq, Hkv, Sq, Sk, sl2, causal, ctx->d_err);
     } else {
         constexpr int smem = AttnCfg<128>::SMEM;
         TB_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-        return launch(ctx, "attn_tc", attn_tc_kernel<128>, grid, dim3(256), smem, mq, mk, mv, out, Hq, Hkv, Sq, Sk, sl2, causal, ctx->d_err);
+        return launch(ctx, "attn_tc", attn_tc_kernel<128>, grid, dim3(ATTN_THREADS), smem, mq, mk, mv, out, Hq, Hkv, Sq, Sk, sl2, causal, ctx->d_err);
     }
     return check_launch(ctx, "attn_tc");
 }
