@@ -367,9 +367,14 @@ def run_c4(args, rank, world, local):
     del wts
     dom_decode = ms_decode * (G - 1) >= ms_prefill
     if dom_decode:
+        # DRAM traffic per launch: the ncu capture of the gate/up GEMV (profiles/gemv_tc_decode_gate_up.md:
+        # 68.01 MB read + written for 67.4 MB of algorithmic bytes) scaled to the average launch of the step
+        traffic = round(gemv_bytes / (4 * nl) * (68.01 / 67.4))
         roof = {"kernel": "gemv_tc_kernel (decode linear layers, bf16 weights, 16 tokens)", "bound": "hbm",
                 "achieved": round(gemv_gbs, 1), "peak": pk["hbm"], "unit": "GB/s",
-                "frac": round(gemv_gbs / pk["hbm"], 3), "traffic": None, "peak_source": pk["src"]}
+                "frac": round(gemv_gbs / pk["hbm"], 3), "traffic": traffic,
+                "traffic_note": "bytes per average launch: ncu dram bytes / algorithmic bytes of the gate/up GEMV capture, times the average algorithmic bytes",
+                "peak_source": pk["src"]}
     else:
         roof = {"kernel": "gemm_tc_kernel (prefill gate/up, 16384x16384x2048)", "bound": "tensor",
                 "achieved": round(gemm_tflops, 1), "peak": pk["tc"], "unit": "TFLOP/s",
@@ -542,6 +547,51 @@ def run_c1(args, rank, world, local):
                        "timing": "CUDA graph of one block forward (latency-bound: 9 library kernels + 4 torch layout copies)"}}
 
 
+def ncu_case(which):
+    """Small fixed cases for ncu captures of one kernel kind (the commands in profiles/):
+    gemv, attn_dec, gemm, fa, conv, or c4 (prefill + 3 decode steps for the launch list)."""
+    import torch
+    from teenygrad_b200 import ops
+    torch.manual_seed(0)
+    if which == "gemv":          # decode gate/up GEMV (SwiGLU), 16 tokens, 3 distinct weights
+        ws = [(torch.randn(16384, 2048, device="cuda") * 0.02).bfloat16() for _ in range(3)]
+        x = torch.randn(16, 2048, device="cuda").bfloat16()
+        for w in ws:
+            ops.linear(x, w, swiglu=True)
+    elif which == "attn_dec":    # C4 decode attention layer: 16 seqs x 8 kv heads x 1100 keys, G = 4
+        q = torch.randn(16, 32, 1, 64, device="cuda").bfloat16()
+        k = torch.randn(16, 8, 1100, 64, device="cuda").bfloat16()
+        v = torch.randn(16, 8, 1100, 64, device="cuda").bfloat16()
+        for _ in range(3):
+            ops.attention(q, k, v, causal=True)
+    elif which == "gemm":        # C4 prefill gate/up GEMM 16384 x 16384 x 2048 with SwiGLU
+        w = (torch.randn(16384, 2048, device="cuda") * 0.02).bfloat16()
+        x = torch.randn(16384, 2048, device="cuda").bfloat16()
+        for _ in range(2):
+            ops.linear(x, w, swiglu=True)
+    elif which == "fa":          # an 8-head slice of C3: B1 H8 S4096 D128 causal
+        q, k, v = (torch.randn(1, 8, 4096, 128, device="cuda").bfloat16() for _ in range(3))
+        for _ in range(2):
+            ops.attention(q, k, v, causal=True)
+    elif which == "conv":        # one C2 conv: B32 64->64 56x56 3x3 + BN + ReLU
+        x = torch.randn(32, 64, 56, 56, device="cuda").bfloat16()
+        w = (torch.randn(64, 64, 3, 3, device="cuda") * 0.05).bfloat16()
+        sc, sh = torch.ones(64, device="cuda"), torch.zeros(64, device="cuda")
+        for _ in range(2):
+            ops.conv2d(x, w, scale=sc, shift=sh, pad=1, act="relu")
+    elif which == "c4":          # C4 decoder: prefill 16 x 1024 + 3 graph-replayed decode steps
+        from teenygrad_b200.decoder import Decoder, DecoderConfig
+        dec = Decoder(DecoderConfig(max_batch=16, max_seq=1024 + 128, max_prefill_tokens=16 * 1024))
+        dec.init_random(1)
+        dec.prefill(torch.randint(0, 32000, (16, 1024), dtype=torch.int32, device="cuda"))
+        for _ in range(3):
+            dec.decode_step()
+    else:
+        raise SystemExit(f"unknown ncu case {which}")
+    torch.cuda.synchronize()
+    print("ok", which)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -550,7 +600,11 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="c4", choices=["c4", "c5", "c3", "c2", "c1"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ncu-case", default=None, help="run one small profiling case and exit")
     args = ap.parse_args()
+    if args.ncu_case:
+        ncu_case(args.ncu_case)
+        return
     rank = int(os.environ.get("RANK", "0"))
     world_env = int(os.environ.get("WORLD_SIZE", "1"))
 

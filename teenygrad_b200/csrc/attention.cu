@@ -208,12 +208,12 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
             float mx8[8];
 #pragma unroll
             for (int u = 0; u < 8; u++) mx8[u] = -INFINITY;
-            if (k0 + 63 <= lim) {   // every key of this half visible: no mask
+            // every key of this half visible (and a positive scale): the max of the raw
+            // scores, scaled once; the scale is folded into the exponent's FMA below
+            const bool raw = k0 + 63 <= lim && scale_log2 > 0.f;
+            if (raw) {
 #pragma unroll
-                for (int c = 0; c < 64; c++) {
-                    s[c] *= scale_log2;
-                    mx8[c & 7] = fmaxf(mx8[c & 7], s[c]);
-                }
+                for (int c = 0; c < 64; c++) mx8[c & 7] = fmaxf(mx8[c & 7], s[c]);
             } else {
 #pragma unroll
                 for (int c = 0; c < 64; c++) {
@@ -222,8 +222,9 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
                     mx8[c & 7] = fmaxf(mx8[c & 7], v);
                 }
             }
-            const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                                   fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+            float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+            if (raw) mx *= scale_log2;
             float alpha = 1.f;
             if (mx > m_ref + C::RESCALE_LOG2) {   // raise the reference max (m_ref = -inf: first visible tile)
                 alpha = ex2(m_ref - mx);           // -inf -> 0
@@ -249,11 +250,20 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
             float rs8[8];
 #pragma unroll
             for (int u = 0; u < 8; u++) rs8[u] = 0.f;
+            if (raw) {
 #pragma unroll
-            for (int c = 0; c < 64; c++) {
-                const float p = ex2(s[c] - m_use);   // s = -inf -> 0
-                s[c] = p;
-                rs8[c & 7] += p;
+                for (int c = 0; c < 64; c++) {
+                    const float p = ex2(fmaf(s[c], scale_log2, -m_use));
+                    s[c] = p;
+                    rs8[c & 7] += p;
+                }
+            } else {
+#pragma unroll
+                for (int c = 0; c < 64; c++) {
+                    const float p = ex2(s[c] - m_use);   // s = -inf -> 0
+                    s[c] = p;
+                    rs8[c & 7] += p;
+                }
             }
             l_run += ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
             // P row half -> shared memory tile sb (free once P V_{j-2} is done): one 64-key atom
