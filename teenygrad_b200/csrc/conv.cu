@@ -139,7 +139,7 @@ constexpr int CONV_WS = 4;                               // weight ring slices (
 constexpr int CONV_W_BYTES = CONV_BN * 128;              // [64 couts][64 channels] bf16
 constexpr int CONV_OUT_BYTES = CONV_NPIX * CONV_BN * 2;   // [32 rows][64 couts][8 columns] bf16
 constexpr int CONV_TMEM = 2 * CONV_NPIX;                  // two 256-column accumulators
-constexpr int CONV_THREADS = 320;                         // warps 0 TMA, 1 MMA, 4-5 + 8-9 epilogue
+constexpr int CONV_THREADS = 320;                         // warps 0 TMA, 1-2 MMA, 4-5 + 8-9 epilogue
 
 __host__ __device__ constexpr int conv_pw(int KW) { return CONV_BW + KW - 1; }
 __host__ __device__ constexpr int conv_patch_bytes(int KH, int KW) { return (CONV_BH + KH - 1) * conv_pw(KW) * 128; }
@@ -266,21 +266,24 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ 
                 mbar_wait(w_full0 + 8 * (k % CONV_WS), (k / CONV_WS) & 1, err, DEV_ERR_TIMEOUT_FULL);
             if (wres && blockIdx.x < units) mbar_wait(w_full0, 0, err, DEV_ERR_TIMEOUT_FULL);
         }
-    } else if (warp == 1) {
-        // ---------------- MMA issuer: D^T[couts][pixels] += W_tap (A) x patch_tap (B)
+    } else if (warp == 1 || warp == 2) {
+        // ---------------- MMA issuers: D^T[couts][pixels] += W_tap (A) x patch_tap (B).
+        // Warp 1 issues the CTA's even tiles (accumulator 0), warp 2 the odd ones
+        // (accumulator 1): one thread issues an MMA per ~80 ns, two keep the pipe busier.
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_bf16_f32(128, CONV_NPIX, false, false);
             // descriptors built once; an operand at byte offset o adds o >> 4 (start-address field)
             const uint64_t b_desc0 = sdesc_sw128(smem_u32(sP), 16, (uint32_t)PW * 128);
             const uint64_t a_desc0 = sdesc_sw128(smem_u32(sW), 16, 1024);
-            int pi = 0, wi = 0, tl = 0;
+            const int par = warp - 1;   // tile parity of this issuer
             bool ok = !wres || blockIdx.x >= units || mbar_wait(w_full0, 0, err, DEV_ERR_TIMEOUT_FULL);
-            for (int t = blockIdx.x; ok && t < units; t += gridDim.x, tl++) {
+            for (int t = blockIdx.x + par * gridDim.x, tl = par; ok && t < units; t += 2 * gridDim.x, tl += 2) {
                 const int ab = tl & 1;
                 if (tl >= 2 && !mbar_wait(acc_empty0 + 8 * ab, ((tl >> 1) - 1) & 1, err, DEV_ERR_TIMEOUT_MISC)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem + ab * CONV_NPIX;
                 for (int c = 0; ok && c < nc; c++) {
+                    const int pi = tl * nc + c;          // patch sequence number (producer order)
                     const int sp = pi % AS;
                     if (!mbar_wait(p_full0 + 8 * sp, (pi / AS) & 1, err, DEV_ERR_TIMEOUT_FULL)) {
                         ok = false;
@@ -288,6 +291,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ 
                     }
                     const uint64_t b_st = b_desc0 + (uint64_t)((sp * a_bytes) >> 4);
                     for (int tap = 0, kh = 0, kw = 0; tap < taps; tap++) {
+                        const int wi = pi * taps + tap;  // weight slice sequence number (streaming mode)
                         const int sw = wres ? c * taps + tap : wi % CONV_WS;
                         if (!wres && !mbar_wait(w_full0 + 8 * sw, (wi / CONV_WS) & 1, err, DEV_ERR_TIMEOUT_FULL)) {
                             ok = false;
@@ -299,17 +303,13 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ 
 #pragma unroll
                         for (int kk = 0; kk < 4; kk++)
                             umma_f16_ss(d_tmem, a_tap + 2 * kk, b_tap + 2 * kk, idesc, (c | tap | kk) != 0);
-                        if (!wres) {
-                            umma_commit(w_empty0 + 8 * sw);
-                            wi++;
-                        }
+                        if (!wres) umma_commit(w_empty0 + 8 * sw);
                         if (++kw == KW) {
                             kw = 0;
                             kh++;
                         }
                     }
                     umma_commit(p_empty0 + 8 * sp);
-                    pi++;
                 }
                 umma_commit(acc_full0 + 8 * ab);
             }
