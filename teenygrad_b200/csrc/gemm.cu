@@ -855,13 +855,14 @@ static int launch_gemm_tc(tb_ctx* ctx, const void* a, const void* b, const Epi& 
 // Cluster size (K splits per weight tile): the largest of 8, 4, 2, 1 that
 // keeps the grid within two CTAs per SM and every split >= 2 K-blocks.
 // Split-K factor: the largest power of two <= max_cs that keeps the grid
-// within two CTAs per SM (the second slot lets the next kernel's CTAs start
-// streaming their weights early) and gives every CTA at least two K-blocks.
-static void gemv_split(int num_sms, int max_cs, int Nw, int K, int* splits_out, int* kb_per_out) {
+// within the resident CTA slots (one wave; with two slots per SM the next
+// kernel's CTAs can start streaming their weights early) and gives every CTA
+// at least two K-blocks.
+static void gemv_split(int slots, int max_cs, int Nw, int K, int* splits_out, int* kb_per_out) {
     const int tiles = (Nw + 255) / 256;
     const int nk = (K + 63) / 64;
     int cs = max_cs;
-    while (cs > 1 && (tiles * cs > 2 * num_sms || nk < 2 * cs)) cs >>= 1;
+    while (cs > 1 && (tiles * cs > slots || nk < 2 * cs)) cs >>= 1;
     int kb_per = (nk + cs - 1) / cs;
     *splits_out = cs;
     *kb_per_out = kb_per;
@@ -910,7 +911,10 @@ static int launch_gemv_tc(tb_ctx* ctx, const void* x, const void* w, const Epi& 
         max_cs.store(ok16 ? 16 : 8);
     }
     int cs, kb_per;
-    gemv_split(ctx->num_sms, max_cs.load(), Nw, K, &cs, &kb_per);
+    // resident CTA slots: two per SM when two rings fit in shared memory (the
+    // int8 and 64-token configurations hold one)
+    constexpr int per_sm = 2 * (C::SMEM + 1024) <= 228 * 1024 ? 2 : 1;
+    gemv_split(per_sm * ctx->num_sms, max_cs.load(), Nw, K, &cs, &kb_per);
     const int tiles = (Nw + 255) / 256;
     TB_CUDA_TRY(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     cudaLaunchConfig_t lc = {};
