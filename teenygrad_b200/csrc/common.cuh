@@ -274,6 +274,18 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// Four signed bytes -> four bf16 (exact), without int->float conversions.  With
+// l = b & 0x7f and the sign bit b & 0x80: bf16 bits 0x43 : l are 128 + l (7-bit
+// mantissa under the exponent of 128.0) and 0x43 : (b & 0x80) are 128 or 256, so
+// b = (128 + l) - (128 or 256); one bf16x2 FMA per pair, exact for [-128, 127].
+__device__ __forceinline__ void i8x4_to_bf16x4(uint32_t w, uint32_t& lo, uint32_t& hi) {
+    const uint32_t m7 = w & 0x7f7f7f7fu, m8 = w & 0x80808080u;
+    const uint32_t a0 = __byte_perm(m7, 0x43u, 0x4140), a1 = __byte_perm(m7, 0x43u, 0x4342);
+    const uint32_t c0 = __byte_perm(m8, 0x43u, 0x4140), c1 = __byte_perm(m8, 0x43u, 0x4342);
+    asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(lo) : "r"(c0), "r"(0xbf80bf80u), "r"(a0));   // a - c
+    asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(hi) : "r"(c1), "r"(0xbf80bf80u), "r"(a1));
+}
+
 __device__ __forceinline__ float bf16_lo(uint32_t v) { return __uint_as_float(v << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }
 

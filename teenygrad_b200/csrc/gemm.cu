@@ -464,12 +464,7 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
                     uint32_t w4[4] = {raw.x, raw.y, raw.z, raw.w};
                     uint32_t o[8];
 #pragma unroll
-                    for (int j = 0; j < 4; j++) {
-                        int b0 = (int)(int8_t)(w4[j] & 0xff), b1 = (int)(int8_t)((w4[j] >> 8) & 0xff);
-                        int b2 = (int)(int8_t)((w4[j] >> 16) & 0xff), b3 = (int)(int8_t)(w4[j] >> 24);
-                        o[2 * j] = pack_bf16x2((float)b0, (float)b1);
-                        o[2 * j + 1] = pack_bf16x2((float)b2, (float)b3);
-                    }
+                    for (int j = 0; j < 4; j++) i8x4_to_bf16x4(w4[j], o[2 * j], o[2 * j + 1]);
                     int p0 = ((2 * ch) ^ (r & 7)) * 16, p1 = ((2 * ch + 1) ^ (r & 7)) * 16;
                     *reinterpret_cast<uint4*>(dst + r * 128 + p0) = make_uint4(o[0], o[1], o[2], o[3]);
                     *reinterpret_cast<uint4*>(dst + r * 128 + p1) = make_uint4(o[4], o[5], o[6], o[7]);
@@ -538,9 +533,54 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
         if (f32o) reinterpret_cast<float*>(ep.out)[off] = o;
         else reinterpret_cast<__nv_bfloat16*>(ep.out)[off] = __float2bfloat16_rn(o);
     };
-    // epilogue for (token m, row pair p): gate/first row p, second row p + 128
-    auto finish = [&](int m, int p, float a0, float a1) {
-        const int n0 = tile * 256 + p, n1 = n0 + 128;
+    // Epilogue of (token m, row pair p): gate/first row p, second row p + 128 of the tile.
+    // A thread's row pair is fixed (the CS == 1 path: p = l; the cluster path: 256 is a
+    // multiple of P), so its per-pair inputs (scales, bias, RoPE position and angle) are
+    // loaded once; per token only the residual is read.
+    struct PairK {
+        int p, n0, n1;
+        bool in0, in1;
+        float sc0, sc1, bi0, bi1;
+        int kind, hd, hh, H, ri, posb;   // RoPE: kind 0 q, 1 k, 2 v, 3 no head
+        float2 cs;
+    };
+    auto pair_consts = [&](int p) {
+        PairK k{};
+        k.p = p;
+        k.n0 = tile * 256 + p;
+        k.n1 = k.n0 + 128;
+        k.in0 = k.n0 < Nw;
+        k.in1 = k.n1 < Nw;
+        k.sc0 = (ep.scale && k.in0) ? ep.scale[k.n0] : 1.f;
+        k.sc1 = (ep.scale && k.in1) ? ep.scale[k.n1] : 1.f;
+        k.bi0 = (ep.bias && !ep.swiglu && k.in0) ? ep.bias[k.n0] : 0.f;
+        k.bi1 = (ep.bias && !ep.swiglu && k.in1) ? ep.bias[k.n1] : 0.f;
+        if (ep.rope_tab) {
+            k.hd = ep.perm_hd;
+            k.hh = k.hd / 2;
+            k.H = tile * (256 / k.hd) + p / k.hh;
+            k.ri = p % k.hh;
+            k.kind = k.H < ep.rope_hq ? 0 : k.H < ep.rope_hq + ep.rope_hkv ? 1 : k.H < ep.rope_hq + 2 * ep.rope_hkv ? 2 : 3;
+            k.posb = ep.pos_ptr ? *ep.pos_ptr : ep.pos_host;
+            k.cs = make_float2(1.f, 0.f);
+            if (ep.rope_s_new == 1 && k.kind <= 1 && k.posb >= 0 && k.posb < ep.max_seq)
+                k.cs = ep.rope_tab[(int64_t)k.posb * k.hh + k.ri];
+        }
+        return k;
+    };
+    auto load_resid = [&](const PairK& k, int m, float& r0, float& r1) {
+        r0 = r1 = 0.f;
+        if (!ep.resid || ep.swiglu || ep.rope_tab || m >= Mtok) return;
+        const int64_t roff = (int64_t)m * ep.ldr;
+        if (f32o) {
+            if (k.in0) r0 = reinterpret_cast<const float*>(ep.resid)[roff + k.n0];
+            if (k.in1) r1 = reinterpret_cast<const float*>(ep.resid)[roff + k.n1];
+        } else {
+            if (k.in0) r0 = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(ep.resid)[roff + k.n0]);
+            if (k.in1) r1 = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(ep.resid)[roff + k.n1]);
+        }
+    };
+    auto finish = [&](const PairK& k, int m, float a0, float a1, float r0, float r1) {
         if (NORM) {
             a0 *= s_ss[m];   // 1 / rms of token m
             a1 *= s_ss[m];
@@ -548,58 +588,47 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
         if (ep.rope_tab) {
             // (a0, a1) = dims (i, i + hd/2) of head slot H; the projection is rounded
             // to bf16 first, as the unfused path stores it, then rotated (rotate-half)
-            const int hd = ep.perm_hd, hh = hd / 2;
-            const int H = tile * (256 / hd) + p / hh, i = p % hh;
-            if (H >= ep.rope_hq + 2 * ep.rope_hkv) return;
+            if (k.kind == 3) return;
             const int b = m / ep.rope_s_new, s = m % ep.rope_s_new;
-            const int pos = (ep.pos_ptr ? *ep.pos_ptr : ep.pos_host) + s;
+            const int pos = k.posb + s;
             if (pos < 0 || pos >= ep.max_seq) {
                 atomicOr(err, 1 << 5);
                 return;
             }
-            if (ep.scale) {
-                a0 *= ep.scale[n0];
-                a1 *= ep.scale[n1];
-            }
+            a0 *= k.sc0;
+            a1 *= k.sc1;
             float x0 = __bfloat162float(__float2bfloat16_rn(a0)), x1 = __bfloat162float(__float2bfloat16_rn(a1));
             __nv_bfloat16* dst;
-            if (H < ep.rope_hq + ep.rope_hkv) {
-                const float2 cs = ep.rope_tab[(int64_t)pos * hh + i];
+            if (k.kind <= 1) {
+                const float2 cs = ep.rope_s_new == 1 ? k.cs : ep.rope_tab[(int64_t)pos * k.hh + k.ri];
                 const float y0 = x0 * cs.x - x1 * cs.y, y1 = x1 * cs.x + x0 * cs.y;
                 x0 = y0;
                 x1 = y1;
             }
-            if (H < ep.rope_hq)
-                dst = reinterpret_cast<__nv_bfloat16*>(ep.out) + (int64_t)m * ep.ldo + (int64_t)H * hd;
-            else if (H < ep.rope_hq + ep.rope_hkv)
+            if (k.kind == 0)
+                dst = reinterpret_cast<__nv_bfloat16*>(ep.out) + (int64_t)m * ep.ldo + (int64_t)k.H * k.hd;
+            else if (k.kind == 1)
                 dst = reinterpret_cast<__nv_bfloat16*>(ep.kcache) +
-                      (((int64_t)b * ep.rope_hkv + (H - ep.rope_hq)) * ep.max_seq + pos) * hd;
+                      (((int64_t)b * ep.rope_hkv + (k.H - ep.rope_hq)) * ep.max_seq + pos) * k.hd;
             else
                 dst = reinterpret_cast<__nv_bfloat16*>(ep.vcache) +
-                      (((int64_t)b * ep.rope_hkv + (H - ep.rope_hq - ep.rope_hkv)) * ep.max_seq + pos) * hd;
-            dst[i] = __float2bfloat16_rn(x0);
-            dst[i + hh] = __float2bfloat16_rn(x1);
+                      (((int64_t)b * ep.rope_hkv + (k.H - ep.rope_hq - ep.rope_hkv)) * ep.max_seq + pos) * k.hd;
+            dst[k.ri] = __float2bfloat16_rn(x0);
+            dst[k.ri + k.hh] = __float2bfloat16_rn(x1);
             return;
         }
         if (ep.swiglu) {
-            if (n1 < Nw) {
-                float sg = ep.scale ? ep.scale[n0] : 1.f, su = ep.scale ? ep.scale[n1] : 1.f;
-                store(m, tile * 128 + p, silu_f(a0 * sg) * (a1 * su));
-            }
+            if (k.in1) store(m, tile * 128 + k.p, silu_f(a0 * k.sc0) * (a1 * k.sc1));
             return;
         }
-#pragma unroll
-        for (int h = 0; h < 2; h++) {
-            const int n = h ? n1 : n0;
-            if (n >= Nw) continue;
-            float o = (h ? a1 : a0) * (ep.scale ? ep.scale[n] : 1.f) + (ep.bias ? ep.bias[n] : 0.f);
-            if (ep.resid) {
-                int64_t roff = (int64_t)m * ep.ldr + n;
-                o += f32o ? reinterpret_cast<const float*>(ep.resid)[roff]
-                          : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(ep.resid)[roff]);
-            }
-            store(m, n, o);
+        // acc * scale + bias, then + residual (added only when present, so -0 stays -0)
+        float o0 = a0 * k.sc0 + k.bi0, o1 = a1 * k.sc1 + k.bi1;
+        if (ep.resid) {
+            o0 += r0;
+            o1 += r1;
         }
+        if (k.in0) store(m, k.n0, o0);
+        if (k.in1) store(m, k.n1, o1);
     };
 
     const float inv_k = 1.0f / (float)K;
@@ -609,10 +638,15 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
             __syncthreads();
         }
         if (ok && ewarp) {
+            const PairK k = pair_consts(l);
 #pragma unroll
             for (int t = 0; t < TP; t++) {
                 const int m = part * TP + t;
-                if (m < Mtok) finish(m, l, acc[0][t], acc[1][t]);
+                if (m < Mtok) {
+                    float r0, r1;
+                    load_resid(k, m, r0, r1);
+                    finish(k, m, acc[0][t], acc[1][t], r0, r1);
+                }
             }
         }
         return;
@@ -682,20 +716,25 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
             }
             __syncthreads();
         }
-        const int items = P * NT;
-        for (int it = threadIdx.x; ewarp && it < items; it += 256) {
-            const int m = it / P, pl2 = it % P;
-            float2 v[16];   // all loads in flight, then a fixed-order sum
+        // this thread: row pair pl2 of the owned slice, tokens m = m_first + u * (256 / P)
+        if (ewarp && ok && got) {
+            const int pl2 = threadIdx.x % P, mstep = 256 / P;
+            const PairK k = pair_consts(split * P + pl2);
+            for (int m = threadIdx.x / P; m < NT; m += mstep) {
+                float r0, r1;
+                load_resid(k, m, r0, r1);
+                float2 v[16];   // all loads in flight, then a fixed-order sum
 #pragma unroll
-            for (int r = 0; r < 16; r++)
-                v[r] = r < CS ? *reinterpret_cast<const float2*>(recvf + r * SF + (m * P + pl2) * 2) : make_float2(0.f, 0.f);
-            float a0 = 0.f, a1 = 0.f;
+                for (int r = 0; r < 16; r++)
+                    v[r] = r < CS ? *reinterpret_cast<const float2*>(recvf + r * SF + (m * P + pl2) * 2) : make_float2(0.f, 0.f);
+                float a0 = 0.f, a1 = 0.f;
 #pragma unroll
-            for (int r = 0; r < 16; r++) {
-                a0 += v[r].x;
-                a1 += v[r].y;
+                for (int r = 0; r < 16; r++) {
+                    a0 += v[r].x;
+                    a1 += v[r].y;
+                }
+                if (m < Mtok) finish(k, m, a0, a1, r0, r1);
             }
-            if (ok && got && m < Mtok) finish(m, split * P + pl2, a0, a1);
         }
     }
 }

@@ -196,6 +196,23 @@ def test_int8_linear(M, N, K):
     assert_close(np_of(y), oracle.int8_linear(x, q, s, resid=res), BF16_TOL)
 
 
+@pytest.mark.parametrize("M", [16, 64])
+def test_int8_linear_every_byte_exact(M):
+    # q[n, k] runs through all 256 byte values (-128 included); one-hot token rows pick
+    # column k = m, so y[m, n] = q[n, m] * 1.0 exactly in bf16: checks the int8 -> bf16
+    # weight conversion bit for bit
+    N, K = 256, 256
+    n, k = np.meshgrid(np.arange(N), np.arange(K), indexing="ij")
+    q = (((n + 3 * k) % 256) - 128).astype(np.int8)
+    s = np.ones(N, np.float32)
+    x = np.zeros((M, K), np.float32)
+    x[np.arange(M), np.arange(M)] = 1.0
+    y = ops().int8_linear(to_gpu(x, torch.bfloat16), to_gpu(q, torch.int8), to_gpu(s))
+    got = np_of(y)
+    np.testing.assert_array_equal(got, q[:, :M].T.astype(np.float32))
+    np.testing.assert_array_equal(got, oracle.int8_linear(x, q, s))
+
+
 def test_int8_linear_swiglu():
     r = rng(9)
     M, K, F = 64, 1024, 512
