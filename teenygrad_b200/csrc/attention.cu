@@ -369,6 +369,7 @@ struct DecTcCfg {
     static constexpr int O_COL = 32;                    // TMEM: S^T buffers at 0 and 16, O at 32
     static constexpr int TMEM_COLS = (32 + D) <= 128 ? 128 : 256;
     static constexpr float RESCALE_LOG2 = 8.f;          // raise the reference max past this margin
+    static constexpr int PREFETCH_TILES = 8;            // cache tiles per split warmed in L2 before the wait
 };
 
 __device__ __forceinline__ void dec_cluster_sync() {
@@ -449,6 +450,20 @@ attn_decode_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_cons
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    if ((warp == 0 || warp == 6) && lane == 0) {
+        // Before the previous kernel has finished: warm L2 with this split's first
+        // cache tiles (K by warp 0, V by warp 6).  The length read here is only a
+        // hint (it may still be the previous step's); the tiles are loaded for real
+        // after the wait, and rows written meanwhile are seen there, not here.
+        const int hint = a.len_ptr ? (*reinterpret_cast<const volatile int*>(a.len_ptr) + a.len) : a.len;
+        const int kb = split * a.chunk;
+        const int ke = min(hint, kb + a.chunk);
+        const int nt = ke > kb ? min((ke - kb + 127) / 128, C::PREFETCH_TILES) : 0;
+        const CUtensorMap* tm = warp == 0 ? &tmK : &tmV;
+        const int64_t r0 = ((int64_t)b * a.Hkv + g) * a.kv_rows + kb;
+        for (int j = 0; j < nt; j++)
+            for (int d = 0; d < DB; d++) tma_prefetch_l2_2d(tm, 64 * d, (int)(r0 + 128 * j));
+    }
     pdl_wait();
     const int L = a.len_ptr ? (*a.len_ptr + a.len) : a.len;
     const int kbeg = split * a.chunk;
