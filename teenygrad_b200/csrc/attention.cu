@@ -60,7 +60,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
                float scale_log2, int causal, int* err) {
     using C = AttnCfg<D>;
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* smem = smem_align1024(smem_raw);
     uint8_t* sQ = smem;
     uint8_t* sK = sQ + C::TILE;
     uint8_t* sV = sK + 2 * C::TILE;
@@ -407,7 +407,7 @@ attn_decode_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_cons
     using C = DecTcCfg<D>;
     constexpr int NS = C::NS, DB = D / 64;
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* smem = smem_align1024(smem_raw);
     uint8_t* sK = smem;                        // [NS] K tiles
     uint8_t* sV = sK + NS * C::TILE;           // [NS] V tiles
     uint8_t* sP = sV + NS * C::TILE;           // [2] P tiles

@@ -98,6 +98,14 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* m) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
 }
 
+// 1024-B aligned start of the dynamic shared memory.  Offsetting the shared
+// symbol itself (instead of masking an integer) keeps the shared address space
+// visible to the compiler, so accesses through the result are shared loads and
+// stores rather than generic ones.
+__device__ __forceinline__ uint8_t* smem_align1024(uint8_t* raw) {
+    return raw + ((1024u - (static_cast<uint32_t>(__cvta_generic_to_shared(raw)) & 1023u)) & 1023u);
+}
+
 // Warm L2 with a 2-D box (no shared-memory destination, no completion).  L2 is
 // the coherence point, so a later write by another kernel still reaches a later load.
 __device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* m, int c0, int c1) {

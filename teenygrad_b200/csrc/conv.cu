@@ -167,7 +167,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ 
                const __grid_constant__ CUtensorMap tmY, ConvEpi ep, int B, int OH, int OW, int Cout, int KH, int KW,
                int Cp, int pad, int AS, int wres, int* err) {
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* smem = smem_align1024(smem_raw);
     const int PW = conv_pw(KW);
     const int a_bytes = (conv_patch_bytes(KH, KW) + 1023) / 1024 * 1024;
     const int nc = (Cp + 63) / 64;            // 64-channel chunks

@@ -82,7 +82,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     constexpr int A_BYTES = GEMM_BM * 128;
     constexpr int B_BYTES = BN * 128;
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* smem = smem_align1024(smem_raw);
     uint8_t* sA = smem;
     uint8_t* sB = smem + STAGES * A_BYTES;
     uint64_t* bars = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
@@ -284,7 +284,7 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
                Epi ep, int Nw, int K, int Mtok, int kb_per_split, int* err) {
     using C = GemvCfg<NT, STAGES, INT8>;
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* smem = smem_align1024(smem_raw);
     uint8_t* sC = smem;                                   // converted bf16 ring (int8 only)
     uint8_t* sW = sC + C::C_STAGES * C::C_BYTES;
     uint8_t* sX = sW + STAGES * C::W_BYTES;
