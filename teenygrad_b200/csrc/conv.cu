@@ -118,9 +118,9 @@ __global__ void reorder_weights_kernel(const T* __restrict__ w, __nv_bfloat16* _
 // ---------------------------------------------------------- tcgen05 conv --
 // Persistent implicit GEMM for Y^T: output channels are the MMA's rows (A =
 // weights [64 couts][64 channels] of one tap and channel chunk), output
-// pixels its columns (B = a tile of 32 x 8 pixels).  A tcgen05.mma holds the
-// tensor pipe for about the same time whatever its N, so every instruction
-// carries N = 256 pixels; the M = 128 instruction also reads the 64 weight
+// pixels its columns (B = a tile of BH x 8 pixels, BH <= 32 chosen per shape
+// so row tiles are not padded, conv_bh).  One thread issues an MMA per ~75 ns
+// whatever its N, so every instruction carries up to N = 256 pixels; the M = 128 instruction also reads the 64 weight
 // rows that follow (next slice), which land in TMEM lanes 64-127 and are
 // never read.  Per tile and 64-channel chunk ONE TMA load brings the haloed
 // NHWC patch [32 + KH - 1 rows][8 + KW - 1 columns][64 channels] (128-B
@@ -132,20 +132,30 @@ __global__ void reorder_weights_kernel(const T* __restrict__ w, __nv_bfloat16* _
 // a ring.  TMEM holds two [128 x 256] f32 accumulators so the epilogue of one
 // tile overlaps the MMAs of the next.  Epilogue: warps 4, 5, 8, 9 (TMEM lanes
 // 0-63 = channels; 128 pixels each) apply bias -> BN -> activation and stage
-// [row][channel][column] (16-byte rows, conflict-free) for a TMA store to NCHW.
-constexpr int CONV_BH = 32, CONV_BW = 8, CONV_BN = 64;   // tile: 32 x 8 pixels x 64 output channels
-constexpr int CONV_NPIX = CONV_BH * CONV_BW;             // 256 = MMA N
-constexpr int CONV_WS = 4;                               // weight ring slices (streaming mode)
-constexpr int CONV_W_BYTES = CONV_BN * 128;              // [64 couts][64 channels] bf16
-constexpr int CONV_OUT_BYTES = CONV_NPIX * CONV_BN * 2;   // [32 rows][64 couts][8 columns] bf16
-constexpr int CONV_TMEM = 2 * CONV_NPIX;                  // two 256-column accumulators
-constexpr int CONV_THREADS = 320;                         // warps 0 TMA, 1-2 MMA, 4-5 + 8-9 epilogue
+// [row][channel][column] (16-byte rows, conflict-free) for a TMA store to NCHW
+// (OS = 1 or 2 staging buffers, whichever fits beside the patch ring).
+constexpr int CONV_BH_MAX = 32, CONV_BW = 8, CONV_BN = 64;   // tile: BH x 8 pixels x 64 output channels
+constexpr int CONV_WS = 4;                                   // weight ring slices (streaming mode)
+constexpr int CONV_W_BYTES = CONV_BN * 128;                  // [64 couts][64 channels] bf16
+constexpr int CONV_ACC_COLS = 256;                           // TMEM columns per accumulator (N <= 256)
+constexpr int CONV_TMEM = 2 * CONV_ACC_COLS;                 // two accumulators
+constexpr int CONV_THREADS = 320;                            // warps 0 TMA, 1-2 MMA, 4-5 + 8-9 epilogue
 
+// Tile height: the fewest row tiles of at most 32 rows, each of even height (the
+// MMA's N = 8 * BH must be a multiple of 16), e.g. 56 output rows -> 2 x 28.
+__host__ __device__ constexpr int conv_bh(int OH) {
+    const int t = (OH + CONV_BH_MAX - 1) / CONV_BH_MAX;
+    const int h = (OH + t - 1) / t;
+    return (h + 1) / 2 * 2;
+}
 __host__ __device__ constexpr int conv_pw(int KW) { return CONV_BW + KW - 1; }
-__host__ __device__ constexpr int conv_patch_bytes(int KH, int KW) { return (CONV_BH + KH - 1) * conv_pw(KW) * 128; }
-// wslots: weight slices held in shared memory (all of them when resident, else the ring)
-__host__ __device__ constexpr int conv_smem_bytes(int KH, int KW, int AS, int wslots) {
-    return AS * ((conv_patch_bytes(KH, KW) + 1023) / 1024 * 1024) + wslots * CONV_W_BYTES + 2 * CONV_OUT_BYTES + 1024 + 256;
+__host__ __device__ constexpr int conv_patch_bytes(int BH, int KH, int KW) { return (BH + KH - 1) * conv_pw(KW) * 128; }
+__host__ __device__ constexpr int conv_out_bytes(int BH) { return BH * CONV_BW * CONV_BN * 2; }   // [BH rows][64 couts][8 columns]
+// wslots: weight slices held in shared memory (all of them when resident, else the ring);
+// OS: output staging buffers (2 lets a tile's staging overlap the previous tile's store)
+__host__ __device__ constexpr int conv_smem_bytes(int BH, int KH, int KW, int AS, int wslots, int OS) {
+    return AS * ((conv_patch_bytes(BH, KH, KW) + 1023) / 1024 * 1024) + wslots * CONV_W_BYTES + OS * conv_out_bytes(BH) +
+           1024 + 256;
 }
 
 __device__ __forceinline__ void tma_store_4d_async(const CUtensorMap* m, uint32_t src, int c0, int c1, int c2, int c3) {
@@ -165,11 +175,13 @@ bool conv_tc_ok(const ConvShape& s, int stride, int KH, int KW);
 __global__ void __launch_bounds__(CONV_THREADS, 1)
 conv_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
                const __grid_constant__ CUtensorMap tmY, ConvEpi ep, int B, int OH, int OW, int Cout, int KH, int KW,
-               int Cp, int pad, int AS, int wres, int* err) {
+               int Cp, int pad, int AS, int wres, int BH, int OS, int* err) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_align1024(smem_raw);
     const int PW = conv_pw(KW);
-    const int a_bytes = (conv_patch_bytes(KH, KW) + 1023) / 1024 * 1024;
+    const int a_bytes = (conv_patch_bytes(BH, KH, KW) + 1023) / 1024 * 1024;
+    const int NPIX = BH * CONV_BW;            // MMA N
+    const int out_bytes = conv_out_bytes(BH);
     const int nc = (Cp + 63) / 64;            // 64-channel chunks
     const int taps = KH * KW;
     const int wslots = wres ? taps * nc : CONV_WS;
@@ -177,7 +189,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ 
     uint8_t* sW = sP + AS * a_bytes;                           // weight slices
     uint8_t* sO = sW + wslots * CONV_W_BYTES;                  // [2] output staging (also the
                                                                // rows past the last weight slice)
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sO + 2 * CONV_OUT_BYTES);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sO + OS * out_bytes);
     // p_full[4], p_empty[4], w_full[WS], w_empty[WS], acc_full[2], acc_empty[2]
     const uint32_t p_full0 = smem_u32(bars), p_empty0 = smem_u32(bars + 4);
     const uint32_t w_full0 = smem_u32(bars + 8), w_empty0 = smem_u32(bars + 8 + CONV_WS);
@@ -186,7 +198,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ 
 
     pdl_trigger();
     const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
-    const int tiles_w = (OW + CONV_BW - 1) / CONV_BW, tiles_h = (OH + CONV_BH - 1) / CONV_BH;
+    const int tiles_w = (OW + CONV_BW - 1) / CONV_BW, tiles_h = (OH + BH - 1) / BH;
     const int nN = (Cout + CONV_BN - 1) / CONV_BN;
     const int units = tiles_w * tiles_h * B * nN;
     auto tile_of = [&](int t, int& b, int& oh0, int& ow0, int& n0) {
@@ -194,7 +206,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ 
         int p = t / nN;
         ow0 = (p % tiles_w) * CONV_BW;
         p /= tiles_w;
-        oh0 = (p % tiles_h) * CONV_BH;
+        oh0 = (p % tiles_h) * BH;
         b = p / tiles_h;
     };
 
@@ -243,7 +255,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ 
                         ok = false;
                         break;
                     }
-                    mbar_expect_tx(p_full0 + 8 * sp, (uint32_t)conv_patch_bytes(KH, KW));
+                    mbar_expect_tx(p_full0 + 8 * sp, (uint32_t)conv_patch_bytes(BH, KH, KW));
                     tma_load_4d(smem_u32(sP + sp * a_bytes), &tmX, p_full0 + 8 * sp, c * 64, ow0 - pad, oh0 - pad, b);
                     pi++;
                     for (int tap = 0; !wres && tap < taps; tap++) {
@@ -271,7 +283,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ 
         // Warp 1 issues the CTA's even tiles (accumulator 0), warp 2 the odd ones
         // (accumulator 1): one thread issues an MMA per ~80 ns, two keep the pipe busier.
         if (lane == 0) {
-            constexpr uint32_t idesc = idesc_bf16_f32(128, CONV_NPIX, false, false);
+            const uint32_t idesc = idesc_bf16_f32(128, NPIX, false, false);
             // descriptors built once; an operand at byte offset o adds o >> 4 (start-address field)
             const uint64_t b_desc0 = sdesc_sw128(smem_u32(sP), 16, (uint32_t)PW * 128);
             const uint64_t a_desc0 = sdesc_sw128(smem_u32(sW), 16, 1024);
@@ -281,7 +293,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ 
                 const int ab = tl & 1;
                 if (tl >= 2 && !mbar_wait(acc_empty0 + 8 * ab, ((tl >> 1) - 1) & 1, err, DEV_ERR_TIMEOUT_MISC)) break;
                 tc_fence_after();
-                const uint32_t d_tmem = tmem + ab * CONV_NPIX;
+                const uint32_t d_tmem = tmem + ab * CONV_ACC_COLS;
                 for (int c = 0; ok && c < nc; c++) {
                     const int pi = tl * nc + c;          // patch sequence number (producer order)
                     const int sp = pi % AS;
@@ -340,37 +352,62 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ 
             }
             ok = mbar_wait(acc_full0 + 8 * ab, (tl >> 1) & 1, err, DEV_ERR_TIMEOUT_ACC) && ok;
             tc_fence_after();
-            // staging buffer ab was last read by the store issued two tiles ago
-            if (warp == 4 && lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+            // TMEM -> registers 32 pixels at a time, the next chunk's load in flight
+            // while the current one is processed; the accumulator is released as
+            // soon as its last chunk has been read
+            const int pbeg = half * 128;
+            const int pend = pbeg + 128 < NPIX ? pbeg + 128 : NPIX;
+            const uint32_t t_acc = tmem + ((uint32_t)(q * 32) << 16) + ab * CONV_ACC_COLS;
+            float v[32];
+            if (pbeg < pend) tmem_ld32(t_acc + pbeg, v);
+            // the staging buffer was last read by the store issued OS tiles ago
+            if (warp == 4 && lane == 0) {
+                if (OS == 2) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+                else asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+            }
             asm volatile("bar.sync 2, 128;" ::: "memory");
-            uint8_t* so = sO + ab * CONV_OUT_BYTES;
+            uint8_t* so = sO + (OS == 2 ? ab : 0) * out_bytes;
+            tmem_wait_ld32(v);
+            if (pbeg >= pend) {
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(acc_empty0 + 8 * ab);
+            }
 #pragma unroll 1
-            for (int p0 = half * 128; p0 < half * 128 + 128; p0 += 32) {
-                float v[32];
-                tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + ab * CONV_NPIX + p0, v);
-                tmem_wait_ld();
-                // v -> ((v + bias) * scale + shift) -> activation (as conv_epi)
+            for (int p0 = pbeg; p0 < pend; p0 += 32) {
+                float c[32];
+#pragma unroll
+                for (int j = 0; j < 32; j++) c[j] = v[j];
+                const bool more = p0 + 32 < pend;
+                if (more) {
+                    tmem_ld32(t_acc + p0 + 32, v);
+                } else {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(acc_empty0 + 8 * ab);
+                }
+                // c -> ((c + bias) * scale + shift) -> activation (as conv_epi)
 #pragma unroll
                 for (int j = 0; j < 32; j++) {
-                    float o = (v[j] + eb) * es + et;
+                    float o = (c[j] + eb) * es + et;
                     if (ep.act == TB_ACT_RELU) o = o > 0.f ? o : 0.f;
                     else if (ep.act == TB_ACT_SILU) o = o / (1.0f + expf(-o));
-                    v[j] = co < Cout ? o : 0.f;
+                    c[j] = co < Cout ? o : 0.f;
                 }
                 // pixels p0 .. p0 + 31 = rows p0 / 8 .. + 3, 8 columns each: [row][channel][column]
+                // (rows past BH, when NPIX is not a multiple of 32, are not staged)
 #pragma unroll
                 for (int r = 0; r < 4; r++) {
+                    if (p0 / 8 + r >= BH) break;
                     uint4 u;
-                    u.x = pack_bf16x2(v[8 * r + 0], v[8 * r + 1]);
-                    u.y = pack_bf16x2(v[8 * r + 2], v[8 * r + 3]);
-                    u.z = pack_bf16x2(v[8 * r + 4], v[8 * r + 5]);
-                    u.w = pack_bf16x2(v[8 * r + 6], v[8 * r + 7]);
+                    u.x = pack_bf16x2(c[8 * r + 0], c[8 * r + 1]);
+                    u.y = pack_bf16x2(c[8 * r + 2], c[8 * r + 3]);
+                    u.z = pack_bf16x2(c[8 * r + 4], c[8 * r + 5]);
+                    u.w = pack_bf16x2(c[8 * r + 6], c[8 * r + 7]);
                     *reinterpret_cast<uint4*>(so + ((p0 / 8 + r) * CONV_BN + col) * 16) = u;
                 }
+                if (more) tmem_wait_ld32(v);
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(acc_empty0 + 8 * ab);
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             asm volatile("bar.sync 2, 128;" ::: "memory");
             if (warp == 4 && lane == 0 && ok) tma_store_4d_async(&tmY, smem_u32(so), ow0, n0, oh0, b);
@@ -494,8 +531,9 @@ static size_t conv_ws_bytes(const ConvShape& s) {
 }
 
 bool conv_tc_ok(const ConvShape& s, int stride, int KH, int KW) {
-    // two patch stages + the weight ring + output staging within 227 KB of shared memory
-    return stride == 1 && s.OW % 8 == 0 && KH <= 7 && KW <= 9 && conv_smem_bytes(KH, KW, 2, CONV_WS) <= 227 * 1024;
+    // two patch stages + the weight ring + one output staging buffer within 227 KB of shared memory
+    return stride == 1 && s.OW % 8 == 0 && KH <= 7 && KW <= 9 &&
+           conv_smem_bytes(conv_bh(s.OH), KH, KW, 2, CONV_WS, 1) <= 227 * 1024;
 }
 
 static bool conv_shape(int B, int C, int Co, int H, int W, int KH, int KW, int stride, int pad, ConvShape* s) {
@@ -558,11 +596,12 @@ int tb_conv2d_fwd(tb_ctx* ctx, int dtype, const void* x, const void* w, const fl
                     (const __nv_bfloat16*)w, wr, Cout, Cin, KH, KW, s.Cp);
         if (rc) return rc;
     }
+    const int BH = conv_bh(s.OH);
     CUtensorMap mx, mw, my;
     {
         uint64_t dims[4] = {(uint64_t)s.Cp, (uint64_t)W, (uint64_t)H, (uint64_t)B};
         uint64_t strides[3] = {(uint64_t)s.Cp * 2, (uint64_t)W * s.Cp * 2, (uint64_t)H * W * s.Cp * 2};
-        uint32_t box[4] = {64, (uint32_t)conv_pw(KW), (uint32_t)(CONV_BH + KH - 1), 1};
+        uint32_t box[4] = {64, (uint32_t)conv_pw(KW), (uint32_t)(BH + KH - 1), 1};
         cuuint32_t es[4] = {1, 1, 1, 1};
         int rc = make_tmap_strided(ctx, &mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, xn, dims, strides, box, es,
                                    CU_TENSOR_MAP_SWIZZLE_128B);
@@ -573,26 +612,31 @@ int tb_conv2d_fwd(tb_ctx* ctx, int dtype, const void* x, const void* w, const fl
         // NCHW output viewed as (w, channel, h, image): the staged tile is [h][channel][w]
         uint64_t ydims[4] = {(uint64_t)s.OW, (uint64_t)Cout, (uint64_t)s.OH, (uint64_t)B};
         uint64_t ystr[3] = {(uint64_t)s.OH * s.OW * 2, (uint64_t)s.OW * 2, (uint64_t)Cout * s.OH * s.OW * 2};
-        uint32_t ybox[4] = {CONV_BW, CONV_BN, CONV_BH, 1};
+        uint32_t ybox[4] = {CONV_BW, CONV_BN, (uint32_t)BH, 1};
         rc = make_tmap(ctx, &my, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, y, ydims, ystr, ybox, CU_TENSOR_MAP_SWIZZLE_NONE);
         if (rc) return rc;
     }
     // Resident weights (all taps x chunks of one 64-channel output block) when
-    // they fit beside two patch stages; otherwise a 4-slice weight ring.
+    // they fit beside two patch stages; otherwise a 4-slice weight ring.  Then
+    // two output staging buffers (a tile's staging overlaps the previous
+    // tile's store) with the deepest patch ring that fits beside them.
     constexpr int kSmemMax = 227 * 1024;
     const int nN = (Cout + CONV_BN - 1) / CONV_BN;
     const int wall = KH * KW * ((s.Cp + 63) / 64);
-    const int wres = conv_smem_bytes(KH, KW, 2, wall) <= kSmemMax && nN <= ctx->num_sms ? 1 : 0;
+    const int wres = conv_smem_bytes(BH, KH, KW, 2, wall, 1) <= kSmemMax && nN <= ctx->num_sms ? 1 : 0;
     const int wslots = wres ? wall : CONV_WS;
-    const int AS = conv_smem_bytes(KH, KW, 3, wslots) <= kSmemMax ? 3 : 2;
-    const int smem = conv_smem_bytes(KH, KW, AS, wslots);
+    int AS = 2, OS = 1;
+    if (conv_smem_bytes(BH, KH, KW, 3, wslots, 2) <= kSmemMax) AS = 3, OS = 2;
+    else if (conv_smem_bytes(BH, KH, KW, 2, wslots, 2) <= kSmemMax) AS = 2, OS = 2;
+    else if (conv_smem_bytes(BH, KH, KW, 3, wslots, 1) <= kSmemMax) AS = 3, OS = 1;
+    const int smem = conv_smem_bytes(BH, KH, KW, AS, wslots, OS);
     TB_CUDA_TRY(ctx, cudaFuncSetAttribute(conv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    const int64_t units = (int64_t)((s.OW + CONV_BW - 1) / CONV_BW) * ((s.OH + CONV_BH - 1) / CONV_BH) * B * nN;
+    const int64_t units = (int64_t)((s.OW + CONV_BW - 1) / CONV_BW) * ((s.OH + BH - 1) / BH) * B * nN;
     // resident weights: a grid that is a multiple of nN keeps each CTA on one output block
     int grid = wres ? (ctx->num_sms / nN) * nN : ctx->num_sms;
     if (units < grid) grid = (int)units;
     return launch(ctx, "conv_tc", conv_tc_kernel, dim3(grid), dim3(CONV_THREADS), smem, mx, mw, my, ep, B, s.OH, s.OW, Cout,
-                  KH, KW, s.Cp, pad, AS, wres, ctx->d_err);
+                  KH, KW, s.Cp, pad, AS, wres, BH, OS, ctx->d_err);
 }
 
 int tb_bn_fold(tb_ctx* ctx, const float* gamma, const float* beta, const float* mean, const float* var,
