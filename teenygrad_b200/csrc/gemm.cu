@@ -259,42 +259,56 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 // partials of row pairs [r*128/CS, (r+1)*128/CS) from its peers by DSMEM bulk
 // copies, sums them in rank order (deterministic) and runs the epilogue.
 //
-// Fused RMSNorm (Epi::norm_w set): warps 2..7 build each activation tile from
-// the raw rows, bf16(x * w), and accumulate each token's sum of squares over
-// the CTA's K range.  1/rms is a per-token factor of every output, so it is
-// applied in the epilogue once the cluster's partial sums are added.
+// Fused RMSNorm (Epi::norm_w set): the converter warps build each activation
+// tile from the raw rows, bf16(x * w), and accumulate each token's sum of
+// squares over the CTA's K range.  1/rms is a per-token factor of every
+// output, so it is applied in the epilogue once the cluster's partial sums
+// are added.
+//
+// bf16 weights: 288 threads; warp 0 TMA, warps 1 and 8 issue the MMAs of one
+// 128-row half each (A and B from shared memory), warps 2-7 build normalised
+// activation tiles.  int8 weights: 384 threads; warps 1 and 2 issue, and
+// warps 4-11 convert: thread <-> weight row (TMEM lane quarter = warp % 4,
+// half = (warp - 4) / 4) reads its 64 int8 of the K block from the 64-B
+// swizzled ring (conflict-free), converts them exactly (i8x4_to_bf16x4) and
+// stores the 32 bf16 pairs into a TMEM A tile with one tcgen05.st; the MMA
+// takes A from TMEM.  Shared-memory traffic per K block is then the TMA
+// writes, one read of the int8 tile and the MMAs' reads of the activations
+// (no bf16 weight tile written and read back through shared memory).
 template <int NT, int STAGES, bool INT8>
 struct GemvCfg {
-    static constexpr int W_BYTES = INT8 ? 256 * 64 : 256 * 128;  // int8: 64 K per row, no swizzle
+    static constexpr int W_BYTES = INT8 ? 256 * 64 : 256 * 128;  // int8: 64 K per row, 64-B swizzle
     static constexpr int X_BYTES = NT * 128;
-    static constexpr int C_STAGES = INT8 ? 2 : 0;                 // converted bf16 ring
-    static constexpr int C_BYTES = 256 * 128;
     // received partials (reuse the rings): CS slots of NT * 256 / CS values + NT sums of squares
     static constexpr int RED_BYTES = (NT * 256 + 16 * NT) * 4;
-    static constexpr int RING = STAGES * (W_BYTES + X_BYTES) + C_STAGES * C_BYTES;
+    static constexpr int RING = STAGES * (W_BYTES + X_BYTES);
     static constexpr int SMEM = (RING > RED_BYTES ? RING : RED_BYTES) + 1024 + 512;
-    static constexpr int TMEM_COLS = (2 * NT) < 32 ? 32 : (2 * NT);
+    // TMEM: accumulators [half][NT] from column 0; int8: converted A tiles
+    // [2 buffers][2 halves][32 columns] from column A_COL
+    static constexpr int A_COL = 128;
+    static constexpr int TMEM_COLS = INT8 ? 256 : ((2 * NT) < 32 ? 32 : (2 * NT));
+    static constexpr int THREADS = INT8 ? 384 : 288;
+    static constexpr int MMA_W1 = INT8 ? 2 : 8;     // second MMA-issuing warp (the first is warp 1)
+    static constexpr int CONV_W0 = INT8 ? 4 : 2;    // first converter warp
+    static constexpr int N_CONV = INT8 ? 8 : 6;     // converter warps
 };
 
-constexpr int GEMV_THREADS = 288;   // warp 0 TMA, warps 1 and 8 MMA (one 128-row half each), 2-7 converters
-
 template <int NT, int STAGES, bool INT8>
-__global__ void __launch_bounds__(GEMV_THREADS, 1)
+__global__ void __launch_bounds__(GemvCfg<NT, STAGES, INT8>::THREADS, 1)
 gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                Epi ep, int Nw, int K, int Mtok, int kb_per_split, int* err) {
     using C = GemvCfg<NT, STAGES, INT8>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_align1024(smem_raw);
-    uint8_t* sC = smem;                                   // converted bf16 ring (int8 only)
-    uint8_t* sW = sC + C::C_STAGES * C::C_BYTES;
+    uint8_t* sW = smem;
     uint8_t* sX = sW + STAGES * C::W_BYTES;
     float* red = reinterpret_cast<float*>(smem);          // [NT][256] partials, after the MMAs
     constexpr int BAR_OFF = (C::RING > C::RED_BYTES ? C::RING : C::RED_BYTES);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + BAR_OFF);
     const uint32_t full0 = smem_u32(bars);
     const uint32_t empty0 = smem_u32(bars + STAGES);
-    const uint32_t cfull0 = smem_u32(bars + 2 * STAGES);
-    const uint32_t cempty0 = smem_u32(bars + 2 * STAGES + 2);
+    const uint32_t cfull0 = smem_u32(bars + 2 * STAGES);       // int8: TMEM A tile [2] converted
+    const uint32_t cempty0 = smem_u32(bars + 2 * STAGES + 2);  // int8: TMEM A tile [2] consumed
     const uint32_t accb = smem_u32(bars + 2 * STAGES + 4);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
     const uint32_t recvb = smem_u32(bars + 2 * STAGES + 6);   // partials from the peers have landed
@@ -309,7 +323,7 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
     const int kb0 = split * kb_per_split;
     const int kb1 = min(nk_total, kb0 + kb_per_split);
     const int nk = kb1 - kb0;
-    constexpr int N_CONV_WARPS = 6;   // warps 2..7
+    constexpr int N_CONV_WARPS = C::N_CONV;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
@@ -359,19 +373,18 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
         }
         for (int i = (issued > STAGES ? issued - STAGES : 0); i < issued; i++)
             mbar_wait(full0 + 8 * (i % STAGES), (i / STAGES) & 1, err, DEV_ERR_TIMEOUT_FULL);
-    } else if ((warp == 1 || warp == 8) && lane == 0) {
+    } else if ((warp == 1 || warp == C::MMA_W1) && lane == 0) {
         // two issuing threads (one MMA per ~80 ns each): warp 1 the weight rows
-        // [0, 128) of the tile, warp 8 the rows [128, 256), into separate accumulators
+        // [0, 128) of the tile, the other the rows [128, 256), into separate accumulators
         constexpr uint32_t idesc = idesc_bf16_f32(128, NT, false, false);
         const int h = warp == 1 ? 0 : 1;
         for (int i = 0; i < nk; i++) {
             int s = i % STAGES;
-            uint32_t w_base;
+            uint32_t w_base = 0;
             if (INT8) {
                 int c = i & 1;
                 if (!mbar_wait(cfull0 + 8 * c, (i >> 1) & 1, err, DEV_ERR_TIMEOUT_MISC)) break;
                 if (!mbar_wait(full0 + 8 * s, (i / STAGES) & 1, err, DEV_ERR_TIMEOUT_FULL)) break;
-                w_base = smem_u32(sC + c * C::C_BYTES);
             } else {
                 if (!mbar_wait(full0 + 8 * s, (i / STAGES) & 1, err, DEV_ERR_TIMEOUT_FULL)) break;
                 if (NORM && !mbar_wait(xrdy0 + 8 * s, (i / STAGES) & 1, err, DEV_ERR_TIMEOUT_MISC)) break;
@@ -382,18 +395,25 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
 #pragma unroll
             for (int kk = 0; kk < 4; kk++) {
                 const uint64_t bd = sdesc_sw128(x_base + kk * 32, 16, 1024);
-                const uint64_t ad = sdesc_sw128(w_base + h * 128 * 128 + kk * 32, 16, 1024);
-                umma_f16_ss(tmem + h * NT, ad, bd, idesc, (i | kk) != 0);
+                if (INT8) {
+                    // A: this half's converted tile, K slice kk = 8 TMEM columns
+                    const uint32_t a_tmem = tmem + C::A_COL + (i & 1) * 64 + h * 32 + kk * 8;
+                    umma_f16_ts(tmem + h * NT, a_tmem, bd, idesc, (i | kk) != 0);
+                } else {
+                    const uint64_t ad = sdesc_sw128(w_base + h * 128 * 128 + kk * 32, 16, 1024);
+                    umma_f16_ss(tmem + h * NT, ad, bd, idesc, (i | kk) != 0);
+                }
             }
             if (INT8) umma_commit(cempty0 + 8 * (i & 1));
             umma_commit(empty0 + 8 * s);
         }
         umma_commit(accb);
-    } else if ((INT8 || NORM) && warp >= 2 && warp < 8) {
-        // ---------------- converter warps 2..7: the normalised activation tile
-        // (when the RMSNorm is fused) and int8 -> bf16 weights (int8 path)
-        const int ct = threadIdx.x - 64;   // 0..191
-        constexpr int XI = (NT * 8 + 191) / 192;   // 16-B activation chunks per thread per stage
+    } else if ((INT8 || NORM) && warp >= C::CONV_W0 && warp < C::CONV_W0 + C::N_CONV) {
+        // ---------------- converter warps: the normalised activation tile (when
+        // the RMSNorm is fused) and int8 -> bf16 weights into TMEM (int8 path)
+        constexpr int CT = 32 * C::N_CONV;                  // converter threads
+        const int ct = threadIdx.x - 32 * C::CONV_W0;       // 0 .. CT - 1
+        constexpr int XI = (NT * 8 + CT - 1) / CT;          // 16-B activation chunks per thread per stage
         uint4 xv[XI], gv[XI];
         const __nv_bfloat16* xg = reinterpret_cast<const __nv_bfloat16*>(ep.norm_x);
         const __nv_bfloat16* gg = reinterpret_cast<const __nv_bfloat16*>(ep.norm_w);
@@ -402,7 +422,7 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
             const int kbase = (kb0 + i) * 64;
 #pragma unroll
             for (int u = 0; u < XI; u++) {
-                const int it = ct + u * 192;
+                const int it = ct + u * CT;
                 const int m = it >> 3, k0 = kbase + 8 * ((it & 7) ^ (m & 7));
                 const bool kin = it < NT * 8 && k0 < K;
                 xv[u] = (kin && m < Mtok) ? *reinterpret_cast<const uint4*>(xg + (int64_t)m * ep.x_ld + k0)
@@ -432,7 +452,7 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
                 uint8_t* xt = sX + s * C::X_BYTES;
 #pragma unroll
                 for (int u = 0; u < XI; u++) {
-                    const int it = ct + u * 192;
+                    const int it = ct + u * CT;
                     if (it < NT * 8) {
                         const uint32_t xa[4] = {xv[u].x, xv[u].y, xv[u].z, xv[u].w};
                         const uint32_t ga[4] = {gv[u].x, gv[u].y, gv[u].z, gv[u].w};
@@ -454,22 +474,29 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
                 if (i + 1 < nk) load_x(i + 1);
             }
             if (INT8) {
-                // the converted ring slot is free once the MMAs of stage i - 2 are done
+                // TMEM A buffer c is free once the MMAs of stage i - 2 are done
                 if (i >= 2 && !mbar_wait(cempty0 + 8 * c, ((i >> 1) - 1) & 1, err, DEV_ERR_TIMEOUT_MISC)) break;
-                const uint8_t* src = sW + s * C::W_BYTES;   // [256 rows][64 B], unswizzled
-                uint8_t* dst = sC + c * C::C_BYTES;          // [256 rows][128 B], 128-B swizzle
-                for (int it = ct; it < 256 * 4; it += 192) {
-                    int r = it >> 2, ch = it & 3;
-                    uint4 raw = *reinterpret_cast<const uint4*>(src + r * 64 + ch * 16);
-                    uint32_t w4[4] = {raw.x, raw.y, raw.z, raw.w};
-                    uint32_t o[8];
+                tc_fence_after();
+                // thread <-> weight row r; the ring holds [256 rows][64 B] with the
+                // 64-B swizzle (16-B chunk index ^= (row / 2) % 4)
+                const int q = warp & 3, hc = (warp - C::CONV_W0) >> 2;
+                const int r = hc * 128 + q * 32 + lane;
+                const uint8_t* src = sW + s * C::W_BYTES + r * 64;
+                uint4 raw[4];
 #pragma unroll
-                    for (int j = 0; j < 4; j++) i8x4_to_bf16x4(w4[j], o[2 * j], o[2 * j + 1]);
-                    int p0 = ((2 * ch) ^ (r & 7)) * 16, p1 = ((2 * ch + 1) ^ (r & 7)) * 16;
-                    *reinterpret_cast<uint4*>(dst + r * 128 + p0) = make_uint4(o[0], o[1], o[2], o[3]);
-                    *reinterpret_cast<uint4*>(dst + r * 128 + p1) = make_uint4(o[4], o[5], o[6], o[7]);
+                for (int ch = 0; ch < 4; ch++) raw[ch] = *reinterpret_cast<const uint4*>(src + ((ch ^ ((r >> 1) & 3)) << 4));
+                uint32_t o[32];   // column ch * 8 + 2j (+1): K = ch * 16 + 4j .. + 3
+#pragma unroll
+                for (int ch = 0; ch < 4; ch++) {
+                    i8x4_to_bf16x4(raw[ch].x, o[ch * 8 + 0], o[ch * 8 + 1]);
+                    i8x4_to_bf16x4(raw[ch].y, o[ch * 8 + 2], o[ch * 8 + 3]);
+                    i8x4_to_bf16x4(raw[ch].z, o[ch * 8 + 4], o[ch * 8 + 5]);
+                    i8x4_to_bf16x4(raw[ch].w, o[ch * 8 + 6], o[ch * 8 + 7]);
                 }
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                tmem_st32u(tmem + ((uint32_t)(q * 32) << 16) + C::A_COL + c * 64 + hc * 32, o);
+                tmem_wait_st();
+                tc_fence_before();
+                if (NORM) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // the activation tile
                 __syncwarp();
                 if (lane == 0) {
                     mbar_arrive(cfull0 + 8 * c);
@@ -486,7 +513,7 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
                 v += __shfl_xor_sync(0xffffffffu, v, 1);
                 v += __shfl_xor_sync(0xffffffffu, v, 2);
                 v += __shfl_xor_sync(0xffffffffu, v, 4);
-                const int it = ct + u * 192;
+                const int it = ct + u * CT;
                 if ((lane & 7) == 0 && it < NT * 8) s_ss[it >> 3] = v;
             }
         }
@@ -507,7 +534,7 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
     const int l = q * 32 + lane;
     const uint32_t t_row = tmem + ((uint32_t)(q * 32) << 16);
     float acc[2][TP];
-    const bool ewarp = warp < 8;   // warps 0-7 hold the accumulator; warp 8 only joins the barriers
+    const bool ewarp = warp < 8;   // warps 0-7 hold the accumulator; warps 8+ only join the barriers
     if (ewarp) {
 #pragma unroll
         for (int h = 0; h < 2; h++) {
@@ -916,7 +943,7 @@ static int launch_gemv_tc(tb_ctx* ctx, const void* x, const void* w, const Epi& 
         uint64_t dims[2] = {(uint64_t)K, (uint64_t)Nw};
         uint64_t strides[1] = {(uint64_t)K};
         uint32_t box[2] = {64, 256};
-        rc = make_tmap(ctx, &tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+        rc = make_tmap(ctx, &tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B);
     } else {
         rc = make_tmap_2d(ctx, &tw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w, Nw, K, K, 64, 256);
     }
@@ -935,7 +962,7 @@ static int launch_gemv_tc(tb_ctx* ctx, const void* x, const void* w, const Epi& 
         int n = 0;
         cudaLaunchConfig_t q = {};
         q.gridDim = dim3(1, 16, 1);
-        q.blockDim = dim3(GEMV_THREADS, 1, 1);
+        q.blockDim = dim3(C::THREADS, 1, 1);
         q.dynamicSmemBytes = C::SMEM;
         cudaLaunchAttribute qa[1];
         qa[0].id = cudaLaunchAttributeClusterDimension;
@@ -950,15 +977,15 @@ static int launch_gemv_tc(tb_ctx* ctx, const void* x, const void* w, const Epi& 
         max_cs.store(ok16 ? 16 : 8);
     }
     int cs, kb_per;
-    // resident CTA slots: two per SM when two rings fit in shared memory (the
-    // int8 and 64-token configurations hold one)
-    constexpr int per_sm = 2 * (C::SMEM + 1024) <= 228 * 1024 ? 2 : 1;
+    // resident CTA slots: two per SM when two rings fit in shared memory (bf16,
+    // 16 or 32 tokens); int8 CTAs (384 threads) and 64-token rings hold one
+    constexpr int per_sm = !INT8 && 2 * (C::SMEM + 1024) <= 228 * 1024 ? 2 : 1;
     gemv_split(per_sm * ctx->num_sms, max_cs.load(), Nw, K, &cs, &kb_per);
     const int tiles = (Nw + 255) / 256;
     TB_CUDA_TRY(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     cudaLaunchConfig_t lc = {};
     lc.gridDim = dim3(tiles, cs, 1);
-    lc.blockDim = dim3(GEMV_THREADS, 1, 1);
+    lc.blockDim = dim3(C::THREADS, 1, 1);
     lc.dynamicSmemBytes = C::SMEM;
     lc.stream = ctx->stream;
     cudaLaunchAttribute attr[2];
@@ -981,9 +1008,9 @@ template <bool INT8>
 static int dispatch_gemv(tb_ctx* ctx, const void* x, const void* w, const Epi& ep, int M, int N, int K) {
     // <= 32 tokens: 3-stage rings (~105 KB) let two CTAs share an SM, so the
     // next layer's GEMV can start streaming weights (PDL) beside this one.
-    if (M <= 16) return launch_gemv_tc<16, INT8 ? 6 : 3, INT8>(ctx, x, w, ep, M, N, K);
-    if (M <= 32) return launch_gemv_tc<32, INT8 ? 6 : 3, INT8>(ctx, x, w, ep, M, N, K);
-    return launch_gemv_tc<64, INT8 ? 6 : 5, INT8>(ctx, x, w, ep, M, N, K);
+    if (M <= 16) return launch_gemv_tc<16, INT8 ? 8 : 3, INT8>(ctx, x, w, ep, M, N, K);
+    if (M <= 32) return launch_gemv_tc<32, INT8 ? 8 : 3, INT8>(ctx, x, w, ep, M, N, K);
+    return launch_gemv_tc<64, INT8 ? 8 : 5, INT8>(ctx, x, w, ep, M, N, K);
 }
 
 int linear_launch(tb_ctx* ctx, int int8, const void* x, const void* w, const Epi& ep, int M, int N, int K) {
