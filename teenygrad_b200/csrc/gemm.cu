@@ -269,24 +269,28 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 // 128-row half each (A and B from shared memory), warps 2-7 build normalised
 // activation tiles.  int8 weights: 384 threads; warps 1 and 2 issue, and
 // warps 4-11 convert: thread <-> weight row (TMEM lane quarter = warp % 4,
-// half = (warp - 4) / 4) reads its 64 int8 of the K block from the 64-B
+// half = (warp - 4) / 4) reads its 128 int8 of the K block from the 128-B
 // swizzled ring (conflict-free), converts them exactly (i8x4_to_bf16x4) and
-// stores the 32 bf16 pairs into a TMEM A tile with one tcgen05.st; the MMA
-// takes A from TMEM.  Shared-memory traffic per K block is then the TMA
+// stores the 64 bf16 pairs into a TMEM A tile with two tcgen05.st; the MMA
+// takes A from TMEM.  int8 K blocks are 128 wide (32 KB of weights) so the
+// per-block synchronisation is spread over twice the bytes of a 64-wide one.  Shared-memory traffic per K block is then the TMA
 // writes, one read of the int8 tile and the MMAs' reads of the activations
 // (no bf16 weight tile written and read back through shared memory).
 template <int NT, int STAGES, bool INT8>
 struct GemvCfg {
-    static constexpr int W_BYTES = INT8 ? 256 * 64 : 256 * 128;  // int8: 64 K per row, 64-B swizzle
-    static constexpr int X_BYTES = NT * 128;
+    static constexpr int KB = INT8 ? 128 : 64;      // K per block
+    static constexpr int RC = KB / 8;               // 16-B activation chunks per token row per block
+    static constexpr int W_BYTES = 256 * 128;       // [256 rows][128 B], 128-B swizzle (bf16 64 K, int8 128 K)
+    static constexpr int X_ATOM = NT * 128;         // [NT][64] bf16, one 128-B swizzle atom wide
+    static constexpr int X_BYTES = (KB / 64) * X_ATOM;
     // received partials (reuse the rings): CS slots of NT * 256 / CS values + NT sums of squares
     static constexpr int RED_BYTES = (NT * 256 + 16 * NT) * 4;
     static constexpr int RING = STAGES * (W_BYTES + X_BYTES);
     static constexpr int SMEM = (RING > RED_BYTES ? RING : RED_BYTES) + 1024 + 512;
     // TMEM: accumulators [half][NT] from column 0; int8: converted A tiles
-    // [2 buffers][2 halves][32 columns] from column A_COL
-    static constexpr int A_COL = 128;
-    static constexpr int TMEM_COLS = INT8 ? 256 : ((2 * NT) < 32 ? 32 : (2 * NT));
+    // [2 buffers][2 halves][64 columns] from column A_COL
+    static constexpr int A_COL = 128;               // int8: [2 buffers][2 halves][KB / 2 columns]
+    static constexpr int TMEM_COLS = INT8 ? 512 : ((2 * NT) < 32 ? 32 : (2 * NT));
     static constexpr int THREADS = INT8 ? 384 : 288;
     static constexpr int MMA_W1 = INT8 ? 2 : 8;     // second MMA-issuing warp (the first is warp 1)
     static constexpr int CONV_W0 = INT8 ? 4 : 2;    // first converter warp
@@ -319,7 +323,8 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
     pdl_trigger();
     const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
     const int tile = blockIdx.x, split = blockIdx.y, CS = gridDim.y;
-    const int nk_total = (K + 63) / 64;
+    constexpr int KB = C::KB;
+    const int nk_total = (K + KB - 1) / KB;
     const int kb0 = split * kb_per_split;
     const int kb1 = min(nk_total, kb0 + kb_per_split);
     const int nk = kb1 - kb0;
@@ -355,20 +360,23 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
         const int pre = nk < STAGES ? nk : STAGES;
         for (int i = 0; i < pre; i++) {
             mbar_expect_tx(full0 + 8 * i, tx_bytes);
-            tma_load_2d(smem_u32(sW + i * C::W_BYTES), &tmW, full0 + 8 * i, (kb0 + i) * 64, tile * 256);
+            tma_load_2d(smem_u32(sW + i * C::W_BYTES), &tmW, full0 + 8 * i, (kb0 + i) * KB, tile * 256);
         }
         pdl_wait();
         if (!NORM)
             for (int i = 0; i < pre; i++)
-                tma_load_2d(smem_u32(sX + i * C::X_BYTES), &tmX, full0 + 8 * i, (kb0 + i) * 64, 0);
+                for (int a = 0; a < KB / 64; a++)
+                    tma_load_2d(smem_u32(sX + i * C::X_BYTES + a * C::X_ATOM), &tmX, full0 + 8 * i, (kb0 + i) * KB + 64 * a, 0);
         int issued = pre;
         for (int i = pre; i < nk; i++) {
             int s = i % STAGES;
             if (!mbar_wait(empty0 + 8 * s, ((i / STAGES) - 1) & 1, err, DEV_ERR_TIMEOUT_EMPTY)) break;
             mbar_expect_tx(full0 + 8 * s, tx_bytes);
-            int kcoord = (kb0 + i) * 64;
+            int kcoord = (kb0 + i) * KB;
             tma_load_2d(smem_u32(sW + s * C::W_BYTES), &tmW, full0 + 8 * s, kcoord, tile * 256);
-            if (!NORM) tma_load_2d(smem_u32(sX + s * C::X_BYTES), &tmX, full0 + 8 * s, kcoord, 0);
+            if (!NORM)
+                for (int a = 0; a < KB / 64; a++)
+                    tma_load_2d(smem_u32(sX + s * C::X_BYTES + a * C::X_ATOM), &tmX, full0 + 8 * s, kcoord + 64 * a, 0);
             issued = i + 1;
         }
         for (int i = (issued > STAGES ? issued - STAGES : 0); i < issued; i++)
@@ -393,11 +401,11 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
             tc_fence_after();
             uint32_t x_base = smem_u32(sX + s * C::X_BYTES);
 #pragma unroll
-            for (int kk = 0; kk < 4; kk++) {
-                const uint64_t bd = sdesc_sw128(x_base + kk * 32, 16, 1024);
+            for (int kk = 0; kk < KB / 16; kk++) {
+                const uint64_t bd = sdesc_sw128(x_base + (kk >> 2) * C::X_ATOM + (kk & 3) * 32, 16, 1024);
                 if (INT8) {
                     // A: this half's converted tile, K slice kk = 8 TMEM columns
-                    const uint32_t a_tmem = tmem + C::A_COL + (i & 1) * 64 + h * 32 + kk * 8;
+                    const uint32_t a_tmem = tmem + C::A_COL + (i & 1) * KB + h * (KB / 2) + kk * 8;
                     umma_f16_ts(tmem + h * NT, a_tmem, bd, idesc, (i | kk) != 0);
                 } else {
                     const uint64_t ad = sdesc_sw128(w_base + h * 128 * 128 + kk * 32, 16, 1024);
@@ -413,18 +421,21 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
         // the RMSNorm is fused) and int8 -> bf16 weights into TMEM (int8 path)
         constexpr int CT = 32 * C::N_CONV;                  // converter threads
         const int ct = threadIdx.x - 32 * C::CONV_W0;       // 0 .. CT - 1
-        constexpr int XI = (NT * 8 + CT - 1) / CT;          // 16-B activation chunks per thread per stage
+        constexpr int RC = C::RC;
+        constexpr int XI = (NT * RC + CT - 1) / CT;         // 16-B activation chunks per thread per stage
         uint4 xv[XI], gv[XI];
         const __nv_bfloat16* xg = reinterpret_cast<const __nv_bfloat16*>(ep.norm_x);
         const __nv_bfloat16* gg = reinterpret_cast<const __nv_bfloat16*>(ep.norm_w);
         // stage i's raw activation chunks and norm gains -> registers (one stage ahead)
         auto load_x = [&](int i) {
-            const int kbase = (kb0 + i) * 64;
+            const int kbase = (kb0 + i) * KB;
 #pragma unroll
             for (int u = 0; u < XI; u++) {
                 const int it = ct + u * CT;
-                const int m = it >> 3, k0 = kbase + 8 * ((it & 7) ^ (m & 7));
-                const bool kin = it < NT * 8 && k0 < K;
+                // token m, physical chunk cc of its row (atom cc / 8, swizzled chunk cc % 8)
+                const int m = it / RC, cc = it % RC;
+                const int k0 = kbase + 64 * (cc >> 3) + 8 * ((cc & 7) ^ (m & 7));
+                const bool kin = it < NT * RC && k0 < K;
                 xv[u] = (kin && m < Mtok) ? *reinterpret_cast<const uint4*>(xg + (int64_t)m * ep.x_ld + k0)
                                           : make_uint4(0, 0, 0, 0);
                 gv[u] = kin ? *reinterpret_cast<const uint4*>(gg + k0) : make_uint4(0, 0, 0, 0);
@@ -447,13 +458,13 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
                 if (!mbar_wait(empty0 + 8 * s, ((i / STAGES) - 1) & 1, err, DEV_ERR_TIMEOUT_EMPTY)) break;
             }
             if (NORM) {
-                // x tile [NT rows][64 k] bf16, 128-B swizzle: bf16(x[m,k] * w[k]); the
-                // per-token 1/rms is a common factor of each output and is applied in the epilogue
+                // x tile [KB / 64 atoms][NT rows][64 k] bf16, 128-B swizzle: bf16(x[m,k] * w[k]);
+                // the per-token 1/rms is a common factor of each output and is applied in the epilogue
                 uint8_t* xt = sX + s * C::X_BYTES;
 #pragma unroll
                 for (int u = 0; u < XI; u++) {
                     const int it = ct + u * CT;
-                    if (it < NT * 8) {
+                    if (it < NT * RC) {
                         const uint32_t xa[4] = {xv[u].x, xv[u].y, xv[u].z, xv[u].w};
                         const uint32_t ga[4] = {gv[u].x, gv[u].y, gv[u].z, gv[u].w};
                         uint32_t o[4];
@@ -463,7 +474,9 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
                             ssv[u] += a0 * a0 + a1 * a1;
                             o[j] = pack_bf16x2(a0 * bf16_lo(ga[j]), a1 * bf16_hi(ga[j]));
                         }
-                        *reinterpret_cast<uint4*>(xt + (it >> 3) * 128 + (it & 7) * 16) = make_uint4(o[0], o[1], o[2], o[3]);
+                        const int m = it / RC, cc = it % RC;
+                        *reinterpret_cast<uint4*>(xt + (cc >> 3) * C::X_ATOM + m * 128 + (cc & 7) * 16) =
+                            make_uint4(o[0], o[1], o[2], o[3]);
                     }
                 }
                 if (!INT8) {
@@ -477,23 +490,28 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
                 // TMEM A buffer c is free once the MMAs of stage i - 2 are done
                 if (i >= 2 && !mbar_wait(cempty0 + 8 * c, ((i >> 1) - 1) & 1, err, DEV_ERR_TIMEOUT_MISC)) break;
                 tc_fence_after();
-                // thread <-> weight row r; the ring holds [256 rows][64 B] with the
-                // 64-B swizzle (16-B chunk index ^= (row / 2) % 4)
+                // thread <-> weight row r; the ring holds [256 rows][128 B] with the
+                // 128-B swizzle (16-B chunk index ^= row % 8); two halves of 64 K
                 const int q = warp & 3, hc = (warp - C::CONV_W0) >> 2;
                 const int r = hc * 128 + q * 32 + lane;
-                const uint8_t* src = sW + s * C::W_BYTES + r * 64;
-                uint4 raw[4];
+                const uint8_t* src = sW + s * C::W_BYTES + r * 128;
+                const uint32_t a_dst = tmem + ((uint32_t)(q * 32) << 16) + C::A_COL + c * KB + hc * (KB / 2);
 #pragma unroll
-                for (int ch = 0; ch < 4; ch++) raw[ch] = *reinterpret_cast<const uint4*>(src + ((ch ^ ((r >> 1) & 3)) << 4));
-                uint32_t o[32];   // column ch * 8 + 2j (+1): K = ch * 16 + 4j .. + 3
+                for (int hb = 0; hb < 2; hb++) {
+                    uint4 raw[4];
 #pragma unroll
-                for (int ch = 0; ch < 4; ch++) {
-                    i8x4_to_bf16x4(raw[ch].x, o[ch * 8 + 0], o[ch * 8 + 1]);
-                    i8x4_to_bf16x4(raw[ch].y, o[ch * 8 + 2], o[ch * 8 + 3]);
-                    i8x4_to_bf16x4(raw[ch].z, o[ch * 8 + 4], o[ch * 8 + 5]);
-                    i8x4_to_bf16x4(raw[ch].w, o[ch * 8 + 6], o[ch * 8 + 7]);
+                    for (int ch = 0; ch < 4; ch++)
+                        raw[ch] = *reinterpret_cast<const uint4*>(src + (((hb * 4 + ch) ^ (r & 7)) << 4));
+                    uint32_t o[32];   // column ch * 8 + 2j (+1): K = 64 hb + 16 ch + 4j .. + 3
+#pragma unroll
+                    for (int ch = 0; ch < 4; ch++) {
+                        i8x4_to_bf16x4(raw[ch].x, o[ch * 8 + 0], o[ch * 8 + 1]);
+                        i8x4_to_bf16x4(raw[ch].y, o[ch * 8 + 2], o[ch * 8 + 3]);
+                        i8x4_to_bf16x4(raw[ch].z, o[ch * 8 + 4], o[ch * 8 + 5]);
+                        i8x4_to_bf16x4(raw[ch].w, o[ch * 8 + 6], o[ch * 8 + 7]);
+                    }
+                    tmem_st32u(a_dst + hb * 32, o);
                 }
-                tmem_st32u(tmem + ((uint32_t)(q * 32) << 16) + C::A_COL + c * 64 + hc * 32, o);
                 tmem_wait_st();
                 tc_fence_before();
                 if (NORM) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // the activation tile
@@ -505,16 +523,17 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
             }
         }
         if (NORM) {
-            // the 8 chunks of a row sit in 8 consecutive lanes: partial sum of squares of
-            // each token row over this CTA's K range
+            // the RC chunks of a row sit in RC consecutive lanes: partial sum of squares
+            // of each token row over this CTA's K range
 #pragma unroll
             for (int u = 0; u < XI; u++) {
                 float v = ssv[u];
                 v += __shfl_xor_sync(0xffffffffu, v, 1);
                 v += __shfl_xor_sync(0xffffffffu, v, 2);
                 v += __shfl_xor_sync(0xffffffffu, v, 4);
+                if (RC == 16) v += __shfl_xor_sync(0xffffffffu, v, 8);
                 const int it = ct + u * CT;
-                if ((lane & 7) == 0 && it < NT * 8) s_ss[it >> 3] = v;
+                if ((lane & (RC - 1)) == 0 && it < NT * RC) s_ss[it / RC] = v;
             }
         }
     }
@@ -924,9 +943,9 @@ static int launch_gemm_tc(tb_ctx* ctx, const void* a, const void* b, const Epi& 
 // within the resident CTA slots (one wave; with two slots per SM the next
 // kernel's CTAs can start streaming their weights early) and gives every CTA
 // at least two K-blocks.
-static void gemv_split(int slots, int max_cs, int Nw, int K, int* splits_out, int* kb_per_out) {
+static void gemv_split(int slots, int max_cs, int Nw, int K, int KB, int* splits_out, int* kb_per_out) {
     const int tiles = (Nw + 255) / 256;
-    const int nk = (K + 63) / 64;
+    const int nk = (K + KB - 1) / KB;
     int cs = max_cs;
     while (cs > 1 && (tiles * cs > slots || nk < 2 * cs)) cs >>= 1;
     int kb_per = (nk + cs - 1) / cs;
@@ -942,8 +961,8 @@ static int launch_gemv_tc(tb_ctx* ctx, const void* x, const void* w, const Epi& 
     if (INT8) {
         uint64_t dims[2] = {(uint64_t)K, (uint64_t)Nw};
         uint64_t strides[1] = {(uint64_t)K};
-        uint32_t box[2] = {64, 256};
-        rc = make_tmap(ctx, &tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B);
+        uint32_t box[2] = {128, 256};
+        rc = make_tmap(ctx, &tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
     } else {
         rc = make_tmap_2d(ctx, &tw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w, Nw, K, K, 64, 256);
     }
@@ -980,7 +999,7 @@ static int launch_gemv_tc(tb_ctx* ctx, const void* x, const void* w, const Epi& 
     // resident CTA slots: two per SM when two rings fit in shared memory (bf16,
     // 16 or 32 tokens); int8 CTAs (384 threads) and 64-token rings hold one
     constexpr int per_sm = !INT8 && 2 * (C::SMEM + 1024) <= 228 * 1024 ? 2 : 1;
-    gemv_split(per_sm * ctx->num_sms, max_cs.load(), Nw, K, &cs, &kb_per);
+    gemv_split(per_sm * ctx->num_sms, max_cs.load(), Nw, K, C::KB, &cs, &kb_per);
     const int tiles = (Nw + 255) / 256;
     TB_CUDA_TRY(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     cudaLaunchConfig_t lc = {};
@@ -1008,9 +1027,9 @@ template <bool INT8>
 static int dispatch_gemv(tb_ctx* ctx, const void* x, const void* w, const Epi& ep, int M, int N, int K) {
     // <= 32 tokens: 3-stage rings (~105 KB) let two CTAs share an SM, so the
     // next layer's GEMV can start streaming weights (PDL) beside this one.
-    if (M <= 16) return launch_gemv_tc<16, INT8 ? 8 : 3, INT8>(ctx, x, w, ep, M, N, K);
-    if (M <= 32) return launch_gemv_tc<32, INT8 ? 8 : 3, INT8>(ctx, x, w, ep, M, N, K);
-    return launch_gemv_tc<64, INT8 ? 8 : 5, INT8>(ctx, x, w, ep, M, N, K);
+    if (M <= 16) return launch_gemv_tc<16, INT8 ? 5 : 3, INT8>(ctx, x, w, ep, M, N, K);
+    if (M <= 32) return launch_gemv_tc<32, INT8 ? 5 : 3, INT8>(ctx, x, w, ep, M, N, K);
+    return launch_gemv_tc<64, INT8 ? 4 : 5, INT8>(ctx, x, w, ep, M, N, K);
 }
 
 int linear_launch(tb_ctx* ctx, int int8, const void* x, const void* w, const Epi& ep, int M, int N, int K) {

@@ -185,7 +185,8 @@ def test_quantize_int8_bit_exact():
     np.testing.assert_array_equal(sb.cpu().numpy(), so)
 
 
-@pytest.mark.parametrize("M,N,K", [(64, 2048, 2048), (16, 3072, 2048), (1, 2048, 8192), (64, 1000, 512)])
+@pytest.mark.parametrize("M,N,K", [(64, 2048, 2048), (16, 3072, 2048), (1, 2048, 8192), (64, 1000, 512),
+                                   (16, 256, 48), (64, 512, 320)])
 def test_int8_linear(M, N, K):
     r = rng(M + N + K)
     w = (r.standard_normal((N, K)) * 0.02).astype(np.float32)
