@@ -762,9 +762,12 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
             }
             __syncthreads();
         }
-        // this thread: row pair pl2 of the owned slice, tokens m = m_first + u * (256 / P)
-        if (ewarp && ok && got) {
-            const int pl2 = threadIdx.x % P, mstep = 256 / P;
+        // this thread: row pair pl2 of the owned slice, tokens m = m_first + u * (ET / P);
+        // every thread of the int8 CTA (384, a multiple of P <= 64) takes items, the
+        // first 256 otherwise
+        constexpr int ET = INT8 ? C::THREADS : 256;
+        if (threadIdx.x < ET && ok && got) {
+            const int pl2 = threadIdx.x % P, mstep = ET / P;
             const PairK k = pair_consts(split * P + pl2);
             for (int m = threadIdx.x / P; m < NT; m += mstep) {
                 float r0, r1;
