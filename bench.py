@@ -549,7 +549,7 @@ def run_c1(args, rank, world, local):
 
 def ncu_case(which):
     """Small fixed cases for ncu captures of one kernel kind (the commands in profiles/):
-    gemv, attn_dec, gemm, fa, conv, or c4 (prefill + 3 decode steps for the launch list)."""
+    gemv, gemv8, attn_dec, gemm, fa, conv, or c4 (prefill + 3 decode steps for the launch list)."""
     import torch
     from teenygrad_b200 import ops
     torch.manual_seed(0)
@@ -558,6 +558,11 @@ def ncu_case(which):
         x = torch.randn(16, 2048, device="cuda").bfloat16()
         for w in ws:
             ops.linear(x, w, swiglu=True)
+    elif which == "gemv8":       # C5 decode gate/up GEMV: 64 tokens, int8 weights (4 distinct, 134 MB)
+        qs = [ops.quantize_int8((torch.randn(16384, 2048, device="cuda") * 0.02)) for _ in range(4)]
+        x = torch.randn(64, 2048, device="cuda").bfloat16()
+        for q, s in qs:
+            ops.int8_linear(x, q, s, swiglu=True)
     elif which == "attn_dec":    # C4 decode attention layer: 16 seqs x 8 kv heads x 1100 keys, G = 4
         q = torch.randn(16, 32, 1, 64, device="cuda").bfloat16()
         k = torch.randn(16, 8, 1100, 64, device="cuda").bfloat16()
