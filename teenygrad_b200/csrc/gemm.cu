@@ -295,6 +295,11 @@ struct GemvCfg {
     static constexpr int MMA_W1 = INT8 ? 2 : 8;     // second MMA-issuing warp (the first is warp 1)
     static constexpr int CONV_W0 = INT8 ? 4 : 2;    // first converter warp
     static constexpr int N_CONV = INT8 ? 8 : 6;     // converter warps
+    // An int8 CTA allocates all 512 TMEM columns (128 + 2 x 128 used; allocations
+    // are powers of two).  Its shared memory (> 114 KB) leaves too little beside it
+    // for any other TMEM-using CTA (the GEMV, attention, conv and GEMM kernels all
+    // need more than 100 KB), so no TMEM allocation ever waits on a neighbour.
+    static_assert(!INT8 || SMEM > 114 * 1024, "int8 GEMV CTAs must not share an SM with another TMEM user");
 };
 
 template <int NT, int STAGES, bool INT8>
