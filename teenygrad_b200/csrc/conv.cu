@@ -31,87 +31,89 @@ __device__ __forceinline__ float conv_epi(const ConvEpi& e, int co, float v) {
 }
 
 // ------------------------------------------------------------ layout prep --
-// x [B][C][H][W] (f32 or bf16) -> xn [B][H][W][Cp] bf16, channels >= C zero.
-// One CTA per (image row, 64 columns, 64 channels): 16-byte loads along w
-// into a shared [channel][column] tile (when rows are 16-byte aligned), then
-// 16-byte stores of 8 channels of one pixel.
-template <typename T>
+// One launch prepares both operands of the tensor-core conv:
+//  * x [B][C][H][W] bf16 -> xn [B][H][W][Cp] bf16, channels >= C zero.  CTA
+//    (image row, 64 columns, 64 channels) for blockIdx.z < B * H: thread
+//    (channel pair p, 8 columns) reads the two channel rows (16-byte loads
+//    when rows are 16-byte aligned), interleaves them into 32-bit (c, c + 1)
+//    words with byte permutes and stores them to a [pair][column] tile whose
+//    row stride of 66 words makes the read-back conflict-free; a thread then
+//    gathers 4 pairs of one column and stores 8 channels of one pixel (16 B).
+//    Only bits are moved: bf16 in, bf16 out.
+//  * w [Co][C][KH][KW] -> wr [Co][KH][KW][Cp] bf16 (channels >= C zero), one
+//    element per thread, by the first CTAs (blockIdx.z < rz), so they are
+//    scheduled first and overlap the transpose instead of trailing it.
+constexpr int PREP_TS = 66;   // tile row stride in 32-bit words (64 columns + 2)
+
 __global__ void __launch_bounds__(256)
-nchw_to_nhwc_kernel(const T* __restrict__ x, __nv_bfloat16* __restrict__ xn, int B, int C, int H, int W, int Cp) {
-    constexpr int V = 16 / sizeof(T);     // elements per 16-byte load
-    __shared__ __nv_bfloat16 tile[64][64 + 2];
+conv_prep_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ xn, int B, int C, int H, int W,
+                 int Cp, const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ wr, int Co, int KH, int KW,
+                 int rz) {
+    __shared__ __align__(16) uint32_t tile[32 * PREP_TS];
     pdl_trigger();
     pdl_wait();
-    const int bh = blockIdx.z;            // b * H + h
+    if ((int)blockIdx.z < rz) {
+        const int64_t total = (int64_t)Co * KH * KW * Cp;
+        const int64_t nrb = (int64_t)rz * gridDim.y * gridDim.x;
+        const int64_t rb = ((int64_t)blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
+        for (int64_t i = rb * 256 + threadIdx.x; i < total; i += nrb * 256) {
+            const int c = (int)(i % Cp);
+            int64_t r = i / Cp;
+            const int kw = (int)(r % KW);
+            r /= KW;
+            const int kh = (int)(r % KH);
+            const int co = (int)(r / KH);
+            wr[i] = c < C ? w[(((int64_t)co * C + c) * KH + kh) * KW + kw] : __float2bfloat16_rn(0.f);
+        }
+        return;
+    }
+    const int bh = blockIdx.z - rz;       // b * H + h
     const int b = bh / H, h = bh % H;
     const int w0 = blockIdx.x * 64, c0 = blockIdx.y * 64;
-    const bool vec = (W % V) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
-    for (int i = threadIdx.x; i < 64 * (64 / V); i += 256) {
-        const int c = i / (64 / V), wv = (i % (64 / V)) * V;
-        const int gc = c0 + c, gw = w0 + wv;
-        const T* row = x + (((int64_t)b * C + gc) * H + h) * W;
-        float v[V];
-        if (gc < C && vec && gw + V <= W) {
-            if constexpr (sizeof(T) == 4) {
-                const float4 f = *reinterpret_cast<const float4*>(row + gw);
-                v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
+    const bool vec = (W % 8) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+    {
+        const int p = threadIdx.x >> 3, ch = threadIdx.x & 7;   // channel pair, 8-column chunk
+        const int ca = c0 + 2 * p, gw = w0 + 8 * ch;
+        uint32_t lo[4] = {0, 0, 0, 0}, hi[4] = {0, 0, 0, 0};  // 8 bf16 of channel ca and ca + 1
+        if (gw < W) {
+            const __nv_bfloat16* ra = x + (((int64_t)b * C + ca) * H + h) * W + gw;
+            const __nv_bfloat16* rb = ra + (int64_t)H * W;
+            if (vec && gw + 8 <= W) {
+                if (ca < C) {
+                    const uint4 u = *reinterpret_cast<const uint4*>(ra);
+                    lo[0] = u.x; lo[1] = u.y; lo[2] = u.z; lo[3] = u.w;
+                }
+                if (ca + 1 < C) {
+                    const uint4 u = *reinterpret_cast<const uint4*>(rb);
+                    hi[0] = u.x; hi[1] = u.y; hi[2] = u.z; hi[3] = u.w;
+                }
             } else {
-                const uint4 u = *reinterpret_cast<const uint4*>(row + gw);
-                const uint32_t a[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-                for (int k = 0; k < 4; k++) {
-                    v[2 * k] = bf16_lo(a[k]);
-                    v[2 * k + 1] = bf16_hi(a[k]);
+                for (int k = 0; k < 8; k++) {
+                    const uint32_t va = (ca < C && gw + k < W) ? __bfloat16_as_ushort(ra[k]) : 0u;
+                    const uint32_t vb = (ca + 1 < C && gw + k < W) ? __bfloat16_as_ushort(rb[k]) : 0u;
+                    lo[k >> 1] |= va << (16 * (k & 1));
+                    hi[k >> 1] |= vb << (16 * (k & 1));
                 }
-            }
-        } else {
-#pragma unroll
-            for (int k = 0; k < V; k++) {
-                float t = 0.f;
-                if (gc < C && gw + k < W) {
-                    if constexpr (sizeof(T) == 4) t = row[gw + k];
-                    else t = __bfloat162float(row[gw + k]);
-                }
-                v[k] = t;
             }
         }
+        // word for column 2j: (ca, ca + 1) = low halves; column 2j + 1: high halves
+        uint32_t* trow = tile + p * PREP_TS + 8 * ch;
 #pragma unroll
-        for (int k = 0; k < V; k++) tile[c][wv + k] = __float2bfloat16_rn(v[k]);
+        for (int j = 0; j < 4; j++)
+            *reinterpret_cast<uint2*>(trow + 2 * j) =
+                make_uint2(__byte_perm(lo[j], hi[j], 0x5410), __byte_perm(lo[j], hi[j], 0x7632));
     }
     __syncthreads();
-    for (int i = threadIdx.x; i < 64 * 8; i += 256) {
-        const int w = i / 8, cg = (i % 8) * 8;
-        const int gw = w0 + w, gc = c0 + cg;
-        if (gw >= W || gc >= Cp) continue;
-        uint32_t o[4];
 #pragma unroll
-        for (int k = 0; k < 4; k++) {
-            const __nv_bfloat16 lo = tile[cg + 2 * k][w], hi = tile[cg + 2 * k + 1][w];
-            o[k] = (uint32_t)__bfloat16_as_ushort(lo) | ((uint32_t)__bfloat16_as_ushort(hi) << 16);
-        }
-        *reinterpret_cast<uint4*>(xn + (((int64_t)b * H + h) * W + gw) * Cp + gc) = make_uint4(o[0], o[1], o[2], o[3]);
-    }
-}
-
-// w [Co][C][KH][KW] -> wr [Co][KH][KW][Cp] bf16 (channels >= C zero)
-template <typename T>
-__global__ void reorder_weights_kernel(const T* __restrict__ w, __nv_bfloat16* __restrict__ wr, int Co, int C, int KH,
-                                       int KW, int Cp) {
-    const int64_t total = (int64_t)Co * KH * KW * Cp;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-        const int c = (int)(i % Cp);
-        int64_t r = i / Cp;
-        const int kw = (int)(r % KW);
-        r /= KW;
-        const int kh = (int)(r % KH);
-        const int co = (int)(r / KH);
-        float v = 0.f;
-        if (c < C) {
-            const T* p = w + (((int64_t)co * C + c) * KH + kh) * KW + kw;
-            if constexpr (sizeof(T) == 4) v = *p;
-            else v = __bfloat162float(*p);
-        }
-        wr[i] = __float2bfloat16_rn(v);
+    for (int k = 0; k < 2; k++) {
+        const int i = threadIdx.x + 256 * k;
+        const int oct = (i >> 3) & 7, col = (i & 7) + 8 * (i >> 6);   // 8-channel group, column
+        const int gw = w0 + col, gc = c0 + 8 * oct;
+        if (gw >= W || gc >= Cp) continue;
+        const uint32_t* t = tile + (4 * oct) * PREP_TS + col;
+        *reinterpret_cast<uint4*>(xn + (((int64_t)b * H + h) * W + gw) * Cp + gc) =
+            make_uint4(t[0], t[PREP_TS], t[2 * PREP_TS], t[3 * PREP_TS]);
     }
 }
 
@@ -586,14 +588,15 @@ int tb_conv2d_fwd(tb_ctx* ctx, int dtype, const void* x, const void* w, const fl
     __nv_bfloat16* wr = reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<uint8_t*>(workspace) +
                                                          (((size_t)B * H * W * s.Cp * 2 + 255) / 256) * 256);
     {
-        dim3 grid((W + 63) / 64, (s.Cp + 63) / 64, B * H);
-        int rc = launch(ctx, "nchw_to_nhwc", nchw_to_nhwc_kernel<__nv_bfloat16>, grid, dim3(256), 0,
-                        (const __nv_bfloat16*)x, xn, B, Cin, H, W, s.Cp);
-        if (rc) return rc;
+        // CTAs for the weight reorder (one element per thread, at most 64 z-slices), then
+        // transpose CTAs for every (image row, 64 columns, 64 channels)
         const int64_t tot = (int64_t)Cout * KH * KW * s.Cp;
-        rc = launch(ctx, "reorder_weights", reorder_weights_kernel<__nv_bfloat16>,
-                    dim3((unsigned)((tot + 255) / 256 < 4096 ? (tot + 255) / 256 : 4096)), dim3(256), 0,
-                    (const __nv_bfloat16*)w, wr, Cout, Cin, KH, KW, s.Cp);
+        const int gx = (W + 63) / 64, gy = (s.Cp + 63) / 64;
+        const int64_t per_z = (int64_t)gx * gy * 256;
+        const int rz = (int)std::min<int64_t>((tot + per_z - 1) / per_z, 64);
+        dim3 grid(gx, gy, rz + B * H);
+        int rc = launch(ctx, "conv_prep", conv_prep_kernel, grid, dim3(256), 0, (const __nv_bfloat16*)x, xn, B, Cin, H, W,
+                        s.Cp, (const __nv_bfloat16*)w, wr, Cout, KH, KW, rz);
         if (rc) return rc;
     }
     const int BH = conv_bh(s.OH);
