@@ -638,8 +638,14 @@ int tb_conv2d_fwd(tb_ctx* ctx, int dtype, const void* x, const void* w, const fl
     // resident weights: a grid that is a multiple of nN keeps each CTA on one output block
     int grid = wres ? (ctx->num_sms / nN) * nN : ctx->num_sms;
     if (units < grid) grid = (int)units;
-    return launch(ctx, "conv_tc", conv_tc_kernel, dim3(grid), dim3(CONV_THREADS), smem, mx, mw, my, ep, B, s.OH, s.OW, Cout,
+    // The conv reads the prep kernel's outputs only after griddepcontrol.wait, so this one
+    // edge may be programmatic: its CTAs start their prologue while the prep drains.
+    const bool pdl_saved = ctx->pdl;
+    ctx->pdl = true;
+    const int rc_conv = launch(ctx, "conv_tc", conv_tc_kernel, dim3(grid), dim3(CONV_THREADS), smem, mx, mw, my, ep, B, s.OH, s.OW, Cout,
                   KH, KW, s.Cp, pad, AS, wres, BH, OS, ctx->d_err);
+    ctx->pdl = pdl_saved;
+    return rc_conv;
 }
 
 int tb_bn_fold(tb_ctx* ctx, const float* gamma, const float* beta, const float* mean, const float* var,
