@@ -72,24 +72,41 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
     const uint32_t s_full0 = smem_u32(bars + 9), s_free0 = smem_u32(bars + 11);     // [2]
     const uint32_t p_full0 = smem_u32(bars + 13), p_free0 = smem_u32(bars + 15);    // [2]
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
+    const uint32_t q_empty = smem_u32(bars + 18);   // the S MMAs of a query tile have read Q
+    const uint32_t o_free = smem_u32(bars + 19);    // a query tile's O has been read out of TMEM
 
     pdl_trigger();
     const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
-    const int q_tile = gridDim.x - 1 - blockIdx.x;   // heaviest causal tiles first
     const int h = blockIdx.y, b = blockIdx.z;
     const int hk = h / (Hq / Hkv);
-    const int q0 = q_tile * C::BM;
     const int diag = Sk - Sq;                         // causal: key j visible to query i iff j <= i + diag
-    int n_tiles = (Sk + C::BN - 1) / C::BN;
+    // Query tiles of this CTA, processed one after the other: causal pairs a heavy
+    // tile with a light one (equal work per CTA), otherwise two neighbours.
+    const int nq_all = (Sq + C::BM - 1) / C::BM;
+    int qts[2], nqt;
     if (causal) {
-        int last_key = q0 + C::BM - 1 + diag;
-        int nt_c = last_key < 0 ? 0 : last_key / C::BN + 1;
-        n_tiles = min(n_tiles, nt_c);
+        qts[0] = nq_all - 1 - (int)blockIdx.x;
+        qts[1] = blockIdx.x;
+        nqt = qts[1] < qts[0] ? 2 : 1;
+    } else {
+        qts[0] = 2 * blockIdx.x;
+        qts[1] = 2 * blockIdx.x + 1;
+        nqt = qts[1] < nq_all ? 2 : 1;
     }
+    auto tiles_of = [&](int qt) {   // key tiles a query tile needs
+        int n = (Sk + C::BN - 1) / C::BN;
+        if (causal) {
+            const int last_key = qt * C::BM + C::BM - 1 + diag;
+            n = min(n, last_key < 0 ? 0 : last_key / C::BN + 1);
+        }
+        return n;
+    };
     constexpr int DB = D / 64;                        // 64-wide d blocks per tile
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
+        mbar_init(q_empty, 1);
+        mbar_init(o_free, 8);
         for (int s = 0; s < 2; s++) {
             mbar_init(k_full0 + 8 * s, 1);
             mbar_init(v_full0 + 8 * s, 1);
@@ -109,92 +126,128 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
     const uint32_t tmem = *tmem_slot;
     pdl_wait();
 
+    // Every ring and barrier continues across the query tiles: g counts key tiles over
+    // the whole CTA (stage / buffer g & 1, phase g >> 1), so each barrier's phases are
+    // waited on in order.
     if (warp == 0 || warp == 3) {
         // ---------------- producers: warp 0 Q and K tiles, warp 3 V tiles
-        if (lane == 0 && n_tiles > 0) {
+        if (lane == 0) {
             const bool isK = warp == 0;
             const CUtensorMap* tm = isK ? &tmK : &tmV;
             uint8_t* ring = isK ? sK : sV;
             const uint32_t full0 = isK ? k_full0 : v_full0, empty0 = isK ? k_empty0 : v_empty0;
             tma_prefetch_desc(tm);
-            if (isK) {
-                tma_prefetch_desc(&tmQ);
-                mbar_expect_tx(q_full, C::TILE);
-                for (int d = 0; d < DB; d++) tma_load_4d(smem_u32(sQ + d * 16384), &tmQ, q_full, 64 * d, h, q0, b);
+            if (isK) tma_prefetch_desc(&tmQ);
+            int g = 0;
+            bool ok = true;
+            for (int qi = 0; ok && qi < nqt; qi++) {
+                const int nt = tiles_of(qts[qi]);
+                if (isK) {
+                    // Q of the next query tile once the S MMAs have read the previous one
+                    if (qi > 0 && !mbar_wait(q_empty, (qi - 1) & 1, err, DEV_ERR_TIMEOUT_EMPTY)) break;
+                    mbar_expect_tx(q_full, C::TILE);
+                    for (int d = 0; d < DB; d++)
+                        tma_load_4d(smem_u32(sQ + d * 16384), &tmQ, q_full, 64 * d, h, qts[qi] * C::BM, b);
+                }
+                for (int j = 0; j < nt; j++, g++) {
+                    const int st = g & 1;
+                    if (g >= 2 && !mbar_wait(empty0 + 8 * st, ((g >> 1) - 1) & 1, err, DEV_ERR_TIMEOUT_EMPTY)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_expect_tx(full0 + 8 * st, C::TILE);
+                    for (int d = 0; d < DB; d++)
+                        tma_load_4d(smem_u32(ring + st * C::TILE + d * 16384), tm, full0 + 8 * st, 64 * d, hk, j * C::BN, b);
+                }
             }
-            int issued = 0;
-            for (int j = 0; j < n_tiles; j++) {
-                const int st = j & 1;
-                if (j >= 2 && !mbar_wait(empty0 + 8 * st, ((j >> 1) - 1) & 1, err, DEV_ERR_TIMEOUT_EMPTY)) break;
-                mbar_expect_tx(full0 + 8 * st, C::TILE);
-                for (int d = 0; d < DB; d++)
-                    tma_load_4d(smem_u32(ring + st * C::TILE + d * 16384), tm, full0 + 8 * st, 64 * d, hk, j * C::BN, b);
-                issued = j + 1;
-            }
-            if (isK) mbar_wait(q_full, 0, err, DEV_ERR_TIMEOUT_FULL);
-            for (int j = (issued > 2 ? issued - 2 : 0); j < issued; j++)
+            // every load this CTA issued has landed before it can exit
+            if (isK) mbar_wait(q_full, (nqt - 1) & 1, err, DEV_ERR_TIMEOUT_FULL);
+            for (int j = (g > 2 ? g - 2 : 0); j < g; j++)
                 mbar_wait(full0 + 8 * (j & 1), (j >> 1) & 1, err, DEV_ERR_TIMEOUT_FULL);
         }
     } else if (warp == 1) {
         // ---------------- S = Q K^T issuer
-        if (lane == 0 && n_tiles > 0) {
+        if (lane == 0) {
             constexpr uint32_t idesc_s = idesc_bf16_f32(128, C::BN, false, false);
             const uint64_t q_desc = sdesc_sw128(smem_u32(sQ), 16, 1024);
             const uint64_t k_desc = sdesc_sw128(smem_u32(sK), 16, 1024);
-            bool ok = mbar_wait(q_full, 0, err, DEV_ERR_TIMEOUT_FULL);
-            for (int j = 0; ok && j < n_tiles; j++) {
-                const int st = j & 1;
-                if (!mbar_wait(k_full0 + 8 * st, (j >> 1) & 1, err, DEV_ERR_TIMEOUT_FULL)) break;
-                if (j >= 2 && !mbar_wait(s_free0 + 8 * st, ((j >> 1) - 1) & 1, err, DEV_ERR_TIMEOUT_MISC)) break;
-                tc_fence_after();
-                const uint64_t kd = k_desc + (uint64_t)((st * C::TILE) >> 4);
+            int g = 0;
+            bool ok = true;
+            for (int qi = 0; ok && qi < nqt; qi++) {
+                const int nt = tiles_of(qts[qi]);
+                ok = mbar_wait(q_full, qi & 1, err, DEV_ERR_TIMEOUT_FULL);
+                for (int j = 0; ok && j < nt; j++, g++) {
+                    const int st = g & 1;
+                    if (!mbar_wait(k_full0 + 8 * st, (g >> 1) & 1, err, DEV_ERR_TIMEOUT_FULL) ||
+                        (g >= 2 && !mbar_wait(s_free0 + 8 * st, ((g >> 1) - 1) & 1, err, DEV_ERR_TIMEOUT_MISC))) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint64_t kd = k_desc + (uint64_t)((st * C::TILE) >> 4);
 #pragma unroll
-                for (int kk = 0; kk < D / 16; kk++) {
-                    const uint32_t off = ((kk >> 2) * 16384 + (kk & 3) * 32) >> 4;
-                    umma_f16_ss(tmem + st * 128, q_desc + off, kd + off, idesc_s, kk != 0);
+                    for (int kk = 0; kk < D / 16; kk++) {
+                        const uint32_t off = ((kk >> 2) * 16384 + (kk & 3) * 32) >> 4;
+                        umma_f16_ss(tmem + st * 128, q_desc + off, kd + off, idesc_s, kk != 0);
+                    }
+                    umma_commit(k_empty0 + 8 * st);
+                    umma_commit(s_full0 + 8 * st);
                 }
-                umma_commit(k_empty0 + 8 * st);
-                umma_commit(s_full0 + 8 * st);
+                umma_commit(q_empty);   // Q may be replaced once these S MMAs have completed
             }
         }
     } else if (warp == 2) {
         // ---------------- O += P V issuer
-        if (lane == 0 && n_tiles > 0) {
+        if (lane == 0) {
             constexpr uint32_t idesc_o = idesc_bf16_f32(128, D, false, true);
             const uint64_t p_desc = sdesc_sw128(smem_u32(sP), 16, 1024);
             const uint64_t v_desc = sdesc_sw128(smem_u32(sV), 16384, 1024);
-            for (int j = 0; j < n_tiles; j++) {
-                const int st = j & 1;
-                if (!mbar_wait(p_full0 + 8 * st, (j >> 1) & 1, err, DEV_ERR_TIMEOUT_MISC)) break;
-                if (!mbar_wait(v_full0 + 8 * st, (j >> 1) & 1, err, DEV_ERR_TIMEOUT_FULL)) break;
-                tc_fence_after();
-                const uint64_t pd = p_desc + (uint64_t)((st * C::P_BYTES) >> 4);
-                const uint64_t vd = v_desc + (uint64_t)((st * C::TILE) >> 4);
-                // keys 0-63 accumulate into O_0 (columns O_COL..), keys 64-127 into O_1 (O_COL + D..)
+            int g = 0;
+            bool ok = true;
+            for (int qi = 0; ok && qi < nqt; qi++) {
+                const int nt = tiles_of(qts[qi]);
+                // O of the previous query tile must have been read out before it is overwritten
+                if (qi > 0) ok = mbar_wait(o_free, (qi - 1) & 1, err, DEV_ERR_TIMEOUT_MISC);
+                for (int j = 0; ok && j < nt; j++, g++) {
+                    const int st = g & 1;
+                    if (!mbar_wait(p_full0 + 8 * st, (g >> 1) & 1, err, DEV_ERR_TIMEOUT_MISC) ||
+                        !mbar_wait(v_full0 + 8 * st, (g >> 1) & 1, err, DEV_ERR_TIMEOUT_FULL)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint64_t pd = p_desc + (uint64_t)((st * C::P_BYTES) >> 4);
+                    const uint64_t vd = v_desc + (uint64_t)((st * C::TILE) >> 4);
+                    // keys 0-63 accumulate into O_0 (columns O_COL..), keys 64-127 into O_1 (O_COL + D..)
 #pragma unroll
-                for (int kk = 0; kk < C::BN / 16; kk++)
-                    umma_f16_ss(tmem + C::O_COL + (kk >> 2) * D, pd + (((kk >> 2) * 16384 + (kk & 3) * 32) >> 4),
-                                vd + ((kk * 16 * 128) >> 4), idesc_o, (j | (kk & 3)) != 0);
-                umma_commit(v_empty0 + 8 * st);
-                umma_commit(p_free0 + 8 * st);
+                    for (int kk = 0; kk < C::BN / 16; kk++)
+                        umma_f16_ss(tmem + C::O_COL + (kk >> 2) * D, pd + (((kk >> 2) * 16384 + (kk & 3) * 32) >> 4),
+                                    vd + ((kk * 16 * 128) >> 4), idesc_o, (j | (kk & 3)) != 0);
+                    umma_commit(v_empty0 + 8 * st);
+                    umma_commit(p_free0 + 8 * st);
+                }
             }
         }
     } else if (warp >= 4) {
         // ---------------- softmax warps 4..11: thread <-> query row r (TMEM lane quarter
         // warp % 4) and key columns [64 * hf, 64 * hf + 64) of every tile (hf = (warp - 4) / 4).
         // Each half keeps its own reference max, row sum and O accumulator (O_hf); the
-        // two are merged once at the end, so no exchange is needed per tile.
+        // two are merged once at the end of each query tile, so no exchange is needed per tile.
         const int quarter = warp & 3, hf = (warp - 4) >> 2;
         const int r = quarter * 32 + lane;
-        const int qi = q0 + r;
         const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
         const uint32_t o_col = C::O_COL + hf * D;
-        const int lim = causal ? min(Sk - 1, qi + diag) : Sk - 1;   // last visible key
-        float m_ref = -INFINITY, l_run = 0.f;
+        int g = 0;
         bool ok = true;
-        for (int j = 0; j < n_tiles; j++) {
-            const int sb = j & 1;
-            ok = mbar_wait(s_full0 + 8 * sb, (j >> 1) & 1, err, DEV_ERR_TIMEOUT_MISC) && ok;
+        for (int qi = 0; qi < nqt; qi++) {
+        const int q0 = qts[qi] * C::BM;
+        const int n_tiles = tiles_of(qts[qi]);
+        const int qrow = q0 + r;
+        const int lim = causal ? min(Sk - 1, qrow + diag) : Sk - 1;   // last visible key
+        float m_ref = -INFINITY, l_run = 0.f;
+        for (int j = 0; j < n_tiles; j++, g++) {
+            const int sb = g & 1;
+            ok = mbar_wait(s_full0 + 8 * sb, (g >> 1) & 1, err, DEV_ERR_TIMEOUT_MISC) && ok;
             tc_fence_after();
             float s[64];
             tmem_ld32(t_lane + sb * 128 + hf * 64, s);
@@ -232,8 +285,8 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
                 l_run *= alpha;
             }
             if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
-                // O_hf holds P V of tiles < j: rescale once P V_{j-1} is done
-                ok = mbar_wait(p_free0 + 8 * ((j - 1) & 1), ((j - 1) >> 1) & 1, err, DEV_ERR_TIMEOUT_MISC) && ok;
+                // O_hf holds P V of this query tile's tiles < j: rescale once P V_{g-1} is done
+                ok = mbar_wait(p_free0 + 8 * ((g - 1) & 1), ((g - 1) >> 1) & 1, err, DEV_ERR_TIMEOUT_MISC) && ok;
                 tc_fence_after();
 #pragma unroll 1
                 for (int c = 0; c < D; c += 16) {
@@ -266,8 +319,8 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
                 }
             }
             l_run += ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
-            // P row half -> shared memory tile sb (free once P V_{j-2} is done): one 64-key atom
-            if (j >= 2) ok = mbar_wait(p_free0 + 8 * sb, ((j - 2) >> 1) & 1, err, DEV_ERR_TIMEOUT_MISC) && ok;
+            // P row half -> shared memory tile sb (free once P V_{g-2} is done): one 64-key atom
+            if (g >= 2) ok = mbar_wait(p_free0 + 8 * sb, ((g - 2) >> 1) & 1, err, DEV_ERR_TIMEOUT_MISC) && ok;
             uint8_t* prow = sP + sb * C::P_BYTES + hf * 16384 + r * 128;
 #pragma unroll
             for (int c8 = 0; c8 < 8; c8++) {
@@ -283,14 +336,17 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
             __syncwarp();
             if (lane == 0) mbar_arrive(p_full0 + 8 * sb);
         }
+        // this query tile's last P V (g - 1); then the P tiles are free: exchange (max, sum)
+        // of the two halves there
         if (n_tiles > 0)
-            ok = mbar_wait(p_free0 + 8 * ((n_tiles - 1) & 1), ((n_tiles - 1) >> 1) & 1, err, DEV_ERR_TIMEOUT_ACC) && ok;
-        // Every P V is done, so the P tiles are free: exchange (max, sum) of the two halves there.
+            ok = mbar_wait(p_free0 + 8 * ((g - 1) & 1), ((g - 1) >> 1) & 1, err, DEV_ERR_TIMEOUT_ACC) && ok;
         float* xch = reinterpret_cast<float*>(sP);   // [2 halves][128 rows][2]
         xch[(hf * 128 + r) * 2] = m_ref;
         xch[(hf * 128 + r) * 2 + 1] = l_run;
         asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
         const float m_o = xch[((hf ^ 1) * 128 + r) * 2], l_o = xch[((hf ^ 1) * 128 + r) * 2 + 1];
+        // both halves have read the exchange before the next query tile's P reuses it
+        asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
         const float M = fmaxf(m_ref, m_o);
         const float w_a = (hf == 0 ? m_ref : m_o) == -INFINITY ? 0.f : ex2((hf == 0 ? m_ref : m_o) - M);
         const float w_b = (hf == 0 ? m_o : m_ref) == -INFINITY ? 0.f : ex2((hf == 0 ? m_o : m_ref) - M);
@@ -300,8 +356,8 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
             tc_fence_after();
             const float inv_l = (l_tot > 0.f) ? 1.0f / l_tot : 0.f;
             const float ca = w_a * inv_l, cb = w_b * inv_l;
-            const bool valid = qi < Sq;
-            const int64_t obase = (int64_t)b * out.o_sb + (int64_t)h * out.o_sh + (int64_t)qi * out.o_ss;
+            const bool valid = qrow < Sq;
+            const int64_t obase = (int64_t)b * out.o_sb + (int64_t)h * out.o_sh + (int64_t)qrow * out.o_ss;
 #pragma unroll 1
             for (int c = hf * (D / 2); c < (hf + 1) * (D / 2); c += 32) {
                 float oa[32], ob[32];
@@ -331,8 +387,13 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
             }
             if (valid && out.lse && hf == 0) {
                 const float lse = (l_tot > 0.f) ? (M + log2f(l_tot)) * kLn2 : -INFINITY;
-                out.lse[((int64_t)b * Hq + h) * Sq + qi] = lse;
+                out.lse[((int64_t)b * Hq + h) * Sq + qrow] = lse;
             }
+        }
+        // O has been read: the next query tile's first P V may overwrite it
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(o_free);
         }
     }
     __syncwarp();
@@ -846,7 +907,8 @@ int attn_tc_launch(tb_ctx* ctx, const AttnTensors& t, int B, int Hq, int Hkv, in
     if (!rc) rc = tmap_heads(ctx, &mv, t.v, D, Hkv, t.kv_len_alloc, B, t.kv_sh, t.kv_ss, t.kv_sb);
     if (rc) return rc;
     AttnOut out{t.o, t.o_sh, t.o_ss, t.o_sb, t.lse};
-    dim3 grid((Sq + 127) / 128, Hq, B);
+    // two query tiles per CTA (a heavy and a light one when causal)
+    dim3 grid(((Sq + 127) / 128 + 1) / 2, Hq, B);
     const float sl2 = scale * kLog2e;
     if (D == 64) {
         // 512 TMEM columns per CTA: keep one CTA per SM (the padding does that).
