@@ -240,160 +240,160 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
         int g = 0;
         bool ok = true;
         for (int qi = 0; qi < nqt; qi++) {
-        const int q0 = qts[qi] * C::BM;
-        const int n_tiles = tiles_of(qts[qi]);
-        const int qrow = q0 + r;
-        const int lim = causal ? min(Sk - 1, qrow + diag) : Sk - 1;   // last visible key
-        float m_ref = -INFINITY, l_run = 0.f;
-        for (int j = 0; j < n_tiles; j++, g++) {
-            const int sb = g & 1;
-            ok = mbar_wait(s_full0 + 8 * sb, (g >> 1) & 1, err, DEV_ERR_TIMEOUT_MISC) && ok;
-            tc_fence_after();
-            float s[64];
-            tmem_ld32(t_lane + sb * 128 + hf * 64, s);
-            tmem_ld32(t_lane + sb * 128 + hf * 64 + 32, s + 32);
-            tmem_wait_ld();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(s_free0 + 8 * sb);   // S buffer sb may be overwritten
-            const int k0 = j * C::BN + hf * 64;
-            // 8 independent max chains (latency, not issue, bounds this loop otherwise)
-            float mx8[8];
-#pragma unroll
-            for (int u = 0; u < 8; u++) mx8[u] = -INFINITY;
-            // every key of this half visible (and a positive scale): the max of the raw
-            // scores, scaled once; the scale is folded into the exponent's FMA below
-            const bool raw = k0 + 63 <= lim && scale_log2 > 0.f;
-            if (raw) {
-#pragma unroll
-                for (int c = 0; c < 64; c++) mx8[c & 7] = fmaxf(mx8[c & 7], s[c]);
-            } else {
-#pragma unroll
-                for (int c = 0; c < 64; c++) {
-                    const float v = (k0 + c <= lim) ? s[c] * scale_log2 : -INFINITY;
-                    s[c] = v;
-                    mx8[c & 7] = fmaxf(mx8[c & 7], v);
-                }
-            }
-            float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
-            if (raw) mx *= scale_log2;
-            float alpha = 1.f;
-            if (mx > m_ref + C::RESCALE_LOG2) {   // raise the reference max (m_ref = -inf: first visible tile)
-                alpha = ex2(m_ref - mx);           // -inf -> 0
-                m_ref = mx;
-                l_run *= alpha;
-            }
-            if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
-                // O_hf holds P V of this query tile's tiles < j: rescale once P V_{g-1} is done
-                ok = mbar_wait(p_free0 + 8 * ((g - 1) & 1), ((g - 1) >> 1) & 1, err, DEV_ERR_TIMEOUT_MISC) && ok;
+            const int q0 = qts[qi] * C::BM;
+            const int n_tiles = tiles_of(qts[qi]);
+            const int qrow = q0 + r;
+            const int lim = causal ? min(Sk - 1, qrow + diag) : Sk - 1;   // last visible key
+            float m_ref = -INFINITY, l_run = 0.f;
+            for (int j = 0; j < n_tiles; j++, g++) {
+                const int sb = g & 1;
+                ok = mbar_wait(s_full0 + 8 * sb, (g >> 1) & 1, err, DEV_ERR_TIMEOUT_MISC) && ok;
                 tc_fence_after();
-#pragma unroll 1
-                for (int c = 0; c < D; c += 16) {
-                    float o[16];
-                    tmem_ld16(t_lane + o_col + c, o);
-                    tmem_wait_ld();
+                float s[64];
+                tmem_ld32(t_lane + sb * 128 + hf * 64, s);
+                tmem_ld32(t_lane + sb * 128 + hf * 64 + 32, s + 32);
+                tmem_wait_ld();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(s_free0 + 8 * sb);   // S buffer sb may be overwritten
+                const int k0 = j * C::BN + hf * 64;
+                // 8 independent max chains (latency, not issue, bounds this loop otherwise)
+                float mx8[8];
 #pragma unroll
-                    for (int i = 0; i < 16; i++) o[i] *= alpha;
-                    tmem_st16(t_lane + o_col + c, o);
-                }
-                tmem_wait_st();
-            }
-            const float m_use = (m_ref == -INFINITY) ? 0.f : m_ref;
-            float rs8[8];
+                for (int u = 0; u < 8; u++) mx8[u] = -INFINITY;
+                // every key of this half visible (and a positive scale): the max of the raw
+                // scores, scaled once; the scale is folded into the exponent's FMA below
+                const bool raw = k0 + 63 <= lim && scale_log2 > 0.f;
+                if (raw) {
 #pragma unroll
-            for (int u = 0; u < 8; u++) rs8[u] = 0.f;
-            if (raw) {
-#pragma unroll
-                for (int c = 0; c < 64; c++) {
-                    const float p = ex2(fmaf(s[c], scale_log2, -m_use));
-                    s[c] = p;
-                    rs8[c & 7] += p;
-                }
-            } else {
-#pragma unroll
-                for (int c = 0; c < 64; c++) {
-                    const float p = ex2(s[c] - m_use);   // s = -inf -> 0
-                    s[c] = p;
-                    rs8[c & 7] += p;
-                }
-            }
-            l_run += ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
-            // P row half -> shared memory tile sb (free once P V_{g-2} is done): one 64-key atom
-            if (g >= 2) ok = mbar_wait(p_free0 + 8 * sb, ((g - 2) >> 1) & 1, err, DEV_ERR_TIMEOUT_MISC) && ok;
-            uint8_t* prow = sP + sb * C::P_BYTES + hf * 16384 + r * 128;
-#pragma unroll
-            for (int c8 = 0; c8 < 8; c8++) {
-                uint4 v;
-                v.x = pack_bf16x2(s[c8 * 8 + 0], s[c8 * 8 + 1]);
-                v.y = pack_bf16x2(s[c8 * 8 + 2], s[c8 * 8 + 3]);
-                v.z = pack_bf16x2(s[c8 * 8 + 4], s[c8 * 8 + 5]);
-                v.w = pack_bf16x2(s[c8 * 8 + 6], s[c8 * 8 + 7]);
-                *reinterpret_cast<uint4*>(prow + ((c8 ^ (r & 7)) << 4)) = v;
-            }
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(p_full0 + 8 * sb);
-        }
-        // this query tile's last P V (g - 1); then the P tiles are free: exchange (max, sum)
-        // of the two halves there
-        if (n_tiles > 0)
-            ok = mbar_wait(p_free0 + 8 * ((g - 1) & 1), ((g - 1) >> 1) & 1, err, DEV_ERR_TIMEOUT_ACC) && ok;
-        float* xch = reinterpret_cast<float*>(sP);   // [2 halves][128 rows][2]
-        xch[(hf * 128 + r) * 2] = m_ref;
-        xch[(hf * 128 + r) * 2 + 1] = l_run;
-        asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
-        const float m_o = xch[((hf ^ 1) * 128 + r) * 2], l_o = xch[((hf ^ 1) * 128 + r) * 2 + 1];
-        // both halves have read the exchange before the next query tile's P reuses it
-        asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
-        const float M = fmaxf(m_ref, m_o);
-        const float w_a = (hf == 0 ? m_ref : m_o) == -INFINITY ? 0.f : ex2((hf == 0 ? m_ref : m_o) - M);
-        const float w_b = (hf == 0 ? m_o : m_ref) == -INFINITY ? 0.f : ex2((hf == 0 ? m_o : m_ref) - M);
-        const float l_tot = (hf == 0 ? l_run : l_o) * w_a + (hf == 0 ? l_o : l_run) * w_b;
-        ok = __all_sync(0xffffffffu, ok);
-        if (ok) {
-            tc_fence_after();
-            const float inv_l = (l_tot > 0.f) ? 1.0f / l_tot : 0.f;
-            const float ca = w_a * inv_l, cb = w_b * inv_l;
-            const bool valid = qrow < Sq;
-            const int64_t obase = (int64_t)b * out.o_sb + (int64_t)h * out.o_sh + (int64_t)qrow * out.o_ss;
-#pragma unroll 1
-            for (int c = hf * (D / 2); c < (hf + 1) * (D / 2); c += 32) {
-                float oa[32], ob[32];
-                if (n_tiles > 0) {
-                    tmem_ld32(t_lane + C::O_COL + c, oa);
-                    tmem_ld32(t_lane + C::O_COL + D + c, ob);
-                    tmem_wait_ld();
+                    for (int c = 0; c < 64; c++) mx8[c & 7] = fmaxf(mx8[c & 7], s[c]);
                 } else {
 #pragma unroll
-                    for (int i = 0; i < 32; i++) oa[i] = ob[i] = 0.f;
-                }
-                if (valid) {
-                    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(out.o) + obase + c;
-#pragma unroll
-                    for (int i = 0; i < 32; i += 8) {
-                        float o[8];
-#pragma unroll
-                        for (int e = 0; e < 8; e++) o[e] = oa[i + e] * ca + ob[i + e] * cb;
-                        uint4 v;
-                        v.x = pack_bf16x2(o[0], o[1]);
-                        v.y = pack_bf16x2(o[2], o[3]);
-                        v.z = pack_bf16x2(o[4], o[5]);
-                        v.w = pack_bf16x2(o[6], o[7]);
-                        *reinterpret_cast<uint4*>(dst + i) = v;
+                    for (int c = 0; c < 64; c++) {
+                        const float v = (k0 + c <= lim) ? s[c] * scale_log2 : -INFINITY;
+                        s[c] = v;
+                        mx8[c & 7] = fmaxf(mx8[c & 7], v);
                     }
                 }
+                float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                                 fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+                if (raw) mx *= scale_log2;
+                float alpha = 1.f;
+                if (mx > m_ref + C::RESCALE_LOG2) {   // raise the reference max (m_ref = -inf: first visible tile)
+                    alpha = ex2(m_ref - mx);           // -inf -> 0
+                    m_ref = mx;
+                    l_run *= alpha;
+                }
+                if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+                    // O_hf holds P V of this query tile's tiles < j: rescale once P V_{g-1} is done
+                    ok = mbar_wait(p_free0 + 8 * ((g - 1) & 1), ((g - 1) >> 1) & 1, err, DEV_ERR_TIMEOUT_MISC) && ok;
+                    tc_fence_after();
+#pragma unroll 1
+                    for (int c = 0; c < D; c += 16) {
+                        float o[16];
+                        tmem_ld16(t_lane + o_col + c, o);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 16; i++) o[i] *= alpha;
+                        tmem_st16(t_lane + o_col + c, o);
+                    }
+                    tmem_wait_st();
+                }
+                const float m_use = (m_ref == -INFINITY) ? 0.f : m_ref;
+                float rs8[8];
+#pragma unroll
+                for (int u = 0; u < 8; u++) rs8[u] = 0.f;
+                if (raw) {
+#pragma unroll
+                    for (int c = 0; c < 64; c++) {
+                        const float p = ex2(fmaf(s[c], scale_log2, -m_use));
+                        s[c] = p;
+                        rs8[c & 7] += p;
+                    }
+                } else {
+#pragma unroll
+                    for (int c = 0; c < 64; c++) {
+                        const float p = ex2(s[c] - m_use);   // s = -inf -> 0
+                        s[c] = p;
+                        rs8[c & 7] += p;
+                    }
+                }
+                l_run += ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
+                // P row half -> shared memory tile sb (free once P V_{g-2} is done): one 64-key atom
+                if (g >= 2) ok = mbar_wait(p_free0 + 8 * sb, ((g - 2) >> 1) & 1, err, DEV_ERR_TIMEOUT_MISC) && ok;
+                uint8_t* prow = sP + sb * C::P_BYTES + hf * 16384 + r * 128;
+#pragma unroll
+                for (int c8 = 0; c8 < 8; c8++) {
+                    uint4 v;
+                    v.x = pack_bf16x2(s[c8 * 8 + 0], s[c8 * 8 + 1]);
+                    v.y = pack_bf16x2(s[c8 * 8 + 2], s[c8 * 8 + 3]);
+                    v.z = pack_bf16x2(s[c8 * 8 + 4], s[c8 * 8 + 5]);
+                    v.w = pack_bf16x2(s[c8 * 8 + 6], s[c8 * 8 + 7]);
+                    *reinterpret_cast<uint4*>(prow + ((c8 ^ (r & 7)) << 4)) = v;
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(p_full0 + 8 * sb);
             }
-            if (valid && out.lse && hf == 0) {
-                const float lse = (l_tot > 0.f) ? (M + log2f(l_tot)) * kLn2 : -INFINITY;
-                out.lse[((int64_t)b * Hq + h) * Sq + qrow] = lse;
+            // this query tile's last P V (g - 1); then the P tiles are free: exchange (max, sum)
+            // of the two halves there
+            if (n_tiles > 0)
+                ok = mbar_wait(p_free0 + 8 * ((g - 1) & 1), ((g - 1) >> 1) & 1, err, DEV_ERR_TIMEOUT_ACC) && ok;
+            float* xch = reinterpret_cast<float*>(sP);   // [2 halves][128 rows][2]
+            xch[(hf * 128 + r) * 2] = m_ref;
+            xch[(hf * 128 + r) * 2 + 1] = l_run;
+            asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
+            const float m_o = xch[((hf ^ 1) * 128 + r) * 2], l_o = xch[((hf ^ 1) * 128 + r) * 2 + 1];
+            // both halves have read the exchange before the next query tile's P reuses it
+            asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
+            const float M = fmaxf(m_ref, m_o);
+            const float w_a = (hf == 0 ? m_ref : m_o) == -INFINITY ? 0.f : ex2((hf == 0 ? m_ref : m_o) - M);
+            const float w_b = (hf == 0 ? m_o : m_ref) == -INFINITY ? 0.f : ex2((hf == 0 ? m_o : m_ref) - M);
+            const float l_tot = (hf == 0 ? l_run : l_o) * w_a + (hf == 0 ? l_o : l_run) * w_b;
+            ok = __all_sync(0xffffffffu, ok);
+            if (ok) {
+                tc_fence_after();
+                const float inv_l = (l_tot > 0.f) ? 1.0f / l_tot : 0.f;
+                const float ca = w_a * inv_l, cb = w_b * inv_l;
+                const bool valid = qrow < Sq;
+                const int64_t obase = (int64_t)b * out.o_sb + (int64_t)h * out.o_sh + (int64_t)qrow * out.o_ss;
+#pragma unroll 1
+                for (int c = hf * (D / 2); c < (hf + 1) * (D / 2); c += 32) {
+                    float oa[32], ob[32];
+                    if (n_tiles > 0) {
+                        tmem_ld32(t_lane + C::O_COL + c, oa);
+                        tmem_ld32(t_lane + C::O_COL + D + c, ob);
+                        tmem_wait_ld();
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 32; i++) oa[i] = ob[i] = 0.f;
+                    }
+                    if (valid) {
+                        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(out.o) + obase + c;
+#pragma unroll
+                        for (int i = 0; i < 32; i += 8) {
+                            float o[8];
+#pragma unroll
+                            for (int e = 0; e < 8; e++) o[e] = oa[i + e] * ca + ob[i + e] * cb;
+                            uint4 v;
+                            v.x = pack_bf16x2(o[0], o[1]);
+                            v.y = pack_bf16x2(o[2], o[3]);
+                            v.z = pack_bf16x2(o[4], o[5]);
+                            v.w = pack_bf16x2(o[6], o[7]);
+                            *reinterpret_cast<uint4*>(dst + i) = v;
+                        }
+                    }
+                }
+                if (valid && out.lse && hf == 0) {
+                    const float lse = (l_tot > 0.f) ? (M + log2f(l_tot)) * kLn2 : -INFINITY;
+                    out.lse[((int64_t)b * Hq + h) * Sq + qrow] = lse;
+                }
             }
-        }
-        // O has been read: the next query tile's first P V may overwrite it
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(o_free);
+            // O has been read: the next query tile's first P V may overwrite it
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(o_free);
         }
     }
     __syncwarp();
