@@ -574,8 +574,8 @@ def ncu_case(which):
         x = torch.randn(16384, 2048, device="cuda").bfloat16()
         for _ in range(2):
             ops.linear(x, w, swiglu=True)
-    elif which == "fa":          # an 8-head slice of C3: B1 H8 S4096 D128 causal
-        q, k, v = (torch.randn(1, 8, 4096, 128, device="cuda").bfloat16() for _ in range(3))
+    elif which == "fa":          # a quarter of C3: B2 H32 S4096 D128 causal (1024 CTAs)
+        q, k, v = (torch.randn(2, 32, 4096, 128, device="cuda").bfloat16() for _ in range(3))
         for _ in range(2):
             ops.attention(q, k, v, causal=True)
     elif which == "conv":        # one C2 conv: B32 64->64 56x56 3x3 + BN + ReLU
