@@ -141,10 +141,12 @@ __global__ void rope_kv_kernel(__nv_bfloat16* __restrict__ qkv, int qkv_n, int B
 // RMSNorm with an input row stride (last-token gather for the LM head).  One
 // warp per row; the row (N <= 4096 bf16) stays in registers: every load is
 // issued before the reduction, and the second pass reads no memory.
+// MAXC: 16-byte chunks per lane (rows up to 256 * MAXC elements); the smallest that
+// fits keeps the registers low enough for more rows in flight per SM.
+template <int MAXC>
 __global__ void rmsnorm_ld_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, const __nv_bfloat16* __restrict__ w,
                                   __nv_bfloat16* __restrict__ y, int M, int N, float eps) {
     pdl_trigger();
-    constexpr int MAXC = 16;   // 16-byte chunks per lane
     const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
     const int lane = threadIdx.x & 31;
     uint4 g[MAXC];
@@ -364,7 +366,10 @@ int lin(tb_decoder* d, const void* x, const void* w, const int8_t* wq, const flo
 
 int rms(tb_decoder* d, const bf16* x, int64_t ldx, const bf16* w, bf16* y, int M) {
     const int N = d->cfg.d_model;
-    return launch(d->ctx, "rmsnorm", rmsnorm_ld_kernel, dim3((M + 7) / 8), dim3(256), 0, x, ldx, w, y, M, N,
+    if (N <= 256 * 8)
+        return launch(d->ctx, "rmsnorm", rmsnorm_ld_kernel<8>, dim3((M + 7) / 8), dim3(256), 0, x, ldx, w, y, M, N,
+                      d->cfg.norm_eps);
+    return launch(d->ctx, "rmsnorm", rmsnorm_ld_kernel<16>, dim3((M + 7) / 8), dim3(256), 0, x, ldx, w, y, M, N,
                   d->cfg.norm_eps);
 }
 
