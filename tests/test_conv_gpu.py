@@ -66,7 +66,8 @@ def _conv_case(B, C, Co, H, W, k, stride, pad, act, dtype, seed, with_bn=True):
 @pytest.mark.parametrize("B,C,Co,H,W,k,p,act", [(2, 64, 64, 24, 24, 3, 1, "relu"), (1, 3, 40, 20, 16, 3, 1, "silu"),
                                                 (2, 128, 96, 16, 32, 3, 1, None), (32, 64, 64, 56, 56, 3, 1, "relu"),
                                                 (2, 32, 64, 16, 16, 1, 0, "relu"), (1, 16, 32, 20, 24, 5, 2, None),
-                                                (1, 8, 64, 22, 24, 7, 3, "relu"), (1, 24, 72, 30, 42, 3, 0, None)])
+                                                (1, 8, 64, 22, 24, 7, 3, "relu"), (1, 24, 72, 30, 42, 3, 0, None),
+                                                (1, 16, 64, 10, 80, 3, 1, "relu")])   # two 64-column prep tiles
 def test_conv2d_bf16_tensor_cores(B, C, Co, H, W, k, p, act):
     got, ref = _conv_case(B, C, Co, H, W, k, 1, p, act, torch.bfloat16, seed=B + C + Co + k)
     assert_close(got, ref, BF16_TOL)
