@@ -268,6 +268,26 @@ def test_attention_bf16_tc(B, Hq, Hkv, Sq, Sk, D, causal):
     assert_close(np_of(lse), rl, 1e-3, "LSE")
 
 
+@pytest.mark.parametrize("D", [64, 128])
+def test_attention_causal_rows_without_keys(D):
+    # causal with Sq > Sk (bottom-right aligned): the first Sq - Sk queries see no key, so
+    # whole query tiles have no key tile at all; O is 0 and LSE -inf there, as in the oracle
+    r = rng(D + 7)
+    B, Hq, Hkv, Sq, Sk = 1, 2, 1, 300, 100
+    q = bf16_round(r.standard_normal((B, Hq, Sq, D)))
+    k = bf16_round(r.standard_normal((B, Hkv, Sk, D)))
+    v = bf16_round(r.standard_normal((B, Hkv, Sk, D)))
+    sc = 1.0 / math.sqrt(D)
+    o, lse = ops().attention(*(to_gpu(a, torch.bfloat16) for a in (q, k, v)), scale=sc, causal=True, return_lse=True)
+    ro, rl = oracle.attention(q, k, v, sc, True)
+    assert_close(np_of(o), ro, BF16_TOL, "O")
+    got = np_of(lse)
+    masked = np.isneginf(rl)
+    assert masked.any() and not masked.all()
+    assert np.array_equal(np.isneginf(got), masked), "LSE -inf pattern"
+    assert_close(got[~masked], rl[~masked], 1e-3, "LSE")
+
+
 @pytest.mark.parametrize("B,Hq,Hkv,Sk,D", [(4, 32, 8, 1000, 64), (2, 8, 8, 2048, 128), (3, 4, 1, 5, 64)])
 def test_attention_decode(B, Hq, Hkv, Sk, D):
     r = rng(Sk + D)
