@@ -140,7 +140,8 @@ def test_linear_bf16_swiglu(M):
     assert_close(np_of(y), ref, BF16_TOL)
 
 
-@pytest.mark.parametrize("M,N,K", [(1, 3072, 2048), (16, 2048, 2048), (33, 1000, 512), (64, 32000, 2048), (16, 2048, 8192)])
+@pytest.mark.parametrize("M,N,K", [(1, 3072, 2048), (16, 2048, 2048), (24, 2048, 2048), (33, 1000, 512), (64, 32000, 2048),
+                                   (16, 2048, 8192)])
 def test_linear_bf16_decode_gemv(M, N, K):
     r = rng(M * 7 + N)
     x = bf16_round(r.standard_normal((M, K)))
@@ -186,7 +187,7 @@ def test_quantize_int8_bit_exact():
 
 
 @pytest.mark.parametrize("M,N,K", [(64, 2048, 2048), (16, 3072, 2048), (1, 2048, 8192), (64, 1000, 512),
-                                   (16, 256, 48), (64, 512, 320)])
+                                   (16, 256, 48), (64, 512, 320), (24, 1024, 1536)])
 def test_int8_linear(M, N, K):
     r = rng(M + N + K)
     w = (r.standard_normal((N, K)) * 0.02).astype(np.float32)
