@@ -92,6 +92,30 @@ def test_decoder_int8():
     no_device_error()
 
 
+@pytest.mark.parametrize("int8", [False, True])
+def test_decoder_wide_split_k(int8):
+    # d_model 1024 and ffn 2048 give the GEMVs enough K blocks to split K over a
+    # cluster, so prefill (40 tokens) and decode (2 tokens) run the cluster exchange
+    # together with the fused RMSNorm's sums of squares and the RoPE / KV-cache
+    # epilogue; the small model's few K blocks never leave the single-CTA path
+    dev()
+    cfg = SmallCfg(d_model=1024, n_heads=16, n_kv_heads=4, ffn_hidden=2048, vocab=512)
+    p = random_params(cfg, seed=6)
+    dec = make(cfg, int8=int8)
+    upload(dec, p)
+    ora = OracleDecoder(cfg, p, int8=int8)
+    ids = np.random.default_rng(11).integers(0, cfg.vocab, (2, 20)).astype(np.int32)
+    nxt, logits = dec.prefill(torch.from_numpy(ids).cuda(), return_logits=True)
+    ref = ora.forward(ids)
+    assert_close(np_of(logits), ref, BF16_TOL, "prefill logits")
+    for step in range(2):
+        tok = np.argmax(ref, axis=1).astype(np.int32)
+        nxt, logits = dec.decode_step(torch.from_numpy(tok).cuda(), return_logits=True)
+        ref = ora.forward(tok[:, None])
+        assert_close(np_of(logits), ref, BF16_TOL, f"decode step {step}")
+    no_device_error()
+
+
 def test_decoder_fill_kv_random_decode_only():
     dev()
     cfg = SmallCfg()
