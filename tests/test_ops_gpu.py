@@ -256,6 +256,7 @@ def test_attention_f32_causal_gqa():
     (2, 4, 1, 256, 256, 128, True),
     (1, 2, 2, 200, 456, 128, True),
     (1, 2, 2, 130, 77, 64, False),
+    (1, 4, 2, 300, 200, 128, False),
 ])
 def test_attention_bf16_tc(B, Hq, Hkv, Sq, Sk, D, causal):
     r = rng(B * 1000 + Sq + Sk + D)
