@@ -30,7 +30,11 @@ __device__ __forceinline__ float ex2(float x) {
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 
-// Per (128-query tile, head, image) CTA.  Warp 0 streams K tiles and warp 3 V
+// Per (head, image) and pair of 128-query tiles, one CTA that takes the two
+// tiles in turn (a heavy and a light one when causal, so CTAs carry equal
+// work); its rings and barrier phases run on across them, so the second tile's
+// loads and first MMAs overlap the first tile's epilogue.  Warp 0 streams Q
+// and K tiles and warp 3 V
 // tiles (TMA, 2-stage rings), warp 1 issues S = Q K^T (M = 128 queries,
 // N = 128 keys) into one of two TMEM buffers and warp 2 issues O += P V
 // (N = D), each on its own issuing thread (one thread issues an MMA per
