@@ -75,6 +75,14 @@ TB_API const char* tb_last_error(tb_ctx* ctx);
  * set (0 = none); clears it when `clear` is non-zero. */
 TB_API int tb_device_error(tb_ctx* ctx, int* code, int clear);
 TB_API int tb_abi_version(void);
+/* Failure-path self-test (no counterpart in the reference, which has no
+ * device-side waits).  Launches two CTAs that wait on an mbarrier nothing
+ * arrives on: CTA 0 with a limit of limit_us, CTA 1 with the kernels' normal
+ * limit (seconds).  CTA 0 gives up and flags the device error word; CTA 1
+ * must then return early.  elapsed_ns: device memory for 2 values, each CTA's
+ * time until it gave up.  Afterwards tb_device_error reports the timeout bit
+ * and the context stays usable. */
+TB_API int tb_selftest_bounded_wait(tb_ctx* ctx, int limit_us, unsigned long long* elapsed_ns);
 
 /* -------------------------------------------------------------- norms --- */
 /* rms_norm_forward (kernels/teeny-kernels/src/nn/norm/rmsnorm.rs:40-122):
@@ -122,7 +130,8 @@ TB_API int tb_dequantize_int8(tb_ctx* ctx, const int8_t* q, const float* scale, 
                        int64_t K);
 /* int8 weight-only linear (the op graph/mod.rs:2595-2600 leaves as TODO):
  * y[M, N] = scale[n] * x[M, K](bf16) * q[N, K]^T (+ residual), bf16 out unless
- * TB_EPI_OUT_F32.  Tensor cores (int8 dequantised to bf16 in shared memory). */
+ * TB_EPI_OUT_F32.  Tensor cores: the int8 weights are converted exactly to
+ * bf16 straight into tensor memory, which the MMA reads as its A operand. */
 TB_API int tb_int8_linear_fwd(tb_ctx* ctx, const void* x, const int8_t* q, const float* scale,
                        const void* residual, void* y, int64_t M, int64_t N, int64_t K, int flags);
 
@@ -256,6 +265,10 @@ TB_API int tb_decoder_generate(tb_decoder* dec, const int32_t* prompt_ids, int B
 /* Decode-only workloads: fill the KV cache of B sequences with len positions
  * of N(0, 1) keys/values and set the current tokens (device int32 [B]). */
 TB_API int tb_decoder_fill_kv_random(tb_decoder* dec, int B, int len, uint64_t seed, const int32_t* ids);
+/* Copies cache positions [0, len) of the first B sequences of one layer into
+ * device bf16 buffers k_out / v_out [B, n_kv_heads, len, head_dim]
+ * (stream-ordered).  Inspection / session save; the reference has no KV cache. */
+TB_API int tb_decoder_read_kv(tb_decoder* dec, int layer, int B, int len, void* k_out, void* v_out);
 /* Tokens currently in the KV cache per sequence. */
 TB_API int tb_decoder_seq_len(tb_decoder* dec, int* len);
 

@@ -259,14 +259,22 @@ def quantize_int8_numpy(w):
     cross-check the C oracle.  Rounding is half away from zero, written as
     sign(t) * floor(|t| + 0.5) -- NOT np.round, which rounds half to even."""
     w = np.asarray(w, dtype=np.float32)
-    lo = np.minimum(w.min(axis=1), np.float32(0))
-    hi = np.maximum(w.max(axis=1), np.float32(0))
-    amax = np.maximum(np.abs(lo), np.abs(hi)).astype(np.float32)
-    scale = np.where(amax == 0, np.float32(1), amax / np.float32(127)).astype(np.float32)
-    t = (w / scale[:, None]).astype(np.float32)
-    # |t| + 0.5 in float64 is exact for any float32 t (no double rounding at
-    # the 0.49999997 boundary).
-    td = t.astype(np.float64)
-    r = np.sign(td) * np.floor(np.abs(td) + 0.5)
+    with np.errstate(invalid="ignore", divide="ignore"):
+        # `x < vmin` / `x > vmax` skip NaN (fmin / fmax do too); an all-NaN row
+        # keeps the +Inf / -Inf start values
+        vmin = np.fmin.reduce(w, axis=1, initial=np.inf)
+        vmax = np.fmax.reduce(w, axis=1, initial=-np.inf)
+        fin = np.isfinite(vmin)
+        lo = np.where(fin, np.minimum(vmin, np.float32(0)), np.float32(0)).astype(np.float32)
+        hi = np.where(fin, np.maximum(vmax, np.float32(0)), np.float32(0)).astype(np.float32)
+        amax = np.maximum(np.abs(lo), np.abs(hi)).astype(np.float32)
+        scale = np.where(amax == 0, np.float32(1), amax / np.float32(127)).astype(np.float32)
+        t = (w / scale[:, None]).astype(np.float32)
+        # |t| + 0.5 in float64 is exact for any float32 t (no double rounding at
+        # the 0.49999997 boundary).
+        td = t.astype(np.float64)
+        r = np.sign(td) * np.floor(np.abs(td) + 0.5)
+        # `as i32` saturates (NaN -> 0) before the clamp to [-127, 127]
+        r = np.where(np.isnan(r), 0.0, r)
     q = np.clip(r, -127, 127).astype(np.int8)
     return q, scale

@@ -309,8 +309,11 @@ void or_batchnorm_inference(const float* x, const float* gamma, const float* bet
  *   qrange = [-127, 127] (:47-51)
  *   lo = min(min(row), 0), hi = max(max(row), 0); amax = max(|lo|, |hi|)
  *   scale = amax == 0 ? 1 : amax / 127            (f32 arithmetic, :112)
- *   q = clamp(round(x / scale), -127, 127)        (:138-139)
- * Rust f32::round rounds half away from zero; C roundf does the same. */
+ *   q = clamp(round(x / scale) as i32, -127, 127) (:138-139)
+ * Rust f32::round rounds half away from zero; C roundf does the same.
+ * Non-finite weights follow Rust: NaN is skipped by the min/max pass (its
+ * comparisons are false), a row holding -Inf has a non-finite minimum and
+ * gets scale 1, a row holding +Inf gets scale Inf; NaN / scale -> 0. */
 void or_quantize_int8(const float* w, int8_t* q, float* scale, int64_t N, int64_t K) {
 #pragma omp parallel for schedule(static)
     for (int64_t n = 0; n < N; n++) {
@@ -329,11 +332,15 @@ void or_quantize_int8(const float* w, int8_t* q, float* scale, int64_t N, int64_
         float s = (amax == 0.0f) ? 1.0f : amax / 127.0f;
         scale[n] = s;
         for (int64_t k = 0; k < K; k++) {
+            /* `(t.round()) as i32` saturates in Rust: NaN -> 0, beyond the
+             * i32 range -> i32::MIN / MAX; clamp(-127, 127) follows (:138-139) */
             float t = wr[k] / s;
-            float r = roundf(t);
-            int v = (int)r;
-            if (v < -127) v = -127;
-            if (v > 127) v = 127;
+            int v;
+            if (t != t) v = 0;
+            else {
+                float r = roundf(t);
+                v = r <= -127.0f ? -127 : (r >= 127.0f ? 127 : (int)r);
+            }
             q[n * K + k] = (int8_t)v;
         }
     }

@@ -25,8 +25,9 @@ __device__ __forceinline__ float ld_as_f32(const __nv_bfloat16* p) { return __bf
 
 // Grid (M, chunks).  Each CTA reduces its slice of the row to (value, index)
 // (greater value wins, equal values keep the lower index, NaN is skipped),
-// folds it into the row's key with atomicMax (key = order-preserving bits of
-// the value << 32 | ~index), and the last CTA of the row writes out[row].
+// folds it into the row's key with atomicMax (argmax_key: order-preserving
+// bits of the value << 32 | ~index, -0.0 keyed as +0.0), and the last CTA of
+// the row writes out[row].
 template <typename T>
 __global__ void argmax_noalloc_kernel(const T* __restrict__ x, int32_t* __restrict__ out, int64_t N, int chunk,
                                       unsigned long long* scratch) {
@@ -71,11 +72,7 @@ __global__ void argmax_noalloc_kernel(const T* __restrict__ x, int32_t* __restri
                 bi = si[w];
             }
         }
-        if (bi >= 0) {
-            const uint32_t u = __float_as_uint(bv);
-            const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-            atomicMax(key, ((unsigned long long)ord << 32) | (unsigned long long)(~(uint32_t)bi));
-        }
+        if (bi >= 0) atomicMax(key, argmax_key(bv, bi));
         __threadfence();
         s_last = atomicAdd(cnt, 1u) == gridDim.y - 1;
     }
@@ -83,7 +80,7 @@ __global__ void argmax_noalloc_kernel(const T* __restrict__ x, int32_t* __restri
     if (threadIdx.x == 0 && s_last) {
         __threadfence();
         const unsigned long long k = atomicExch(key, 0ull);
-        out[row] = k ? (int32_t)(~(uint32_t)(k & 0xffffffffull)) : 0;
+        out[row] = k ? argmax_key_index(k) : 0;
         *cnt = 0u;
     }
 }
@@ -127,11 +124,15 @@ extern "C" int tb_argmax_noalloc_fwd(tb_ctx* ctx, int dtype, const void* x, int3
     if (rc) return rc;
     // the rows this call uses start from zero, whatever an earlier (possibly failed) call left
     TB_CUDA_TRY(ctx, cudaMemsetAsync(scratch, 0, (size_t)M * 16, ctx->stream));
-    const int chunk = 2048;
+    // 2048 columns per CTA, widened for rows so long that the chunk count
+    // would pass the 65535 limit of gridDim.y
+    int64_t chunk = 2048;
+    if ((N + chunk - 1) / chunk > 65535) chunk = (N + 65534) / 65535;
     const dim3 grid((unsigned)M, (unsigned)((N + chunk - 1) / chunk));
     if (dtype == TB_F32)
-        argmax_noalloc_kernel<float><<<grid, 256, 0, ctx->stream>>>((const float*)x, out, N, chunk, scratch);
+        argmax_noalloc_kernel<float><<<grid, 256, 0, ctx->stream>>>((const float*)x, out, N, (int)chunk, scratch);
     else
-        argmax_noalloc_kernel<__nv_bfloat16><<<grid, 256, 0, ctx->stream>>>((const __nv_bfloat16*)x, out, N, chunk, scratch);
+        argmax_noalloc_kernel<__nv_bfloat16><<<grid, 256, 0, ctx->stream>>>((const __nv_bfloat16*)x, out, N, (int)chunk,
+                                                                        scratch);
     return check_launch(ctx, "argmax_noalloc");
 }

@@ -1,13 +1,17 @@
 // Attention forward on B200.
 //
 //  * attn_tc_kernel<D>: flash-style forward for bf16 Q/K/V, D in {64, 128}.
-//    One CTA per (128-query tile, head, batch).  Warp 0 streams K and V tiles
-//    of 128 keys with TMA (two-stage ring), warp 1 issues tcgen05.mma:
-//    S = Q K^T into one of two TMEM score buffers, then O += P V into a TMEM
-//    accumulator.  Warps 2-5 own one query row per thread: they read the row
-//    of S from TMEM, run the online softmax in the exp2 domain, rescale O in
-//    TMEM when the running max grows, and write P (bf16) into a 128-B
-//    swizzled shared-memory tile that the next MMA reads as its A operand.
+//    Each CTA takes two 128-query tiles of one (head, batch) in turn (a heavy
+//    and a light one when causal).  Warps 0 and 3 stream K and V tiles of 128
+//    keys with TMA (two-stage rings; warp 0 also loads Q), warp 1 issues
+//    S = Q K^T into one of two TMEM score buffers, warp 2 issues O += P V, so
+//    neither MMA stream queues behind the other.  Eight softmax warps, two
+//    per TMEM lane quarter, each take 64 of a tile's 128 keys for their rows
+//    with their own running max, row sum and TMEM O accumulator (merged once
+//    at the end): they read S from TMEM, run the online softmax in the exp2
+//    domain, rescale O in TMEM only when the max passes the reference by 2^8,
+//    and write P (bf16) into a double-buffered 128-B swizzled shared tile that
+//    the P.V MMA reads as its A operand.
 //    The same online-softmax recurrence as flash_attention2_forward
 //    (nn/attention/flash_attn2.rs:98-140), over 128-key tiles instead of one
 //    key at a time, plus the causal mask and GQA head mapping.

@@ -75,9 +75,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Bounded wait for the phase with the given parity to complete.  Returns false
-// (and records `code` in *err) after kWaitLimitNs, or early if *err is already
+// (and records `code` in *err) after limit_ns, or early if *err is already
 // non-zero because another CTA gave up.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err, int code) {
+__device__ __forceinline__ bool mbar_wait_ns(uint32_t bar, uint32_t parity, int* err, int code,
+                                             unsigned long long limit_ns) {
     if (mbar_try_wait(bar, parity)) return true;
     unsigned long long t0 = globaltimer();
     uint32_t spins = 0;
@@ -85,12 +86,16 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* er
         if (mbar_try_wait(bar, parity)) return true;
         if ((++spins & 255u) == 0) {
             if (*(volatile int*)err != 0) return false;
-            if (globaltimer() - t0 > kWaitLimitNs) {
+            if (globaltimer() - t0 > limit_ns) {
                 atomicOr(err, code);
                 return false;
             }
         }
     }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err, int code) {
+    return mbar_wait_ns(bar, parity, err, code, kWaitLimitNs);
 }
 
 // -------------------------------------------------------------------- TMA --
@@ -334,5 +339,16 @@ __device__ __forceinline__ float bf16_lo(uint32_t v) { return __uint_as_float(v 
 __device__ __forceinline__ float bf16_hi(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
+
+// 64-bit key of a (value, index) candidate of a split-row argmax: atomicMax
+// over keys keeps the greater value and, for equal values, the lower index.
+// The value bits are mapped to an order-preserving unsigned (sign flips the
+// rest); -0.0 maps like +0.0, since the two compare equal.
+__device__ __forceinline__ unsigned long long argmax_key(float v, int i) {
+    const uint32_t u = v == 0.f ? 0u : __float_as_uint(v);
+    const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return ((unsigned long long)ord << 32) | (unsigned long long)(~(uint32_t)i);
+}
+__device__ __forceinline__ int argmax_key_index(unsigned long long k) { return (int)(~(uint32_t)(k & 0xffffffffull)); }
 
 }  // namespace tb

@@ -240,11 +240,7 @@ __global__ void argmax_step_kernel(const float* __restrict__ logits, int V, int 
     __syncthreads();
     if (threadIdx.x == 0) {
         for (int w = 1; w < (int)(blockDim.x / 32); w++) amax_merge2(bv, bi, sv[w], si[w]);
-        if (bi >= 0) {
-            uint32_t u = __float_as_uint(bv);
-            uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-            atomicMax(&keys[row], ((unsigned long long)ord << 32) | (unsigned long long)(~(uint32_t)bi));
-        }
+        if (bi >= 0) atomicMax(&keys[row], argmax_key(bv, bi));
         __threadfence();
         s_last = atomicAdd(&cnt[row], 1u) == gridDim.y - 1;
     }
@@ -252,7 +248,7 @@ __global__ void argmax_step_kernel(const float* __restrict__ logits, int V, int 
     if (threadIdx.x == 0 && s_last) {
         __threadfence();
         unsigned long long k = atomicExch(&keys[row], 0ull);
-        int id = k ? (int)(~(uint32_t)(k & 0xffffffffull)) : 0;
+        int id = k ? argmax_key_index(k) : 0;
         cur_ids[row] = id;
         int step = state[1];
         if (step < max_gen) out_ids[(int64_t)row * max_gen + step] = id;
@@ -808,6 +804,22 @@ int tb_decoder_fill_kv_random(tb_decoder* d, int B, int len, uint64_t seed, cons
     d->host_len = len;
     d->host_step = 0;
     return check_launch(ctx, "fill_kv_random");
+}
+
+int tb_decoder_read_kv(tb_decoder* d, int layer, int B, int len, void* k_out, void* v_out) {
+    if (!d || !k_out || !v_out) return TB_ERR_ARG;
+    tb_ctx* ctx = d->ctx;
+    const tb_decoder_config& c = d->cfg;
+    TB_REQUIRE(ctx, layer >= 0 && layer < c.n_layers && B > 0 && B <= c.max_batch && len > 0 && len <= c.max_seq,
+               TB_ERR_SHAPE, "read_kv: layer %d, B %d, len %d", layer, B, len);
+    // cache rows [b][kv head][max_seq][hd] -> [b][kv head][len][hd]
+    const size_t row = (size_t)len * c.head_dim * sizeof(bf16), pitch = (size_t)c.max_seq * c.head_dim * sizeof(bf16);
+    const int64_t off = (int64_t)layer * d->cache_layer_elems;
+    TB_CUDA_TRY(ctx, cudaMemcpy2DAsync(k_out, row, d->kcache + off, pitch, row, (size_t)B * c.n_kv_heads,
+                                       cudaMemcpyDeviceToDevice, ctx->stream));
+    TB_CUDA_TRY(ctx, cudaMemcpy2DAsync(v_out, row, d->vcache + off, pitch, row, (size_t)B * c.n_kv_heads,
+                                       cudaMemcpyDeviceToDevice, ctx->stream));
+    return TB_OK;
 }
 
 int tb_decoder_seq_len(tb_decoder* d, int* len) {

@@ -207,6 +207,8 @@ __global__ void ew_kernel(const T* __restrict__ a, const T* __restrict__ b, T* _
 // amax == 0 ? 1 : amax / 127 in IEEE f32 (:103-112); pass 2: q = clamp(
 // roundf(x / scale), -127, 127) (:135-143).  roundf rounds half away from zero
 // like Rust's f32::round; `/` is IEEE division (no fast-math in this build).
+// Rust's `as i32` saturates and sends NaN to 0, so NaN / scale (and Inf / Inf
+// when a row holds +Inf) quantises to 0 and +-Inf / finite to +-127.
 template <typename T>
 __global__ void quantize_int8_kernel(const T* __restrict__ w, int8_t* __restrict__ q,
                                      float* __restrict__ scale, int64_t K) {
@@ -250,9 +252,8 @@ __global__ void quantize_int8_kernel(const T* __restrict__ w, int8_t* __restrict
     __syncthreads();
     float s = s_scale;
     for (int64_t k = threadIdx.x; k < K; k += blockDim.x) {
-        float t = __fdiv_rn(to_f(wr[k]), s);
-        float r = roundf(t);
-        r = fminf(fmaxf(r, -127.f), 127.f);
+        const float t = __fdiv_rn(to_f(wr[k]), s);
+        const float r = t != t ? 0.f : fminf(fmaxf(roundf(t), -127.f), 127.f);
         q[n * K + k] = (int8_t)(int)r;
     }
 }

@@ -9,9 +9,9 @@
 //    are the MMA's M dimension (two 128-row halves per CTA), the tokens its N.
 //    K is split across the CTAs of a thread-block cluster (up to 16), which
 //    exchange their partials over DSMEM; each CTA finishes a slice of the
-//    rows.  Weights are bf16, or int8 converted to bf16 in shared memory by
-//    six converter warps (exact: |q| <= 127).  An RMSNorm of the activations
-//    can be fused in front.
+//    rows.  Weights are bf16, or int8 converted exactly (|q| <= 127) to bf16
+//    straight into TMEM by eight converter warps, the MMA taking its A operand
+//    from TMEM.  An RMSNorm of the activations can be fused in front.
 //  * linear_f32_kernel / matmul_f32_kernel: exact-f32 CUDA-core tiles for the
 //    fp32 configurations (the reference's TF32 dot, linear.rs:86, misses the
 //    1e-4 fp32 tolerance at K >= 256).

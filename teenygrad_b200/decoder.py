@@ -156,6 +156,20 @@ class Decoder:
                                                         ctypes.c_uint64(seed), ctypes.c_void_p(ids.data_ptr())))
         self.B = ids.numel()
 
+    def read_kv(self, layer: int, batch: int, length: int):
+        """Copies of the cached keys and values of `layer`: bf16 [batch, n_kv_heads,
+        length, head_dim] each (positions [0, length) of the first `batch` sequences)."""
+        c = self.cfg
+        dev = torch.device("cuda", self.device)
+        k = torch.empty(batch, c.n_kv_heads, length, c.head_dim, device=dev, dtype=torch.bfloat16)
+        v = torch.empty_like(k)
+        self._ctx()
+        check(self.ctx, lib().tb_decoder_read_kv(self._h, ctypes.c_int(layer), ctypes.c_int(batch),
+                                                 ctypes.c_int(length), ctypes.c_void_p(k.data_ptr()),
+                                                 ctypes.c_void_p(v.data_ptr())))
+        torch.cuda.current_stream(dev).synchronize()
+        return k, v
+
     def seq_len(self) -> int:
         n = ctypes.c_int(0)
         check(self.ctx, lib().tb_decoder_seq_len(self._h, ctypes.byref(n)))

@@ -116,6 +116,70 @@ def test_decoder_wide_split_k(int8):
     no_device_error()
 
 
+def _oracle_with_cache(dec, cfg, p, B, length, int8):
+    """Oracle decoder whose KV cache holds the executor's cache contents."""
+    ora = OracleDecoder(cfg, p, int8=int8)
+    ks, vs = [], []
+    for l in range(cfg.n_layers):
+        k, v = dec.read_kv(l, B, length)
+        ks.append(k.float().cpu().numpy())
+        vs.append(v.float().cpu().numpy())
+    ora.k, ora.v, ora.len = np.stack(ks), np.stack(vs), length
+    return ora
+
+
+# The benchmarked model width (C4 / C5: d 2048, 32 / 8 heads x 64, SwiGLU 8192,
+# vocab 32000) with 2 of its 16 layers, so every GEMV runs the benchmark's
+# configuration: 16-CTA split-K clusters, fused RMSNorm, the RoPE / KV-cache
+# epilogue, the 16-chunk argmax over 32000 logits.
+C4_WIDTH = dict(n_layers=2, d_model=2048, n_heads=32, n_kv_heads=8, head_dim=64, ffn_hidden=8192, vocab=32000)
+
+
+def test_decoder_c4_width_bf16():
+    # prefill: 16 sequences x 16 tokens (256 rows: the tensor-core GEMM path and
+    # prefill attention); then decode at batch 16 (the benchmark's decode GEMVs)
+    dev()
+    cfg = SmallCfg(**C4_WIDTH)
+    p = random_params(cfg, seed=12)
+    dec = make(cfg, max_batch=16, max_seq=64)
+    upload(dec, p)
+    ora = OracleDecoder(cfg, p)
+    ids = np.random.default_rng(13).integers(0, cfg.vocab, (16, 16)).astype(np.int32)
+    nxt, logits = dec.prefill(torch.from_numpy(ids).cuda(), return_logits=True)
+    ref = ora.forward(ids)
+    assert_close(np_of(logits), ref, BF16_TOL, "prefill logits")
+    check_tokens(nxt.cpu().numpy(), ref)
+    for step in range(2):
+        tok = np.argmax(ref, axis=1).astype(np.int32)
+        nxt, logits = dec.decode_step(torch.from_numpy(tok).cuda(), return_logits=True)
+        ref = ora.forward(tok[:, None])
+        assert_close(np_of(logits), ref, BF16_TOL, f"decode step {step}")
+        check_tokens(nxt.cpu().numpy(), ref)
+    no_device_error()
+
+
+def test_decoder_c5_width_int8_decode():
+    # C5: int8 weights, decode-only batch 64 over a 2048-position cache of N(0, 1)
+    # keys / values; the oracle is given the same cache contents
+    dev()
+    cfg = SmallCfg(**C4_WIDTH)
+    p = random_params(cfg, seed=14)
+    B, L = 64, 2048
+    dec = make(cfg, int8=True, max_batch=B, max_seq=L + 8)
+    upload(dec, p)
+    tok = np.random.default_rng(15).integers(0, cfg.vocab, B).astype(np.int32)
+    dec.fill_kv_random(torch.from_numpy(tok).cuda(), L, seed=16)
+    ora = _oracle_with_cache(dec, cfg, p, B, L, int8=True)
+    for step in range(2):
+        nxt, logits = dec.decode_step(torch.from_numpy(tok).cuda(), return_logits=True)
+        ref = ora.forward(tok[:, None])
+        assert_close(np_of(logits), ref, BF16_TOL, f"int8 decode step {step}")
+        check_tokens(nxt.cpu().numpy(), ref)
+        tok = np.argmax(ref, axis=1).astype(np.int32)
+    assert dec.seq_len() == L + 2
+    no_device_error()
+
+
 def test_decoder_fill_kv_random_decode_only():
     dev()
     cfg = SmallCfg()

@@ -172,10 +172,22 @@ def test_quantize_int8_bit_exact():
     w[0] = 0.0
     w[1, :5] = [0.5, -0.5, 1.5, -2.5, 127.0]
     w[2, 0] = -0.0
+    # non-finite weights follow Rust's saturating `as i32` (affine.rs:101-139):
+    # NaN -> 0; a row with -Inf gets scale 1; a row with +Inf gets scale Inf
+    w[3, 7] = np.nan
+    w[4, 2] = -np.inf
+    w[5, 3] = np.inf
+    w[6, 1:3] = [np.inf, np.nan]
+    w[7, :] = np.nan
+    w[8, 0] = 1e30
     q, s = ops().quantize_int8(to_gpu(w))
     qo, so = oracle.quantize_int8(w)
     np.testing.assert_array_equal(q.cpu().numpy(), qo)
     np.testing.assert_array_equal(s.cpu().numpy(), so)
+    qn, sn = oracle.quantize_int8_numpy(w)
+    np.testing.assert_array_equal(qo, qn)
+    assert qo[3, 7] == 0 and so[4] == 1.0 and qo[4, 2] == -127 and np.isinf(so[5]) and qo[5, 3] == 0
+    assert not qo[7].any() and so[7] == 1.0
     deq = ops().dequantize_int8(q, s)
     np.testing.assert_array_equal(deq.cpu().numpy(), oracle.dequantize_int8(qo, so))
     # bf16 weights (upcast exactly)
@@ -266,6 +278,22 @@ def test_attention_bf16_tc(B, Hq, Hkv, Sq, Sk, D, causal):
     sc = 1.0 / math.sqrt(D)
     o, lse = ops().attention(*(to_gpu(a, torch.bfloat16) for a in (q, k, v)), scale=sc, causal=causal, return_lse=True)
     ro, rl = oracle.attention(q, k, v, sc, causal)
+    assert_close(np_of(o), ro, BF16_TOL, "O")
+    assert_close(np_of(lse), rl, 1e-3, "LSE")
+
+
+# The benchmarked shapes: a slice of C3 (causal prefill, S 4096, D 128, 2 of its
+# 256 (batch, head) pairs) and C4 prefill (GQA 32 / 8 heads, D 64, S 1024, 2 of
+# its 16 sequences), each with O and LSE against the oracle.
+@pytest.mark.parametrize("B,Hq,Hkv,S,D", [(1, 2, 2, 4096, 128), (2, 32, 8, 1024, 64)])
+def test_attention_bf16_benchmark_shapes(B, Hq, Hkv, S, D):
+    r = rng(S + D)
+    q = bf16_round(r.standard_normal((B, Hq, S, D)))
+    k = bf16_round(r.standard_normal((B, Hkv, S, D)))
+    v = bf16_round(r.standard_normal((B, Hkv, S, D)))
+    sc = 1.0 / math.sqrt(D)
+    o, lse = ops().attention(*(to_gpu(a, torch.bfloat16) for a in (q, k, v)), scale=sc, causal=True, return_lse=True)
+    ro, rl = oracle.attention(q, k, v, sc, True)
     assert_close(np_of(o), ro, BF16_TOL, "O")
     assert_close(np_of(lse), rl, 1e-3, "LSE")
 

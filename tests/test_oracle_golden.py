@@ -140,6 +140,30 @@ def test_quantize_int8_c_vs_numpy():
     assert np.all(np.abs(deq - w) <= s[:, None] * 0.5 + 1e-12)
 
 
+def test_quantize_int8_non_finite():
+    # Rust semantics (affine.rs:91-139): NaN fails every comparison, so the
+    # min/max pass skips it; a row holding -Inf has a non-finite minimum and
+    # gets scale 1; a row holding +Inf gets scale Inf; `round() as i32`
+    # saturates (NaN -> 0, +-Inf -> i32 limits) before the clamp.
+    w = np.full((6, 5), 0.25, np.float32)
+    w[0, 1] = np.nan
+    w[1, 2] = -np.inf
+    w[2, 3] = np.inf
+    w[3, :] = np.nan
+    w[4, 0], w[4, 1] = np.inf, np.nan
+    w[5, 0] = 3e38
+    q, s = oracle.quantize_int8(w)
+    qn, sn = oracle.quantize_int8_numpy(w)
+    np.testing.assert_array_equal(q, qn)
+    np.testing.assert_array_equal(s, sn)
+    assert q[0].tolist() == [127, 0, 127, 127, 127]
+    assert s[1] == 1.0 and q[1].tolist() == [0, 0, -127, 0, 0]
+    assert np.isinf(s[2]) and q[2].tolist() == [0, 0, 0, 0, 0]
+    assert s[3] == 1.0 and not q[3].any()
+    assert np.isinf(s[4]) and q[4].tolist() == [0, 0, 0, 0, 0]
+    assert q[5, 0] == 127 and q[5, 1] == 0
+
+
 def test_quantize_half_away_from_zero():
     # amax = 2.54 -> scale = 0.02; 0.01/0.02 = 0.5 exactly representable? use
     # a scale of 1 row (amax = 127) so x/scale = x and ties are exact.

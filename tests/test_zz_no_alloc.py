@@ -14,7 +14,8 @@ import ctypes
 import numpy as np
 import pytest
 
-from gpu_util import dev, torch
+import oracle
+from gpu_util import bf16_round, dev, torch
 
 pytestmark = pytest.mark.gpu
 
@@ -37,6 +38,14 @@ def test_argmax_noalloc_matches_argmax_twice():
         logits[0, [5, 4000]] = 40.0          # tie across two blocks: lower index wins
         logits[1, :] = -np.inf
         logits[2, 17] = np.nan
+        logits[3, :] = -1.0                  # maximum 0: -0.0 in the first block, +0.0 in a later one
+        logits[3, 5] = -0.0
+        logits[3, 4000] = 0.0
+        logits[4, :] = -2.0                  # +0.0 first, -0.0 later
+        logits[4, 9] = 0.0
+        logits[4, 4090] = -0.0
+        if dtype == TB_BF16:
+            logits = bf16_round(logits)
         x = torch.from_numpy(logits).cuda()
         if dtype == TB_BF16:
             x = x.bfloat16()
@@ -46,7 +55,8 @@ def test_argmax_noalloc_matches_argmax_twice():
         _lib.check(ctx, _call(lib.tb_argmax_noalloc_fwd, ctx, dtype, x, got, M, N))
         torch.cuda.synchronize()
         assert torch.equal(got, ref), f"call {call}"
-        assert int(got[0]) == 5
+        np.testing.assert_array_equal(got.cpu().numpy(), oracle.argmax(logits), err_msg=f"call {call}")
+        assert int(got[0]) == 5 and int(got[3]) == 5 and int(got[4]) == 9
 
 
 def test_argmax_noalloc_rejects_too_many_rows():
