@@ -146,6 +146,14 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* m, 
         : "memory");
 }
 
+// Untiled bulk copy global -> this CTA's shared memory, completing on an
+// mbarrier (addresses 16-B aligned, size a multiple of 16).
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+
 // ---------------------------------------------------------------- tcgen05 --
 // TMEM allocation: one full warp executes these.  The base address is written
 // to shared memory at `slot`.

@@ -259,11 +259,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 // partials of row pairs [r*128/CS, (r+1)*128/CS) from its peers by DSMEM bulk
 // copies, sums them in rank order (deterministic) and runs the epilogue.
 //
-// Fused RMSNorm (Epi::norm_w set): the converter warps build each activation
-// tile from the raw rows, bf16(x * w), and accumulate each token's sum of
-// squares over the CTA's K range.  1/rms is a per-token factor of every
-// output, so it is applied in the epilogue once the cluster's partial sums
-// are added.
+// Fused RMSNorm (Epi::norm_w set): the raw activation rows and the norm
+// gains arrive through the ring with the weights (TMA / bulk copies); the
+// converter warps turn each activation tile into bf16(x * w) in place and
+// accumulate each token's sum of squares over the CTA's K range.  1/rms is a
+// per-token factor of every output, so it is applied in the epilogue once the
+// cluster's partial sums are added.
 //
 // bf16 weights: 288 threads; warp 0 TMA, warps 1 and 8 issue the MMAs of one
 // 128-row half each (A and B from shared memory), warps 2-7 build normalised
@@ -276,17 +277,23 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 // per-block synchronisation is spread over twice the bytes of a 64-wide one.  Shared-memory traffic per K block is then the TMA
 // writes, one read of the int8 tile and the MMAs' reads of the activations
 // (no bf16 weight tile written and read back through shared memory).
-template <int NT, int STAGES, bool INT8>
+// MINB: CTAs per SM the kernel is compiled for (registers); the grid is sized
+// to the resident CTA slots that shared memory and MINB allow.
+template <int NT, int STAGES, bool INT8, int MINB>
 struct GemvCfg {
     static constexpr int KB = INT8 ? 128 : 64;      // K per block
     static constexpr int RC = KB / 8;               // 16-B activation chunks per token row per block
     static constexpr int W_BYTES = 256 * 128;       // [256 rows][128 B], 128-B swizzle (bf16 64 K, int8 128 K)
     static constexpr int X_ATOM = NT * 128;         // [NT][64] bf16, one 128-B swizzle atom wide
     static constexpr int X_BYTES = (KB / 64) * X_ATOM;
+    static constexpr int G_BYTES = KB * 2;          // fused norm: the gains of the K block (bf16)
     // received partials (reuse the rings): CS slots of NT * 256 / CS values + NT sums of squares
     static constexpr int RED_BYTES = (NT * 256 + 16 * NT) * 4;
-    static constexpr int RING = STAGES * (W_BYTES + X_BYTES);
-    static constexpr int SMEM = (RING > RED_BYTES ? RING : RED_BYTES) + 1024 + 512;
+    static constexpr int RING = STAGES * (W_BYTES + X_BYTES + G_BYTES);
+    static constexpr int BAR_OFF = RING > RED_BYTES ? RING : RED_BYTES;
+    static constexpr int SMEM = BAR_OFF + 1024 + 512;
+    static constexpr int SLOTS_SMEM = (227 * 1024 + 1024) / (SMEM + 1024);   // per SM, shared memory
+    static constexpr int PER_SM = SLOTS_SMEM < MINB ? SLOTS_SMEM : MINB;
     // TMEM: accumulators [half][NT] from column 0; int8: converted A tiles
     // [2 buffers][2 halves][64 columns] from column A_COL
     static constexpr int A_COL = 128;               // int8: [2 buffers][2 halves][KB / 2 columns]
@@ -302,17 +309,18 @@ struct GemvCfg {
     static_assert(!INT8 || SMEM > 114 * 1024, "int8 GEMV CTAs must not share an SM with another TMEM user");
 };
 
-template <int NT, int STAGES, bool INT8>
-__global__ void __launch_bounds__(GemvCfg<NT, STAGES, INT8>::THREADS, 1)
+template <int NT, int STAGES, bool INT8, int MINB>
+__global__ void __launch_bounds__(GemvCfg<NT, STAGES, INT8, MINB>::THREADS, MINB)
 gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                Epi ep, int Nw, int K, int Mtok, int kb_per_split, int* err) {
-    using C = GemvCfg<NT, STAGES, INT8>;
+    using C = GemvCfg<NT, STAGES, INT8, MINB>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_align1024(smem_raw);
     uint8_t* sW = smem;
     uint8_t* sX = sW + STAGES * C::W_BYTES;
-    float* red = reinterpret_cast<float*>(smem);          // [NT][256] partials, after the MMAs
-    constexpr int BAR_OFF = (C::RING > C::RED_BYTES ? C::RING : C::RED_BYTES);
+    uint8_t* sG = sX + STAGES * C::X_BYTES;                      // fused norm: [STAGES][KB] gains
+    float* red = reinterpret_cast<float*>(smem);   // [NT][256] received partials, after the MMAs
+    constexpr int BAR_OFF = C::BAR_OFF;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + BAR_OFF);
     const uint32_t full0 = smem_u32(bars);
     const uint32_t empty0 = smem_u32(bars + STAGES);
@@ -358,30 +366,32 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
     if (warp == 0 && lane == 0) {
         tma_prefetch_desc(&tmW);
         tma_prefetch_desc(&tmX);
-        // Weights do not depend on the previous kernel: start streaming the
-        // first STAGES K-blocks before waiting for it, then fetch activations.
-        // With the norm fused the converter warps write the activation tiles.
-        const uint32_t tx_bytes = C::W_BYTES + (NORM ? 0 : C::X_BYTES);
+        // Weights (and the fused norm's gains) do not depend on the previous
+        // kernel: start streaming the first STAGES K-blocks before waiting for
+        // it, then fetch the activations.  Gains: the K block's bytes inside K
+        // (a multiple of 16, K % 8 == 0).
+        auto g_bytes = [&](int i) { return (uint32_t)(2 * min(KB, K - (kb0 + i) * KB)); };
+        const __nv_bfloat16* gains = reinterpret_cast<const __nv_bfloat16*>(ep.norm_w);
         const int pre = nk < STAGES ? nk : STAGES;
         for (int i = 0; i < pre; i++) {
-            mbar_expect_tx(full0 + 8 * i, tx_bytes);
+            mbar_expect_tx(full0 + 8 * i, C::W_BYTES + C::X_BYTES + (NORM ? g_bytes(i) : 0));
             tma_load_2d(smem_u32(sW + i * C::W_BYTES), &tmW, full0 + 8 * i, (kb0 + i) * KB, tile * 256);
+            if (NORM) bulk_load(smem_u32(sG + i * C::G_BYTES), gains + (kb0 + i) * KB, g_bytes(i), full0 + 8 * i);
         }
         pdl_wait();
-        if (!NORM)
-            for (int i = 0; i < pre; i++)
-                for (int a = 0; a < KB / 64; a++)
-                    tma_load_2d(smem_u32(sX + i * C::X_BYTES + a * C::X_ATOM), &tmX, full0 + 8 * i, (kb0 + i) * KB + 64 * a, 0);
+        for (int i = 0; i < pre; i++)
+            for (int a = 0; a < KB / 64; a++)
+                tma_load_2d(smem_u32(sX + i * C::X_BYTES + a * C::X_ATOM), &tmX, full0 + 8 * i, (kb0 + i) * KB + 64 * a, 0);
         int issued = pre;
         for (int i = pre; i < nk; i++) {
             int s = i % STAGES;
             if (!mbar_wait(empty0 + 8 * s, ((i / STAGES) - 1) & 1, err, DEV_ERR_TIMEOUT_EMPTY)) break;
-            mbar_expect_tx(full0 + 8 * s, tx_bytes);
+            mbar_expect_tx(full0 + 8 * s, C::W_BYTES + C::X_BYTES + (NORM ? g_bytes(i) : 0));
             int kcoord = (kb0 + i) * KB;
             tma_load_2d(smem_u32(sW + s * C::W_BYTES), &tmW, full0 + 8 * s, kcoord, tile * 256);
-            if (!NORM)
-                for (int a = 0; a < KB / 64; a++)
-                    tma_load_2d(smem_u32(sX + s * C::X_BYTES + a * C::X_ATOM), &tmX, full0 + 8 * s, kcoord + 64 * a, 0);
+            if (NORM) bulk_load(smem_u32(sG + s * C::G_BYTES), gains + kcoord, g_bytes(i), full0 + 8 * s);
+            for (int a = 0; a < KB / 64; a++)
+                tma_load_2d(smem_u32(sX + s * C::X_BYTES + a * C::X_ATOM), &tmX, full0 + 8 * s, kcoord + 64 * a, 0);
             issued = i + 1;
         }
         for (int i = (issued > STAGES ? issued - STAGES : 0); i < issued; i++)
@@ -428,50 +438,34 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
         const int ct = threadIdx.x - 32 * C::CONV_W0;       // 0 .. CT - 1
         constexpr int RC = C::RC;
         constexpr int XI = (NT * RC + CT - 1) / CT;         // 16-B activation chunks per thread per stage
-        uint4 xv[XI], gv[XI];
-        const __nv_bfloat16* xg = reinterpret_cast<const __nv_bfloat16*>(ep.norm_x);
-        const __nv_bfloat16* gg = reinterpret_cast<const __nv_bfloat16*>(ep.norm_w);
-        // stage i's raw activation chunks and norm gains -> registers (one stage ahead)
-        auto load_x = [&](int i) {
-            const int kbase = (kb0 + i) * KB;
-#pragma unroll
-            for (int u = 0; u < XI; u++) {
-                const int it = ct + u * CT;
-                // token m, physical chunk cc of its row (atom cc / 8, swizzled chunk cc % 8)
-                const int m = it / RC, cc = it % RC;
-                const int k0 = kbase + 64 * (cc >> 3) + 8 * ((cc & 7) ^ (m & 7));
-                const bool kin = it < NT * RC && k0 < K;
-                xv[u] = (kin && m < Mtok) ? *reinterpret_cast<const uint4*>(xg + (int64_t)m * ep.x_ld + k0)
-                                          : make_uint4(0, 0, 0, 0);
-                gv[u] = kin ? *reinterpret_cast<const uint4*>(gg + k0) : make_uint4(0, 0, 0, 0);
-            }
-        };
         float ssv[XI];   // sum of squares of this thread's raw activation chunks (one row each)
 #pragma unroll
         for (int u = 0; u < XI; u++) ssv[u] = 0.f;
-        if (NORM) {
-            pdl_wait();
-            if (nk > 0) load_x(0);
-        }
         for (int i = 0; i < nk; i++) {
             int s = i % STAGES, c = i & 1;
-            if (INT8) {
-                // W landing in slot s also means the MMAs of stage i - STAGES are done (x slot free)
-                if (!mbar_wait(full0 + 8 * s, (i / STAGES) & 1, err, DEV_ERR_TIMEOUT_FULL)) break;
-            } else if (i >= STAGES) {
-                // x slot s is free once the MMAs of stage i - STAGES completed
-                if (!mbar_wait(empty0 + 8 * s, ((i / STAGES) - 1) & 1, err, DEV_ERR_TIMEOUT_EMPTY)) break;
-            }
+            // the stage's weights, raw activations and gains have landed (for the int8
+            // path this also means the MMAs of stage i - STAGES are done)
+            if ((INT8 || NORM) && !mbar_wait(full0 + 8 * s, (i / STAGES) & 1, err, DEV_ERR_TIMEOUT_FULL)) break;
             if (NORM) {
-                // x tile [KB / 64 atoms][NT rows][64 k] bf16, 128-B swizzle: bf16(x[m,k] * w[k]);
-                // the per-token 1/rms is a common factor of each output and is applied in the epilogue
+                // x tile [KB / 64 atoms][NT rows][64 k] bf16, 128-B swizzle, rewritten in
+                // place as bf16(x[m,k] * w[k]); rows past the tokens and columns past K
+                // arrived as zeros.  The per-token 1/rms is a common factor of each
+                // output and is applied in the epilogue.
                 uint8_t* xt = sX + s * C::X_BYTES;
+                const uint8_t* gt = sG + s * C::G_BYTES;
+                const int kbase = (kb0 + i) * KB;
 #pragma unroll
                 for (int u = 0; u < XI; u++) {
                     const int it = ct + u * CT;
                     if (it < NT * RC) {
-                        const uint32_t xa[4] = {xv[u].x, xv[u].y, xv[u].z, xv[u].w};
-                        const uint32_t ga[4] = {gv[u].x, gv[u].y, gv[u].z, gv[u].w};
+                        // token m, physical chunk cc of its row (atom cc / 8, swizzled chunk cc % 8)
+                        const int m = it / RC, cc = it % RC;
+                        const int kk = 64 * (cc >> 3) + 8 * ((cc & 7) ^ (m & 7));
+                        uint4* px = reinterpret_cast<uint4*>(xt + (cc >> 3) * C::X_ATOM + m * 128 + (cc & 7) * 16);
+                        const uint4 xv = *px;
+                        const uint4 gv = kbase + kk < K ? *reinterpret_cast<const uint4*>(gt + 2 * kk) : make_uint4(0, 0, 0, 0);
+                        const uint32_t xa[4] = {xv.x, xv.y, xv.z, xv.w};
+                        const uint32_t ga[4] = {gv.x, gv.y, gv.z, gv.w};
                         uint32_t o[4];
 #pragma unroll
                         for (int j = 0; j < 4; j++) {
@@ -479,9 +473,7 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
                             ssv[u] += a0 * a0 + a1 * a1;
                             o[j] = pack_bf16x2(a0 * bf16_lo(ga[j]), a1 * bf16_hi(ga[j]));
                         }
-                        const int m = it / RC, cc = it % RC;
-                        *reinterpret_cast<uint4*>(xt + (cc >> 3) * C::X_ATOM + m * 128 + (cc & 7) * 16) =
-                            make_uint4(o[0], o[1], o[2], o[3]);
+                        *px = make_uint4(o[0], o[1], o[2], o[3]);
                     }
                 }
                 if (!INT8) {
@@ -489,7 +481,6 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
                     __syncwarp();
                     if (lane == 0) mbar_arrive(xrdy0 + 8 * s);
                 }
-                if (i + 1 < nk) load_x(i + 1);
             }
             if (INT8) {
                 // TMEM A buffer c is free once the MMAs of stage i - 2 are done
@@ -753,6 +744,24 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
                 }
             }
         }
+        // this thread's epilogue items: row pair pl2 of the owned slice, tokens
+        // m = m_first + u * (ET / P); every thread of the int8 CTA (384, a multiple
+        // of P <= 64) takes items, the first 256 otherwise.  Their per-pair constants
+        // and first residuals are loaded now, while the partials are in flight.
+        constexpr int ET = INT8 ? C::THREADS : 256;
+        constexpr int MAXI = 4;
+        const bool eth = threadIdx.x < ET;
+        const int pl2 = threadIdx.x % P, mstep = ET / P, m0 = threadIdx.x / P;
+        PairK kc{};
+        float rr0[MAXI], rr1[MAXI];
+#pragma unroll
+        for (int u = 0; u < MAXI; u++) rr0[u] = rr1[u] = 0.f;
+        if (eth) {
+            kc = pair_consts(split * P + pl2);
+#pragma unroll
+            for (int u = 0; u < MAXI; u++)
+                if (m0 + u * mstep < NT) load_resid(kc, m0 + u * mstep, rr0[u], rr1[u]);
+        }
         const bool got = __all_sync(0xffffffffu, mbar_wait(recvb, 0, err, DEV_ERR_TIMEOUT_MISC));
         __syncthreads();   // the local slot, written by other threads
         if (NORM) {
@@ -767,16 +776,17 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
             }
             __syncthreads();
         }
-        // this thread: row pair pl2 of the owned slice, tokens m = m_first + u * (ET / P);
-        // every thread of the int8 CTA (384, a multiple of P <= 64) takes items, the
-        // first 256 otherwise
-        constexpr int ET = INT8 ? C::THREADS : 256;
-        if (threadIdx.x < ET && ok && got) {
-            const int pl2 = threadIdx.x % P, mstep = ET / P;
-            const PairK k = pair_consts(split * P + pl2);
-            for (int m = threadIdx.x / P; m < NT; m += mstep) {
-                float r0, r1;
-                load_resid(k, m, r0, r1);
+        if (eth && ok && got) {
+            const PairK& k = kc;
+            for (int u = 0, m = m0; m < NT; u++, m += mstep) {
+                float r0 = 0.f, r1 = 0.f;
+                if (u >= MAXI) load_resid(k, m, r0, r1);
+#pragma unroll
+                for (int j = 0; j < MAXI; j++)
+                    if (u == j) {
+                        r0 = rr0[j];
+                        r1 = rr1[j];
+                    }
                 float2 v[16];   // all loads in flight, then a fixed-order sum
 #pragma unroll
                 for (int r = 0; r < 16; r++)
@@ -961,9 +971,9 @@ static void gemv_split(int slots, int max_cs, int Nw, int K, int KB, int* splits
     *kb_per_out = kb_per;
 }
 
-template <int NT, int STAGES, bool INT8>
+template <int NT, int STAGES, bool INT8, int MINB>
 static int launch_gemv_tc(tb_ctx* ctx, const void* x, const void* w, const Epi& ep, int Mtok, int Nw, int K) {
-    using C = GemvCfg<NT, STAGES, INT8>;
+    using C = GemvCfg<NT, STAGES, INT8, MINB>;
     CUtensorMap tw, tx;
     int rc;
     if (INT8) {
@@ -980,7 +990,7 @@ static int launch_gemv_tc(tb_ctx* ctx, const void* x, const void* w, const Epi& 
     Epi e2 = ep;
     e2.x_ld = ep.x_ld ? ep.x_ld : K;
     e2.norm_x = x;
-    auto kern = gemv_tc_kernel<NT, STAGES, INT8>;
+    auto kern = gemv_tc_kernel<NT, STAGES, INT8, MINB>;
     // bf16: clusters of 16 (non-portable) when the device can co-schedule them,
     // else 8.  int8 (one CTA per SM, converter-bound) is fastest at 8.
     static std::atomic<int> max_cs{INT8 ? 8 : 0};
@@ -1004,10 +1014,7 @@ static int launch_gemv_tc(tb_ctx* ctx, const void* x, const void* w, const Epi& 
         max_cs.store(ok16 ? 16 : 8);
     }
     int cs, kb_per;
-    // resident CTA slots: two per SM when two rings fit in shared memory (bf16,
-    // 16 or 32 tokens); int8 CTAs (384 threads) and 64-token rings hold one
-    constexpr int per_sm = !INT8 && 2 * (C::SMEM + 1024) <= 228 * 1024 ? 2 : 1;
-    gemv_split(per_sm * ctx->num_sms, max_cs.load(), Nw, K, C::KB, &cs, &kb_per);
+    gemv_split(C::PER_SM * ctx->num_sms, max_cs.load(), Nw, K, C::KB, &cs, &kb_per);
     const int tiles = (Nw + 255) / 256;
     TB_CUDA_TRY(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     cudaLaunchConfig_t lc = {};
@@ -1035,9 +1042,11 @@ template <bool INT8>
 static int dispatch_gemv(tb_ctx* ctx, const void* x, const void* w, const Epi& ep, int M, int N, int K) {
     // <= 32 tokens: 3-stage rings (~105 KB) let two CTAs share an SM, so the
     // next layer's GEMV can start streaming weights (PDL) beside this one.
-    if (M <= 16) return launch_gemv_tc<16, INT8 ? 5 : 3, INT8>(ctx, x, w, ep, M, N, K);
-    if (M <= 32) return launch_gemv_tc<32, INT8 ? 5 : 3, INT8>(ctx, x, w, ep, M, N, K);
-    return launch_gemv_tc<64, INT8 ? 4 : 5, INT8>(ctx, x, w, ep, M, N, K);
+    // (Measured on C4 and not kept: 2-stage rings with three CTAs per SM -6%;
+    // one CTA per SM with 6-stage rings for grids of <= 148 CTAs -13%.)
+    if (M <= 16) return launch_gemv_tc<16, INT8 ? 5 : 3, INT8, INT8 ? 1 : 2>(ctx, x, w, ep, M, N, K);
+    if (M <= 32) return launch_gemv_tc<32, INT8 ? 5 : 3, INT8, INT8 ? 1 : 2>(ctx, x, w, ep, M, N, K);
+    return launch_gemv_tc<64, INT8 ? 4 : 5, INT8, 1>(ctx, x, w, ep, M, N, K);
 }
 
 int linear_launch(tb_ctx* ctx, int int8, const void* x, const void* w, const Epi& ep, int M, int N, int K) {
