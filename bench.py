@@ -2,13 +2,17 @@
 
 Default workload (BASELINE metric "tokens/s (1B decoder)"): the Llama-style
 1B decoder (16 layers, d 2048, 32/8 heads x 64, SwiGLU 8192, vocab 32000,
-bf16, N(0, 0.02) random init), batch 16 prompts of 1024 uniform-random ids
-per GPU, prefill + 128 greedy tokens.  One step = that whole generation.
-Multi-GPU: one process per GPU, weak scaling (16 sequences per GPU), the
-generated ids all-gathered over NCCL at the end of every step.
+bf16, N(0, 0.02) random init), a global batch of 16 prompts of 1024
+uniform-random ids, prefill + 128 greedy tokens.  One step = that whole
+generation.  Multi-GPU: one process per GPU, the 16 sequences sharded by
+batch (16 / N per GPU, strong scaling, the headline), the generated ids
+all-gathered over NCCL at the end of every step; the same run with 16
+sequences per GPU (weak scaling) is reported beside it.  At N = 1 the line
+also carries the C3 (flash attention), C5 (int8 decode) and C2 (conv stage)
+figures, each with its own clock record.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload c4|c5|c3]
+                    [--workload c4|c5|c3|c2|c1]
 
 --impl reference times the CPU oracle port of the same workload (the
 reference has no runnable CPU or GPU implementation) on a bounded sample.
@@ -35,6 +39,9 @@ C5 = dict(n_layers=16, d_model=2048, n_heads=32, n_kv_heads=8, head_dim=64, ffn_
 C3 = dict(B=8, H=32, S=4096, D=128)
 C2 = dict(B=32, C=64, H=56, W=56, layers=4)
 C1 = dict(B=1, S=128, d=256, heads=4, ffn=1024)
+# DRAM bytes (read + written) per algorithmic byte of the decode GEMV, from an ncu
+# capture of the gate/up launch (bench.py --ncu-case gemv): 67.96 MB for 67.37 MB
+GEMV_TRAFFIC_RATIO = 1.009
 
 
 def peaks():
@@ -258,6 +265,60 @@ def cpu_baseline_c5(budget_s=20.0):
             "sample": f"oracle C port: one decoder layer's int8 GEMVs + decode attention for 1 of 64 sequences ({t:.2f}s)"}
 
 
+def cpu_baseline_c3():
+    """Oracle causal attention on 1 of the 256 (batch, head) pairs of C3, TFLOP/s."""
+    import numpy as np
+    import oracle
+    c = C3
+    r = np.random.default_rng(0)
+    q, k, v = (oracle.round_bf16(r.standard_normal((1, 1, c["S"], c["D"]), dtype=np.float32)) for _ in range(3))
+    t0 = time.perf_counter()
+    oracle.attention(q, k, v, 1.0 / math.sqrt(c["D"]), True)
+    t = time.perf_counter() - t0
+    fl = 4 * c["D"] * c["S"] * (c["S"] + 1) / 2
+    return {"value": fl / t / 1e12, "unit": "TFLOP/s", "cores": oracle.num_threads(), "kind": "port",
+            "sample": f"oracle C port: 1 of 256 (batch, head) pairs, S 4096 D 128 causal ({t:.2f}s)"}
+
+
+def cpu_baseline_c2():
+    """Oracle conv + folded BN + ReLU on 1 of the 32 images, one of the 4 convs; images/s."""
+    import numpy as np
+    import oracle
+    c = C2
+    r = np.random.default_rng(0)
+    x = r.standard_normal((1, c["C"], c["H"], c["W"]), dtype=np.float32)
+    w = (r.standard_normal((c["C"], c["C"], 3, 3), dtype=np.float32) * math.sqrt(2.0 / (c["C"] * 9))).astype(np.float32)
+    sc, sh = np.ones(c["C"], np.float32), np.zeros(c["C"], np.float32)
+    t0 = time.perf_counter()
+    oracle.conv2d(x, w, scale=sc, shift=sh, pad=1, act="relu")
+    t = (time.perf_counter() - t0) * c["layers"]
+    return {"value": 1.0 / t, "unit": "images/s", "cores": oracle.num_threads(), "kind": "port",
+            "sample": f"oracle C port (f32): 1 image x 1 conv, times 4 convs ({t:.3f}s per image)"}
+
+
+def cpu_baseline_c1():
+    """Oracle fp32 pre-norm block (the whole C1 workload), us per block."""
+    import numpy as np
+    import oracle  # noqa: F401
+    from oracle.decoder import block_forward
+    c = C1
+    r = np.random.default_rng(0)
+    d, F = c["d"], c["ffn"]
+    p = {n: (r.standard_normal(sh, dtype=np.float32) * 0.02).astype(np.float32)
+         for n, sh in (("wq", (d, d)), ("wk", (d, d)), ("wv", (d, d)), ("wo", (d, d)), ("w_gate", (F, d)),
+                       ("w_up", (F, d)), ("w_down", (d, F)))}
+    p["attn_norm"], p["mlp_norm"] = np.ones(d, np.float32), np.ones(d, np.float32)
+    x = r.standard_normal((c["B"], c["S"], d), dtype=np.float32)
+    block_forward(x, p, c["heads"])
+    t0 = time.perf_counter()
+    n = 10
+    for _ in range(n):
+        block_forward(x, p, c["heads"])
+    t = (time.perf_counter() - t0) / n
+    return {"value": t * 1e6, "unit": "us", "cores": oracle.num_threads(), "kind": "port",
+            "sample": f"oracle C port: the whole C1 block, mean of {n}"}
+
+
 # ----------------------------------------------------------------- C4 -------
 def c4_bytes_flops():
     c = C4
@@ -268,27 +329,31 @@ def c4_bytes_flops():
     return shapes, layer_params
 
 
-def run_c4(args, rank, world, local):
-    import numpy as np
-    import torch
+def _c4_decoder(B, local):
     from teenygrad_b200.decoder import Decoder, DecoderConfig
-    from teenygrad_b200 import ops
     c = C4
-    B, S, G = c["batch"], c["prompt"], c["gen"]
+    S, G = c["prompt"], c["gen"]
     cfg = DecoderConfig(n_layers=c["n_layers"], d_model=c["d_model"], n_heads=c["n_heads"], n_kv_heads=c["n_kv_heads"],
                         head_dim=c["head_dim"], ffn_hidden=c["ffn_hidden"], vocab=c["vocab"], max_batch=B,
                         max_seq=S + G, max_prefill_tokens=B * S)
     dec = Decoder(cfg, device=local)
     dec.init_random(seed=1234, std=0.02)
-    gen = torch.Generator(device="cpu").manual_seed(42 + rank)
+    return dec
+
+
+def _c4_generation(args, dec, B, rank, world, comm, seed_base):
+    """Times `steps` generations of B local sequences (+ the all-gather of the
+    ids): device-resident prompts, then end to end from pinned host memory.
+    Returns ms per step (max over ranks), e2e ms, this rank's ms, prefill ms,
+    all-gather ms and the gathered ids of the last step."""
+    import torch
+    c = C4
+    S, G = c["prompt"], c["gen"]
+    gen = torch.Generator(device="cpu").manual_seed(seed_base + rank)
     prompt_host = torch.randint(0, c["vocab"], (B, S), generator=gen, dtype=torch.int32).pin_memory()
     prompt = prompt_host.cuda()
     out = torch.empty(B, G, device="cuda", dtype=torch.int32)
     gathered = torch.empty(world * B, G, device="cuda", dtype=torch.int32)
-    comm = None
-    if world > 1:
-        from teenygrad_b200.dist import Comm
-        comm = Comm(rank, world, timeout_ms=60000, device=local)
 
     def step():
         dec.generate(prompt, G, out=out)
@@ -298,21 +363,16 @@ def run_c4(args, rank, world, local):
     for _ in range(args.warmup):
         step()
     barrier(world)
-    clk = Clocks(local) if rank == 0 else None
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier(world)
     ev0.record()
     for _ in range(args.steps):
         step()
     ev1.record()
     barrier(world)
-    clocks = clk.stop() if clk else None
-    ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps, world)
-    tokens = world * B * (S + G)
-    value = tokens / (ms / 1e3)
+    my_ms = ev0.elapsed_time(ev1) / args.steps
+    ms = max_over_ranks(my_ms, world)
 
-    # ---- end to end through the public API with host buffers
-    out_host = torch.empty(B, G, dtype=torch.int32).pin_memory()
+    # end to end through the public API with host buffers
     gathered_host = torch.empty(world * B, G, dtype=torch.int32).pin_memory()
 
     def e2e_step():
@@ -322,12 +382,11 @@ def run_c4(args, rank, world, local):
             comm.all_gather(o, gathered)
             gathered_host.copy_(gathered, non_blocking=True)
         else:
-            out_host.copy_(o, non_blocking=True)
+            gathered_host.copy_(o, non_blocking=True)
         torch.cuda.current_stream().synchronize()
 
     e2e_step()
     barrier(world)
-    t0 = time.perf_counter()
     ev0.record()
     for _ in range(args.steps):
         e2e_step()
@@ -335,10 +394,71 @@ def run_c4(args, rank, world, local):
     barrier(world)
     e2e_ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps, world)
 
-    # ---- phase split: prefill vs decode (CUDA events)
-    ms_prefill = time_loop(lambda: dec.prefill(prompt), 2)
-    dec.prefill(prompt)
-    ms_decode = time_loop(lambda: dec.decode_step(), G - 1)
+    # phase split (CUDA events): prefill alone; the all-gather alone
+    ms_prefill = max_over_ranks(time_loop(lambda: dec.prefill(prompt), 3), world)
+    ms_ag = 0.0
+    if comm is not None:
+        barrier(world)
+        ms_ag = max_over_ranks(time_loop(lambda: comm.all_gather(out, gathered), 20), world)
+    return ms, e2e_ms, my_ms, ms_prefill, ms_ag, gathered, out
+
+
+def run_c4(args, rank, world, local):
+    import torch
+    from teenygrad_b200 import ops
+    from teenygrad_b200.dist import shard
+    c = C4
+    Bg, S, G = c["batch"], c["prompt"], c["gen"]
+    # strong scaling (the config): the global batch of 16 sharded over the ranks
+    start, B = shard(Bg, world, rank)
+    assert Bg % world == 0, "the all-gather needs equal shards (N must divide 16)"
+    comm = None
+    if world > 1:
+        from teenygrad_b200.dist import Comm
+        comm = Comm(rank, world, timeout_ms=60000, device=local)
+    dec = _c4_decoder(B, local)
+    clk = Clocks(local) if rank == 0 else None
+    ms, e2e_ms, my_ms, ms_prefill, ms_ag, gathered, out = _c4_generation(args, dec, B, rank, world, comm, 42)
+    clocks = clk.stop() if clk else None
+    per_rank = [my_ms]
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([my_ms], device="cuda", dtype=torch.float64)
+        allt = [torch.zeros_like(t) for _ in range(world)]
+        dist.all_gather(allt, t)
+        per_rank = [round(float(x.item()), 3) for x in allt]
+    per_rank = [round(x, 3) for x in per_rank]
+    # the gathered ids: this rank's block is its own generation, and every rank
+    # holds the same gathered array (checksum min == max over ranks)
+    ids_ok = True
+    if comm is not None:
+        import torch.distributed as dist
+        torch.cuda.synchronize()
+        ids_ok = bool(torch.equal(gathered[rank * B:(rank + 1) * B], out))
+        ck = (gathered.long() * torch.arange(1, gathered.numel() + 1, device="cuda").view_as(gathered)).sum()
+        lo, hi = ck.clone(), ck.clone()
+        dist.all_reduce(lo, op=dist.ReduceOp.MIN)
+        dist.all_reduce(hi, op=dist.ReduceOp.MAX)
+        ok_t = torch.tensor([int(ids_ok and bool(lo == hi))], device="cuda")
+        dist.all_reduce(ok_t, op=dist.ReduceOp.MIN)
+        ids_ok = bool(ok_t.item())
+    tokens = Bg * (S + G)
+    value = tokens / (ms / 1e3)
+    decode_ms = (ms - ms_prefill - ms_ag) / (G - 1)
+
+    # weak scaling (16 sequences per GPU) beside it, for N > 1
+    weak = None
+    if world > 1:
+        del dec
+        torch.cuda.empty_cache()
+        dec_w = _c4_decoder(Bg, local)
+        wms = _c4_generation(args, dec_w, Bg, rank, world, comm, 4242)[0]
+        weak = {"tokens_per_s": round(world * Bg * (S + G) / (wms / 1e3), 1), "ms_per_step": round(wms, 3),
+                "sequences_per_gpu": Bg}
+        del dec_w
+        torch.cuda.empty_cache()
+    else:
+        del dec
 
     # ---- dominant kernels, timed live on this stream:
     # decode GEMV: the 4 linear layers x 16 layers with distinct weights (1.9 GB,
@@ -348,7 +468,7 @@ def run_c4(args, rank, world, local):
     shapes, layer_params = c4_bytes_flops()
     nl = c["n_layers"]
     wts = [{k: (torch.randn(n, kk, device="cuda") * 0.02).bfloat16() for k, (n, kk) in shapes.items()} for _ in range(nl)]
-    xs = {k: torch.randn(B, kk, device="cuda").bfloat16() for k, (n, kk) in shapes.items()}
+    xs = {k: torch.randn(Bg, kk, device="cuda").bfloat16() for k, (n, kk) in shapes.items()}
 
     def gemv_all():
         for L in wts:
@@ -356,33 +476,27 @@ def run_c4(args, rank, world, local):
                 ops.linear(xs[k], L[k], swiglu=(k == "gate_up"))
 
     gemv_ms = graph_time(gemv_all, iters=10)
-    gemv_bytes = nl * sum(2 * n * kk + 2 * B * kk + 2 * B * (n // 2 if k == "gate_up" else n)
+    gemv_bytes = nl * sum(2 * n * kk + 2 * Bg * kk + 2 * Bg * (n // 2 if k == "gate_up" else n)
                           for k, (n, kk) in shapes.items())
     gemv_gbs = gemv_bytes / (gemv_ms / 1e3) / 1e9
-    xp = torch.randn(B * S, c["d_model"], device="cuda").bfloat16()
+    xp = torch.randn(Bg * S, c["d_model"], device="cuda").bfloat16()
     n_gu = shapes["gate_up"][0]
     ops.linear(xp, wts[0]["gate_up"], swiglu=True)
     gemm_ms = time_loop(lambda: ops.linear(xp, wts[0]["gate_up"], swiglu=True), 10)
-    gemm_tflops = 2 * B * S * n_gu * c["d_model"] / (gemm_ms / 1e3) / 1e12
-    del wts
-    dom_decode = ms_decode * (G - 1) >= ms_prefill
-    if dom_decode:
-        # DRAM traffic per launch: the ncu capture of the gate/up GEMV (profiles/gemv_tc_decode_gate_up.md:
-        # 68.01 MB read + written for 67.4 MB of algorithmic bytes) scaled to the average launch of the step
-        traffic = round(gemv_bytes / (4 * nl) * (68.01 / 67.4))
-        roof = {"kernel": "gemv_tc_kernel (decode linear layers, bf16 weights, 16 tokens)", "bound": "hbm",
-                "achieved": round(gemv_gbs, 1), "peak": pk["hbm"], "unit": "GB/s",
-                "frac": round(gemv_gbs / pk["hbm"], 3), "traffic": traffic,
-                "traffic_note": "bytes per average launch: ncu dram bytes / algorithmic bytes of the gate/up GEMV capture, times the average algorithmic bytes",
-                "peak_source": pk["src"]}
-    else:
-        roof = {"kernel": "gemm_tc_kernel (prefill gate/up, 16384x16384x2048)", "bound": "tensor",
-                "achieved": round(gemm_tflops, 1), "peak": pk["tc"], "unit": "TFLOP/s",
-                "frac": round(gemm_tflops / pk["tc"], 3), "traffic": None, "peak_source": pk["src"]}
-    secondary = {"prefill_gemm_gate_up_tflops": round(gemm_tflops, 1),
-                 "prefill_gemm_frac_of_peak": round(gemm_tflops / pk["tc"], 3),
-                 "decode_gemv_gbs": round(gemv_gbs, 1), "decode_gemv_frac_of_hbm": round(gemv_gbs / pk["hbm"], 3),
-                 "decode_gemv_ms_per_step": round(gemv_ms, 4)}
+    gemm_tflops = 2 * Bg * S * n_gu * c["d_model"] / (gemm_ms / 1e3) / 1e12
+    del wts, xp
+    torch.cuda.empty_cache()
+    # DRAM bytes per launch from ncu captures of the same kernels (dram__bytes_read.sum +
+    # dram__bytes_write.sum; commands: bench.py --ncu-case gemv / gemm under
+    # ncu --set full -k regex:<kernel> -s 1 -c 1): the gate/up GEMV read+wrote 1.009x its
+    # algorithmic bytes, scaled here to the average launch of the 64
+    traffic = round(gemv_bytes / (4 * nl) * GEMV_TRAFFIC_RATIO)
+    roof = {"kernel": "gemv_tc_kernel (decode linear layers, bf16 weights, 16 tokens)", "bound": "hbm",
+            "achieved": round(gemv_gbs, 1), "peak": pk["hbm"], "unit": "GB/s",
+            "frac": round(gemv_gbs / pk["hbm"], 3), "traffic": traffic,
+            "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of the gate/up decode GEMV "
+                              "(small case), per algorithmic byte, times the average launch's algorithmic bytes",
+            "peak_source": pk["src"]}
     if comm is not None:
         comm.close()
     # prefill: set_state, embedding, per layer (rmsnorm, QKV GEMM, rope_kv, attention,
@@ -392,20 +506,31 @@ def run_c4(args, rank, world, local):
     launches_prefill = 2 + 8 * c["n_layers"] + 3
     launches_decode = 1 + 5 * c["n_layers"] + 3
     launches = launches_prefill + (G - 1) * launches_decode
+    cfg = {"workload": "C4: Llama-style 1B decoder, global batch 16 x 1024-token prompts + 128 greedy tokens, "
+                       "batch-sharded over the GPUs",
+           "model": "llama-1b (16L, d2048, 32q/8kv x 64, SwiGLU 8192, vocab 32000)", "global_batch": Bg,
+           "sequences_per_gpu": B, "seq_len": S, "gen_tokens": G,
+           "parallelism": f"dp{world} (batch-sharded; generated ids all-gathered with the library's NCCL communicator)",
+           "tokens_counted": "prompt + generated tokens of all sequences",
+           "l2": "inputs larger than L2 (2.2 GB of weights streamed per step)",
+           "prefill_ms": round(ms_prefill, 3), "decode_ms_per_token": round(decode_ms, 4),
+           "decode_ms_source": "(timed step - prefill - all-gather) / 127 graph-replayed decode steps",
+           "prefill_tokens_per_s": round(Bg * S / (ms_prefill / 1e3), 1),
+           "decode_tokens_per_s": round(Bg / (decode_ms / 1e3), 1),
+           "per_rank_ms": per_rank, "allgather_ms": round(ms_ag, 4), "allgather_ids_checked": ids_ok,
+           "prefill_gemm_gate_up_tflops": round(gemm_tflops, 1),
+           "prefill_gemm_frac_of_peak": round(gemm_tflops / pk["tc"], 3),
+           "decode_gemv_gbs": round(gemv_gbs, 1), "decode_gemv_frac_of_hbm": round(gemv_gbs / pk["hbm"], 3),
+           "decode_gemv_ms_per_step": round(gemv_ms, 4)}
+    if weak is not None:
+        cfg["weak_scaling"] = weak
     res = {
         "metric": "tokens/s (1B decoder)", "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (uniform-random ids, N(0,0.02) random-init weights)",
-        "config": {"workload": "C4: Llama-style 1B decoder, batch 16 x 1024-token prompts + 128 greedy tokens per GPU",
-                   "model": "llama-1b (16L, d2048, 32q/8kv x 64, SwiGLU 8192, vocab 32000)", "global_batch": world * B,
-                   "seq_len": S, "gen_tokens": G, "parallelism": f"dp{world} (batch-sharded; generated ids all-gathered with the library's NCCL communicator)",
-                   "tokens_counted": "prompt + generated tokens of all sequences",
-                   "l2": "inputs larger than L2 (2.2 GB of weights streamed per step)",
-                   "prefill_ms": round(ms_prefill, 3), "decode_ms_per_token": round(ms_decode, 4),
-                   "prefill_tokens_per_s": round(B * S / (ms_prefill / 1e3), 1),
-                   "decode_tokens_per_s": round(B / (ms_decode / 1e3), 1), **secondary},
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (uniform-random ids, N(0,0.02) random-init weights)", "config": cfg,
         "e2e": {"value": round(tokens / (e2e_ms / 1e3), 1), "unit": "tokens/s", "h2d_bytes_per_step": B * S * 4,
-                "d2h_bytes_per_step": (world * B if world > 1 else B) * G * 4},
+                "d2h_bytes_per_step": Bg * G * 4},
         "gpu_launches": launches * args.steps,
         "roofline": roof,
         "clocks": clocks,
@@ -416,8 +541,9 @@ def run_c4(args, rank, world, local):
 def run_c5(args, rank, world, local):
     import torch
     from teenygrad_b200.decoder import Decoder, DecoderConfig
+    from teenygrad_b200.dist import shard
     c = C5
-    B = c["batch"]
+    B = shard(c["batch"], world, rank)[1]     # the batch of 64 sharded over the ranks
     cfg = DecoderConfig(n_layers=c["n_layers"], d_model=c["d_model"], n_heads=c["n_heads"], n_kv_heads=c["n_kv_heads"],
                         head_dim=c["head_dim"], ffn_hidden=c["ffn_hidden"], vocab=c["vocab"], max_batch=B,
                         max_seq=c["ctx"] + 64, max_prefill_tokens=B, weights_int8=True)
@@ -425,31 +551,40 @@ def run_c5(args, rank, world, local):
     dec.init_random(seed=7)
     ids = torch.randint(0, c["vocab"], (B,), dtype=torch.int32, device="cuda")
     steps = min(args.steps * 8, 60)
+    clk = Clocks(local) if rank == 0 else None
     dec.fill_kv_random(ids, c["ctx"], seed=5)
     for _ in range(args.warmup):
         dec.decode_step()
-    dec.fill_kv_random(ids, c["ctx"], seed=5)
-    barrier(world)
-    clk = Clocks(local) if rank == 0 else None
-    ms = time_loop(lambda: dec.decode_step(), steps)
+    # blocks of `steps` decode steps from a freshly filled cache (it holds ctx + 64
+    # positions) until >= 0.6 s were timed, so the clock record samples them
+    tot, n = 0.0, 0
+    while tot < 600.0 or n < 1:
+        dec.fill_kv_random(ids, c["ctx"], seed=5)
+        barrier(world)
+        tot += time_loop(lambda: dec.decode_step(), steps) * steps
+        n += steps
     clocks = clk.stop() if clk else None
-    ms = max_over_ranks(ms, world)
+    ms = max_over_ranks(tot / n, world)
     d, F, V = c["d_model"], c["ffn_hidden"], c["vocab"]
     qkv = (c["n_heads"] + 2 * c["n_kv_heads"]) * c["head_dim"]
     w_bytes = c["n_layers"] * (qkv * d + d * c["n_heads"] * c["head_dim"] + 2 * F * d + d * F) + V * d
     s_bytes = 4 * (c["n_layers"] * (qkv + d + 2 * F + d) + V)
     ctx_mean = c["ctx"] + steps / 2
     kv_bytes = c["n_layers"] * B * c["n_kv_heads"] * ctx_mean * c["head_dim"] * 2 * 2
-    step_bytes = w_bytes + s_bytes + kv_bytes
+    step_bytes = w_bytes + s_bytes + kv_bytes          # this rank's bytes per decode step
     pk = peaks()
     gbs = world * step_bytes / (ms / 1e3) / 1e9
     return {"metric": "HBM GB/s (int8 weight-only decode, 1B decoder)", "value": round(gbs, 1), "unit": "GB/s",
             "n_gpus": world, "steps": steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8 x bf16",
-            "data": "synthetic", "config": {"workload": "C5: int8 weight-only decode, batch 64, KV 2048 pre-filled N(0,1)",
-                                            "tokens_per_s": round(world * B / (ms / 1e3), 1),
-                                            "bytes_per_step": int(step_bytes)},
-            "roofline": {"bound": "hbm", "achieved": round(gbs / world, 1), "peak": pk["hbm"], "unit": "GB/s",
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8 x bf16",
+            "data": "synthetic", "config": {"workload": "C5: int8 weight-only decode, batch 64 (sharded over the GPUs), "
+                                                        "KV 2048 pre-filled N(0,1)",
+                                            "sequences_per_gpu": B,
+                                            "tokens_per_s": round(c["batch"] / (ms / 1e3), 1),
+                                            "bytes_per_step_per_gpu": int(step_bytes),
+                                            "l2": "inputs larger than L2 (1.04 GB of int8 weights + 4.3 GB KV per step)"},
+            "roofline": {"kernel": "decode step (int8 GEMVs + decode attention), bytes per step / step time",
+                         "bound": "hbm", "achieved": round(gbs / world, 1), "peak": pk["hbm"], "unit": "GB/s",
                          "frac": round(gbs / world / pk["hbm"], 3), "traffic": None, "peak_source": pk["src"]},
             "clocks": clocks}
 
@@ -457,25 +592,33 @@ def run_c5(args, rank, world, local):
 def run_c3(args, rank, world, local):
     import torch
     from teenygrad_b200 import ops
+    from teenygrad_b200.dist import shard
     c = C3
-    B, H, S, D = c["B"], c["H"], c["S"], c["D"]
-    q = torch.randn(B, H, S, D, device="cuda").bfloat16()
-    k = torch.randn(B, H, S, D, device="cuda").bfloat16()
-    v = torch.randn(B, H, S, D, device="cuda").bfloat16()
+    Bg, H, S, D = c["B"], c["H"], c["S"], c["D"]
+    # the 256 (batch, head) pairs sharded over the ranks (heads are independent: no GQA in C3)
+    npairs = shard(Bg * H, world, rank)[1]
+    B = 1
+    q = torch.randn(1, npairs, S, D, device="cuda").bfloat16()
+    k = torch.randn(1, npairs, S, D, device="cuda").bfloat16()
+    v = torch.randn(1, npairs, S, D, device="cuda").bfloat16()
+    H = npairs
+    clk = Clocks(local) if rank == 0 else None
     for _ in range(args.warmup):
         ops.attention(q, k, v, causal=True, return_lse=True)
+    est = time_loop(lambda: ops.attention(q, k, v, causal=True, return_lse=True), 2)
+    steps = max(args.steps, int(math.ceil(600.0 / max(est, 1e-3))))   # >= 0.6 s, so the clock record samples it
     barrier(world)
-    clk = Clocks(local) if rank == 0 else None
-    ms = time_loop(lambda: ops.attention(q, k, v, causal=True, return_lse=True), args.steps)
+    ms = time_loop(lambda: ops.attention(q, k, v, causal=True, return_lse=True), steps)
     clocks = clk.stop() if clk else None
     ms = max_over_ranks(ms, world)
-    flops = 4 * B * H * D * S * (S + 1) / 2
+    flops = 4 * B * H * D * S * (S + 1) / 2            # this rank's share
     tf = flops / (ms / 1e3) / 1e12
     pk = peaks()
-    return {"metric": "TFLOP/s (causal flash-attention prefill bf16)", "value": round(world * tf, 1), "unit": "TFLOP/s",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "C3: B8 H32 S4096 D128 causal, O + LSE"},
+    return {"metric": "TFLOP/s (causal flash-attention prefill bf16)", "value": round(4 * Bg * c["H"] * D * S * (S + 1) / 2 / (ms / 1e3) / 1e12, 1),
+            "unit": "TFLOP/s", "n_gpus": world, "steps": steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "C3: B8 H32 S4096 D128 causal, O + LSE; the 256 (batch, head) pairs sharded over the GPUs",
+                       "pairs_per_gpu": H, "l2": "inputs larger than L2 (Q, K, V, O: 1.07 GB per GPU at N = 1)"},
             "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": pk["tc"], "unit": "TFLOP/s",
                          "frac": round(tf / pk["tc"], 3), "traffic": None, "peak_source": pk["src"]},
             "clocks": clocks}
@@ -485,8 +628,9 @@ def run_c2(args, rank, world, local):
     """4 x (3x3 conv 64->64, pad 1 + bias + folded BN + ReLU), NCHW, batch 32, 56x56."""
     import torch
     from teenygrad_b200 import ops
+    from teenygrad_b200.dist import shard
     c = C2
-    B, C, H, W = c["B"], c["C"], c["H"], c["W"]
+    B, C, H, W = shard(c["B"], world, rank)[1], c["C"], c["H"], c["W"]   # the 32 images sharded over the ranks
     g = torch.Generator(device="cpu").manual_seed(0)
     res = {}
     pk = peaks()
@@ -508,27 +652,37 @@ def run_c2(args, rank, world, local):
                 y = ops.conv2d(y, w, scale=sc, shift=sh, pad=1, act="relu")
             return y
 
+        clk = Clocks(local) if (rank == 0 and dt == torch.bfloat16) else None
         for _ in range(args.warmup):
             stage()
-        # CUDA-graph replays of the stage (and of one conv) with L2 flushed before each
-        ms = graph_time_flushed(stage, max(args.steps, 3))
+        # CUDA-graph replays of the stage (and of one conv) with L2 flushed before each;
+        # the bf16 stage is replayed for >= 0.6 s so that the clock record samples it
+        est = graph_time_flushed(stage, 3)
+        iters = max(args.steps, 3) if dt != torch.bfloat16 else max(args.steps, int(math.ceil(600.0 / max(est + 0.1, 1e-3))))
+        ms = graph_time_flushed(stage, iters)
+        if clk:
+            res["clocks"] = clk.stop()
         ms_conv = graph_time_flushed(
             lambda: ops.conv2d(x, layers[0][0], scale=layers[0][1], shift=layers[0][2], pad=1, act="relu"), 5)
         res[str(dt).split(".")[1]] = (ms, ms_conv)
     ms_bf16, conv_bf16 = res["bfloat16"]
     ms_f32, conv_f32 = res["float32"]
+    clocks = res.get("clocks")
     tf = flops_conv / (conv_bf16 / 1e3) / 1e12
-    return {"metric": "images/s (ResNet-style conv stage, 4 x conv3x3 + bias + BN + ReLU)", "value": round(world * B / (ms_bf16 / 1e3), 1),
+    ms_bf16 = max_over_ranks(ms_bf16, world)
+    return {"metric": "images/s (ResNet-style conv stage, 4 x conv3x3 + bias + BN + ReLU)", "value": round(c["B"] / (ms_bf16 / 1e3), 1),
             "unit": "images/s", "n_gpus": world, "steps": max(args.steps, 3), "warmup": args.warmup, "ms_per_step": round(ms_bf16, 4),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "C2: 4 x 3x3 conv 64->64 + bias + folded BN + ReLU, B32 56x56 NCHW",
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "C2: 4 x 3x3 conv 64->64 + bias + folded BN + ReLU, B32 56x56 NCHW (images sharded over the GPUs)",
+                       "images_per_gpu": B,
                        "timing": "CUDA graph replays, L2 flushed (256 MB write) before each", "l2": "flushed",
                        "fp32_ms_per_step": round(ms_f32, 3), "fp32_images_per_s": round(B / (ms_f32 / 1e3), 1),
                        "bf16_conv_ms": round(conv_bf16, 4), "fp32_conv_ms": round(conv_f32, 4),
                        "fp32_conv_tflops": round(flops_conv / (conv_f32 / 1e3) / 1e12, 1)},
             "roofline": {"kernel": "conv_tc_kernel (+ NHWC transpose), one conv", "bound": "tensor", "achieved": round(tf, 1),
                          "peak": pk["tc"], "unit": "TFLOP/s", "frac": round(tf / pk["tc"], 3), "traffic": None,
-                         "peak_source": pk["src"]}}
+                         "peak_source": pk["src"]},
+            "clocks": clocks}
 
 
 def run_c1(args, rank, world, local):
@@ -597,6 +751,20 @@ def ncu_case(which):
     print("ok", which)
 
 
+def secondary_n1(args, local):
+    """C3, C5 and C2 at N = 1, each timed with its own clock record, for the
+    default (C4) line."""
+    import torch
+    a = argparse.Namespace(steps=max(3, min(args.steps, 10)), warmup=3)
+    out = {}
+    for name, fn in (("c3", run_c3), ("c5", run_c5), ("c2", run_c2)):
+        r = fn(a, 0, 1, local)
+        out[name] = {"metric": r["metric"], "value": r["value"], "unit": r["unit"], "ms_per_step": r["ms_per_step"],
+                     "workload": r["config"]["workload"], "roofline": r["roofline"], "clocks": r.get("clocks")}
+        torch.cuda.empty_cache()
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -605,6 +773,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="c4", choices=["c4", "c5", "c3", "c2", "c1"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-secondary", action="store_true", help="C4 at N = 1: skip the C3 / C5 / C2 fields")
     ap.add_argument("--ncu-case", default=None, help="run one small profiling case and exit")
     args = ap.parse_args()
     if args.ncu_case:
@@ -613,14 +782,20 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     world_env = int(os.environ.get("WORLD_SIZE", "1"))
 
+    baselines = {"c4": cpu_baseline_c4, "c5": cpu_baseline_c5, "c3": cpu_baseline_c3, "c2": cpu_baseline_c2,
+                 "c1": cpu_baseline_c1}
     if args.impl == "reference":
         if rank != 0:
             return 0
-        cb = cpu_baseline_c5() if args.workload == "c5" else cpu_baseline_c4()
+        import oracle
+        oracle.set_num_threads(len(os.sched_getaffinity(0)))   # every host core this process may use
+        cb = baselines[args.workload]()
         metric = {"c4": "tokens/s (1B decoder)", "c5": "HBM GB/s (int8 weight-only decode, 1B decoder)",
-                  "c3": "tokens/s (1B decoder)"}[args.workload]
+                  "c3": "TFLOP/s (causal flash-attention prefill bf16)",
+                  "c2": "images/s (ResNet-style conv stage, 4 x conv3x3 + bias + BN + ReLU)",
+                  "c1": "us per block (fp32 pre-norm transformer block)"}[args.workload]
         print(json.dumps({"impl": "reference", "metric": metric, "value": cb["value"], "unit": cb["unit"],
-                          "n_gpus": args.gpus, "steps": 1, "warmup": 0, "higher_is_better": True,
+                          "n_gpus": args.gpus, "steps": 1, "warmup": 0, "higher_is_better": args.workload != "c1",
                           "config": {"workload": args.workload.upper()}, "cpu_baseline": cb,
                           "e2e": {"value": cb["value"], "unit": cb["unit"], "h2d_bytes_per_step": 0,
                                   "d2h_bytes_per_step": 0}}), flush=True)
@@ -629,8 +804,12 @@ def main():
     rank, world, local = dist_setup(max(args.gpus, world_env))
     run = {"c4": run_c4, "c5": run_c5, "c3": run_c3, "c2": run_c2, "c1": run_c1}[args.workload]
     res = run(args, rank, world, local)
-    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload in ("c4", "c5"):
-        res["cpu_baseline"] = cpu_baseline_c5() if args.workload == "c5" else cpu_baseline_c4()
+    if world == 1 and args.workload == "c4" and not args.no_secondary:
+        res["secondary_workloads"] = secondary_n1(args, local)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        import oracle
+        oracle.set_num_threads(len(os.sched_getaffinity(0)))
+        res["cpu_baseline"] = baselines[args.workload]()
     if rank == 0:
         print(json.dumps(res), flush=True)
     if world > 1:

@@ -104,6 +104,23 @@ TB_API int tb_swiglu_fwd(tb_ctx* ctx, int dtype, const void* gate, const void* u
 /* elemwise_add_forward (nn/tensor/elemwise_add.rs:29). */
 TB_API int tb_add_fwd(tb_ctx* ctx, int dtype, const void* a, const void* b, void* y, int64_t n);
 
+/* --------------------------------------------------- allocation queries --- */
+/* Operator ids for the queries below. */
+typedef enum tb_op {
+    TB_OP_LINEAR = 0, TB_OP_MATMUL = 1, TB_OP_INT8_LINEAR = 2, TB_OP_RMSNORM = 3, TB_OP_LAYERNORM = 4,
+    TB_OP_ACT = 5, TB_OP_ATTN = 6, TB_OP_CONV2D = 7, TB_OP_QUANTIZE_INT8 = 8
+} tb_op;
+/* Row stride (elements) an executor should allocate for an op's output rows
+ * of row_elems elements: RuntimeOp::forward_output_row_stride
+ * (core/teeny-core/src/model/mod.rs:100-115); for linear layers the
+ * reference pads rows to 16 bytes (LinearForward, nn/mlp/linear.rs:267-272),
+ * every other op writes dense rows.  Needs no GPU. */
+TB_API int tb_output_row_stride(int op, int dtype, int64_t row_elems, int64_t* stride);
+/* Device workspace an op needs, in bytes (0 for all but the bf16
+ * tensor-core conv2d).  shape: TB_OP_CONV2D {B, Cin, Cout, H, W, KH, KW,
+ * stride, pad}; ignored for the others.  Needs no GPU. */
+TB_API int tb_workspace_bytes(int op, int dtype, const int64_t* shape, int n_shape, size_t* bytes);
+
 /* ------------------------------------------------------------- linear --- */
 /* linear_forward (nn/mlp/linear.rs:22-117; LinearForward RuntimeOp :251-388):
  * y[M, N] = x[M, K] * w[N, K]^T (+ bias) (+ residual), epilogue per `flags`.
@@ -111,6 +128,14 @@ TB_API int tb_add_fwd(tb_ctx* ctx, int dtype, const void* a, const void* b, void
  * TB_F32: f32 CUDA-core path (exact f32 accumulate). */
 TB_API int tb_linear_fwd(tb_ctx* ctx, int dtype, const void* x, const void* w, const float* bias,
                   const void* residual, void* y, int64_t M, int64_t N, int64_t K, int flags);
+/* The same with row strides, as LinearForward's pack_args passes them
+ * (nn/mlp/linear.rs:274-300: stride_xm, and stride_ym = the padded
+ * output_row_stride): x rows ldx >= K elements apart, y rows (and the
+ * residual's) ldy >= N (N / 2 with SwiGLU) apart.  TB_BF16 needs ldx and ldy
+ * multiples of 8; columns of y past N are not written. */
+TB_API int tb_linear_fwd_strided(tb_ctx* ctx, int dtype, const void* x, int64_t ldx, const void* w,
+                                 const float* bias, const void* residual, void* y, int64_t ldy, int64_t M,
+                                 int64_t N, int64_t K, int flags);
 
 /* matmul_forward (math/gemm.rs:44-105; MatMulRuntimeOp gemm.rs:232):
  * c[M, N] = a[M, K] * b[K, N]. */

@@ -145,6 +145,54 @@ int tb_set_stream(tb_ctx* ctx, void* stream) {
     return TB_OK;
 }
 
+int tb_output_row_stride(int op, int dtype, int64_t row_elems, int64_t* stride) {
+    if (!stride || row_elems < 0) return TB_ERR_ARG;
+    const int64_t esz = dtype == TB_F32 || dtype == TB_I32 ? 4 : dtype == TB_BF16 ? 2 : dtype == TB_I8 ? 1 : 0;
+    if (!esz) return TB_ERR_UNSUPPORTED;
+    switch (op) {
+        case TB_OP_LINEAR:
+        case TB_OP_INT8_LINEAR: {
+            // rows padded to 16 bytes (LinearForward::forward_output_row_stride)
+            const int64_t align = 16 / esz;
+            *stride = (row_elems + align - 1) / align * align;
+            return TB_OK;
+        }
+        case TB_OP_MATMUL:
+        case TB_OP_RMSNORM:
+        case TB_OP_LAYERNORM:
+        case TB_OP_ACT:
+        case TB_OP_ATTN:
+        case TB_OP_CONV2D:
+        case TB_OP_QUANTIZE_INT8:
+            *stride = row_elems;   // dense rows
+            return TB_OK;
+        default: return TB_ERR_ARG;
+    }
+}
+
+int tb_workspace_bytes(int op, int dtype, const int64_t* shape, int n_shape, size_t* bytes) {
+    if (!bytes) return TB_ERR_ARG;
+    *bytes = 0;
+    switch (op) {
+        case TB_OP_CONV2D:
+            // shape = {B, Cin, Cout, H, W, KH, KW, stride, pad}
+            if (!shape || n_shape != 9) return TB_ERR_ARG;
+            return tb_conv2d_workspace_size(dtype, (int)shape[0], (int)shape[1], (int)shape[2], (int)shape[3],
+                                            (int)shape[4], (int)shape[5], (int)shape[6], (int)shape[7], (int)shape[8],
+                                            bytes);
+        case TB_OP_LINEAR:
+        case TB_OP_INT8_LINEAR:
+        case TB_OP_MATMUL:
+        case TB_OP_RMSNORM:
+        case TB_OP_LAYERNORM:
+        case TB_OP_ACT:
+        case TB_OP_ATTN:
+        case TB_OP_QUANTIZE_INT8:
+            return TB_OK;   // no workspace: split-K and attention splits reduce on chip
+        default: return TB_ERR_ARG;
+    }
+}
+
 int tb_device_error(tb_ctx* ctx, int* code, int clear) {
     if (!ctx || !code) return TB_ERR_ARG;
     TB_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));

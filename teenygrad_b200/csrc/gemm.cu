@@ -812,10 +812,12 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
 // cluster (gridDim.z CTAs); the partial tiles are summed over DSMEM in rank
 // order (deterministic), each rank finishing 64 / splits rows.
 // B_KN: b is [K, N] (matmul_forward); else b is [N, K] (linear_forward).
+// lda: row stride of a; ldy: row stride of y and of the residual.
 template <bool B_KN>
 __global__ void __launch_bounds__(256)
 gemm_f32_kernel(const float* __restrict__ a, const float* __restrict__ b, const float* __restrict__ bias,
-                const float* __restrict__ resid, float* __restrict__ y, int M, int N, int K, int k_per_split) {
+                const float* __restrict__ resid, float* __restrict__ y, int M, int N, int K, int k_per_split,
+                int64_t lda, int64_t ldy) {
     __shared__ float sa[2][32][64 + 4];
     __shared__ float sb[2][32][64 + 4];
     const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
@@ -832,7 +834,7 @@ gemm_f32_kernel(const float* __restrict__ a, const float* __restrict__ b, const 
             const int e = tid + 256 * u;
             {
                 const int r = e / 32, kk = e % 32, gm = m0 + r, gk = k0 + kk;
-                ra[u] = (gm < M && gk < kend) ? a[(int64_t)gm * K + gk] : 0.f;
+                ra[u] = (gm < M && gk < kend) ? a[(int64_t)gm * lda + gk] : 0.f;
             }
             if (B_KN) {
                 const int kr = e / 64, c = e % 64, gn = n0 + c, gk = k0 + kr;
@@ -879,8 +881,8 @@ gemm_f32_kernel(const float* __restrict__ a, const float* __restrict__ b, const 
     auto finish = [&](int m, int n, float v) {
         if (m >= M || n >= N) return;
         if (bias) v += bias[n];
-        if (resid) v += resid[(int64_t)m * N + n];
-        y[(int64_t)m * N + n] = v;
+        if (resid) v += resid[(int64_t)m * ldy + n];
+        y[(int64_t)m * ldy + n] = v;
     };
     if (S == 1) {
 #pragma unroll
@@ -918,7 +920,7 @@ gemm_f32_kernel(const float* __restrict__ a, const float* __restrict__ b, const 
 // the output tiles alone would leave most SMs idle.
 template <bool B_KN>
 static int launch_gemm_f32(tb_ctx* ctx, const float* a, const float* b, const float* bias, const float* resid, float* y,
-                           int M, int N, int K) {
+                           int M, int N, int K, int64_t lda, int64_t ldy) {
     const int tiles = ((N + 63) / 64) * ((M + 63) / 64);
     int S = 1;
     while (S < 8 && tiles * S * 2 <= ctx->num_sms && K / (S * 2) >= 64) S *= 2;
@@ -934,7 +936,7 @@ static int launch_gemm_f32(tb_ctx* ctx, const float* a, const float* b, const fl
     attr[0].val.clusterDim.z = S;
     lc.attrs = attr;
     lc.numAttrs = 1;
-    TB_CUDA_TRY(ctx, cudaLaunchKernelEx(&lc, gemm_f32_kernel<B_KN>, a, b, bias, resid, y, M, N, K, kps));
+    TB_CUDA_TRY(ctx, cudaLaunchKernelEx(&lc, gemm_f32_kernel<B_KN>, a, b, bias, resid, y, M, N, K, kps, lda, ldy));
     return check_launch(ctx, "gemm_f32");
 }
 
@@ -942,7 +944,7 @@ static int launch_gemm_f32(tb_ctx* ctx, const float* a, const float* b, const fl
 template <int BN, int STAGES, bool B_MN>
 static int launch_gemm_tc(tb_ctx* ctx, const void* a, const void* b, const Epi& ep, int M, int N, int K) {
     CUtensorMap ta, tbm;
-    int rc = make_tmap_2d(ctx, &ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a, M, K, K, 64, GEMM_BM);
+    int rc = make_tmap_2d(ctx, &ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a, M, K, ep.x_ld ? ep.x_ld : K, 64, GEMM_BM);
     if (rc) return rc;
     if (!B_MN) rc = make_tmap_2d(ctx, &tbm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, b, N, K, K, 64, BN);
     else rc = make_tmap_2d(ctx, &tbm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, b, K, N, N, 64, 64);
@@ -1055,12 +1057,12 @@ int linear_launch(tb_ctx* ctx, int int8, const void* x, const void* w, const Epi
             (ep.rope_tab && (M > 64 || ep.rope_s_new <= 0)) || (!ep.rope_tab && (M <= 64 || int8)))
             return set_error(ctx, TB_ERR_UNSUPPORTED, "linear: permuted QKV epilogue configuration");
     }
-    if (ep.norm_w || (ep.x_ld && ep.x_ld != K)) {
-        if (M > 64 || K % 8 || ep.x_ld % 8 || (reinterpret_cast<uintptr_t>(x) & 15) ||
-            (reinterpret_cast<uintptr_t>(ep.norm_w) & 15))
-            return set_error(ctx, TB_ERR_UNSUPPORTED,
-                             "linear: fused norm / strided rows need <= 64 tokens, K and row stride %% 8, 16-B alignment");
-    }
+    if (ep.norm_w && (M > 64 || K % 8 || ep.x_ld % 8 || (reinterpret_cast<uintptr_t>(x) & 15) ||
+                      (reinterpret_cast<uintptr_t>(ep.norm_w) & 15)))
+        return set_error(ctx, TB_ERR_UNSUPPORTED,
+                         "linear: fused norm needs <= 64 tokens, K and row stride %% 8, 16-B alignment");
+    if (ep.x_ld && ep.x_ld != K && (ep.x_ld < K || ep.x_ld % 8 || (reinterpret_cast<uintptr_t>(x) & 15)))
+        return set_error(ctx, TB_ERR_ALIGN, "linear: row stride of x must be >= K and a multiple of 8 elements");
     if (int8) {
         if (M > 64) return set_error(ctx, TB_ERR_UNSUPPORTED, "int8 linear: at most 64 tokens");
         return dispatch_gemv<true>(ctx, x, w, ep, M, N, K);
@@ -1076,25 +1078,30 @@ using namespace tb;
 
 extern "C" {
 
-int tb_linear_fwd(tb_ctx* ctx, int dtype, const void* x, const void* w, const float* bias,
-                  const void* residual, void* y, int64_t M, int64_t N, int64_t K, int flags) {
+int tb_linear_fwd_strided(tb_ctx* ctx, int dtype, const void* x, int64_t ldx, const void* w, const float* bias,
+                          const void* residual, void* y, int64_t ldy, int64_t M, int64_t N, int64_t K, int flags) {
     if (!ctx || !x || !w || !y) return TB_ERR_ARG;
     TB_REQUIRE(ctx, M >= 0 && N > 0 && K > 0 && M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31),
                TB_ERR_SHAPE, "linear: bad shape M=%lld N=%lld K=%lld", (long long)M, (long long)N, (long long)K);
+    const bool swiglu = (flags & TB_EPI_SWIGLU) != 0;
+    const int64_t ncols = swiglu ? N / 2 : N;
+    TB_REQUIRE(ctx, ldx >= K && ldy >= ncols, TB_ERR_SHAPE, "linear: row strides ldx=%lld < K or ldy=%lld < %lld",
+               (long long)ldx, (long long)ldy, (long long)ncols);
     if (M == 0) return TB_OK;
     if ((flags & TB_EPI_BIAS) && !bias) return set_error(ctx, TB_ERR_ARG, "linear: TB_EPI_BIAS without bias");
     if ((flags & TB_EPI_RESIDUAL) && !residual) return set_error(ctx, TB_ERR_ARG, "linear: TB_EPI_RESIDUAL without residual");
-    const bool swiglu = (flags & TB_EPI_SWIGLU) != 0;
     if (dtype == TB_F32) {
         if (swiglu) return set_error(ctx, TB_ERR_UNSUPPORTED, "linear f32: SwiGLU epilogue is bf16-only");
         return launch_gemm_f32<false>(ctx, (const float*)x, (const float*)w, (flags & TB_EPI_BIAS) ? bias : nullptr,
                                       (flags & TB_EPI_RESIDUAL) ? (const float*)residual : nullptr, (float*)y, (int)M,
-                                      (int)N, (int)K);
+                                      (int)N, (int)K, ldx, ldy);
     }
     if (dtype != TB_BF16) return set_error(ctx, TB_ERR_UNSUPPORTED, "linear: dtype %d", dtype);
     TB_REQUIRE(ctx, K % 8 == 0 && N % 8 == 0, TB_ERR_SHAPE, "linear bf16: K and N must be multiples of 8");
     TB_REQUIRE(ctx, aligned16(x) && aligned16(w) && aligned16(y) && (!residual || aligned16(residual)),
                TB_ERR_ALIGN, "linear bf16: pointers must be 16-byte aligned");
+    TB_REQUIRE(ctx, ldx % 8 == 0 && ldy % 8 == 0, TB_ERR_ALIGN,
+               "linear bf16: row strides must be multiples of 8 elements (16 bytes)");
     if (swiglu) {
         TB_REQUIRE(ctx, N % 256 == 0, TB_ERR_SHAPE, "linear SwiGLU: N must be a multiple of 256");
         TB_REQUIRE(ctx, !(flags & (TB_EPI_BIAS | TB_EPI_RESIDUAL)), TB_ERR_UNSUPPORTED,
@@ -1103,12 +1110,19 @@ int tb_linear_fwd(tb_ctx* ctx, int dtype, const void* x, const void* w, const fl
     Epi ep{};
     ep.out = y;
     ep.out_f32 = (flags & TB_EPI_OUT_F32) ? 1 : 0;
-    ep.ldo = swiglu ? N / 2 : N;
+    ep.ldo = ldy;
     ep.bias = (flags & TB_EPI_BIAS) ? bias : nullptr;
     ep.resid = (flags & TB_EPI_RESIDUAL) ? residual : nullptr;
-    ep.ldr = N;
+    ep.ldr = ldy;
     ep.swiglu = swiglu ? 1 : 0;
+    ep.x_ld = ldx;
     return linear_launch(ctx, 0, x, w, ep, (int)M, (int)N, (int)K);
+}
+
+int tb_linear_fwd(tb_ctx* ctx, int dtype, const void* x, const void* w, const float* bias,
+                  const void* residual, void* y, int64_t M, int64_t N, int64_t K, int flags) {
+    const int64_t ncols = (flags & TB_EPI_SWIGLU) ? N / 2 : N;
+    return tb_linear_fwd_strided(ctx, dtype, x, K, w, bias, residual, y, ncols, M, N, K, flags);
 }
 
 int tb_matmul_fwd(tb_ctx* ctx, int dtype, const void* a, const void* b, void* c, int64_t M, int64_t N, int64_t K) {
@@ -1118,7 +1132,7 @@ int tb_matmul_fwd(tb_ctx* ctx, int dtype, const void* a, const void* b, void* c,
     if (M == 0) return TB_OK;
     if (dtype == TB_F32) {
         return launch_gemm_f32<true>(ctx, (const float*)a, (const float*)b, nullptr, nullptr, (float*)c, (int)M, (int)N,
-                                     (int)K);
+                                     (int)K, K, N);
     }
     if (dtype != TB_BF16) return set_error(ctx, TB_ERR_UNSUPPORTED, "matmul: dtype %d", dtype);
     TB_REQUIRE(ctx, K % 8 == 0 && N % 8 == 0, TB_ERR_SHAPE, "matmul bf16: K and N must be multiples of 8");

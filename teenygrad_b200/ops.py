@@ -155,6 +155,38 @@ def linear(x, w, bias=None, residual=None, swiglu=False, out_f32=False):
     return y
 
 
+TB_OP = {"linear": 0, "matmul": 1, "int8_linear": 2, "rmsnorm": 3, "layernorm": 4, "act": 5, "attn": 6,
+         "conv2d": 7, "quantize_int8": 8}
+
+
+def output_row_stride(op, dtype, row_elems):
+    """RuntimeOp::forward_output_row_stride (core/teeny-core/src/model/mod.rs:100):
+    the row stride an executor allocates for the op's output rows."""
+    out = ctypes.c_int64(0)
+    dt = _DT[dtype] if isinstance(dtype, torch.dtype) else dtype
+    check(None, lib().tb_output_row_stride(ctypes.c_int(TB_OP[op]), ctypes.c_int(dt), _i64(row_elems), ctypes.byref(out)))
+    return out.value
+
+
+def linear_padded(x, w, bias=None):
+    """LinearForward as the reference executor runs it (nn/mlp/linear.rs:251-300):
+    the output buffer's rows are padded to 16 bytes (output_row_stride) and the
+    kernel writes the first N columns of each.  Returns (buffer [M, stride], y view [M, N])."""
+    _cuda(x, w, bias)
+    K = x.shape[-1]
+    M = x.numel() // K
+    N = w.shape[0]
+    ld = output_row_stride("linear", x.dtype, N)
+    buf = torch.full((M, ld), float("nan"), device=x.device, dtype=x.dtype)
+    if bias is not None and bias.dtype != torch.float32:
+        bias = bias.float().contiguous()
+    ctx = context()
+    check(ctx, lib().tb_linear_fwd_strided(ctx, _dt(x), _p(x), _i64(K), _p(w), _p(bias), _p(None), _p(buf), _i64(ld),
+                                           _i64(M), _i64(N), _i64(K),
+                                           ctypes.c_int(TB_EPI_BIAS if bias is not None else 0)))
+    return buf, buf[:, :N]
+
+
 def interleave_gate_up(w_gate, w_up, block=128):
     """[F, K] gate and up weights -> [2F, K] in the (gate block, up block) order
     the fused SwiGLU epilogue expects."""

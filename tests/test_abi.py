@@ -56,3 +56,19 @@ def test_no_oracle_import_in_product():
                 src = open(os.path.join(dirpath, f)).read()
                 assert not re.search(r"^\s*(import|from)\s+oracle", src, flags=re.M), f
                 assert "liboracle" not in src, f
+
+
+def test_output_row_stride_and_workspace_need_no_gpu():
+    l = tg.lib()
+    out = ctypes.c_int64(0)
+    # linear rows padded to 16 bytes (LinearForward::forward_output_row_stride)
+    for dt, n, want in ((0, 6, 8), (0, 48, 48), (1, 6, 8), (1, 24, 24), (1, 25, 32)):
+        assert l.tb_output_row_stride(0, dt, ctypes.c_int64(n), ctypes.byref(out)) == 0
+        assert out.value == want, (dt, n, out.value)
+    assert l.tb_output_row_stride(1, 0, ctypes.c_int64(6), ctypes.byref(out)) == 0 and out.value == 6   # matmul: dense
+    assert l.tb_output_row_stride(99, 0, ctypes.c_int64(6), ctypes.byref(out)) != 0
+    b = ctypes.c_size_t(123)
+    shape = (ctypes.c_int64 * 9)(32, 64, 64, 56, 56, 3, 3, 1, 1)
+    assert l.tb_workspace_bytes(7, 1, shape, 9, ctypes.byref(b)) == 0 and b.value > 32 * 56 * 56 * 64 * 2
+    assert l.tb_workspace_bytes(7, 0, shape, 9, ctypes.byref(b)) == 0 and b.value == 0   # f32 conv: none
+    assert l.tb_workspace_bytes(0, 1, None, 0, ctypes.byref(b)) == 0 and b.value == 0    # linear: none

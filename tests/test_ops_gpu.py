@@ -154,6 +154,45 @@ def test_linear_bf16_decode_gemv(M, N, K):
     assert torch.equal(y, y2)
 
 
+def test_linear_padded_output_rows_f32():
+    # the reference executor gives LinearForward an output whose rows are padded to 16
+    # bytes (N = 6 f32 -> stride 8) and the kernel writes only the first N columns
+    r = rng(21)
+    x = r.standard_normal((64, 64)).astype(np.float32)
+    w = r.standard_normal((6, 64)).astype(np.float32)
+    b = r.standard_normal(6).astype(np.float32)
+    buf, y = ops().linear_padded(to_gpu(x), to_gpu(w), to_gpu(b))
+    assert buf.shape == (64, 8)
+    assert_close(np_of(y), oracle.linear(x, w, b), F32_TOL)
+    assert torch.isnan(buf[:, 6:]).all()
+
+
+@pytest.mark.parametrize("M", [16, 256])
+def test_linear_strided_bf16(M):
+    # x rows read from a wider buffer (ldx > K), y rows written into a wider one
+    # (ldy > N): the decode GEMV (M = 16) and the tensor-core GEMM (M = 256)
+    from teenygrad_b200 import _lib
+    import ctypes
+    r = rng(M + 5)
+    K, N, ldx, ldy = 256, 48, 320, 64
+    xw = bf16_round(r.standard_normal((M, ldx)))
+    w = bf16_round(r.standard_normal((N, K)) * 0.05)
+    bias = r.standard_normal(N).astype(np.float32)
+    xg = to_gpu(xw, torch.bfloat16)
+    wg = to_gpu(w, torch.bfloat16)
+    bg = to_gpu(bias)
+    y = torch.full((M, ldy), 7.0, device="cuda", dtype=torch.bfloat16)
+    ctx = ops().context()
+    _lib.check(ctx, _lib.lib().tb_linear_fwd_strided(ctx, 1, ctypes.c_void_p(xg.data_ptr()), ctypes.c_int64(ldx),
+                                                     ctypes.c_void_p(wg.data_ptr()), ctypes.c_void_p(bg.data_ptr()),
+                                                     None, ctypes.c_void_p(y.data_ptr()), ctypes.c_int64(ldy),
+                                                     ctypes.c_int64(M), ctypes.c_int64(N), ctypes.c_int64(K),
+                                                     ctypes.c_int(1)))
+    torch.cuda.synchronize()
+    assert_close(np_of(y[:, :N]), oracle.linear(xw[:, :K], w, bias), BF16_TOL)
+    assert (y[:, N:] == 7.0).all()
+
+
 def test_matmul():
     r = rng(11)
     a = r.standard_normal((70, 96)).astype(np.float32)
