@@ -108,7 +108,8 @@ TB_API int tb_add_fwd(tb_ctx* ctx, int dtype, const void* a, const void* b, void
 /* Operator ids for the queries below. */
 typedef enum tb_op {
     TB_OP_LINEAR = 0, TB_OP_MATMUL = 1, TB_OP_INT8_LINEAR = 2, TB_OP_RMSNORM = 3, TB_OP_LAYERNORM = 4,
-    TB_OP_ACT = 5, TB_OP_ATTN = 6, TB_OP_CONV2D = 7, TB_OP_QUANTIZE_INT8 = 8
+    TB_OP_ACT = 5, TB_OP_ATTN = 6, TB_OP_CONV2D = 7, TB_OP_QUANTIZE_INT8 = 8,
+    TB_OP_RMSNORM_BWD = 9, TB_OP_LINEAR_BWD = 10, TB_OP_ATTN_BWD = 11, TB_OP_CONV2D_BWD = 12
 } tb_op;
 /* Row stride (elements) an executor should allocate for an op's output rows
  * of row_elems elements: RuntimeOp::forward_output_row_stride
@@ -116,9 +117,10 @@ typedef enum tb_op {
  * reference pads rows to 16 bytes (LinearForward, nn/mlp/linear.rs:267-272),
  * every other op writes dense rows.  Needs no GPU. */
 TB_API int tb_output_row_stride(int op, int dtype, int64_t row_elems, int64_t* stride);
-/* Device workspace an op needs, in bytes (0 for all but the bf16
- * tensor-core conv2d).  shape: TB_OP_CONV2D {B, Cin, Cout, H, W, KH, KW,
- * stride, pad}; ignored for the others.  Needs no GPU. */
+/* Device workspace an op needs, in bytes.  shape: TB_OP_CONV2D {B, Cin,
+ * Cout, H, W, KH, KW, stride, pad} (bf16 tensor-core path only);
+ * TB_OP_RMSNORM_BWD {M, N}; TB_OP_LINEAR_BWD {M, N, K}; TB_OP_ATTN_BWD
+ * {B, Hq, Sq}; ignored for the others (no workspace).  Needs no GPU. */
 TB_API int tb_workspace_bytes(int op, int dtype, const int64_t* shape, int n_shape, size_t* bytes);
 
 /* ------------------------------------------------------------- linear --- */
@@ -197,6 +199,38 @@ TB_API int tb_bn_fold(tb_ctx* ctx, const float* gamma, const float* beta, const 
 TB_API int tb_batchnorm_fwd(tb_ctx* ctx, int dtype, const void* x, const float* gamma, const float* beta,
                             const float* mean, const float* var, void* y, int64_t B, int64_t C, int64_t HW,
                             float eps);
+
+/* ----------------------------------------------------------- backward --- */
+/* Gradients for the reference's training executor (LoadedModel::backward,
+ * drivers/teeny-cuda/src/model/mod.rs:963).  dtype TB_F32 or TB_BF16 for the
+ * tensors; f32 math; deterministic (fixed-order reductions, no atomics). */
+
+/* rms_norm_backward (nn/norm/rmsnorm.rs:125-277): dx[m,n] = rrms[m] *
+ * (w[n] dy[m,n] - x[m,n] rrms[m]^2 sum_n(dy w x) / N); dw (f32 [N], may be
+ * NULL) accumulates sum_m dy x rrms, as the reference's dweight does.  rrms
+ * is the forward's f32 [M] output.  Workspace: tb_workspace_bytes
+ * (TB_OP_RMSNORM_BWD, {M, N}) when dw is given. */
+TB_API int tb_rmsnorm_bwd(tb_ctx* ctx, int dtype, const void* dy, const void* x, const void* w, const float* rrms,
+                          void* dx, float* dw, int64_t M, int64_t N, void* workspace, size_t workspace_bytes);
+/* linear_backward (nn/mlp/linear.rs:119-249) of y = x w^T + b: dx = dy w
+ * [M, K], dw = dy^T x [N, K] (dtype; either may be NULL), db = sum_m dy
+ * (f32 [N], may be NULL).  TB_BF16 on the tensor cores (M, N, K multiples of
+ * 8); TB_F32 exact.  Workspace: TB_OP_LINEAR_BWD {M, N, K}. */
+TB_API int tb_linear_bwd(tb_ctx* ctx, int dtype, const void* x, const void* w, const void* dy, void* dx, void* dw,
+                         float* db, int64_t M, int64_t N, int64_t K, void* workspace, size_t workspace_bytes);
+/* flash_attention2_backward_dq / _dkv (nn/attention/flash_attn2.rs:160-447)
+ * with the forward's causal mask and GQA: dq [B, Hq, Sq, D], dk / dv
+ * [B, Hkv, Sk, D] (summed over each kv head's query heads).  o and lse are
+ * the forward's outputs (lse f32 [B, Hq, Sq]).  D <= 128.  Workspace:
+ * TB_OP_ATTN_BWD {B, Hq, Sq}. */
+TB_API int tb_attn_bwd(tb_ctx* ctx, int dtype, const void* q, const void* k, const void* v, const void* o,
+                       const void* dout, const float* lse, void* dq, void* dk, void* dv, int B, int Hq, int Hkv, int Sq,
+                       int Sk, int D, float scale, int causal, void* workspace, size_t workspace_bytes);
+/* conv2d_backward (nn/conv/conv2d.rs:395-521), groups = 1, zero padding:
+ * dx [B, Cin, H, W] and dw [Cout, Cin, KH, KW] (either may be NULL), both
+ * written (not accumulated).  KH * KW <= 49.  No workspace. */
+TB_API int tb_conv2d_bwd(tb_ctx* ctx, int dtype, const void* dy, const void* x, const void* w, void* dx, void* dw,
+                         int B, int Cin, int Cout, int H, int W, int KH, int KW, int stride, int pad);
 
 /* ------------------------------------------------------------ decoder --- */
 /* RoPE, rotate-half pairing (d, d + D/2), inv_freq = theta^(-2i/D).

@@ -278,3 +278,48 @@ def quantize_int8_numpy(w):
         r = np.where(np.isnan(r), 0.0, r)
     q = np.clip(r, -127, 127).astype(np.int8)
     return q, scale
+
+
+# -------------------------------------------------------------- backward ----
+def rmsnorm_bwd(dy, x, w, rrms, dw=None):
+    """dx and dw (accumulated into a copy of dw, zeros if None); rmsnorm.rs:125-277."""
+    dy, x, w, rrms = map(_f32, (dy, x, w, rrms))
+    M, N = x.shape
+    dx = np.empty_like(x)
+    dwo = np.zeros(N, np.float32) if dw is None else np.array(dw, dtype=np.float32, copy=True)
+    lib().or_rmsnorm_bwd(_p(dy), _p(x), _p(w), _p(rrms), _p(dx), _p(dwo), _I64(M), _I64(N))
+    return dx, dwo
+
+
+def linear_bwd(x, w, dy):
+    """(dx, dw, db) of y = x w^T + b; linear.rs:119-249."""
+    x, w, dy = map(_f32, (x, w, dy))
+    M, K = x.shape
+    N = w.shape[0]
+    dx = np.empty((M, K), np.float32)
+    dw = np.empty((N, K), np.float32)
+    db = np.empty(N, np.float32)
+    lib().or_linear_bwd(_p(x), _p(w), _p(dy), _p(dx), _p(dw), _p(db), _I64(M), _I64(N), _I64(K))
+    return dx, dw, db
+
+
+def attention_bwd(q, k, v, o, do, lse, scale, causal):
+    """(dq, dk, dv); flash_attn2.rs:160-447 plus causal / GQA."""
+    q, k, v, o, do, lse = map(_f32, (q, k, v, o, do, lse))
+    B, Hq, Sq, D = q.shape
+    Hkv, Sk = k.shape[1], k.shape[2]
+    dq, dk, dv = np.empty_like(q), np.empty_like(k), np.empty_like(v)
+    lib().or_attention_bwd(_p(q), _p(k), _p(v), _p(o), _p(do), _p(lse), _p(dq), _p(dk), _p(dv), _I64(B), _I64(Hq),
+                           _I64(Hkv), _I64(Sq), _I64(Sk), _I64(D), ctypes.c_float(scale), ctypes.c_int(int(causal)))
+    return dq, dk, dv
+
+
+def conv2d_bwd(dy, x, w, stride=1, pad=0):
+    """(dx, dw); conv2d.rs:395-521 (groups = 1)."""
+    dy, x, w = map(_f32, (dy, x, w))
+    B, Cin, H, W = x.shape
+    Cout, _, KH, KW = w.shape
+    dx, dw = np.empty_like(x), np.empty_like(w)
+    lib().or_conv2d_bwd(_p(dy), _p(x), _p(w), _p(dx), _p(dw), _I64(B), _I64(Cin), _I64(Cout), _I64(H), _I64(W),
+                        _I64(KH), _I64(KW), _I64(stride), _I64(pad))
+    return dx, dw

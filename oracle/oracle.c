@@ -421,3 +421,181 @@ void or_argmax(const float* x, int32_t* out, int64_t M, int64_t N) {
         out[m] = (int32_t)best;
     }
 }
+
+/* ========================================================== backward ===== */
+
+/* rms_norm_backward, kernels/teeny-kernels/src/nn/norm/rmsnorm.rs:125-277:
+ *   dot    = sum_n dy[m,n] * w[n] * x[m,n]
+ *   dx[m,n] = rrms[m] * (w[n] * dy[m,n] - x[m,n] * rrms[m]^2 * dot / N)
+ *   dw[n] += sum_m dy[m,n] * x[m,n] * rrms[m]       (accumulated into dw)
+ * rrms[m] is the forward's 1 / sqrt(mean(x^2) + eps).  dx is the gradient of
+ * y = x * rrms * w; the reference's dx line (rmsnorm.rs:232) also multiplies
+ * the correction term by w[n], which agrees with it only where w[n] == 1. */
+void or_rmsnorm_bwd(const float* dy, const float* x, const float* w, const float* rrms, float* dx, float* dw,
+                    int64_t M, int64_t N) {
+#pragma omp parallel for schedule(static)
+    for (int64_t m = 0; m < M; m++) {
+        const float* xr = x + m * N;
+        const float* dr = dy + m * N;
+        double dot = 0.0;
+        for (int64_t n = 0; n < N; n++) dot += (double)dr[n] * (double)w[n] * (double)xr[n];
+        const double r = (double)rrms[m], sc = dot / (double)N;
+        for (int64_t n = 0; n < N; n++)
+            dx[m * N + n] = (float)(r * ((double)w[n] * (double)dr[n] - (double)xr[n] * r * r * sc));
+    }
+    if (dw) {
+#pragma omp parallel for schedule(static)
+        for (int64_t n = 0; n < N; n++) {
+            double acc = 0.0;
+            for (int64_t m = 0; m < M; m++) acc += (double)dy[m * N + n] * (double)x[m * N + n] * (double)rrms[m];
+            dw[n] = (float)((double)dw[n] + acc);
+        }
+    }
+}
+
+/* linear_backward, nn/mlp/linear.rs:119-249 (y = x w^T + b):
+ *   dx = dy w   [M, K];   dw = dy^T x   [N, K];   db = sum_m dy   [N]. */
+void or_linear_bwd(const float* x, const float* w, const float* dy, float* dx, float* dw, float* db, int64_t M,
+                   int64_t N, int64_t K) {
+    if (dx) {
+#pragma omp parallel for collapse(2) schedule(static)
+        for (int64_t m = 0; m < M; m++)
+            for (int64_t k = 0; k < K; k++) {
+                double acc = 0.0;
+                for (int64_t n = 0; n < N; n++) acc += (double)dy[m * N + n] * (double)w[n * K + k];
+                dx[m * K + k] = (float)acc;
+            }
+    }
+    if (dw) {
+#pragma omp parallel for collapse(2) schedule(static)
+        for (int64_t n = 0; n < N; n++)
+            for (int64_t k = 0; k < K; k++) {
+                double acc = 0.0;
+                for (int64_t m = 0; m < M; m++) acc += (double)dy[m * N + n] * (double)x[m * K + k];
+                dw[n * K + k] = (float)acc;
+            }
+    }
+    if (db) {
+        for (int64_t n = 0; n < N; n++) {
+            double acc = 0.0;
+            for (int64_t m = 0; m < M; m++) acc += (double)dy[m * N + n];
+            db[n] = (float)acc;
+        }
+    }
+}
+
+/* flash_attention2_backward_dq / _dkv, nn/attention/flash_attn2.rs:160-447,
+ * extended (as the forward) with the causal mask and GQA:
+ *   p_ij  = exp(q_i . k_j * scale - L_i)          (L: the forward's LSE)
+ *   D_i   = sum_d O_i[d] dO_i[d]
+ *   dS_ij = p_ij (dO_i . v_j - D_i)
+ *   dQ_i  = scale * sum_j dS_ij k_j;  dK_j = scale * sum_i dS_ij q_i;  dV_j = sum_i p_ij dO_i
+ * with dK / dV of a kv head summed over the query heads of its group. */
+void or_attention_bwd(const float* q, const float* k, const float* v, const float* o, const float* dout,
+                      const float* lse, float* dq, float* dk, float* dv, int64_t B, int64_t Hq, int64_t Hkv,
+                      int64_t Sq, int64_t Sk, int64_t D, float scale, int causal) {
+    const int64_t group = Hq / Hkv;
+    double* acc_k = (double*)calloc((size_t)(B * Hkv * Sk * D), sizeof(double));
+    double* acc_v = (double*)calloc((size_t)(B * Hkv * Sk * D), sizeof(double));
+    for (int64_t b = 0; b < B; b++) {
+#pragma omp parallel for schedule(static)
+        for (int64_t hk = 0; hk < Hkv; hk++) {
+            for (int64_t h = hk * group; h < (hk + 1) * group; h++) {
+                for (int64_t i = 0; i < Sq; i++) {
+                    const float* qr = q + ((b * Hq + h) * Sq + i) * D;
+                    const float* orow = o + ((b * Hq + h) * Sq + i) * D;
+                    const float* dor = dout + ((b * Hq + h) * Sq + i) * D;
+                    const float* kb = k + (b * Hkv + hk) * Sk * D;
+                    const float* vb = v + (b * Hkv + hk) * Sk * D;
+                    double* akb = acc_k + (b * Hkv + hk) * Sk * D;
+                    double* avb = acc_v + (b * Hkv + hk) * Sk * D;
+                    int64_t jmax = causal ? i + (Sk - Sq) : Sk - 1;
+                    if (jmax > Sk - 1) jmax = Sk - 1;
+                    const double L = (double)lse[(b * Hq + h) * Sq + i];
+                    double Di = 0.0;
+                    for (int64_t d = 0; d < D; d++) Di += (double)orow[d] * (double)dor[d];
+                    double* dqa = (double*)calloc((size_t)D, sizeof(double));
+                    for (int64_t j = 0; j <= jmax; j++) {
+                        double s = 0.0, dp = 0.0;
+                        for (int64_t d = 0; d < D; d++) {
+                            s += (double)qr[d] * (double)kb[j * D + d];
+                            dp += (double)dor[d] * (double)vb[j * D + d];
+                        }
+                        const double p = exp(s * (double)scale - L);
+                        const double ds = p * (dp - Di);
+                        for (int64_t d = 0; d < D; d++) {
+                            dqa[d] += ds * (double)kb[j * D + d];
+                            akb[j * D + d] += ds * (double)qr[d];
+                            avb[j * D + d] += p * (double)dor[d];
+                        }
+                    }
+                    float* dqr = dq + ((b * Hq + h) * Sq + i) * D;
+                    for (int64_t d = 0; d < D; d++) dqr[d] = (float)(dqa[d] * (double)scale);
+                    free(dqa);
+                }
+            }
+        }
+    }
+    for (int64_t e = 0; e < B * Hkv * Sk * D; e++) {
+        dk[e] = (float)(acc_k[e] * (double)scale);
+        dv[e] = (float)acc_v[e];
+    }
+    free(acc_k);
+    free(acc_v);
+}
+
+/* conv2d_backward, nn/conv/conv2d.rs:395-521 (groups = 1, zero padding):
+ *   dx[b,ci,ih,iw] = sum_{co,kh,kw} dy[b,co,oh,ow] w[co,ci,kh,kw]
+ *                    over oh*stride + kh - pad = ih, ow*stride + kw - pad = iw
+ *   dw[co,ci,kh,kw] = sum_{b,oh,ow} dy[b,co,oh,ow] x[b,ci,oh*stride+kh-pad,ow*stride+kw-pad]
+ * The reference scatters both with atomic adds; this restatement gathers. */
+void or_conv2d_bwd(const float* dy, const float* x, const float* w, float* dx, float* dw, int64_t B, int64_t Cin,
+                   int64_t Cout, int64_t H, int64_t W, int64_t KH, int64_t KW, int64_t stride, int64_t pad) {
+    const int64_t OH = (H + 2 * pad - KH) / stride + 1, OW = (W + 2 * pad - KW) / stride + 1;
+    if (dx) {
+#pragma omp parallel for collapse(2) schedule(static)
+        for (int64_t b = 0; b < B; b++)
+            for (int64_t ci = 0; ci < Cin; ci++)
+                for (int64_t ih = 0; ih < H; ih++)
+                    for (int64_t iw = 0; iw < W; iw++) {
+                        double acc = 0.0;
+                        for (int64_t co = 0; co < Cout; co++)
+                            for (int64_t kh = 0; kh < KH; kh++) {
+                                const int64_t th = ih + pad - kh;
+                                if (th < 0 || th % stride) continue;
+                                const int64_t oh = th / stride;
+                                if (oh >= OH) continue;
+                                for (int64_t kw = 0; kw < KW; kw++) {
+                                    const int64_t tw = iw + pad - kw;
+                                    if (tw < 0 || tw % stride) continue;
+                                    const int64_t ow = tw / stride;
+                                    if (ow >= OW) continue;
+                                    acc += (double)dy[((b * Cout + co) * OH + oh) * OW + ow] *
+                                           (double)w[((co * Cin + ci) * KH + kh) * KW + kw];
+                                }
+                            }
+                        dx[((b * Cin + ci) * H + ih) * W + iw] = (float)acc;
+                    }
+    }
+    if (dw) {
+#pragma omp parallel for collapse(2) schedule(static)
+        for (int64_t co = 0; co < Cout; co++)
+            for (int64_t ci = 0; ci < Cin; ci++)
+                for (int64_t kh = 0; kh < KH; kh++)
+                    for (int64_t kw = 0; kw < KW; kw++) {
+                        double acc = 0.0;
+                        for (int64_t b = 0; b < B; b++)
+                            for (int64_t oh = 0; oh < OH; oh++) {
+                                const int64_t ih = oh * stride + kh - pad;
+                                if (ih < 0 || ih >= H) continue;
+                                for (int64_t ow = 0; ow < OW; ow++) {
+                                    const int64_t iw = ow * stride + kw - pad;
+                                    if (iw < 0 || iw >= W) continue;
+                                    acc += (double)dy[((b * Cout + co) * OH + oh) * OW + ow] *
+                                           (double)x[((b * Cin + ci) * H + ih) * W + iw];
+                                }
+                            }
+                        dw[((co * Cin + ci) * KH + kh) * KW + kw] = (float)acc;
+                    }
+    }
+}

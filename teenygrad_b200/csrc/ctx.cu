@@ -164,6 +164,10 @@ int tb_output_row_stride(int op, int dtype, int64_t row_elems, int64_t* stride) 
         case TB_OP_ATTN:
         case TB_OP_CONV2D:
         case TB_OP_QUANTIZE_INT8:
+        case TB_OP_RMSNORM_BWD:
+        case TB_OP_LINEAR_BWD:
+        case TB_OP_ATTN_BWD:
+        case TB_OP_CONV2D_BWD:
             *stride = row_elems;   // dense rows
             return TB_OK;
         default: return TB_ERR_ARG;
@@ -189,6 +193,11 @@ int tb_workspace_bytes(int op, int dtype, const int64_t* shape, int n_shape, siz
         case TB_OP_ATTN:
         case TB_OP_QUANTIZE_INT8:
             return TB_OK;   // no workspace: split-K and attention splits reduce on chip
+        case TB_OP_RMSNORM_BWD:
+        case TB_OP_LINEAR_BWD:
+        case TB_OP_ATTN_BWD:
+        case TB_OP_CONV2D_BWD:
+            return tb_backward_workspace_bytes(op, dtype, shape, n_shape, bytes);
         default: return TB_ERR_ARG;
     }
 }

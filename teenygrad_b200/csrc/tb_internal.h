@@ -47,6 +47,13 @@ int make_tmap_2d(tb_ctx* ctx, CUtensorMap* out, CUtensorMapDataType dt, int elem
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+}  // namespace tb
+
+// Workspace of the backward ops (backward.cu); tb_workspace_bytes forwards to it.
+extern "C" int tb_backward_workspace_bytes(int op, int dtype, const int64_t* shape, int n_shape, size_t* bytes);
+
+namespace tb {
+
 // cudaLaunchKernelEx on ctx->stream; adds the programmatic-serialization
 // attribute when ctx->pdl is set (the kernel must call pdl_wait()).
 template <typename... KArgs, typename... Args>

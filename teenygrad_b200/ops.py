@@ -387,3 +387,77 @@ def conv2d(x, w, bias=None, scale=None, shift=None, stride=1, pad=0, act=None):
 
 class Conv2dBiasForward(_Op):
     fn = staticmethod(conv2d)
+
+
+# --------------------------------------------------------------- backward ---
+def _workspace(op, dtype, shape, device):
+    n = ctypes.c_size_t(0)
+    arr = (ctypes.c_int64 * len(shape))(*shape)
+    check(None, lib().tb_workspace_bytes(ctypes.c_int(TB_OP[op]), ctypes.c_int(dtype), arr, ctypes.c_int(len(shape)),
+                                         ctypes.byref(n)))
+    return torch.empty(max(n.value, 16), dtype=torch.uint8, device=device), n.value
+
+
+TB_OP.update({"rmsnorm_bwd": 9, "linear_bwd": 10, "attn_bwd": 11, "conv2d_bwd": 12})
+
+
+def rms_norm_backward(dy, x, w, rrms, dw=None):
+    """rms_norm_backward (nn/norm/rmsnorm.rs:125-277): returns (dx, dw); dw (f32 [N])
+    accumulates into the given tensor (zeros when None)."""
+    _cuda(dy, x, w, rrms, dw)
+    N = x.shape[-1]
+    M = x.numel() // N
+    dx = torch.empty_like(x)
+    if dw is None:
+        dw = torch.zeros(N, device=x.device, dtype=torch.float32)
+    ws, nb = _workspace("rmsnorm_bwd", _dt(x), (M, N), x.device)
+    ctx = context()
+    check(ctx, lib().tb_rmsnorm_bwd(ctx, _dt(x), _p(dy), _p(x), _p(w), _p(rrms), _p(dx), _p(dw), _i64(M), _i64(N),
+                                    _p(ws), ctypes.c_size_t(nb)))
+    return dx, dw
+
+
+def linear_backward(x, w, dy, bias=True):
+    """linear_backward (nn/mlp/linear.rs:119-249): (dx, dw, db) of y = x w^T + b."""
+    _cuda(x, w, dy)
+    K = x.shape[-1]
+    M = x.numel() // K
+    N = w.shape[0]
+    dx = torch.empty_like(x)
+    dw = torch.empty_like(w)
+    db = torch.empty(N, device=x.device, dtype=torch.float32) if bias else None
+    ws, nb = _workspace("linear_bwd", _dt(x), (M, N, K), x.device)
+    ctx = context()
+    check(ctx, lib().tb_linear_bwd(ctx, _dt(x), _p(x), _p(w), _p(dy), _p(dx), _p(dw), _p(db), _i64(M), _i64(N),
+                                   _i64(K), _p(ws), ctypes.c_size_t(nb)))
+    return dx, dw, db
+
+
+def attention_backward(q, k, v, o, do, lse, scale=None, causal=False):
+    """flash_attention2_backward_dq / _dkv (nn/attention/flash_attn2.rs:160-447)
+    with causal masking and GQA: returns (dq, dk, dv)."""
+    _cuda(q, k, v, o, do, lse)
+    B, Hq, Sq, D = q.shape
+    Hkv, Sk = k.shape[1], k.shape[2]
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    ws, nb = _workspace("attn_bwd", _dt(q), (B, Hq, Sq), q.device)
+    ctx = context()
+    check(ctx, lib().tb_attn_bwd(ctx, _dt(q), _p(q), _p(k), _p(v), _p(o), _p(do), _p(lse), _p(dq), _p(dk), _p(dv),
+                                 ctypes.c_int(B), ctypes.c_int(Hq), ctypes.c_int(Hkv), ctypes.c_int(Sq), ctypes.c_int(Sk),
+                                 ctypes.c_int(D), _f(scale), ctypes.c_int(int(causal)), _p(ws), ctypes.c_size_t(nb)))
+    return dq, dk, dv
+
+
+def conv2d_backward(dy, x, w, stride=1, pad=0):
+    """conv2d_backward (nn/conv/conv2d.rs:395-521), groups = 1: returns (dx, dw)."""
+    _cuda(dy, x, w)
+    B, Cin, H, W = x.shape
+    Cout, _, KH, KW = w.shape
+    dx, dw = torch.empty_like(x), torch.empty_like(w)
+    ctx = context()
+    check(ctx, lib().tb_conv2d_bwd(ctx, _dt(x), _p(dy), _p(x), _p(w), _p(dx), _p(dw), ctypes.c_int(B),
+                                   ctypes.c_int(Cin), ctypes.c_int(Cout), ctypes.c_int(H), ctypes.c_int(W),
+                                   ctypes.c_int(KH), ctypes.c_int(KW), ctypes.c_int(stride), ctypes.c_int(pad)))
+    return dx, dw

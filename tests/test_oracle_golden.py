@@ -191,3 +191,108 @@ def test_bf16_rounding():
     t = pytest.importorskip("torch")
     r = t.from_numpy(np.random.default_rng(0).standard_normal(4096).astype(np.float32))
     np.testing.assert_array_equal(oracle.round_bf16(r.numpy()), r.bfloat16().float().numpy())
+
+
+# ---------------------------------------------------------------- backward --
+def _rel(got, ref):
+    return float(np.abs(got - ref).max()) / max(1.0, float(np.abs(ref).max()))
+
+
+def test_attention_bwd_oracle_golden():
+    # fixtures: BH 4, N 8, HD 64, non-causal (generate.py:701-747); tolerance of test_flash_attn2.rs
+    sh = (1, 4, 8, 64)
+    q, k, v = (load("flash_attn2", f, sh) for f in ("q.bin", "k.bin", "v.bin"))
+    o = load("flash_attn2", "expected_forward_o.bin", sh)
+    lse = load("flash_attn2", "expected_forward_l.bin", (1, 4, 8))
+    do = load("flash_attn2", "do.bin", sh)
+    dq, dk, dv = oracle.attention_bwd(q, k, v, o, do, lse, 0.125, False)
+    assert _rel(dq, load("flash_attn2", "expected_backward_dq.bin", sh)) < 1e-4
+    assert _rel(dk, load("flash_attn2", "expected_backward_dk.bin", sh)) < 1e-4
+    assert _rel(dv, load("flash_attn2", "expected_backward_dv.bin", sh)) < 1e-4
+
+
+def test_attention_bwd_oracle_causal_gqa_vs_torch():
+    torch = pytest.importorskip("torch")
+    r = np.random.default_rng(3)
+    B, Hq, Hkv, Sq, Sk, D = 2, 4, 2, 9, 13, 16
+    q = r.standard_normal((B, Hq, Sq, D)).astype(np.float32)
+    k = r.standard_normal((B, Hkv, Sk, D)).astype(np.float32)
+    v = r.standard_normal((B, Hkv, Sk, D)).astype(np.float32)
+    do = r.standard_normal((B, Hq, Sq, D)).astype(np.float32)
+    o, lse = oracle.attention(q, k, v, 0.25, True)
+    dq, dk, dv = oracle.attention_bwd(q, k, v, o, do, lse, 0.25, True)
+    tq, tk, tv = (torch.from_numpy(a).double().requires_grad_(True) for a in (q, k, v))
+    kk, vv = tk.repeat_interleave(Hq // Hkv, 1), tv.repeat_interleave(Hq // Hkv, 1)
+    s = tq @ kk.transpose(-1, -2) * 0.25
+    mask = torch.ones(Sq, Sk, dtype=torch.bool).tril(Sk - Sq)
+    s = s.masked_fill(~mask, float("-inf"))
+    (torch.softmax(s, -1) @ vv).backward(torch.from_numpy(do).double())
+    assert _rel(dq, tq.grad.numpy()) < 1e-5
+    assert _rel(dk, tk.grad.numpy()) < 1e-5
+    assert _rel(dv, tv.grad.numpy()) < 1e-5
+
+
+def test_linear_bwd_oracle_golden():
+    x = load("linear", "input.bin", (64, 64))
+    w = load("linear", "weight.bin", (48, 64))
+    dy = load("linear", "dy.bin", (64, 48))
+    dx, dw, db = oracle.linear_bwd(x, w, dy)
+    assert _rel(dx, load("linear", "expected_dx.bin", (64, 64))) < 1e-5
+    assert _rel(dw, load("linear", "expected_dw.bin", (48, 64))) < 1e-5
+    assert _rel(db, load("linear", "expected_db.bin", (48,))) < 1e-5
+
+
+@pytest.mark.parametrize("name,pad,oh", [("conv2d", 0, 6), ("conv2d_padded", 1, 8)])
+def test_conv2d_bwd_oracle_golden(name, pad, oh):
+    x = load(name, "x.bin", (1, 2, 8, 8))
+    w = load(name, "w.bin", (4, 2, 3, 3))
+    dy = load(name, "dy.bin", (1, 4, oh, oh))
+    dx, dw = oracle.conv2d_bwd(dy, x, w, 1, pad)
+    assert _rel(dx, load(name, "expected_dx.bin", (1, 2, 8, 8))) < 1e-5
+    assert _rel(dw, load(name, "expected_dw.bin", (4, 2, 3, 3))) < 1e-5
+
+
+def test_conv2d_bwd_oracle_strided_vs_torch():
+    torch = pytest.importorskip("torch")
+    r = np.random.default_rng(4)
+    x = r.standard_normal((2, 3, 11, 9)).astype(np.float32)
+    w = r.standard_normal((5, 3, 3, 3)).astype(np.float32)
+    tx, tw = torch.from_numpy(x).double().requires_grad_(True), torch.from_numpy(w).double().requires_grad_(True)
+    y = torch.nn.functional.conv2d(tx, tw, stride=2, padding=1)
+    dy = r.standard_normal(tuple(y.shape)).astype(np.float32)
+    y.backward(torch.from_numpy(dy).double())
+    dx, dw = oracle.conv2d_bwd(dy, x, w, 2, 1)
+    assert _rel(dx, tx.grad.numpy()) < 1e-5
+    assert _rel(dw, tw.grad.numpy()) < 1e-5
+
+
+def test_rmsnorm_bwd_oracle_vs_torch():
+    # the reference holds no rmsnorm backward vectors; torch autograd of the
+    # forward formula (rmsnorm.rs:40-122) is the cross-check
+    torch = pytest.importorskip("torch")
+    r = np.random.default_rng(5)
+    x = r.uniform(-2, 2, (16, 128)).astype(np.float32)
+    w = r.uniform(0.5, 1.5, 128).astype(np.float32)
+    dy = r.uniform(-1, 1, (16, 128)).astype(np.float32)
+    _, rrms = oracle.rmsnorm(x, w, 1e-8)
+    dw0 = r.standard_normal(128).astype(np.float32)
+    dx, dw = oracle.rmsnorm_bwd(dy, x, w, rrms, dw0)
+    tx, tw = torch.from_numpy(x).double().requires_grad_(True), torch.from_numpy(w).double().requires_grad_(True)
+    y = tx * torch.rsqrt((tx * tx).mean(-1, keepdim=True) + 1e-8) * tw
+    y.backward(torch.from_numpy(dy).double())
+    assert _rel(dx, tx.grad.numpy()) < 1e-5
+    assert _rel(dw - dw0, tw.grad.numpy()) < 1e-5
+
+
+def test_rmsnorm_bwd_oracle_matches_reference_formula_at_unit_gain():
+    # with w == 1 the reference's dx line (rmsnorm.rs:232) and the gradient agree
+    r = np.random.default_rng(6)
+    x = r.uniform(-2, 2, (8, 64)).astype(np.float32)
+    dy = r.uniform(-1, 1, (8, 64)).astype(np.float32)
+    w = np.ones(64, np.float32)
+    _, rrms = oracle.rmsnorm(x, w, 1e-8)
+    dx, _ = oracle.rmsnorm_bwd(dy, x, w, rrms)
+    rr = rrms.astype(np.float64)[:, None]
+    dot = (dy.astype(np.float64) * w * x).sum(-1, keepdims=True)
+    ref = rr * w * (dy - x * rr * rr * dot / 64)
+    assert _rel(dx, ref) < 1e-6
