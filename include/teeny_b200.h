@@ -302,6 +302,13 @@ TB_API int tb_decoder_destroy(tb_decoder* dec);
  * PyTorch layout listed above) into the decoder's own layout. */
 TB_API int tb_decoder_set_param(tb_decoder* dec, int layer, int kind, const void* src, int src_dtype,
                                 int src_on_host);
+/* Copies one int8 weight with its per-output-channel f32 scales, as
+ * teeny-quant stores them (I8 [rows, cols] + F32 `_scale` [rows],
+ * utilities/teeny-quant/src/format.rs:145-182), into the int8 GEMV layout
+ * without re-quantising.  Linear kinds need a weights_int8 decoder;
+ * TB_P_EMBED is dequantised (q * scale) into the bf16 gather table. */
+TB_API int tb_decoder_set_param_int8(tb_decoder* dec, int layer, int kind, const int8_t* q, const float* scale,
+                                     int src_on_host);
 /* Fills every parameter from a counter-based N(0, std) generator (norm
  * weights = 1).  Deterministic in seed. */
 TB_API int tb_decoder_init_random(tb_decoder* dec, uint64_t seed, float std);
@@ -330,6 +337,32 @@ TB_API int tb_decoder_fill_kv_random(tb_decoder* dec, int B, int len, uint64_t s
 TB_API int tb_decoder_read_kv(tb_decoder* dec, int layer, int B, int len, void* k_out, void* v_out);
 /* Tokens currently in the KV cache per sequence. */
 TB_API int tb_decoder_seq_len(tb_decoder* dec, int* len);
+
+/* --------------------------------------------------------- checkpoints --- */
+/* safetensors files (memory-mapped, read in place), as the reference's
+ * loader reads them (utilities/teeny-data/src/safetensors/mod.rs:22-45).
+ * Host code only: needs no GPU. */
+typedef struct tb_st tb_st;
+TB_API int tb_st_open(const char* path, tb_st** out);
+TB_API int tb_st_close(tb_st* st);
+/* Number of tensors, and the i-th name in header order. */
+TB_API int tb_st_count(tb_st* st);
+TB_API const char* tb_st_name(tb_st* st, int i);
+/* dtype: TB_F32 / TB_BF16 / TB_I8 / TB_I32, or -1 for other safetensors
+ * dtypes; *rank in: capacity of shape, out: the tensor's rank; data points
+ * into the mapping (valid until tb_st_close).  Any output may be NULL. */
+TB_API int tb_st_tensor(tb_st* st, const char* name, int* dtype, int64_t* shape, int* rank, const void** data,
+                        size_t* bytes);
+/* A "__metadata__" value (e.g. teeny-quant's "quantization_config" JSON), or NULL. */
+TB_API const char* tb_st_metadata(tb_st* st, const char* key);
+/* Loads a Llama-layout checkpoint (model.embed_tokens.weight,
+ * model.layers.N.{input_layernorm, self_attn.{q,k,v,o}_proj,
+ * post_attention_layernorm, mlp.{gate,up,down}_proj}.weight, model.norm.weight,
+ * lm_head.weight, tied to the embedding when absent) into the decoder, then
+ * prepares it.  F32 / BF16 tensors go through tb_decoder_set_param; I8 tensors
+ * with a `<name>_scale` (teeny-quant symmetric per-channel int8) through
+ * tb_decoder_set_param_int8. */
+TB_API int tb_decoder_load_safetensors(tb_decoder* dec, tb_st* st);
 
 /* ---------------------------------------------------------- multi-GPU --- */
 /* Batch-sharded runs: one process per GPU, each on its own shard; the only

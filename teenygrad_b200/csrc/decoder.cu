@@ -27,6 +27,30 @@ __global__ void convert_rows_kernel(const void* __restrict__ src, int src_f32, _
     }
 }
 
+// int8 rows (and their per-row f32 scales) into the decoder's layout, with the
+// same row mapping as convert_rows_kernel; scale_dst / scale_src may be null.
+__global__ void copy_rows_i8_kernel(const int8_t* __restrict__ src, const float* __restrict__ scale_src,
+                                    int8_t* __restrict__ dst, float* __restrict__ scale_dst, int64_t rows, int64_t cols,
+                                    int64_t row_off, int64_t block, int64_t block_stride, int perm_hd) {
+    const int64_t total = rows * cols;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / cols, c = i % cols;
+        int64_t dr = row_off + (r / block) * block_stride + (r % block);
+        if (perm_hd) dr = qkv_perm_row(dr, perm_hd);
+        dst[dr * cols + c] = src[i];
+        if (c == 0 && scale_dst) scale_dst[dr] = scale_src[r];
+    }
+}
+
+// dequantize_affine (teeny-quant quant/affine.rs:151-159) into bf16: int8
+// embeddings of a quantised checkpoint become the bf16 gather table.
+__global__ void dequant_rows_bf16_kernel(const int8_t* __restrict__ q, const float* __restrict__ scale,
+                                         __nv_bfloat16* __restrict__ dst, int64_t rows, int64_t cols) {
+    const int64_t total = rows * cols;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x)
+        dst[i] = __float2bfloat16_rn((float)q[i] * scale[i / cols]);
+}
+
 __device__ __forceinline__ uint64_t splitmix64(uint64_t x) {
     x += 0x9E3779B97F4A7C15ull;
     x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
@@ -293,11 +317,13 @@ struct tb_decoder {
         bf16 *attn_norm, *mlp_norm, *wqkv, *wo, *wgu, *wdown;
         int8_t *qqkv = nullptr, *qo = nullptr, *qgu = nullptr, *qdown = nullptr;
         float *sqkv = nullptr, *so = nullptr, *sgu = nullptr, *sdown = nullptr;
+        unsigned i8_loaded = 0;   // bit (1 << kind): set from int8 checkpoint tensors, not quantised here
     };
     std::vector<Layer> layers;
     bf16 *embed = nullptr, *lm_head = nullptr, *final_norm = nullptr;
     int8_t* qlm = nullptr;
     float* slm = nullptr;
+    bool lm_i8_loaded = false;
     bf16 *kcache = nullptr, *vcache = nullptr;
     int64_t cache_layer_elems = 0;
     float2* rope_tab = nullptr;
@@ -680,6 +706,66 @@ int tb_decoder_set_param(tb_decoder* d, int layer, int kind, const void* src, in
         cudaStreamSynchronize(ctx->stream);
         cudaFree(staging);
     }
+    if (L) L->i8_loaded &= ~(1u << kind);
+    if (kind == TB_P_LM_HEAD) d->lm_i8_loaded = false;
+    d->quantized = false;
+    return rc;
+}
+
+int tb_decoder_set_param_int8(tb_decoder* d, int layer, int kind, const int8_t* q, const float* scale,
+                              int src_on_host) {
+    if (!d || !q || !scale) return TB_ERR_ARG;
+    tb_ctx* ctx = d->ctx;
+    const tb_decoder_config& c = d->cfg;
+    const bool per_layer = kind >= TB_P_ATTN_NORM && kind <= TB_P_W_DOWN;
+    TB_REQUIRE(ctx, !per_layer || (layer >= 0 && layer < c.n_layers), TB_ERR_ARG, "set_param_int8: layer %d", layer);
+    tb_decoder::Layer* L = per_layer ? &d->layers[layer] : nullptr;
+    const int64_t dm = c.d_model, F = c.ffn_hidden;
+    int8_t* dst = nullptr;
+    float* sdst = nullptr;
+    bf16* deq = nullptr;   // int8 tensors that the decoder keeps in bf16 (the embedding table)
+    int64_t rows = 0, cols = dm, row_off = 0, block = 1ll << 40, bstride = 0;
+    switch (kind) {
+        case TB_P_EMBED: deq = d->embed; rows = c.vocab; break;
+        case TB_P_LM_HEAD: dst = d->qlm; sdst = d->slm; rows = c.vocab; break;
+        case TB_P_WQ: dst = L->qqkv; sdst = L->sqkv; rows = d->q_dim; break;
+        case TB_P_WK: dst = L->qqkv; sdst = L->sqkv; rows = d->kv_dim; row_off = d->q_dim; break;
+        case TB_P_WV: dst = L->qqkv; sdst = L->sqkv; rows = d->kv_dim; row_off = d->q_dim + d->kv_dim; break;
+        case TB_P_WO: dst = L->qo; sdst = L->so; rows = dm; cols = d->q_dim; break;
+        case TB_P_W_GATE: dst = L->qgu; sdst = L->sgu; rows = F; block = 128; bstride = 256; break;
+        case TB_P_W_UP: dst = L->qgu; sdst = L->sgu; rows = F; row_off = 128; block = 128; bstride = 256; break;
+        case TB_P_W_DOWN: dst = L->qdown; sdst = L->sdown; rows = dm; cols = F; break;
+        default: return set_error(ctx, TB_ERR_ARG, "set_param_int8: kind %d has no int8 form", kind);
+    }
+    TB_REQUIRE(ctx, deq || c.weights_int8, TB_ERR_UNSUPPORTED,
+               "set_param_int8: int8 linear weights need a decoder created with weights_int8");
+    const size_t qbytes = (size_t)rows * cols, sbytes = (size_t)rows * sizeof(float);
+    const int8_t* dq = q;
+    const float* ds = scale;
+    void* staging = nullptr;
+    if (src_on_host) {
+        TB_CUDA_TRY(ctx, cudaMalloc(&staging, qbytes + sbytes + 256));
+        uint8_t* sp = reinterpret_cast<uint8_t*>(staging);
+        TB_CUDA_TRY(ctx, cudaMemcpyAsync(sp, q, qbytes, cudaMemcpyHostToDevice, ctx->stream));
+        TB_CUDA_TRY(ctx, cudaMemcpyAsync(sp + (qbytes + 255) / 256 * 256, scale, sbytes, cudaMemcpyHostToDevice,
+                                         ctx->stream));
+        dq = reinterpret_cast<const int8_t*>(sp);
+        ds = reinterpret_cast<const float*>(sp + (qbytes + 255) / 256 * 256);
+    }
+    if (deq) {
+        dequant_rows_bf16_kernel<<<grid_for(ctx, rows * cols), 256, 0, ctx->stream>>>(dq, ds, deq, rows, cols);
+    } else {
+        const bool qkv = kind == TB_P_WQ || kind == TB_P_WK || kind == TB_P_WV;
+        copy_rows_i8_kernel<<<grid_for(ctx, rows * cols), 256, 0, ctx->stream>>>(
+            dq, ds, dst, sdst, rows, cols, row_off, block, bstride, qkv && d->qkv_perm ? c.head_dim : 0);
+    }
+    int rc = check_launch(ctx, "set_param_int8");
+    if (staging) {
+        cudaStreamSynchronize(ctx->stream);
+        cudaFree(staging);
+    }
+    if (L) L->i8_loaded |= 1u << kind;
+    if (kind == TB_P_LM_HEAD) d->lm_i8_loaded = true;
     d->quantized = false;
     return rc;
 }
@@ -715,13 +801,28 @@ int tb_decoder_prepare(tb_decoder* d) {
     tb_ctx* ctx = d->ctx;
     const tb_decoder_config& c = d->cfg;
     const int64_t dm = c.d_model, F = c.ffn_hidden;
-    for (auto& L : d->layers) {
-        TB_TRY(tb_quantize_int8_bf16(ctx, L.wqkv, L.qqkv, L.sqkv, d->qkv_n, dm));
-        TB_TRY(tb_quantize_int8_bf16(ctx, L.wo, L.qo, L.so, dm, d->q_dim));
-        TB_TRY(tb_quantize_int8_bf16(ctx, L.wgu, L.qgu, L.sgu, 2 * F, dm));
-        TB_TRY(tb_quantize_int8_bf16(ctx, L.wdown, L.qdown, L.sdown, dm, F));
+    // a fused matrix is quantised here from its bf16 values unless all of its
+    // parts came in as int8 (tb_decoder_set_param_int8); a mix is an error
+    auto need = [&](const tb_decoder::Layer& L, unsigned kinds, const char* what, int l, bool* q) {
+        const unsigned got = L.i8_loaded & kinds;
+        if (got && got != kinds)
+            return set_error(ctx, TB_ERR_ARG, "prepare: layer %d %s mixes int8 and float parts", l, what);
+        *q = got == 0;
+        return (int)TB_OK;
+    };
+    for (int l = 0; l < c.n_layers; l++) {
+        tb_decoder::Layer& L = d->layers[l];
+        bool q;
+        TB_TRY(need(L, (1u << TB_P_WQ) | (1u << TB_P_WK) | (1u << TB_P_WV), "QKV", l, &q));
+        if (q) TB_TRY(tb_quantize_int8_bf16(ctx, L.wqkv, L.qqkv, L.sqkv, d->qkv_n, dm));
+        TB_TRY(need(L, 1u << TB_P_WO, "O", l, &q));
+        if (q) TB_TRY(tb_quantize_int8_bf16(ctx, L.wo, L.qo, L.so, dm, d->q_dim));
+        TB_TRY(need(L, (1u << TB_P_W_GATE) | (1u << TB_P_W_UP), "gate/up", l, &q));
+        if (q) TB_TRY(tb_quantize_int8_bf16(ctx, L.wgu, L.qgu, L.sgu, 2 * F, dm));
+        TB_TRY(need(L, 1u << TB_P_W_DOWN, "down", l, &q));
+        if (q) TB_TRY(tb_quantize_int8_bf16(ctx, L.wdown, L.qdown, L.sdown, dm, F));
     }
-    TB_TRY(tb_quantize_int8_bf16(ctx, d->lm_head, d->qlm, d->slm, c.vocab, dm));
+    if (!d->lm_i8_loaded) TB_TRY(tb_quantize_int8_bf16(ctx, d->lm_head, d->qlm, d->slm, c.vocab, dm));
     d->quantized = true;
     return TB_OK;
 }
@@ -804,6 +905,94 @@ int tb_decoder_fill_kv_random(tb_decoder* d, int B, int len, uint64_t seed, cons
     d->host_len = len;
     d->host_step = 0;
     return check_launch(ctx, "fill_kv_random");
+}
+
+int tb_decoder_load_safetensors(tb_decoder* d, tb_st* st) {
+    if (!d || !st) return TB_ERR_ARG;
+    tb_ctx* ctx = d->ctx;
+    const tb_decoder_config& c = d->cfg;
+    // Llama checkpoint names (Hugging Face layout) -> parameter kinds
+    struct Name {
+        int kind;
+        const char* fmt;
+    };
+    static const Name global_names[] = {{TB_P_EMBED, "model.embed_tokens.weight"},
+                                        {TB_P_FINAL_NORM, "model.norm.weight"},
+                                        {TB_P_LM_HEAD, "lm_head.weight"}};
+    static const Name layer_names[] = {{TB_P_ATTN_NORM, "model.layers.%d.input_layernorm.weight"},
+                                       {TB_P_WQ, "model.layers.%d.self_attn.q_proj.weight"},
+                                       {TB_P_WK, "model.layers.%d.self_attn.k_proj.weight"},
+                                       {TB_P_WV, "model.layers.%d.self_attn.v_proj.weight"},
+                                       {TB_P_WO, "model.layers.%d.self_attn.o_proj.weight"},
+                                       {TB_P_MLP_NORM, "model.layers.%d.post_attention_layernorm.weight"},
+                                       {TB_P_W_GATE, "model.layers.%d.mlp.gate_proj.weight"},
+                                       {TB_P_W_UP, "model.layers.%d.mlp.up_proj.weight"},
+                                       {TB_P_W_DOWN, "model.layers.%d.mlp.down_proj.weight"}};
+    const int64_t dm = c.d_model, F = c.ffn_hidden, V = c.vocab;
+    auto expected = [&](int kind, int64_t* r, int64_t* k) {
+        switch (kind) {
+            case TB_P_EMBED: case TB_P_LM_HEAD: *r = V; *k = dm; return 2;
+            case TB_P_FINAL_NORM: case TB_P_ATTN_NORM: case TB_P_MLP_NORM: *r = dm; *k = 1; return 1;
+            case TB_P_WQ: *r = d->q_dim; *k = dm; return 2;
+            case TB_P_WK: case TB_P_WV: *r = d->kv_dim; *k = dm; return 2;
+            case TB_P_WO: *r = dm; *k = d->q_dim; return 2;
+            case TB_P_W_GATE: case TB_P_W_UP: *r = F; *k = dm; return 2;
+            default: *r = dm; *k = F; return 2;   // TB_P_W_DOWN
+        }
+    };
+    auto load_one = [&](int layer, int kind, const char* name) -> int {
+        int dt = -1, rank = 4;
+        int64_t shape[4] = {0, 0, 0, 0};
+        const void* data = nullptr;
+        if (tb_st_tensor(st, name, &dt, shape, &rank, &data, nullptr) != TB_OK) {
+            if (kind == TB_P_LM_HEAD) return 1;   // tied to the embedding (handled below)
+            return set_error(ctx, TB_ERR_ARG, "checkpoint: tensor %s missing", name);
+        }
+        int64_t r, k;
+        const int want = expected(kind, &r, &k);
+        if (rank != want || shape[0] != r || (want == 2 && shape[1] != k))
+            return set_error(ctx, TB_ERR_SHAPE, "checkpoint: %s has the wrong shape for this decoder", name);
+        if (dt == TB_I8) {
+            const std::string zname = std::string(name) + "_zero_point";
+            if (tb_st_tensor(st, zname.c_str(), nullptr, nullptr, nullptr, nullptr, nullptr) == TB_OK)
+                return set_error(ctx, TB_ERR_UNSUPPORTED, "checkpoint: %s is asymmetric int8 (has %s)", name,
+                                 zname.c_str());
+            const std::string sname = std::string(name) + "_scale";
+            int sdt = -1, srank = 1;
+            int64_t sshape[1] = {0};
+            const void* sdata = nullptr;
+            if (tb_st_tensor(st, sname.c_str(), &sdt, sshape, &srank, &sdata, nullptr) != TB_OK || sdt != TB_F32 ||
+                srank != 1 || sshape[0] != r)
+                return set_error(ctx, TB_ERR_SHAPE,
+                                 "checkpoint: %s is I8 but %s is not an F32 scale per output channel (only "
+                                 "symmetric per-channel int8 is supported)",
+                                 name, sname.c_str());
+            return tb_decoder_set_param_int8(d, layer, kind, reinterpret_cast<const int8_t*>(data),
+                                             reinterpret_cast<const float*>(sdata), 1);
+        }
+        if (dt != TB_F32 && dt != TB_BF16)
+            return set_error(ctx, TB_ERR_UNSUPPORTED, "checkpoint: %s: dtype not F32, BF16 or I8", name);
+        return tb_decoder_set_param(d, layer, kind, data, dt, 1);
+    };
+    bool tied = false;
+    for (const Name& n : global_names) {
+        const int rc = load_one(0, n.kind, n.fmt);
+        if (rc == 1) tied = true;
+        else if (rc) return rc;
+    }
+    char buf[256];
+    for (int l = 0; l < c.n_layers; l++)
+        for (const Name& n : layer_names) {
+            snprintf(buf, sizeof(buf), n.fmt, l);
+            TB_TRY(load_one(l, n.kind, buf));
+        }
+    if (tied) {   // no lm_head.weight: the output projection shares the embedding table
+        TB_CUDA_TRY(ctx, cudaMemcpyAsync(d->lm_head, d->embed, (size_t)V * dm * sizeof(bf16), cudaMemcpyDeviceToDevice,
+                                         ctx->stream));
+        d->lm_i8_loaded = false;
+    }
+    TB_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+    return tb_decoder_prepare(d);
 }
 
 int tb_decoder_read_kv(tb_decoder* d, int layer, int B, int len, void* k_out, void* v_out) {

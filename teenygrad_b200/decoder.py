@@ -99,6 +99,27 @@ class Decoder:
         check(self.ctx, lib().tb_decoder_set_param(self._h, ctypes.c_int(layer), ctypes.c_int(kind),
                                                    ctypes.c_void_p(ptr), ctypes.c_int(dt), ctypes.c_int(host)))
 
+    def set_param_int8(self, kind: int, q, scale, layer: int = 0):
+        """int8 weight [rows, cols] + f32 scale [rows] (teeny-quant's I8 + _scale), numpy or torch."""
+        import numpy as np
+        if isinstance(q, np.ndarray):
+            qk, sk = np.ascontiguousarray(q, np.int8), np.ascontiguousarray(scale, np.float32)
+            qp, sp, host = qk.ctypes.data, sk.ctypes.data, 1
+        else:
+            qk, sk = q.contiguous(), scale.float().contiguous()
+            qp, sp, host = qk.data_ptr(), sk.data_ptr(), 0 if qk.is_cuda else 1
+        self._ctx()
+        check(self.ctx, lib().tb_decoder_set_param_int8(self._h, ctypes.c_int(layer), ctypes.c_int(kind),
+                                                        ctypes.c_void_p(qp), ctypes.c_void_p(sp), ctypes.c_int(host)))
+
+    def load_checkpoint(self, path: str):
+        """Loads a Llama-layout .safetensors checkpoint (F32 / BF16, or teeny-quant
+        int8 with per-channel scales) and prepares the decoder."""
+        from .checkpoint import SafeTensors
+        with SafeTensors(path) as st:
+            self._ctx()
+            check(self.ctx, lib().tb_decoder_load_safetensors(self._h, st._h))
+
     def init_random(self, seed: int = 0, std: float = 0.02):
         self._ctx()
         check(self.ctx, lib().tb_decoder_init_random(self._h, ctypes.c_uint64(seed), ctypes.c_float(std)))
