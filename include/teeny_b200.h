@@ -364,6 +364,70 @@ TB_API const char* tb_st_metadata(tb_st* st, const char* key);
  * tb_decoder_set_param_int8. */
 TB_API int tb_decoder_load_safetensors(tb_decoder* dec, tb_st* st);
 
+/* ------------------------------------------------------ graph executor --- */
+/* The counterpart of LoadedModel::forward (drivers/teeny-cuda/src/model/
+ * mod.rs:524-700) for a whole lowered DAG: nodes named after the reference's
+ * graph ops (kernels/teeny-kernels/src/graph/mod.rs), shapes inferred as
+ * nodes are added, every input and intermediate planned once into one
+ * device arena by liveness (tb_graph_plan allocates it; runs allocate
+ * nothing), node launches stream-ordered on the context's stream with no
+ * synchronisation, optionally captured once into a CUDA graph and replayed.
+ * Parameters stay in the caller's device memory. */
+typedef struct tb_graph tb_graph;
+
+typedef enum tb_graph_op {
+    TB_G_LINEAR = 0,    /* x [.., K], w [N, K] (+ f32 bias [N], + residual [.., N]; pass -1 to skip) */
+    TB_G_MATMUL = 1,    /* a [.., K], b [K, N] */
+    TB_G_RMSNORM = 2,   /* x [.., N], w [N]; eps   (the reference's RuntimeOp is a stub, graph/mod.rs:454) */
+    TB_G_LAYERNORM = 3, /* x [.., N], w [N], b [N]; eps */
+    TB_G_ACT = 4,       /* x; act (tb_act) */
+    TB_G_ADD = 5,       /* a, b */
+    TB_G_SWIGLU = 6,    /* gate, up: silu(gate) * up (Silu + Mul fused) */
+    TB_G_ATTENTION = 7, /* q [B, S, heads * D], k / v [B, S, kv_heads * D], or one fused qkv
+                           [B, S, (heads + 2 kv_heads) * D] -> [B, S, heads * D], read in place;
+                           heads, kv_heads, causal, scale (0: 1/sqrt(D)) (TODO in the reference, :2477) */
+    TB_G_ROPE = 8,      /* x [T, H, D], positions int32 [T]; theta (0: 10000) (TODO :2472) */
+    TB_G_GATHER = 9,    /* table [V, D], ids int32 [..] -> [.., D] (TODO :2527) */
+    TB_G_ARGMAX = 10,   /* x [.., N] -> int32 [..] (TODO :2250) */
+    TB_G_CONV2D = 11,   /* x [B, C, H, W], w [Co, C, KH, KW] (+ f32 bias, bn scale, bn shift [Co]; -1 skips);
+                           stride, pad, act (TB_ACT_NONE = -1 for none) */
+    TB_G_BATCHNORM = 12 /* x [B, C, ..], gamma, beta, mean, var f32 [C]; eps */
+} tb_graph_op;
+
+typedef struct tb_node_attr {
+    float eps;        /* norms */
+    int act;          /* TB_G_ACT, TB_G_CONV2D: a tb_act */
+    int heads, kv_heads, causal;
+    float scale;      /* attention softmax scale, 0: 1 / sqrt(head dim) */
+    float theta;      /* RoPE base, 0: 10000 */
+    int stride, pad;  /* conv2d */
+} tb_node_attr;
+
+TB_API int tb_graph_create(tb_ctx* ctx, tb_graph** out);
+TB_API int tb_graph_destroy(tb_graph* g);
+/* A graph input (written before each run into its planned buffer, whose
+ * pointer tb_graph_tensor_ptr returns after tb_graph_plan). */
+TB_API int tb_graph_input(tb_graph* g, int dtype, int rank, const int64_t* shape, int* id);
+/* A parameter in the caller's device memory (not copied). */
+TB_API int tb_graph_param(tb_graph* g, int dtype, int rank, const int64_t* shape, const void* dev_ptr, int* id);
+/* Appends a node; inputs are tensor ids (-1 for skipped optional inputs);
+ * attr may be NULL; *out_id is the node's output tensor. */
+TB_API int tb_graph_node(tb_graph* g, int op, const int* inputs, int n_inputs, const tb_node_attr* attr, int* out_id);
+/* Keeps a tensor's buffer for reading after the run (tensors nothing consumes are kept anyway). */
+TB_API int tb_graph_mark_output(tb_graph* g, int id);
+/* Plans the arena and allocates it (the only allocation); capture = 1
+ * records the node launches into a CUDA graph at the first run and replays it. */
+TB_API int tb_graph_plan(tb_graph* g, int capture);
+TB_API int tb_graph_arena_bytes(tb_graph* g, size_t* bytes);
+/* Device pointer of a tensor (inputs, outputs, intermediates: in the arena). */
+TB_API int tb_graph_tensor_ptr(tb_graph* g, int id, void** ptr);
+/* Stream-ordered copies into / out of a planned tensor's buffer (host or
+ * device memory on the other side; bytes must be the tensor's size). */
+TB_API int tb_graph_write(tb_graph* g, int id, const void* src, size_t bytes);
+TB_API int tb_graph_read(tb_graph* g, int id, void* dst, size_t bytes);
+/* Enqueues every node on the context's stream (no synchronisation). */
+TB_API int tb_graph_run(tb_graph* g);
+
 /* ---------------------------------------------------------- multi-GPU --- */
 /* Batch-sharded runs: one process per GPU, each on its own shard; the only
  * exchange is an all-gather of the final outputs (the reference has no

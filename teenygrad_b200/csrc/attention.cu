@@ -816,11 +816,17 @@ attn_decode_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_cons
 // One warp per query row, f32 throughout.  Keys go 32 at a time, lane j
 // computing the full dot product of key j (q staged in shared memory); an
 // online softmax (running max, rescaled sum and output) merges the chunks,
-// and the output dims are spread over the lanes for P V.
+// and the output dims are spread over the lanes for P V.  Tensors are
+// addressed through (head, position, batch) strides in elements (d is
+// contiguous); lse is [B, Hq, Sq].
+struct F32Strides {
+    int64_t q_sh, q_ss, q_sb, kv_sh, kv_ss, kv_sb, o_sh, o_ss, o_sb;
+};
+
 __global__ void __launch_bounds__(256)
 attn_f32_kernel(const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
                 float* __restrict__ o, float* __restrict__ lse, int B, int Hq, int Hkv, int Sq, int Sk, int D,
-                float scale, int causal) {
+                float scale, int causal, F32Strides st) {
     __shared__ float sq[8][128];
     const int w = threadIdx.x / 32, lane = threadIdx.x & 31;
     const int64_t row = (int64_t)blockIdx.x * 8 + w;
@@ -831,22 +837,24 @@ attn_f32_kernel(const float* __restrict__ q, const float* __restrict__ k, const 
         const int64_t bh = row / Sq;
         h = (int)(bh % Hq);
         b = (int)(bh / Hq);
-        for (int d = lane; d < D; d += 32) sq[w][d] = q[row * D + d];
+        const float* qr = q + (int64_t)b * st.q_sb + (int64_t)h * st.q_sh + (int64_t)i * st.q_ss;
+        for (int d = lane; d < D; d += 32) sq[w][d] = qr[d];
     }
     __syncwarp();
     if (!live) return;
     const int hk = h / (Hq / Hkv);
-    const float* kb = k + ((int64_t)b * Hkv + hk) * Sk * D;
-    const float* vb = v + ((int64_t)b * Hkv + hk) * Sk * D;
+    const float* kb = k + (int64_t)b * st.kv_sb + (int64_t)hk * st.kv_sh;
+    const float* vb = v + (int64_t)b * st.kv_sb + (int64_t)hk * st.kv_sh;
+    const bool vec = (D & 3) == 0 && (reinterpret_cast<uintptr_t>(kb) & 15) == 0 && (st.kv_ss & 3) == 0;
     const int jmax = causal ? min(Sk - 1, i + (Sk - Sq)) : Sk - 1;
     float m = -INFINITY, l = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
     for (int j0 = 0; j0 <= jmax; j0 += 32) {
         const int j = j0 + lane;
         float sc = -INFINITY;
         if (j <= jmax) {
-            const float* kr = kb + (int64_t)j * D;
+            const float* kr = kb + (int64_t)j * st.kv_ss;
             float dot = 0.f;
-            if ((D & 3) == 0 && (reinterpret_cast<uintptr_t>(k) & 15) == 0) {   // 16-byte rows
+            if (vec) {   // 16-byte rows
 #pragma unroll 8
                 for (int d = 0; d < D; d += 4) {
                     const float4 kv = *reinterpret_cast<const float4*>(kr + d);
@@ -880,7 +888,7 @@ attn_f32_kernel(const float* __restrict__ q, const float* __restrict__ k, const 
             for (int u = 0; u < 8; u++)
 #pragma unroll
                 for (int t = 0; t < 4; t++)
-                    vv[u][t] = (jb + u < nj && lane + 32 * t < D) ? vb[(int64_t)(j0 + jb + u) * D + lane + 32 * t] : 0.f;
+                    vv[u][t] = (jb + u < nj && lane + 32 * t < D) ? vb[(int64_t)(j0 + jb + u) * st.kv_ss + lane + 32 * t] : 0.f;
 #pragma unroll
             for (int u = 0; u < 8; u++) {
                 const float pj = __shfl_sync(0xffffffffu, p, (jb + u) & 31);
@@ -890,13 +898,25 @@ attn_f32_kernel(const float* __restrict__ q, const float* __restrict__ k, const 
         }
         m = m_new;
     }
-    float* orow = o + row * D;
+    float* orow = o + (int64_t)b * st.o_sb + (int64_t)h * st.o_sh + (int64_t)i * st.o_ss;
     for (int t = 0; t < 4; t++)
         if (lane + 32 * t < D) orow[lane + 32 * t] = (jmax >= 0) ? acc[t] / l : 0.f;
     if (lse && lane == 0) lse[row] = (jmax >= 0) ? m + logf(l) : -INFINITY;
 }
 
 // ------------------------------------------------------------ host side ----
+int attn_f32_launch(tb_ctx* ctx, const AttnTensors& t, int B, int Hq, int Hkv, int Sq, int Sk, int D, float scale,
+                    int causal) {
+    if (D > 128) return set_error(ctx, TB_ERR_SHAPE, "attn f32: D <= 128");
+    const int64_t rows = (int64_t)B * Hq * Sq;
+    if (rows == 0) return TB_OK;
+    const F32Strides st{t.q_sh, t.q_ss, t.q_sb, t.kv_sh, t.kv_ss, t.kv_sb, t.o_sh, t.o_ss, t.o_sb};
+    attn_f32_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, ctx->stream>>>(
+        (const float*)t.q, (const float*)t.k, (const float*)t.v, (float*)t.o, t.lse, B, Hq, Hkv, Sq, Sk, D, scale,
+        causal, st);
+    return check_launch(ctx, "attn_f32");
+}
+
 static int tmap_heads(tb_ctx* ctx, CUtensorMap* m, const void* base, int D, int H, int S, int B,
                       int64_t sh, int64_t ss, int64_t sb) {
     // dims (d, h, s, b), box (64, 1, 128, 1); strides in elements -> bytes
@@ -990,11 +1010,16 @@ extern "C" int tb_attn_fwd(tb_ctx* ctx, int dtype, const void* q, const void* k,
                TB_ERR_SHAPE, "attn: bad shape");
     if (B == 0 || Sq == 0) return TB_OK;
     if (dtype == TB_F32) {
-        TB_REQUIRE(ctx, D <= 128, TB_ERR_SHAPE, "attn f32: D <= 128");
-        int64_t rows = (int64_t)B * Hq * Sq;
-        attn_f32_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, ctx->stream>>>(
-            (const float*)q, (const float*)k, (const float*)v, (float*)o, lse, B, Hq, Hkv, Sq, Sk, D, scale, causal);
-        return check_launch(ctx, "attn_f32");
+        AttnTensors t{};
+        t.q = q;
+        t.q_ss = D, t.q_sh = (int64_t)Sq * D, t.q_sb = (int64_t)Hq * Sq * D;
+        t.k = k;
+        t.v = v;
+        t.kv_ss = D, t.kv_sh = (int64_t)Sk * D, t.kv_sb = (int64_t)Hkv * Sk * D;
+        t.o = o;
+        t.o_ss = D, t.o_sh = (int64_t)Sq * D, t.o_sb = (int64_t)Hq * Sq * D;
+        t.lse = lse;
+        return attn_f32_launch(ctx, t, B, Hq, Hkv, Sq, Sk, D, scale, causal);
     }
     if (dtype != TB_BF16) return set_error(ctx, TB_ERR_UNSUPPORTED, "attn: dtype %d", dtype);
     TB_REQUIRE(ctx, D == 64 || D == 128, TB_ERR_SHAPE, "attn bf16: D must be 64 or 128");

@@ -45,6 +45,9 @@ struct DecodeArgs {
     int chunk;             // keys per split (set by attn_decode_launch)
 };
 
+// f32 CUDA-core attention over strided q / k / v / o (lse [B, Hq, Sq], may be null).
+int attn_f32_launch(tb_ctx* ctx, const AttnTensors& t, int B, int Hq, int Hkv, int Sq, int Sk, int D, float scale,
+                    int causal);
 int attn_tc_launch(tb_ctx* ctx, const AttnTensors& t, int B, int Hq, int Hkv, int Sq, int Sk, int D,
                    float scale, int causal);
 // Decode attention over a KV cache of capacity >= max_len; no global scratch.
