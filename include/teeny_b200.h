@@ -248,12 +248,11 @@ TB_API int tb_argmax_fwd(tb_ctx* ctx, int dtype, const void* x, int32_t* out, in
  * split-row kernel whose cross-block reduction state lives in a static device
  * array, so the call needs no workspace from the caller and never calls
  * cudaMalloc/cudaFree: for callers that cannot allocate device memory, such as
- * code running while a CUDA graph is being captured, or a serving loop whose
- * device memory belongs to an external pool.  At most
+ * a serving loop whose device memory belongs to an external pool.  At most
  * TB_ARGMAX_NOALLOC_MAX_ROWS rows per call (larger M returns TB_ERR_SHAPE).
  * The array (64 KiB) stays resident on every GPU that loads the library until
  * the process exits.  The first call on a device looks up the array's device
- * address; make that first call before any stream capture.  All calls share
+ * address and caches it for the life of the process.  All calls share
  * the array: calls that overlap on the GPU (two streams or two host threads
  * at once) race.  dtype TB_F32 or TB_BF16. */
 #define TB_ARGMAX_NOALLOC_MAX_ROWS 4096

@@ -1,8 +1,7 @@
 """tb_argmax_noalloc_fwd: the argmax entry point that allocates no device memory.
 
-Some callers cannot call cudaMalloc -- for instance code that runs while a CUDA
-graph is being captured, or a serving loop whose device memory is owned by an
-external pool.  This entry point keeps its cross-block scratch in a static
+Some callers cannot call cudaMalloc -- for instance a serving loop whose device
+memory is owned by an external pool.  This entry point keeps its cross-block scratch in a static
 device array instead.  The test calls it through the C ABI twice in a row (the
 scratch keeps the previous call's contents, so the second call checks that it
 starts clean) and compares each result with tb_argmax_fwd's, which must agree
