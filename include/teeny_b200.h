@@ -139,6 +139,33 @@ TB_API int tb_linear_fwd_strided(tb_ctx* ctx, int dtype, const void* x, int64_t 
                                  const float* bias, const void* residual, void* y, int64_t ldy, int64_t M,
                                  int64_t N, int64_t K, int flags);
 
+/* A chain of dependent decode linear layers in one persistent launch: step
+ * i + 1 may read what step i wrote (e.g. a layer's output projection with its
+ * residual, gate/up with the RMSNorm fused and SwiGLU, then down with its
+ * residual).  No counterpart in the reference, whose executor launches one
+ * kernel per op (drivers/teeny-cuda/src/model/mod.rs:524-700); each step has
+ * linear_forward's semantics (nn/mlp/linear.rs:22-117), plus an optional
+ * RMSNorm of x (rmsnorm.rs:19-134, gains norm_w) fused in front.
+ * bf16 only; M <= 64 tokens; N % 256 == 0 (N <= 32768) and K % 64 == 0;
+ * ldx, ldy multiples of 8 elements; at most TB_LINEAR_CHAIN_MAX steps.
+ * flags: TB_EPI_RESIDUAL (residual rows ldy apart; may alias y) and / or
+ * TB_EPI_SWIGLU (w rows interleaved as for tb_linear_fwd; y has N / 2 columns).
+ * Its split-K reduction uses ctx scratch memory allocated on the first call. */
+#define TB_LINEAR_CHAIN_MAX 4
+typedef struct tb_linear_step {
+    const void* x;      /* bf16 [M, K], rows ldx apart */
+    int64_t ldx;
+    const void* w;      /* bf16 [N, K] */
+    const void* norm_w; /* bf16 [K] RMSNorm gains, or NULL: no norm */
+    float norm_eps;
+    const void* residual;
+    void* y;            /* bf16 [M, N] (N / 2 with SwiGLU), rows ldy apart */
+    int64_t ldy;
+    int64_t N, K;
+    int flags;
+} tb_linear_step;
+TB_API int tb_linear_chain_fwd(tb_ctx* ctx, const tb_linear_step* steps, int n_steps, int64_t M);
+
 /* matmul_forward (math/gemm.rs:44-105; MatMulRuntimeOp gemm.rs:232):
  * c[M, N] = a[M, K] * b[K, N]. */
 TB_API int tb_matmul_fwd(tb_ctx* ctx, int dtype, const void* a, const void* b, void* c, int64_t M,

@@ -1,11 +1,14 @@
 // Decoder executor: parameters, KV cache, activation buffers, prefill and
 // CUDA-graph decode steps, built from the library's kernels.
 #include <math.h>
+#include <stdlib.h>
 
+#include <algorithm>
 #include <vector>
 
 #include "attention.h"
 #include "common.cuh"
+#include "decode_chain.h"
 #include "gemm.h"
 
 namespace tb {
@@ -340,6 +343,10 @@ struct tb_decoder {
     int S0 = 0;      // prompt length
     int host_len = 0, host_step = 0;
     bool quantized = false;
+    // Persistent decode chain (bf16 decode): O, gate/up, down and the next
+    // layer's QKV projection of each layer run as one launch.
+    bool use_chain = false;
+    ChainScratch chain;
     std::vector<void*> allocs;
 
     template <typename T>
@@ -420,6 +427,35 @@ int norm_lin(tb_decoder* d, const bf16* x, int64_t ldx, const bf16* norm_w, cons
     return linear_launch(d->ctx, int8 ? 1 : 0, x, int8 ? (const void*)wq : w, ep, M, N, K);
 }
 
+// Decode attention of layer l: one new token per sequence against the cache.
+int decode_attention(tb_decoder* d, int l, int B) {
+    const tb_decoder_config& c = d->cfg;
+    const int hd = c.head_dim;
+    const float scale = 1.0f / sqrtf((float)hd);
+    bf16* kc = d->kcache + (int64_t)l * d->cache_layer_elems;
+    bf16* vc = d->vcache + (int64_t)l * d->cache_layer_elems;
+    DecodeArgs a{};
+    a.q = d->qkv;
+    a.q_sb = d->qkv_n;
+    a.q_sh = hd;
+    a.k = kc;
+    a.v = vc;
+    a.kv_sb = (int64_t)c.n_kv_heads * c.max_seq * hd;
+    a.kv_sh = (int64_t)c.max_seq * hd;
+    a.kv_ss = hd;
+    a.kv_rows = c.max_seq;
+    a.o = d->attn;
+    a.o_sb = d->q_dim;
+    a.o_sh = hd;
+    a.lse = nullptr;
+    a.Hq = c.n_heads;
+    a.Hkv = c.n_kv_heads;
+    a.len = 1;         // keys = tokens already cached + this one
+    a.len_ptr = d->state;
+    a.scale_log2 = scale * 1.4426950408889634f;
+    return attn_decode_launch(d->ctx, a, B, hd, c.max_seq);
+}
+
 // One transformer layer over T = B * S_new tokens.  decode: S_new == 1 and
 // positions come from d->state[0].
 int layer_forward(tb_decoder* d, int l, int B, int S_new, bool decode) {
@@ -475,26 +511,7 @@ int layer_forward(tb_decoder* d, int l, int B, int S_new, bool decode) {
         t.lse = nullptr;
         TB_TRY(attn_tc_launch(ctx, t, B, c.n_heads, c.n_kv_heads, S_new, S_new, hd, scale, 1));
     } else {
-        DecodeArgs a{};
-        a.q = d->qkv;
-        a.q_sb = d->qkv_n;
-        a.q_sh = hd;
-        a.k = kc;
-        a.v = vc;
-        a.kv_sb = (int64_t)c.n_kv_heads * c.max_seq * hd;
-        a.kv_sh = (int64_t)c.max_seq * hd;
-        a.kv_ss = hd;
-        a.kv_rows = c.max_seq;
-        a.o = d->attn;
-        a.o_sb = d->q_dim;
-        a.o_sh = hd;
-        a.lse = nullptr;
-        a.Hq = c.n_heads;
-        a.Hkv = c.n_kv_heads;
-        a.len = 1;                 // keys = tokens already cached + this one
-        a.len_ptr = d->state;
-        a.scale_log2 = scale * 1.4426950408889634f;
-        TB_TRY(attn_decode_launch(ctx, a, B, hd, c.max_seq));
+        TB_TRY(decode_attention(d, l, B));
     }
     TB_TRY(lin(d, d->attn, L.wo, L.qo, L.so, d->x, T, dm, d->q_dim, d->x, false, false));
     TB_TRY(norm_lin(d, d->x, dm, L.mlp_norm, L.wgu, L.qgu, L.sgu, d->act, T, 2 * c.ffn_hidden, true, false));
@@ -513,10 +530,110 @@ int head_forward(tb_decoder* d, int B, int64_t last_row_stride, int64_t last_row
                   d->amax_cnt);
 }
 
+// The decode chain's GEMVs of layer l (one token per sequence, B sequences).
+ChainStep chain_qkv(tb_decoder* d, int l) {
+    const tb_decoder_config& c = d->cfg;
+    const tb_decoder::Layer& L = d->layers[l];
+    ChainStep s{};
+    s.x = d->x;
+    s.x_ld = c.d_model;
+    s.w = L.wqkv;
+    s.Nw = d->qkv_n;
+    s.K = c.d_model;
+    Epi& e = s.ep;
+    e.out = d->qkv;
+    e.ldo = d->qkv_n;
+    e.ldr = d->qkv_n;
+    e.norm_w = L.attn_norm;
+    e.norm_eps = c.norm_eps;
+    e.perm_hd = c.head_dim;
+    e.rope_tab = d->rope_tab;
+    e.rope_hq = c.n_heads;
+    e.rope_hkv = c.n_kv_heads;
+    e.rope_s_new = 1;
+    e.pos_ptr = d->state;
+    e.kcache = d->kcache + (int64_t)l * d->cache_layer_elems;
+    e.vcache = d->vcache + (int64_t)l * d->cache_layer_elems;
+    e.max_seq = c.max_seq;
+    return s;
+}
+
+ChainStep chain_o(tb_decoder* d, int l) {
+    ChainStep s{};
+    s.x = d->attn;
+    s.x_ld = d->q_dim;
+    s.w = d->layers[l].wo;
+    s.Nw = d->cfg.d_model;
+    s.K = d->q_dim;
+    s.ep.out = d->x;
+    s.ep.ldo = d->cfg.d_model;
+    s.ep.resid = d->x;
+    s.ep.ldr = d->cfg.d_model;
+    return s;
+}
+
+ChainStep chain_gate_up(tb_decoder* d, int l) {
+    const tb_decoder_config& c = d->cfg;
+    ChainStep s{};
+    s.x = d->x;
+    s.x_ld = c.d_model;
+    s.w = d->layers[l].wgu;
+    s.Nw = 2 * c.ffn_hidden;
+    s.K = c.d_model;
+    s.ep.out = d->act;
+    s.ep.ldo = c.ffn_hidden;
+    s.ep.ldr = 2 * c.ffn_hidden;
+    s.ep.swiglu = 1;
+    s.ep.norm_w = d->layers[l].mlp_norm;
+    s.ep.norm_eps = c.norm_eps;
+    return s;
+}
+
+ChainStep chain_down(tb_decoder* d, int l) {
+    const tb_decoder_config& c = d->cfg;
+    ChainStep s{};
+    s.x = d->act;
+    s.x_ld = c.ffn_hidden;
+    s.w = d->layers[l].wdown;
+    s.Nw = c.d_model;
+    s.K = c.ffn_hidden;
+    s.ep.out = d->x;
+    s.ep.ldo = c.d_model;
+    s.ep.resid = d->x;
+    s.ep.ldr = c.d_model;
+    return s;
+}
+
+// Whether this decode step runs on the chain: bf16 weights, permuted QKV rows
+// and every GEMV's shape within the chain's limits.
+bool chain_fits(tb_decoder* d, int B) {
+    if (!d->use_chain || B > 64) return false;
+    return chain_step_ok(chain_qkv(d, 0), B) && chain_step_ok(chain_o(d, 0), B) &&
+           chain_step_ok(chain_gate_up(d, 0), B) && chain_step_ok(chain_down(d, 0), B);
+}
+
 int decode_step_body(tb_decoder* d) {
     const int B = d->B;
+    const int nl = d->cfg.n_layers;
     TB_TRY(tb_embedding_fwd(d->ctx, TB_BF16, d->embed, d->cur_ids, d->x, B, d->cfg.d_model, d->cfg.vocab));
-    for (int l = 0; l < d->cfg.n_layers; l++) TB_TRY(layer_forward(d, l, B, 1, true));
+    if (chain_fits(d, B)) {
+        // QKV of layer 0, then per layer: attention, and one chain launch for
+        // O, gate/up, down and the next layer's QKV
+        ChainStep st[kChainMaxPhases];
+        st[0] = chain_qkv(d, 0);
+        TB_TRY(chain_launch(d->ctx, st, 1, B, d->chain));
+        for (int l = 0; l < nl; l++) {
+            TB_TRY(decode_attention(d, l, B));
+            st[0] = chain_o(d, l);
+            st[1] = chain_gate_up(d, l);
+            st[2] = chain_down(d, l);
+            int n = 3;
+            if (l + 1 < nl) st[n++] = chain_qkv(d, l + 1);
+            TB_TRY(chain_launch(d->ctx, st, n, B, d->chain));
+        }
+    } else {
+        for (int l = 0; l < nl; l++) TB_TRY(layer_forward(d, l, B, 1, true));
+    }
     TB_TRY(head_forward(d, B, d->cfg.d_model, 0));
     return launch(d->ctx, "advance", advance_kernel, dim3(1), dim3(1), 0, d->state, 1, 1);
 }
@@ -631,6 +748,29 @@ int tb_decoder_create(tb_ctx* ctx, const tb_decoder_config* cfg, tb_decoder** ou
     if (rc) {
         tb_decoder_destroy(d);
         return rc;
+    }
+    {
+        // the decode chain (opt-in, TB_DECODE_CHAIN=1): bf16 weights with permuted
+        // QKV rows.  Measured slower than one cluster-reduced GEMV launch per
+        // matrix on C4 (its split-K exchange goes through L2 under the weight
+        // stream), so the per-GEMV path is the default.
+        const char* env = getenv("TB_DECODE_CHAIN");
+        if (!c.weights_int8 && d->qkv_perm && c.max_batch <= 64 && env && env[0] == '1') {
+            const int cols = (int)std::max<int64_t>(std::max<int64_t>(dm, F), d->qkv_n);
+            d->chain.part_words = chain_part_words(ctx->num_sms, c.max_batch);
+            d->chain.ll_words = chain_ll_words(c.max_batch, cols);
+            A(&d->chain.sync, (size_t)kChainSyncWords);
+            A(&d->chain.part, d->chain.part_words);
+            A(&d->chain.ll, d->chain.ll_words);
+            if (rc) {
+                tb_decoder_destroy(d);
+                return rc;
+            }
+            cudaMemset(d->chain.sync, 0, kChainSyncWords * sizeof(unsigned));
+            cudaMemset(d->chain.part, 0, d->chain.part_words * sizeof(uint64_t));
+            cudaMemset(d->chain.ll, 0, d->chain.ll_words * sizeof(uint64_t));
+            d->use_chain = true;
+        }
     }
     cudaMemset(d->amax_keys, 0, (size_t)c.max_batch * sizeof(unsigned long long));
     cudaMemset(d->amax_cnt, 0, (size_t)c.max_batch * sizeof(unsigned));

@@ -155,6 +155,39 @@ def linear(x, w, bias=None, residual=None, swiglu=False, out_f32=False):
     return y
 
 
+class _LinearStep(ctypes.Structure):
+    _fields_ = [("x", ctypes.c_void_p), ("ldx", ctypes.c_int64), ("w", ctypes.c_void_p),
+                ("norm_w", ctypes.c_void_p), ("norm_eps", ctypes.c_float), ("residual", ctypes.c_void_p),
+                ("y", ctypes.c_void_p), ("ldy", ctypes.c_int64), ("N", ctypes.c_int64), ("K", ctypes.c_int64),
+                ("flags", ctypes.c_int)]
+
+
+def linear_chain(steps):
+    """Dependent decode linear layers in one persistent launch (tb_linear_chain_fwd).
+
+    steps: dicts with x [M, K] and w [N, K] (bf16), y (the output tensor, written;
+    step i + 1 may take step i's y as its x or residual) and optional norm_w
+    ([K] RMSNorm gains fused in front of the matmul), eps, residual (may be y),
+    swiglu.  Every step has the same M <= 64 rows."""
+    arr = (_LinearStep * len(steps))()
+    M = None
+    for i, st in enumerate(steps):
+        x, w, y = st["x"], st["w"], st["y"]
+        _cuda(x, w, y, st.get("norm_w"), st.get("residual"))
+        K = x.shape[-1]
+        m = x.numel() // K
+        M = m if M is None else M
+        if m != M:
+            raise ValueError("linear_chain: every step needs the same number of rows")
+        flags = (TB_EPI_SWIGLU if st.get("swiglu") else 0) | (TB_EPI_RESIDUAL if st.get("residual") is not None else 0)
+        addr = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+        arr[i] = _LinearStep(addr(x), x.stride(-2) if x.dim() > 1 else K, addr(w), addr(st.get("norm_w")),
+                             float(st.get("eps", 1e-5)), addr(st.get("residual")), addr(y),
+                             y.stride(-2) if y.dim() > 1 else y.shape[-1], w.shape[0], K, flags)
+    ctx = context()
+    check(ctx, lib().tb_linear_chain_fwd(ctx, arr, ctypes.c_int(len(steps)), _i64(M)))
+
+
 TB_OP = {"linear": 0, "matmul": 1, "int8_linear": 2, "rmsnorm": 3, "layernorm": 4, "act": 5, "attn": 6,
          "conv2d": 7, "quantize_int8": 8}
 

@@ -135,10 +135,15 @@ def _oracle_with_cache(dec, cfg, p, B, length, int8):
 C4_WIDTH = dict(n_layers=2, d_model=2048, n_heads=32, n_kv_heads=8, head_dim=64, ffn_hidden=8192, vocab=32000)
 
 
-def test_decoder_c4_width_bf16():
+# chain: decode runs O, gate/up, down and the next layer's QKV of each layer as
+# one persistent launch (opt-in, TB_DECODE_CHAIN=1); off: one GEMV launch per
+# matrix (the default).
+@pytest.mark.parametrize("chain", [True, False])
+def test_decoder_c4_width_bf16(chain, monkeypatch):
     # prefill: 16 sequences x 16 tokens (256 rows: the tensor-core GEMM path and
     # prefill attention); then decode at batch 16 (the benchmark's decode GEMVs)
     dev()
+    monkeypatch.setenv("TB_DECODE_CHAIN", "1" if chain else "0")
     cfg = SmallCfg(**C4_WIDTH)
     p = random_params(cfg, seed=12)
     dec = make(cfg, max_batch=16, max_seq=64)
