@@ -136,7 +136,6 @@ int tb_destroy(tb_ctx* ctx) {
     cudaSetDevice(ctx->device);
     if (ctx->d_err) cudaFree(ctx->d_err);
     if (ctx->chain_sync) cudaFree(ctx->chain_sync);
-    if (ctx->chain_part) cudaFree(ctx->chain_part);
     if (ctx->chain_ll) cudaFree(ctx->chain_ll);
     delete ctx;
     return TB_OK;

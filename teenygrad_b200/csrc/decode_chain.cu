@@ -9,39 +9,44 @@
 // RMSNorm, RoPE, KV-cache write) -- as phases of one persistent grid, one CTA
 // per SM.  Weights never depend on the previous phase, so each CTA's weight
 // producer streams straight on into the next phase's tiles while the current
-// phase's partial sums are still being reduced.
+// phase is still being reduced.
 //
-// Work split: each phase's weight blocks (256 rows x 64 K, tile-major) are
-// cut into equal contiguous ranges, one per CTA; a range is cut again at tile
-// boundaries into items (tile, K range).  The CTAs that share a tile
-// ("contributors", consecutive CTAs) publish their 256 x NT f32 partial sums
-// in global slots; each then reduces a 1/n slice of the tile's row pairs over
-// all slots in contributor order (deterministic) and runs the epilogue on it.
-// An item that covers its tile's whole K range finishes from registers.
+// Work split: the grid is NC thread-block clusters of CS CTAs.  A phase's
+// 256-row weight tiles are dealt to the clusters in turn (phases with fewer
+// tiles than clusters start where the previous phase stopped, so they fall on
+// different clusters); the CS CTAs of a cluster split each tile's K range.
+// The split-K partial sums are reduced inside the cluster over distributed
+// shared memory: rank r owns the row pairs [r*P, (r+1)*P), P = 128 / CS, and
+// every rank pushes its partials of those pairs into the owner's receive
+// buffer with st.async (completing on the owner's mbarrier); owners add the
+// CS slots in rank order (deterministic) and run the epilogue.  Receive
+// buffers are double-buffered; an owner frees a buffer by arriving on each
+// sender's mbarrier.
 //
-// Handoffs inside the grid use flagged words instead of fences and counters:
-// every partial sum, and every output value a later phase reads (its x or its
-// residual), is stored as one 8-byte word (f32 value, 32-bit flag) with a
-// single store, and the reader polls the words themselves until the flag of
-// this launch and phase appears (epoch * 8 + phase + 1; the epoch advances at
-// the end of every launch).  A handoff is then one L2 round trip, with no
-// release fence on the writer's side and no flag word to poll first.  Outputs
-// are also written in their normal layout (for the kernels after this one),
-// except where a later phase of the same launch rewrites the same buffer.
+// Handoffs between phases (a phase's x, or its residual, written by an
+// earlier phase) use flagged words: such an output is also stored as 8-byte
+// words (f32 value, 32-bit flag) with single stores, and the readers poll the
+// words until the flag of this launch and phase appears (epoch * 8 + phase +
+// 1; the epoch advances at the end of every launch) -- one L2 round trip, no
+// fence on the writer's side.  Outputs are also written in their normal
+// layout for the kernels after this one, except where a later phase of the
+// same launch rewrites the same buffer.
 //
-// All CTAs are resident (grid = SMs, one CTA per SM by shared memory), and
-// every wait is bounded: a wait that gives up sets the device error word and
-// every other wait then returns at once.  The last CTA to finish advances the
-// epoch for the next launch.
+// All CTAs are resident (grid = the clusters that fit, one CTA per SM by
+// shared memory), and every wait is bounded: a wait that gives up sets the
+// device error word and every other wait then returns at once.  The last CTA
+// to finish advances the epoch for the next launch.
 //
 // Roles (16 warps): warp 0 streams weights (and the norm gains) with TMA,
 // warps 1 and 2 issue the MMAs of one 128-row half each into double-buffered
 // TMEM accumulators, warp 3 loads activation tiles that come from before the
-// launch (TMA) and owns the TMEM allocation, warps 4-11 run the epilogue and
-// warps 12-15 build the activation tiles that come from an earlier phase
-// (from flagged words) and apply the fused RMSNorm (bf16(x * w), with each
-// token's sum of squares).
+// launch (TMA) and owns the TMEM allocation, warps 4-11 run the exchange and
+// the epilogue and warps 12-15 build the activation tiles that come from an
+// earlier phase (from flagged words) and apply the fused RMSNorm (bf16(x * w),
+// with each token's sum of squares).
 #include <string.h>
+
+#include <mutex>
 
 #include "common.cuh"
 #include "decode_chain.h"
@@ -53,8 +58,8 @@ namespace {
 
 struct PhaseInfo {
     Epi ep;
-    int Nw, K, nk, tiles, blocks, g_eff, ncols;
-    int base;               // the phase's CTA range starts at CTA base (mod the grid)
+    int Nw, K, nk, tiles, ncols;
+    int base;               // the first cluster of the phase's tiles
     int norm;
     int x_src;              // -1: x is from before the launch (TMA); else the phase that wrote it
     int r_src;              // -1: the residual is from before the launch; else the phase that wrote it
@@ -63,7 +68,6 @@ struct PhaseInfo {
     uint64_t* ll;           // this phase's flagged output [Mtok][ncols]
     const uint64_t* x_ll;   // x as flagged words [Mtok][K] (x_src >= 0)
     const uint64_t* r_ll;   // the residual as flagged words [Mtok][ncols] (r_src >= 0)
-    uint64_t* part;         // this phase's partial slots
 };
 
 struct ChainPhaseParams {
@@ -74,7 +78,7 @@ struct ChainPhaseParams {
 
 struct ChainParams {
     ChainPhaseParams ph[kChainMaxPhases];
-    int nph, Mtok;
+    int nph, Mtok, cs;
     int* err;
     unsigned* sync;   // [0] CTAs finished, [1] epoch
 };
@@ -82,8 +86,6 @@ struct ChainParams {
 constexpr int kConvWarps = 4;
 constexpr int kEpiThreads = 256;
 constexpr unsigned long long kDrainNs = 10000000ull;   // copies still in flight when a CTA gives up
-
-__host__ __device__ constexpr int slot_words(int nt) { return nt * 256 + nt; }   // [NT][128 pairs][2] + [NT] sums of squares
 
 __device__ __forceinline__ void named_bar(int id, int n) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
@@ -103,6 +105,16 @@ __device__ __forceinline__ bool named_bar_and(int id, int n, bool v) {
     return r != 0;
 }
 
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t map_rank(uint32_t local, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+    return r;
+}
+
 // ------------------------------------------------------------ flagged words
 __device__ __forceinline__ uint64_t ll_word(float v, uint32_t flag) {
     return ((uint64_t)flag << 32) | (uint64_t)__float_as_uint(v);
@@ -112,9 +124,6 @@ __device__ __forceinline__ float ll_val(uint64_t w) { return __uint_as_float((ui
 
 __device__ __forceinline__ void st_ll(uint64_t* p, uint64_t w) {
     asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
-}
-__device__ __forceinline__ void st_ll2(uint64_t* p, uint64_t a, uint64_t b) {
-    asm volatile("st.relaxed.gpu.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b) : "memory");
 }
 __device__ __forceinline__ uint64_t ld_ll(const uint64_t* p) {
     uint64_t v;
@@ -134,7 +143,6 @@ struct Repoll {
     uint32_t spins = 0;
     __device__ __forceinline__ bool again(int* err) {
         if (t0 == 0) t0 = globaltimer();
-        __nanosleep(128);
         if ((++spins & 15u) == 0) {
             if (*(volatile int*)err != 0) return false;
             if (globaltimer() - t0 > kWaitLimitNs) {
@@ -154,69 +162,29 @@ __device__ void drain_wait(uint32_t bar, uint32_t parity, unsigned long long dea
 }
 
 // ------------------------------------------------------------------- items
+// A cluster's tiles in a phase: base-rotated cluster index g', tiles g',
+// g' + NC, ...; every rank takes the K blocks [r*nk/CS, (r+1)*nk/CS) of each.
 struct Cursor {
-    int b, b1;
-    int c;   // this CTA's index in the phase's (rotated) range
+    int t;
 };
 struct Item {
-    int t, kb0, kb1, c_lo, n;
+    int t, kb0, kb1;
 };
 
-// This CTA's contiguous range of the phase's blocks.  A phase's g_eff CTAs
-// start at CTA `base` (mod the grid), so phases that use part of the grid
-// fall on different CTAs.
-__device__ __forceinline__ Cursor item_begin(const PhaseInfo& ph, int cta) {
-    const int c = (cta - ph.base + (int)gridDim.x) % (int)gridDim.x;
-    Cursor cur{0, 0, c};
-    if (c < ph.g_eff) {
-        cur.b = (int)((int64_t)c * ph.blocks / ph.g_eff);
-        cur.b1 = (int)((int64_t)(c + 1) * ph.blocks / ph.g_eff);
-    }
-    return cur;
+__device__ __forceinline__ Cursor item_begin(const PhaseInfo& ph, int cluster, int nc) {
+    return Cursor{(cluster - ph.base % nc + nc) % nc};
 }
 
-// The CTA whose range holds block b (g_eff <= blocks: no range is empty).
-__device__ __forceinline__ int block_owner(const PhaseInfo& ph, int b) {
-    return (int)(((int64_t)(b + 1) * ph.g_eff - 1) / ph.blocks);
-}
-
-__device__ __forceinline__ bool item_next(const PhaseInfo& ph, Cursor& cur, Item& it) {
-    if (cur.b >= cur.b1) return false;
-    const int t = cur.b / ph.nk;
-    const int e = min(cur.b1, (t + 1) * ph.nk);
-    it.t = t;
-    it.kb0 = cur.b - t * ph.nk;
-    it.kb1 = e - t * ph.nk;
-    it.c_lo = block_owner(ph, t * ph.nk);
-    it.n = block_owner(ph, (t + 1) * ph.nk - 1) - it.c_lo + 1;
-    cur.b = e;
+__device__ __forceinline__ bool item_next(const PhaseInfo& ph, Cursor& cur, Item& it, int nc, int rank, int cs) {
+    if (cur.t >= ph.tiles) return false;
+    it.t = cur.t;
+    it.kb0 = rank * ph.nk / cs;
+    it.kb1 = (rank + 1) * ph.nk / cs;
+    cur.t += nc;
     return true;
 }
 
 // ------------------------------------------------------------- epilogue I/O
-// Residual of token m for the pair: flagged words of an earlier phase, or the
-// normal layout (written before the launch).
-__device__ __forceinline__ void chain_resid(const PhaseInfo& ph, const EpiPair& k, int m, int Mtok, uint32_t rflag,
-                                            int* err, float& r0, float& r1) {
-    r0 = r1 = 0.f;
-    const Epi& ep = ph.ep;
-    if (!ep.resid || ep.swiglu || ep.rope_tab || m >= Mtok) return;
-    if (ph.r_src >= 0) {
-        const uint64_t* r = ph.r_ll + (int64_t)m * ph.ncols;
-        const uint64_t ok0 = (uint64_t)rflag << 32;
-        uint64_t w0 = ok0, w1 = ok0;
-        Repoll rp;
-        do {
-            if (k.in0) w0 = ld_ll(r + k.n0);
-            if (k.in1) w1 = ld_ll(r + k.n1);
-        } while (!(ll_ok(w0, rflag) && ll_ok(w1, rflag)) && rp.again(err));
-        r0 = ll_val(w0);
-        r1 = ll_val(w1);
-    } else {
-        epi_resid_bf16(ep, k, m, Mtok, r0, r1);
-    }
-}
-
 // Epilogue of (token m, pair): RoPE phases store q / k / v in their normal
 // layout only; others store y normally (std_out) and / or as flagged words.
 __device__ __forceinline__ void chain_finish(const PhaseInfo& ph, const EpiPair& k, int tile, int m, float a0,
@@ -252,35 +220,39 @@ __device__ __forceinline__ void chain_finish(const PhaseInfo& ph, const EpiPair&
     }
 }
 
-template <int NT, int STAGES>
+template <int NT, int STAGES, int RBUF>
 struct ChainCfg {
     static constexpr int W_BYTES = 256 * 128;   // [256 rows][64 bf16], 128-B swizzle
     static constexpr int X_BYTES = NT * 128;    // [NT][64 bf16], one swizzle atom wide
     static constexpr int G_BYTES = 128;         // the block's 64 norm gains
+    // a message from one rank to one owner: [NT tokens][P pairs][2] partials, then
+    // the sender's NT sums of squares; an owner's buffer holds CS of them (<= 8)
+    static constexpr int RECV_F = NT * 256 + 8 * NT;
     static constexpr int OFF_X = STAGES * W_BYTES;
     static constexpr int OFF_G = OFF_X + STAGES * X_BYTES;
-    static constexpr int OFF_BAR = OFF_G + STAGES * G_BYTES;
-    static constexpr int N_BARS = 3 * STAGES + 9;
+    static constexpr int OFF_RECV = OFF_G + STAGES * G_BYTES;
+    static constexpr int OFF_BAR = OFF_RECV + RBUF * RECV_F * 4;
+    static constexpr int N_BARS = 3 * STAGES + 9 + 2 * RBUF;
     static constexpr int OFF_SLOT = OFF_BAR + N_BARS * 8;
     static constexpr int OFF_SS = OFF_SLOT + 16;            // [2][NT] item sums of squares
-    static constexpr int OFF_RINV = OFF_SS + 2 * NT * 4;     // [NT] 1/rms of the reduced slice
+    static constexpr int OFF_RINV = OFF_SS + 2 * NT * 4;     // [NT] 1/rms of the owned slice
     static constexpr int OFF_INFO = (OFF_RINV + NT * 4 + 15) & ~15;
     static constexpr int SMEM = OFF_INFO + kChainMaxPhases * (int)sizeof(PhaseInfo) + 1024;
     static constexpr int THREADS = 512;
     static constexpr int TMEM_COLS = 4 * NT < 32 ? 32 : 4 * NT;   // [2 buffers][2 halves][NT]
-    static constexpr int SLOT_W = slot_words(NT);
     static_assert(SMEM <= 227 * 1024, "shared memory");
     static_assert(SMEM > 114 * 1024, "one CTA per SM: the grid's CTAs wait on one another");
 };
 
-template <int NT, int STAGES>
+template <int NT, int STAGES, int RBUF>
 __global__ void __launch_bounds__(512, 1) decode_chain_kernel(const __grid_constant__ ChainParams P) {
-    using C = ChainCfg<NT, STAGES>;
+    using C = ChainCfg<NT, STAGES, RBUF>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_align1024(smem_raw);
     uint8_t* sW = smem;
     uint8_t* sX = smem + C::OFF_X;
     uint8_t* sG = smem + C::OFF_G;
+    float* recv = reinterpret_cast<float*>(smem + C::OFF_RECV);   // [RBUF][RECV_F]
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
     const uint32_t full0 = smem_u32(bars);                  // [STAGES] weights (+ TMA activations) landed
     const uint32_t empty0 = smem_u32(bars + STAGES);        // [STAGES] MMAs done with the stage
@@ -290,6 +262,8 @@ __global__ void __launch_bounds__(512, 1) decode_chain_kernel(const __grid_const
     const uint32_t ssf0 = accf0 + 32;                       // [2] item sums of squares written
     const uint32_t sse0 = accf0 + 48;                       // [2] item sums of squares read
     const uint32_t mmad = accf0 + 64;                       // every MMA of the CTA done
+    const uint32_t rfull0 = accf0 + 72;                     // [RBUF] peers' messages landed
+    const uint32_t rfree0 = rfull0 + 8 * RBUF;              // [RBUF] every owner has read my last messages
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_SLOT);
     float* s_ss = reinterpret_cast<float*>(smem + C::OFF_SS);
     float* s_rinv = reinterpret_cast<float*>(smem + C::OFF_RINV);
@@ -297,8 +271,11 @@ __global__ void __launch_bounds__(512, 1) decode_chain_kernel(const __grid_const
 
     pdl_trigger();
     const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
-    const int cta = blockIdx.x;
-    const int nph = P.nph, Mtok = P.Mtok;
+    const int nph = P.nph, Mtok = P.Mtok, CS = P.cs;
+    const int rank = (int)(blockIdx.x % (unsigned)CS), cluster = (int)(blockIdx.x / (unsigned)CS);
+    const int NC = (int)(gridDim.x / (unsigned)CS);
+    const int PP = 128 / CS;                                 // row pairs an owner reduces
+    const int MSG_F = NT * PP * 2 + NT;                      // floats per message
     int* err = P.err;
 
     if (threadIdx.x == 0) {
@@ -314,13 +291,21 @@ __global__ void __launch_bounds__(512, 1) decode_chain_kernel(const __grid_const
             mbar_init(sse0 + 8 * b, kEpiThreads / 32);
         }
         mbar_init(mmad, 2);
+        for (int b = 0; b < RBUF; b++) {
+            mbar_init(rfull0 + 8 * b, 1);
+            mbar_init(rfree0 + 8 * b, CS > 1 ? CS - 1 : 1);
+        }
         fence_barrier_init();
+        // arm every receive buffer for its first messages
+        if (CS > 1)
+            for (int b = 0; b < RBUF; b++) mbar_expect_tx(rfull0 + 8 * b, (uint32_t)((CS - 1) * MSG_F * 4));
     }
     if (threadIdx.x < nph) info[threadIdx.x] = P.ph[threadIdx.x].info;
     if (warp == 3) tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    if (CS > 1) cluster_sync_all();   // the peers' barriers exist before any message
     const uint32_t tmem = *tmem_slot;
 
     if (warp == 0) {
@@ -332,9 +317,9 @@ __global__ void __launch_bounds__(512, 1) decode_chain_kernel(const __grid_const
             for (int p = 0; p < nph && ok; p++) {
                 const PhaseInfo& ph = info[p];
                 const __nv_bfloat16* gains = reinterpret_cast<const __nv_bfloat16*>(ph.ep.norm_w);
-                Cursor cur = item_begin(ph, cta);
+                Cursor cur = item_begin(ph, cluster, NC);
                 Item it;
-                while (ok && item_next(ph, cur, it)) {
+                while (ok && item_next(ph, cur, it, NC, rank, CS)) {
                     for (int kb = it.kb0; kb < it.kb1; kb++, blk++) {
                         const int s = blk % STAGES;
                         if (blk >= STAGES && !mbar_wait(empty0 + 8 * s, ((blk / STAGES) - 1) & 1, err, DEV_ERR_TIMEOUT_EMPTY)) {
@@ -361,9 +346,9 @@ __global__ void __launch_bounds__(512, 1) decode_chain_kernel(const __grid_const
             bool ok = true;
             for (int p = 0; p < nph && ok; p++) {
                 const PhaseInfo& ph = info[p];
-                Cursor cur = item_begin(ph, cta);
+                Cursor cur = item_begin(ph, cluster, NC);
                 Item it;
-                while (ok && item_next(ph, cur, it)) {
+                while (ok && item_next(ph, cur, it, NC, rank, CS)) {
                     const int buf = j & 1;
                     if (j >= 2 && !mbar_wait(acce0 + 8 * buf, ((j >> 1) - 1) & 1, err, DEV_ERR_TIMEOUT_MISC)) {
                         ok = false;
@@ -407,9 +392,9 @@ __global__ void __launch_bounds__(512, 1) decode_chain_kernel(const __grid_const
             bool ok = true;
             for (int p = 0; p < nph && ok; p++) {
                 const PhaseInfo& ph = info[p];
-                Cursor cur = item_begin(ph, cta);
+                Cursor cur = item_begin(ph, cluster, NC);
                 Item it;
-                while (ok && item_next(ph, cur, it)) {
+                while (ok && item_next(ph, cur, it, NC, rank, CS)) {
                     for (int kb = it.kb0; kb < it.kb1; kb++, blk++) {
                         const int s = blk % STAGES;
                         if (blk >= STAGES && !mbar_wait(empty0 + 8 * s, ((blk / STAGES) - 1) & 1, err, DEV_ERR_TIMEOUT_EMPTY)) {
@@ -427,17 +412,17 @@ __global__ void __launch_bounds__(512, 1) decode_chain_kernel(const __grid_const
             }
         }
     } else if (warp < 12) {
-        // ---------------- epilogue warps.  Per phase, first every item of this
-        // CTA: read the accumulator out, finish an item that covers its whole tile,
-        // else publish its partial slot.  Then reduce this CTA's slice of the
-        // shared tiles (only the first and the last item of a CTA's range can
-        // share a tile).
+        // ---------------- exchange and epilogue warps.  Per tile: read the
+        // accumulator out; push each owner its row pairs (st.async into the
+        // owner's receive buffer); as owner, add the CS messages in rank order and
+        // run the epilogue on the owned pairs; free the buffer on every sender.
         pdl_wait();
         const uint32_t ep_base = *(volatile const unsigned*)(P.sync + 1) * 8u + 1u;   // flag of phase 0
         const int e = threadIdx.x - 128;
         const int q = warp & 3, part = (warp - 4) >> 2, l = q * 32 + lane;
         constexpr int TP = NT / 2;
         const uint32_t t_row = tmem + ((uint32_t)(q * 32) << 16);
+        const int owner = l / PP, pl = l % PP;
         bool ok = true;
         int j = 0;
         for (int p = 0; p < nph && ok; p++) {
@@ -445,13 +430,11 @@ __global__ void __launch_bounds__(512, 1) decode_chain_kernel(const __grid_const
             const Epi& ep = ph.ep;
             const uint32_t flag = ep_base + (uint32_t)p;
             const uint32_t rflag = ep_base + (uint32_t)(ph.r_src < 0 ? 0 : ph.r_src);
-            Cursor cur = item_begin(ph, cta);
-            const int cr = cur.c;   // rotated CTA index: slot and contributor numbering
-            Item it, dfr[2];
-            int nd = 0;
             const int posb = epi_posb(ep);
-            while (item_next(ph, cur, it)) {
-                const int buf = j & 1;
+            Cursor cur = item_begin(ph, cluster, NC);
+            Item it;
+            while (item_next(ph, cur, it, NC, rank, CS)) {
+                const int buf = j & 1, rb = j % RBUF, ru = j / RBUF;
                 ok = named_bar_and(1, kEpiThreads, mbar_wait(accf0 + 8 * buf, (j >> 1) & 1, err, DEV_ERR_TIMEOUT_ACC));
                 if (!ok) break;
                 tc_fence_after();
@@ -473,17 +456,14 @@ __global__ void __launch_bounds__(512, 1) decode_chain_kernel(const __grid_const
                 float ss_e = 0.f;
 #pragma unroll
                 for (int t = 0; t < TP; t++) ss_tok[t] = ph.norm ? s_ss[buf * NT + part * TP + t] : 0.f;
-                if (ph.norm && e < NT) ss_e = s_ss[buf * NT + e];
+                if (e < NT) ss_e = ph.norm ? s_ss[buf * NT + e] : 0.f;
                 __syncwarp();
                 if (lane == 0) mbar_arrive(sse0 + 8 * buf);
-                ok = named_bar_and(1, kEpiThreads, sok && (it.n == 1 || nd < 2));
-                if (!ok) {
-                    if (e == 0 && sok) atomicOr(err, DEV_ERR_TIMEOUT_MISC);   // (a third shared tile cannot occur)
-                    break;
-                }
                 j++;
-                if (it.n == 1) {
-                    // the item covers its tile's whole K range: finish from registers
+                if (CS == 1) {
+                    ok = named_bar_and(1, kEpiThreads, sok);
+                    if (!ok) break;
+                    // one CTA holds the tile's whole K range: finish from registers
                     EpiPair kp = epi_pair(ep, it.t, ph.Nw, l, posb);
                     kp.cs = epi_rope_cs(ep, kp);
 #pragma unroll
@@ -491,192 +471,144 @@ __global__ void __launch_bounds__(512, 1) decode_chain_kernel(const __grid_const
                         const int m = part * TP + t;
                         if (m < Mtok) {
                             const float rs = ph.norm ? rsqrtf(ss_tok[t] * (1.0f / (float)ph.K) + ep.norm_eps) : 1.f;
-                            float r0, r1;
-                            chain_resid(ph, kp, m, Mtok, rflag, err, r0, r1);
-                            chain_finish(ph, kp, it.t, m, acc[0][t] * rs, acc[1][t] * rs, r0, r1, flag, err);
-                        }
-                    }   // (a residual here is rare: residual phases have few tiles, so their items share tiles)
-                } else {
-                    // publish the partial slot as flagged words: no fence, no counter
-                    uint64_t* ps = ph.part + (int64_t)(cr + it.t) * C::SLOT_W;
-#pragma unroll
-                    for (int t = 0; t < TP; t++)
-                        st_ll2(ps + ((part * TP + t) * 128 + l) * 2, ll_word(acc[0][t], flag), ll_word(acc[1][t], flag));
-                    if (ph.norm && e < NT) st_ll(ps + NT * 256 + e, ll_word(ss_e, flag));
-                    dfr[nd++] = it;
-                }
-            }
-            // the shared tiles: reduce this CTA's slice of the row pairs over every
-            // contributor's slot in contributor order.  Thread e takes items
-            // idx = e + u * 256 (token idx / np, pair p0 + idx % np).  Every word
-            // the slice needs -- its slot words, the sums of squares, the
-            // residuals -- is loaded in one batch before any flag is checked, so
-            // the reduction costs one L2 round trip (the host keeps n <= 8).
-            for (int di = 0; di < nd && ok; di++) {
-                const Item& dt = dfr[di];
-                const int k = cr - dt.c_lo;
-                const int p0 = k * 128 / dt.n, np = (k + 1) * 128 / dt.n - p0;
-                const int nitems = np * Mtok;
-                const int U = (nitems + kEpiThreads - 1) / kEpiThreads;
-                const uint64_t* base0 = ph.part + (int64_t)(dt.c_lo + dt.t) * C::SLOT_W;
-                constexpr int kBatch = 12;   // slot words (pairs of acc) one thread loads at once
-                if (U <= 4 && U * dt.n <= kBatch && dt.n <= 8) {
-                    // per item u: slot word offset, residual word offset (flagged
-                    // residual), RoPE angle; then the (item, contributor) loads flattened
-                    int off[4], ro[4];
-                    float a0[4], a1[4];
-                    float2 pcs[4];
-                    bool rin0[4], rin1[4];
-#pragma unroll
-                    for (int u = 0; u < 4; u++) {
-                        const int idx = e + u * kEpiThreads;
-                        off[u] = idx < nitems ? ((idx / np) * 128 + p0 + idx % np) * 2 : -1;
-                        ro[u] = -1;
-                        rin0[u] = rin1[u] = false;
-                        a0[u] = a1[u] = 0.f;
-                        pcs[u] = make_float2(1.f, 0.f);
-                        if (idx < nitems) {
-                            const EpiPair kp = epi_pair(ep, dt.t, ph.Nw, p0 + idx % np, posb);
-                            pcs[u] = epi_rope_cs(ep, kp);
-                            if (ep.resid && !ep.swiglu && !ep.rope_tab && ph.r_src >= 0) {
-                                ro[u] = (idx / np) * ph.ncols + kp.n0;
-                                rin0[u] = kp.in0;
-                                rin1[u] = kp.in1;
-                            }
-                        }
-                    }
-                    const int total = U * dt.n;
-                    uint64_t va[kBatch], vb[kBatch], vs[8], rw0[4], rw1[4];
-                    bool good;
-                    Repoll rp;
-                    do {
-                        good = true;
-                        int uu = 0, rr = 0;
-#pragma unroll
-                        for (int i = 0; i < kBatch; i++) {
-                            const int o = uu == 0 ? off[0] : uu == 1 ? off[1] : uu == 2 ? off[2] : off[3];
-                            va[i] = vb[i] = (uint64_t)flag << 32;
-                            if (i < total && o >= 0) ld_ll2(base0 + (int64_t)rr * C::SLOT_W + o, va[i], vb[i]);
-                            if (++rr == dt.n) {
-                                rr = 0;
-                                uu++;
-                            }
-                        }
-#pragma unroll
-                        for (int r = 0; r < 8; r++) {
-                            vs[r] = (uint64_t)flag << 32;
-                            if (ph.norm && e < NT && r < dt.n) vs[r] = ld_ll(base0 + (int64_t)r * C::SLOT_W + NT * 256 + e);
-                        }
-#pragma unroll
-                        for (int u = 0; u < 4; u++) {
-                            rw0[u] = rw1[u] = (uint64_t)rflag << 32;
-                            if (ro[u] >= 0 && rin0[u]) rw0[u] = ld_ll(ph.r_ll + ro[u]);
-                            if (ro[u] >= 0 && rin1[u]) rw1[u] = ld_ll(ph.r_ll + ro[u] + 128);
-                        }
-#pragma unroll
-                        for (int i = 0; i < kBatch; i++) good = good && ll_ok(va[i], flag) && ll_ok(vb[i], flag);
-#pragma unroll
-                        for (int r = 0; r < 8; r++) good = good && ll_ok(vs[r], flag);
-#pragma unroll
-                        for (int u = 0; u < 4; u++) good = good && ll_ok(rw0[u], rflag) && ll_ok(rw1[u], rflag);
-                    } while (!good && rp.again(err));
-                    // sums in contributor order
-                    {
-                        int uu = 0, rr = 0;
-#pragma unroll
-                        for (int i = 0; i < kBatch; i++) {
-                            if (i < total) {
-                                const float x0 = ll_val(va[i]), x1 = ll_val(vb[i]);
-#pragma unroll
-                                for (int w = 0; w < 4; w++)
-                                    if (uu == w) {
-                                        a0[w] += x0;
-                                        a1[w] += x1;
-                                    }
-                            }
-                            if (++rr == dt.n) {
-                                rr = 0;
-                                uu++;
-                            }
-                        }
-                    }
-                    if (ph.norm) {
-                        float ssum = 0.f;
-#pragma unroll
-                        for (int r = 0; r < 8; r++)
-                            if (r < dt.n) ssum += ll_val(vs[r]);
-                        if (e < NT) s_rinv[e] = rsqrtf(ssum * (1.0f / (float)ph.K) + ep.norm_eps);
-                        named_bar(1, kEpiThreads);
-                    }
-#pragma unroll
-                    for (int u = 0; u < 4; u++) {
-                        const int idx = e + u * kEpiThreads;
-                        if (idx < nitems) {
-                            const int m = idx / np;
-                            EpiPair kp = epi_pair(ep, dt.t, ph.Nw, p0 + idx % np, posb);
-                            kp.cs = pcs[u];
-                            float r0v = 0.f, r1v = 0.f;
-                            if (ro[u] >= 0) {
-                                r0v = ll_val(rw0[u]);
-                                r1v = ll_val(rw1[u]);
-                            } else {
-                                epi_resid_bf16(ep, kp, m, Mtok, r0v, r1v);
-                            }
-                            const float rs = ph.norm ? s_rinv[m] : 1.f;
-                            chain_finish(ph, kp, dt.t, m, a0[u] * rs, a1[u] * rs, r0v, r1v, flag, err);
-                        }
-                    }
-                } else {
-                    // more contributors or items than one batch holds: one item at a
-                    // time, slots in rounds of 8
-                    if (ph.norm) {
-                        float ssum = 0.f;
-                        if (e < NT)
-                            for (int r0 = 0; r0 < dt.n; r0++) {
-                                const uint64_t* sp = base0 + (int64_t)r0 * C::SLOT_W + NT * 256 + e;
-                                uint64_t w;
+                            float r0 = 0.f, r1 = 0.f;
+                            if (ep.resid && ph.r_src >= 0) {
+                                const uint64_t* rr = ph.r_ll + (int64_t)m * ph.ncols;
+                                uint64_t w0 = (uint64_t)rflag << 32, w1 = w0;
                                 Repoll rp;
                                 do {
-                                    w = ld_ll(sp);
-                                } while (!ll_ok(w, flag) && rp.again(err));
-                                ssum += ll_val(w);
+                                    if (kp.in0) w0 = ld_ll(rr + kp.n0);
+                                    if (kp.in1) w1 = ld_ll(rr + kp.n1);
+                                } while (!(ll_ok(w0, rflag) && ll_ok(w1, rflag)) && rp.again(err));
+                                r0 = ll_val(w0);
+                                r1 = ll_val(w1);
+                            } else {
+                                epi_resid_bf16(ep, kp, m, Mtok, r0, r1);
                             }
-                        if (e < NT) s_rinv[e] = rsqrtf(ssum * (1.0f / (float)ph.K) + ep.norm_eps);
-                        named_bar(1, kEpiThreads);
-                    }
-                    for (int idx = e; idx < nitems; idx += kEpiThreads) {
-                        const int m = idx / np;
-                        EpiPair kp = epi_pair(ep, dt.t, ph.Nw, p0 + idx % np, posb);
-                        kp.cs = epi_rope_cs(ep, kp);
-                        float r0v, r1v;
-                        chain_resid(ph, kp, m, Mtok, rflag, err, r0v, r1v);
-                        const uint64_t* src = base0 + (int64_t)((m * 128 + p0 + idx % np) * 2);
-                        float s0 = 0.f, s1 = 0.f;
-                        for (int r0 = 0; r0 < dt.n; r0 += 8) {
-                            uint64_t va[8], vb[8];
-                            bool good;
-                            Repoll rp;
-                            do {
-                                good = true;
-#pragma unroll
-                                for (int i = 0; i < 8; i++) {
-                                    va[i] = vb[i] = (uint64_t)flag << 32;
-                                    if (r0 + i < dt.n) ld_ll2(src + (int64_t)(r0 + i) * C::SLOT_W, va[i], vb[i]);
-                                    good = good && ll_ok(va[i], flag) && ll_ok(vb[i], flag);
-                                }
-                            } while (!good && rp.again(err));
-#pragma unroll
-                            for (int i = 0; i < 8; i++)
-                                if (r0 + i < dt.n) {
-                                    s0 += ll_val(va[i]);
-                                    s1 += ll_val(vb[i]);
-                                }
+                            chain_finish(ph, kp, it.t, m, acc[0][t] * rs, acc[1][t] * rs, r0, r1, flag, err);
                         }
-                        const float rs = ph.norm ? s_rinv[m] : 1.f;
-                        chain_finish(ph, kp, dt.t, m, s0 * rs, s1 * rs, r0v, r1v, flag, err);
+                    }
+                    continue;
+                }
+                // ---- send: my partials of owner o's pairs into o's buffer rb, slot [rank]
+                bool fok = true;
+                if (ru >= 1) fok = mbar_wait(rfree0 + 8 * rb, (ru - 1) & 1, err, DEV_ERR_TIMEOUT_MISC);
+                ok = named_bar_and(1, kEpiThreads, sok && fok);
+                if (!ok) break;
+                {
+                    float* slot = recv + rb * C::RECV_F + rank * MSG_F;
+                    const uint32_t loc = smem_u32(slot + (part * TP * PP + pl) * 2);
+                    if (owner == rank) {
+#pragma unroll
+                        for (int t = 0; t < TP; t++)
+                            *reinterpret_cast<float2*>(slot + ((part * TP + t) * PP + pl) * 2) = make_float2(acc[0][t], acc[1][t]);
+                    } else {
+                        const uint32_t rdst = map_rank(loc, owner), rbar = map_rank(rfull0 + 8 * rb, owner);
+#pragma unroll
+                        for (int t = 0; t < TP; t++)
+                            asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(
+                                             rdst + t * PP * 8),
+                                         "f"(acc[0][t]), "f"(acc[1][t]), "r"(rbar)
+                                         : "memory");
                     }
                 }
-                if (ph.norm) named_bar(1, kEpiThreads);   // s_rinv is rewritten by the next slice
+                // sums of squares (zeros without the norm): thread e < NT sends
+                // token e's to every owner
+                if (e < NT) {
+                    for (int o = 0; o < CS; o++) {
+                        float* slot = recv + rb * C::RECV_F + rank * MSG_F + NT * PP * 2 + e;
+                        if (o == rank) {
+                            *slot = ss_e;
+                        } else {
+                            const uint32_t rdst = map_rank(smem_u32(slot), o), rbar = map_rank(rfull0 + 8 * rb, o);
+                            asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.f32 [%0], %1, [%2];" ::"r"(rdst),
+                                         "f"(ss_e), "r"(rbar)
+                                         : "memory");
+                        }
+                    }
+                }
+                // ---- receive: owned pairs [rank*PP, (rank+1)*PP) of tile it.t.  The
+                // residuals and RoPE angles of my items are loaded while the
+                // messages are in flight.
+                const int nitems = PP * Mtok;
+                float pr0[4], pr1[4];
+                float2 pcs[4];
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    pr0[u] = pr1[u] = 0.f;
+                    pcs[u] = make_float2(1.f, 0.f);
+                    const int idx = e + u * kEpiThreads;
+                    if (idx < nitems) {
+                        const int m = idx / PP;
+                        const EpiPair kp = epi_pair(ep, it.t, ph.Nw, rank * PP + idx % PP, posb);
+                        pcs[u] = epi_rope_cs(ep, kp);
+                        if (ep.resid && ph.r_src >= 0) {
+                            const uint64_t* rr = ph.r_ll + (int64_t)m * ph.ncols;
+                            uint64_t w0 = (uint64_t)rflag << 32, w1 = w0;
+                            Repoll rp;
+                            do {
+                                if (kp.in0) w0 = ld_ll(rr + kp.n0);
+                                if (kp.in1) w1 = ld_ll(rr + kp.n1);
+                            } while (!(ll_ok(w0, rflag) && ll_ok(w1, rflag)) && rp.again(err));
+                            pr0[u] = ll_val(w0);
+                            pr1[u] = ll_val(w1);
+                        } else {
+                            epi_resid_bf16(ep, kp, m, Mtok, pr0[u], pr1[u]);
+                        }
+                    }
+                }
+                const bool got = mbar_wait(rfull0 + 8 * rb, ru & 1, err, DEV_ERR_TIMEOUT_MISC);
+                ok = named_bar_and(1, kEpiThreads, got);   // (also: my own slot's stores are visible)
+                if (!ok) break;
+                const float* rbuf = recv + rb * C::RECV_F;
+                if (ph.norm) {
+                    if (e < NT) {
+                        float v[8];
+#pragma unroll
+                        for (int r = 0; r < 8; r++) v[r] = r < CS ? rbuf[r * MSG_F + NT * PP * 2 + e] : 0.f;
+                        float s = 0.f;
+#pragma unroll
+                        for (int r = 0; r < 8; r++) s += v[r];
+                        s_rinv[e] = rsqrtf(s * (1.0f / (float)ph.K) + ep.norm_eps);
+                    }
+                    named_bar(1, kEpiThreads);
+                }
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    const int idx = e + u * kEpiThreads;
+                    if (idx < nitems) {
+                        const int m = idx / PP, pi = idx % PP;
+                        float2 v[8];
+#pragma unroll
+                        for (int r = 0; r < 8; r++)
+                            v[r] = r < CS ? *reinterpret_cast<const float2*>(rbuf + r * MSG_F + (m * PP + pi) * 2) : make_float2(0.f, 0.f);
+                        float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+                        for (int r = 0; r < 8; r++) {
+                            a0 += v[r].x;
+                            a1 += v[r].y;
+                        }
+                        EpiPair kp = epi_pair(ep, it.t, ph.Nw, rank * PP + pi, posb);
+                        kp.cs = pcs[u];
+                        const float rs = ph.norm ? s_rinv[m] : 1.f;
+                        chain_finish(ph, kp, it.t, m, a0 * rs, a1 * rs, pr0[u], pr1[u], flag, err);
+                    }
+                }
+                // ---- every read of buffer rb is done: re-arm it, then free it on
+                // every sender (their next message into it may follow).  The arrive
+                // is relaxed: it orders nothing but this CTA's reads of the buffer,
+                // which have returned their values (a release would first wait for
+                // this thread's global stores to drain).
+                named_bar(1, kEpiThreads);
+                if (e == 0) {
+                    mbar_expect_tx(rfull0 + 8 * rb, (uint32_t)((CS - 1) * MSG_F * 4));
+                    for (int o = 0; o < CS; o++)
+                        if (o != rank)
+                            asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(
+                                             map_rank(rfree0 + 8 * rb, o))
+                                         : "memory");
+                }
+                __syncwarp();
             }
         }
     } else {
@@ -693,9 +625,9 @@ __global__ void __launch_bounds__(512, 1) decode_chain_kernel(const __grid_const
         for (int p = 0; p < nph && ok; p++) {
             const PhaseInfo& ph = info[p];
             const uint32_t xflag = ep_base + (uint32_t)(ph.x_src < 0 ? 0 : ph.x_src);
-            Cursor cur = item_begin(ph, cta);
+            Cursor cur = item_begin(ph, cluster, NC);
             Item it;
-            while (ok && item_next(ph, cur, it)) {
+            while (ok && item_next(ph, cur, it, NC, rank, CS)) {
                 float ssv[XI];
 #pragma unroll
                 for (int u = 0; u < XI; u++) ssv[u] = 0.f;
@@ -793,12 +725,14 @@ __global__ void __launch_bounds__(512, 1) decode_chain_kernel(const __grid_const
         }
     }
 
-    // ---------------- exit: free TMEM once every MMA is done; the last CTA
-    // to leave advances the epoch for the next launch
+    // ---------------- exit: every peer is done with this CTA's shared memory
+    // (messages, frees) before it leaves; free TMEM once every MMA is done; the
+    // last CTA to leave advances the epoch for the next launch
     __syncwarp();
     pdl_wait();
     tc_fence_before();
     __syncthreads();
+    if (CS > 1) cluster_sync_all();
     if (warp == 3) {
         drain_wait(mmad, 0, globaltimer() + kDrainNs);
         tc_fence_after();
@@ -857,37 +791,48 @@ int plan_phases(tb_ctx* ctx, const ChainStep* steps, int n, PhasePlan* pl) {
     return TB_OK;
 }
 
-// CTAs a phase runs on: the most (up to the grid) for which no tile has more
-// than kMaxContrib contributors, so each reduction reads at most kMaxContrib
-// slots in one batch.  The other CTAs stream the next phases' weights meanwhile.
-constexpr int kMaxContrib = 8;
-
-int max_contributors(int blocks, int nk, int g) {
-    int mx = 1;
-    for (int t = 0; t * nk < blocks; t++) {
-        const int lo = (int)(((int64_t)(t * nk + 1) * g - 1) / blocks);
-        const int hi = (int)(((int64_t)((t + 1) * nk) * g - 1) / blocks);
-        mx = hi - lo + 1 > mx ? hi - lo + 1 : mx;
-    }
-    return mx;
-}
-
-int phase_ctas(int blocks, int nk, int grid) {
-    int g = blocks < grid ? blocks : grid;
-    while (g > 1 && max_contributors(blocks, nk, g) > kMaxContrib) g--;
-    return g;
-}
-
-template <int NT, int STAGES>
+template <int NT, int STAGES, int RBUF>
 int launch_chain(tb_ctx* ctx, const ChainStep* steps, int n, int Mtok, const ChainScratch& scr) {
-    using C = ChainCfg<NT, STAGES>;
+    using C = ChainCfg<NT, STAGES, RBUF>;
     PhasePlan pl[kChainMaxPhases];
     int rc = plan_phases(ctx, steps, n, pl);
     if (rc) return rc;
+    // cluster size: the largest of 8, 4, 2, 1 that leaves every rank a K block
+    int cs = 8;
+    for (int i = 0; i < n; i++)
+        while (cs > 1 && steps[i].K / 64 < cs) cs >>= 1;
+    auto kern = decode_chain_kernel<NT, STAGES, RBUF>;
+    TB_CUDA_TRY(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    // clusters that can be resident at once (all of the grid waits on one another)
+    static std::mutex mu;
+    static int nc_cache[4] = {0, 0, 0, 0};
+    const int ci = cs == 8 ? 3 : cs == 4 ? 2 : cs == 2 ? 1 : 0;
+    int nc;
+    {
+        std::lock_guard<std::mutex> g(mu);
+        if (!nc_cache[ci]) {
+            cudaLaunchConfig_t q = {};
+            q.gridDim = dim3((unsigned)cs, 1, 1);
+            q.blockDim = dim3(C::THREADS, 1, 1);
+            q.dynamicSmemBytes = C::SMEM;
+            cudaLaunchAttribute qa[1];
+            qa[0].id = cudaLaunchAttributeClusterDimension;
+            qa[0].val.clusterDim.x = (unsigned)cs;
+            qa[0].val.clusterDim.y = 1;
+            qa[0].val.clusterDim.z = 1;
+            q.attrs = qa;
+            q.numAttrs = 1;
+            int m = 0;
+            if (cudaOccupancyMaxActiveClusters(&m, kern, &q) != cudaSuccess || m < 1) {
+                cudaGetLastError();
+                return set_error(ctx, TB_ERR_CUDA, "decode chain: no resident cluster of %d CTAs", cs);
+            }
+            nc_cache[ci] = m * cs > ctx->num_sms ? ctx->num_sms / cs : m;
+        }
+        nc = nc_cache[ci];
+    }
     ChainParams prm;
     memset(&prm, 0, sizeof(prm));
-    const int grid = ctx->num_sms;
-    const size_t region = (size_t)(grid + kChainMaxTiles) * C::SLOT_W;
     size_t ll_used = 0;
     int base = 0;
     for (int i = 0; i < n; i++) {
@@ -904,24 +849,20 @@ int launch_chain(tb_ctx* ctx, const ChainStep* steps, int n, int Mtok, const Cha
         ph.K = s.K;
         ph.nk = s.K / 64;
         ph.tiles = s.Nw / 256;
-        ph.blocks = ph.tiles * ph.nk;
-        ph.g_eff = phase_ctas(ph.blocks, ph.nk, grid);
-        ph.base = base;
-        base = (base + ph.g_eff) % grid;
         ph.ncols = pl[i].ncols;
+        ph.base = base;
+        base = (base + (ph.tiles < nc ? ph.tiles : 0)) % nc;   // a phase that fills the grid keeps the rotation
         ph.norm = s.ep.norm_w != nullptr;
         ph.x_src = pl[i].x_src;
         ph.r_src = pl[i].r_src;
         ph.std_out = pl[i].std_out;
         ph.ll_out = pl[i].ll_out;
-        ph.part = scr.part + (size_t)i * region;
         if (ph.ll_out) {
             ph.ll = scr.ll + ll_used;
             ll_used += (size_t)Mtok * ph.ncols;
         }
     }
-    if ((size_t)n * region > scr.part_words || ll_used > scr.ll_words)
-        return set_error(ctx, TB_ERR_ARG, "decode chain: scratch too small");
+    if (ll_used > scr.ll_words) return set_error(ctx, TB_ERR_ARG, "decode chain: scratch too small");
     for (int i = 0; i < n; i++) {
         PhaseInfo& ph = prm.ph[i].info;
         if (ph.x_src >= 0) ph.x_ll = prm.ph[ph.x_src].info.ll;
@@ -929,20 +870,31 @@ int launch_chain(tb_ctx* ctx, const ChainStep* steps, int n, int Mtok, const Cha
     }
     prm.nph = n;
     prm.Mtok = Mtok;
+    prm.cs = cs;
     prm.err = ctx->d_err;
     prm.sync = scr.sync;
-    auto kern = decode_chain_kernel<NT, STAGES>;
-    TB_CUDA_TRY(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
-    return launch(ctx, "decode_chain", kern, dim3(grid), dim3(C::THREADS), (size_t)C::SMEM, prm);
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3((unsigned)(nc * cs), 1, 1);
+    lc.blockDim = dim3(C::THREADS, 1, 1);
+    lc.dynamicSmemBytes = C::SMEM;
+    lc.stream = ctx->stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)cs;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    lc.attrs = attr;
+    lc.numAttrs = 1;
+    if (ctx->pdl) {
+        attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[1].val.programmaticStreamSerializationAllowed = 1;
+        lc.numAttrs = 2;
+    }
+    TB_CUDA_TRY(ctx, cudaLaunchKernelEx(&lc, kern, prm));
+    return TB_OK;
 }
-
-int nt_of(int Mtok) { return Mtok <= 16 ? 16 : Mtok <= 32 ? 32 : 64; }
 
 }  // namespace
-
-size_t chain_part_words(int num_sms, int Mtok) {
-    return (size_t)kChainMaxPhases * (num_sms + kChainMaxTiles) * slot_words(nt_of(Mtok));
-}
 
 size_t chain_ll_words(int Mtok, int max_cols) { return (size_t)kChainMaxPhases * Mtok * max_cols; }
 
@@ -955,13 +907,13 @@ bool chain_step_ok(const ChainStep& s, int Mtok) {
 }
 
 int chain_launch(tb_ctx* ctx, const ChainStep* steps, int n, int Mtok, const ChainScratch& scr) {
-    if (n < 1 || n > kChainMaxPhases || !scr.sync || !scr.part || !scr.ll)
+    if (n < 1 || n > kChainMaxPhases || !scr.sync || !scr.ll)
         return set_error(ctx, TB_ERR_ARG, "decode chain: bad phase count or scratch");
     for (int i = 0; i < n; i++)
         if (!chain_step_ok(steps[i], Mtok)) return set_error(ctx, TB_ERR_UNSUPPORTED, "decode chain: step %d shape", i);
-    if (Mtok <= 16) return launch_chain<16, 6>(ctx, steps, n, Mtok, scr);
-    if (Mtok <= 32) return launch_chain<32, 6>(ctx, steps, n, Mtok, scr);
-    return launch_chain<64, 5>(ctx, steps, n, Mtok, scr);
+    if (Mtok <= 16) return launch_chain<16, 5, 2>(ctx, steps, n, Mtok, scr);
+    if (Mtok <= 32) return launch_chain<32, 4, 2>(ctx, steps, n, Mtok, scr);
+    return launch_chain<64, 3, 1>(ctx, steps, n, Mtok, scr);
 }
 
 }  // namespace tb
@@ -1009,8 +961,8 @@ extern "C" int tb_linear_chain_fwd(tb_ctx* ctx, const tb_linear_step* steps, int
         if (ncol > max_cols) max_cols = (int)ncol;
     }
     // scratch: grown (and zeroed) when a call needs more than the last one
-    const size_t pw = chain_part_words(ctx->num_sms, (int)M), lw = chain_ll_words((int)M, max_cols);
-    if (!ctx->chain_sync || pw > ctx->chain_part_words || lw > ctx->chain_ll_words) {
+    const size_t lw = chain_ll_words((int)M, max_cols);
+    if (!ctx->chain_sync || lw > ctx->chain_ll_words) {
         TB_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
         if (!ctx->chain_sync) {
             unsigned* sw = nullptr;
@@ -1022,25 +974,18 @@ extern "C" int tb_linear_chain_fwd(tb_ctx* ctx, const tb_linear_step* steps, int
             }
             ctx->chain_sync = sw;
         }
-        auto grow = [&](uint64_t** p, size_t* have, size_t need) {
-            if (need <= *have) return true;
-            if (*p) cudaFree(*p);
-            *p = nullptr;
-            *have = 0;
-            if (cudaMalloc(p, need * sizeof(uint64_t)) != cudaSuccess || cudaMemset(*p, 0, need * sizeof(uint64_t)) != cudaSuccess) {
-                cudaGetLastError();
-                return false;
-            }
-            *have = need;
-            return true;
-        };
-        if (!grow(&ctx->chain_part, &ctx->chain_part_words, pw) || !grow(&ctx->chain_ll, &ctx->chain_ll_words, lw))
+        if (ctx->chain_ll) cudaFree(ctx->chain_ll);
+        ctx->chain_ll = nullptr;
+        ctx->chain_ll_words = 0;
+        if (cudaMalloc(&ctx->chain_ll, lw * sizeof(uint64_t)) != cudaSuccess ||
+            cudaMemset(ctx->chain_ll, 0, lw * sizeof(uint64_t)) != cudaSuccess) {
+            cudaGetLastError();
             return set_error(ctx, TB_ERR_OOM, "linear chain: scratch allocation failed");
+        }
+        ctx->chain_ll_words = lw;
     }
     ChainScratch scr;
     scr.sync = ctx->chain_sync;
-    scr.part = ctx->chain_part;
-    scr.part_words = ctx->chain_part_words;
     scr.ll = ctx->chain_ll;
     scr.ll_words = ctx->chain_ll_words;
     int rc = chain_launch(ctx, cs, n_steps, (int)M, scr);

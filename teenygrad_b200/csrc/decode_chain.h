@@ -28,15 +28,12 @@ struct ChainStep {
 // use it (launches in stream order).
 struct ChainScratch {
     unsigned* sync = nullptr;   // kChainSyncWords
-    uint64_t* part = nullptr;   // split-K partial slots (flagged words)
-    size_t part_words = 0;
     uint64_t* ll = nullptr;     // outputs read by later phases (flagged words)
     size_t ll_words = 0;
 };
 
-// Words of partial-slot storage for up to Mtok tokens on num_sms SMs, and of
-// flagged outputs for outputs of up to max_cols columns.
-size_t chain_part_words(int num_sms, int Mtok);
+// Words of flagged-output storage for up to Mtok tokens and outputs of up to
+// max_cols columns.
 size_t chain_ll_words(int Mtok, int max_cols);
 
 // Whether the chain runs this step (shape limits), without launching.

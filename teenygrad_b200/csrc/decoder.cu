@@ -757,17 +757,14 @@ int tb_decoder_create(tb_ctx* ctx, const tb_decoder_config* cfg, tb_decoder** ou
         const char* env = getenv("TB_DECODE_CHAIN");
         if (!c.weights_int8 && d->qkv_perm && c.max_batch <= 64 && env && env[0] == '1') {
             const int cols = (int)std::max<int64_t>(std::max<int64_t>(dm, F), d->qkv_n);
-            d->chain.part_words = chain_part_words(ctx->num_sms, c.max_batch);
             d->chain.ll_words = chain_ll_words(c.max_batch, cols);
             A(&d->chain.sync, (size_t)kChainSyncWords);
-            A(&d->chain.part, d->chain.part_words);
             A(&d->chain.ll, d->chain.ll_words);
             if (rc) {
                 tb_decoder_destroy(d);
                 return rc;
             }
             cudaMemset(d->chain.sync, 0, kChainSyncWords * sizeof(unsigned));
-            cudaMemset(d->chain.part, 0, d->chain.part_words * sizeof(uint64_t));
             cudaMemset(d->chain.ll, 0, d->chain.ll_words * sizeof(uint64_t));
             d->use_chain = true;
         }

@@ -20,8 +20,6 @@ struct tb_ctx {
     void* comm = nullptr;           // NCCL communicator state (comm.cu)
     bool pdl = false;               // launch with programmatic stream serialization
     unsigned* chain_sync = nullptr; // tb_linear_chain_fwd scratch (allocated on first use)
-    uint64_t* chain_part = nullptr;
-    size_t chain_part_words = 0;
     uint64_t* chain_ll = nullptr;
     size_t chain_ll_words = 0;
 };
