@@ -679,7 +679,7 @@ def run_c2(args, rank, world, local):
                        "fp32_ms_per_step": round(ms_f32, 3), "fp32_images_per_s": round(B / (ms_f32 / 1e3), 1),
                        "bf16_conv_ms": round(conv_bf16, 4), "fp32_conv_ms": round(conv_f32, 4),
                        "fp32_conv_tflops": round(flops_conv / (conv_f32 / 1e3) / 1e12, 1)},
-            "roofline": {"kernel": "conv_tc_kernel (+ NHWC transpose), one conv", "bound": "tensor", "achieved": round(tf, 1),
+            "roofline": {"kernel": "conv_pm_kernel (+ NHWC transpose), one conv", "bound": "tensor", "achieved": round(tf, 1),
                          "peak": pk["tc"], "unit": "TFLOP/s", "frac": round(tf / pk["tc"], 3), "traffic": None,
                          "peak_source": pk["src"]},
             "clocks": clocks}

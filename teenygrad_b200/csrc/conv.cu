@@ -10,6 +10,8 @@
 //  * CUDA cores: implicit GEMM with exact f32 FMA accumulation, for f32 I/O
 //    (the reference's fp32 kernels, conv2d.rs:44-148 / :643-764, and its 1e-4
 //    tolerance) and for the bf16 shapes the tensor-core path does not take.
+#include <stdlib.h>
+
 #include "common.cuh"
 
 namespace tb {
@@ -422,6 +424,229 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ 
     if (warp == 1) tmem_dealloc(tmem, CONV_TMEM);
 }
 
+// ------------------------------------------- tcgen05 conv, pixels as rows --
+// The same implicit GEMM with output PIXELS as the MMA's M = 128 rows (a tile of
+// 16 output rows x 8 columns) and the 64 output channels of a block as N.
+// Every MMA row is a real output (conv_tc_kernel's 64-channel M leaves half of
+// each instruction's rows unused), and the accumulator spans all four TMEM
+// lane quarters, so the epilogue runs on all four SM sub-partitions.
+//   A = the haloed NHWC patch read in place per tap (8-pixel groups one patch
+//       row apart, as conv_tc_kernel's B operand);  B = the tap's resident
+//       weights [64 couts][64 channels].
+// One thread issues a tcgen05.mma about every 87 ns whatever its N, and an
+// N = 64 instruction needs ~26 ns of the tensor pipe, so four warps (1, 2, 3,
+// 12) issue the tiles tl = i, i + 4, ... of this CTA, each into its own two of
+// eight 64-column TMEM accumulators.  Two epilogue groups (warps 4-7 and 8-11,
+// one warp per lane quarter) take alternate tiles: thread = pixel, 64 channels
+// each, staged as [channel][row][column] for one TMA store into NCHW.
+constexpr int PM_BH = 16;                          // tile rows (16 x 8 = 128 pixels = M)
+constexpr int PM_THREADS = 416;                    // 13 warps
+constexpr int PM_ACC = 8;                          // TMEM accumulators of 64 columns
+constexpr int PM_ISSUERS = 4;
+constexpr int PM_OUT_BYTES = CONV_BN * PM_BH * CONV_BW * 2;   // [64 couts][16 rows][8 columns] bf16
+
+__host__ __device__ constexpr int pm_smem_bytes(int KH, int KW, int AS, int wslots) {
+    return AS * ((conv_patch_bytes(PM_BH, KH, KW) + 1023) / 1024 * 1024) + wslots * CONV_W_BYTES + 2 * PM_OUT_BYTES +
+           2 * CONV_BN * 4 + 1024 + 512;
+}
+
+__device__ __forceinline__ int pm_issuer(int warp) { return warp >= 1 && warp <= 3 ? warp - 1 : warp == 12 ? 3 : -1; }
+
+__global__ void __launch_bounds__(PM_THREADS, 1)
+conv_pm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
+               const __grid_constant__ CUtensorMap tmY, ConvEpi ep, int B, int OH, int OW, int Cout, int KH, int KW,
+               int Cp, int pad, int AS, int* err) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = smem_align1024(smem_raw);
+    const int PW = conv_pw(KW);
+    const int a_bytes = (conv_patch_bytes(PM_BH, KH, KW) + 1023) / 1024 * 1024;
+    const int nc = (Cp + 63) / 64;            // 64-channel chunks
+    const int taps = KH * KW;
+    const int wslots = taps * nc;             // resident weights of this CTA's output block
+    uint8_t* sP = smem;                                        // [AS] patches
+    uint8_t* sW = sP + AS * a_bytes;                           // weight slices
+    uint8_t* sO = sW + wslots * CONV_W_BYTES;                  // [2 groups] output staging
+    float2* sC = reinterpret_cast<float2*>(sO + 2 * PM_OUT_BYTES);   // [64] (scale, bias * scale + shift)
+    uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(sC) + 2 * CONV_BN * 4);
+    // p_full[8], p_empty[8], w_full, acc_full[8], acc_empty[8]
+    const uint32_t p_full0 = smem_u32(bars), p_empty0 = smem_u32(bars + 8);
+    const uint32_t w_full = smem_u32(bars + 16);
+    const uint32_t acc_full0 = smem_u32(bars + 17), acc_empty0 = smem_u32(bars + 25);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 33);
+
+    pdl_trigger();
+    const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+    const int tiles_w = OW / CONV_BW, tiles_h = (OH + PM_BH - 1) / PM_BH;
+    const int nN = (Cout + CONV_BN - 1) / CONV_BN;
+    const int units = tiles_w * tiles_h * B * nN;
+    const int n0c = (blockIdx.x % nN) * CONV_BN;   // grid % nN == 0: this CTA's output block
+    auto tile_of = [&](int t, int& b, int& oh0, int& ow0) {
+        int p = t / nN;
+        ow0 = (p % tiles_w) * CONV_BW;
+        p /= tiles_w;
+        oh0 = (p % tiles_h) * PM_BH;
+        b = p / tiles_h;
+    };
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < 8; s++) {
+            mbar_init(p_full0 + 8 * s, 1);
+            mbar_init(p_empty0 + 8 * s, 1);
+        }
+        mbar_init(w_full, 1);
+        for (int s = 0; s < PM_ACC; s++) {
+            mbar_init(acc_full0 + 8 * s, 1);
+            mbar_init(acc_empty0 + 8 * s, 4);
+        }
+        fence_barrier_init();
+    }
+    if (warp == 1) tmem_alloc(smem_u32(tmem_slot), 512);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    pdl_wait();
+    // per-channel epilogue constants of the block: (c + bias) * scale + shift as one
+    // FMA, c * scale + (bias * scale + shift)
+    if (threadIdx.x < CONV_BN) {
+        const int co = n0c + threadIdx.x;
+        float eb = 0.f, es = 1.f, et = 0.f;
+        if (co < Cout) {
+            if (ep.bias && !ep.shift) eb = ep.bias[co];
+            if (ep.scale) es = ep.scale[co];
+            if (ep.shift) et = ep.shift[co];
+        }
+        sC[threadIdx.x] = make_float2(es, fmaf(eb, es, et));
+    }
+    __syncthreads();
+
+    const int iss = pm_issuer(warp);
+    if (warp == 0) {
+        // ---------------- producer: the block's weights once, then one haloed patch per (tile, chunk)
+        if (lane == 0) {
+            tma_prefetch_desc(&tmX);
+            tma_prefetch_desc(&tmW);
+            int pi = 0;
+            bool ok = true;
+            if (blockIdx.x < units) {
+                mbar_expect_tx(w_full, (uint32_t)(wslots * CONV_W_BYTES));
+                for (int k = 0; k < wslots; k++)
+                    tma_load_2d(smem_u32(sW + k * CONV_W_BYTES), &tmW, w_full, (k % taps) * Cp + (k / taps) * 64, n0c);
+            }
+            for (int t = blockIdx.x; ok && t < units; t += gridDim.x) {
+                int b, oh0, ow0;
+                tile_of(t, b, oh0, ow0);
+                for (int c = 0; ok && c < nc; c++) {
+                    const int sp = pi % AS;
+                    if (pi >= AS && !mbar_wait(p_empty0 + 8 * sp, ((pi / AS) - 1) & 1, err, DEV_ERR_TIMEOUT_EMPTY)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_expect_tx(p_full0 + 8 * sp, (uint32_t)conv_patch_bytes(PM_BH, KH, KW));
+                    tma_load_4d(smem_u32(sP + sp * a_bytes), &tmX, p_full0 + 8 * sp, c * 64, ow0 - pad, oh0 - pad, b);
+                    pi++;
+                }
+            }
+            // every load issued has landed before the CTA can exit
+            for (int k = (pi > AS ? pi - AS : 0); k < pi; k++)
+                mbar_wait(p_full0 + 8 * (k % AS), (k / AS) & 1, err, DEV_ERR_TIMEOUT_FULL);
+            if (blockIdx.x < units) mbar_wait(w_full, 0, err, DEV_ERR_TIMEOUT_FULL);
+        }
+    } else if (iss >= 0) {
+        // ---------------- MMA issuer iss: tiles tl = iss, iss + 4, ... of this CTA into
+        // accumulators tl % 8.  D[pixels][couts] += patch_tap (A) x W_tap (B).
+        if (lane == 0) {
+            const uint32_t idesc = idesc_bf16_f32(128, CONV_BN, false, false);
+            const uint64_t a_desc0 = sdesc_sw128(smem_u32(sP), 16, (uint32_t)PW * 128);
+            const uint64_t b_desc0 = sdesc_sw128(smem_u32(sW), 16, 1024);
+            bool ok = blockIdx.x >= units || mbar_wait(w_full, 0, err, DEV_ERR_TIMEOUT_FULL);
+            for (int t = blockIdx.x + iss * gridDim.x, tl = iss; ok && t < units; t += PM_ISSUERS * gridDim.x, tl += PM_ISSUERS) {
+                const int ab = tl % PM_ACC;
+                if (tl >= PM_ACC && !mbar_wait(acc_empty0 + 8 * ab, ((tl / PM_ACC) - 1) & 1, err, DEV_ERR_TIMEOUT_MISC)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem + ab * CONV_BN;
+                for (int c = 0; ok && c < nc; c++) {
+                    const int pi = tl * nc + c;          // patch sequence number (producer order)
+                    const int sp = pi % AS;
+                    if (!mbar_wait(p_full0 + 8 * sp, (pi / AS) & 1, err, DEV_ERR_TIMEOUT_FULL)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint64_t a_st = a_desc0 + (uint64_t)((sp * a_bytes) >> 4);
+                    for (int tap = 0, kh = 0, kw = 0; tap < taps; tap++) {
+                        const uint64_t a_tap = a_st + (uint64_t)((kh * PW + kw) * 8);   // rows of 128 B
+                        const uint64_t b_tap = b_desc0 + (uint64_t)((c * taps + tap) * (CONV_W_BYTES >> 4));
+#pragma unroll
+                        for (int kk = 0; kk < 4; kk++)
+                            umma_f16_ss(d_tmem, a_tap + 2 * kk, b_tap + 2 * kk, idesc, (c | tap | kk) != 0);
+                        if (++kw == KW) {
+                            kw = 0;
+                            kh++;
+                        }
+                    }
+                    umma_commit(p_empty0 + 8 * sp);
+                }
+                umma_commit(acc_full0 + 8 * ab);
+            }
+        }
+    } else if (warp >= 4 && warp < 12) {
+        // ---------------- epilogue group g (warps 4-7 or 8-11): tiles tl = g, g + 2, ...;
+        // thread <-> pixel m = 32 * (warp % 4) + lane (TMEM lane) = row m / 8, column m % 8
+        const int g = (warp - 4) >> 2, q = warp & 3;
+        const int m = q * 32 + lane, pr = m >> 3, pc = m & 7;
+        uint8_t* so = sO + g * PM_OUT_BYTES;
+        const int bar_id = 2 + g;
+        bool ok = true;
+        for (int t = blockIdx.x + g * gridDim.x, tl = g; t < units; t += 2 * gridDim.x, tl += 2) {
+            int b, oh0, ow0;
+            tile_of(t, b, oh0, ow0);
+            const int ab = tl % PM_ACC;
+            ok = mbar_wait(acc_full0 + 8 * ab, (tl / PM_ACC) & 1, err, DEV_ERR_TIMEOUT_ACC) && ok;
+            tc_fence_after();
+            const uint32_t t_acc = tmem + ((uint32_t)(q * 32) << 16) + ab * CONV_BN;
+            float v[64];
+            tmem_ld32(t_acc, v);
+            tmem_ld32(t_acc + 32, v + 32);
+            // the staging buffer was last read by this group's previous store
+            if (q == 0 && lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+            tmem_wait_ld();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acc_empty0 + 8 * ab);
+            asm volatile("bar.sync %0, 128;" ::"r"(bar_id) : "memory");
+            // channel j of pixel (pr, pc) -> staging [j][pr][pc]: a warp's 32 pixels are 64
+            // contiguous bytes of one channel plane (conflict-free).  The constants of 8
+            // channels are loaded before their 8 stores (the stores could alias them,
+            // so a per-channel load would wait for the previous channel's store).
+            __nv_bfloat16* sob = reinterpret_cast<__nv_bfloat16*>(so) + pr * CONV_BW + pc;
+            const int act = ep.act;
+#pragma unroll
+            for (int j0 = 0; j0 < 64; j0 += 8) {
+                float4 kc[4];
+#pragma unroll
+                for (int i = 0; i < 4; i++) kc[i] = reinterpret_cast<const float4*>(sC + j0)[i];
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    const float es = (i & 1) ? kc[i >> 1].z : kc[i >> 1].x, et = (i & 1) ? kc[i >> 1].w : kc[i >> 1].y;
+                    float o = fmaf(v[j0 + i], es, et);
+                    if (act == TB_ACT_RELU) o = o > 0.f ? o : 0.f;
+                    else if (act == TB_ACT_SILU) o = o / (1.0f + expf(-o));
+                    sob[(j0 + i) * PM_BH * CONV_BW] = __float2bfloat16_rn(o);
+                }
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            asm volatile("bar.sync %0, 128;" ::"r"(bar_id) : "memory");
+            if (q == 0 && lane == 0 && ok) tma_store_4d_async(&tmY, smem_u32(so), ow0, oh0, n0c, b);
+        }
+        if (q == 0 && lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    }
+    __syncwarp();
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
 // ------------------------------------------------------------- f32 conv ---
 // Implicit GEMM on CUDA cores: 64 output pixels x 64 output channels per CTA,
 // K = C * KH * KW in slices of 16, the im2col gather done while loading.
@@ -599,6 +824,47 @@ int tb_conv2d_fwd(tb_ctx* ctx, int dtype, const void* x, const void* w, const fl
                         s.Cp, (const __nv_bfloat16*)w, wr, Cout, KH, KW, rz);
         if (rc) return rc;
     }
+    constexpr int kSmemMax = 227 * 1024;
+    const int nN = (Cout + CONV_BN - 1) / CONV_BN;
+    const int wall = KH * KW * ((s.Cp + 63) / 64);
+    {
+        // pixels-as-rows kernel: resident weights and at least four patch stages
+        // (one per MMA issuer) must fit; TB_CONV_PM=0 keeps conv_tc_kernel
+        static const bool pm_off = getenv("TB_CONV_PM") && getenv("TB_CONV_PM")[0] == '0';
+        int AS = 0;
+        for (int a = 8; a >= 4 && !AS; a--)
+            if (pm_smem_bytes(KH, KW, a, wall) <= kSmemMax) AS = a;
+        if (!pm_off && AS && nN <= ctx->num_sms && PM_BH + KH - 1 <= 256) {
+            CUtensorMap mx, mw, my;
+            uint64_t dims[4] = {(uint64_t)s.Cp, (uint64_t)W, (uint64_t)H, (uint64_t)B};
+            uint64_t strides[3] = {(uint64_t)s.Cp * 2, (uint64_t)W * s.Cp * 2, (uint64_t)H * W * s.Cp * 2};
+            uint32_t box[4] = {64, (uint32_t)conv_pw(KW), (uint32_t)(PM_BH + KH - 1), 1};
+            cuuint32_t es[4] = {1, 1, 1, 1};
+            int rc = make_tmap_strided(ctx, &mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, xn, dims, strides, box, es,
+                                       CU_TENSOR_MAP_SWIZZLE_128B);
+            if (rc) return rc;
+            rc = make_tmap_2d(ctx, &mw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, wr, Cout, (uint64_t)KH * KW * s.Cp,
+                              (uint64_t)KH * KW * s.Cp, 64, CONV_BN);
+            if (rc) return rc;
+            // NCHW output as (w, h, channel, image): the staged tile is [channel][h][w]
+            uint64_t ydims[4] = {(uint64_t)s.OW, (uint64_t)s.OH, (uint64_t)Cout, (uint64_t)B};
+            uint64_t ystr[3] = {(uint64_t)s.OW * 2, (uint64_t)s.OH * s.OW * 2, (uint64_t)Cout * s.OH * s.OW * 2};
+            uint32_t ybox[4] = {CONV_BW, PM_BH, CONV_BN, 1};
+            rc = make_tmap(ctx, &my, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, y, ydims, ystr, ybox, CU_TENSOR_MAP_SWIZZLE_NONE);
+            if (rc) return rc;
+            const int smem = pm_smem_bytes(KH, KW, AS, wall);
+            TB_CUDA_TRY(ctx, cudaFuncSetAttribute(conv_pm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+            const int64_t units = (int64_t)(s.OW / CONV_BW) * ((s.OH + PM_BH - 1) / PM_BH) * B * nN;
+            int grid = (ctx->num_sms / nN) * nN;   // a multiple of nN: each CTA keeps one output block
+            if (units < grid) grid = (int)units;
+            const bool pdl_saved = ctx->pdl;
+            ctx->pdl = true;
+            rc = launch(ctx, "conv_pm", conv_pm_kernel, dim3(grid), dim3(PM_THREADS), smem, mx, mw, my, ep, B, s.OH, s.OW,
+                        Cout, KH, KW, s.Cp, pad, AS, ctx->d_err);
+            ctx->pdl = pdl_saved;
+            return rc;
+        }
+    }
     const int BH = conv_bh(s.OH);
     CUtensorMap mx, mw, my;
     {
@@ -623,9 +889,6 @@ int tb_conv2d_fwd(tb_ctx* ctx, int dtype, const void* x, const void* w, const fl
     // they fit beside two patch stages; otherwise a 4-slice weight ring.  Then
     // two output staging buffers (a tile's staging overlaps the previous
     // tile's store) with the deepest patch ring that fits beside them.
-    constexpr int kSmemMax = 227 * 1024;
-    const int nN = (Cout + CONV_BN - 1) / CONV_BN;
-    const int wall = KH * KW * ((s.Cp + 63) / 64);
     const int wres = conv_smem_bytes(BH, KH, KW, 2, wall, 1) <= kSmemMax && nN <= ctx->num_sms ? 1 : 0;
     const int wslots = wres ? wall : CONV_WS;
     int AS = 2, OS = 1;
