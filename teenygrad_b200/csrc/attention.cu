@@ -41,8 +41,8 @@ constexpr float kLn2 = 0.6931471805599453f;
 // and K tiles and warp 3 V
 // tiles (TMA, 2-stage rings), warp 1 issues S = Q K^T (M = 128 queries,
 // N = 128 keys) into one of two TMEM buffers and warp 2 issues O += P V
-// (N = D), each on its own issuing thread (one thread issues an MMA per
-// ~80 ns).  Softmax warps 4-11: two per row quarter, one query row and half
+// (N = D), each on its own issuing thread, so S of the next tile never
+// queues behind P V of this one.  Softmax warps 4-11: two per row quarter, one query row and half
 // of each tile's keys per thread (exp2 domain); each half has its own running
 // max, sum and O accumulator, merged at the end.  A
 // row's reference max is raised (and its O row and sum rescaled) only when a

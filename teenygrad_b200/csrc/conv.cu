@@ -285,7 +285,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ 
     } else if (warp == 1 || warp == 2) {
         // ---------------- MMA issuers: D^T[couts][pixels] += W_tap (A) x patch_tap (B).
         // Warp 1 issues the CTA's even tiles (accumulator 0), warp 2 the odd ones
-        // (accumulator 1): one thread issues an MMA per ~80 ns, two keep the pipe busier.
+        // (accumulator 1), so one tile's MMAs do not wait on the other's patch.
         if (lane == 0) {
             const uint32_t idesc = idesc_bf16_f32(128, NPIX, false, false);
             // descriptors built once; an operand at byte offset o adds o >> 4 (start-address field)
@@ -433,10 +433,10 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ 
 //   A = the haloed NHWC patch read in place per tap (8-pixel groups one patch
 //       row apart, as conv_tc_kernel's B operand);  B = the tap's resident
 //       weights [64 couts][64 channels].
-// One thread issues a tcgen05.mma about every 87 ns whatever its N, and an
-// N = 64 instruction needs ~26 ns of the tensor pipe, so four warps (1, 2, 3,
-// 12) issue the tiles tl = i, i + 4, ... of this CTA, each into its own two of
-// eight 64-column TMEM accumulators.  Two epilogue groups (warps 4-7 and 8-11,
+// An N = 64 tcgen05.mma takes ~26 ns of the tensor pipe (10 TFLOP/s per SM).
+// Four warps (1, 2, 3, 12) issue the tiles tl = i, i + 4, ... of this CTA,
+// each into its own two of eight 64-column TMEM accumulators, so a tile whose
+// patch or accumulator is late does not hold up the others' MMAs.  Two epilogue groups (warps 4-7 and 8-11,
 // one warp per lane quarter) take alternate tiles: thread = pixel, 64 channels
 // each, staged as [channel][row][column] for one TMA store into NCHW.
 constexpr int PM_BH = 16;                          // tile rows (16 x 8 = 128 pixels = M)

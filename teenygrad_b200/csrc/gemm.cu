@@ -69,16 +69,31 @@ constexpr int gemm_smem_bytes() {
 }
 constexpr int GEMM_THREADS = 384;   // warp 0 TMA, warp 1 MMA, warps 4-11 epilogue
 
-// Persistent: one CTA per SM walks the output tiles (t += gridDim.x; m fastest,
-// so concurrently running CTAs share the weight tile).  The f32 accumulator
+// Persistent: one CTA per SM walks the output tiles (t += gridDim.x) in groups
+// of gm 128-row tile rows (gemm_tile): m fastest inside a group, so running
+// CTAs share the weight tile, and the group's activation rows (gm x 128 x K,
+// at most 32 MB as the launcher picks gm) stay in L2 while every weight tile
+// streams past them once per group.  A plain m-fastest walk over all rows
+// re-read the activations from DRAM (601 MB for 128 MB of operands on the
+// 16384 x 16384 x 2048 gate/up GEMM).  The f32 accumulator
 // is double-buffered in TMEM (2 x BN columns): the epilogue of tile i (warps
 // 4-11: TMEM lane quarter warp % 4, column half (warp - 4) / 4) overlaps the
 // MMAs of tile i + 1.
 // B_MN: b operand stored [K, N] (N contiguous), as matmul_forward's B.
+// Output tile t -> (row tile mi, column tile ni): groups of gm row tiles (the
+// last may be shorter), rows fastest inside a group.
+__device__ __forceinline__ void gemm_tile(int t, int mt, int ntl, int gm, int& mi, int& ni) {
+    const int grp = t / (gm * ntl), r = t - grp * gm * ntl;
+    const int g0 = grp * gm;
+    const int rows = min(gm, mt - g0);
+    mi = g0 + r % rows;
+    ni = r / rows;
+}
+
 template <int BN, int STAGES, bool B_MN>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-               Epi ep, int M, int N, int K, int* err) {
+               Epi ep, int M, int N, int K, int gm, int* err) {
     constexpr int A_BYTES = GEMM_BM * 128;
     constexpr int B_BYTES = BN * 128;
     extern __shared__ uint8_t smem_raw[];
@@ -124,7 +139,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             int it = 0;
             bool ok = true;
             for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x) {
-                const int m0 = (t % mt) * GEMM_BM, n0 = (t / mt) * BN;
+                int mi, ni;
+                gemm_tile(t, mt, ntl, gm, mi, ni);
+                const int m0 = mi * GEMM_BM, n0 = ni * BN;
                 for (int kb = 0; kb < nk; kb++, it++) {
                     const int s = it % STAGES;
                     if (it >= STAGES && !mbar_wait(empty0 + 8 * s, ((it / STAGES) - 1) & 1, err, DEV_ERR_TIMEOUT_EMPTY)) {
@@ -185,7 +202,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         bool ok = true;
         int tl = 0;
         for (int t = blockIdx.x; t < tiles; t += gridDim.x, tl++) {
-            const int m0 = (t % mt) * GEMM_BM, n0 = (t / mt) * BN;
+            int mi, ni;
+            gemm_tile(t, mt, ntl, gm, mi, ni);
+            const int m0 = mi * GEMM_BM, n0 = ni * BN;
             const int ab = tl & 1;
             ok = mbar_wait(accf0 + 8 * ab, (tl >> 1) & 1, err, DEV_ERR_TIMEOUT_ACC) && ok;
             tc_fence_after();
@@ -397,8 +416,8 @@ gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
         for (int i = (issued > STAGES ? issued - STAGES : 0); i < issued; i++)
             mbar_wait(full0 + 8 * (i % STAGES), (i / STAGES) & 1, err, DEV_ERR_TIMEOUT_FULL);
     } else if ((warp == 1 || warp == C::MMA_W1) && lane == 0) {
-        // two issuing threads (one MMA per ~80 ns each): warp 1 the weight rows
-        // [0, 128) of the tile, the other the rows [128, 256), into separate accumulators
+        // two issuing threads: warp 1 the weight rows [0, 128) of the tile, the
+        // other the rows [128, 256), into separate accumulators
         constexpr uint32_t idesc = idesc_bf16_f32(128, NT, false, false);
         const int h = warp == 1 ? 0 : 1;
         for (int i = 0; i < nk; i++) {
@@ -952,9 +971,15 @@ static int launch_gemm_tc(tb_ctx* ctx, const void* a, const void* b, const Epi& 
     constexpr int smem = gemm_smem_bytes<BN, STAGES>();
     auto kern = gemm_tc_kernel<BN, STAGES, B_MN>;
     TB_CUDA_TRY(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    const int64_t tiles = (int64_t)((N + BN - 1) / BN) * ((M + GEMM_BM - 1) / GEMM_BM);
+    const int mt = (M + GEMM_BM - 1) / GEMM_BM;
+    const int64_t tiles = (int64_t)((N + BN - 1) / BN) * mt;
     const int grid = (int)(tiles < ctx->num_sms ? tiles : ctx->num_sms);
-    return launch(ctx, "gemm_tc", kern, dim3(grid), dim3(GEMM_THREADS), smem, ta, tbm, ep, M, N, K, ctx->d_err);
+    // row tiles per raster group: the most (a power of two) whose activation
+    // rows fit in 32 MB of L2
+    const int64_t row_bytes = (int64_t)GEMM_BM * K * 2;
+    int gm = 1;
+    while (gm * 2 <= mt && (int64_t)gm * 2 * row_bytes <= (32ll << 20)) gm *= 2;
+    return launch(ctx, "gemm_tc", kern, dim3(grid), dim3(GEMM_THREADS), smem, ta, tbm, ep, M, N, K, gm, ctx->d_err);
 }
 
 // Cluster size (K splits per weight tile): the largest of 8, 4, 2, 1 that
