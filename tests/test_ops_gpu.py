@@ -357,12 +357,35 @@ def test_attention_causal_rows_without_keys(D):
     assert_close(got[~masked], rl[~masked], 1e-3, "LSE")
 
 
-@pytest.mark.parametrize("B,Hq,Hkv,Sk,D", [(4, 32, 8, 1000, 64), (2, 8, 8, 2048, 128), (3, 4, 1, 5, 64)])
+# (16, 32, 8, 1100, 64) is the C4 decode shape: two splits of five 128-key tiles, three
+# tile pairs per split with the last one short.
+@pytest.mark.parametrize("B,Hq,Hkv,Sk,D", [(4, 32, 8, 1000, 64), (2, 8, 8, 2048, 128), (3, 4, 1, 5, 64),
+                                           (16, 32, 8, 1100, 64)])
 def test_attention_decode(B, Hq, Hkv, Sk, D):
     r = rng(Sk + D)
     q = bf16_round(r.standard_normal((B, Hq, 1, D)))
     k = bf16_round(r.standard_normal((B, Hkv, Sk, D)))
     v = bf16_round(r.standard_normal((B, Hkv, Sk, D)))
+    sc = 1.0 / math.sqrt(D)
+    o, lse = ops().attention(*(to_gpu(a, torch.bfloat16) for a in (q, k, v)), scale=sc, causal=True, return_lse=True)
+    ro, rl = oracle.attention(q, k, v, sc, True)
+    assert_close(np_of(o), ro, BF16_TOL, "O")
+    assert_close(np_of(lse), rl, 1e-3, "LSE")
+
+
+@pytest.mark.parametrize("pos", [200, 700, 1050])
+def test_attention_decode_late_max(pos):
+    """A key far more aligned with the queries than the rest, at a late position: the
+    split that holds it raises its reference max (and rescales O and the row sums) on
+    the tile pair of that key, after earlier pairs were accumulated."""
+    B, Hq, Hkv, Sk, D = 4, 32, 8, 1100, 64
+    r = rng(pos)
+    q = bf16_round(r.standard_normal((B, Hq, 1, D)))
+    k = bf16_round(r.standard_normal((B, Hkv, Sk, D)))
+    v = bf16_round(r.standard_normal((B, Hkv, Sk, D)))
+    G = Hq // Hkv
+    for g in range(Hkv):   # key pos of group g points along its first query head
+        k[:, g, pos, :] = bf16_round(q[:, g * G, 0, :] * 1.5)
     sc = 1.0 / math.sqrt(D)
     o, lse = ops().attention(*(to_gpu(a, torch.bfloat16) for a in (q, k, v)), scale=sc, causal=True, return_lse=True)
     ro, rl = oracle.attention(q, k, v, sc, True)
