@@ -644,12 +644,20 @@ def run_c2(args, rank, world, local):
             gam, bet = (torch.rand(C, generator=g) + 0.5).cuda(), (torch.randn(C, generator=g) * 0.1).cuda()
             mu, var = (torch.randn(C, generator=g) * 0.1).cuda(), (torch.rand(C, generator=g) + 0.5).cuda()
             sc, sh = ops.bn_fold(gam, bet, mu, var, 1e-5, bias)
-            layers.append((w, sc, sh))
+            # bf16: weights packed once (as an executor does at load time)
+            layers.append((ops.conv2d_pack_weights(w) if dt == torch.bfloat16 else w, sc, sh))
 
         def stage():
+            # bf16: NCHW in and out, NHWC between the convolutions (no per-conv
+            # transpose launch); f32: the CUDA-core NCHW path
             y = x
-            for w, sc, sh in layers:
-                y = ops.conv2d(y, w, scale=sc, shift=sh, pad=1, act="relu")
+            n = len(layers)
+            for i, (w, sc, sh) in enumerate(layers):
+                if dt == torch.bfloat16:
+                    y = ops.conv2d(y, w, scale=sc, shift=sh, pad=1, act="relu", x_nhwc=i > 0, y_nhwc=i < n - 1,
+                                   w_packed=True)
+                else:
+                    y = ops.conv2d(y, w, scale=sc, shift=sh, pad=1, act="relu")
             return y
 
         clk = Clocks(local) if (rank == 0 and dt == torch.bfloat16) else None
@@ -662,8 +670,14 @@ def run_c2(args, rank, world, local):
         ms = graph_time_flushed(stage, iters)
         if clk:
             res["clocks"] = clk.stop()
-        ms_conv = graph_time_flushed(
-            lambda: ops.conv2d(x, layers[0][0], scale=layers[0][1], shift=layers[0][2], pad=1, act="relu"), 5)
+        if dt == torch.bfloat16:   # one inner convolution: NHWC in and out, packed weights
+            xh = x.permute(0, 2, 3, 1).contiguous()
+            ms_conv = graph_time_flushed(
+                lambda: ops.conv2d(xh, layers[1][0], scale=layers[1][1], shift=layers[1][2], pad=1, act="relu",
+                                   x_nhwc=True, y_nhwc=True, w_packed=True), 5)
+        else:
+            ms_conv = graph_time_flushed(
+                lambda: ops.conv2d(x, layers[0][0], scale=layers[0][1], shift=layers[0][2], pad=1, act="relu"), 5)
         res[str(dt).split(".")[1]] = (ms, ms_conv)
     ms_bf16, conv_bf16 = res["bfloat16"]
     ms_f32, conv_f32 = res["float32"]
@@ -674,12 +688,14 @@ def run_c2(args, rank, world, local):
             "unit": "images/s", "n_gpus": world, "steps": max(args.steps, 3), "warmup": args.warmup, "ms_per_step": round(ms_bf16, 4),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": "C2: 4 x 3x3 conv 64->64 + bias + folded BN + ReLU, B32 56x56 NCHW (images sharded over the GPUs)",
+                       "layout": "bf16: NCHW stage input and output, NHWC between the convolutions, weights packed once "
+                                 "before timing; f32: NCHW throughout",
                        "images_per_gpu": B,
                        "timing": "CUDA graph replays, L2 flushed (256 MB write) before each", "l2": "flushed",
                        "fp32_ms_per_step": round(ms_f32, 3), "fp32_images_per_s": round(B / (ms_f32 / 1e3), 1),
                        "bf16_conv_ms": round(conv_bf16, 4), "fp32_conv_ms": round(conv_f32, 4),
                        "fp32_conv_tflops": round(flops_conv / (conv_f32 / 1e3) / 1e12, 1)},
-            "roofline": {"kernel": "conv_pm_kernel (+ NHWC transpose), one conv", "bound": "tensor", "achieved": round(tf, 1),
+            "roofline": {"kernel": "conv_pm_kernel, one inner conv (NHWC in and out)", "bound": "tensor", "achieved": round(tf, 1),
                          "peak": pk["tc"], "unit": "TFLOP/s", "frac": round(tf / pk["tc"], 3), "traffic": None,
                          "peak_source": pk["src"]},
             "clocks": clocks}
@@ -735,12 +751,15 @@ def ncu_case(which):
         q, k, v = (torch.randn(2, 32, 4096, 128, device="cuda").bfloat16() for _ in range(3))
         for _ in range(2):
             ops.attention(q, k, v, causal=True)
-    elif which == "conv":        # one C2 conv: B32 64->64 56x56 3x3 + BN + ReLU
+    elif which == "conv":        # C2 convs: B32 64->64 56x56 3x3 + BN + ReLU; NCHW, then NHWC in and out
         x = torch.randn(32, 64, 56, 56, device="cuda").bfloat16()
         w = (torch.randn(64, 64, 3, 3, device="cuda") * 0.05).bfloat16()
         sc, sh = torch.ones(64, device="cuda"), torch.zeros(64, device="cuda")
         for _ in range(2):
             ops.conv2d(x, w, scale=sc, shift=sh, pad=1, act="relu")
+        xh, wp = x.permute(0, 2, 3, 1).contiguous(), ops.conv2d_pack_weights(w)
+        for _ in range(2):
+            ops.conv2d(xh, wp, scale=sc, shift=sh, pad=1, act="relu", x_nhwc=True, y_nhwc=True, w_packed=True)
     elif which == "c4":          # C4 decoder: prefill 16 x 1024 + 3 graph-replayed decode steps
         from teenygrad_b200.decoder import Decoder, DecoderConfig
         dec = Decoder(DecoderConfig(max_batch=16, max_seq=1024 + 128, max_prefill_tokens=16 * 1024))

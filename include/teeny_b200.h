@@ -217,6 +217,30 @@ TB_API int tb_conv2d_fwd(tb_ctx* ctx, int dtype, const void* x, const void* w, c
                          const float* bn_scale, const float* bn_shift, void* y, int B, int Cin, int Cout, int H,
                          int W, int KH, int KW, int stride, int pad, int act, void* workspace,
                          size_t workspace_bytes);
+/* Layout options of tb_conv2d_fwd_ex for an executor that chains convolutions
+ * (the reference's NCHW API is flags = 0, i.e. tb_conv2d_fwd).  The NCHW ->
+ * NHWC copy of x and the weight reorder that the tensor-core path otherwise
+ * makes in its workspace, in a launch of their own, are skipped when the
+ * caller already holds those layouts:
+ *   TB_CONV_X_NHWC   x is [B, H, W, Cin]
+ *   TB_CONV_W_PACKED w is [Cout, KH, KW, Cin] (tb_conv2d_pack_weights)
+ *   TB_CONV_Y_NHWC   y is written [B, OH, OW, Cout]
+ * The options need TB_BF16, Cin % 8 == 0 and the tensor-core path (stride 1,
+ * OW % 8 == 0); TB_CONV_Y_NHWC also needs Cout % 8 == 0 and a shape whose block
+ * weights stay resident (3 x 3 and 1 x 1 filters at <= 64 input channels, as the
+ * C2 stage).  Other shapes return TB_ERR_UNSUPPORTED.  The workspace may be NULL
+ * when both TB_CONV_X_NHWC and TB_CONV_W_PACKED are given. */
+#define TB_CONV_X_NHWC 1
+#define TB_CONV_Y_NHWC 2
+#define TB_CONV_W_PACKED 4
+TB_API int tb_conv2d_fwd_ex(tb_ctx* ctx, int dtype, const void* x, const void* w, const float* bias,
+                            const float* bn_scale, const float* bn_shift, void* y, int B, int Cin, int Cout, int H,
+                            int W, int KH, int KW, int stride, int pad, int act, int flags, void* workspace,
+                            size_t workspace_bytes);
+/* w [Cout, Cin, KH, KW] -> w_packed [Cout, KH, KW, Cin] (bf16, Cin % 8 == 0), the
+ * weight layout TB_CONV_W_PACKED takes; done once per weight tensor. */
+TB_API int tb_conv2d_pack_weights(tb_ctx* ctx, int dtype, const void* w, void* w_packed, int Cout, int Cin, int KH,
+                                  int KW);
 /* BN folding (nn/fused/conv2d_bn_silu.rs:33-35): scale = gamma / sqrt(var + eps),
  * shift = beta - scale * mean (+ scale * bias when bias is given).  f32 [C]. */
 TB_API int tb_bn_fold(tb_ctx* ctx, const float* gamma, const float* beta, const float* mean, const float* var,

@@ -455,7 +455,7 @@ __device__ __forceinline__ int pm_issuer(int warp) { return warp >= 1 && warp <=
 __global__ void __launch_bounds__(PM_THREADS, 1)
 conv_pm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
                const __grid_constant__ CUtensorMap tmY, ConvEpi ep, int B, int OH, int OW, int Cout, int KH, int KW,
-               int Cp, int pad, int AS, int* err) {
+               int Cp, int pad, int AS, int y_nhwc, int* err) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_align1024(smem_raw);
     const int PW = conv_pw(KW);
@@ -615,10 +615,12 @@ conv_pm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ 
             __syncwarp();
             if (lane == 0) mbar_arrive(acc_empty0 + 8 * ab);
             asm volatile("bar.sync %0, 128;" ::"r"(bar_id) : "memory");
-            // channel j of pixel (pr, pc) -> staging [j][pr][pc]: a warp's 32 pixels are 64
-            // contiguous bytes of one channel plane (conflict-free).  The constants of 8
-            // channels are loaded before their 8 stores (the stores could alias them,
-            // so a per-channel load would wait for the previous channel's store).
+            // NCHW: channel j of pixel (pr, pc) -> staging [j][pr][pc]: a warp's 32 pixels
+            // are 64 contiguous bytes of one channel plane (conflict-free).  NHWC: the
+            // pixel's 64 channels -> staging row m of 128 B, 16-byte chunk k at k ^ (m % 8)
+            // (the tensor map's 128-B swizzle; 8 consecutive pixels cover all banks).
+            // The constants of 8 channels are loaded before their stores (the stores
+            // could alias them, so a per-channel load would wait for the previous store).
             __nv_bfloat16* sob = reinterpret_cast<__nv_bfloat16*>(so) + pr * CONV_BW + pc;
             const int act = ep.act;
 #pragma unroll
@@ -626,18 +628,30 @@ conv_pm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ 
                 float4 kc[4];
 #pragma unroll
                 for (int i = 0; i < 4; i++) kc[i] = reinterpret_cast<const float4*>(sC + j0)[i];
+                float o8[8];
 #pragma unroll
                 for (int i = 0; i < 8; i++) {
                     const float es = (i & 1) ? kc[i >> 1].z : kc[i >> 1].x, et = (i & 1) ? kc[i >> 1].w : kc[i >> 1].y;
                     float o = fmaf(v[j0 + i], es, et);
                     if (act == TB_ACT_RELU) o = o > 0.f ? o : 0.f;
                     else if (act == TB_ACT_SILU) o = o / (1.0f + expf(-o));
-                    sob[(j0 + i) * PM_BH * CONV_BW] = __float2bfloat16_rn(o);
+                    o8[i] = o;
+                }
+                if (y_nhwc) {
+                    *reinterpret_cast<uint4*>(so + m * 128 + ((((j0 >> 3) ^ m) & 7) << 4)) =
+                        make_uint4(pack_bf16x2(o8[0], o8[1]), pack_bf16x2(o8[2], o8[3]), pack_bf16x2(o8[4], o8[5]),
+                                   pack_bf16x2(o8[6], o8[7]));
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 8; i++) sob[(j0 + i) * PM_BH * CONV_BW] = __float2bfloat16_rn(o8[i]);
                 }
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             asm volatile("bar.sync %0, 128;" ::"r"(bar_id) : "memory");
-            if (q == 0 && lane == 0 && ok) tma_store_4d_async(&tmY, smem_u32(so), ow0, oh0, n0c, b);
+            if (q == 0 && lane == 0 && ok) {
+                if (y_nhwc) tma_store_4d_async(&tmY, smem_u32(so), n0c, ow0, oh0, b);
+                else tma_store_4d_async(&tmY, smem_u32(so), ow0, oh0, n0c, b);
+            }
         }
         if (q == 0 && lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
     }
@@ -790,10 +804,41 @@ int tb_conv2d_workspace_size(int dtype, int B, int Cin, int Cout, int H, int W, 
 int tb_conv2d_fwd(tb_ctx* ctx, int dtype, const void* x, const void* w, const float* bias, const float* bn_scale,
                   const float* bn_shift, void* y, int B, int Cin, int Cout, int H, int W, int KH, int KW, int stride,
                   int pad, int act, void* workspace, size_t workspace_bytes) {
+    return tb_conv2d_fwd_ex(ctx, dtype, x, w, bias, bn_scale, bn_shift, y, B, Cin, Cout, H, W, KH, KW, stride, pad, act,
+                            0, workspace, workspace_bytes);
+}
+
+int tb_conv2d_pack_weights(tb_ctx* ctx, int dtype, const void* w, void* w_packed, int Cout, int Cin, int KH, int KW) {
+    if (!ctx || !w || !w_packed) return TB_ERR_ARG;
+    TB_REQUIRE(ctx, dtype == TB_BF16, TB_ERR_UNSUPPORTED, "conv2d_pack_weights: bf16 only");
+    TB_REQUIRE(ctx, Cout > 0 && Cin > 0 && Cin % 8 == 0 && KH > 0 && KW > 0, TB_ERR_SHAPE,
+               "conv2d_pack_weights: Cout, KH, KW > 0 and Cin a positive multiple of 8");
+    const int64_t tot = (int64_t)Cout * KH * KW * Cin;
+    const int rz = (int)std::min<int64_t>((tot + 255) / 256, 64);
+    return launch(ctx, "conv_pack_weights", conv_prep_kernel, dim3(1, 1, rz), dim3(256), 0,
+                  (const __nv_bfloat16*)nullptr, (__nv_bfloat16*)nullptr, 0, Cin, 1, 1, Cin,
+                  (const __nv_bfloat16*)w, (__nv_bfloat16*)w_packed, Cout, KH, KW, rz);
+}
+
+int tb_conv2d_fwd_ex(tb_ctx* ctx, int dtype, const void* x, const void* w, const float* bias, const float* bn_scale,
+                     const float* bn_shift, void* y, int B, int Cin, int Cout, int H, int W, int KH, int KW, int stride,
+                     int pad, int act, int flags, void* workspace, size_t workspace_bytes) {
     if (!ctx || !x || !w || !y) return TB_ERR_ARG;
     ConvShape s;
     TB_REQUIRE(ctx, conv_shape(B, Cin, Cout, H, W, KH, KW, stride, pad, &s), TB_ERR_SHAPE, "conv2d: bad shape");
     TB_REQUIRE(ctx, act == TB_ACT_NONE || act == TB_ACT_RELU || act == TB_ACT_SILU, TB_ERR_ARG, "conv2d: act %d", act);
+    TB_REQUIRE(ctx, (flags & ~(TB_CONV_X_NHWC | TB_CONV_Y_NHWC | TB_CONV_W_PACKED)) == 0, TB_ERR_ARG,
+               "conv2d: unknown flags %#x", flags);
+    const bool x_nhwc = flags & TB_CONV_X_NHWC, y_nhwc = flags & TB_CONV_Y_NHWC, w_packed = flags & TB_CONV_W_PACKED;
+    if (flags) {
+        TB_REQUIRE(ctx, dtype == TB_BF16 && conv_tc_ok(s, stride, KH, KW), TB_ERR_UNSUPPORTED,
+                   "conv2d: layout flags need bf16 and the tensor-core path (stride 1, OW %% 8 == 0)");
+        TB_REQUIRE(ctx, !((x_nhwc || w_packed) && Cin % 8), TB_ERR_UNSUPPORTED,
+                   "conv2d: NHWC x / packed w need Cin %% 8 == 0");
+        TB_REQUIRE(ctx, !(y_nhwc && Cout % 8), TB_ERR_UNSUPPORTED, "conv2d: NHWC y needs Cout %% 8 == 0");
+        TB_REQUIRE(ctx, !x_nhwc || aligned16(x), TB_ERR_ALIGN, "conv2d: NHWC x must be 16-byte aligned");
+        TB_REQUIRE(ctx, !w_packed || aligned16(w), TB_ERR_ALIGN, "conv2d: packed w must be 16-byte aligned");
+    }
     ConvEpi ep{bias, bn_scale, bn_shift, act};
     const int64_t P = (int64_t)B * s.OH * s.OW;
     const dim3 sgrid((unsigned)((P + 63) / 64), (unsigned)((Cout + 63) / 64));
@@ -806,20 +851,23 @@ int tb_conv2d_fwd(tb_ctx* ctx, int dtype, const void* x, const void* w, const fl
                       (const __nv_bfloat16*)x, (const __nv_bfloat16*)w, ep, (__nv_bfloat16*)y, B, Cin, Cout, H, W, KH,
                       KW, stride, pad, s.OH, s.OW);
     TB_REQUIRE(ctx, aligned16(y), TB_ERR_ALIGN, "conv2d bf16: y must be 16-byte aligned");
-    const size_t need = conv_ws_bytes(s);
-    TB_REQUIRE(ctx, workspace && workspace_bytes >= need && aligned16(workspace), TB_ERR_ARG,
+    // workspace: the NHWC copy of x, then the reordered weights (each only when the
+    // caller does not already hold that layout)
+    const size_t xn_bytes = x_nhwc ? 0 : (((size_t)B * H * W * s.Cp * 2 + 255) / 256) * 256;
+    const size_t need = xn_bytes + (w_packed ? 0 : (((size_t)Cout * KH * KW * s.Cp * 2 + 255) / 256) * 256);
+    TB_REQUIRE(ctx, need == 0 || (workspace && workspace_bytes >= need && aligned16(workspace)), TB_ERR_ARG,
                "conv2d bf16: workspace of %zu bytes required (tb_conv2d_workspace_size)", need);
-    __nv_bfloat16* xn = reinterpret_cast<__nv_bfloat16*>(workspace);
-    __nv_bfloat16* wr = reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<uint8_t*>(workspace) +
-                                                         (((size_t)B * H * W * s.Cp * 2 + 255) / 256) * 256);
-    {
+    __nv_bfloat16* xn = x_nhwc ? (__nv_bfloat16*)x : reinterpret_cast<__nv_bfloat16*>(workspace);
+    __nv_bfloat16* wr = w_packed ? (__nv_bfloat16*)w
+                                 : reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<uint8_t*>(workspace) + xn_bytes);
+    if (!x_nhwc || !w_packed) {
         // CTAs for the weight reorder (one element per thread, at most 64 z-slices), then
         // transpose CTAs for every (image row, 64 columns, 64 channels)
-        const int64_t tot = (int64_t)Cout * KH * KW * s.Cp;
+        const int64_t tot = w_packed ? 0 : (int64_t)Cout * KH * KW * s.Cp;
         const int gx = (W + 63) / 64, gy = (s.Cp + 63) / 64;
         const int64_t per_z = (int64_t)gx * gy * 256;
         const int rz = (int)std::min<int64_t>((tot + per_z - 1) / per_z, 64);
-        dim3 grid(gx, gy, rz + B * H);
+        dim3 grid(gx, gy, rz + (x_nhwc ? 0 : B * H));
         int rc = launch(ctx, "conv_prep", conv_prep_kernel, grid, dim3(256), 0, (const __nv_bfloat16*)x, xn, B, Cin, H, W,
                         s.Cp, (const __nv_bfloat16*)w, wr, Cout, KH, KW, rz);
         if (rc) return rc;
@@ -846,11 +894,22 @@ int tb_conv2d_fwd(tb_ctx* ctx, int dtype, const void* x, const void* w, const fl
             rc = make_tmap_2d(ctx, &mw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, wr, Cout, (uint64_t)KH * KW * s.Cp,
                               (uint64_t)KH * KW * s.Cp, 64, CONV_BN);
             if (rc) return rc;
-            // NCHW output as (w, h, channel, image): the staged tile is [channel][h][w]
-            uint64_t ydims[4] = {(uint64_t)s.OW, (uint64_t)s.OH, (uint64_t)Cout, (uint64_t)B};
-            uint64_t ystr[3] = {(uint64_t)s.OW * 2, (uint64_t)s.OH * s.OW * 2, (uint64_t)Cout * s.OH * s.OW * 2};
-            uint32_t ybox[4] = {CONV_BW, PM_BH, CONV_BN, 1};
-            rc = make_tmap(ctx, &my, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, y, ydims, ystr, ybox, CU_TENSOR_MAP_SWIZZLE_NONE);
+            if (y_nhwc) {
+                // NHWC output as (channel, w, h, image): the staged tile is [h][w][64 channels],
+                // 128-B swizzled
+                uint64_t ydims[4] = {(uint64_t)Cout, (uint64_t)s.OW, (uint64_t)s.OH, (uint64_t)B};
+                uint64_t ystr[3] = {(uint64_t)Cout * 2, (uint64_t)s.OW * Cout * 2, (uint64_t)s.OH * s.OW * Cout * 2};
+                uint32_t ybox[4] = {CONV_BN, CONV_BW, PM_BH, 1};
+                rc = make_tmap(ctx, &my, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, y, ydims, ystr, ybox,
+                               CU_TENSOR_MAP_SWIZZLE_128B);
+            } else {
+                // NCHW output as (w, h, channel, image): the staged tile is [channel][h][w]
+                uint64_t ydims[4] = {(uint64_t)s.OW, (uint64_t)s.OH, (uint64_t)Cout, (uint64_t)B};
+                uint64_t ystr[3] = {(uint64_t)s.OW * 2, (uint64_t)s.OH * s.OW * 2, (uint64_t)Cout * s.OH * s.OW * 2};
+                uint32_t ybox[4] = {CONV_BW, PM_BH, CONV_BN, 1};
+                rc = make_tmap(ctx, &my, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, y, ydims, ystr, ybox,
+                               CU_TENSOR_MAP_SWIZZLE_NONE);
+            }
             if (rc) return rc;
             const int smem = pm_smem_bytes(KH, KW, AS, wall);
             TB_CUDA_TRY(ctx, cudaFuncSetAttribute(conv_pm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
@@ -860,11 +919,13 @@ int tb_conv2d_fwd(tb_ctx* ctx, int dtype, const void* x, const void* w, const fl
             const bool pdl_saved = ctx->pdl;
             ctx->pdl = true;
             rc = launch(ctx, "conv_pm", conv_pm_kernel, dim3(grid), dim3(PM_THREADS), smem, mx, mw, my, ep, B, s.OH, s.OW,
-                        Cout, KH, KW, s.Cp, pad, AS, ctx->d_err);
+                        Cout, KH, KW, s.Cp, pad, AS, y_nhwc ? 1 : 0, ctx->d_err);
             ctx->pdl = pdl_saved;
             return rc;
         }
     }
+    TB_REQUIRE(ctx, !y_nhwc, TB_ERR_UNSUPPORTED,
+               "conv2d: NHWC y needs resident block weights (conv_pm_kernel); this shape takes conv_tc_kernel");
     const int BH = conv_bh(s.OH);
     CUtensorMap mx, mw, my;
     {

@@ -396,26 +396,53 @@ def batch_norm_inference(x, gamma, beta, mean, var, eps=1e-5):
 _CONV_ACT = {None: -1, "relu": 2, "silu": 0}
 
 
-def conv2d(x, w, bias=None, scale=None, shift=None, stride=1, pad=0, act=None):
+def conv2d(x, w, bias=None, scale=None, shift=None, stride=1, pad=0, act=None, x_nhwc=False, y_nhwc=False,
+           w_packed=False):
     """conv2d_bias_forward (nn/conv/conv2d.rs:643-764) + folded-BN epilogue
-    (nn/fused/conv2d_bn_silu.rs:141-170); NCHW, groups = 1."""
+    (nn/fused/conv2d_bn_silu.rs:141-170); NCHW, groups = 1.
+
+    Layout options for chained convolutions (tb_conv2d_fwd_ex, bf16 tensor-core
+    shapes): x_nhwc takes x as [B, H, W, C], y_nhwc returns y as [B, OH, OW, Co],
+    w_packed takes w as [Co, KH, KW, C] (conv2d_pack_weights)."""
     _cuda(x, w, bias, scale, shift)
-    B, C, H, W = x.shape
-    Co, _, KH, KW = w.shape
+    if x_nhwc:
+        B, H, W, C = x.shape
+    else:
+        B, C, H, W = x.shape
+    if w_packed:
+        Co, KH, KW, _ = w.shape
+    else:
+        Co, _, KH, KW = w.shape
     OH = (H + 2 * pad - KH) // stride + 1
     OW = (W + 2 * pad - KW) // stride + 1
-    y = torch.empty(B, Co, OH, OW, device=x.device, dtype=x.dtype)
+    shape = (B, OH, OW, Co) if y_nhwc else (B, Co, OH, OW)
+    y = torch.empty(*shape, device=x.device, dtype=x.dtype)
+    flags = (1 if x_nhwc else 0) | (2 if y_nhwc else 0) | (4 if w_packed else 0)
     nbytes = ctypes.c_size_t(0)
-    st = lib().tb_conv2d_workspace_size(ctypes.c_int(_dt(x)), *(ctypes.c_int(v) for v in (B, C, Co, H, W, KH, KW, stride, pad)),
-                                        ctypes.byref(nbytes))
-    check(None, st)
+    if not (x_nhwc and w_packed):
+        st = lib().tb_conv2d_workspace_size(ctypes.c_int(_dt(x)),
+                                            *(ctypes.c_int(v) for v in (B, C, Co, H, W, KH, KW, stride, pad)),
+                                            ctypes.byref(nbytes))
+        check(None, st)
     ws = torch.empty(max(1, nbytes.value), device=x.device, dtype=torch.uint8) if nbytes.value else None
     ctx = context()
     f = [t if t is None or t.dtype == torch.float32 else t.float().contiguous() for t in (bias, scale, shift)]
-    check(ctx, lib().tb_conv2d_fwd(ctx, ctypes.c_int(_dt(x)), _p(x), _p(w), _p(f[0]), _p(f[1]), _p(f[2]), _p(y),
-                                   *(ctypes.c_int(v) for v in (B, C, Co, H, W, KH, KW, stride, pad, _CONV_ACT[act])),
-                                   _p(ws), ctypes.c_size_t(nbytes.value)))
+    check(ctx, lib().tb_conv2d_fwd_ex(ctx, ctypes.c_int(_dt(x)), _p(x), _p(w), _p(f[0]), _p(f[1]), _p(f[2]), _p(y),
+                                      *(ctypes.c_int(v) for v in (B, C, Co, H, W, KH, KW, stride, pad, _CONV_ACT[act],
+                                                                   flags)),
+                                      _p(ws), ctypes.c_size_t(nbytes.value)))
     return y
+
+
+def conv2d_pack_weights(w):
+    """w [Co, C, KH, KW] bf16 -> [Co, KH, KW, C], the layout conv2d(w_packed=True) takes."""
+    _cuda(w)
+    Co, C, KH, KW = w.shape
+    out = torch.empty(Co, KH, KW, C, device=w.device, dtype=w.dtype)
+    ctx = context()
+    check(ctx, lib().tb_conv2d_pack_weights(ctx, ctypes.c_int(_dt(w)), _p(w), _p(out),
+                                            *(ctypes.c_int(v) for v in (Co, C, KH, KW))))
+    return out
 
 
 class Conv2dBiasForward(_Op):

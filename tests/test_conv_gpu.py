@@ -73,6 +73,67 @@ def test_conv2d_bf16_tensor_cores(B, C, Co, H, W, k, p, act):
     assert_close(got, ref, BF16_TOL)
 
 
+def test_conv2d_pack_weights_exact():
+    r = rng(11)
+    w = bf16_round(r.standard_normal((72, 24, 3, 5)))
+    got = np_of(ops().conv2d_pack_weights(to_gpu(w, torch.bfloat16)))
+    np.testing.assert_array_equal(got, w.transpose(0, 2, 3, 1))
+
+
+@pytest.mark.parametrize("B,C,H,W,layers,act", [(32, 64, 56, 56, 4, "relu"), (3, 64, 20, 24, 3, "silu"),
+                                                 (2, 32, 17, 16, 2, None)])
+def test_conv2d_nhwc_chain(B, C, H, W, layers, act):
+    """The C2 stage as an executor runs it: NCHW in, NHWC between the convolutions,
+    NCHW out, weights packed once; against the oracle's NCHW chain (each layer's
+    input rounded to bf16, as the device stores it), and the NHWC intermediate
+    against the oracle's first layer."""
+    r = rng(B + C + layers)
+    x = bf16_round(r.standard_normal((B, C, H, W)))
+    params = []
+    for _ in range(layers):
+        w = bf16_round(r.standard_normal((C, C, 3, 3)) * np.sqrt(2.0 / (C * 9)))
+        bias = r.normal(0, 0.1, C).astype(np.float32)
+        sc, sh = oracle.bn_fold(r.uniform(0.5, 1.5, C), r.normal(0, .1, C), r.normal(0, .1, C),
+                                r.uniform(0.5, 1.5, C), 1e-5, bias)
+        params.append((w, sc, sh))
+    ref, refs = x, []
+    for w, sc, sh in params:
+        ref = bf16_round(oracle.conv2d(ref, w, scale=sc, shift=sh, pad=1, act=act))
+        refs.append(ref)
+    y = to_gpu(x, torch.bfloat16)
+    outs = []
+    for i, (w, sc, sh) in enumerate(params):
+        wp = ops().conv2d_pack_weights(to_gpu(w, torch.bfloat16))
+        y = ops().conv2d(y, wp, scale=to_gpu(sc), shift=to_gpu(sh), pad=1, act=act, x_nhwc=i > 0,
+                         y_nhwc=i < layers - 1, w_packed=True)
+        outs.append(y)
+    assert tuple(outs[0].shape) == (B, H, W, C)
+    assert_close(np_of(outs[0]).transpose(0, 3, 1, 2), refs[0], BF16_TOL, "NHWC intermediate")
+    assert tuple(y.shape) == (B, C, H, W)
+    assert_close(np_of(y), refs[-1], BF16_TOL, "stage output")
+
+
+def test_conv2d_layout_flags_rejected():
+    from teenygrad_b200._lib import TB_ERR_UNSUPPORTED, TeenyError
+    r = rng(3)
+    x = to_gpu(bf16_round(r.standard_normal((1, 12, 16, 16))), torch.bfloat16)     # Cin % 8 != 0
+    w = to_gpu(bf16_round(r.standard_normal((16, 12, 3, 3))), torch.bfloat16)
+    with pytest.raises(TeenyError) as e:
+        ops().conv2d(x.permute(0, 2, 3, 1).contiguous(), w, pad=1, x_nhwc=True)
+    assert e.value.status == TB_ERR_UNSUPPORTED
+    xf = to_gpu(r.standard_normal((1, 16, 16, 16)).astype(np.float32))           # f32: CUDA-core path only
+    wf = to_gpu(r.standard_normal((16, 16, 3, 3)).astype(np.float32))
+    with pytest.raises(TeenyError) as e:
+        ops().conv2d(xf, wf, pad=1, y_nhwc=True)
+    assert e.value.status == TB_ERR_UNSUPPORTED
+    x7 = to_gpu(bf16_round(r.standard_normal((1, 16, 20, 24))), torch.bfloat16)   # 7 x 7: conv_tc_kernel
+    w7 = to_gpu(bf16_round(r.standard_normal((64, 16, 7, 7))), torch.bfloat16)
+    with pytest.raises(TeenyError) as e:
+        ops().conv2d(x7, w7, pad=3, y_nhwc=True)
+    assert e.value.status == TB_ERR_UNSUPPORTED
+    no_device_error()
+
+
 def test_conv2d_bf16_cuda_core_shapes():
     got, ref = _conv_case(2, 16, 24, 17, 19, 3, 2, 1, "relu", torch.bfloat16, seed=5)   # stride 2, OW % 8 != 0
     assert_close(got, ref, BF16_TOL)
