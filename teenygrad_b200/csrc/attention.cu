@@ -1,8 +1,8 @@
 // Attention forward on B200.
 //
 //  * attn_tc_kernel<D>: flash-style forward for bf16 Q/K/V, D in {64, 128}.
-//    Each CTA takes two 128-query tiles of one (head, batch) in turn (a heavy
-//    and a light one when causal).  Warps 0 and 3 stream K and V tiles of 128
+//    Persistent, one CTA per SM; each item is two 128-query tiles of one
+//    (head, batch) taken in turn (a heavy and a light one when causal).  Warps 0 and 3 stream K and V tiles of 128
 //    keys with TMA (two-stage rings; warp 0 also loads Q), warp 1 issues
 //    S = Q K^T into one of two TMEM score buffers, warp 2 issues O += P V, so
 //    neither MMA stream queues behind the other.  Eight softmax warps, two
@@ -34,10 +34,11 @@ __device__ __forceinline__ float ex2(float x) {
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 
-// Per (head, image) and pair of 128-query tiles, one CTA that takes the two
-// tiles in turn (a heavy and a light one when causal, so CTAs carry equal
-// work); its rings and barrier phases run on across them, so the second tile's
-// loads and first MMAs overlap the first tile's epilogue.  Warp 0 streams Q
+// One CTA per SM walks items, an item being a pair of 128-query tiles of one
+// (head, image) taken in turn (a heavy and a light one when causal, so items
+// carry equal work); its rings and barrier phases run on across tiles and
+// items, so each tile's loads and first MMAs overlap the previous tile's
+// epilogue, and launch, TMEM allocation and pipeline fill are paid once per SM.  Warp 0 streams Q
 // and K tiles and warp 3 V
 // tiles (TMA, 2-stage rings), warp 1 issues S = Q K^T (M = 128 queries,
 // N = 128 keys) into one of two TMEM buffers and warp 2 issues O += P V
@@ -64,7 +65,7 @@ constexpr int ATTN_THREADS = 384;   // warps 0/3 TMA, 1 S MMA, 2 P.V MMA, 4-11 s
 template <int D>
 __global__ void __launch_bounds__(ATTN_THREADS, 1)
 attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-               const __grid_constant__ CUtensorMap tmV, AttnOut out, int Hq, int Hkv, int Sq, int Sk,
+               const __grid_constant__ CUtensorMap tmV, AttnOut out, int B, int Hq, int Hkv, int Sq, int Sk,
                float scale_log2, int causal, int* err) {
     using C = AttnCfg<D>;
     extern __shared__ uint8_t smem_raw[];
@@ -85,22 +86,36 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
 
     pdl_trigger();
     const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
-    const int h = blockIdx.y, b = blockIdx.z;
-    const int hk = h / (Hq / Hkv);
     const int diag = Sk - Sq;                         // causal: key j visible to query i iff j <= i + diag
-    // Query tiles of this CTA, processed one after the other: causal pairs a heavy
-    // tile with a light one (equal work per CTA), otherwise two neighbours.
+    // Persistent: one CTA per SM takes the items it = blockIdx.x, + gridDim.x, ...
+    // An item is a pair of query tiles of one (head, image), taken one after the
+    // other: causal pairs a heavy tile with a light one (equal work per item),
+    // otherwise two neighbours.  Items run pair-fastest, then head, then image,
+    // so the items in flight together share their K / V tiles in L2.
     const int nq_all = (Sq + C::BM - 1) / C::BM;
-    int qts[2], nqt;
-    if (causal) {
-        qts[0] = nq_all - 1 - (int)blockIdx.x;
-        qts[1] = blockIdx.x;
-        nqt = qts[1] < qts[0] ? 2 : 1;
-    } else {
-        qts[0] = 2 * blockIdx.x;
-        qts[1] = 2 * blockIdx.x + 1;
-        nqt = qts[1] < nq_all ? 2 : 1;
-    }
+    const int n_pairs = (nq_all + 1) / 2;
+    const int n_items = n_pairs * Hq * B;
+    struct Item {
+        int h, b, hk, nqt, qt0, qt1;
+        __device__ int qt(int qi) const { return qi ? qt1 : qt0; }
+    };
+    auto item_of = [&](int it) {
+        Item m;
+        const int x = it % n_pairs;
+        m.h = (it / n_pairs) % Hq;
+        m.b = it / (n_pairs * Hq);
+        m.hk = m.h / (Hq / Hkv);
+        if (causal) {
+            m.qt0 = nq_all - 1 - x;
+            m.qt1 = x;
+            m.nqt = m.qt1 < m.qt0 ? 2 : 1;
+        } else {
+            m.qt0 = 2 * x;
+            m.qt1 = 2 * x + 1;
+            m.nqt = m.qt1 < nq_all ? 2 : 1;
+        }
+        return m;
+    };
     auto tiles_of = [&](int qt) {   // key tiles a query tile needs
         int n = (Sk + C::BN - 1) / C::BN;
         if (causal) {
@@ -134,9 +149,9 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
     const uint32_t tmem = *tmem_slot;
     pdl_wait();
 
-    // Every ring and barrier continues across the query tiles: g counts key tiles over
-    // the whole CTA (stage / buffer g & 1, phase g >> 1), so each barrier's phases are
-    // waited on in order.
+    // Every ring and barrier continues across the query tiles and items: g counts key
+    // tiles over the whole CTA (stage / buffer g & 1, phase g >> 1) and gq query tiles
+    // (Q and O hand-offs, phase gq & 1), so each barrier's phases are waited on in order.
     if (warp == 0 || warp == 3) {
         // ---------------- producers: warp 0 Q and K tiles, warp 3 V tiles
         if (lane == 0) {
@@ -146,30 +161,38 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
             const uint32_t full0 = isK ? k_full0 : v_full0, empty0 = isK ? k_empty0 : v_empty0;
             tma_prefetch_desc(tm);
             if (isK) tma_prefetch_desc(&tmQ);
-            int g = 0;
+            int g = 0, gq = 0;
             bool ok = true;
-            for (int qi = 0; ok && qi < nqt; qi++) {
-                const int nt = tiles_of(qts[qi]);
-                if (isK) {
-                    // Q of the next query tile once the S MMAs have read the previous one
-                    if (qi > 0 && !mbar_wait(q_empty, (qi - 1) & 1, err, DEV_ERR_TIMEOUT_EMPTY)) break;
-                    mbar_expect_tx(q_full, C::TILE);
-                    for (int d = 0; d < DB; d++)
-                        tma_load_4d(smem_u32(sQ + d * 16384), &tmQ, q_full, 64 * d, h, qts[qi] * C::BM, b);
-                }
-                for (int j = 0; j < nt; j++, g++) {
-                    const int st = g & 1;
-                    if (g >= 2 && !mbar_wait(empty0 + 8 * st, ((g >> 1) - 1) & 1, err, DEV_ERR_TIMEOUT_EMPTY)) {
-                        ok = false;
-                        break;
+            for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x) {
+                const Item m = item_of(it);
+                for (int qi = 0; ok && qi < m.nqt; qi++, gq++) {
+                    const int nt = tiles_of(m.qt(qi));
+                    if (isK) {
+                        // Q of the next query tile once the S MMAs have read the previous one
+                        if (gq > 0 && !mbar_wait(q_empty, (gq - 1) & 1, err, DEV_ERR_TIMEOUT_EMPTY)) {
+                            ok = false;
+                            break;
+                        }
+                        mbar_expect_tx(q_full, C::TILE);
+                        for (int d = 0; d < DB; d++)
+                            tma_load_4d(smem_u32(sQ + d * 16384), &tmQ, q_full, 64 * d, m.h, m.qt(qi) * C::BM, m.b);
                     }
-                    mbar_expect_tx(full0 + 8 * st, C::TILE);
-                    for (int d = 0; d < DB; d++)
-                        tma_load_4d(smem_u32(ring + st * C::TILE + d * 16384), tm, full0 + 8 * st, 64 * d, hk, j * C::BN, b);
+                    for (int j = 0; j < nt; j++, g++) {
+                        const int st = g & 1;
+                        if (g >= 2 && !mbar_wait(empty0 + 8 * st, ((g >> 1) - 1) & 1, err, DEV_ERR_TIMEOUT_EMPTY)) {
+                            ok = false;
+                            break;
+                        }
+                        mbar_expect_tx(full0 + 8 * st, C::TILE);
+                        for (int d = 0; d < DB; d++)
+                            tma_load_4d(smem_u32(ring + st * C::TILE + d * 16384), tm, full0 + 8 * st, 64 * d, m.hk,
+                                        j * C::BN, m.b);
+                    }
                 }
             }
-            // every load this CTA issued has landed before it can exit
-            if (isK) mbar_wait(q_full, (nqt - 1) & 1, err, DEV_ERR_TIMEOUT_FULL);
+            // every load this CTA issued has landed before it can exit (a Q load is
+            // counted in gq once issued)
+            if (isK && gq > 0) mbar_wait(q_full, (gq - 1) & 1, err, DEV_ERR_TIMEOUT_FULL);
             for (int j = (g > 2 ? g - 2 : 0); j < g; j++)
                 mbar_wait(full0 + 8 * (j & 1), (j >> 1) & 1, err, DEV_ERR_TIMEOUT_FULL);
         }
@@ -179,11 +202,13 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
             constexpr uint32_t idesc_s = idesc_bf16_f32(128, C::BN, false, false);
             const uint64_t q_desc = sdesc_sw128(smem_u32(sQ), 16, 1024);
             const uint64_t k_desc = sdesc_sw128(smem_u32(sK), 16, 1024);
-            int g = 0;
+            int g = 0, gq = 0;
             bool ok = true;
-            for (int qi = 0; ok && qi < nqt; qi++) {
-                const int nt = tiles_of(qts[qi]);
-                ok = mbar_wait(q_full, qi & 1, err, DEV_ERR_TIMEOUT_FULL);
+            for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x) {
+              const Item m = item_of(it);
+              for (int qi = 0; ok && qi < m.nqt; qi++, gq++) {
+                const int nt = tiles_of(m.qt(qi));
+                ok = mbar_wait(q_full, gq & 1, err, DEV_ERR_TIMEOUT_FULL);
                 for (int j = 0; ok && j < nt; j++, g++) {
                     const int st = g & 1;
                     if (!mbar_wait(k_full0 + 8 * st, (g >> 1) & 1, err, DEV_ERR_TIMEOUT_FULL) ||
@@ -202,6 +227,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
                     umma_commit(s_full0 + 8 * st);
                 }
                 umma_commit(q_empty);   // Q may be replaced once these S MMAs have completed
+              }
             }
         }
     } else if (warp == 2) {
@@ -210,12 +236,14 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
             constexpr uint32_t idesc_o = idesc_bf16_f32(128, D, false, true);
             const uint64_t p_desc = sdesc_sw128(smem_u32(sP), 16, 1024);
             const uint64_t v_desc = sdesc_sw128(smem_u32(sV), 16384, 1024);
-            int g = 0;
+            int g = 0, gq = 0;
             bool ok = true;
-            for (int qi = 0; ok && qi < nqt; qi++) {
-                const int nt = tiles_of(qts[qi]);
+            for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x) {
+              const Item m = item_of(it);
+              for (int qi = 0; ok && qi < m.nqt; qi++, gq++) {
+                const int nt = tiles_of(m.qt(qi));
                 // O of the previous query tile must have been read out before it is overwritten
-                if (qi > 0) ok = mbar_wait(o_free, (qi - 1) & 1, err, DEV_ERR_TIMEOUT_MISC);
+                if (gq > 0) ok = mbar_wait(o_free, (gq - 1) & 1, err, DEV_ERR_TIMEOUT_MISC);
                 for (int j = 0; ok && j < nt; j++, g++) {
                     const int st = g & 1;
                     if (!mbar_wait(p_full0 + 8 * st, (g >> 1) & 1, err, DEV_ERR_TIMEOUT_MISC) ||
@@ -234,6 +262,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
                     umma_commit(v_empty0 + 8 * st);
                     umma_commit(p_free0 + 8 * st);
                 }
+              }
             }
         }
     } else if (warp >= 4) {
@@ -247,9 +276,12 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
         const uint32_t o_col = C::O_COL + hf * D;
         int g = 0;
         bool ok = true;
-        for (int qi = 0; qi < nqt; qi++) {
-            const int q0 = qts[qi] * C::BM;
-            const int n_tiles = tiles_of(qts[qi]);
+        for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
+          const Item m = item_of(it);
+          const int h = m.h, b = m.b;
+          for (int qi = 0; qi < m.nqt; qi++) {
+            const int q0 = m.qt(qi) * C::BM;
+            const int n_tiles = tiles_of(m.qt(qi));
             const int qrow = q0 + r;
             const int lim = causal ? min(Sk - 1, qrow + diag) : Sk - 1;   // last visible key
             float m_ref = -INFINITY, l_run = 0.f;
@@ -402,6 +434,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(o_free);
+          }
         }
     }
     __syncwarp();
@@ -935,18 +968,21 @@ int attn_tc_launch(tb_ctx* ctx, const AttnTensors& t, int B, int Hq, int Hkv, in
     if (!rc) rc = tmap_heads(ctx, &mv, t.v, D, Hkv, t.kv_len_alloc, B, t.kv_sh, t.kv_ss, t.kv_sb);
     if (rc) return rc;
     AttnOut out{t.o, t.o_sh, t.o_ss, t.o_sb, t.lse};
-    // two query tiles per CTA (a heavy and a light one when causal)
-    dim3 grid(((Sq + 127) / 128 + 1) / 2, Hq, B);
+    // persistent: one CTA per SM (512 TMEM columns each) over the items, an item
+    // being two query tiles of one (head, image), a heavy and a light one when causal
+    const int64_t items = (int64_t)(((Sq + 127) / 128 + 1) / 2) * Hq * B;
+    if (items >= (1ll << 31)) return set_error(ctx, TB_ERR_SHAPE, "attention: too many query tiles");
+    dim3 grid((unsigned)std::min<int64_t>(items, ctx->num_sms));
     const float sl2 = scale * kLog2e;
     if (D == 64) {
         // 512 TMEM columns per CTA: keep one CTA per SM (the padding does that).
         constexpr int smem = AttnCfg<64>::SMEM > 120 * 1024 ? AttnCfg<64>::SMEM : 120 * 1024;
         TB_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-        return launch(ctx, "attn_tc", attn_tc_kernel<64>, grid, dim3(ATTN_THREADS), smem, mq, mk, mv, out, Hq, Hkv, Sq, Sk, sl2, causal, ctx->d_err);
+        return launch(ctx, "attn_tc", attn_tc_kernel<64>, grid, dim3(ATTN_THREADS), smem, mq, mk, mv, out, B, Hq, Hkv, Sq, Sk, sl2, causal, ctx->d_err);
     } else {
         constexpr int smem = AttnCfg<128>::SMEM;
         TB_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-        return launch(ctx, "attn_tc", attn_tc_kernel<128>, grid, dim3(ATTN_THREADS), smem, mq, mk, mv, out, Hq, Hkv, Sq, Sk, sl2, causal, ctx->d_err);
+        return launch(ctx, "attn_tc", attn_tc_kernel<128>, grid, dim3(ATTN_THREADS), smem, mq, mk, mv, out, B, Hq, Hkv, Sq, Sk, sl2, causal, ctx->d_err);
     }
     return check_launch(ctx, "attn_tc");
 }
