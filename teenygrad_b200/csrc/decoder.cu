@@ -229,57 +229,69 @@ __device__ __forceinline__ void amax_merge2(float& v, int& i, float v2, int i2) 
     }
 }
 
-// Greedy token per row, lowest index on ties, NaN skipped.  Grid (B, chunks):
-// each CTA reduces its chunk of the row to (value, index), folds it into a
-// per-row 64-bit key with atomicMax (key = order-preserving bits of the value
-// << 32 | ~index, so equal values prefer the lower index), and the last CTA
-// of the row writes cur_ids[b] and out_ids[b * max_gen + state[1]] and resets
-// the key and counter.
-__global__ void argmax_step_kernel(const float* __restrict__ logits, int V, int chunk, int32_t* __restrict__ cur_ids,
-                                   int32_t* __restrict__ out_ids, int max_gen, const int* __restrict__ state,
-                                   unsigned long long* __restrict__ keys, unsigned* __restrict__ cnt) {
+// Greedy token per row, lowest index on ties, NaN skipped: one 1024-thread CTA
+// per row, every thread with all of its 128-bit loads in flight at once (one
+// round for a 32000-entry vocabulary), then a warp and a block reduction, and
+// thread 0 writes cur_ids[b] and out_ids[b * max_gen + state[1]].  (A grid of
+// row chunks merged through atomics and a last-CTA election took ~7 us after
+// the LM head in the decode step, a chain of dependent global round trips; one
+// CTA per row takes ~2.)  The (value, index) selection is order-independent, so
+// -0.0 and +0.0 tie and the lower index wins, as in the oracle.
+constexpr int kArgmaxThreads = 1024, kArgmaxU = 8;
+__global__ void __launch_bounds__(kArgmaxThreads)
+argmax_step_kernel(const float* __restrict__ logits, int V, int32_t* __restrict__ cur_ids,
+                   int32_t* __restrict__ out_ids, int max_gen, const int* __restrict__ state) {
     pdl_trigger();
     pdl_wait();
     const int row = blockIdx.x;
     const float* xr = logits + (int64_t)row * V;
-    const int c0 = blockIdx.y * chunk, c1 = min(V, c0 + chunk);
     float bv = -INFINITY;
     int bi = -1;
-    for (int c = c0 + threadIdx.x; c < c1; c += blockDim.x) {
-        float v = xr[c];
-        if (v != v) continue;
-        amax_merge2(bv, bi, v, c);
+    if ((V & 3) == 0 && (reinterpret_cast<uintptr_t>(xr) & 15) == 0) {
+        const float4* x4 = reinterpret_cast<const float4*>(xr);
+        const int n4 = V >> 2;
+        for (int c0 = threadIdx.x; c0 < n4; c0 += kArgmaxU * kArgmaxThreads) {
+            float4 v[kArgmaxU];
+#pragma unroll
+            for (int u = 0; u < kArgmaxU; u++) {
+                const int i4 = c0 + u * kArgmaxThreads;
+                v[u] = i4 < n4 ? x4[i4] : make_float4(NAN, NAN, NAN, NAN);
+            }
+#pragma unroll
+            for (int u = 0; u < kArgmaxU; u++) {
+                const int c = 4 * (c0 + u * kArgmaxThreads);
+                const float e[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+                for (int j = 0; j < 4; j++)
+                    if (e[j] == e[j]) amax_merge2(bv, bi, e[j], c + j);
+            }
+        }
+    } else {
+        for (int c = threadIdx.x; c < V; c += kArgmaxThreads) {
+            const float v = xr[c];
+            if (v == v) amax_merge2(bv, bi, v, c);
+        }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
-        float v2 = __shfl_xor_sync(0xffffffffu, bv, o);
-        int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+        const float v2 = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
         amax_merge2(bv, bi, v2, i2);
     }
-    __shared__ float sv[32];
-    __shared__ int si[32];
-    __shared__ int s_last;
-    int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+    __shared__ float sv[kArgmaxThreads / 32];
+    __shared__ int si[kArgmaxThreads / 32];
+    const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
     if (lane == 0) {
         sv[warp] = bv;
         si[warp] = bi;
     }
     __syncthreads();
     if (threadIdx.x == 0) {
-        for (int w = 1; w < (int)(blockDim.x / 32); w++) amax_merge2(bv, bi, sv[w], si[w]);
-        if (bi >= 0) atomicMax(&keys[row], argmax_key(bv, bi));
-        __threadfence();
-        s_last = atomicAdd(&cnt[row], 1u) == gridDim.y - 1;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0 && s_last) {
-        __threadfence();
-        unsigned long long k = atomicExch(&keys[row], 0ull);
-        int id = k ? argmax_key_index(k) : 0;
+        for (int w = 1; w < kArgmaxThreads / 32; w++) amax_merge2(bv, bi, sv[w], si[w]);
+        const int id = bi >= 0 ? bi : 0;
         cur_ids[row] = id;
-        int step = state[1];
+        const int step = state[1];
         if (step < max_gen) out_ids[(int64_t)row * max_gen + step] = id;
-        cnt[row] = 0u;
     }
 }
 
@@ -334,10 +346,13 @@ struct tb_decoder {
     float* logits = nullptr;
     int32_t *ids_in = nullptr, *cur_ids = nullptr, *out_ids = nullptr;
     int* state = nullptr;   // [0] tokens in cache, [1] tokens generated
-    unsigned long long* amax_keys = nullptr;   // [max_batch], zero between launches
-    unsigned* amax_cnt = nullptr;              // [max_batch], zero between launches
     cudaStream_t cap_stream = nullptr;
     cudaGraphExec_t graph = nullptr;
+    // generate(): kGenGraphSteps decode steps captured back to back in one graph,
+    // so consecutive steps are chained by programmatic dependent launch instead
+    // of paying a graph launch each (~6 us of idle GPU between replays)
+    cudaGraphExec_t graph_multi = nullptr;
+    int graph_multi_B = 0;
     int graph_B = 0;
     int B = 0;       // batch of the current sequences
     int S0 = 0;      // prompt length
@@ -524,10 +539,8 @@ int head_forward(tb_decoder* d, int B, int64_t last_row_stride, int64_t last_row
     const tb_decoder_config& c = d->cfg;
     TB_TRY(norm_lin(d, d->x + last_row_off, last_row_stride, d->final_norm, d->lm_head, d->qlm, d->slm, d->logits, B,
                     c.vocab, false, true));
-    const int chunk = 2048, nch = (c.vocab + chunk - 1) / chunk;
-    return launch(d->ctx, "argmax_step", argmax_step_kernel, dim3(B, nch), dim3(256), 0, (const float*)d->logits,
-                  c.vocab, chunk, d->cur_ids, d->out_ids, c.max_seq, (const int*)d->state, d->amax_keys,
-                  d->amax_cnt);
+    return launch(d->ctx, "argmax_step", argmax_step_kernel, dim3(B), dim3(kArgmaxThreads), 0, (const float*)d->logits,
+                  c.vocab, d->cur_ids, d->out_ids, c.max_seq, (const int*)d->state);
 }
 
 // The decode chain's GEMVs of layer l (one token per sequence, B sequences).
@@ -638,11 +651,14 @@ int decode_step_body(tb_decoder* d) {
     return launch(d->ctx, "advance", advance_kernel, dim3(1), dim3(1), 0, d->state, 1, 1);
 }
 
-int ensure_graph(tb_decoder* d) {
-    if (d->graph && d->graph_B == d->B) return TB_OK;
-    if (d->graph) {
-        cudaGraphExecDestroy(d->graph);
-        d->graph = nullptr;
+constexpr int kGenGraphSteps = 8;
+
+// Capture `steps` decode steps into *exec (rebuilt when the batch changes).
+int capture_steps(tb_decoder* d, int steps, cudaGraphExec_t* exec, int* exec_B) {
+    if (*exec && *exec_B == d->B) return TB_OK;
+    if (*exec) {
+        cudaGraphExecDestroy(*exec);
+        *exec = nullptr;
     }
     tb_ctx* ctx = d->ctx;
     cudaStream_t saved = ctx->stream;
@@ -656,7 +672,8 @@ int ensure_graph(tb_decoder* d) {
         ctx->stream = saved;
         return set_error(ctx, TB_ERR_CUDA, "decode graph: begin capture: %s", cudaGetErrorString(e));
     }
-    int rc = decode_step_body(d);
+    int rc = TB_OK;
+    for (int i = 0; i < steps && !rc; i++) rc = decode_step_body(d);
     e = cudaStreamEndCapture(d->cap_stream, &g);
     ctx->stream = saved;
     if (rc) {
@@ -664,12 +681,14 @@ int ensure_graph(tb_decoder* d) {
         return rc;
     }
     if (e != cudaSuccess) return set_error(ctx, TB_ERR_CUDA, "decode graph: end capture: %s", cudaGetErrorString(e));
-    e = cudaGraphInstantiate(&d->graph, g, 0);
+    e = cudaGraphInstantiate(exec, g, 0);
     cudaGraphDestroy(g);
     if (e != cudaSuccess) return set_error(ctx, TB_ERR_CUDA, "decode graph: instantiate: %s", cudaGetErrorString(e));
-    d->graph_B = d->B;
+    *exec_B = d->B;
     return TB_OK;
 }
+
+int ensure_graph(tb_decoder* d) { return capture_steps(d, 1, &d->graph, &d->graph_B); }
 
 }  // namespace
 
@@ -743,8 +762,6 @@ int tb_decoder_create(tb_ctx* ctx, const tb_decoder_config* cfg, tb_decoder** ou
     A(&d->cur_ids, (size_t)c.max_batch);
     A(&d->out_ids, (size_t)c.max_batch * c.max_seq);
     A(&d->state, 4);
-    A(&d->amax_keys, (size_t)c.max_batch);
-    A(&d->amax_cnt, (size_t)c.max_batch);
     if (rc) {
         tb_decoder_destroy(d);
         return rc;
@@ -769,8 +786,6 @@ int tb_decoder_create(tb_ctx* ctx, const tb_decoder_config* cfg, tb_decoder** ou
             d->use_chain = true;
         }
     }
-    cudaMemset(d->amax_keys, 0, (size_t)c.max_batch * sizeof(unsigned long long));
-    cudaMemset(d->amax_cnt, 0, (size_t)c.max_batch * sizeof(unsigned));
     cudaMemset(d->state, 0, 4 * sizeof(int));
     cudaMemset(d->kcache, 0, (size_t)d->cache_layer_elems * c.n_layers * sizeof(bf16));
     cudaMemset(d->vcache, 0, (size_t)d->cache_layer_elems * c.n_layers * sizeof(bf16));
@@ -794,6 +809,7 @@ int tb_decoder_destroy(tb_decoder* d) {
     if (!d) return TB_OK;
     cudaSetDevice(d->ctx->device);
     if (d->graph) cudaGraphExecDestroy(d->graph);
+    if (d->graph_multi) cudaGraphExecDestroy(d->graph_multi);
     if (d->cap_stream) cudaStreamDestroy(d->cap_stream);
     for (void* p : d->allocs) cudaFree(p);
     delete d;
@@ -1014,7 +1030,14 @@ int tb_decoder_generate(tb_decoder* d, const int32_t* prompt_ids, int B, int S, 
     if (!d || !prompt_ids || !out_ids) return TB_ERR_ARG;
     TB_REQUIRE(d->ctx, n_new >= 1 && S + n_new <= d->cfg.max_seq, TB_ERR_SHAPE, "generate: S + n_new > max_seq");
     TB_TRY(tb_decoder_prefill(d, prompt_ids, B, S, nullptr, nullptr));
-    for (int i = 1; i < n_new; i++) TB_TRY(tb_decoder_decode_step(d, nullptr, nullptr, nullptr));
+    int left = n_new - 1;
+    if (left >= kGenGraphSteps) TB_TRY(capture_steps(d, kGenGraphSteps, &d->graph_multi, &d->graph_multi_B));
+    for (; left >= kGenGraphSteps; left -= kGenGraphSteps) {
+        TB_CUDA_TRY(d->ctx, cudaGraphLaunch(d->graph_multi, d->ctx->stream));
+        d->host_len += kGenGraphSteps;
+        d->host_step += kGenGraphSteps;
+    }
+    for (; left > 0; left--) TB_TRY(tb_decoder_decode_step(d, nullptr, nullptr, nullptr));
     TB_CUDA_TRY(d->ctx, cudaMemcpy2DAsync(out_ids, (size_t)n_new * sizeof(int32_t), d->out_ids,
                                           (size_t)d->cfg.max_seq * sizeof(int32_t), (size_t)n_new * sizeof(int32_t), B,
                                           cudaMemcpyDeviceToDevice, d->ctx->stream));

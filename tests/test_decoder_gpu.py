@@ -73,6 +73,26 @@ def test_decoder_generate_matches_stepwise():
     no_device_error()
 
 
+def test_decoder_generate_long_matches_stepwise():
+    """generate() replays a graph of several decode steps (plus single steps for the
+    rest): the tokens equal prefill + one decode_step at a time, again on the same
+    decoder (the graphs are reused) and at another batch size (rebuilt)."""
+    dev()
+    cfg = SmallCfg()
+    p = random_params(cfg, seed=6)
+    dec = make(cfg)
+    upload(dec, p)
+    rng = np.random.default_rng(10)
+    for B, n_new in ((3, 20), (3, 17), (2, 9)):
+        ids = torch.from_numpy(rng.integers(0, cfg.vocab, (B, 40)).astype(np.int32)).cuda()
+        out = dec.generate(ids, n_new=n_new)
+        toks = [dec.prefill(ids)]
+        for _ in range(n_new - 1):
+            toks.append(dec.decode_step())
+        assert torch.equal(out, torch.stack(toks, dim=1)), (B, n_new)
+    no_device_error()
+
+
 def test_decoder_int8():
     dev()
     cfg = SmallCfg()
