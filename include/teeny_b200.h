@@ -316,8 +316,9 @@ TB_API int tb_argmax_noalloc_fwd(tb_ctx* ctx, int dtype, const void* x, int32_t*
  * mod.rs:2472-2530).  It plays the role of LoadedModel (drivers/teeny-cuda/
  * src/model/mod.rs:231-700): it owns the parameters, a KV cache and every
  * activation buffer (allocated once at create, not per forward), runs prefill
- * stream-ordered without per-op synchronisation, and replays each decode step
- * as one captured CUDA graph (capture_graph, model/mod.rs:1245).
+ * stream-ordered without per-op synchronisation, and replays decode steps as
+ * captured CUDA graphs (capture_graph, model/mod.rs:1245): one step per
+ * tb_decoder_decode_step, eight steps per replay inside tb_decoder_generate.
  * Pre-norm blocks: x += Wo attn(rope(Wqkv rmsnorm(x))); x += Wdown swiglu(
  * Wgate/up rmsnorm(x)); logits = lm_head rmsnorm(x_last); greedy argmax. */
 typedef struct tb_decoder tb_decoder;
