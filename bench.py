@@ -722,7 +722,8 @@ def run_c1(args, rank, world, local):
 
 def ncu_case(which):
     """Small fixed cases for ncu captures of one kernel kind (the commands in profiles/):
-    gemv, gemv8, attn_dec, gemm, fa, conv, or c4 (prefill + 3 decode steps for the launch list)."""
+    gemv, gemv8, attn_dec, gemm, fa, conv, c4 (prefill + 3 decode steps for the launch list) or c5
+    (the int8 decoder: KV fill + 2 decode steps)."""
     import torch
     from teenygrad_b200 import ops
     torch.manual_seed(0)
@@ -760,6 +761,15 @@ def ncu_case(which):
         xh, wp = x.permute(0, 2, 3, 1).contiguous(), ops.conv2d_pack_weights(w)
         for _ in range(2):
             ops.conv2d(xh, wp, scale=sc, shift=sh, pad=1, act="relu", x_nhwc=True, y_nhwc=True, w_packed=True)
+    elif which == "c5":          # C5 int8 decoder: batch 64 over a 2048-position cache, 2 decode steps
+        from teenygrad_b200.decoder import Decoder, DecoderConfig
+        c = C5
+        dec = Decoder(DecoderConfig(max_batch=c["batch"], max_seq=c["ctx"] + 64, max_prefill_tokens=c["batch"],
+                                    weights_int8=True))
+        dec.init_random(7)
+        dec.fill_kv_random(torch.randint(0, c["vocab"], (c["batch"],), dtype=torch.int32, device="cuda"), c["ctx"], seed=5)
+        for _ in range(2):
+            dec.decode_step()
     elif which == "c4":          # C4 decoder: prefill 16 x 1024 + 3 graph-replayed decode steps
         from teenygrad_b200.decoder import Decoder, DecoderConfig
         dec = Decoder(DecoderConfig(max_batch=16, max_seq=1024 + 128, max_prefill_tokens=16 * 1024))
