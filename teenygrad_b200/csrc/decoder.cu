@@ -426,6 +426,16 @@ int norm_lin(tb_decoder* d, const bf16* x, int64_t ldx, const bf16* norm_w, cons
     const int K = d->cfg.d_model;
     if (M > 64) {
         TB_TRY(rms(d, x, ldx, norm_w, d->h, M));
+        if (qkv && qkv->rope_tab) {
+            // the QKV GEMM with RoPE and the KV-cache write in its epilogue
+            Epi ep = *qkv;
+            ep.out = y;
+            ep.ldo = N;
+            ep.ldr = N;
+            const bool int8 = d->cfg.weights_int8 && wq;
+            if (int8) ep.scale = wscale;
+            return linear_launch(d->ctx, int8 ? 1 : 0, d->h, int8 ? (const void*)wq : w, ep, M, N, K);
+        }
         return lin(d, d->h, w, wq, wscale, y, M, N, K, nullptr, swiglu, out_f32, qkv ? qkv->perm_hd : 0);
     }
     Epi ep = qkv ? *qkv : Epi{};
@@ -482,10 +492,10 @@ int layer_forward(tb_decoder* d, int l, int B, int S_new, bool decode) {
     bf16* kc = d->kcache + (int64_t)l * d->cache_layer_elems;
     bf16* vc = d->vcache + (int64_t)l * d->cache_layer_elems;
 
-    // QKV projection.  With permuted QKV weights and <= 64 tokens (the decode
-    // GEMV) RoPE and the KV-cache writes happen in the GEMV epilogue; otherwise
-    // the projection is written in natural order and rope_kv follows.
-    const bool fused_rope = d->qkv_perm && T <= 64;
+    // QKV projection.  With permuted QKV weights RoPE and the KV-cache writes
+    // happen in the epilogue (the decode GEMV and the prefill GEMM alike);
+    // otherwise the projection is written in natural order and rope_kv follows.
+    const bool fused_rope = d->qkv_perm;
     Epi qe{};
     if (d->qkv_perm) qe.perm_hd = hd;
     if (fused_rope) {

@@ -199,6 +199,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         const int q = warp & 3, half = (warp - 4) >> 2;
         const uint32_t t_lane = tmem + ((uint32_t)(q * 32) << 16);
         const bool f32o = ep.out_f32 != 0;
+        const int pos_base = ep.rope_tab ? (ep.pos_ptr ? *ep.pos_ptr : ep.pos_host) : 0;
         bool ok = true;
         int tl = 0;
         for (int t = blockIdx.x; t < tiles; t += gridDim.x, tl++) {
@@ -210,7 +211,62 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             tc_fence_after();
             const uint32_t t_row = t_lane + ab * BN;
             const int row = m0 + q * 32 + lane;
-            if (!ep.swiglu) {
+            if (ep.rope_tab) {
+                // QKV with RoPE and the KV-cache write: the weight rows are permuted per
+                // 256-row tile (qkv_perm_row), so columns p < 128 and p + 128 of the tile
+                // are dims (i, i + hd/2) of one head, and a chunk of 32 pairs lies in one
+                // head.  The projection is rounded to bf16 first, as the unfused path
+                // stores it, then rotated (rotate-half); q goes to out in natural order,
+                // k and v to the caches at position pos_base + (row % rope_s_new).
+                const int hd = ep.perm_hd, hh = hd / 2;
+                __nv_bfloat16* outb = reinterpret_cast<__nv_bfloat16*>(ep.out);
+#pragma unroll 1
+                for (int c = half * 64; c < half * 64 + 64; c += 32) {
+                    float a[32], bv[32];
+                    tmem_ld32(t_row + c, a);
+                    tmem_ld32(t_row + 128 + c, bv);
+                    tmem_wait_ld();
+                    const int H = (n0 / 256) * (256 / hd) + c / hh, ri0 = c % hh;
+                    const int kind = H < ep.rope_hq ? 0
+                                   : H < ep.rope_hq + ep.rope_hkv ? 1
+                                   : H < ep.rope_hq + 2 * ep.rope_hkv ? 2 : 3;
+                    if (!ok || row >= M || kind == 3) continue;
+                    const int bs = row / ep.rope_s_new, pos = pos_base + row % ep.rope_s_new;
+                    if (pos < 0 || pos >= ep.max_seq) {
+                        atomicOr(err, 1 << 5);
+                        continue;
+                    }
+                    __nv_bfloat16* dst;
+                    if (kind == 0)
+                        dst = outb + (int64_t)row * ep.ldo + (int64_t)H * hd;
+                    else if (kind == 1)
+                        dst = reinterpret_cast<__nv_bfloat16*>(ep.kcache) +
+                              (((int64_t)bs * ep.rope_hkv + (H - ep.rope_hq)) * ep.max_seq + pos) * hd;
+                    else
+                        dst = reinterpret_cast<__nv_bfloat16*>(ep.vcache) +
+                              (((int64_t)bs * ep.rope_hkv + (H - ep.rope_hq - ep.rope_hkv)) * ep.max_seq + pos) * hd;
+                    const float2* tab = ep.rope_tab + (int64_t)pos * hh + ri0;
+#pragma unroll
+                    for (int j = 0; j < 32; j += 8) {
+                        float y0[8], y1[8];
+#pragma unroll
+                        for (int i = 0; i < 8; i++) {
+                            const float x0 = __bfloat162float(__float2bfloat16_rn(a[j + i]));
+                            const float x1 = __bfloat162float(__float2bfloat16_rn(bv[j + i]));
+                            if (kind <= 1) {
+                                const float2 cs = tab[j + i];
+                                y0[i] = x0 * cs.x - x1 * cs.y;
+                                y1[i] = x1 * cs.x + x0 * cs.y;
+                            } else {
+                                y0[i] = x0;
+                                y1[i] = x1;
+                            }
+                        }
+                        store_row8(dst, false, ri0 + j, y0);
+                        store_row8(dst, false, hh + ri0 + j, y1);
+                    }
+                }
+            } else if (!ep.swiglu) {
 #pragma unroll 1
                 for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 32) {
                     float v[32];
@@ -1085,7 +1141,7 @@ static int dispatch_gemv(tb_ctx* ctx, const void* x, const void* w, const Epi& e
 int linear_launch(tb_ctx* ctx, int int8, const void* x, const void* w, const Epi& ep, int M, int N, int K) {
     if (ep.perm_hd) {
         if ((ep.perm_hd != 64 && ep.perm_hd != 128) || N % 256 || ep.bias || ep.resid || ep.swiglu || ep.out_f32 ||
-            (ep.rope_tab && (M > 64 || ep.rope_s_new <= 0)) || (!ep.rope_tab && (M <= 64 || int8)))
+            (ep.rope_tab && ep.rope_s_new <= 0) || (!ep.rope_tab && (M <= 64 || int8)))
             return set_error(ctx, TB_ERR_UNSUPPORTED, "linear: permuted QKV epilogue configuration");
     }
     if (ep.norm_w && (M > 64 || K % 8 || ep.x_ld % 8 || (reinterpret_cast<uintptr_t>(x) & 15) ||
