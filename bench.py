@@ -499,11 +499,12 @@ def run_c4(args, rank, world, local):
             "peak_source": pk["src"]}
     if comm is not None:
         comm.close()
-    # prefill: set_state, embedding, per layer (rmsnorm, QKV GEMM, rope_kv, attention,
-    # O GEMM, rmsnorm, gate/up GEMM, down GEMM), LM-head GEMV (norm fused), argmax, advance.
+    # prefill: set_state, embedding, per layer (rmsnorm, QKV GEMM with RoPE + KV-cache write
+    # fused, attention, O GEMM, rmsnorm, gate/up GEMM, down GEMM), LM-head GEMV (norm fused),
+    # argmax, advance.
     # decode: embedding, per layer (QKV GEMV with norm + RoPE + KV-cache write fused,
     # attention, O GEMV, gate/up GEMV with norm fused, down GEMV), LM head, argmax, advance.
-    launches_prefill = 2 + 8 * c["n_layers"] + 3
+    launches_prefill = 2 + 7 * c["n_layers"] + 3
     launches_decode = 1 + 5 * c["n_layers"] + 3
     launches = launches_prefill + (G - 1) * launches_decode
     cfg = {"workload": "C4: Llama-style 1B decoder, global batch 16 x 1024-token prompts + 128 greedy tokens, "
