@@ -129,13 +129,37 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    pdl_wait();
 
     if (warp == 0) {
-        // ---------------- TMA producer
+        // ---------------- TMA producer.  The weights (B) do not depend on the
+        // previous kernel: the first tile's first STAGES K-blocks of them are
+        // requested before waiting for it, the activations (A) after.
         if (lane == 0) {
             tma_prefetch_desc(&tmA);
             tma_prefetch_desc(&tmB);
+            auto load_b = [&](int s, int kb, int n0) {
+                if (!B_MN) {
+                    tma_load_2d(smem_u32(sB + s * B_BYTES), &tmB, full0 + 8 * s, kb * GEMM_BK, n0);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < BN / 64; j++)
+                        tma_load_2d(smem_u32(sB + s * B_BYTES + j * 64 * 128), &tmB, full0 + 8 * s, n0 + 64 * j,
+                                    kb * GEMM_BK);
+                }
+            };
+            int pre = 0;
+            if ((int)blockIdx.x < tiles) {
+                int mi, ni;
+                gemm_tile(blockIdx.x, mt, ntl, gm, mi, ni);
+                pre = nk < STAGES ? nk : STAGES;
+                for (int kb = 0; kb < pre; kb++) {
+                    mbar_expect_tx(full0 + 8 * kb, A_BYTES + B_BYTES);
+                    load_b(kb, kb, ni * BN);
+                }
+                pdl_wait();
+                for (int kb = 0; kb < pre; kb++)
+                    tma_load_2d(smem_u32(sA + kb * A_BYTES), &tmA, full0 + 8 * kb, kb * GEMM_BK, mi * GEMM_BM);
+            }
             int it = 0;
             bool ok = true;
             for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x) {
@@ -143,6 +167,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 gemm_tile(t, mt, ntl, gm, mi, ni);
                 const int m0 = mi * GEMM_BM, n0 = ni * BN;
                 for (int kb = 0; kb < nk; kb++, it++) {
+                    if (it < pre) continue;   // requested above
                     const int s = it % STAGES;
                     if (it >= STAGES && !mbar_wait(empty0 + 8 * s, ((it / STAGES) - 1) & 1, err, DEV_ERR_TIMEOUT_EMPTY)) {
                         ok = false;
@@ -150,14 +175,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     }
                     mbar_expect_tx(full0 + 8 * s, A_BYTES + B_BYTES);
                     tma_load_2d(smem_u32(sA + s * A_BYTES), &tmA, full0 + 8 * s, kb * GEMM_BK, m0);
-                    if (!B_MN) {
-                        tma_load_2d(smem_u32(sB + s * B_BYTES), &tmB, full0 + 8 * s, kb * GEMM_BK, n0);
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < BN / 64; j++)
-                            tma_load_2d(smem_u32(sB + s * B_BYTES + j * 64 * 128), &tmB, full0 + 8 * s, n0 + 64 * j,
-                                        kb * GEMM_BK);
-                    }
+                    load_b(s, kb, n0);
                 }
             }
             // every issued stage has landed before the CTA can exit
@@ -196,6 +214,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         }
     } else if (warp >= 4) {
         // ---------------- epilogue: TMEM lane quarter q = warp % 4, column half
+        pdl_wait();   // the previous kernel is done before any global read or write here
         const int q = warp & 3, half = (warp - 4) >> 2;
         const uint32_t t_lane = tmem + ((uint32_t)(q * 32) << 16);
         const bool f32o = ep.out_f32 != 0;
