@@ -463,6 +463,11 @@ conv_pm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ 
     const int nc = (Cp + 63) / 64;            // 64-channel chunks
     const int taps = KH * KW;
     const int wslots = taps * nc;             // resident weights of this CTA's output block
+    // The patch ring is split into one sub-ring of PD slots per MMA issuer (slots
+    // i * PD ..): the issuers take tiles in turn, and a slot shared between them
+    // could be waited on two fills ahead of its barrier, which a parity wait
+    // cannot tell from one fill behind.  One producer and one consumer per slot.
+    const int PD = AS / PM_ISSUERS;
     uint8_t* sP = smem;                                        // [AS] patches
     uint8_t* sW = sP + AS * a_bytes;                           // weight slices
     uint8_t* sO = sW + wslots * CONV_W_BYTES;                  // [2 groups] output staging
@@ -526,30 +531,32 @@ conv_pm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ 
         if (lane == 0) {
             tma_prefetch_desc(&tmX);
             tma_prefetch_desc(&tmW);
-            int pi = 0;
+            int jc[PM_ISSUERS] = {0, 0, 0, 0};   // patches handed to each issuer so far
             bool ok = true;
             if (blockIdx.x < units) {
                 mbar_expect_tx(w_full, (uint32_t)(wslots * CONV_W_BYTES));
                 for (int k = 0; k < wslots; k++)
                     tma_load_2d(smem_u32(sW + k * CONV_W_BYTES), &tmW, w_full, (k % taps) * Cp + (k / taps) * 64, n0c);
             }
-            for (int t = blockIdx.x; ok && t < units; t += gridDim.x) {
+            for (int t = blockIdx.x, tl = 0; ok && t < units; t += gridDim.x, tl++) {
                 int b, oh0, ow0;
                 tile_of(t, b, oh0, ow0);
+                const int i = tl % PM_ISSUERS;
                 for (int c = 0; ok && c < nc; c++) {
-                    const int sp = pi % AS;
-                    if (pi >= AS && !mbar_wait(p_empty0 + 8 * sp, ((pi / AS) - 1) & 1, err, DEV_ERR_TIMEOUT_EMPTY)) {
+                    const int j = jc[i]++;
+                    const int sp = i * PD + j % PD;
+                    if (j >= PD && !mbar_wait(p_empty0 + 8 * sp, ((j / PD) - 1) & 1, err, DEV_ERR_TIMEOUT_EMPTY)) {
                         ok = false;
                         break;
                     }
                     mbar_expect_tx(p_full0 + 8 * sp, (uint32_t)conv_patch_bytes(PM_BH, KH, KW));
                     tma_load_4d(smem_u32(sP + sp * a_bytes), &tmX, p_full0 + 8 * sp, c * 64, ow0 - pad, oh0 - pad, b);
-                    pi++;
                 }
             }
             // every load issued has landed before the CTA can exit
-            for (int k = (pi > AS ? pi - AS : 0); k < pi; k++)
-                mbar_wait(p_full0 + 8 * (k % AS), (k / AS) & 1, err, DEV_ERR_TIMEOUT_FULL);
+            for (int i = 0; i < PM_ISSUERS; i++)
+                for (int j = (jc[i] > PD ? jc[i] - PD : 0); j < jc[i]; j++)
+                    mbar_wait(p_full0 + 8 * (i * PD + j % PD), (j / PD) & 1, err, DEV_ERR_TIMEOUT_FULL);
             if (blockIdx.x < units) mbar_wait(w_full, 0, err, DEV_ERR_TIMEOUT_FULL);
         }
     } else if (iss >= 0) {
@@ -566,9 +573,9 @@ conv_pm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ 
                 tc_fence_after();
                 const uint32_t d_tmem = tmem + ab * CONV_BN;
                 for (int c = 0; ok && c < nc; c++) {
-                    const int pi = tl * nc + c;          // patch sequence number (producer order)
-                    const int sp = pi % AS;
-                    if (!mbar_wait(p_full0 + 8 * sp, (pi / AS) & 1, err, DEV_ERR_TIMEOUT_FULL)) {
+                    const int j = (tl / PM_ISSUERS) * nc + c;   // this issuer's patch number
+                    const int sp = iss * PD + j % PD;
+                    if (!mbar_wait(p_full0 + 8 * sp, (j / PD) & 1, err, DEV_ERR_TIMEOUT_FULL)) {
                         ok = false;
                         break;
                     }
@@ -879,8 +886,8 @@ int tb_conv2d_fwd_ex(tb_ctx* ctx, int dtype, const void* x, const void* w, const
         // pixels-as-rows kernel: resident weights and at least four patch stages
         // (one per MMA issuer) must fit; TB_CONV_PM=0 keeps conv_tc_kernel
         static const bool pm_off = getenv("TB_CONV_PM") && getenv("TB_CONV_PM")[0] == '0';
-        int AS = 0;
-        for (int a = 8; a >= 4 && !AS; a--)
+        int AS = 0;   // patch slots: a sub-ring of AS / 4 per MMA issuer
+        for (int a = 8; a >= 4 && !AS; a -= 4)
             if (pm_smem_bytes(KH, KW, a, wall) <= kSmemMax) AS = a;
         if (!pm_off && AS && nN <= ctx->num_sms && PM_BH + KH - 1 <= 256) {
             CUtensorMap mx, mw, my;
