@@ -189,6 +189,11 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ 
     const int nc = (Cp + 63) / 64;            // 64-channel chunks
     const int taps = KH * KW;
     const int wslots = wres ? taps * nc : CONV_WS;
+    // Patch and (streaming) weight rings: one half per MMA issuer (slots i * PD ..,
+    // i * WD ..).  The issuers take tiles in turn, and a slot shared between them
+    // could be waited on two fills ahead of its barrier, which a parity wait
+    // cannot tell from one fill behind.  One producer and one consumer per slot.
+    const int PD = AS / 2, WD = CONV_WS / 2;
     uint8_t* sP = smem;                                        // [AS] patches
     uint8_t* sW = sP + AS * a_bytes;                           // weight slices
     uint8_t* sO = sW + wslots * CONV_W_BYTES;                  // [2] output staging (also the
@@ -241,7 +246,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ 
         if (lane == 0) {
             tma_prefetch_desc(&tmX);
             tma_prefetch_desc(&tmW);
-            int pi = 0, wi = 0;
+            int jp[2] = {0, 0}, jw[2] = {0, 0};   // patches / weight slices handed to each issuer
             bool ok = true;
             if (wres && blockIdx.x < units) {
                 // every weight slice of this CTA's output block (grid % nN == 0: fixed block)
@@ -250,36 +255,38 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ 
                 for (int k = 0; k < wslots; k++)
                     tma_load_2d(smem_u32(sW + k * CONV_W_BYTES), &tmW, w_full0, (k % taps) * Cp + (k / taps) * 64, n0);
             }
-            for (int t = blockIdx.x; ok && t < units; t += gridDim.x) {
+            for (int t = blockIdx.x, tl = 0; ok && t < units; t += gridDim.x, tl++) {
                 int b, oh0, ow0, n0;
                 tile_of(t, b, oh0, ow0, n0);
+                const int i = tl & 1;   // the issuer of this tile
                 for (int c = 0; ok && c < nc; c++) {
-                    const int sp = pi % AS;
-                    if (pi >= AS && !mbar_wait(p_empty0 + 8 * sp, ((pi / AS) - 1) & 1, err, DEV_ERR_TIMEOUT_EMPTY)) {
+                    const int j = jp[i]++;
+                    const int sp = i * PD + j % PD;
+                    if (j >= PD && !mbar_wait(p_empty0 + 8 * sp, ((j / PD) - 1) & 1, err, DEV_ERR_TIMEOUT_EMPTY)) {
                         ok = false;
                         break;
                     }
                     mbar_expect_tx(p_full0 + 8 * sp, (uint32_t)conv_patch_bytes(BH, KH, KW));
                     tma_load_4d(smem_u32(sP + sp * a_bytes), &tmX, p_full0 + 8 * sp, c * 64, ow0 - pad, oh0 - pad, b);
-                    pi++;
                     for (int tap = 0; !wres && tap < taps; tap++) {
-                        const int sw = wi % CONV_WS;
-                        if (wi >= CONV_WS &&
-                            !mbar_wait(w_empty0 + 8 * sw, ((wi / CONV_WS) - 1) & 1, err, DEV_ERR_TIMEOUT_EMPTY)) {
+                        const int jj = jw[i]++;
+                        const int sw = i * WD + jj % WD;
+                        if (jj >= WD && !mbar_wait(w_empty0 + 8 * sw, ((jj / WD) - 1) & 1, err, DEV_ERR_TIMEOUT_EMPTY)) {
                             ok = false;
                             break;
                         }
                         mbar_expect_tx(w_full0 + 8 * sw, CONV_W_BYTES);
                         tma_load_2d(smem_u32(sW + sw * CONV_W_BYTES), &tmW, w_full0 + 8 * sw, tap * Cp + c * 64, n0);
-                        wi++;
                     }
                 }
             }
             // every load issued has landed before the CTA can exit
-            for (int k = (pi > AS ? pi - AS : 0); k < pi; k++)
-                mbar_wait(p_full0 + 8 * (k % AS), (k / AS) & 1, err, DEV_ERR_TIMEOUT_FULL);
-            for (int k = (wi > CONV_WS ? wi - CONV_WS : 0); k < wi; k++)
-                mbar_wait(w_full0 + 8 * (k % CONV_WS), (k / CONV_WS) & 1, err, DEV_ERR_TIMEOUT_FULL);
+            for (int i = 0; i < 2; i++) {
+                for (int j = (jp[i] > PD ? jp[i] - PD : 0); j < jp[i]; j++)
+                    mbar_wait(p_full0 + 8 * (i * PD + j % PD), (j / PD) & 1, err, DEV_ERR_TIMEOUT_FULL);
+                for (int j = (jw[i] > WD ? jw[i] - WD : 0); j < jw[i]; j++)
+                    mbar_wait(w_full0 + 8 * (i * WD + j % WD), (j / WD) & 1, err, DEV_ERR_TIMEOUT_FULL);
+            }
             if (wres && blockIdx.x < units) mbar_wait(w_full0, 0, err, DEV_ERR_TIMEOUT_FULL);
         }
     } else if (warp == 1 || warp == 2) {
@@ -299,17 +306,17 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ 
                 tc_fence_after();
                 const uint32_t d_tmem = tmem + ab * CONV_ACC_COLS;
                 for (int c = 0; ok && c < nc; c++) {
-                    const int pi = tl * nc + c;          // patch sequence number (producer order)
-                    const int sp = pi % AS;
-                    if (!mbar_wait(p_full0 + 8 * sp, (pi / AS) & 1, err, DEV_ERR_TIMEOUT_FULL)) {
+                    const int j = (tl >> 1) * nc + c;    // this issuer's patch number
+                    const int sp = par * PD + j % PD;
+                    if (!mbar_wait(p_full0 + 8 * sp, (j / PD) & 1, err, DEV_ERR_TIMEOUT_FULL)) {
                         ok = false;
                         break;
                     }
                     const uint64_t b_st = b_desc0 + (uint64_t)((sp * a_bytes) >> 4);
                     for (int tap = 0, kh = 0, kw = 0; tap < taps; tap++) {
-                        const int wi = pi * taps + tap;  // weight slice sequence number (streaming mode)
-                        const int sw = wres ? c * taps + tap : wi % CONV_WS;
-                        if (!wres && !mbar_wait(w_full0 + 8 * sw, (wi / CONV_WS) & 1, err, DEV_ERR_TIMEOUT_FULL)) {
+                        const int wi = j * taps + tap;   // this issuer's weight slice number (streaming mode)
+                        const int sw = wres ? c * taps + tap : par * WD + wi % WD;
+                        if (!wres && !mbar_wait(w_full0 + 8 * sw, (wi / WD) & 1, err, DEV_ERR_TIMEOUT_FULL)) {
                             ok = false;
                             break;
                         }
@@ -959,10 +966,9 @@ int tb_conv2d_fwd_ex(tb_ctx* ctx, int dtype, const void* x, const void* w, const
     // tile's store) with the deepest patch ring that fits beside them.
     const int wres = conv_smem_bytes(BH, KH, KW, 2, wall, 1) <= kSmemMax && nN <= ctx->num_sms ? 1 : 0;
     const int wslots = wres ? wall : CONV_WS;
-    int AS = 2, OS = 1;
-    if (conv_smem_bytes(BH, KH, KW, 3, wslots, 2) <= kSmemMax) AS = 3, OS = 2;
+    int AS = 2, OS = 1;   // patch slots: a half per MMA issuer, so an even count
+    if (conv_smem_bytes(BH, KH, KW, 4, wslots, 2) <= kSmemMax) AS = 4, OS = 2;
     else if (conv_smem_bytes(BH, KH, KW, 2, wslots, 2) <= kSmemMax) AS = 2, OS = 2;
-    else if (conv_smem_bytes(BH, KH, KW, 3, wslots, 1) <= kSmemMax) AS = 3, OS = 1;
     const int smem = conv_smem_bytes(BH, KH, KW, AS, wslots, OS);
     TB_CUDA_TRY(ctx, cudaFuncSetAttribute(conv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     const int64_t units = (int64_t)((s.OW + CONV_BW - 1) / CONV_BW) * ((s.OH + BH - 1) / BH) * B * nN;
