@@ -1,12 +1,10 @@
 // Row argmax that allocates nothing.
 //
-// The split-row argmax used by the decoder (several CTAs per row, one per
-// slice of the vocabulary, combined through a per-row 64-bit key and an
-// arrival counter) needs cross-CTA scratch.  The decoder allocates that
-// scratch when it is created.  This entry point serves callers that cannot
-// allocate device memory at all -- e.g. a serving loop whose device memory is
-// owned by an external pool -- by keeping the scratch in a file-scope device
-// array instead.
+// A split-row argmax (several CTAs per row, one per slice of the vocabulary,
+// combined through a per-row 64-bit key and an arrival counter) needs
+// cross-CTA scratch.  This entry point serves callers that cannot allocate
+// device memory at all -- e.g. a serving loop whose device memory is owned by
+// an external pool -- by keeping that scratch in a file-scope device array.
 //
 // Scratch: 16 bytes per row (key, counter), TB_ARGMAX_NOALLOC_MAX_ROWS rows,
 // resident on every GPU that loads the library until the process exits.
