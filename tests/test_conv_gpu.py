@@ -113,6 +113,22 @@ def test_conv2d_nhwc_chain(B, C, H, W, layers, act):
     assert_close(np_of(y), refs[-1], BF16_TOL, "stage output")
 
 
+@pytest.mark.parametrize("Cin,Cout,H,W", [(16, 24, 18, 16), (64, 72, 20, 24), (64, 48, 9, 8), (32, 16, 33, 40)])
+def test_conv2d_nhwc_out_channels(Cin, Cout, H, W):
+    """NHWC output written from registers: 16-byte stores (Cout % 16 == 8), 32-byte
+    stores (Cout % 16 == 0), a partial second channel block (Cout 72), clipped rows."""
+    r = rng(Cin + Cout + H)
+    x = bf16_round(r.standard_normal((2, Cin, H, W)))
+    w = bf16_round(r.standard_normal((Cout, Cin, 3, 3)) * np.sqrt(2.0 / (Cin * 9)))
+    sc = r.uniform(0.5, 1.5, Cout).astype(np.float32)
+    sh = r.normal(0, 0.1, Cout).astype(np.float32)
+    ref = bf16_round(oracle.conv2d(x, w, scale=sc, shift=sh, pad=1, act="relu"))
+    y = ops().conv2d(to_gpu(x, torch.bfloat16), to_gpu(w, torch.bfloat16), scale=to_gpu(sc), shift=to_gpu(sh), pad=1,
+                     act="relu", y_nhwc=True)
+    assert tuple(y.shape) == (2, H, W, Cout)
+    assert_close(np_of(y).transpose(0, 3, 1, 2), ref, BF16_TOL, "NHWC output")
+
+
 def test_conv2d_layout_flags_rejected():
     from teenygrad_b200._lib import TB_ERR_UNSUPPORTED, TeenyError
     r = rng(3)
