@@ -10,8 +10,8 @@
 //    with their own running max, row sum and TMEM O accumulator (merged once
 //    at the end): they read S from TMEM, run the online softmax in the exp2
 //    domain, rescale O in TMEM only when the max passes the reference by 2^8,
-//    and write P (bf16) into a double-buffered 128-B swizzled shared tile that
-//    the P.V MMA reads as its A operand.
+//    and write P (bf16) into TMEM over the S columns it came from, where the
+//    P.V MMA reads it as its A operand.
 //    The same online-softmax recurrence as flash_attention2_forward
 //    (nn/attention/flash_attn2.rs:98-140), over 128-key tiles instead of one
 //    key at a time, plus the causal mask and GQA head mapping.
@@ -48,14 +48,16 @@ constexpr float kLn2 = 0.6931471805599453f;
 // max, sum and O accumulator, merged at the end.  A
 // row's reference max is raised (and its O row and sum rescaled) only when a
 // tile's max passes it by 2^8; P = 2^(s - m) <= 256 is otherwise used as is,
-// so a tile normally needs no wait on the previous P V.  P is bf16 in one of
-// two swizzled shared-memory tiles (A operand), V the MN-major B operand.
+// so a tile normally needs no wait on the previous P V.  P is bf16 in TMEM over
+// the S columns it came from (the A operand of P V; no shared-memory round trip or
+// async-proxy fence), V the MN-major B operand; an S buffer takes the next S once
+// the P V that read its P has completed.
 template <int D>
 struct AttnCfg {
     static constexpr int BM = 128, BN = 128;
     static constexpr int TILE = 128 * D * 2;           // Q, K or V tile bytes
-    static constexpr int P_BYTES = 128 * 128 * 2;
-    static constexpr int SMEM = TILE /*Q*/ + 2 * TILE /*K*/ + 2 * TILE /*V*/ + 2 * P_BYTES + 1024 + 256;
+    static constexpr int XCH_BYTES = 2 * 128 * 2 * 4;  // (max, sum) of both key halves per row
+    static constexpr int SMEM = TILE /*Q*/ + 2 * TILE /*K*/ + 2 * TILE /*V*/ + XCH_BYTES + 1024 + 256;
     static constexpr int O_COL = 256;                  // TMEM columns: S0 [0,128), S1 [128,256), O_0, O_1 (D each)
     static constexpr float RESCALE_LOG2 = 8.f;
 };
@@ -73,8 +75,8 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
     uint8_t* sQ = smem;
     uint8_t* sK = sQ + C::TILE;
     uint8_t* sV = sK + 2 * C::TILE;
-    uint8_t* sP = sV + 2 * C::TILE;                  // [2]
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * C::P_BYTES);
+    float* xch = reinterpret_cast<float*>(sV + 2 * C::TILE);   // [2 halves][128 rows][2]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sV + 2 * C::TILE + C::XCH_BYTES);
     const uint32_t q_full = smem_u32(bars + 0);
     const uint32_t k_full0 = smem_u32(bars + 1), v_full0 = smem_u32(bars + 3);      // [2]
     const uint32_t k_empty0 = smem_u32(bars + 5), v_empty0 = smem_u32(bars + 7);    // [2]
@@ -136,7 +138,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
             mbar_init(k_empty0 + 8 * s, 1);
             mbar_init(v_empty0 + 8 * s, 1);
             mbar_init(s_full0 + 8 * s, 1);
-            mbar_init(s_free0 + 8 * s, 8);
+            mbar_init(s_free0 + 8 * s, 1);
             mbar_init(p_full0 + 8 * s, 8);
             mbar_init(p_free0 + 8 * s, 1);
         }
@@ -234,7 +236,6 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
         // ---------------- O += P V issuer
         if (lane == 0) {
             constexpr uint32_t idesc_o = idesc_bf16_f32(128, D, false, true);
-            const uint64_t p_desc = sdesc_sw128(smem_u32(sP), 16, 1024);
             const uint64_t v_desc = sdesc_sw128(smem_u32(sV), 16384, 1024);
             int g = 0, gq = 0;
             bool ok = true;
@@ -252,15 +253,17 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
                         break;
                     }
                     tc_fence_after();
-                    const uint64_t pd = p_desc + (uint64_t)((st * C::P_BYTES) >> 4);
                     const uint64_t vd = v_desc + (uint64_t)((st * C::TILE) >> 4);
-                    // keys 0-63 accumulate into O_0 (columns O_COL..), keys 64-127 into O_1 (O_COL + D..)
+                    // keys 0-63 accumulate into O_0 (columns O_COL..), keys 64-127 into O_1 (O_COL + D..);
+                    // P of key half hf is bf16 in TMEM (two keys per column) over the first
+                    // 32 columns of that half's S: S buffer st, columns 64 hf .. 64 hf + 31
 #pragma unroll
                     for (int kk = 0; kk < C::BN / 16; kk++)
-                        umma_f16_ss(tmem + C::O_COL + (kk >> 2) * D, pd + (((kk >> 2) * 16384 + (kk & 3) * 32) >> 4),
+                        umma_f16_ts(tmem + C::O_COL + (kk >> 2) * D, tmem + st * 128 + (kk >> 2) * 64 + (kk & 3) * 8,
                                     vd + ((kk * 16 * 128) >> 4), idesc_o, (j | (kk & 3)) != 0);
                     umma_commit(v_empty0 + 8 * st);
-                    umma_commit(p_free0 + 8 * st);
+                    umma_commit(p_free0 + 8 * st);   // P V of this tile done (O may be rescaled / read)
+                    umma_commit(s_free0 + 8 * st);   // S buffer st (holding P) may be overwritten
                 }
               }
             }
@@ -293,9 +296,6 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
                 tmem_ld32(t_lane + sb * 128 + hf * 64, s);
                 tmem_ld32(t_lane + sb * 128 + hf * 64 + 32, s + 32);
                 tmem_wait_ld();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(s_free0 + 8 * sb);   // S buffer sb may be overwritten
                 const int k0 = j * C::BN + hf * 64;
                 // 8 independent max chains (latency, not issue, bounds this loop otherwise)
                 float mx8[8];
@@ -359,33 +359,26 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
                     }
                 }
                 l_run += ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
-                // P row half -> shared memory tile sb (free once P V_{g-2} is done): one 64-key atom
-                if (g >= 2) ok = mbar_wait(p_free0 + 8 * sb, ((g - 2) >> 1) & 1, err, DEV_ERR_TIMEOUT_MISC) && ok;
-                uint8_t* prow = sP + sb * C::P_BYTES + hf * 16384 + r * 128;
+                // P row half -> TMEM over this half's own S columns (already read): key
+                // 2c in the low and 2c + 1 in the high half of column c, the A operand of P V
+                uint32_t pk[32];
 #pragma unroll
-                for (int c8 = 0; c8 < 8; c8++) {
-                    uint4 v;
-                    v.x = pack_bf16x2(s[c8 * 8 + 0], s[c8 * 8 + 1]);
-                    v.y = pack_bf16x2(s[c8 * 8 + 2], s[c8 * 8 + 3]);
-                    v.z = pack_bf16x2(s[c8 * 8 + 4], s[c8 * 8 + 5]);
-                    v.w = pack_bf16x2(s[c8 * 8 + 6], s[c8 * 8 + 7]);
-                    *reinterpret_cast<uint4*>(prow + ((c8 ^ (r & 7)) << 4)) = v;
-                }
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                for (int c = 0; c < 32; c++) pk[c] = pack_bf16x2(s[2 * c], s[2 * c + 1]);
+                tmem_st32u(t_lane + sb * 128 + hf * 64, pk);
+                tmem_wait_st();
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(p_full0 + 8 * sb);
             }
-            // this query tile's last P V (g - 1); then the P tiles are free: exchange (max, sum)
-            // of the two halves there
+            // this query tile's last P V (g - 1) has completed O; exchange (max, sum) of the
+            // two halves
             if (n_tiles > 0)
                 ok = mbar_wait(p_free0 + 8 * ((g - 1) & 1), ((g - 1) >> 1) & 1, err, DEV_ERR_TIMEOUT_ACC) && ok;
-            float* xch = reinterpret_cast<float*>(sP);   // [2 halves][128 rows][2]
             xch[(hf * 128 + r) * 2] = m_ref;
             xch[(hf * 128 + r) * 2 + 1] = l_run;
             asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
             const float m_o = xch[((hf ^ 1) * 128 + r) * 2], l_o = xch[((hf ^ 1) * 128 + r) * 2 + 1];
-            // both halves have read the exchange before the next query tile's P reuses it
+            // both halves have read the exchange before the next query tile writes it
             asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
             const float M = fmaxf(m_ref, m_o);
             const float w_a = (hf == 0 ? m_ref : m_o) == -INFINITY ? 0.f : ex2((hf == 0 ? m_ref : m_o) - M);
