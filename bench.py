@@ -704,7 +704,7 @@ def run_c2(args, rank, world, local):
                        "bf16_conv_timing": f"{CONV_REPS} launches on distinct NHWC inputs (more than L2) per graph "
                                            "replay, L2 flushed before each replay; ms per launch",
                        "fp32_conv_tflops": round(flops_conv / (conv_f32 / 1e3) / 1e12, 1)},
-            "roofline": {"kernel": "conv_pm_kernel, one inner conv (NHWC in and out), mean of CONV_REPS launches", "bound": "tensor", "achieved": round(tf, 1),
+            "roofline": {"kernel": f"conv_pm_kernel, one inner conv (NHWC in and out), mean of {CONV_REPS} launches", "bound": "tensor", "achieved": round(tf, 1),
                          "peak": pk["tc"], "unit": "TFLOP/s", "frac": round(tf / pk["tc"], 3), "traffic": None,
                          "peak_source": pk["src"]},
             "clocks": clocks}
