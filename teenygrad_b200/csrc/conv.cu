@@ -747,6 +747,102 @@ conv_simt_kernel(const T* __restrict__ x, const T* __restrict__ w, ConvEpi ep, T
     }
 }
 
+// ------------------------------------------------- f32 3 x 3 direct conv ---
+// fp32, 3 x 3, stride 1, pad 1 (the fp32 C2 stage): a CTA computes one output
+// row of one image for 64 output channels; thread (cg, seg) the 8 consecutive
+// pixels [8 seg, 8 seg + 8) x the 8 channels [8 cg, 8 cg + 8) of the block, 64
+// accumulators.  Per chunk of 8 input channels the three input rows the output
+// row needs ([8][3][W + 2], zero padded) and the chunk's weights, transposed to
+// [8][9][64] so that a thread's 8 output channels are two 16-byte words, are
+// staged in shared memory; per (channel, kh) a thread reads one 10-float input
+// window, reused by the three kw taps, and 24 weights: 192 FMAs for 9 loads.
+// Many small CTAs (rows x images, 8 resident per SM) keep the SMs evenly loaded
+// and cover each other's staging.  Accumulation order: channel, kh, kw.
+constexpr int C3_CC = 8;                 // input channels per chunk
+constexpr int C3_WS = 64 + 4;            // weight row stride (16-byte aligned rows)
+
+__global__ void __launch_bounds__(128, 4)
+conv3x3_f32_kernel(const float* __restrict__ x, const float* __restrict__ w, ConvEpi ep, float* __restrict__ y, int C,
+                   int Co, int H, int W) {
+    pdl_trigger();
+    pdl_wait();
+    extern __shared__ float c3_smem[];
+    const int XW = W + 4;                            // input row stride: columns -1 .. W, 16-byte aligned rows
+    float* xs = c3_smem;                             // [C3_CC * 3][XW]
+    float* ws = xs + C3_CC * 3 * XW;                 // [C3_CC * 9][C3_WS]
+    const int oh = blockIdx.x, b = blockIdx.y, co0 = blockIdx.z * 64;
+    const int t = threadIdx.x, nt = blockDim.x;
+    const int cg = t & 7, seg = t >> 3;
+    float acc[8][8];
+#pragma unroll
+    for (int j = 0; j < 8; j++)
+#pragma unroll
+        for (int i = 0; i < 8; i++) acc[j][i] = 0.f;
+    const int K9 = C * 9;
+    for (int c0 = 0; c0 < C; c0 += C3_CC) {
+        // input rows oh - 1 .. oh + 1 of the chunk's channels, columns -1 .. W (zero
+        // outside): row by row, the CTA's threads along each
+#pragma unroll 1
+        for (int rc = 0; rc < C3_CC * 3; rc++) {
+            const int r = rc % 3, cc = rc / 3;
+            const int ih = oh - 1 + r;
+            const bool row_in = ih >= 0 && ih < H;
+            const float* xrow = x + (((int64_t)b * C + c0 + cc) * H + (row_in ? ih : 0)) * W;
+            for (int col = t; col < W + 2; col += nt) {
+                const int iw = col - 1;
+                xs[rc * XW + col] = (row_in && iw >= 0 && iw < W) ? xrow[iw] : 0.f;
+            }
+        }
+        // weights w[co][c][kh][kw] of the chunk (72 contiguous floats per output channel,
+        // 16-byte aligned) -> ws[cc * 9 + tap][co]
+        for (int i = t; i < 64 * (C3_CC * 9 / 4); i += nt) {
+            const int co = i / (C3_CC * 9 / 4), q = i % (C3_CC * 9 / 4);
+            const float4 v = *reinterpret_cast<const float4*>(w + (int64_t)(co0 + co) * K9 + c0 * 9 + q * 4);
+            ws[(q * 4 + 0) * C3_WS + co] = v.x;
+            ws[(q * 4 + 1) * C3_WS + co] = v.y;
+            ws[(q * 4 + 2) * C3_WS + co] = v.z;
+            ws[(q * 4 + 3) * C3_WS + co] = v.w;
+        }
+        __syncthreads();
+#pragma unroll 1
+        for (int cc = 0; cc < C3_CC; cc++) {
+#pragma unroll
+            for (int kh = 0; kh < 3; kh++) {
+                const float* xr = xs + (cc * 3 + kh) * XW + seg * 8;
+                float xin[10];
+                const float4 x0 = *reinterpret_cast<const float4*>(xr);
+                const float4 x1 = *reinterpret_cast<const float4*>(xr + 4);
+                const float2 x2 = *reinterpret_cast<const float2*>(xr + 8);
+                xin[0] = x0.x; xin[1] = x0.y; xin[2] = x0.z; xin[3] = x0.w;
+                xin[4] = x1.x; xin[5] = x1.y; xin[6] = x1.z; xin[7] = x1.w;
+                xin[8] = x2.x; xin[9] = x2.y;
+#pragma unroll
+                for (int kw = 0; kw < 3; kw++) {
+                    const float* wr = ws + (cc * 9 + kh * 3 + kw) * C3_WS + cg * 8;
+                    const float4 w0 = *reinterpret_cast<const float4*>(wr);
+                    const float4 w1 = *reinterpret_cast<const float4*>(wr + 4);
+                    const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+                    for (int j = 0; j < 8; j++)
+#pragma unroll
+                        for (int i = 0; i < 8; i++) acc[j][i] = fmaf(xin[i + kw], wv[j], acc[j][i]);
+                }
+            }
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const int co = co0 + cg * 8 + j;
+        float o[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++) o[i] = conv_epi(ep, co, acc[j][i]);
+        float* dst = y + (((int64_t)b * Co + co) * H + oh) * W + seg * 8;
+        *reinterpret_cast<float4*>(dst) = make_float4(o[0], o[1], o[2], o[3]);
+        *reinterpret_cast<float4*>(dst + 4) = make_float4(o[4], o[5], o[6], o[7]);
+    }
+}
+
 // ------------------------------------------------------------ batchnorm ---
 __global__ void bn_fold_kernel(const float* g, const float* be, const float* mu, const float* var, const float* bias,
                                float eps, float* scale, float* shift, int C) {
@@ -856,6 +952,14 @@ int tb_conv2d_fwd_ex(tb_ctx* ctx, int dtype, const void* x, const void* w, const
     ConvEpi ep{bias, bn_scale, bn_shift, act};
     const int64_t P = (int64_t)B * s.OH * s.OW;
     const dim3 sgrid((unsigned)((P + 63) / 64), (unsigned)((Cout + 63) / 64));
+    if (dtype == TB_F32 && stride == 1 && KH == 3 && KW == 3 && pad == 1 && Cin % C3_CC == 0 && Cout % 64 == 0 &&
+        W % 8 == 0 && W <= 128 && B <= 65535 && aligned16(y) && aligned16(x) && aligned16(w)) {
+        // fp32 3 x 3 direct conv: one output row x 64 output channels per CTA
+        const int smem = (C3_CC * 3 * (W + 4) + C3_CC * 9 * C3_WS) * (int)sizeof(float);
+        TB_CUDA_TRY(ctx, cudaFuncSetAttribute(conv3x3_f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        return launch(ctx, "conv3x3_f32", conv3x3_f32_kernel, dim3((unsigned)H, (unsigned)B, (unsigned)(Cout / 64)),
+                      dim3((unsigned)(W / 8 * 8)), smem, (const float*)x, (const float*)w, ep, (float*)y, Cin, Cout, H, W);
+    }
     if (dtype == TB_F32)
         return launch(ctx, "conv2d_f32", conv_simt_kernel<float>, sgrid, dim3(256), 0, (const float*)x, (const float*)w,
                       ep, (float*)y, B, Cin, Cout, H, W, KH, KW, stride, pad, s.OH, s.OW);

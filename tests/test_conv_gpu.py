@@ -161,6 +161,16 @@ def test_conv2d_f32(B, C, Co, H, W, k, s, p):
     assert_close(got, ref, F32_TOL)
 
 
+@pytest.mark.parametrize("B,C,Co,H,W,act,bn", [(2, 16, 128, 9, 16, "silu", True), (3, 8, 64, 5, 8, None, False),
+                                                (1, 64, 64, 3, 128, "relu", True), (2, 24, 64, 7, 40, "relu", False)])
+def test_conv2d_f32_direct3x3(B, C, Co, H, W, act, bn):
+    """The fp32 3 x 3 / stride 1 / pad 1 direct kernel: two output-channel blocks,
+    the narrowest and widest rows it takes, bias without BN, SiLU."""
+    got, ref = _conv_case(B, C, Co, H, W, 3, 1, 1, act, torch.float32, seed=H + W + C, with_bn=bn)
+    assert_close(got, ref, F32_TOL)
+    no_device_error()
+
+
 def test_conv2d_plain_bias_no_bn():
     got, ref = _conv_case(1, 64, 64, 16, 16, 3, 1, 1, None, torch.bfloat16, seed=11, with_bn=False)
     assert_close(got, ref, BF16_TOL)
