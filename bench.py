@@ -731,7 +731,7 @@ def run_c1(args, rank, world, local):
 
 def ncu_case(which):
     """Small fixed cases for ncu captures of one kernel kind (the commands in profiles/):
-    gemv, gemv8, attn_dec, gemm, fa, conv, c4 (prefill + 3 decode steps for the launch list) or c5
+    gemv, gemv8, attn_dec, gemm, fa, conv, conv32, c4 (prefill + 3 decode steps for the launch list) or c5
     (the int8 decoder: KV fill + 2 decode steps)."""
     import torch
     from teenygrad_b200 import ops
@@ -770,6 +770,12 @@ def ncu_case(which):
         xh, wp = x.permute(0, 2, 3, 1).contiguous(), ops.conv2d_pack_weights(w)
         for _ in range(2):
             ops.conv2d(xh, wp, scale=sc, shift=sh, pad=1, act="relu", x_nhwc=True, y_nhwc=True, w_packed=True)
+    elif which == "conv32":      # C2 fp32 conv: B32 64->64 56x56 3x3 + BN + ReLU, NCHW (conv3x3_f32_kernel)
+        x = torch.randn(32, 64, 56, 56, device="cuda")
+        w = torch.randn(64, 64, 3, 3, device="cuda") * 0.05
+        sc, sh = torch.ones(64, device="cuda"), torch.zeros(64, device="cuda")
+        for _ in range(2):
+            ops.conv2d(x, w, scale=sc, shift=sh, pad=1, act="relu")
     elif which == "c5":          # C5 int8 decoder: batch 64 over a 2048-position cache, 2 decode steps
         from teenygrad_b200.decoder import Decoder, DecoderConfig
         c = C5

@@ -781,8 +781,9 @@ conv3x3_f32_kernel(const float* __restrict__ x, const float* __restrict__ w, Con
     const int K9 = C * 9;
     for (int c0 = 0; c0 < C; c0 += C3_CC) {
         // input rows oh - 1 .. oh + 1 of the chunk's channels, columns -1 .. W (zero
-        // outside): row by row, the CTA's threads along each
-#pragma unroll 1
+        // outside): row by row, the CTA's threads along each (unrolled, so a thread's
+        // loads of several rows are in flight before their stores)
+#pragma unroll 6
         for (int rc = 0; rc < C3_CC * 3; rc++) {
             const int r = rc % 3, cc = rc / 3;
             const int ih = oh - 1 + r;
@@ -794,9 +795,12 @@ conv3x3_f32_kernel(const float* __restrict__ x, const float* __restrict__ w, Con
             }
         }
         // weights w[co][c][kh][kw] of the chunk (72 contiguous floats per output channel,
-        // 16-byte aligned) -> ws[cc * 9 + tap][co]
+        // 16-byte aligned) -> ws[cc * 9 + tap][co]; consecutive threads take consecutive
+        // output channels, so the transposing stores hit 32 different banks (the loads
+        // are 2.3 KB apart, but each output channel's 288 bytes stay in L1 across q)
+#pragma unroll 4
         for (int i = t; i < 64 * (C3_CC * 9 / 4); i += nt) {
-            const int co = i / (C3_CC * 9 / 4), q = i % (C3_CC * 9 / 4);
+            const int co = i & 63, q = i >> 6;
             const float4 v = *reinterpret_cast<const float4*>(w + (int64_t)(co0 + co) * K9 + c0 * 9 + q * 4);
             ws[(q * 4 + 0) * C3_WS + co] = v.x;
             ws[(q * 4 + 1) * C3_WS + co] = v.y;
