@@ -748,31 +748,36 @@ conv_simt_kernel(const T* __restrict__ x, const T* __restrict__ w, ConvEpi ep, T
 }
 
 // ------------------------------------------------- f32 3 x 3 direct conv ---
-// fp32, 3 x 3, stride 1, pad 1 (the fp32 C2 stage): a CTA computes one output
-// row of one image for 64 output channels; thread (cg, seg) the 8 consecutive
-// pixels [8 seg, 8 seg + 8) x the 8 channels [8 cg, 8 cg + 8) of the block, 64
-// accumulators.  Per chunk of 8 input channels the three input rows the output
-// row needs ([8][3][W + 2], zero padded) and the chunk's weights, transposed to
+// fp32, 3 x 3, stride 1, pad 1 (the fp32 C2 stage): a CTA computes two output
+// rows of one image for 64 output channels; thread (cg, seg, row) the 8
+// consecutive pixels [8 seg, 8 seg + 8) of its row x the 8 channels [8 cg, 8 cg + 8)
+// of the block, 64 accumulators.  Per chunk of 8 input channels the four input
+// rows the two output rows need ([8][4][W + 2], zero padded) and the chunk's weights, transposed to
 // [8][9][64] so that a thread's 8 output channels are two 16-byte words, are
 // staged in shared memory; per (channel, kh) a thread reads one 10-float input
 // window, reused by the three kw taps, and 24 weights: 192 FMAs for 9 loads.
-// Many small CTAs (rows x images, 8 resident per SM) keep the SMs evenly loaded
-// and cover each other's staging.  Accumulation order: channel, kh, kw.
+// Many small CTAs (row pairs x images, 4 resident per SM at W = 56) keep the SMs
+// evenly loaded and cover each other's staging; a chunk's weights serve both rows.
+// Accumulation order: channel, kh, kw.
 constexpr int C3_CC = 8;                 // input channels per chunk
 constexpr int C3_WS = 64 + 4;            // weight row stride (16-byte aligned rows)
+constexpr int C3_TR = 2;                 // output rows per CTA (the chunk's weights serve both)
 
-__global__ void __launch_bounds__(128, 4)
+__global__ void __launch_bounds__(256, 2)
 conv3x3_f32_kernel(const float* __restrict__ x, const float* __restrict__ w, ConvEpi ep, float* __restrict__ y, int C,
                    int Co, int H, int W) {
     pdl_trigger();
     pdl_wait();
     extern __shared__ float c3_smem[];
+    constexpr int XR = C3_TR + 2;                    // input rows per channel
     const int XW = W + 4;                            // input row stride: columns -1 .. W, 16-byte aligned rows
-    float* xs = c3_smem;                             // [C3_CC * 3][XW]
-    float* ws = xs + C3_CC * 3 * XW;                 // [C3_CC * 9][C3_WS]
-    const int oh = blockIdx.x, b = blockIdx.y, co0 = blockIdx.z * 64;
+    float* xs = c3_smem;                             // [C3_CC * XR][XW]
+    float* ws = xs + C3_CC * XR * XW;                // [C3_CC * 9][C3_WS]
+    const int oh0 = blockIdx.x * C3_TR, b = blockIdx.y, co0 = blockIdx.z * 64;
     const int t = threadIdx.x, nt = blockDim.x;
-    const int cg = t & 7, seg = t >> 3;
+    const int SEG = W / 8;
+    const int cg = t & 7, seg = (t >> 3) % SEG, rr = (t >> 3) / SEG;   // rr: this thread's output row
+    const int oh = oh0 + rr;
     float acc[8][8];
 #pragma unroll
     for (int j = 0; j < 8; j++)
@@ -780,13 +785,13 @@ conv3x3_f32_kernel(const float* __restrict__ x, const float* __restrict__ w, Con
         for (int i = 0; i < 8; i++) acc[j][i] = 0.f;
     const int K9 = C * 9;
     for (int c0 = 0; c0 < C; c0 += C3_CC) {
-        // input rows oh - 1 .. oh + 1 of the chunk's channels, columns -1 .. W (zero
+        // input rows oh0 - 1 .. oh0 + C3_TR of the chunk's channels, columns -1 .. W (zero
         // outside): row by row, the CTA's threads along each (unrolled, so a thread's
         // loads of several rows are in flight before their stores)
-#pragma unroll 6
-        for (int rc = 0; rc < C3_CC * 3; rc++) {
-            const int r = rc % 3, cc = rc / 3;
-            const int ih = oh - 1 + r;
+#pragma unroll 8
+        for (int rc = 0; rc < C3_CC * XR; rc++) {
+            const int r = rc % XR, cc = rc / XR;
+            const int ih = oh0 - 1 + r;
             const bool row_in = ih >= 0 && ih < H;
             const float* xrow = x + (((int64_t)b * C + c0 + cc) * H + (row_in ? ih : 0)) * W;
             for (int col = t; col < W + 2; col += nt) {
@@ -812,7 +817,7 @@ conv3x3_f32_kernel(const float* __restrict__ x, const float* __restrict__ w, Con
         for (int cc = 0; cc < C3_CC; cc++) {
 #pragma unroll
             for (int kh = 0; kh < 3; kh++) {
-                const float* xr = xs + (cc * 3 + kh) * XW + seg * 8;
+                const float* xr = xs + (cc * XR + rr + kh) * XW + seg * 8;
                 float xin[10];
                 const float4 x0 = *reinterpret_cast<const float4*>(xr);
                 const float4 x1 = *reinterpret_cast<const float4*>(xr + 4);
@@ -835,6 +840,7 @@ conv3x3_f32_kernel(const float* __restrict__ x, const float* __restrict__ w, Con
         }
         __syncthreads();
     }
+    if (oh >= H) return;   // the second row of the last CTA when H is odd
 #pragma unroll
     for (int j = 0; j < 8; j++) {
         const int co = co0 + cg * 8 + j;
@@ -959,10 +965,11 @@ int tb_conv2d_fwd_ex(tb_ctx* ctx, int dtype, const void* x, const void* w, const
     if (dtype == TB_F32 && stride == 1 && KH == 3 && KW == 3 && pad == 1 && Cin % C3_CC == 0 && Cout % 64 == 0 &&
         W % 8 == 0 && W <= 128 && B <= 65535 && aligned16(y) && aligned16(x) && aligned16(w)) {
         // fp32 3 x 3 direct conv: one output row x 64 output channels per CTA
-        const int smem = (C3_CC * 3 * (W + 4) + C3_CC * 9 * C3_WS) * (int)sizeof(float);
+        const int smem = (C3_CC * (C3_TR + 2) * (W + 4) + C3_CC * 9 * C3_WS) * (int)sizeof(float);
         TB_CUDA_TRY(ctx, cudaFuncSetAttribute(conv3x3_f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-        return launch(ctx, "conv3x3_f32", conv3x3_f32_kernel, dim3((unsigned)H, (unsigned)B, (unsigned)(Cout / 64)),
-                      dim3((unsigned)(W / 8 * 8)), smem, (const float*)x, (const float*)w, ep, (float*)y, Cin, Cout, H, W);
+        return launch(ctx, "conv3x3_f32", conv3x3_f32_kernel,
+                      dim3((unsigned)((H + C3_TR - 1) / C3_TR), (unsigned)B, (unsigned)(Cout / 64)),
+                      dim3((unsigned)(C3_TR * W)), smem, (const float*)x, (const float*)w, ep, (float*)y, Cin, Cout, H, W);
     }
     if (dtype == TB_F32)
         return launch(ctx, "conv2d_f32", conv_simt_kernel<float>, sgrid, dim3(256), 0, (const float*)x, (const float*)w,
