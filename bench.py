@@ -731,7 +731,7 @@ def run_c1(args, rank, world, local):
 
 def ncu_case(which):
     """Small fixed cases for ncu captures of one kernel kind (the commands in profiles/):
-    gemv, gemv8, attn_dec, gemm, fa, conv, conv32, c4 (prefill + 3 decode steps for the launch list) or c5
+    gemv, gemv8, attn_dec, gemm, fa, conv, conv32, c1, c4 (prefill + 3 decode steps for the launch list) or c5
     (the int8 decoder: KV fill + 2 decode steps)."""
     import torch
     from teenygrad_b200 import ops
@@ -776,6 +776,13 @@ def ncu_case(which):
         sc, sh = torch.ones(64, device="cuda"), torch.zeros(64, device="cuda")
         for _ in range(2):
             ops.conv2d(x, w, scale=sc, shift=sh, pad=1, act="relu")
+    elif which == "c1":          # C1 fp32 block on the graph executor: 3 replays
+        from teenygrad_b200.block import block_graph, random_block_params
+        c = C1
+        g = block_graph(random_block_params(d=c["d"], F=c["ffn"], seed=0), c["B"], c["S"], c["heads"], 1e-6, capture=True)
+        g.run(torch.randn(c["B"], c["S"], c["d"], device="cuda"))
+        for _ in range(3):
+            g.launch()
     elif which == "c5":          # C5 int8 decoder: batch 64 over a 2048-position cache, 2 decode steps
         from teenygrad_b200.decoder import Decoder, DecoderConfig
         c = C5
