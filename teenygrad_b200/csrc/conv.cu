@@ -964,7 +964,7 @@ int tb_conv2d_fwd_ex(tb_ctx* ctx, int dtype, const void* x, const void* w, const
     const dim3 sgrid((unsigned)((P + 63) / 64), (unsigned)((Cout + 63) / 64));
     if (dtype == TB_F32 && stride == 1 && KH == 3 && KW == 3 && pad == 1 && Cin % C3_CC == 0 && Cout % 64 == 0 &&
         W % 8 == 0 && W <= 128 && B <= 65535 && aligned16(y) && aligned16(x) && aligned16(w)) {
-        // fp32 3 x 3 direct conv: one output row x 64 output channels per CTA
+        // fp32 3 x 3 direct conv: two output rows x 64 output channels per CTA (2W threads)
         const int smem = (C3_CC * (C3_TR + 2) * (W + 4) + C3_CC * 9 * C3_WS) * (int)sizeof(float);
         TB_CUDA_TRY(ctx, cudaFuncSetAttribute(conv3x3_f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
         return launch(ctx, "conv3x3_f32", conv3x3_f32_kernel,
